@@ -1,0 +1,145 @@
+/*
+ * qwen_asr_b200.h - C ABI of the B200 decoder library (libqwen_asr_b200.so).
+ *
+ * This library replaces, for the Qwen3 decoder, the reference's
+ * qwen_asr_decoder.c and the decoder-used kernels of qwen_asr_kernels*.c
+ * (dispatch in qwen_asr_kernels_impl.h). Plain pointers and sizes only.
+ * Host code of the reference (qwen_asr.c) keeps calling
+ * qwen_decoder_load / qwen_decoder_prefill / qwen_decoder_forward; the thin C
+ * adapter in qwen-asr_b200/dropin/qwen_asr_decoder_b200.c implements those
+ * three symbols on top of the functions below.
+ *
+ * Conventions
+ *  - Weights: bf16 (uint16_t bit patterns) row-major [out, in] matrices and
+ *    f32 norm vectors, given as HOST pointers; each is copied to the device
+ *    once. The caller may free or unmap them after qdb_model_finalize().
+ *  - Activations at the boundary are f32, as in the reference.
+ *  - Return codes: 0 = ok, -1 = error (message via qdb_last_error()).
+ *    Token-returning calls return the token id (>= 0) or -1.
+ *  - All work of a model runs on one CUDA stream owned by the model; every
+ *    host-pointer call is synchronous like the reference's CPU functions.
+ *  - Not thread-safe per model (the reference API is single-caller).
+ */
+#ifndef QWEN_ASR_B200_H
+#define QWEN_ASR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QDB_TOKEN_ENDOFTEXT 151643
+#define QDB_TOKEN_IM_END    151645
+
+/* Decoder shape. Mirrors the decoder fields of qwen_config_t
+ * (qwen_asr.h:59-68). head_dim must be 128; hidden and intermediate must be
+ * multiples of 256; heads must be a multiple of kv_heads. */
+typedef struct {
+    int hidden;
+    int layers;
+    int heads;
+    int kv_heads;
+    int head_dim;
+    int intermediate;
+    int vocab;
+    float eps;
+    float theta;
+} qdb_config;
+
+typedef struct qdb_model qdb_model;
+typedef struct qdb_session qdb_session;
+
+/* Last error message of the calling thread ("" if none). */
+const char *qdb_last_error(void);
+
+/* Number of CUDA devices visible (0 when no GPU/driver). Never fails. */
+int qdb_device_count(void);
+
+/* ---- Model (weights), replaces qwen_decoder_load (qwen_asr_decoder.c:45-116) ---- */
+
+/* Creates an empty model on `device` and allocates device storage for all
+ * weights. Returns NULL on error. */
+qdb_model *qdb_model_create(const qdb_config *cfg, int device);
+
+/* Token embedding / tied lm_head [vocab, hidden] bf16 and final norm [hidden]
+ * f32 (thinker.model.embed_tokens.weight, thinker.model.norm.weight). */
+int qdb_model_set_embed(qdb_model *m, const uint16_t *embed, const float *final_norm);
+
+/* One decoder layer (thinker.model.layers.{i}.*): q/k/v/o, gate/up/down bf16
+ * matrices, q_norm/k_norm [head_dim] and input/post-attention norms [hidden]
+ * f32. gate and up are separate [intermediate, hidden] matrices; the library
+ * builds its own fused layout (the reference's gate_up interleave,
+ * qwen_asr_decoder.c:95-107). */
+int qdb_model_set_layer(qdb_model *m, int layer,
+                        const uint16_t *wq, const uint16_t *wk, const uint16_t *wv,
+                        const uint16_t *wo, const uint16_t *gate, const uint16_t *up,
+                        const uint16_t *down,
+                        const float *q_norm, const float *k_norm,
+                        const float *input_norm, const float *post_attn_norm);
+
+/* Checks every weight was set and waits for the uploads. */
+int qdb_model_finalize(qdb_model *m);
+void qdb_model_free(qdb_model *m);
+
+/* Benchmark switch: when set, greedy selection never returns 151643 or
+ * 151645 (fixed-length decoding). The reference has no such switch. */
+int qdb_model_set_mask_eos(qdb_model *m, int enable);
+
+/* ---- Session: one utterance's device KV cache (qwen_ctx_t KV fields,
+ * qwen_asr.h:187-191; kv_cache_init / kv_cache_grow, qwen_asr_decoder.c:122-160).
+ * K/V are stored bf16 [layer][kv_head][pos][head_dim]; the cache grows
+ * (doubling, contents kept) when a call needs more positions than it holds. */
+qdb_session *qdb_session_create(qdb_model *m, int initial_capacity);
+void qdb_session_free(qdb_session *s);
+int qdb_session_capacity(const qdb_session *s);
+int qdb_session_reserve(qdb_session *s, int positions);
+
+/* ---- Prefill, replaces qwen_decoder_prefill (qwen_asr_decoder.c:262-359) ----
+ * Appends seq_len positions starting at absolute position start_pos (the
+ * caller's kv_cache_len, which stays authoritative on the host: the caller may
+ * rewind it, as the streaming loop does at qwen_asr.c:1764). embeds: host f32
+ * [seq_len, hidden]. seq_len == 0 is a no-op. */
+int qdb_prefill(qdb_session *s, const float *embeds, int seq_len, int start_pos);
+
+/* Same with a DEVICE pointer to the embeddings (no host copy). */
+int qdb_prefill_device(qdb_session *s, const float *embeds_dev, int seq_len, int start_pos);
+
+/* ---- One decode step, replaces qwen_decoder_forward (qwen_asr_decoder.c:388-476) ----
+ * Runs position `pos` with the host f32 embedding [hidden]; returns the greedy
+ * token. hidden_out (nullable, host, [hidden]) receives the final-normed hidden
+ * state the reference leaves in ctx->dec_x; logits_out (nullable, host,
+ * [vocab]) the final-layer logits. */
+int qdb_forward(qdb_session *s, const float *embed, int pos, float *hidden_out,
+                float *logits_out);
+
+/* ---- Device-resident greedy loop (embedding lookup on the device, the
+ * caller loop of qwen_asr.c:729-759 without the tokenizer). Starts from
+ * `first_token` at position `pos` and runs n_steps steps back to back;
+ * tokens_out (host, [n_steps]) receives the greedy tokens. */
+int qdb_decode_greedy(qdb_session *s, int first_token, int pos, int n_steps, int *tokens_out);
+
+/* ---- Batched decode of independent utterances (no reference counterpart:
+ * the reference decodes one utterance per process). Row b runs session
+ * sessions[b] at position pos[b] with embedding row b of embeds (host f32
+ * [n, hidden]); tokens_out[b] receives its greedy token. */
+int qdb_forward_batch(qdb_session *const *sessions, int n, const float *embeds,
+                      const int *pos, int *tokens_out);
+
+/* Batched device-resident greedy loop over n sessions: row b starts from
+ * first_tokens[b] at pos[b]; tokens_out is [n_steps, n] (host). */
+int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, const int *first_tokens,
+                            const int *pos, int n_steps, int *tokens_out);
+
+/* Waits for all queued work of the model's stream. */
+int qdb_model_sync(qdb_model *m);
+
+/* The cudaStream_t (as void*) every call of this model runs on, for callers
+ * that time or order work against it. */
+void *qdb_model_stream(qdb_model *m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,264 @@
+"""qwen-asr_b200: B200 decoder hot path of qwen-asr behind a C ABI.
+
+Host-side Python mirror of the reference decoder interface
+(qwen_decoder_prefill / qwen_decoder_forward, qwen_asr.h:313-317) over
+libqwen_asr_b200.so (include/qwen_asr_b200.h). The CUDA library is the only
+compute path: importing this package fails loudly when the library is missing,
+and there is no CPU fallback.
+
+    ctx = Decoder(model, capacity)      # one utterance: device KV cache
+    ctx.kv_cache_len = 0                # host-owned length, as qwen_ctx_t
+    ctx.prefill(input_embeds)           # appends len(input_embeds) positions
+    tok = ctx.forward(embed)            # one position, returns greedy token
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libqwen_asr_b200.so")
+
+QWEN_TOKEN_ENDOFTEXT = 151643
+QWEN_TOKEN_IM_END = 151645
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+_i32p = ctypes.POINTER(ctypes.c_int)
+
+
+class QdbConfig(ctypes.Structure):
+    _fields_ = [("hidden", ctypes.c_int), ("layers", ctypes.c_int), ("heads", ctypes.c_int),
+                ("kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("intermediate", ctypes.c_int),
+                ("vocab", ctypes.c_int), ("eps", ctypes.c_float), ("theta", ctypes.c_float)]
+
+
+# Every symbol include/qwen_asr_b200.h declares: name -> (restype, argtypes).
+ABI = {
+    "qdb_last_error": (ctypes.c_char_p, []),
+    "qdb_device_count": (ctypes.c_int, []),
+    "qdb_model_create": (ctypes.c_void_p, [ctypes.POINTER(QdbConfig), ctypes.c_int]),
+    "qdb_model_set_embed": (ctypes.c_int, [ctypes.c_void_p, _u16p, _f32p]),
+    "qdb_model_set_layer": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int] + [_u16p] * 7 + [_f32p] * 4),
+    "qdb_model_finalize": (ctypes.c_int, [ctypes.c_void_p]),
+    "qdb_model_free": (None, [ctypes.c_void_p]),
+    "qdb_model_set_mask_eos": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "qdb_session_create": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int]),
+    "qdb_session_free": (None, [ctypes.c_void_p]),
+    "qdb_session_capacity": (ctypes.c_int, [ctypes.c_void_p]),
+    "qdb_session_reserve": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "qdb_prefill": (ctypes.c_int, [ctypes.c_void_p, _f32p, ctypes.c_int, ctypes.c_int]),
+    "qdb_prefill_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int]),
+    "qdb_forward": (ctypes.c_int, [ctypes.c_void_p, _f32p, ctypes.c_int, _f32p, _f32p]),
+    "qdb_decode_greedy": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _i32p]),
+    "qdb_forward_batch": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _f32p, _i32p, _i32p]),
+    "qdb_decode_greedy_batch": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _i32p, _i32p,
+                                               ctypes.c_int, _i32p]),
+    "qdb_model_sync": (ctypes.c_int, [ctypes.c_void_p]),
+    "qdb_model_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
+}
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(f"{LIB_PATH} is missing: build it with `make -C qwen-asr_b200` "
+                          "(the CUDA library is the only compute path)")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in ABI.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+class QdbError(RuntimeError):
+    pass
+
+
+def _err(what):
+    msg = lib.qdb_last_error()
+    return QdbError(f"{what}: {msg.decode() if msg else ''}")
+
+
+def _ptr(a, t):
+    return a.ctypes.data_as(t)
+
+
+def device_count() -> int:
+    return lib.qdb_device_count()
+
+
+class Model:
+    """Device copy of one decoder's weights (replaces qwen_decoder_load,
+    qwen_asr_decoder.c:45-116). `weights` is a synth.WeightSet or any object
+    with .cfg, .embed, .final_norm and .layer(i)."""
+
+    def __init__(self, weights, device: int = 0, mask_eos: bool = False):
+        cfg = weights.cfg
+        self.cfg = cfg
+        c = QdbConfig(cfg.hidden, cfg.layers, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.intermediate,
+                      cfg.vocab, cfg.eps, cfg.theta)
+        self.h = lib.qdb_model_create(ctypes.byref(c), device)
+        if not self.h:
+            raise _err("qdb_model_create")
+        emb = np.ascontiguousarray(weights.embed)
+        fn = np.ascontiguousarray(weights.final_norm, dtype=np.float32)
+        if lib.qdb_model_set_embed(self.h, _ptr(emb, _u16p), _ptr(fn, _f32p)):
+            raise _err("qdb_model_set_embed")
+        for i in range(cfg.layers):
+            L = weights.layer(i)
+            mats = [np.ascontiguousarray(L[k]) for k in ("wq", "wk", "wv", "wo", "gate", "up", "down")]
+            norms = [np.ascontiguousarray(L[k], dtype=np.float32)
+                     for k in ("q_norm", "k_norm", "input_norm", "post_attn_norm")]
+            if lib.qdb_model_set_layer(self.h, i, *[_ptr(a, _u16p) for a in mats], *[_ptr(a, _f32p) for a in norms]):
+                raise _err(f"qdb_model_set_layer({i})")
+        if lib.qdb_model_finalize(self.h):
+            raise _err("qdb_model_finalize")
+        self.set_mask_eos(mask_eos)
+
+    def set_mask_eos(self, on: bool):
+        lib.qdb_model_set_mask_eos(self.h, 1 if on else 0)
+
+    @property
+    def stream_handle(self) -> int:
+        """cudaStream_t of this model (for torch.cuda.ExternalStream)."""
+        return lib.qdb_model_stream(self.h) or 0
+
+    def session(self, capacity: int = 1024) -> "Session":
+        return Session(self, capacity)
+
+    def sync(self):
+        if lib.qdb_model_sync(self.h):
+            raise _err("qdb_model_sync")
+
+    def close(self):
+        if self.h:
+            lib.qdb_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Session:
+    """One utterance's device KV cache (qwen_ctx_t KV fields)."""
+
+    def __init__(self, model: Model, capacity: int = 1024):
+        self.model = model
+        self.h = lib.qdb_session_create(model.h, capacity)
+        if not self.h:
+            raise _err("qdb_session_create")
+
+    @property
+    def capacity(self) -> int:
+        return lib.qdb_session_capacity(self.h)
+
+    def prefill(self, embeds: np.ndarray, start_pos: int):
+        e = np.ascontiguousarray(embeds, dtype=np.float32)
+        n = 0 if e.size == 0 else e.shape[0]
+        if lib.qdb_prefill(self.h, _ptr(e, _f32p), n, start_pos):
+            raise _err("qdb_prefill")
+
+    def prefill_device(self, dev_ptr: int, n: int, start_pos: int):
+        if lib.qdb_prefill_device(self.h, ctypes.c_void_p(dev_ptr), n, start_pos):
+            raise _err("qdb_prefill_device")
+
+    def forward(self, embed: np.ndarray, pos: int, want_hidden=False, want_logits=False):
+        cfg = self.model.cfg
+        e = np.ascontiguousarray(embed, dtype=np.float32).reshape(cfg.hidden)
+        hid = np.empty(cfg.hidden, np.float32) if want_hidden else None
+        log = np.empty(cfg.vocab, np.float32) if want_logits else None
+        tok = lib.qdb_forward(self.h, _ptr(e, _f32p), pos, _ptr(hid, _f32p) if hid is not None else None,
+                              _ptr(log, _f32p) if log is not None else None)
+        if tok < 0:
+            raise _err("qdb_forward")
+        return tok, hid, log
+
+    def decode_greedy(self, first_token: int, pos: int, n_steps: int) -> np.ndarray:
+        out = np.empty(max(n_steps, 1), np.int32)
+        if lib.qdb_decode_greedy(self.h, first_token, pos, n_steps, _ptr(out, _i32p)):
+            raise _err("qdb_decode_greedy")
+        return out[:n_steps]
+
+    def close(self):
+        if self.h:
+            lib.qdb_session_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def _handles(sessions):
+    arr = (ctypes.c_void_p * len(sessions))(*[s.h for s in sessions])
+    return arr
+
+
+def forward_batch(sessions, embeds: np.ndarray, pos) -> np.ndarray:
+    n = len(sessions)
+    e = np.ascontiguousarray(embeds, dtype=np.float32)
+    p = np.ascontiguousarray(pos, dtype=np.int32)
+    out = np.empty(n, np.int32)
+    if lib.qdb_forward_batch(_handles(sessions), n, _ptr(e, _f32p), _ptr(p, _i32p), _ptr(out, _i32p)):
+        raise _err("qdb_forward_batch")
+    return out
+
+
+def decode_greedy_batch(sessions, first_tokens, pos, n_steps: int) -> np.ndarray:
+    n = len(sessions)
+    f = np.ascontiguousarray(first_tokens, dtype=np.int32)
+    p = np.ascontiguousarray(pos, dtype=np.int32)
+    out = np.empty((max(n_steps, 1), n), np.int32)
+    if lib.qdb_decode_greedy_batch(_handles(sessions), n, _ptr(f, _i32p), _ptr(p, _i32p), n_steps,
+                                   _ptr(out, _i32p)):
+        raise _err("qdb_decode_greedy_batch")
+    return out[:n_steps]
+
+
+class Decoder:
+    """Mirror of the reference's per-context decoder calls. kv_cache_len is
+    host-owned exactly like qwen_ctx_t.kv_cache_len (the caller may reset or
+    rewind it, qwen_asr.c:704, :1764). Errors follow the reference: prefill
+    returns silently leaving kv_cache_len unchanged (qwen_asr_decoder.c:276-282)
+    and forward returns QWEN_TOKEN_IM_END (qwen_asr_decoder.c:417, :421); the
+    message is kept in .last_error."""
+
+    def __init__(self, model: Model, capacity: int = 1024):
+        self.session = Session(model, capacity)
+        self.kv_cache_len = 0
+        self.dec_x = None  # final-normed hidden of the last forward (ctx->dec_x)
+        self.last_error = ""
+
+    def prefill(self, input_embeds: np.ndarray, seq_len: int | None = None):
+        e = np.asarray(input_embeds, dtype=np.float32)
+        if seq_len is None:
+            seq_len = e.shape[0]
+        try:
+            self.session.prefill(e[:seq_len], self.kv_cache_len)
+        except QdbError as ex:
+            self.last_error = str(ex)
+            return
+        self.kv_cache_len += seq_len
+
+    def forward(self, input_embed: np.ndarray, want_logits: bool = False):
+        try:
+            tok, hid, log = self.session.forward(input_embed, self.kv_cache_len, want_hidden=True,
+                                                 want_logits=want_logits)
+        except QdbError as ex:
+            self.last_error = str(ex)
+            return QWEN_TOKEN_IM_END
+        self.kv_cache_len += 1
+        self.dec_x = hid
+        self.logits = log
+        return tok

@@ -1,0 +1,81 @@
+// qdb_common.cuh - device helpers shared by the decoder kernels (sm_100a).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define QDB_HD 128            // head_dim (fixed)
+#define QDB_ENDOFTEXT 151643
+#define QDB_IM_END 151645
+
+// Error codes written to the device error word (first writer wins).
+enum {
+    QDB_ERR_NONE = 0,
+    QDB_ERR_BARRIER_TIMEOUT = 1,
+    QDB_ERR_BAD_ARG = 2,
+};
+
+// About one second at the B200's ~1.9 GHz SM clock: the bound on every spin.
+#define QDB_SPIN_LIMIT_CYCLES (2000000000ll)
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// 8 bf16 (one 16-byte vector) times 8 f32, accumulated in order into acc.
+__device__ __forceinline__ float dot8(const uint4 w, const float4 a, const float4 b, float acc) {
+    acc = fmaf(bf16lo(w.x), a.x, acc);
+    acc = fmaf(bf16hi(w.x), a.y, acc);
+    acc = fmaf(bf16lo(w.y), a.z, acc);
+    acc = fmaf(bf16hi(w.y), a.w, acc);
+    acc = fmaf(bf16lo(w.z), b.x, acc);
+    acc = fmaf(bf16hi(w.z), b.y, acc);
+    acc = fmaf(bf16lo(w.w), b.z, acc);
+    acc = fmaf(bf16hi(w.w), b.w, acc);
+    return acc;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Streaming 16-byte load that does not allocate in L1 (weights are read once).
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+
+// Greedy-argmax key: larger value wins; on an exact tie the lower index wins
+// (the reference's strict '>' scan from the lowest row). NaN never wins.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    uint32_t b = __float_as_uint(v);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((unsigned long long)b << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
+}
+__device__ __forceinline__ int argmax_key_index(unsigned long long k) {
+    return (int)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+    // g / (1 + e^-g) * u, the reference's SwiGLU (qwen_asr_kernels.c:925-927)
+    return g / (1.0f + expf(-g)) * u;
+}
+
+__device__ __forceinline__ void set_error(int *err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+__device__ __forceinline__ uint16_t f32_to_bf16_rn(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7f800000u) == 0x7f800000u) return (uint16_t)((u >> 16) | ((u & 0xffffu) ? 0x40u : 0u));
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}

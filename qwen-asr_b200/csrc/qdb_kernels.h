@@ -1,0 +1,99 @@
+// qdb_kernels.h - device-side data layout and kernel entry points shared by
+// the host runtime (qdb_runtime.cu) and the kernel files.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+// One decoder layer's device weights. Matrices are bf16 row-major [out, in].
+//   qkv : [Hq*128 + 2*Hkv*128, h]  rows of q_proj, then k_proj, then v_proj
+//   o   : [h, Hq*128]
+//   gu  : [2*I, h]  gate row j at 2j, up row j at 2j+1 (the reference's
+//                   interleave, qwen_asr_decoder.c:95-107)
+//   down: [h, I]
+struct QdbLayerW {
+    const uint16_t *qkv, *o, *gu, *down;
+    const float *q_norm, *k_norm, *in_norm, *post_norm;
+};
+
+struct QdbDims {
+    int h, L, Hq, Hkv, I, V;
+    float eps;
+};
+
+// Arguments of the persistent single-utterance decode step.
+struct QdbStepArgs {
+    QdbDims d;
+    const QdbLayerW *layers;      // device [L]
+    const uint16_t *embed;        // [V, h]
+    const float *final_norm;      // [h]
+    const float2 *rope;           // [rope_cap][64] (cos, sin)
+    uint16_t *kc, *vc;            // [L][Hkv][cap][128] bf16
+    int cap;
+    int pos;                      // absolute position of this step
+    const int *token_in;          // device token (embedding gathered on device) or null
+    int *token_out;               // device [1]
+    float *x;                     // [h] residual stream (holds the input embedding when token_in is null)
+    float *qkv;                   // [Hq*128 + 2*Hkv*128]
+    float *attn;                  // [Hq*128]
+    float *act;                   // [I]
+    float *part;                  // [Hq][splits][2 + 128] attention partials
+    unsigned *cnt;                // [Hkv] combine counters, zero between steps
+    int splits;                   // attention splits per kv head
+    float *hidden_out;            // nullable [h]
+    float *logits_out;            // nullable [V]
+    unsigned long long *best;     // argmax key, zero between steps
+    unsigned *bar;                // grid barrier counter
+    unsigned bar_base;            // counter value at kernel start
+    int *err;
+    int mask_eos;
+};
+
+// Number of grid barriers one decode step performs (host keeps the counter base).
+static inline unsigned qdb_step_barriers(int layers) { return 5u * (unsigned)layers + 1u; }
+
+#define QDB_STEP_THREADS 256
+
+extern "C" {
+// Launches one persistent step. grid = co-resident CTAs (one per SM).
+cudaError_t qdb_launch_step(const QdbStepArgs &a, int grid, cudaStream_t st);
+int qdb_step_max_grid(int device);
+int qdb_step_smem_bytes(const QdbDims &d);
+
+// RoPE table: tab[p][i] = (cos, sin) of (float)p * inv_freq[i], p < n_pos.
+cudaError_t qdb_launch_rope_table(float2 *tab, int n_pos, float theta, cudaStream_t st);
+
+// ---- row-batched path (prefill and multi-utterance decode) ----
+// Per-row KV target: the row's cache base pointers, capacity and position.
+struct QdbRowKV {
+    uint16_t *kc, *vc;
+    int cap, pos;
+};
+
+cudaError_t qdb_launch_rmsnorm_rows(const float *x, const float *w, float *out, int n, int h,
+                                    float eps, cudaStream_t st);
+// Y = X W^T with epilogue: 0 store [n,N], 1 add into Y [n,N], 2 SwiGLU pairs -> Y [n,N/2]
+cudaError_t qdb_launch_gemm_rows(const float *X, const uint16_t *W, float *Y, int n, int N, int K,
+                                 int mode, cudaStream_t st);
+// Per-row targets: row b writes position rows[b].pos + row_pos_offset.
+cudaError_t qdb_launch_qk_rope_append(const float *qkv, float *q_out, const QdbRowKV *rows,
+                                      int row_pos_offset, int layer, int n, int Hq, int Hkv,
+                                      const float *q_norm, const float *k_norm, const float2 *rope,
+                                      float eps, cudaStream_t st);
+// One session: row i writes position row0->pos + i.
+cudaError_t qdb_launch_qk_rope_append_single(const float *qkv, float *q_out, const QdbRowKV *row0,
+                                             int layer, int n, int Hq, int Hkv, const float *q_norm,
+                                             const float *k_norm, const float2 *rope, float eps,
+                                             cudaStream_t st);
+// Causal attention of n query rows of ONE session (rows at start_pos + i).
+cudaError_t qdb_launch_attn_prefill(const float *q, const uint16_t *kc, const uint16_t *vc, int cap,
+                                    int layer, int start_pos, int n, int Hq, int Hkv, float *out,
+                                    cudaStream_t st);
+// Independent rows (one query each) over per-row caches.
+cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
+                                 int n, int Hq, int Hkv, int splits, float *part, float *out,
+                                 cudaStream_t st);
+cudaError_t qdb_launch_argmax_rows(const float *logits, int n, int V, int mask_eos, int *tokens,
+                                   cudaStream_t st);
+cudaError_t qdb_launch_embed_rows(const uint16_t *embed, const int *tokens, float *x, int n, int h,
+                                  cudaStream_t st);
+}

@@ -1,0 +1,491 @@
+// qdb_rows.cu - row-batched decoder kernels: prefill of one utterance
+// (qwen_decoder_prefill, qwen_asr_decoder.c:262-359) and one decode step of
+// many independent utterances. Every row is one position; the weight matrix
+// is streamed once per launch for all rows.
+#include "qdb_common.cuh"
+#include "qdb_kernels.h"
+
+namespace {
+
+// ---------------------------------------------------------------- RMSNorm
+__global__ void rmsnorm_rows_kernel(const float *x, const float *w, float *out, int h, float eps) {
+    __shared__ float red[32];
+    const float *xr = x + (size_t)blockIdx.x * h;
+    float *orow = out + (size_t)blockIdx.x * h;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < h; i += blockDim.x) ss += xr[i] * xr[i];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float inv = 1.0f / sqrtf(red[0] / (float)h + eps);
+    for (int i = threadIdx.x; i < h; i += blockDim.x) orow[i] = xr[i] * inv * w[i];
+}
+
+// ---------------------------------------------------------------- GEMM
+// Y[n, N] (op)= X[n, K] (f32) * W[N, K]^T (bf16), f32 accumulation in
+// ascending k per output. Tile 64 rows x 128 weight rows x 32 k.
+constexpr int GB_M = 64, GB_N = 128, GB_K = 32;
+
+__global__ void __launch_bounds__(256) gemm_rows_kernel(const float *__restrict__ X,
+                                                        const uint16_t *__restrict__ W,
+                                                        float *__restrict__ Y, int n, int N, int K,
+                                                        int mode) {
+    __shared__ __align__(16) float As[GB_K][GB_M + 4];
+    __shared__ __align__(16) float Bs[GB_K][GB_N + 4];
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int m0 = blockIdx.y * GB_M, n0 = blockIdx.x * GB_N;
+    float acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) acc[i][j] = 0.f;
+
+    for (int k0 = 0; k0 < K; k0 += GB_K) {
+        // X tile: 64 x 32 floats, 2 float4 per thread
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int idx = tid + u * 256;  // 0..511 float4 slots
+            const int r = idx >> 3, c4 = (idx & 7) * 4;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (m0 + r < n) v = *reinterpret_cast<const float4 *>(X + (size_t)(m0 + r) * K + k0 + c4);
+            As[c4 + 0][r] = v.x;
+            As[c4 + 1][r] = v.y;
+            As[c4 + 2][r] = v.z;
+            As[c4 + 3][r] = v.w;
+        }
+        // W tile: 128 x 32 bf16, 2 uint4 per thread
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int idx = tid + u * 256;  // 0..511 uint4 slots
+            const int r = idx >> 2, c8 = (idx & 3) * 8;
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (n0 + r < N) v = ldg_stream(W + (size_t)(n0 + r) * K + k0 + c8);
+            Bs[c8 + 0][r] = bf16lo(v.x);
+            Bs[c8 + 1][r] = bf16hi(v.x);
+            Bs[c8 + 2][r] = bf16lo(v.y);
+            Bs[c8 + 3][r] = bf16hi(v.y);
+            Bs[c8 + 4][r] = bf16lo(v.z);
+            Bs[c8 + 5][r] = bf16hi(v.z);
+            Bs[c8 + 6][r] = bf16lo(v.w);
+            Bs[c8 + 7][r] = bf16hi(v.w);
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < GB_K; k++) {
+            const float4 a = *reinterpret_cast<const float4 *>(&As[k][ty * 4]);
+            const float4 b0 = *reinterpret_cast<const float4 *>(&Bs[k][tx * 8]);
+            const float4 b1 = *reinterpret_cast<const float4 *>(&Bs[k][tx * 8 + 4]);
+            const float av[4] = {a.x, a.y, a.z, a.w};
+            const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 8; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = m0 + ty * 4 + i;
+        if (r >= n) continue;
+        if (mode == 2) {
+            const int NO = N / 2;
+#pragma unroll
+            for (int p = 0; p < 4; p++) {
+                const int c = n0 + tx * 8 + 2 * p;
+                if (c + 1 < N) Y[(size_t)r * NO + c / 2] = silu_mul(acc[i][2 * p], acc[i][2 * p + 1]);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int c = n0 + tx * 8 + j;
+                if (c < N) {
+                    float *dst = Y + (size_t)r * N + c;
+                    *dst = mode == 1 ? *dst + acc[i][j] : acc[i][j];
+                }
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- Q/K norm, RoPE, KV append
+// One warp per (row, head slot). Slots: [0, Hq) query heads -> q_out,
+// [Hq, Hq+Hkv) key heads -> cache K, [Hq+Hkv, Hq+2Hkv) value heads -> cache V.
+__global__ void qk_rope_append_kernel(const float *qkv, float *q_out, const QdbRowKV *rows, int n_rowkv,
+                                      int row_pos_offset, int layer, int n, int Hq, int Hkv,
+                                      const float *q_norm, const float *k_norm, const float2 *rope, float eps) {
+    const int lane = threadIdx.x & 31;
+    const int slot = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int row = blockIdx.x;
+    if (slot >= Hq + 2 * Hkv || row >= n) return;
+    const bool single = (n_rowkv == 1);
+    const QdbRowKV rk = rows[single ? 0 : row];
+    const int pos = rk.pos + (single ? row : 0) + row_pos_offset;
+    const int width = (Hq + 2 * Hkv) * QDB_HD;
+    const float *src = qkv + (size_t)row * width + (size_t)slot * QDB_HD;
+    float e[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) e[i] = src[lane + 32 * i];
+    if (slot < Hq + Hkv) {
+        const float *w = slot < Hq ? q_norm : k_norm;
+        float ss = warp_sum(e[0] * e[0] + e[1] * e[1] + e[2] * e[2] + e[3] * e[3]);
+        const float inv = 1.0f / sqrtf(ss / (float)QDB_HD + eps);
+#pragma unroll
+        for (int i = 0; i < 4; i++) e[i] = e[i] * inv * w[lane + 32 * i];
+        const float2 *rr = rope + (size_t)pos * (QDB_HD / 2);
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const float2 cs = rr[lane + 32 * i];
+            const float x1 = e[i], x2 = e[i + 2];
+            e[i] = x1 * cs.x - x2 * cs.y;
+            e[i + 2] = x2 * cs.x + x1 * cs.y;
+        }
+    }
+    if (slot < Hq) {
+        float *dst = q_out + (size_t)row * Hq * QDB_HD + (size_t)slot * QDB_HD;
+#pragma unroll
+        for (int i = 0; i < 4; i++) dst[lane + 32 * i] = e[i];
+    } else {
+        const bool is_k = slot < Hq + Hkv;
+        const int g = is_k ? slot - Hq : slot - Hq - Hkv;
+        uint16_t *base = is_k ? rk.kc : rk.vc;
+        uint16_t *dst = base + (((size_t)layer * Hkv + g) * (size_t)rk.cap + pos) * QDB_HD;
+#pragma unroll
+        for (int i = 0; i < 4; i++) dst[lane + 32 * i] = f32_to_bf16_rn(e[i]);
+    }
+}
+
+// ---------------------------------------------------------------- prefill attention
+// Causal GQA attention for n query rows of one session at positions
+// start_pos + i over keys [0, start_pos + i] (qwen_causal_attention with
+// q_offset = start_pos, qwen_asr_kernels.c:1050-1141). CTA = (query tile of
+// AQ rows, KV head g); its R*AQ query vectors share each K/V tile in smem.
+// Online softmax per query row over 64-key tiles.
+constexpr int AQ = 16;   // query rows per CTA
+constexpr int AK = 64;   // keys per tile
+
+template <int R>
+__global__ void __launch_bounds__(256) attn_prefill_kernel(const float *q, const uint16_t *kc, const uint16_t *vc,
+                                                           int cap, int layer, int start_pos, int n, int Hq,
+                                                           int Hkv, float *out) {
+    constexpr int NQ = R * AQ;         // query vectors per CTA
+    constexpr int TPQ = 256 / NQ;      // threads per query vector
+    extern __shared__ __align__(16) float sm[];
+    float *Qs = sm;                            // [NQ][128]
+    float *Ks = Qs + NQ * QDB_HD;              // [AK][129]
+    float *Vs = Ks + AK * (QDB_HD + 1);        // [AK][128]
+    float *Ps = Vs + AK * QDB_HD;              // [NQ][AK]
+    const int tid = threadIdx.x;
+    const int g = blockIdx.y;
+    const int i0 = blockIdx.x * AQ;
+    const int qv = tid / TPQ, sub = tid % TPQ;  // this thread's query vector and lane within it
+    const int qi = qv / R, hh = qv % R;         // row within tile, head within group
+    const int row = i0 + qi;
+    const bool row_ok = row < n;
+    const int qpos = start_pos + row;
+    const float scale = 1.0f / sqrtf((float)QDB_HD);
+
+    for (int t = tid; t < NQ * QDB_HD; t += 256) {
+        const int v = t / QDB_HD, dd = t % QDB_HD;
+        const int r = i0 + v / R, h = g * R + v % R;
+        Qs[t] = r < n ? q[(size_t)r * Hq * QDB_HD + (size_t)h * QDB_HD + dd] : 0.f;
+    }
+    constexpr int DPT = QDB_HD / TPQ;   // output dims per thread
+    constexpr int KPT = AK / TPQ;       // keys per thread per tile
+    float o[DPT];
+#pragma unroll
+    for (int e = 0; e < DPT; e++) o[e] = 0.f;
+    float m = -INFINITY, l = 0.f;
+
+    const size_t head_base = ((size_t)layer * Hkv + g) * (size_t)cap * QDB_HD;
+    const int last_row = min(n, i0 + AQ) - 1;
+    const int kend = start_pos + last_row + 1;  // keys needed by this tile
+    for (int k0 = 0; k0 < kend; k0 += AK) {
+        __syncthreads();
+        for (int t = tid; t < AK * QDB_HD / 8; t += 256) {
+            const int kr = t / (QDB_HD / 8), c8 = (t % (QDB_HD / 8)) * 8;
+            uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+            if (k0 + kr < kend) {
+                kv = *reinterpret_cast<const uint4 *>(kc + head_base + (size_t)(k0 + kr) * QDB_HD + c8);
+                vv = *reinterpret_cast<const uint4 *>(vc + head_base + (size_t)(k0 + kr) * QDB_HD + c8);
+            }
+            float *kd = Ks + kr * (QDB_HD + 1) + c8;
+            kd[0] = bf16lo(kv.x); kd[1] = bf16hi(kv.x); kd[2] = bf16lo(kv.y); kd[3] = bf16hi(kv.y);
+            kd[4] = bf16lo(kv.z); kd[5] = bf16hi(kv.z); kd[6] = bf16lo(kv.w); kd[7] = bf16hi(kv.w);
+            float *vd = Vs + kr * QDB_HD + c8;
+            vd[0] = bf16lo(vv.x); vd[1] = bf16hi(vv.x); vd[2] = bf16lo(vv.y); vd[3] = bf16hi(vv.y);
+            vd[4] = bf16lo(vv.z); vd[5] = bf16hi(vv.z); vd[6] = bf16lo(vv.w); vd[7] = bf16hi(vv.w);
+        }
+        __syncthreads();
+        // scores for keys sub, sub+TPQ, ... of this tile
+        float sc[KPT];
+        float cmax = -INFINITY;
+        const float *qrow = Qs + qv * QDB_HD;
+#pragma unroll
+        for (int u = 0; u < KPT; u++) {
+            const int kr = sub + u * TPQ;
+            const float *krow = Ks + kr * (QDB_HD + 1);
+            float acc = 0.f;
+#pragma unroll 16
+            for (int dd = 0; dd < QDB_HD; dd++) acc = fmaf(qrow[dd], krow[dd], acc);
+            const bool ok = row_ok && (k0 + kr <= qpos);
+            sc[u] = ok ? acc * scale : -INFINITY;
+            cmax = fmaxf(cmax, sc[u]);
+        }
+#pragma unroll
+        for (int off = TPQ / 2; off > 0; off >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, off));
+        const float mn = fmaxf(m, cmax);
+        float psum = 0.f;
+#pragma unroll
+        for (int u = 0; u < KPT; u++) {
+            const float p = (sc[u] == -INFINITY) ? 0.f : expf(sc[u] - mn);
+            Ps[qv * AK + sub + u * TPQ] = p;
+            psum += p;
+        }
+#pragma unroll
+        for (int off = TPQ / 2; off > 0; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
+        const float corr = (m == -INFINITY) ? 0.f : expf(m - mn);
+        if (mn != -INFINITY) {
+            l = l * corr + psum;
+            m = mn;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int e = 0; e < DPT; e++) o[e] *= (mn != -INFINITY ? corr : 1.f);
+        for (int kr = 0; kr < AK; kr++) {
+            const float p = Ps[qv * AK + kr];
+            const float *vrow = Vs + kr * QDB_HD + sub * DPT;
+#pragma unroll
+            for (int e = 0; e < DPT; e++) o[e] = fmaf(p, vrow[e], o[e]);
+        }
+    }
+    if (row_ok) {
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
+        float *dst = out + (size_t)row * Hq * QDB_HD + (size_t)(g * R + hh) * QDB_HD + sub * DPT;
+#pragma unroll
+        for (int e = 0; e < DPT; e++) dst[e] = o[e] * inv;
+    }
+}
+
+// ---------------------------------------------------------------- independent-row attention
+// Unit = (row, KV head g, split s), one warp per query head of the group,
+// keys [p0, p1) of ctx = pos + 1; partial (m, l, o[128]) per query head.
+__global__ void attn_rows_partial_kernel(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
+                                         int Hq, int Hkv, int S, float *part) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int R = Hq / Hkv;
+    const int row = blockIdx.x / Hkv, g = blockIdx.x % Hkv, s = blockIdx.y;
+    if (w >= R) return;
+    const QdbRowKV rk = rows[row];
+    const int pos = rk.pos + row_pos_offset;
+    const int ctx = pos + 1;
+    const int per = (ctx + S - 1) / S;
+    const int p0 = s * per, p1 = min(ctx, p0 + per);
+    const int h = g * R + w;
+    const float *qv = q + (size_t)row * Hq * QDB_HD + (size_t)h * QDB_HD;
+    float qr[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) qr[i] = qv[lane * 4 + i];
+    const size_t head_base = ((size_t)layer * Hkv + g) * (size_t)rk.cap * QDB_HD;
+    const uint16_t *kc = rk.kc + head_base, *vc = rk.vc + head_base;
+    const float scale = 1.0f / sqrtf((float)QDB_HD);
+    float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int j0 = p0; j0 < p1; j0 += 8) {
+        uint2 kk[8], vv[8];
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+            if (j0 + t < p1) {
+                kk[t] = *reinterpret_cast<const uint2 *>(kc + (size_t)(j0 + t) * QDB_HD + lane * 4);
+                vv[t] = *reinterpret_cast<const uint2 *>(vc + (size_t)(j0 + t) * QDB_HD + lane * 4);
+            } else {
+                kk[t] = make_uint2(0u, 0u);
+                vv[t] = kk[t];
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < 8; t++) {
+            if (j0 + t >= p1) break;
+            float sc = qr[0] * bf16lo(kk[t].x) + qr[1] * bf16hi(kk[t].x) + qr[2] * bf16lo(kk[t].y) +
+                       qr[3] * bf16hi(kk[t].y);
+            sc = warp_sum(sc) * scale;
+            if (sc > m) {
+                const float corr = expf(m - sc);
+                l = l * corr + 1.f;
+                o[0] = o[0] * corr + bf16lo(vv[t].x);
+                o[1] = o[1] * corr + bf16hi(vv[t].x);
+                o[2] = o[2] * corr + bf16lo(vv[t].y);
+                o[3] = o[3] * corr + bf16hi(vv[t].y);
+                m = sc;
+            } else {
+                const float p = expf(sc - m);
+                l += p;
+                o[0] = fmaf(p, bf16lo(vv[t].x), o[0]);
+                o[1] = fmaf(p, bf16hi(vv[t].x), o[1]);
+                o[2] = fmaf(p, bf16lo(vv[t].y), o[2]);
+                o[3] = fmaf(p, bf16hi(vv[t].y), o[3]);
+            }
+        }
+    }
+    float *dst = part + (((size_t)row * Hq + h) * S + s) * (2 + QDB_HD);
+    if (lane == 0) {
+        dst[0] = m;
+        dst[1] = l;
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) dst[2 + lane * 4 + i] = o[i];
+}
+
+__global__ void attn_rows_merge_kernel(const float *part, int S, int Hq, float *out) {
+    const int row = blockIdx.x, h = blockIdx.y, dd = threadIdx.x;
+    const float *src = part + ((size_t)row * Hq + h) * S * (2 + QDB_HD);
+    float M = -INFINITY;
+    for (int s = 0; s < S; s++) M = fmaxf(M, src[s * (2 + QDB_HD)]);
+    float L = 0.f, O = 0.f;
+    for (int s = 0; s < S; s++) {
+        const float ms = src[s * (2 + QDB_HD)];
+        if (ms == -INFINITY) continue;
+        const float f = expf(ms - M);
+        L += src[s * (2 + QDB_HD) + 1] * f;
+        O += src[s * (2 + QDB_HD) + 2 + dd] * f;
+    }
+    out[(size_t)row * Hq * QDB_HD + (size_t)h * QDB_HD + dd] = L > 0.f ? O / L : 0.f;
+}
+
+// ---------------------------------------------------------------- argmax / embed
+__global__ void argmax_rows_kernel(const float *logits, int V, int mask_eos, int *tokens) {
+    __shared__ unsigned long long red[32];
+    const float *lr = logits + (size_t)blockIdx.x * V;
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        if (mask_eos && (i == QDB_ENDOFTEXT || i == QDB_IM_END)) continue;
+        const float v = lr[i];
+        if (isnan(v)) continue;
+        const unsigned long long k = argmax_key(v, i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+        best = t > best ? t : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        best = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0ull;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+            best = t > best ? t : best;
+        }
+        if (threadIdx.x == 0) tokens[blockIdx.x] = argmax_key_index(best);
+    }
+}
+
+__global__ void embed_rows_kernel(const uint16_t *embed, const int *tokens, float *x, int h) {
+    const int row = blockIdx.x;
+    const uint16_t *src = embed + (size_t)tokens[row] * h;
+    for (int i = threadIdx.x; i < h; i += blockDim.x) x[(size_t)row * h + i] = __uint_as_float(((uint32_t)src[i]) << 16);
+}
+
+}  // namespace
+
+extern "C" cudaError_t qdb_launch_rmsnorm_rows(const float *x, const float *w, float *out, int n, int h, float eps,
+                                               cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    rmsnorm_rows_kernel<<<n, 256, 0, st>>>(x, w, out, h, eps);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t qdb_launch_gemm_rows(const float *X, const uint16_t *W, float *Y, int n, int N, int K, int mode,
+                                            cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    if (K % GB_K) return cudaErrorInvalidValue;
+    dim3 grid((N + GB_N - 1) / GB_N, (n + GB_M - 1) / GB_M);
+    gemm_rows_kernel<<<grid, 256, 0, st>>>(X, W, Y, n, N, K, mode);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t qdb_launch_qk_rope_append(const float *qkv, float *q_out, const QdbRowKV *rows, int row_pos_offset,
+                                                 int layer, int n, int Hq, int Hkv, const float *q_norm,
+                                                 const float *k_norm, const float2 *rope, float eps,
+                                                 cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const int slots = Hq + 2 * Hkv;
+    dim3 grid(n, (slots + 3) / 4);
+    // n_rowkv: callers pass a single-entry array for one session (rows[0].pos is the first row's position)
+    qk_rope_append_kernel<<<grid, 128, 0, st>>>(qkv, q_out, rows, 0, row_pos_offset, layer, n, Hq, Hkv, q_norm,
+                                                k_norm, rope, eps);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t qdb_launch_qk_rope_append_single(const float *qkv, float *q_out, const QdbRowKV *row0,
+                                                        int layer, int n, int Hq, int Hkv, const float *q_norm,
+                                                        const float *k_norm, const float2 *rope, float eps,
+                                                        cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const int slots = Hq + 2 * Hkv;
+    dim3 grid(n, (slots + 3) / 4);
+    qk_rope_append_kernel<<<grid, 128, 0, st>>>(qkv, q_out, row0, 1, 0, layer, n, Hq, Hkv, q_norm, k_norm, rope,
+                                                eps);
+    return cudaGetLastError();
+}
+
+template <int R>
+static cudaError_t attn_prefill_r(const float *q, const uint16_t *kc, const uint16_t *vc, int cap, int layer,
+                                  int start_pos, int n, int Hq, int Hkv, float *out, cudaStream_t st) {
+    constexpr int NQ = R * AQ;
+    const size_t smem = sizeof(float) * (NQ * QDB_HD + AK * (QDB_HD + 1) + AK * QDB_HD + NQ * AK);
+    cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((n + AQ - 1) / AQ, Hkv);
+    attn_prefill_kernel<R><<<grid, 256, smem, st>>>(q, kc, vc, cap, layer, start_pos, n, Hq, Hkv, out);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t qdb_launch_attn_prefill(const float *q, const uint16_t *kc, const uint16_t *vc, int cap,
+                                               int layer, int start_pos, int n, int Hq, int Hkv, float *out,
+                                               cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    switch (Hq / Hkv) {
+        case 1: return attn_prefill_r<1>(q, kc, vc, cap, layer, start_pos, n, Hq, Hkv, out, st);
+        case 2: return attn_prefill_r<2>(q, kc, vc, cap, layer, start_pos, n, Hq, Hkv, out, st);
+        case 4: return attn_prefill_r<4>(q, kc, vc, cap, layer, start_pos, n, Hq, Hkv, out, st);
+        case 8: return attn_prefill_r<8>(q, kc, vc, cap, layer, start_pos, n, Hq, Hkv, out, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+extern "C" cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
+                                            int n, int Hq, int Hkv, int S, float *part, float *out,
+                                            cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    const int R = Hq / Hkv;
+    dim3 grid(n * Hkv, S);
+    attn_rows_partial_kernel<<<grid, 32 * R, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    attn_rows_merge_kernel<<<dim3(n, Hq), QDB_HD, 0, st>>>(part, S, Hq, out);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t qdb_launch_argmax_rows(const float *logits, int n, int V, int mask_eos, int *tokens,
+                                              cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    argmax_rows_kernel<<<n, 1024, 0, st>>>(logits, V, mask_eos, tokens);
+    return cudaGetLastError();
+}
+
+extern "C" cudaError_t qdb_launch_embed_rows(const uint16_t *embed, const int *tokens, float *x, int n, int h,
+                                             cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    embed_rows_kernel<<<n, 256, 0, st>>>(embed, tokens, x, h);
+    return cudaGetLastError();
+}

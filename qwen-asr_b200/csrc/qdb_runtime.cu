@@ -1,0 +1,628 @@
+// qdb_runtime.cu - host runtime behind the C ABI in include/qwen_asr_b200.h:
+// device weight upload, per-utterance KV sessions, launch sequencing on the
+// model's stream. Replaces the decoder's host-side state handling of the
+// reference (qwen_asr_decoder.c: load :45-116, KV cache :122-170, prefill
+// :262-359, forward :388-476).
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/qwen_asr_b200.h"
+#include "qdb_kernels.h"
+
+#define QDB_HD 128  // head_dim (the kernels support only this)
+
+static thread_local std::string g_err;
+
+static int fail(const char *fmt, ...) __attribute__((format(printf, 1, 2)));
+static int fail(const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return -1;
+}
+
+#define CK(call)                                                                              \
+    do {                                                                                      \
+        cudaError_t e_ = (call);                                                              \
+        if (e_ != cudaSuccess) return fail("%s: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                                           __FILE__, __LINE__);                              \
+    } while (0)
+
+template <typename T>
+static int dev_alloc(T **p, size_t count) {
+    *p = nullptr;
+    if (count == 0) count = 1;
+    cudaError_t e = cudaMalloc((void **)p, count * sizeof(T));
+    if (e != cudaSuccess) return fail("cudaMalloc(%zu bytes): %s", count * sizeof(T), cudaGetErrorString(e));
+    return 0;
+}
+
+struct RowScratch {
+    int cap = 0;
+    float *X = nullptr, *XN = nullptr, *QKV = nullptr, *Q = nullptr, *ATT = nullptr, *ACT = nullptr;
+    float *LOG = nullptr;  // [cap, V] only for batched decode
+    int log_cap = 0;
+    float *part = nullptr;
+    size_t part_cap = 0;
+    QdbRowKV *rowkv = nullptr;
+    int rowkv_cap = 0;
+    int *tok = nullptr;
+    size_t tok_cap = 0;
+};
+
+struct qdb_model {
+    qdb_config cfg;
+    QdbDims d;
+    int device = 0;
+    int sms = 0;
+    cudaStream_t st = nullptr;
+    int qd = 0, kvd = 0;
+
+    uint16_t *w = nullptr;  // all layer matrices
+    size_t layer_elems = 0, off_qkv = 0, off_o = 0, off_gu = 0, off_down = 0;
+    float *norms = nullptr;  // per layer: in[h], post[h], q[128], k[128]
+    size_t norm_stride = 0;
+    uint16_t *embed = nullptr;
+    float *final_norm = nullptr;
+    QdbLayerW *layers_dev = nullptr;
+    std::vector<QdbLayerW> layers_host;
+    std::vector<char> layer_set;
+    bool embed_set = false;
+    bool finalized = false;
+    int mask_eos = 0;
+
+    float2 *rope = nullptr;
+    int rope_cap = 0;
+
+    // single-utterance step scratch
+    float *x = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *part = nullptr;
+    float *hidden_dev = nullptr, *logits_dev = nullptr;
+    unsigned *cnt = nullptr, *bar = nullptr;
+    unsigned bar_base = 0;
+    unsigned long long *best = nullptr;
+    int *err = nullptr;
+    int *tok_dev = nullptr;
+    int tok_cap = 0;
+    int max_splits = 1;
+    float *h_stage = nullptr;  // pinned [max(h, V)]
+    int *h_tok = nullptr;      // pinned
+    RowScratch rs;
+};
+
+struct qdb_session {
+    qdb_model *m;
+    uint16_t *kc = nullptr, *vc = nullptr;
+    int cap = 0;
+};
+
+extern "C" const char *qdb_last_error(void) { return g_err.c_str(); }
+
+extern "C" int qdb_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+static int set_dev(qdb_model *m) {
+    CK(cudaSetDevice(m->device));
+    return 0;
+}
+
+static int ensure_rope(qdb_model *m, int n_pos) {
+    if (n_pos <= m->rope_cap) return 0;
+    int cap = m->rope_cap ? m->rope_cap : 4096;
+    while (cap < n_pos) cap *= 2;
+    float2 *t = nullptr;
+    if (dev_alloc(&t, (size_t)cap * (QDB_HD / 2))) return -1;
+    CK(qdb_launch_rope_table(t, cap, m->cfg.theta, m->st));
+    CK(cudaStreamSynchronize(m->st));
+    if (m->rope) cudaFree(m->rope);
+    m->rope = t;
+    m->rope_cap = cap;
+    return 0;
+}
+
+extern "C" qdb_model *qdb_model_create(const qdb_config *cfg, int device) {
+    g_err.clear();
+    if (!cfg) { fail("null config"); return nullptr; }
+    if (cfg->head_dim != QDB_HD) { fail("head_dim must be %d (got %d)", QDB_HD, cfg->head_dim); return nullptr; }
+    if (cfg->hidden <= 0 || cfg->hidden % 256 || cfg->intermediate <= 0 || cfg->intermediate % 256) {
+        fail("hidden and intermediate must be positive multiples of 256");
+        return nullptr;
+    }
+    if (cfg->kv_heads <= 0 || cfg->heads % cfg->kv_heads) { fail("heads must be a multiple of kv_heads"); return nullptr; }
+    const int R = cfg->heads / cfg->kv_heads;
+    if (R != 1 && R != 2 && R != 4 && R != 8) { fail("heads/kv_heads must be 1, 2, 4 or 8"); return nullptr; }
+    if (cfg->layers <= 0 || cfg->vocab <= 0) { fail("bad layers/vocab"); return nullptr; }
+    if (cfg->heads * QDB_HD % 256) { fail("heads*head_dim must be a multiple of 256"); return nullptr; }
+    int ndev = qdb_device_count();
+    if (device < 0 || device >= ndev) { fail("CUDA device %d not available (%d visible)", device, ndev); return nullptr; }
+
+    qdb_model *m = new qdb_model();
+    m->cfg = *cfg;
+    m->device = device;
+    m->d = QdbDims{cfg->hidden, cfg->layers, cfg->heads, cfg->kv_heads, cfg->intermediate, cfg->vocab, cfg->eps};
+    m->qd = cfg->heads * QDB_HD;
+    m->kvd = cfg->kv_heads * QDB_HD;
+    auto bad = [&]() { qdb_model_free(m); return (qdb_model *)nullptr; };
+    if (set_dev(m)) return bad();
+    if (cudaStreamCreateWithFlags(&m->st, cudaStreamNonBlocking) != cudaSuccess) { fail("stream create"); return bad(); }
+    m->sms = qdb_step_max_grid(device);
+
+    const size_t h = cfg->hidden, I = cfg->intermediate;
+    auto al = [](size_t e) { return (e + 127) & ~(size_t)127; };  // 256-byte aligned offsets
+    m->off_qkv = 0;
+    m->off_o = m->off_qkv + al((m->qd + 2 * m->kvd) * h);
+    m->off_gu = m->off_o + al(h * m->qd);
+    m->off_down = m->off_gu + al(2 * I * h);
+    m->layer_elems = m->off_down + al(h * I);
+    if (dev_alloc(&m->w, m->layer_elems * cfg->layers)) return bad();
+    m->norm_stride = al(2 * h + 2 * QDB_HD);
+    if (dev_alloc(&m->norms, m->norm_stride * cfg->layers)) return bad();
+    if (dev_alloc(&m->embed, (size_t)cfg->vocab * h)) return bad();
+    if (dev_alloc(&m->final_norm, h)) return bad();
+    m->layers_host.resize(cfg->layers);
+    m->layer_set.assign(cfg->layers, 0);
+    for (int l = 0; l < cfg->layers; l++) {
+        uint16_t *b = m->w + m->layer_elems * l;
+        float *nb = m->norms + m->norm_stride * l;
+        m->layers_host[l] = QdbLayerW{b + m->off_qkv, b + m->off_o, b + m->off_gu, b + m->off_down,
+                                      nb + 2 * h, nb + 2 * h + QDB_HD, nb, nb + h};
+    }
+    if (dev_alloc(&m->layers_dev, cfg->layers)) return bad();
+    if (cudaMemcpy(m->layers_dev, m->layers_host.data(), sizeof(QdbLayerW) * cfg->layers,
+                   cudaMemcpyHostToDevice) != cudaSuccess) { fail("layer table upload"); return bad(); }
+
+    // step scratch
+    m->max_splits = m->sms / cfg->kv_heads;
+    if (m->max_splits < 1) m->max_splits = 1;
+    if (dev_alloc(&m->x, h) || dev_alloc(&m->qkv, m->qd + 2 * m->kvd) || dev_alloc(&m->attn, m->qd) ||
+        dev_alloc(&m->act, I) || dev_alloc(&m->part, (size_t)cfg->heads * m->max_splits * (2 + QDB_HD)) ||
+        dev_alloc(&m->hidden_dev, h) || dev_alloc(&m->logits_dev, cfg->vocab) || dev_alloc(&m->cnt, cfg->kv_heads) ||
+        dev_alloc(&m->bar, 1) || dev_alloc(&m->best, 1) || dev_alloc(&m->err, 1))
+        return bad();
+    if (cudaMemset(m->cnt, 0, sizeof(unsigned) * cfg->kv_heads) != cudaSuccess ||
+        cudaMemset(m->bar, 0, sizeof(unsigned)) != cudaSuccess ||
+        cudaMemset(m->best, 0, sizeof(unsigned long long)) != cudaSuccess ||
+        cudaMemset(m->err, 0, sizeof(int)) != cudaSuccess) { fail("scratch memset"); return bad(); }
+    size_t stage = h > (size_t)cfg->vocab ? h : (size_t)cfg->vocab;
+    if (cudaMallocHost((void **)&m->h_stage, stage * sizeof(float)) != cudaSuccess ||
+        cudaMallocHost((void **)&m->h_tok, sizeof(int) * 4096) != cudaSuccess) { fail("pinned alloc"); return bad(); }
+    if (ensure_rope(m, 4096)) return bad();
+    return m;
+}
+
+extern "C" void qdb_model_free(qdb_model *m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->st) cudaStreamSynchronize(m->st);
+    cudaFree(m->w); cudaFree(m->norms); cudaFree(m->embed); cudaFree(m->final_norm); cudaFree(m->layers_dev);
+    cudaFree(m->rope); cudaFree(m->x); cudaFree(m->qkv); cudaFree(m->attn); cudaFree(m->act); cudaFree(m->part);
+    cudaFree(m->hidden_dev); cudaFree(m->logits_dev); cudaFree(m->cnt); cudaFree(m->bar); cudaFree(m->best);
+    cudaFree(m->err); cudaFree(m->tok_dev);
+    RowScratch &r = m->rs;
+    cudaFree(r.X); cudaFree(r.XN); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT); cudaFree(r.LOG);
+    cudaFree(r.part); cudaFree(r.rowkv); cudaFree(r.tok);
+    if (m->h_stage) cudaFreeHost(m->h_stage);
+    if (m->h_tok) cudaFreeHost(m->h_tok);
+    if (m->st) cudaStreamDestroy(m->st);
+    delete m;
+}
+
+extern "C" int qdb_model_set_embed(qdb_model *m, const uint16_t *embed, const float *final_norm) {
+    g_err.clear();
+    if (!m || !embed || !final_norm) return fail("null argument");
+    if (set_dev(m)) return -1;
+    const size_t h = m->cfg.hidden;
+    CK(cudaMemcpy(m->embed, embed, (size_t)m->cfg.vocab * h * 2, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(m->final_norm, final_norm, h * 4, cudaMemcpyHostToDevice));
+    m->embed_set = true;
+    return 0;
+}
+
+extern "C" int qdb_model_set_layer(qdb_model *m, int layer, const uint16_t *wq, const uint16_t *wk,
+                                   const uint16_t *wv, const uint16_t *wo, const uint16_t *gate,
+                                   const uint16_t *up, const uint16_t *down, const float *q_norm,
+                                   const float *k_norm, const float *input_norm, const float *post_attn_norm) {
+    g_err.clear();
+    if (!m) return fail("null model");
+    if (layer < 0 || layer >= m->cfg.layers) return fail("layer %d out of range", layer);
+    if (!wq || !wk || !wv || !wo || !gate || !up || !down || !q_norm || !k_norm || !input_norm || !post_attn_norm)
+        return fail("null weight pointer for layer %d", layer);
+    if (set_dev(m)) return -1;
+    const size_t h = m->cfg.hidden, I = m->cfg.intermediate, qd = m->qd, kvd = m->kvd;
+    uint16_t *b = m->w + m->layer_elems * layer;
+    CK(cudaMemcpy(b + m->off_qkv, wq, qd * h * 2, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(b + m->off_qkv + qd * h, wk, kvd * h * 2, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(b + m->off_qkv + (qd + kvd) * h, wv, kvd * h * 2, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(b + m->off_o, wo, h * qd * 2, cudaMemcpyHostToDevice));
+    // gate row j -> fused row 2j, up row j -> fused row 2j+1
+    CK(cudaMemcpy2D(b + m->off_gu, 4 * h, gate, 2 * h, 2 * h, I, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy2D(b + m->off_gu + h, 4 * h, up, 2 * h, 2 * h, I, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(b + m->off_down, down, h * I * 2, cudaMemcpyHostToDevice));
+    float *nb = m->norms + m->norm_stride * layer;
+    CK(cudaMemcpy(nb, input_norm, h * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(nb + h, post_attn_norm, h * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(nb + 2 * h, q_norm, QDB_HD * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(nb + 2 * h + QDB_HD, k_norm, QDB_HD * 4, cudaMemcpyHostToDevice));
+    m->layer_set[layer] = 1;
+    return 0;
+}
+
+extern "C" int qdb_model_finalize(qdb_model *m) {
+    g_err.clear();
+    if (!m) return fail("null model");
+    if (!m->embed_set) return fail("embedding / final norm not set");
+    for (int l = 0; l < m->cfg.layers; l++)
+        if (!m->layer_set[l]) return fail("layer %d not set", l);
+    if (set_dev(m)) return -1;
+    CK(cudaDeviceSynchronize());
+    m->finalized = true;
+    return 0;
+}
+
+extern "C" int qdb_model_set_mask_eos(qdb_model *m, int enable) {
+    if (!m) return fail("null model");
+    m->mask_eos = enable ? 1 : 0;
+    return 0;
+}
+
+extern "C" void *qdb_model_stream(qdb_model *m) { return m ? (void *)m->st : nullptr; }
+
+extern "C" int qdb_model_sync(qdb_model *m) {
+    if (!m) return fail("null model");
+    if (set_dev(m)) return -1;
+    CK(cudaStreamSynchronize(m->st));
+    return 0;
+}
+
+// ------------------------------------------------------------------ sessions
+extern "C" qdb_session *qdb_session_create(qdb_model *m, int initial_capacity) {
+    g_err.clear();
+    if (!m || !m->finalized) { fail("model missing or not finalized"); return nullptr; }
+    qdb_session *s = new qdb_session();
+    s->m = m;
+    if (qdb_session_reserve(s, initial_capacity > 0 ? initial_capacity : 1024)) {
+        delete s;
+        return nullptr;
+    }
+    return s;
+}
+
+extern "C" void qdb_session_free(qdb_session *s) {
+    if (!s) return;
+    cudaSetDevice(s->m->device);
+    cudaStreamSynchronize(s->m->st);
+    cudaFree(s->kc);
+    cudaFree(s->vc);
+    delete s;
+}
+
+extern "C" int qdb_session_capacity(const qdb_session *s) { return s ? s->cap : 0; }
+
+// Grows the cache (doubling, like kv_cache_grow, qwen_asr_decoder.c:133-160)
+// and keeps the first `cap` positions of every (layer, kv head) block.
+extern "C" int qdb_session_reserve(qdb_session *s, int positions) {
+    if (!s) return fail("null session");
+    if (positions <= s->cap) return 0;
+    qdb_model *m = s->m;
+    if (set_dev(m)) return -1;
+    int cap = s->cap ? s->cap : 256;
+    while (cap < positions) cap *= 2;
+    const size_t blocks = (size_t)m->cfg.layers * m->cfg.kv_heads;
+    const size_t row = QDB_HD * 2;
+    uint16_t *kc = nullptr, *vc = nullptr;
+    if (dev_alloc(&kc, blocks * cap * QDB_HD)) return -1;
+    if (dev_alloc(&vc, blocks * cap * QDB_HD)) { cudaFree(kc); return -1; }
+    if (s->cap) {
+        CK(cudaMemcpy2DAsync(kc, cap * row, s->kc, s->cap * row, s->cap * row, blocks, cudaMemcpyDeviceToDevice, m->st));
+        CK(cudaMemcpy2DAsync(vc, cap * row, s->vc, s->cap * row, s->cap * row, blocks, cudaMemcpyDeviceToDevice, m->st));
+        CK(cudaStreamSynchronize(m->st));
+        cudaFree(s->kc);
+        cudaFree(s->vc);
+    }
+    s->kc = kc;
+    s->vc = vc;
+    s->cap = cap;
+    return ensure_rope(m, cap);
+}
+
+// ------------------------------------------------------------------ single-utterance step
+static int check_err(qdb_model *m) {
+    int e = 0;
+    CK(cudaMemcpy(&e, m->err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) {
+        cudaMemset(m->err, 0, sizeof(int));
+        cudaMemset(m->bar, 0, sizeof(unsigned));
+        cudaMemset(m->cnt, 0, sizeof(unsigned) * m->cfg.kv_heads);
+        cudaMemset(m->best, 0, sizeof(unsigned long long));
+        m->bar_base = 0;
+        return fail("device error code %d (grid barrier wait ran out)", e);
+    }
+    return 0;
+}
+
+static QdbStepArgs step_args(qdb_session *s, int pos) {
+    qdb_model *m = s->m;
+    QdbStepArgs a;
+    memset(&a, 0, sizeof(a));
+    a.d = m->d;
+    a.layers = m->layers_dev;
+    a.embed = m->embed;
+    a.final_norm = m->final_norm;
+    a.rope = m->rope;
+    a.kc = s->kc;
+    a.vc = s->vc;
+    a.cap = s->cap;
+    a.pos = pos;
+    a.x = m->x;
+    a.qkv = m->qkv;
+    a.attn = m->attn;
+    a.act = m->act;
+    a.part = m->part;
+    a.cnt = m->cnt;
+    const int ctx = pos + 1;
+    int S = (ctx + 31) / 32;
+    if (S > m->max_splits) S = m->max_splits;
+    if (S < 1) S = 1;
+    a.splits = S;
+    a.best = m->best;
+    a.bar = m->bar;
+    a.err = m->err;
+    a.mask_eos = m->mask_eos;
+    return a;
+}
+
+static int launch_step(qdb_model *m, QdbStepArgs &a) {
+    a.bar_base = m->bar_base;
+    CK(qdb_launch_step(a, m->sms, m->st));
+    m->bar_base += qdb_step_barriers(m->cfg.layers) * (unsigned)m->sms;
+    return 0;
+}
+
+static int prep_pos(qdb_session *s, int last_pos) {
+    if (qdb_session_reserve(s, last_pos + 1)) return -1;
+    return ensure_rope(s->m, last_pos + 1);
+}
+
+extern "C" int qdb_forward(qdb_session *s, const float *embed, int pos, float *hidden_out, float *logits_out) {
+    g_err.clear();
+    if (!s || !embed) return fail("null argument");
+    if (pos < 0) return fail("negative position");
+    qdb_model *m = s->m;
+    if (set_dev(m) || prep_pos(s, pos)) return -1;
+    const size_t h = m->cfg.hidden;
+    memcpy(m->h_stage, embed, h * 4);
+    CK(cudaMemcpyAsync(m->x, m->h_stage, h * 4, cudaMemcpyHostToDevice, m->st));
+    if (m->tok_cap < 2) {
+        cudaFree(m->tok_dev);
+        if (dev_alloc(&m->tok_dev, 4096)) return -1;
+        m->tok_cap = 4096;
+    }
+    QdbStepArgs a = step_args(s, pos);
+    a.token_out = m->tok_dev;
+    a.hidden_out = hidden_out ? m->hidden_dev : nullptr;
+    a.logits_out = logits_out ? m->logits_dev : nullptr;
+    if (launch_step(m, a)) return -1;
+    CK(cudaMemcpyAsync(m->h_tok, m->tok_dev, sizeof(int), cudaMemcpyDeviceToHost, m->st));
+    if (hidden_out) CK(cudaMemcpyAsync(hidden_out, m->hidden_dev, h * 4, cudaMemcpyDeviceToHost, m->st));
+    if (logits_out)
+        CK(cudaMemcpyAsync(logits_out, m->logits_dev, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->st));
+    CK(cudaStreamSynchronize(m->st));
+    if (check_err(m)) return -1;
+    return m->h_tok[0];
+}
+
+extern "C" int qdb_decode_greedy(qdb_session *s, int first_token, int pos, int n_steps, int *tokens_out) {
+    g_err.clear();
+    if (!s || (n_steps > 0 && !tokens_out)) return fail("null argument");
+    if (n_steps <= 0) return 0;
+    qdb_model *m = s->m;
+    if (first_token < 0 || first_token >= m->cfg.vocab) return fail("token %d out of range", first_token);
+    if (pos < 0) return fail("negative position");
+    if (set_dev(m) || prep_pos(s, pos + n_steps - 1)) return -1;
+    if (m->tok_cap < n_steps + 1) {
+        cudaFree(m->tok_dev);
+        m->tok_cap = 0;
+        if (dev_alloc(&m->tok_dev, (size_t)n_steps + 1)) return -1;
+        m->tok_cap = n_steps + 1;
+    }
+    m->h_tok[0] = first_token;
+    CK(cudaMemcpyAsync(m->tok_dev, m->h_tok, sizeof(int), cudaMemcpyHostToDevice, m->st));
+    for (int i = 0; i < n_steps; i++) {
+        QdbStepArgs a = step_args(s, pos + i);
+        a.token_in = m->tok_dev + i;
+        a.token_out = m->tok_dev + i + 1;
+        if (launch_step(m, a)) return -1;
+    }
+    CK(cudaMemcpyAsync(tokens_out, m->tok_dev + 1, sizeof(int) * n_steps, cudaMemcpyDeviceToHost, m->st));
+    CK(cudaStreamSynchronize(m->st));
+    return check_err(m);
+}
+
+// ------------------------------------------------------------------ row-batched path
+static int ensure_rows(qdb_model *m, int n, bool logits) {
+    RowScratch &r = m->rs;
+    const size_t h = m->cfg.hidden, I = m->cfg.intermediate;
+    if (n > r.cap) {
+        int cap = r.cap ? r.cap : 64;
+        while (cap < n) cap *= 2;
+        cudaFree(r.X); cudaFree(r.XN); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT);
+        r.X = r.XN = r.QKV = r.Q = r.ATT = r.ACT = nullptr;
+        r.cap = 0;
+        if (dev_alloc(&r.X, cap * h) || dev_alloc(&r.XN, cap * h) || dev_alloc(&r.QKV, cap * (size_t)(m->qd + 2 * m->kvd)) ||
+            dev_alloc(&r.Q, cap * (size_t)m->qd) || dev_alloc(&r.ATT, cap * (size_t)m->qd) || dev_alloc(&r.ACT, cap * I))
+            return -1;
+        r.cap = cap;
+    }
+    if (logits && n > r.log_cap) {
+        cudaFree(r.LOG);
+        r.LOG = nullptr;
+        r.log_cap = 0;
+        if (dev_alloc(&r.LOG, (size_t)n * m->cfg.vocab)) return -1;
+        r.log_cap = n;
+    }
+    if (n > r.rowkv_cap) {
+        cudaFree(r.rowkv);
+        r.rowkv = nullptr;
+        r.rowkv_cap = 0;
+        if (dev_alloc(&r.rowkv, n)) return -1;
+        r.rowkv_cap = n;
+    }
+    return 0;
+}
+
+// One transformer stack over the rows already in rs.X. single: all rows belong
+// to one session and are consecutive positions (prefill); otherwise row b uses
+// rowkv[b] at position rowkv[b].pos + pos_off (multi-utterance decode).
+static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, int pos_off, const qdb_session *s1,
+                    int start_pos) {
+    RowScratch &r = m->rs;
+    const int h = m->cfg.hidden, I = m->cfg.intermediate, Hq = m->cfg.heads, Hkv = m->cfg.kv_heads;
+    const int qkvd = m->qd + 2 * m->kvd;
+    int S = 1;
+    if (!single) {
+        const int units = n * Hkv;
+        S = (2 * m->sms + units - 1) / units;
+        if (S > 16) S = 16;
+        if (S < 1) S = 1;
+        const size_t need = (size_t)n * Hq * S * (2 + QDB_HD);
+        if (need > r.part_cap) {
+            cudaFree(r.part);
+            r.part = nullptr;
+            r.part_cap = 0;
+            if (dev_alloc(&r.part, need)) return -1;
+            r.part_cap = need;
+        }
+    }
+    for (int l = 0; l < m->cfg.layers; l++) {
+        const QdbLayerW &lw = m->layers_host[l];
+        CK(qdb_launch_rmsnorm_rows(r.X, lw.in_norm, r.XN, n, h, m->cfg.eps, m->st));
+        CK(qdb_launch_gemm_rows(r.XN, lw.qkv, r.QKV, n, qkvd, h, 0, m->st));
+        if (single) {
+            CK(qdb_launch_qk_rope_append_single(r.QKV, r.Q, row0_dev, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
+                                                m->cfg.eps, m->st));
+            CK(qdb_launch_attn_prefill(r.Q, s1->kc, s1->vc, s1->cap, l, start_pos, n, Hq, Hkv, r.ATT, m->st));
+        } else {
+            CK(qdb_launch_qk_rope_append(r.QKV, r.Q, row0_dev, pos_off, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
+                                         m->cfg.eps, m->st));
+            CK(qdb_launch_attn_rows(r.Q, row0_dev, pos_off, l, n, Hq, Hkv, S, r.part, r.ATT, m->st));
+        }
+        CK(qdb_launch_gemm_rows(r.ATT, lw.o, r.X, n, h, m->qd, 1, m->st));
+        CK(qdb_launch_rmsnorm_rows(r.X, lw.post_norm, r.XN, n, h, m->cfg.eps, m->st));
+        CK(qdb_launch_gemm_rows(r.XN, lw.gu, r.ACT, n, 2 * I, h, 2, m->st));
+        CK(qdb_launch_gemm_rows(r.ACT, lw.down, r.X, n, h, I, 1, m->st));
+    }
+    return 0;
+}
+
+static int prefill_impl(qdb_session *s, const float *embeds, bool device_ptr, int seq_len, int start_pos) {
+    g_err.clear();
+    if (!s) return fail("null session");
+    if (seq_len < 0 || start_pos < 0) return fail("negative length or position");
+    if (seq_len == 0) return 0;
+    if (!embeds) return fail("null embeddings");
+    qdb_model *m = s->m;
+    if (set_dev(m) || prep_pos(s, start_pos + seq_len - 1) || ensure_rows(m, seq_len, false)) return -1;
+    const size_t h = m->cfg.hidden;
+    CK(cudaMemcpyAsync(m->rs.X, embeds, (size_t)seq_len * h * 4,
+                       device_ptr ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, m->st));
+    QdbRowKV rk{s->kc, s->vc, s->cap, start_pos};
+    CK(cudaMemcpyAsync(m->rs.rowkv, &rk, sizeof(rk), cudaMemcpyHostToDevice, m->st));
+    if (run_rows(m, seq_len, true, m->rs.rowkv, 0, s, start_pos)) return -1;
+    CK(cudaStreamSynchronize(m->st));
+    return 0;
+}
+
+extern "C" int qdb_prefill(qdb_session *s, const float *embeds, int seq_len, int start_pos) {
+    return prefill_impl(s, embeds, false, seq_len, start_pos);
+}
+
+extern "C" int qdb_prefill_device(qdb_session *s, const float *embeds_dev, int seq_len, int start_pos) {
+    return prefill_impl(s, embeds_dev, true, seq_len, start_pos);
+}
+
+static int batch_setup(qdb_session *const *ss, int n, const int *pos, int extra_steps, qdb_model **mo) {
+    if (!ss || n <= 0 || !pos) return fail("bad batch arguments");
+    qdb_model *m = ss[0] ? ss[0]->m : nullptr;
+    if (!m) return fail("null session");
+    for (int b = 0; b < n; b++) {
+        if (!ss[b] || ss[b]->m != m) return fail("row %d: sessions must share one model", b);
+        if (pos[b] < 0) return fail("row %d: negative position", b);
+    }
+    if (set_dev(m) || ensure_rows(m, n, true)) return -1;
+    std::vector<QdbRowKV> rk(n);
+    for (int b = 0; b < n; b++) {
+        if (prep_pos(ss[b], pos[b] + extra_steps)) return -1;
+    }
+    for (int b = 0; b < n; b++) rk[b] = QdbRowKV{ss[b]->kc, ss[b]->vc, ss[b]->cap, pos[b]};
+    CK(cudaMemcpyAsync(m->rs.rowkv, rk.data(), sizeof(QdbRowKV) * n, cudaMemcpyHostToDevice, m->st));
+    CK(cudaStreamSynchronize(m->st));  // rk is a stack vector
+    *mo = m;
+    return 0;
+}
+
+static int batch_tail(qdb_model *m, int n, int *tok_dev) {
+    RowScratch &r = m->rs;
+    CK(qdb_launch_rmsnorm_rows(r.X, m->final_norm, r.XN, n, m->cfg.hidden, m->cfg.eps, m->st));
+    CK(qdb_launch_gemm_rows(r.XN, m->embed, r.LOG, n, m->cfg.vocab, m->cfg.hidden, 0, m->st));
+    CK(qdb_launch_argmax_rows(r.LOG, n, m->cfg.vocab, m->mask_eos, tok_dev, m->st));
+    return 0;
+}
+
+static int ensure_tok(qdb_model *m, size_t count) {
+    RowScratch &r = m->rs;
+    if (count <= r.tok_cap) return 0;
+    cudaFree(r.tok);
+    r.tok = nullptr;
+    r.tok_cap = 0;
+    if (dev_alloc(&r.tok, count)) return -1;
+    r.tok_cap = count;
+    return 0;
+}
+
+extern "C" int qdb_forward_batch(qdb_session *const *sessions, int n, const float *embeds, const int *pos,
+                                 int *tokens_out) {
+    g_err.clear();
+    qdb_model *m = nullptr;
+    if (!embeds || !tokens_out) return fail("null argument");
+    if (batch_setup(sessions, n, pos, 0, &m) || ensure_tok(m, n)) return -1;
+    CK(cudaMemcpyAsync(m->rs.X, embeds, (size_t)n * m->cfg.hidden * 4, cudaMemcpyHostToDevice, m->st));
+    if (run_rows(m, n, false, m->rs.rowkv, 0, nullptr, 0) || batch_tail(m, n, m->rs.tok)) return -1;
+    CK(cudaMemcpyAsync(tokens_out, m->rs.tok, sizeof(int) * n, cudaMemcpyDeviceToHost, m->st));
+    CK(cudaStreamSynchronize(m->st));
+    return 0;
+}
+
+extern "C" int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, const int *first_tokens, const int *pos,
+                                       int n_steps, int *tokens_out) {
+    g_err.clear();
+    qdb_model *m = nullptr;
+    if (!first_tokens || (n_steps > 0 && !tokens_out)) return fail("null argument");
+    if (n_steps <= 0) return 0;
+    if (batch_setup(sessions, n, pos, n_steps - 1, &m) || ensure_tok(m, (size_t)n * (n_steps + 1))) return -1;
+    for (int b = 0; b < n; b++)
+        if (first_tokens[b] < 0 || first_tokens[b] >= m->cfg.vocab) return fail("row %d: token out of range", b);
+    CK(cudaMemcpyAsync(m->rs.tok, first_tokens, sizeof(int) * n, cudaMemcpyHostToDevice, m->st));
+    for (int i = 0; i < n_steps; i++) {
+        int *tin = m->rs.tok + (size_t)i * n;
+        CK(qdb_launch_embed_rows(m->embed, tin, m->rs.X, n, m->cfg.hidden, m->st));
+        if (run_rows(m, n, false, m->rs.rowkv, i, nullptr, 0) || batch_tail(m, n, tin + n)) return -1;
+    }
+    CK(cudaMemcpyAsync(tokens_out, m->rs.tok + n, sizeof(int) * (size_t)n * n_steps, cudaMemcpyDeviceToHost, m->st));
+    CK(cudaStreamSynchronize(m->st));
+    return 0;
+}

@@ -1,0 +1,198 @@
+"""Seeded synthetic decoder weights and inputs in the reference's tensor layout.
+
+No checkpoints or datasets are available offline, so parity tests and the
+benchmark use random-init weights of the real architectures:
+
+* Decoder shapes follow the reference's hard-coded variants
+  (qwen_asr.c:135-191): 0.6B = hidden 1024 / intermediate 3072, 1.7B = hidden
+  2048 / intermediate 6144; 28 layers, 16 query / 8 KV heads, head_dim 128,
+  vocab 151936, RMSNorm eps 1e-6, RoPE theta 1e6.
+* Tensor names are the reference's (qwen_asr_decoder.c:45-116), all bf16.
+  Matrices are N(0, 0.02) drawn from one torch.Generator(seed) in sorted
+  tensor-name order; norm weights are 1 (optionally jittered for tests so the
+  norm weights are exercised).
+* Every tensor lives inside one contiguous uint16 host blob (256-byte aligned
+  slots) so the same bytes can be handed to the CUDA library, the CPU oracle
+  and the reference's own loader without copies.
+"""
+from __future__ import annotations
+
+import dataclasses
+
+import numpy as np
+
+# Prompt template ids of the reference (qwen_asr.c:339-350): 9 prefix ids
+# before the audio embeddings and 6 suffix ids after them.
+PROMPT_PREFIX = (151644, 8948, 198, 151645, 198, 151644, 872, 198, 151669)
+PROMPT_SUFFIX = (151670, 151645, 198, 151644, 77091, 198)
+ENC_TOKENS_PER_SECOND = 13  # 13 encoder tokens per 100 mel frames (1 s)
+
+
+@dataclasses.dataclass(frozen=True)
+class Config:
+    hidden: int
+    layers: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    intermediate: int
+    vocab: int
+    eps: float = 1e-6
+    theta: float = 1e6
+
+    def as_tuple(self):
+        return (self.hidden, self.layers, self.heads, self.kv_heads, self.head_dim,
+                self.intermediate, self.vocab)
+
+
+PRESETS = {
+    "0.6b": Config(1024, 28, 16, 8, 128, 3072, 151936),
+    "1.7b": Config(2048, 28, 16, 8, 128, 6144, 151936),
+    # Small shapes for parity tests (the oracle finishes them in seconds).
+    "tiny": Config(256, 2, 4, 2, 128, 512, 1000),
+    "small": Config(512, 3, 8, 4, 128, 768, 4099),
+    "gqa4": Config(256, 2, 8, 2, 128, 512, 777),
+}
+
+BF16 = 2  # safetensor_dtype_t DTYPE_BF16 in the reference loader
+
+
+def tensor_specs(cfg: Config):
+    """(name, shape) of every decoder tensor, reference naming."""
+    h, hd, I = cfg.hidden, cfg.head_dim, cfg.intermediate
+    qd, kvd = cfg.heads * hd, cfg.kv_heads * hd
+    specs = [("thinker.model.embed_tokens.weight", (cfg.vocab, h)),
+             ("thinker.model.norm.weight", (h,))]
+    for i in range(cfg.layers):
+        p = f"thinker.model.layers.{i}."
+        specs += [
+            (p + "self_attn.q_proj.weight", (qd, h)),
+            (p + "self_attn.k_proj.weight", (kvd, h)),
+            (p + "self_attn.v_proj.weight", (kvd, h)),
+            (p + "self_attn.o_proj.weight", (h, qd)),
+            (p + "self_attn.q_norm.weight", (hd,)),
+            (p + "self_attn.k_norm.weight", (hd,)),
+            (p + "input_layernorm.weight", (h,)),
+            (p + "post_attention_layernorm.weight", (h,)),
+            (p + "mlp.gate_proj.weight", (I, h)),
+            (p + "mlp.up_proj.weight", (I, h)),
+            (p + "mlp.down_proj.weight", (h, I)),
+        ]
+    return specs
+
+
+def _is_norm(name: str) -> bool:
+    return "norm" in name
+
+
+class WeightSet:
+    """All decoder tensors of one synthetic model in one bf16 host blob."""
+
+    def __init__(self, cfg: Config, seed: int = 0, norm_jitter: float = 0.0, pin: bool = False):
+        import torch
+
+        self.cfg = cfg
+        specs = tensor_specs(cfg)
+        self.offsets = {}
+        self.shapes = {}
+        off = 0
+        for name, shape in specs:
+            n = int(np.prod(shape))
+            self.offsets[name] = off
+            self.shapes[name] = shape
+            off += (n + 127) // 128 * 128  # 256-byte slots
+        self.n_elems = off
+        if pin:
+            self._blob_t = torch.empty(off, dtype=torch.int16).pin_memory()
+            self.blob = self._blob_t.numpy().view(np.uint16)
+        else:
+            self.blob = np.empty(off, dtype=np.uint16)
+        g = torch.Generator().manual_seed(seed)
+        for name in sorted(self.offsets):
+            shape = self.shapes[name]
+            view = self.view(name)
+            if _is_norm(name):
+                t = torch.ones(shape)
+                if norm_jitter:
+                    t = t + norm_jitter * torch.randn(shape, generator=g)
+            else:
+                t = torch.randn(shape, generator=g) * 0.02
+            view[...] = t.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+        self._f32 = {}
+
+    def view(self, name):
+        off = self.offsets[name]
+        shape = self.shapes[name]
+        return self.blob[off:off + int(np.prod(shape))].reshape(shape)
+
+    def f32(self, name):
+        """bf16 tensor widened to f32 (what the reference's load_f32 returns)."""
+        if name not in self._f32:
+            self._f32[name] = bf16_to_f32(self.view(name))
+        return self._f32[name]
+
+    def table(self):
+        """(names, byte offsets, byte sizes, shapes) for the reference loader."""
+        names, offs, sizes, shapes = [], [], [], []
+        for name, _ in tensor_specs(self.cfg):
+            names.append(name)
+            offs.append(self.offsets[name] * 2)
+            sizes.append(int(np.prod(self.shapes[name])) * 2)
+            s = self.shapes[name]
+            shapes.append((s[0], s[1] if len(s) > 1 else 0))
+        return names, offs, sizes, shapes
+
+    def layer(self, i):
+        p = f"thinker.model.layers.{i}."
+        return dict(
+            wq=self.view(p + "self_attn.q_proj.weight"),
+            wk=self.view(p + "self_attn.k_proj.weight"),
+            wv=self.view(p + "self_attn.v_proj.weight"),
+            wo=self.view(p + "self_attn.o_proj.weight"),
+            gate=self.view(p + "mlp.gate_proj.weight"),
+            up=self.view(p + "mlp.up_proj.weight"),
+            down=self.view(p + "mlp.down_proj.weight"),
+            q_norm=self.f32(p + "self_attn.q_norm.weight"),
+            k_norm=self.f32(p + "self_attn.k_norm.weight"),
+            input_norm=self.f32(p + "input_layernorm.weight"),
+            post_attn_norm=self.f32(p + "post_attention_layernorm.weight"),
+        )
+
+    @property
+    def embed(self):
+        return self.view("thinker.model.embed_tokens.weight")
+
+    @property
+    def final_norm(self):
+        return self.f32("thinker.model.norm.weight")
+
+
+def bf16_to_f32(a: np.ndarray) -> np.ndarray:
+    return (a.astype(np.uint32) << 16).view(np.float32)
+
+
+def embed_rows(ws: WeightSet, ids) -> np.ndarray:
+    """Host token embedding, bf16 -> f32 (tok_embed_bf16_to_f32, qwen_asr.c:353-360)."""
+    return bf16_to_f32(ws.embed[np.asarray(ids, dtype=np.int64)])
+
+
+def audio_embeddings(cfg: Config, n_tokens: int, seed: int) -> np.ndarray:
+    """Stand-in for the encoder output (the encoder is outside this library):
+    seeded N(0, 1) f32 rows of the decoder width."""
+    rng = np.random.default_rng(seed)
+    return rng.standard_normal((n_tokens, cfg.hidden), dtype=np.float32)
+
+
+def prompt_embeddings(ws: WeightSet, audio: np.ndarray) -> np.ndarray:
+    """[prefix ids][audio rows][suffix ids], the reference's input_embeds
+    layout without a system prompt or forced language (qwen_asr.c:626-700).
+    Small test vocabularies take the ids modulo their size."""
+    V = ws.cfg.vocab
+    pre = embed_rows(ws, [t % V for t in PROMPT_PREFIX])
+    suf = embed_rows(ws, [t % V for t in PROMPT_SUFFIX])
+    return np.ascontiguousarray(np.concatenate([pre, audio, suf], axis=0), dtype=np.float32)
+
+
+def utterance(ws: WeightSet, seconds: float, seed: int) -> np.ndarray:
+    n = int(round(seconds * ENC_TOKENS_PER_SECOND))
+    return prompt_embeddings(ws, audio_embeddings(ws.cfg, n, seed))

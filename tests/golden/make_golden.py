@@ -1,0 +1,103 @@
+"""Generates the golden vectors in this directory from the REFERENCE itself.
+
+The reference's own decoder sources (qwen_asr_decoder.c, qwen_asr_kernels*.c,
+qwen_asr_safetensors.c) are compiled unmodified into oracle/_ref/ by
+oracle/Makefile and driven through qwen_decoder_load / qwen_decoder_prefill /
+qwen_decoder_forward (oracle/ref_harness.c). This script runs them on seeded
+synthetic weights and inputs and stores tokens and logits, so the parity tests
+can pin both the oracle restatement and the CUDA path on a machine without the
+reference tree.
+
+Run here (needs oracle/_ref built):  python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+
+import __graft_entry__ as ge  # noqa: E402
+from oracle.pyoracle import RefDecoder, margin_top2  # noqa: E402
+
+synth = ge.load_synth()
+
+# Small configurations: full logits of every step.
+SMALL_CASES = [
+    # (preset, norm_jitter, n_audio_tokens, audio_seed, steps)
+    ("tiny", 0.1, 20, 1, 10),
+    ("gqa4", 0.1, 33, 2, 10),
+    ("small", 0.1, 57, 3, 10),
+]
+# Full-size shapes: tokens, top-64 logits and checksums of every step.
+FULL_CASES = [
+    ("0.6b", 0.0, 40, 1, 4),
+    ("1.7b", 0.0, 24, 1, 3),
+]
+TOPK = 64
+
+
+def run_case(preset, jitter, n_audio, seed, steps, full_logits, threads):
+    cfg = synth.PRESETS[preset]
+    ws = synth.WeightSet(cfg, seed=0, norm_jitter=jitter)
+    emb = synth.prompt_embeddings(ws, synth.audio_embeddings(cfg, n_audio, seed))
+    ref = RefDecoder(ws, threads=threads)
+    ref.kv_cache_len = 0
+    ref.prefill(emb[:-1])
+    e = emb[-1]
+    toks, logits, tops, topi, sums, sqs, margins = [], [], [], [], [], [], []
+    for _ in range(steps):
+        tok, _, lg = ref.forward(e, mask_eos=True)
+        toks.append(tok)
+        margins.append(margin_top2(lg, mask_eos=True))
+        if full_logits:
+            logits.append(lg.copy())
+        idx = np.argsort(-lg, kind="stable")[:TOPK]
+        topi.append(idx.astype(np.int32))
+        tops.append(lg[idx])
+        sums.append(float(lg.astype(np.float64).sum()))
+        sqs.append(float((lg.astype(np.float64) ** 2).sum()))
+        e = synth.embed_rows(ws, [tok])[0]
+    # Rewind (the streaming caller's prefix reuse, qwen_asr.c:1764): back to
+    # the prefill length + 2 and re-run 3 steps from there.
+    rew = emb.shape[0] - 1 + 2
+    ref.kv_cache_len = rew
+    e = synth.embed_rows(ws, [toks[1]])[0]
+    rew_toks, rew_logits = [], []
+    for _ in range(3):
+        tok, _, lg = ref.forward(e, mask_eos=True)
+        rew_toks.append(tok)
+        if full_logits:
+            rew_logits.append(lg.copy())
+        e = synth.embed_rows(ws, [tok])[0]
+    out = dict(preset=preset, norm_jitter=jitter, n_audio=n_audio, audio_seed=seed, weight_seed=0,
+               prefill_len=emb.shape[0] - 1, tokens=np.array(toks, np.int32), margins=np.array(margins),
+               top_idx=np.array(topi), top_val=np.array(tops, np.float32), logit_sum=np.array(sums),
+               logit_sumsq=np.array(sqs), rewind_pos=rew, rewind_tokens=np.array(rew_toks, np.int32))
+    if full_logits:
+        out["logits"] = np.array(logits, np.float32)
+        out["rewind_logits"] = np.array(rew_logits, np.float32)
+    ref.close()
+    return out
+
+
+def main():
+    threads = min(os.cpu_count() or 1, 16)
+    for case in SMALL_CASES:
+        d = run_case(*case, full_logits=True, threads=threads)
+        np.savez_compressed(os.path.join(HERE, f"ref_{case[0]}.npz"), **d)
+        print("wrote", case[0], d["tokens"], d["margins"].round(4))
+    if "--small-only" in sys.argv:
+        return
+    for case in FULL_CASES:
+        d = run_case(*case, full_logits=False, threads=threads)
+        np.savez_compressed(os.path.join(HERE, f"ref_{case[0]}.npz"), **d)
+        print("wrote", case[0], d["tokens"], d["margins"].round(4))
+
+
+if __name__ == "__main__":
+    main()
