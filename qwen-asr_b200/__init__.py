@@ -13,6 +13,7 @@ and there is no CPU fallback.
 """
 from __future__ import annotations
 
+import atexit
 import ctypes
 import os
 
@@ -74,6 +75,11 @@ def _load():
 
 
 lib = _load()
+
+# At interpreter exit the process releases device memory itself; finalizers
+# then skip their frees (object finalization order is arbitrary at shutdown).
+_exiting = [False]
+atexit.register(lambda: _exiting.__setitem__(0, True))
 
 
 class QdbError(RuntimeError):
@@ -137,9 +143,9 @@ class Model:
             raise _err("qdb_model_sync")
 
     def close(self):
-        if self.h:
+        if self.h and not _exiting[0]:
             lib.qdb_model_free(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:
@@ -189,9 +195,9 @@ class Session:
         return out[:n_steps]
 
     def close(self):
-        if self.h:
+        if self.h and not _exiting[0]:
             lib.qdb_session_free(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:

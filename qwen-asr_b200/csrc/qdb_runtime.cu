@@ -97,10 +97,11 @@ struct qdb_model {
     float *h_stage = nullptr;  // pinned [max(h, V)]
     int *h_tok = nullptr;      // pinned
     RowScratch rs;
+    std::vector<qdb_session *> sessions;  // live sessions (detached when the model is freed)
 };
 
 struct qdb_session {
-    qdb_model *m;
+    qdb_model *m;  // null once the model has been freed (session detached)
     uint16_t *kc = nullptr, *vc = nullptr;
     int cap = 0;
 };
@@ -209,6 +210,16 @@ extern "C" void qdb_model_free(qdb_model *m) {
     if (!m) return;
     cudaSetDevice(m->device);
     if (m->st) cudaStreamSynchronize(m->st);
+    // Sessions still alive are detached: their device KV is released here and
+    // a later qdb_session_free only deletes the handle.
+    for (qdb_session *s : m->sessions) {
+        cudaFree(s->kc);
+        cudaFree(s->vc);
+        s->kc = s->vc = nullptr;
+        s->cap = 0;
+        s->m = nullptr;
+    }
+    m->sessions.clear();
     cudaFree(m->w); cudaFree(m->norms); cudaFree(m->embed); cudaFree(m->final_norm); cudaFree(m->layers_dev);
     cudaFree(m->rope); cudaFree(m->x); cudaFree(m->qkv); cudaFree(m->attn); cudaFree(m->act); cudaFree(m->part);
     cudaFree(m->hidden_dev); cudaFree(m->logits_dev); cudaFree(m->cnt); cudaFree(m->bar); cudaFree(m->best);
@@ -299,15 +310,23 @@ extern "C" qdb_session *qdb_session_create(qdb_model *m, int initial_capacity) {
         delete s;
         return nullptr;
     }
+    m->sessions.push_back(s);
     return s;
 }
 
 extern "C" void qdb_session_free(qdb_session *s) {
     if (!s) return;
-    cudaSetDevice(s->m->device);
-    cudaStreamSynchronize(s->m->st);
-    cudaFree(s->kc);
-    cudaFree(s->vc);
+    if (qdb_model *m = s->m) {
+        cudaSetDevice(m->device);
+        cudaStreamSynchronize(m->st);
+        cudaFree(s->kc);
+        cudaFree(s->vc);
+        for (size_t i = 0; i < m->sessions.size(); i++)
+            if (m->sessions[i] == s) {
+                m->sessions.erase(m->sessions.begin() + i);
+                break;
+            }
+    }
     delete s;
 }
 
@@ -317,6 +336,7 @@ extern "C" int qdb_session_capacity(const qdb_session *s) { return s ? s->cap : 
 // and keeps the first `cap` positions of every (layer, kv head) block.
 extern "C" int qdb_session_reserve(qdb_session *s, int positions) {
     if (!s) return fail("null session");
+    if (!s->m) return fail("session's model has been freed");
     if (positions <= s->cap) return 0;
     qdb_model *m = s->m;
     if (set_dev(m)) return -1;
@@ -401,6 +421,7 @@ static int prep_pos(qdb_session *s, int last_pos) {
 extern "C" int qdb_forward(qdb_session *s, const float *embed, int pos, float *hidden_out, float *logits_out) {
     g_err.clear();
     if (!s || !embed) return fail("null argument");
+    if (!s->m) return fail("session's model has been freed");
     if (pos < 0) return fail("negative position");
     qdb_model *m = s->m;
     if (set_dev(m) || prep_pos(s, pos)) return -1;
@@ -429,6 +450,7 @@ extern "C" int qdb_forward(qdb_session *s, const float *embed, int pos, float *h
 extern "C" int qdb_decode_greedy(qdb_session *s, int first_token, int pos, int n_steps, int *tokens_out) {
     g_err.clear();
     if (!s || (n_steps > 0 && !tokens_out)) return fail("null argument");
+    if (!s->m) return fail("session's model has been freed");
     if (n_steps <= 0) return 0;
     qdb_model *m = s->m;
     if (first_token < 0 || first_token >= m->cfg.vocab) return fail("token %d out of range", first_token);
@@ -532,6 +554,7 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
 static int prefill_impl(qdb_session *s, const float *embeds, bool device_ptr, int seq_len, int start_pos) {
     g_err.clear();
     if (!s) return fail("null session");
+    if (!s->m) return fail("session's model has been freed");
     if (seq_len < 0 || start_pos < 0) return fail("negative length or position");
     if (seq_len == 0) return 0;
     if (!embeds) return fail("null embeddings");
@@ -558,7 +581,7 @@ extern "C" int qdb_prefill_device(qdb_session *s, const float *embeds_dev, int s
 static int batch_setup(qdb_session *const *ss, int n, const int *pos, int extra_steps, qdb_model **mo) {
     if (!ss || n <= 0 || !pos) return fail("bad batch arguments");
     qdb_model *m = ss[0] ? ss[0]->m : nullptr;
-    if (!m) return fail("null session");
+    if (!m) return fail("null session or session's model has been freed");
     for (int b = 0; b < n; b++) {
         if (!ss[b] || ss[b]->m != m) return fail("row %d: sessions must share one model", b);
         if (pos[b] < 0) return fail("row %d: negative position", b);

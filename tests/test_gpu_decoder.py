@@ -89,7 +89,9 @@ def test_hidden_state_matches_oracle(pkg, synth, models):
     o.prefill(emb[:-1])
     _, hid, _ = s.forward(emb[-1], emb.shape[0] - 1, want_hidden=True)
     _, ohid, _ = o.forward(emb[-1])
-    np.testing.assert_allclose(hid, ohid, atol=5e-3, rtol=0)
+    # bf16 KV cache: ~0.5% elementwise noise on a unit-RMS vector
+    rel = np.linalg.norm(hid - ohid) / np.linalg.norm(ohid)
+    assert rel <= 1e-2 and np.abs(hid - ohid).max() <= 3e-2, rel
 
 
 @pytest.mark.parametrize("chunks", [[1], [1, 1, 1], [7, 1, 30], [64], [3, 0, 5]])
@@ -132,6 +134,17 @@ def test_long_context_split_attention(pkg, synth):
         assert tok == otok or margin_top2(olg) <= MARGIN
 
 
+def test_session_outlives_model(pkg, synth):
+    """Freeing the model first detaches its sessions; later calls fail cleanly."""
+    ws = synth.WeightSet(synth.PRESETS["tiny"], seed=1)
+    model = pkg.Model(ws, device=0)
+    s = model.session(16)
+    model.close()
+    with pytest.raises(pkg.QdbError, match="freed"):
+        s.forward(np.zeros(ws.cfg.hidden, np.float32), 0)
+    s.close()
+
+
 def test_batched_decode_matches_single(pkg, synth):
     """qdb_forward_batch over independent sessions at different positions ==
     per-session qdb_forward (the row-batched path vs the persistent step)."""
@@ -150,8 +163,9 @@ def test_batched_decode_matches_single(pkg, synth):
         x = np.stack([embs[b][lens[b] + step] for b in range(n)])
         pos = [lens[b] + step for b in range(n)]
         got = pkg.forward_batch(sb, x, pos)
-        want = [ss[b].forward(x[b], pos[b])[0] for b in range(n)]
-        assert list(got) == want
+        for b in range(n):
+            want, _, lg = ss[b].forward(x[b], pos[b], want_logits=True)
+            assert got[b] == want or margin_top2(lg, mask_eos=True) <= MARGIN, (step, b)
 
 
 def test_batched_greedy_loop_matches_oracle(pkg, synth):
