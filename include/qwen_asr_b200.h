@@ -89,7 +89,7 @@ int qdb_model_set_mask_eos(qdb_model *m, int enable);
 
 /* ---- Session: one utterance's device KV cache (qwen_ctx_t KV fields,
  * qwen_asr.h:187-191; kv_cache_init / kv_cache_grow, qwen_asr_decoder.c:122-160).
- * K/V are stored bf16 [layer][kv_head][pos][head_dim]; the cache grows
+ * K/V are stored fp16 [layer][kv_head][pos][head_dim]; the cache grows
  * (doubling, contents kept) when a call needs more positions than it holds. */
 qdb_session *qdb_session_create(qdb_model *m, int initial_capacity);
 void qdb_session_free(qdb_session *s);

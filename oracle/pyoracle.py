@@ -70,6 +70,7 @@ def _oracle_lib():
         lib.orc_state_len.restype = ctypes.c_int
         lib.orc_state_len.argtypes = [ctypes.c_void_p]
         lib.orc_state_set_len.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        lib.orc_state_set_kv_round.argtypes = [ctypes.c_void_p, ctypes.c_int]
         lib.orc_prefill.restype = ctypes.c_int
         lib.orc_prefill.argtypes = [ctypes.c_void_p, _f32p, ctypes.c_int]
         lib.orc_forward.restype = ctypes.c_int
@@ -113,6 +114,9 @@ class Oracle:
     @kv_cache_len.setter
     def kv_cache_len(self, v):
         self.lib.orc_state_set_len(self.s, v)
+
+    def set_kv_round(self, mode: int):
+        self.lib.orc_state_set_kv_round(self.s, mode)
 
     def prefill(self, embeds):
         e = np.ascontiguousarray(embeds, dtype=np.float32)

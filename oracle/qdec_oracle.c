@@ -35,7 +35,26 @@ struct orc_state {
     orc_model *m;
     float *k_cache, *v_cache; /* [layers][max_pos][kv_heads*head_dim] */
     int len, max_pos;
+    int kv_round; /* 0: f32 as the reference; 1: round stored K/V to bf16; 2: to fp16 */
 };
+
+void orc_state_set_kv_round(orc_state *s, int mode) { s->kv_round = mode; }
+
+static float round_bf16(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    u &= 0xffff0000u;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+static void round_kv(float *v, int n, int mode) {
+    if (mode == 1)
+        for (int i = 0; i < n; i++) v[i] = round_bf16(v[i]);
+    else if (mode == 2)
+        for (int i = 0; i < n; i++) v[i] = (float)(_Float16)v[i];
+}
 
 static int g_threads = 1;
 
@@ -346,6 +365,8 @@ static void run_layers(orc_state *s, float *x, int seq, int start) {
             apply_rope(k + (size_t)r * kvd, rc + (size_t)r * hd, rs + (size_t)r * hd, c->kv_heads, hd);
             memcpy(kv_at(s, s->k_cache, li, start + r), k + (size_t)r * kvd, sizeof(float) * kvd);
             memcpy(kv_at(s, s->v_cache, li, start + r), v + (size_t)r * kvd, sizeof(float) * kvd);
+            round_kv(kv_at(s, s->k_cache, li, start + r), kvd, s->kv_round);
+            round_kv(kv_at(s, s->v_cache, li, start + r), kvd, s->kv_round);
         }
         causal_attention(att, q, kv_at(s, s->k_cache, li, 0), kv_at(s, s->v_cache, li, 0),
                          seq, start + seq, c->heads, c->kv_heads, hd, scale, start);

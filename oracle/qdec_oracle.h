@@ -53,6 +53,9 @@ orc_state *orc_state_create(orc_model *m, int max_pos);
 void orc_state_free(orc_state *s);
 int orc_state_len(const orc_state *s);
 void orc_state_set_len(orc_state *s, int len);
+/* Test-only: round the stored K/V (0 = f32 as the reference, 1 = bf16,
+ * 2 = fp16) to measure what a 16-bit device cache costs in parity. */
+void orc_state_set_kv_round(orc_state *s, int mode);
 
 /* Appends seq_len positions at the current length; returns 0 / -1. */
 int orc_prefill(orc_state *s, const float *embeds, int seq_len);

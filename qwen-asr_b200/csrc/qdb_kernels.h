@@ -20,43 +20,46 @@ struct QdbDims {
     float eps;
 };
 
-// Arguments of the persistent single-utterance decode step.
+// Arguments of the persistent single-utterance decode step. Inter-CTA
+// vectors are tagged 64-bit words (epoch << 32 | f32 bits); all must be zero
+// before the first launch and epochs start at 1.
 struct QdbStepArgs {
     QdbDims d;
     const QdbLayerW *layers;      // device [L]
     const uint16_t *embed;        // [V, h]
     const float *final_norm;      // [h]
     const float2 *rope;           // [rope_cap][64] (cos, sin)
-    uint16_t *kc, *vc;            // [L][Hkv][cap][128] bf16
+    uint16_t *kc, *vc;            // [L][Hkv][cap][128] fp16
     int cap;
     int pos;                      // absolute position of this step
     const int *token_in;          // device token (embedding gathered on device) or null
+    const float *x_in;            // [h] input embedding when token_in is null
     int *token_out;               // device [1]
-    float *x;                     // [h] residual stream (holds the input embedding when token_in is null)
-    float *qkv;                   // [Hq*128 + 2*Hkv*128]
-    float *attn;                  // [Hq*128]
-    float *act;                   // [I]
-    float *part;                  // [Hq][splits][2 + 128] attention partials
-    unsigned *cnt;                // [Hkv] combine counters, zero between steps
-    int splits;                   // attention splits per kv head
+    unsigned long long *tx;       // [h] residual stream
+    unsigned long long *tqkv;     // [Hq*128 + 2*Hkv*128]
+    unsigned long long *tattn;    // [Hq*128]
+    unsigned long long *tact;     // [I]
+    unsigned long long *tpart;    // [Hq][splits][2 + 128] attention partials
+    int splits;                   // attention splits per kv head (Hkv * splits <= grid)
     float *hidden_out;            // nullable [h]
     float *logits_out;            // nullable [V]
     unsigned long long *best;     // argmax key, zero between steps
-    unsigned *bar;                // grid barrier counter
-    unsigned bar_base;            // counter value at kernel start
+    unsigned *done;               // CTA completion counter, zero between steps
+    unsigned epoch;               // first epoch of this launch
     int *err;
     int mask_eos;
 };
 
-// Number of grid barriers one decode step performs (host keeps the counter base).
-static inline unsigned qdb_step_barriers(int layers) { return 5u * (unsigned)layers + 1u; }
+// Epochs one decode step consumes (host advances the base by this much).
+static inline unsigned qdb_step_epochs(int layers) { return 5u * (unsigned)layers + 1u; }
 
-#define QDB_STEP_THREADS 256
+#define QDB_STEP_THREADS 288
 
 extern "C" {
 // Launches one persistent step. grid = co-resident CTAs (one per SM).
 cudaError_t qdb_launch_step(const QdbStepArgs &a, int grid, cudaStream_t st);
 int qdb_step_max_grid(int device);
+int qdb_step_max_splits(int grid, int kv_heads);
 int qdb_step_smem_bytes(const QdbDims &d);
 
 // RoPE table: tab[p][i] = (cos, sin) of (float)p * inv_freq[i], p < n_pos.

@@ -158,7 +158,7 @@ __global__ void qk_rope_append_kernel(const float *qkv, float *q_out, const QdbR
         uint16_t *base = is_k ? rk.kc : rk.vc;
         uint16_t *dst = base + (((size_t)layer * Hkv + g) * (size_t)rk.cap + pos) * QDB_HD;
 #pragma unroll
-        for (int i = 0; i < 4; i++) dst[lane + 32 * i] = f32_to_bf16_rn(e[i]);
+        for (int i = 0; i < 4; i++) dst[lane + 32 * i] = f32_to_kv(e[i]);
     }
 }
 
@@ -217,11 +217,11 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float *q, const
                 vv = *reinterpret_cast<const uint4 *>(vc + head_base + (size_t)(k0 + kr) * QDB_HD + c8);
             }
             float *kd = Ks + kr * (QDB_HD + 1) + c8;
-            kd[0] = bf16lo(kv.x); kd[1] = bf16hi(kv.x); kd[2] = bf16lo(kv.y); kd[3] = bf16hi(kv.y);
-            kd[4] = bf16lo(kv.z); kd[5] = bf16hi(kv.z); kd[6] = bf16lo(kv.w); kd[7] = bf16hi(kv.w);
+            kd[0] = kvlo(kv.x); kd[1] = kvhi(kv.x); kd[2] = kvlo(kv.y); kd[3] = kvhi(kv.y);
+            kd[4] = kvlo(kv.z); kd[5] = kvhi(kv.z); kd[6] = kvlo(kv.w); kd[7] = kvhi(kv.w);
             float *vd = Vs + kr * QDB_HD + c8;
-            vd[0] = bf16lo(vv.x); vd[1] = bf16hi(vv.x); vd[2] = bf16lo(vv.y); vd[3] = bf16hi(vv.y);
-            vd[4] = bf16lo(vv.z); vd[5] = bf16hi(vv.z); vd[6] = bf16lo(vv.w); vd[7] = bf16hi(vv.w);
+            vd[0] = kvlo(vv.x); vd[1] = kvhi(vv.x); vd[2] = kvlo(vv.y); vd[3] = kvhi(vv.y);
+            vd[4] = kvlo(vv.z); vd[5] = kvhi(vv.z); vd[6] = kvlo(vv.w); vd[7] = kvhi(vv.w);
         }
         __syncthreads();
         // scores for keys sub, sub+TPQ, ... of this tile
@@ -312,24 +312,24 @@ __global__ void attn_rows_partial_kernel(const float *q, const QdbRowKV *rows, i
 #pragma unroll
         for (int t = 0; t < 8; t++) {
             if (j0 + t >= p1) break;
-            float sc = qr[0] * bf16lo(kk[t].x) + qr[1] * bf16hi(kk[t].x) + qr[2] * bf16lo(kk[t].y) +
-                       qr[3] * bf16hi(kk[t].y);
+            float sc = qr[0] * kvlo(kk[t].x) + qr[1] * kvhi(kk[t].x) + qr[2] * kvlo(kk[t].y) +
+                       qr[3] * kvhi(kk[t].y);
             sc = warp_sum(sc) * scale;
             if (sc > m) {
                 const float corr = expf(m - sc);
                 l = l * corr + 1.f;
-                o[0] = o[0] * corr + bf16lo(vv[t].x);
-                o[1] = o[1] * corr + bf16hi(vv[t].x);
-                o[2] = o[2] * corr + bf16lo(vv[t].y);
-                o[3] = o[3] * corr + bf16hi(vv[t].y);
+                o[0] = o[0] * corr + kvlo(vv[t].x);
+                o[1] = o[1] * corr + kvhi(vv[t].x);
+                o[2] = o[2] * corr + kvlo(vv[t].y);
+                o[3] = o[3] * corr + kvhi(vv[t].y);
                 m = sc;
             } else {
                 const float p = expf(sc - m);
                 l += p;
-                o[0] = fmaf(p, bf16lo(vv[t].x), o[0]);
-                o[1] = fmaf(p, bf16hi(vv[t].x), o[1]);
-                o[2] = fmaf(p, bf16lo(vv[t].y), o[2]);
-                o[3] = fmaf(p, bf16hi(vv[t].y), o[3]);
+                o[0] = fmaf(p, kvlo(vv[t].x), o[0]);
+                o[1] = fmaf(p, kvhi(vv[t].x), o[1]);
+                o[2] = fmaf(p, kvlo(vv[t].y), o[2]);
+                o[3] = fmaf(p, kvhi(vv[t].y), o[3]);
             }
         }
     }

@@ -10,6 +10,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <string>
 #include <vector>
 
@@ -84,11 +85,15 @@ struct qdb_model {
     float2 *rope = nullptr;
     int rope_cap = 0;
 
-    // single-utterance step scratch
-    float *x = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *part = nullptr;
+    // single-utterance step scratch (tagged inter-CTA vectors, see qdb_step.cu)
+    int grid = 0;                    // CTAs of the persistent step
+    unsigned long long *tags = nullptr;  // one allocation: tx | tqkv | tattn | tact | tpart
+    size_t tags_len = 0;
+    unsigned long long *tx = nullptr, *tqkv = nullptr, *tattn = nullptr, *tact = nullptr, *tpart = nullptr;
+    unsigned epoch = 1;
+    float *x_in = nullptr;
     float *hidden_dev = nullptr, *logits_dev = nullptr;
-    unsigned *cnt = nullptr, *bar = nullptr;
-    unsigned bar_base = 0;
+    unsigned *done = nullptr;
     unsigned long long *best = nullptr;
     int *err = nullptr;
     int *tok_dev = nullptr;
@@ -187,16 +192,29 @@ extern "C" qdb_model *qdb_model_create(const qdb_config *cfg, int device) {
     if (cudaMemcpy(m->layers_dev, m->layers_host.data(), sizeof(QdbLayerW) * cfg->layers,
                    cudaMemcpyHostToDevice) != cudaSuccess) { fail("layer table upload"); return bad(); }
 
-    // step scratch
-    m->max_splits = m->sms / cfg->kv_heads;
-    if (m->max_splits < 1) m->max_splits = 1;
-    if (dev_alloc(&m->x, h) || dev_alloc(&m->qkv, m->qd + 2 * m->kvd) || dev_alloc(&m->attn, m->qd) ||
-        dev_alloc(&m->act, I) || dev_alloc(&m->part, (size_t)cfg->heads * m->max_splits * (2 + QDB_HD)) ||
-        dev_alloc(&m->hidden_dev, h) || dev_alloc(&m->logits_dev, cfg->vocab) || dev_alloc(&m->cnt, cfg->kv_heads) ||
-        dev_alloc(&m->bar, 1) || dev_alloc(&m->best, 1) || dev_alloc(&m->err, 1))
+    // step scratch. Every CTA of the persistent step must own at least one row
+    // of every phase (the tagged-data ordering argument in qdb_step.cu), so the
+    // grid is capped by the smallest phase.
+    m->grid = m->sms;
+    const int min_rows = (int)std::min<size_t>(std::min<size_t>(h, I), (size_t)(m->qd + 2 * m->kvd));
+    if (m->grid > min_rows) m->grid = min_rows;
+    if (m->grid < cfg->kv_heads) { fail("GPU too small for the persistent step"); return bad(); }
+    m->max_splits = qdb_step_max_splits(m->grid, cfg->kv_heads);
+    {
+        const size_t n_x = h, n_qkv = m->qd + 2 * m->kvd, n_attn = m->qd, n_act = I;
+        const size_t n_part = (size_t)cfg->heads * m->max_splits * (2 + QDB_HD);
+        m->tags_len = n_x + n_qkv + n_attn + n_act + n_part;
+        if (dev_alloc(&m->tags, m->tags_len)) return bad();
+        m->tx = m->tags;
+        m->tqkv = m->tx + n_x;
+        m->tattn = m->tqkv + n_qkv;
+        m->tact = m->tattn + n_attn;
+        m->tpart = m->tact + n_act;
+    }
+    if (dev_alloc(&m->x_in, h) || dev_alloc(&m->hidden_dev, h) || dev_alloc(&m->logits_dev, cfg->vocab) ||
+        dev_alloc(&m->done, 1) || dev_alloc(&m->best, 1) || dev_alloc(&m->err, 1))
         return bad();
-    if (cudaMemset(m->cnt, 0, sizeof(unsigned) * cfg->kv_heads) != cudaSuccess ||
-        cudaMemset(m->bar, 0, sizeof(unsigned)) != cudaSuccess ||
+    if (cudaMemset(m->tags, 0, m->tags_len * 8) != cudaSuccess || cudaMemset(m->done, 0, sizeof(unsigned)) != cudaSuccess ||
         cudaMemset(m->best, 0, sizeof(unsigned long long)) != cudaSuccess ||
         cudaMemset(m->err, 0, sizeof(int)) != cudaSuccess) { fail("scratch memset"); return bad(); }
     size_t stage = h > (size_t)cfg->vocab ? h : (size_t)cfg->vocab;
@@ -221,8 +239,8 @@ extern "C" void qdb_model_free(qdb_model *m) {
     }
     m->sessions.clear();
     cudaFree(m->w); cudaFree(m->norms); cudaFree(m->embed); cudaFree(m->final_norm); cudaFree(m->layers_dev);
-    cudaFree(m->rope); cudaFree(m->x); cudaFree(m->qkv); cudaFree(m->attn); cudaFree(m->act); cudaFree(m->part);
-    cudaFree(m->hidden_dev); cudaFree(m->logits_dev); cudaFree(m->cnt); cudaFree(m->bar); cudaFree(m->best);
+    cudaFree(m->rope); cudaFree(m->tags); cudaFree(m->x_in);
+    cudaFree(m->hidden_dev); cudaFree(m->logits_dev); cudaFree(m->done); cudaFree(m->best);
     cudaFree(m->err); cudaFree(m->tok_dev);
     RowScratch &r = m->rs;
     cudaFree(r.X); cudaFree(r.XN); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT); cudaFree(r.LOG);
@@ -365,12 +383,14 @@ static int check_err(qdb_model *m) {
     int e = 0;
     CK(cudaMemcpy(&e, m->err, sizeof(int), cudaMemcpyDeviceToHost));
     if (e) {
+        // A bounded wait ran out: reset the step's device state.
         cudaMemset(m->err, 0, sizeof(int));
-        cudaMemset(m->bar, 0, sizeof(unsigned));
-        cudaMemset(m->cnt, 0, sizeof(unsigned) * m->cfg.kv_heads);
+        cudaMemset(m->tags, 0, m->tags_len * 8);
+        cudaMemset(m->done, 0, sizeof(unsigned));
         cudaMemset(m->best, 0, sizeof(unsigned long long));
-        m->bar_base = 0;
-        return fail("device error code %d (grid barrier wait ran out)", e);
+        cudaDeviceSynchronize();
+        m->epoch = 1;
+        return fail("device error code %d (a bounded wait in the decode step ran out)", e);
     }
     return 0;
 }
@@ -388,28 +408,34 @@ static QdbStepArgs step_args(qdb_session *s, int pos) {
     a.vc = s->vc;
     a.cap = s->cap;
     a.pos = pos;
-    a.x = m->x;
-    a.qkv = m->qkv;
-    a.attn = m->attn;
-    a.act = m->act;
-    a.part = m->part;
-    a.cnt = m->cnt;
+    a.x_in = m->x_in;
+    a.tx = m->tx;
+    a.tqkv = m->tqkv;
+    a.tattn = m->tattn;
+    a.tact = m->tact;
+    a.tpart = m->tpart;
+    // attention splits: about 64 keys per unit, at most grid / Hkv units per head
     const int ctx = pos + 1;
-    int S = (ctx + 31) / 32;
+    int S = (ctx + 63) / 64;
     if (S > m->max_splits) S = m->max_splits;
     if (S < 1) S = 1;
     a.splits = S;
     a.best = m->best;
-    a.bar = m->bar;
+    a.done = m->done;
     a.err = m->err;
     a.mask_eos = m->mask_eos;
     return a;
 }
 
 static int launch_step(qdb_model *m, QdbStepArgs &a) {
-    a.bar_base = m->bar_base;
-    CK(qdb_launch_step(a, m->sms, m->st));
-    m->bar_base += qdb_step_barriers(m->cfg.layers) * (unsigned)m->sms;
+    const unsigned span = qdb_step_epochs(m->cfg.layers);
+    if (m->epoch > 0xffffffffu - 2 * span) {  // epoch wrap: clear the tags and restart
+        CK(cudaMemsetAsync(m->tags, 0, m->tags_len * 8, m->st));
+        m->epoch = 1;
+    }
+    a.epoch = m->epoch;
+    CK(qdb_launch_step(a, m->grid, m->st));
+    m->epoch += span;
     return 0;
 }
 
@@ -427,7 +453,7 @@ extern "C" int qdb_forward(qdb_session *s, const float *embed, int pos, float *h
     if (set_dev(m) || prep_pos(s, pos)) return -1;
     const size_t h = m->cfg.hidden;
     memcpy(m->h_stage, embed, h * 4);
-    CK(cudaMemcpyAsync(m->x, m->h_stage, h * 4, cudaMemcpyHostToDevice, m->st));
+    CK(cudaMemcpyAsync(m->x_in, m->h_stage, h * 4, cudaMemcpyHostToDevice, m->st));
     if (m->tok_cap < 2) {
         cudaFree(m->tok_dev);
         if (dev_alloc(&m->tok_dev, 4096)) return -1;

@@ -1,156 +1,312 @@
 // qdb_step.cu - persistent single-utterance decode step (batch 1).
 //
-// One cooperative launch runs a whole decode position: 28 layers plus the
-// tied lm_head and greedy argmax (qwen_decoder_forward,
-// qwen_asr_decoder.c:388-476). One CTA per SM; phases are separated by a
-// grid barrier whose spin is bounded (error word + early return, never a
-// trap). Per layer:
-//   A  input RMSNorm (every CTA, redundantly) -> QKV matvec rows
-//   B  per-head Q/K RMSNorm + NeoX RoPE + bf16 KV append + split-K attention;
-//      the last CTA of each KV head merges the splits
-//   C  O-proj matvec rows + residual
-//   D  post-attention RMSNorm -> gate/up row pairs + SwiGLU
-//   E  down matvec rows + residual
-// then F: final RMSNorm, lm_head rows with a (value, lowest index) argmax.
+// One cooperative launch runs one decode position end to end: 28 layers, the
+// tied lm_head and the greedy argmax (qwen_decoder_forward,
+// qwen_asr_decoder.c:388-476). One CTA per SM, two roles:
 //
-// Weights are streamed once per step with 16-byte non-allocating loads; all
-// data that other CTAs write during the launch is read with ld.global.cg so
-// a stale L1 line is never used.
+//  * producer warp: streams this CTA's slice of EVERY weight matrix of the
+//    step (layer by layer, then the lm_head rows) into a ring of shared-memory
+//    stages with cp.async.bulk + mbarrier transaction counts. It never waits
+//    for activations, so weight traffic runs ahead across phase boundaries
+//    and the whole step is one continuous HBM stream.
+//  * 8 consumer warps: per layer
+//      A  input RMSNorm (each CTA, from the full residual) -> QKV rows
+//      B  per-head QK RMSNorm + NeoX RoPE + fp16 KV append + split-K
+//         attention (one unit per (KV head, key range) CTA; split 0 merges)
+//      C  O-proj rows + residual
+//      D  post-attention RMSNorm -> gate/up row pairs + SwiGLU
+//      E  down rows + residual
+//    then F: final RMSNorm, lm_head rows, (value, lowest index) argmax.
+//
+// Inter-CTA data are "tagged" 64-bit words: high 32 bits = epoch of the
+// phase that wrote it, low 32 bits = the f32 value. One 64-bit store is
+// single-copy atomic, so a reader polls the data itself until the epoch
+// matches: no grid barrier, no fence, one L2 round trip per dependency, and
+// attention units wait only for the q/k/v rows of their own KV head.
+//
+// Every wait is bounded (about one second of SM clock). A wait that runs out
+// records an error code, raises a CTA-local abort flag and returns; all
+// consumer warps still pass every named barrier, the producer stops issuing
+// and waits (bounded) for its copies in flight, and the kernel returns.
 #include "qdb_common.cuh"
 #include "qdb_kernels.h"
 
 namespace {
 
-constexpr int WPB = QDB_STEP_THREADS / 32;  // warps per CTA
-constexpr int ATT_KEYS = 8;                 // keys per warp iteration
-constexpr int MAX_GQA = 8;                  // query heads per KV head supported
+constexpr int NCW = 8;                    // consumer warps
+constexpr int NCT = NCW * 32;             // consumer threads
+constexpr int NTHREADS = NCT + 32;        // + producer warp
+constexpr int STAGE_BYTES = 16384;
+constexpr int NSTAGE = 11;
+constexpr int ATT_KEYS = 8;               // keys per warp iteration
+constexpr int MAX_GQA = 8;
+constexpr int POLL = 24;                  // tagged words per consumer thread per vector load
 
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+static_assert(NTHREADS == QDB_STEP_THREADS, "thread count mismatch");
+
+typedef unsigned long long u64;
+
+struct Ctl {
+    volatile int *abort;  // CTA-local
+    int *err;             // global
+};
+
+__device__ __forceinline__ void st_tag(u64 *p, float v, unsigned ep) {
+    const u64 w = ((u64)ep << 32) | (u64)__float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ u64 ld_tag(const u64 *p) {
+    u64 w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+__device__ __forceinline__ unsigned tag_ep(u64 w) { return (unsigned)(w >> 32); }
+__device__ __forceinline__ float tag_val(u64 w) { return __uint_as_float((unsigned)w); }
+
+__device__ __forceinline__ bool timed_out(long long t0) { return clock64() - t0 > QDB_SPIN_LIMIT_CYCLES; }
+
+__device__ __forceinline__ void abort_now(const Ctl &c) {
+    *c.abort = 1;
+    set_error(c.err, QDB_ERR_BARRIER_TIMEOUT);
 }
 
-// Grid barrier on a monotonically increasing counter. Returns false when the
-// wait ran out (error recorded); callers then return from the kernel.
-__device__ bool grid_barrier(unsigned *bar, unsigned target, int *err, volatile int *s_ok) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(bar, 1u);
-        long long t0 = clock64();
-        int ok = 1;
-        while ((int)(ld_acquire_u32(bar) - target) < 0) {
-            if (clock64() - t0 > QDB_SPIN_LIMIT_CYCLES) {
-                ok = 0;
-                set_error(err, QDB_ERR_BARRIER_TIMEOUT);
-                break;
+// Checks the CTA flag and, every so often, the global error word (so one
+// CTA's failure stops the others quickly).
+__device__ __forceinline__ bool should_stop(const Ctl &c, int iter) {
+    if (*c.abort) return true;
+    if ((iter & 255) == 255 && *(volatile int *)c.err) {
+        *c.abort = 1;
+        return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory"); }
+
+// ---------------------------------------------------------------- mbarriers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(u64 *bar, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(u64 *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(u64 *bar, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try(u64 *bar, unsigned parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait; `check` = honour the abort flag.
+__device__ bool mbar_wait(u64 *bar, unsigned parity, const Ctl &c, bool check) {
+    const long long t0 = clock64();
+    for (int it = 0;; it++) {
+        if (mbar_try(bar, parity)) return true;
+        if (check && should_stop(c, it)) return false;
+        if (timed_out(t0)) {
+            abort_now(c);
+            return false;
+        }
+    }
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, u64 *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ---------------------------------------------------------------- schedule
+// A phase's matrix slice for CTA `c` of `G`: rows [r0, r1) of a [R, K] matrix,
+// processed in items of `ipr` rows (an item fits one ring stage).
+struct Slice {
+    const uint16_t *w;
+    int r0, r1, K, ipr;
+    __device__ int items() const { return r1 > r0 ? (r1 - r0 + ipr - 1) / ipr : 0; }
+};
+
+__device__ __forceinline__ Slice make_slice(const uint16_t *w, int R, int K, int c, int G, bool pairs) {
+    Slice s;
+    s.w = w;
+    s.K = K;
+    const int units = pairs ? R / 2 : R;
+    const int u0 = (int)((long long)units * c / G), u1 = (int)((long long)units * (c + 1) / G);
+    s.r0 = pairs ? 2 * u0 : u0;
+    s.r1 = pairs ? 2 * u1 : u1;
+    int ipr = STAGE_BYTES / (K * 2);
+    if (ipr > 32) ipr = 32;  // one output row per lane
+    if (pairs) ipr &= ~1;
+    s.ipr = ipr < 1 ? 1 : ipr;
+    return s;
+}
+
+// Phase p (0..3 = QKV, O, GU, DOWN) of a layer, or the lm_head (p = 4).
+__device__ __forceinline__ Slice phase_slice(const QdbStepArgs &a, int layer, int p) {
+    const QdbDims &d = a.d;
+    const int qd = d.Hq * QDB_HD, kvd = d.Hkv * QDB_HD;
+    const int c = blockIdx.x, G = gridDim.x;
+    if (p == 4) return make_slice(a.embed, d.V, d.h, c, G, false);
+    const QdbLayerW &lw = a.layers[layer];
+    switch (p) {
+        case 0: return make_slice(lw.qkv, qd + 2 * kvd, d.h, c, G, false);
+        case 1: return make_slice(lw.o, d.h, qd, c, G, false);
+        case 2: return make_slice(lw.gu, 2 * d.I, d.h, c, G, true);
+        default: return make_slice(lw.down, d.h, d.I, c, G, false);
+    }
+}
+
+// ---------------------------------------------------------------- producer
+__device__ __noinline__ void producer(const QdbStepArgs &a, unsigned char *ring, u64 *full, u64 *empty, const Ctl &c) {
+    const int lane = threadIdx.x & 31;
+    if (lane != 0) return;
+    unsigned it = 0;
+    bool ok = true;
+    for (int layer = 0; layer <= a.d.L && ok; layer++) {
+        const int p_end = layer < a.d.L ? 4 : 5;
+        for (int p = layer < a.d.L ? 0 : 4; p < p_end && ok; p++) {
+            const Slice s = phase_slice(a, layer, p);
+            const size_t row_bytes = (size_t)s.K * 2;
+            for (int r = s.r0; r < s.r1 && ok; r += s.ipr, it++) {
+                const int nr = min(s.ipr, s.r1 - r);
+                const unsigned st = it % NSTAGE;
+                if (it >= NSTAGE && !mbar_wait(&empty[st], ((it / NSTAGE) - 1) & 1, c, true)) {
+                    ok = false;
+                    break;
+                }
+                const unsigned bytes = (unsigned)(nr * row_bytes);
+                mbar_expect_tx(&full[st], bytes);
+                bulk_g2s(ring + (size_t)st * STAGE_BYTES, s.w + (size_t)r * s.K, bytes, &full[st]);
             }
         }
-        __threadfence();
-        *s_ok = ok;
     }
-    __syncthreads();
-    return *s_ok != 0;
+    if (!ok) {
+        // Drain: wait (bounded, ignoring the abort flag) for the copies in
+        // flight, i.e. the latest item issued into each stage.
+        for (unsigned k = 0; k < NSTAGE && k < it; k++) {
+            const unsigned i = it - 1 - k;
+            mbar_wait(&full[i % NSTAGE], (i / NSTAGE) & 1, c, false);
+        }
+    }
 }
 
-// Block-wide sum (all threads get the result). red: >= WPB floats of smem.
-__device__ float block_sum(float v, float *red) {
+// ---------------------------------------------------------------- consumer helpers
+// Fills dst[0..n) from tagged words src expecting epoch ep (n <= POLL*NCT).
+// All still-missing words are re-read together each round.
+__device__ __noinline__ bool load_tagged(const u64 *src, int n, unsigned ep, float *dst, const Ctl &c) {
+    const int t = threadIdx.x;
+    uint32_t pending = 0;
+    u64 w[POLL];
+#pragma unroll
+    for (int j = 0; j < POLL; j++) {
+        const int i = t + j * NCT;
+        if (i < n) {
+            pending |= 1u << j;
+            w[j] = ld_tag(src + i);
+        }
+    }
+    const long long t0 = clock64();
+    for (int iter = 0;; iter++) {
+#pragma unroll
+        for (int j = 0; j < POLL; j++)
+            if ((pending >> j) & 1u) {
+                if (tag_ep(w[j]) == ep) {
+                    dst[t + j * NCT] = tag_val(w[j]);
+                    pending &= ~(1u << j);
+                }
+            }
+        if (!pending) return true;
+        if (should_stop(c, iter)) return false;
+        if (timed_out(t0)) {
+            abort_now(c);
+            return false;
+        }
+#pragma unroll
+        for (int j = 0; j < POLL; j++)
+            if ((pending >> j) & 1u) w[j] = ld_tag(src + t + j * NCT);
+    }
+}
+
+// Consumer-wide sum; red has NCW floats.
+__device__ float consumer_sum(float v, float *red) {
     v = warp_sum(v);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    __syncthreads();
     if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = lane < WPB ? red[lane] : 0.f;
-    return warp_sum(t);
+    consumer_sync();
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NCW; i++) s += red[i];
+    consumer_sync();
+    return s;
 }
 
-// xs[i] = x[i] * (1/sqrtf(mean(x^2)+eps)) * w[i] into shared memory
-// (qwen_rms_norm, qwen_asr_kernels.c:750-809). x is either global f32
-// (read through L2) or, when emb != null, a bf16 embedding row.
-__device__ void norm_to_smem(const float *x, const uint16_t *emb, const float *w, int h, float eps,
-                             float *xs, float *red) {
+// act[i] = x[i] * (1/sqrtf(mean(x^2)+eps)) * w[i]  (qwen_rms_norm,
+// qwen_asr_kernels.c:750-809), x already in xraw.
+__device__ void rmsnorm_smem(const float *xraw, const float *w, int h, float eps, float *act, float *red) {
     float ss = 0.f;
-    for (int i = threadIdx.x; i < h; i += blockDim.x) {
-        float v = emb ? __uint_as_float(((uint32_t)emb[i]) << 16) : __ldcg(x + i);
-        xs[i] = v;
-        ss += v * v;
-    }
-    ss = block_sum(ss, red);
+    for (int i = threadIdx.x; i < h; i += NCT) ss += xraw[i] * xraw[i];
+    ss = consumer_sum(ss, red);
     const float inv = 1.0f / sqrtf(ss / (float)h + eps);
-    for (int i = threadIdx.x; i < h; i += blockDim.x) xs[i] = xs[i] * inv * w[i];
-    __syncthreads();
+    for (int i = threadIdx.x; i < h; i += NCT) act[i] = xraw[i] * inv * w[i];
+    consumer_sync();
 }
 
-__device__ void load_to_smem(const float *src, int n, float *xs) {
-    for (int i = threadIdx.x; i < n; i += blockDim.x) xs[i] = __ldcg(src + i);
-    __syncthreads();
-}
-
-// Dot of one bf16 weight row (K elements, K % 256 == 0) with xs (smem), one
-// warp; every lane gets the sum. Up to 8 16-byte loads per lane in flight.
-__device__ __forceinline__ float row_dot(const uint16_t *wrow, const float *xs, int K) {
+// Dot products of nr rows (bf16, row length K, in smem) with act (smem f32).
+// out[r] for r < nr (nr <= 32). Two rows at a time; lanes stride 8 elements.
+__device__ __forceinline__ void stage_dots(const uint16_t *wst, int nr, int K, const float *act, float *out) {
     const int lane = threadIdx.x & 31;
-    const uint4 *wp = reinterpret_cast<const uint4 *>(wrow);
     const int nv = K >> 8;
-    float acc = 0.f;
-    for (int i0 = 0; i0 < nv; i0 += 8) {
-        uint4 w[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++)
-            if (i0 + u < nv) w[u] = ldg_stream(wp + (i0 + u) * 32 + lane);
-#pragma unroll
-        for (int u = 0; u < 8; u++)
-            if (i0 + u < nv) {
-                const float4 *xp = reinterpret_cast<const float4 *>(xs + ((i0 + u) * 32 + lane) * 8);
-                acc = dot8(w[u], xp[0], xp[1], acc);
-            }
+    for (int r = 0; r < nr; r += 2) {
+        const bool two = r + 1 < nr;
+        const uint4 *p0 = reinterpret_cast<const uint4 *>(wst + (size_t)r * K);
+        const uint4 *p1 = reinterpret_cast<const uint4 *>(wst + (size_t)(r + (two ? 1 : 0)) * K);
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll 4
+        for (int j = 0; j < nv; j++) {
+            const int e = (j * 32 + lane);
+            const uint4 w0 = p0[e];
+            const uint4 w1 = p1[e];
+            const float4 xa = *reinterpret_cast<const float4 *>(act + e * 8);
+            const float4 xb = *reinterpret_cast<const float4 *>(act + e * 8 + 4);
+            a0 = dot8(w0, xa, xb, a0);
+            a1 = dot8(w1, xa, xb, a1);
+        }
+        a0 = warp_sum(a0);
+        a1 = warp_sum(a1);
+        out[r] = a0;
+        if (two) out[r + 1] = a1;
     }
-    return warp_sum(acc);
 }
 
-// Two rows at once (independent loads in flight for both).
-__device__ __forceinline__ void row_dot2(const uint16_t *r0, const uint16_t *r1, const float *xs, int K,
-                                         float &s0, float &s1) {
-    const int lane = threadIdx.x & 31;
-    const uint4 *p0 = reinterpret_cast<const uint4 *>(r0);
-    const uint4 *p1 = reinterpret_cast<const uint4 *>(r1);
-    const int nv = K >> 8;
-    float a0 = 0.f, a1 = 0.f;
-    for (int i0 = 0; i0 < nv; i0 += 4) {
-        uint4 w0[4], w1[4];
-#pragma unroll
-        for (int u = 0; u < 4; u++)
-            if (i0 + u < nv) {
-                w0[u] = ldg_stream(p0 + (i0 + u) * 32 + lane);
-                w1[u] = ldg_stream(p1 + (i0 + u) * 32 + lane);
-            }
-#pragma unroll
-        for (int u = 0; u < 4; u++)
-            if (i0 + u < nv) {
-                const float4 *xp = reinterpret_cast<const float4 *>(xs + ((i0 + u) * 32 + lane) * 8);
-                const float4 xa = xp[0], xb = xp[1];
-                a0 = dot8(w0[u], xa, xb, a0);
-                a1 = dot8(w1[u], xa, xb, a1);
-            }
-    }
-    s0 = warp_sum(a0);
-    s1 = warp_sum(a1);
-}
+// ---------------------------------------------------------------- attention
+struct AttnSmem {
+    float q[MAX_GQA][QDB_HD];
+    float knew[QDB_HD];
+    float vnew[QDB_HD];
+    float m[NCW][MAX_GQA];
+    float l[NCW][MAX_GQA];
+    float o[NCW][MAX_GQA][QDB_HD];
+};
 
-// Per-head RMSNorm then NeoX rotation of one 128-float head held in smem,
-// one warp (qwen_rms_norm_per_head :811-873, qwen_apply_rope_neox :1182-1247).
+// Per-head RMSNorm then NeoX rotation of one 128-float head in smem, one warp
+// (qwen_rms_norm_per_head :811-873, qwen_apply_rope_neox :1182-1247).
 __device__ void head_norm_rope(float *v, const float *w, const float2 *rope_row, float eps) {
     const int lane = threadIdx.x & 31;
     float e[4];
 #pragma unroll
     for (int i = 0; i < 4; i++) e[i] = v[lane + 32 * i];
-    float ss = e[0] * e[0] + e[1] * e[1] + e[2] * e[2] + e[3] * e[3];
-    ss = warp_sum(ss);
+    const float ss = warp_sum(e[0] * e[0] + e[1] * e[1] + e[2] * e[2] + e[3] * e[3]);
     const float inv = 1.0f / sqrtf(ss / (float)QDB_HD + eps);
 #pragma unroll
     for (int i = 0; i < 4; i++) e[i] = e[i] * inv * w[lane + 32 * i];
-    // lane + 32*i: i = 0,1 first half (d = lane, lane+32); i = 2,3 second half.
 #pragma unroll
     for (int i = 0; i < 2; i++) {
         const float2 cs = rope_row[lane + 32 * i];
@@ -164,18 +320,39 @@ __device__ void head_norm_rope(float *v, const float *w, const float2 *rope_row,
     __syncwarp();
 }
 
-struct AttnSmem {
-    float q[MAX_GQA][QDB_HD];
-    float knew[QDB_HD];
-    float m[WPB][MAX_GQA];
-    float l[WPB][MAX_GQA];
-    float o[WPB][MAX_GQA][QDB_HD];
-};
+// Polls one 128-word head (4 words per lane, all in flight) with one warp.
+__device__ bool warp_load_head(const u64 *src, unsigned ep, float *dst, const Ctl &c) {
+    const int lane = threadIdx.x & 31;
+    u64 w[4];
+    uint32_t pending = 0xfu;
+#pragma unroll
+    for (int j = 0; j < 4; j++) w[j] = ld_tag(src + lane + 32 * j);
+    const long long t0 = clock64();
+    for (int iter = 0;; iter++) {
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            if (((pending >> j) & 1u) && tag_ep(w[j]) == ep) {
+                dst[lane + 32 * j] = tag_val(w[j]);
+                pending &= ~(1u << j);
+            }
+        if (!__any_sync(0xffffffffu, pending != 0)) break;
+        if (should_stop(c, iter)) return false;
+        if (timed_out(t0)) {
+            abort_now(c);
+            return false;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+            if ((pending >> j) & 1u) w[j] = ld_tag(src + lane + 32 * j);
+    }
+    __syncwarp();
+    return true;
+}
 
-// One attention work unit: KV head g, keys [p0, p1) of ctx = pos + 1.
-// Writes the unnormalised partial (m, l, o[128]) for its query heads.
+// Attention unit (KV head g, split s of S) for this step's position.
 template <int R>
-__device__ void attn_unit(const QdbStepArgs &a, int layer, int g, int s, int S, AttnSmem *sm) {
+__device__ __noinline__ void attn_unit(const QdbStepArgs &a, int layer, int g, int s, int S, unsigned ep, AttnSmem *sm,
+                          const Ctl &c) {
     const QdbDims &d = a.d;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int ctx = a.pos + 1;
@@ -186,29 +363,28 @@ __device__ void attn_unit(const QdbStepArgs &a, int layer, int g, int s, int S, 
     const QdbLayerW &lw = a.layers[layer];
     const float2 *rope_row = a.rope + (size_t)a.pos * (QDB_HD / 2);
     const size_t head_base = ((size_t)layer * d.Hkv + g) * (size_t)a.cap * QDB_HD;
-    const uint16_t *kc = a.kc + head_base;
-    const uint16_t *vc = a.vc + head_base;
-
-    // Query heads of this group: normalise + rotate (one warp per head).
-    for (int h = warp; h < R; h += WPB) {
-        for (int i = lane; i < QDB_HD; i += 32) sm->q[h][i] = __ldcg(a.qkv + (g * R + h) * QDB_HD + i);
-        __syncwarp();
-        head_norm_rope(sm->q[h], lw.q_norm, rope_row, d.eps);
-    }
-    // The unit holding position pos appends the new K/V row (bf16).
+    uint16_t *kc = a.kc + head_base;
+    uint16_t *vc = a.vc + head_base;
     const bool owns_new = (p0 <= a.pos && a.pos < p1);
-    if (owns_new && warp == WPB - 1) {
-        for (int i = lane; i < QDB_HD; i += 32) sm->knew[i] = __ldcg(a.qkv + qd + g * QDB_HD + i);
-        __syncwarp();
-        head_norm_rope(sm->knew, lw.k_norm, rope_row, d.eps);
-        uint16_t *kdst = const_cast<uint16_t *>(kc) + (size_t)a.pos * QDB_HD;
-        uint16_t *vdst = const_cast<uint16_t *>(vc) + (size_t)a.pos * QDB_HD;
-        for (int i = lane; i < QDB_HD; i += 32) {
-            kdst[i] = f32_to_bf16_rn(sm->knew[i]);
-            vdst[i] = f32_to_bf16_rn(__ldcg(a.qkv + qd + kvd + g * QDB_HD + i));
+
+    // q heads of this group (and the new K/V row for the owner), one warp each
+    for (int h = warp; h < R + (owns_new ? 2 : 0); h += NCW) {
+        if (h < R) {
+            if (warp_load_head(a.tqkv + (size_t)(g * R + h) * QDB_HD, ep, sm->q[h], c))
+                head_norm_rope(sm->q[h], lw.q_norm, rope_row, d.eps);
+        } else if (h == R) {
+            if (warp_load_head(a.tqkv + qd + (size_t)g * QDB_HD, ep, sm->knew, c)) {
+                head_norm_rope(sm->knew, lw.k_norm, rope_row, d.eps);
+                for (int i = lane; i < QDB_HD; i += 32)
+                    kc[(size_t)a.pos * QDB_HD + i] = f32_to_kv(sm->knew[i]);
+            }
+        } else {
+            if (warp_load_head(a.tqkv + qd + kvd + (size_t)g * QDB_HD, ep, sm->vnew, c))
+                for (int i = lane; i < QDB_HD; i += 32)
+                    vc[(size_t)a.pos * QDB_HD + i] = f32_to_kv(sm->vnew[i]);
         }
     }
-    __syncthreads();
+    consumer_sync();  // new K/V row stored (global writes by this CTA are visible to it)
 
     const float scale = 1.0f / sqrtf((float)QDB_HD);
     const int sub = lane & 3, kk = lane >> 2;
@@ -220,67 +396,68 @@ __device__ void attn_unit(const QdbStepArgs &a, int layer, int g, int s, int S, 
 #pragma unroll
         for (int e = 0; e < 4; e++) o[h][e] = 0.f;
     }
-    for (int base = p0 + warp * ATT_KEYS; base < p1; base += WPB * ATT_KEYS) {
-        const int j = base + kk;
-        const bool valid = j < p1;
-        uint4 kv4[4];
-        if (valid) {
-            const uint4 *kp = reinterpret_cast<const uint4 *>(kc + (size_t)j * QDB_HD + sub * 32);
-#pragma unroll
-            for (int u = 0; u < 4; u++) kv4[u] = __ldcg(kp + u);
-        }
-        uint2 vv[ATT_KEYS];
-#pragma unroll
-        for (int t = 0; t < ATT_KEYS; t++) {
-            const int jt = base + t;
-            if (jt < p1) vv[t] = __ldcg(reinterpret_cast<const uint2 *>(vc + (size_t)jt * QDB_HD + lane * 4));
-            else vv[t] = make_uint2(0u, 0u);
-        }
-        float sc[R];
-#pragma unroll
-        for (int h = 0; h < R; h++) {
-            float acc = 0.f;
+    if (!*c.abort) {
+        for (int base = p0 + warp * ATT_KEYS; base < p1; base += NCW * ATT_KEYS) {
+            const int j = base + kk;
+            const bool valid = j < p1;
+            uint4 kv4[4];
             if (valid) {
-                const float *qv = sm->q[h] + sub * 32;
+                const uint4 *kp = reinterpret_cast<const uint4 *>(kc + (size_t)j * QDB_HD + sub * 32);
 #pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const float4 qa = *reinterpret_cast<const float4 *>(qv + u * 8);
-                    const float4 qb = *reinterpret_cast<const float4 *>(qv + u * 8 + 4);
-                    acc = dot8(kv4[u], qa, qb, acc);
-                }
+                for (int u = 0; u < 4; u++) kv4[u] = __ldcg(kp + u);
             }
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-            sc[h] = valid ? acc * scale : -INFINITY;
-        }
-#pragma unroll
-        for (int h = 0; h < R; h++) {
-            float cm = sc[h];
-            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
-            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
-            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
-            const float mn = fmaxf(m[h], cm);
-            const float corr = expf(m[h] - mn);
-            const float p = valid ? expf(sc[h] - mn) : 0.f;
-            float ps = p;
-            ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-            ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-            ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-            l[h] = l[h] * corr + ps;  // xor 4/8/16 sums the 8 keys once each
-#pragma unroll
-            for (int e = 0; e < 4; e++) o[h][e] *= corr;
+            uint2 vv[ATT_KEYS];
 #pragma unroll
             for (int t = 0; t < ATT_KEYS; t++) {
-                const float pt = __shfl_sync(0xffffffffu, p, t * 4);
-                o[h][0] = fmaf(pt, bf16lo(vv[t].x), o[h][0]);
-                o[h][1] = fmaf(pt, bf16hi(vv[t].x), o[h][1]);
-                o[h][2] = fmaf(pt, bf16lo(vv[t].y), o[h][2]);
-                o[h][3] = fmaf(pt, bf16hi(vv[t].y), o[h][3]);
+                const int jt = base + t;
+                vv[t] = jt < p1 ? __ldcg(reinterpret_cast<const uint2 *>(vc + (size_t)jt * QDB_HD + lane * 4))
+                                : make_uint2(0u, 0u);
             }
-            m[h] = mn;
+            float sc[R];
+#pragma unroll
+            for (int h = 0; h < R; h++) {
+                float acc = 0.f;
+                if (valid) {
+                    const float *qv = sm->q[h] + sub * 32;
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const float4 qa = *reinterpret_cast<const float4 *>(qv + u * 8);
+                        const float4 qb = *reinterpret_cast<const float4 *>(qv + u * 8 + 4);
+                        acc = dot8_kv(kv4[u], qa, qb, acc);
+                    }
+                }
+                acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+                sc[h] = valid ? acc * scale : -INFINITY;
+            }
+#pragma unroll
+            for (int h = 0; h < R; h++) {
+                float cm = sc[h];
+                cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
+                cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
+                cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
+                const float mn = fmaxf(m[h], cm);
+                const float corr = expf(m[h] - mn);
+                const float p = valid ? expf(sc[h] - mn) : 0.f;
+                float ps = p;
+                ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+                ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+                ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+                l[h] = l[h] * corr + ps;
+#pragma unroll
+                for (int e = 0; e < 4; e++) o[h][e] *= corr;
+#pragma unroll
+                for (int t = 0; t < ATT_KEYS; t++) {
+                    const float pt = __shfl_sync(0xffffffffu, p, t * 4);
+                    o[h][0] = fmaf(pt, kvlo(vv[t].x), o[h][0]);
+                    o[h][1] = fmaf(pt, kvhi(vv[t].x), o[h][1]);
+                    o[h][2] = fmaf(pt, kvlo(vv[t].y), o[h][2]);
+                    o[h][3] = fmaf(pt, kvhi(vv[t].y), o[h][3]);
+                }
+                m[h] = mn;
+            }
         }
     }
-    // Merge the warps of this CTA.
 #pragma unroll
     for (int h = 0; h < R; h++) {
         if (lane == 0) {
@@ -290,179 +467,220 @@ __device__ void attn_unit(const QdbStepArgs &a, int layer, int g, int s, int S, 
 #pragma unroll
         for (int e = 0; e < 4; e++) sm->o[warp][h][lane * 4 + e] = o[h][e];
     }
-    __syncthreads();
-    for (int t = threadIdx.x; t < R * QDB_HD; t += blockDim.x) {
+    consumer_sync();
+    // merge the warps; write the unit partial (m, l, o) tagged
+    for (int t = threadIdx.x; t < R * QDB_HD; t += NCT) {
         const int h = t / QDB_HD, dd = t % QDB_HD;
         float M = -INFINITY;
-        for (int w = 0; w < WPB; w++) M = fmaxf(M, sm->m[w][h]);
+#pragma unroll
+        for (int w = 0; w < NCW; w++) M = fmaxf(M, sm->m[w][h]);
         float L = 0.f, O = 0.f;
         if (M != -INFINITY) {
-            for (int w = 0; w < WPB; w++) {
+#pragma unroll
+            for (int w = 0; w < NCW; w++) {
                 const float f = expf(sm->m[w][h] - M);
                 L += sm->l[w][h] * f;
                 O += sm->o[w][h][dd] * f;
             }
         }
-        float *dst = a.part + ((size_t)(g * R + h) * S + s) * (2 + QDB_HD);
+        u64 *dst = a.tpart + ((size_t)(g * R + h) * S + s) * (2 + QDB_HD);
         if (dd == 0) {
-            dst[0] = M;
-            dst[1] = L;
+            st_tag(dst, M, ep);
+            st_tag(dst + 1, L, ep);
         }
-        dst[2 + dd] = O;
+        st_tag(dst + 2 + dd, O, ep);
     }
-}
-
-// Last unit of KV head g: merge the S split partials into attn.
-template <int R>
-__device__ void attn_merge(const QdbStepArgs &a, int g, int S) {
-    for (int t = threadIdx.x; t < R * QDB_HD; t += blockDim.x) {
+    if (s != 0) return;
+    // split 0 merges all splits of its KV head into attn (running max merge)
+    for (int t = threadIdx.x; t < R * QDB_HD; t += NCT) {
         const int h = t / QDB_HD, dd = t % QDB_HD;
-        const float *src = a.part + (size_t)(g * R + h) * S * (2 + QDB_HD);
-        float M = -INFINITY;
-        for (int s = 0; s < S; s++) M = fmaxf(M, __ldcg(src + s * (2 + QDB_HD)));
-        float L = 0.f, O = 0.f;
-        for (int s = 0; s < S; s++) {
-            const float ms = __ldcg(src + s * (2 + QDB_HD));
-            if (ms == -INFINITY) continue;
-            const float f = expf(ms - M);
-            L += __ldcg(src + s * (2 + QDB_HD) + 1) * f;
-            O += __ldcg(src + s * (2 + QDB_HD) + 2 + dd) * f;
-        }
-        a.attn[(g * R + h) * QDB_HD + dd] = L > 0.f ? O / L : 0.f;
-    }
-}
-
-template <int R>
-__device__ void phase_attention(const QdbStepArgs &a, int layer, AttnSmem *sm, volatile int *s_last) {
-    const int S = a.splits;
-    const int units = a.d.Hkv * S;
-    for (int u = blockIdx.x; u < units; u += gridDim.x) {
-        const int g = u / S, s = u % S;
-        attn_unit<R>(a, layer, g, s, S, sm);
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence();
-            const unsigned old = atomicAdd(a.cnt + g, 1u);
-            *s_last = (old == (unsigned)S - 1u);
-            __threadfence();
-        }
-        __syncthreads();
-        if (*s_last) {
-            attn_merge<R>(a, g, S);
-            __syncthreads();
-            if (threadIdx.x == 0) a.cnt[g] = 0u;
-        }
-        __syncthreads();
-    }
-}
-
-template <int R>
-__global__ void __launch_bounds__(QDB_STEP_THREADS, 1) step_kernel(const QdbStepArgs a) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    __shared__ float red[32];
-    __shared__ volatile int s_flag;
-    float *xs = reinterpret_cast<float *>(smem_raw);
-    AttnSmem *asm_ = reinterpret_cast<AttnSmem *>(smem_raw);
-
-    const QdbDims &d = a.d;
-    const int h = d.h, qd = d.Hq * QDB_HD, kvd = d.Hkv * QDB_HD, I = d.I;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gw = blockIdx.x * WPB + warp, TW = gridDim.x * WPB;
-    unsigned target = a.bar_base;
-
-    const uint16_t *emb_row = nullptr;
-    if (a.token_in) emb_row = a.embed + (size_t)__ldcg(a.token_in) * h;
-
-    for (int layer = 0; layer < d.L; layer++) {
-        const QdbLayerW &lw = a.layers[layer];
-        // ---- A: input norm + QKV rows ----
-        const bool first = (layer == 0 && emb_row != nullptr);
-        norm_to_smem(a.x, first ? emb_row : nullptr, lw.in_norm, h, d.eps, xs, red);
-        if (first && blockIdx.x == 0)
-            for (int i = threadIdx.x; i < h; i += blockDim.x) a.x[i] = __uint_as_float(((uint32_t)emb_row[i]) << 16);
-        {
-            const int R3 = qd + 2 * kvd;
-            for (int r = gw; r < R3; r += 2 * TW) {
-                const int r1 = r + TW;
-                if (r1 < R3) {
-                    float s0, s1;
-                    row_dot2(lw.qkv + (size_t)r * h, lw.qkv + (size_t)r1 * h, xs, h, s0, s1);
-                    if (lane == 0) { a.qkv[r] = s0; a.qkv[r1] = s1; }
-                } else {
-                    const float s0 = row_dot(lw.qkv + (size_t)r * h, xs, h);
-                    if (lane == 0) a.qkv[r] = s0;
+        const u64 *src = a.tpart + (size_t)(g * R + h) * S * (2 + QDB_HD);
+        float M = -INFINITY, L = 0.f, O = 0.f;
+        const long long t0 = clock64();
+        for (int q = 0; q < S; q++) {
+            const u64 *e = src + (size_t)q * (2 + QDB_HD);
+            float mq, lq, oq;
+            for (int iter = 0;; iter++) {
+                const u64 w0 = ld_tag(e), w1 = ld_tag(e + 1), w2 = ld_tag(e + 2 + dd);
+                if (tag_ep(w0) == ep && tag_ep(w1) == ep && tag_ep(w2) == ep) {
+                    mq = tag_val(w0);
+                    lq = tag_val(w1);
+                    oq = tag_val(w2);
+                    break;
+                }
+                if (should_stop(c, iter)) return;
+                if (timed_out(t0)) {
+                    abort_now(c);
+                    return;
                 }
             }
+            if (mq == -INFINITY) continue;
+            if (mq > M) {
+                const float f = expf(M - mq);
+                L = L * f + lq;
+                O = O * f + oq;
+                M = mq;
+            } else {
+                const float f = expf(mq - M);
+                L += lq * f;
+                O += oq * f;
+            }
         }
-        target += gridDim.x;
-        if (!grid_barrier(a.bar, target, a.err, &s_flag)) return;
+        st_tag(a.tattn + (size_t)(g * R + h) * QDB_HD + dd, L > 0.f ? O / L : 0.f, ep);
+    }
+}
 
-        // ---- B: QK norm, RoPE, KV append, attention ----
-        phase_attention<R>(a, layer, asm_, &s_flag);
-        target += gridDim.x;
-        if (!grid_barrier(a.bar, target, a.err, &s_flag)) return;
+// ---------------------------------------------------------------- the kernel
+template <int R>
+__global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    __shared__ __align__(8) u64 full[NSTAGE], empty[NSTAGE];
+    __shared__ float red[NCW];
+    __shared__ float outs[NCW][32];
+    __shared__ u64 wbest[NCW];
+    __shared__ volatile int s_abort;
+    __shared__ int s_last;
 
-        // ---- C: O-proj + residual ----
-        load_to_smem(a.attn, qd, xs);
-        for (int r = gw; r < h; r += TW) {
-            const float s0 = row_dot(lw.o + (size_t)r * qd, xs, qd);
-            if (lane == 0) a.x[r] = __ldcg(a.x + r) + s0;
+    const QdbDims &d = a.d;
+    const int h = d.h, qd = d.Hq * QDB_HD, I = d.I;
+    unsigned char *ring = smem_raw;
+    float *xraw = reinterpret_cast<float *>(smem_raw + (size_t)NSTAGE * STAGE_BYTES);
+    float *act = xraw + h;
+    AttnSmem *asm_ = reinterpret_cast<AttnSmem *>(act);
+
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        for (int i = 0; i < NSTAGE; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
         }
-        target += gridDim.x;
-        if (!grid_barrier(a.bar, target, a.err, &s_flag)) return;
-
-        // ---- D: post-attention norm + gate/up pairs + SwiGLU ----
-        norm_to_smem(a.x, nullptr, lw.post_norm, h, d.eps, xs, red);
-        for (int j = gw; j < I; j += TW) {
-            float g, u;
-            row_dot2(lw.gu + (size_t)(2 * j) * h, lw.gu + (size_t)(2 * j + 1) * h, xs, h, g, u);
-            if (lane == 0) a.act[j] = silu_mul(g, u);
-        }
-        target += gridDim.x;
-        if (!grid_barrier(a.bar, target, a.err, &s_flag)) return;
-
-        // ---- E: down + residual ----
-        load_to_smem(a.act, I, xs);
-        for (int r = gw; r < h; r += TW) {
-            const float s0 = row_dot(lw.down + (size_t)r * I, xs, I);
-            if (lane == 0) a.x[r] = __ldcg(a.x + r) + s0;
-        }
-        target += gridDim.x;
-        if (!grid_barrier(a.bar, target, a.err, &s_flag)) return;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    Ctl c{&s_abort, a.err};
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp == NCW) {
+        producer(a, ring, full, empty, c);
+        return;
     }
 
-    // ---- F: final norm + tied lm_head + greedy argmax ----
-    norm_to_smem(a.x, nullptr, a.final_norm, h, d.eps, xs, red);
+    unsigned it = 0;  // ring item counter (same sequence as the producer)
+    auto run_items = [&](const Slice &s, int mode, unsigned ep, u64 &best) {
+        // mode 0: QKV store, 1: O + residual, 2: gate/up SwiGLU, 3: down + residual, 4: lm_head
+        const int n = s.items();
+        for (int k = 0; k < n; k++, it++) {
+            if ((int)(it % NCW) != warp) continue;
+            const unsigned st = it % NSTAGE;
+            if (*c.abort || !mbar_wait(&full[st], (it / NSTAGE) & 1, c, true)) continue;
+            const int r = s.r0 + k * s.ipr;
+            const int nr = min(s.ipr, s.r1 - r);
+            const uint16_t *wst = reinterpret_cast<const uint16_t *>(ring + (size_t)st * STAGE_BYTES);
+            stage_dots(wst, nr, s.K, act, outs[warp]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+            if (mode == 4) {
+                if (lane < nr) {
+                    const int row = r + lane;
+                    const float v = outs[warp][lane];
+                    if (a.logits_out) a.logits_out[row] = v;
+                    if (!(a.mask_eos && (row == QDB_ENDOFTEXT || row == QDB_IM_END)) && !isnan(v)) {
+                        const u64 key = argmax_key(v, row);
+                        best = key > best ? key : best;
+                    }
+                }
+            } else if (mode == 2) {
+                if (lane < nr / 2) {
+                    const int pr = r / 2 + lane;
+                    st_tag(a.tact + pr, silu_mul(outs[warp][2 * lane], outs[warp][2 * lane + 1]), ep);
+                }
+            } else if (lane < nr) {
+                const int row = r + lane;
+                const float v = outs[warp][lane];
+                if (mode == 0) st_tag(a.tqkv + row, v, ep);
+                else st_tag(a.tx + row, xraw[row] + v, ep);
+            }
+            __syncwarp();
+        }
+    };
+
+    u64 best = 0ull;
+    for (int layer = 0; layer < d.L; layer++) {
+        const unsigned epA = a.epoch + 5u * layer;
+        const QdbLayerW &lw = a.layers[layer];
+        // ---- A: residual -> xraw, input norm -> act, QKV rows
+        consumer_sync();
+        if (layer == 0) {
+            if (a.token_in) {
+                const uint16_t *e = a.embed + (size_t)(*a.token_in) * h;
+                for (int i = threadIdx.x; i < h; i += NCT) xraw[i] = __uint_as_float(((uint32_t)e[i]) << 16);
+            } else {
+                for (int i = threadIdx.x; i < h; i += NCT) xraw[i] = a.x_in[i];
+            }
+        } else if (!*c.abort) {
+            load_tagged(a.tx, h, epA - 1, xraw, c);  // written by E of the previous layer
+        }
+        consumer_sync();
+        rmsnorm_smem(xraw, lw.in_norm, h, d.eps, act, red);
+        run_items(phase_slice(a, layer, 0), 0, epA, best);
+
+        // ---- B: attention units
+        const int S = a.splits;
+        if ((int)blockIdx.x < d.Hkv * S) {
+            consumer_sync();
+            const int u = blockIdx.x;
+            attn_unit<R>(a, layer, u / S, u % S, S, epA + 1, asm_, c);
+        }
+
+        // ---- C: O-proj + residual
+        consumer_sync();
+        if (!*c.abort) load_tagged(a.tattn, qd, epA + 1, act, c);
+        consumer_sync();
+        run_items(phase_slice(a, layer, 1), 1, epA + 2, best);
+
+        // ---- D: post-attention norm + gate/up + SwiGLU
+        consumer_sync();
+        if (!*c.abort) load_tagged(a.tx, h, epA + 2, xraw, c);
+        consumer_sync();
+        rmsnorm_smem(xraw, lw.post_norm, h, d.eps, act, red);
+        run_items(phase_slice(a, layer, 2), 2, epA + 3, best);
+
+        // ---- E: down + residual
+        consumer_sync();
+        if (!*c.abort) load_tagged(a.tact, I, epA + 3, act, c);
+        consumer_sync();
+        run_items(phase_slice(a, layer, 3), 3, epA + 4, best);
+    }
+    // ---- F: final norm + lm_head + argmax
+    const unsigned epF = a.epoch + 5u * d.L;
+    consumer_sync();
+    if (!*c.abort) load_tagged(a.tx, h, epF - 1, xraw, c);
+    consumer_sync();
+    rmsnorm_smem(xraw, a.final_norm, h, d.eps, act, red);
     if (blockIdx.x == 0 && a.hidden_out)
-        for (int i = threadIdx.x; i < h; i += blockDim.x) a.hidden_out[i] = xs[i];
-    unsigned long long best = 0ull;
-    for (int r = gw; r < d.V; r += 2 * TW) {
-        const int r1 = r + TW;
-        float s0, s1 = 0.f;
-        if (r1 < d.V) row_dot2(a.embed + (size_t)r * h, a.embed + (size_t)r1 * h, xs, h, s0, s1);
-        else s0 = row_dot(a.embed + (size_t)r * h, xs, h);
-        if (lane == 0) {
-            if (a.logits_out) {
-                a.logits_out[r] = s0;
-                if (r1 < d.V) a.logits_out[r1] = s1;
-            }
-            if (!(a.mask_eos && (r == QDB_ENDOFTEXT || r == QDB_IM_END)) && !isnan(s0)) {
-                const unsigned long long k = argmax_key(s0, r);
-                best = k > best ? k : best;
-            }
-            if (r1 < d.V && !(a.mask_eos && (r1 == QDB_ENDOFTEXT || r1 == QDB_IM_END)) && !isnan(s1)) {
-                const unsigned long long k = argmax_key(s1, r1);
-                best = k > best ? k : best;
-            }
-        }
+        for (int i = threadIdx.x; i < h; i += NCT) a.hidden_out[i] = act[i];
+    run_items(phase_slice(a, 0, 4), 4, epF, best);
+    // reduce this CTA's best, publish, elect the last CTA
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const u64 t = __shfl_xor_sync(0xffffffffu, best, o);
+        best = t > best ? t : best;
     }
-    if (lane == 0 && best) atomicMax(a.best, best);
-    target += gridDim.x;
-    if (!grid_barrier(a.bar, target, a.err, &s_flag)) return;
-    if (blockIdx.x == 0 && threadIdx.x == 0) {
-        const unsigned long long b = __ldcg(a.best);
-        *a.token_out = argmax_key_index(b);
-        *a.best = 0ull;
+    if (lane == 0) wbest[warp] = best;
+    consumer_sync();
+    if (threadIdx.x == 0) {
+        u64 b = 0ull;
+        for (int w = 0; w < NCW; w++) b = wbest[w] > b ? wbest[w] : b;
+        if (b) atomicMax(a.best, b);
+        __threadfence();
+        const unsigned prev = atomicAdd(a.done, 1u);
+        s_last = (prev == gridDim.x - 1);
+        if (s_last) {
+            __threadfence();
+            const u64 fin = atomicMax(a.best, 0ull);
+            *a.token_out = argmax_key_index(fin);
+            atomicExch(a.best, 0ull);
+            atomicExch(a.done, 0u);
+        }
     }
 }
 
@@ -487,9 +705,14 @@ extern "C" int qdb_step_smem_bytes(const QdbDims &d) {
     int n = d.h;
     if (qd > n) n = qd;
     if (d.I > n) n = d.I;
-    int bytes = n * (int)sizeof(float);
-    if ((int)sizeof(AttnSmem) > bytes) bytes = (int)sizeof(AttnSmem);
-    return bytes;
+    int act = n * (int)sizeof(float);
+    if ((int)sizeof(AttnSmem) > act) act = (int)sizeof(AttnSmem);
+    return NSTAGE * STAGE_BYTES + d.h * (int)sizeof(float) + act;
+}
+
+extern "C" int qdb_step_max_splits(int grid, int kv_heads) {
+    int s = grid / kv_heads;
+    return s < 1 ? 1 : (s > 64 ? 64 : s);
 }
 
 template <int R>
@@ -498,13 +721,14 @@ static cudaError_t launch_r(const QdbStepArgs &a, int grid, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(step_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     void *args[] = {const_cast<QdbStepArgs *>(&a)};
-    return cudaLaunchCooperativeKernel((const void *)step_kernel<R>, dim3(grid), dim3(QDB_STEP_THREADS), args,
+    return cudaLaunchCooperativeKernel((const void *)step_kernel<R>, dim3(grid), dim3(NTHREADS), args,
                                        (size_t)smem, st);
 }
 
 extern "C" cudaError_t qdb_launch_step(const QdbStepArgs &a, int grid, cudaStream_t st) {
-    const int R = a.d.Hq / a.d.Hkv;
-    switch (R) {
+    if (a.d.h > POLL * NCT || a.d.I > POLL * NCT || a.d.Hq * QDB_HD > POLL * NCT) return cudaErrorInvalidValue;
+    if (a.splits < 1 || a.splits > 64 || a.d.Hkv * a.splits > grid) return cudaErrorInvalidValue;
+    switch (a.d.Hq / a.d.Hkv) {
         case 1: return launch_r<1>(a, grid, st);
         case 2: return launch_r<2>(a, grid, st);
         case 4: return launch_r<4>(a, grid, st);
