@@ -132,6 +132,17 @@ int qdb_forward_batch(qdb_session *const *sessions, int n, const float *embeds,
 int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, const int *first_tokens,
                             const int *pos, int n_steps, int *tokens_out);
 
+/* Profiling: runs one greedy step (token at position pos) with per-phase
+ * timestamps. trace_out receives [ctas][events] globaltimer values (ns); the
+ * events of each CTA are: start, then per layer {A entered, A data ready,
+ * B entered, C entered, C ready, D entered, D ready, E entered, E ready},
+ * then {F entered, F ready, end} (A = input norm + QKV, B = attention,
+ * C = O-proj, D = post-norm + gate/up, E = down, F = lm_head + argmax).
+ * Returns the number of events per CTA, or -1 (e.g. when max_words is too
+ * small). Stands in for the reference's per-stage timers
+ * (qwen_asr.c:606-607, :714-715) at the granularity of one step. */
+int qdb_trace_step(qdb_session *s, int token, int pos, unsigned long long *trace_out, int max_words);
+
 /* Waits for all queued work of the model's stream. */
 int qdb_model_sync(qdb_model *m);
 

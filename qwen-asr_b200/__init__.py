@@ -59,6 +59,8 @@ ABI = {
                                                ctypes.c_int, _i32p]),
     "qdb_model_sync": (ctypes.c_int, [ctypes.c_void_p]),
     "qdb_model_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
+    "qdb_trace_step": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                      ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]),
 }
 
 
@@ -193,6 +195,17 @@ class Session:
         if lib.qdb_decode_greedy(self.h, first_token, pos, n_steps, _ptr(out, _i32p)):
             raise _err("qdb_decode_greedy")
         return out[:n_steps]
+
+    def trace_step(self, token: int, pos: int, max_ctas: int = 1024) -> np.ndarray:
+        """One greedy step with per-phase globaltimer stamps: [ctas, events] ns."""
+        L = self.model.cfg.layers
+        ev = 1 + 9 * L + 3
+        buf = np.zeros(max_ctas * ev, np.uint64)
+        n = lib.qdb_trace_step(self.h, token, pos, buf.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), buf.size)
+        if n < 0:
+            raise _err("qdb_trace_step")
+        t = buf.reshape(-1, ev)
+        return t[t[:, 0] != 0]
 
     def close(self):
         if self.h and not _exiting[0]:

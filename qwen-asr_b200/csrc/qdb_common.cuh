@@ -13,6 +13,7 @@ enum {
     QDB_ERR_NONE = 0,
     QDB_ERR_BARRIER_TIMEOUT = 1,
     QDB_ERR_BAD_ARG = 2,
+    QDB_ERR_BOUNDS = 3,  // a self-check refused an access (details in err[1..3])
 };
 
 // About one second at the B200's ~1.9 GHz SM clock: the bound on every spin.
@@ -72,6 +73,18 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 
 __device__ __forceinline__ void set_error(int *err, int code) {
     if (err) atomicCAS(err, 0, code);
+}
+
+// Records a refused access: err[0] = QDB_ERR_BOUNDS (if first), err[1..3] =
+// which check and two values. Returns false so callers can skip the access.
+__device__ __forceinline__ bool check_or_record(bool ok, int *err, int which, long long v0, long long v1) {
+    if (ok) return true;
+    if (err && atomicCAS(err, 0, QDB_ERR_BOUNDS) == 0) {
+        err[1] = which;
+        err[2] = (int)v0;
+        err[3] = (int)v1;
+    }
+    return false;
 }
 
 __device__ __forceinline__ uint16_t f32_to_bf16_rn(float f) {

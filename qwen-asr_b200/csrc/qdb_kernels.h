@@ -46,12 +46,22 @@ struct QdbStepArgs {
     unsigned long long *best;     // argmax key, zero between steps
     unsigned *done;               // CTA completion counter, zero between steps
     unsigned epoch;               // first epoch of this launch
-    int *err;
+    int *err;                     // [4]: error code, then details of the first failed check
     int mask_eos;
+    // extents for the kernel's own bounds checks
+    const uint16_t *w_lo, *w_hi;  // all layer matrices
+    int rope_cap;
+    int part_len;                 // words in tpart
+    unsigned long long *trace;    // nullable [grid][qdb_step_trace_events(L)] globaltimer stamps (ns)
 };
 
+// Trace events of one step per CTA: start, then per layer A entered, A data
+// ready, B entered, C entered, C ready, D entered, D ready, E entered,
+// E ready; then F entered, F ready, end.
+__host__ __device__ static inline int qdb_step_trace_events(int layers) { return 1 + 9 * layers + 3; }
+
 // Epochs one decode step consumes (host advances the base by this much).
-static inline unsigned qdb_step_epochs(int layers) { return 5u * (unsigned)layers + 1u; }
+__host__ __device__ static inline unsigned qdb_step_epochs(int layers) { return 5u * (unsigned)layers + 1u; }
 
 #define QDB_STEP_THREADS 288
 
@@ -97,6 +107,6 @@ cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_p
                                  cudaStream_t st);
 cudaError_t qdb_launch_argmax_rows(const float *logits, int n, int V, int mask_eos, int *tokens,
                                    cudaStream_t st);
-cudaError_t qdb_launch_embed_rows(const uint16_t *embed, const int *tokens, float *x, int n, int h,
+cudaError_t qdb_launch_embed_rows(const uint16_t *embed, const int *tokens, float *x, int n, int h, int V,
                                   cudaStream_t st);
 }

@@ -384,13 +384,15 @@ __global__ void argmax_rows_kernel(const float *logits, int V, int mask_eos, int
             const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
             best = t > best ? t : best;
         }
-        if (threadIdx.x == 0) tokens[blockIdx.x] = argmax_key_index(best);
+        if (threadIdx.x == 0) tokens[blockIdx.x] = best ? argmax_key_index(best) : 0;
     }
 }
 
-__global__ void embed_rows_kernel(const uint16_t *embed, const int *tokens, float *x, int h) {
+__global__ void embed_rows_kernel(const uint16_t *embed, const int *tokens, float *x, int h, int V) {
     const int row = blockIdx.x;
-    const uint16_t *src = embed + (size_t)tokens[row] * h;
+    int tok = tokens[row];
+    if (tok < 0 || tok >= V) tok = 0;  // never gather outside the table
+    const uint16_t *src = embed + (size_t)tok * h;
     for (int i = threadIdx.x; i < h; i += blockDim.x) x[(size_t)row * h + i] = __uint_as_float(((uint32_t)src[i]) << 16);
 }
 
@@ -484,8 +486,8 @@ extern "C" cudaError_t qdb_launch_argmax_rows(const float *logits, int n, int V,
 }
 
 extern "C" cudaError_t qdb_launch_embed_rows(const uint16_t *embed, const int *tokens, float *x, int n, int h,
-                                             cudaStream_t st) {
+                                             int V, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
-    embed_rows_kernel<<<n, 256, 0, st>>>(embed, tokens, x, h);
+    embed_rows_kernel<<<n, 256, 0, st>>>(embed, tokens, x, h, V);
     return cudaGetLastError();
 }

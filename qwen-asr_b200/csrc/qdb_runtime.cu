@@ -152,7 +152,7 @@ extern "C" qdb_model *qdb_model_create(const qdb_config *cfg, int device) {
     if (cfg->kv_heads <= 0 || cfg->heads % cfg->kv_heads) { fail("heads must be a multiple of kv_heads"); return nullptr; }
     const int R = cfg->heads / cfg->kv_heads;
     if (R != 1 && R != 2 && R != 4 && R != 8) { fail("heads/kv_heads must be 1, 2, 4 or 8"); return nullptr; }
-    if (cfg->layers <= 0 || cfg->vocab <= 0) { fail("bad layers/vocab"); return nullptr; }
+    if (cfg->layers <= 0 || cfg->layers > 32 || cfg->vocab <= 0) { fail("layers must be 1..32 and vocab > 0"); return nullptr; }
     if (cfg->heads * QDB_HD % 256) { fail("heads*head_dim must be a multiple of 256"); return nullptr; }
     int ndev = qdb_device_count();
     if (device < 0 || device >= ndev) { fail("CUDA device %d not available (%d visible)", device, ndev); return nullptr; }
@@ -212,11 +212,11 @@ extern "C" qdb_model *qdb_model_create(const qdb_config *cfg, int device) {
         m->tpart = m->tact + n_act;
     }
     if (dev_alloc(&m->x_in, h) || dev_alloc(&m->hidden_dev, h) || dev_alloc(&m->logits_dev, cfg->vocab) ||
-        dev_alloc(&m->done, 1) || dev_alloc(&m->best, 1) || dev_alloc(&m->err, 1))
+        dev_alloc(&m->done, 1) || dev_alloc(&m->best, 1) || dev_alloc(&m->err, 4))
         return bad();
     if (cudaMemset(m->tags, 0, m->tags_len * 8) != cudaSuccess || cudaMemset(m->done, 0, sizeof(unsigned)) != cudaSuccess ||
         cudaMemset(m->best, 0, sizeof(unsigned long long)) != cudaSuccess ||
-        cudaMemset(m->err, 0, sizeof(int)) != cudaSuccess) { fail("scratch memset"); return bad(); }
+        cudaMemset(m->err, 0, 4 * sizeof(int)) != cudaSuccess) { fail("scratch memset"); return bad(); }
     size_t stage = h > (size_t)cfg->vocab ? h : (size_t)cfg->vocab;
     if (cudaMallocHost((void **)&m->h_stage, stage * sizeof(float)) != cudaSuccess ||
         cudaMallocHost((void **)&m->h_tok, sizeof(int) * 4096) != cudaSuccess) { fail("pinned alloc"); return bad(); }
@@ -380,17 +380,23 @@ extern "C" int qdb_session_reserve(qdb_session *s, int positions) {
 
 // ------------------------------------------------------------------ single-utterance step
 static int check_err(qdb_model *m) {
-    int e = 0;
-    CK(cudaMemcpy(&e, m->err, sizeof(int), cudaMemcpyDeviceToHost));
+    int ev[4] = {0, 0, 0, 0};
+    CK(cudaMemcpy(ev, m->err, sizeof(ev), cudaMemcpyDeviceToHost));
+    const int e = ev[0];
     if (e) {
-        // A bounded wait ran out: reset the step's device state.
-        cudaMemset(m->err, 0, sizeof(int));
+        // A bounded wait ran out or a check refused an access: reset the
+        // step's device state.
+        cudaMemset(m->err, 0, 4 * sizeof(int));
         cudaMemset(m->tags, 0, m->tags_len * 8);
         cudaMemset(m->done, 0, sizeof(unsigned));
         cudaMemset(m->best, 0, sizeof(unsigned long long));
         cudaDeviceSynchronize();
         m->epoch = 1;
-        return fail("device error code %d (a bounded wait in the decode step ran out)", e);
+        return fail("device error code %d (%s; check %d: %d %d)", e,
+                    e == 1   ? "a bounded wait in the decode step ran out"
+                    : e == 2 ? "invalid token in the decode step"
+                             : "an access refused by a bounds check",
+                    ev[1], ev[2], ev[3]);
     }
     return 0;
 }
@@ -424,6 +430,10 @@ static QdbStepArgs step_args(qdb_session *s, int pos) {
     a.done = m->done;
     a.err = m->err;
     a.mask_eos = m->mask_eos;
+    a.w_lo = m->w;
+    a.w_hi = m->w + m->layer_elems * m->cfg.layers;
+    a.rope_cap = m->rope_cap;
+    a.part_len = (int)((size_t)m->cfg.heads * m->max_splits * (2 + QDB_HD));
     return a;
 }
 
@@ -499,6 +509,40 @@ extern "C" int qdb_decode_greedy(qdb_session *s, int first_token, int pos, int n
     CK(cudaMemcpyAsync(tokens_out, m->tok_dev + 1, sizeof(int) * n_steps, cudaMemcpyDeviceToHost, m->st));
     CK(cudaStreamSynchronize(m->st));
     return check_err(m);
+}
+
+extern "C" int qdb_trace_step(qdb_session *s, int token, int pos, unsigned long long *trace_out, int max_words) {
+    g_err.clear();
+    if (!s || !trace_out) return fail("null argument");
+    if (!s->m) return fail("session's model has been freed");
+    qdb_model *m = s->m;
+    if (token < 0 || token >= m->cfg.vocab || pos < 0) return fail("bad token or position");
+    const int ev = qdb_step_trace_events(m->cfg.layers);
+    const size_t words = (size_t)m->grid * ev;
+    if ((size_t)max_words < words) return fail("trace buffer needs %zu words", words);
+    if (set_dev(m) || prep_pos(s, pos)) return -1;
+    unsigned long long *tr = nullptr;
+    if (dev_alloc(&tr, words)) return -1;
+    if (m->tok_cap < 2) {
+        cudaFree(m->tok_dev);
+        m->tok_cap = 0;
+        if (dev_alloc(&m->tok_dev, 4096)) { cudaFree(tr); return -1; }
+        m->tok_cap = 4096;
+    }
+    m->h_tok[0] = token;
+    int rc = 0;
+    QdbStepArgs a = step_args(s, pos);
+    a.token_in = m->tok_dev;
+    a.token_out = m->tok_dev + 1;
+    a.trace = tr;
+    if (cudaMemcpyAsync(m->tok_dev, m->h_tok, sizeof(int), cudaMemcpyHostToDevice, m->st) != cudaSuccess ||
+        launch_step(m, a) ||
+        cudaMemcpyAsync(trace_out, tr, words * 8, cudaMemcpyDeviceToHost, m->st) != cudaSuccess ||
+        cudaStreamSynchronize(m->st) != cudaSuccess)
+        rc = fail("trace step failed: %s", cudaGetErrorString(cudaGetLastError()));
+    cudaFree(tr);
+    if (rc == 0 && check_err(m)) return -1;
+    return rc ? -1 : ev;
 }
 
 // ------------------------------------------------------------------ row-batched path
@@ -668,7 +712,7 @@ extern "C" int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, cons
     CK(cudaMemcpyAsync(m->rs.tok, first_tokens, sizeof(int) * n, cudaMemcpyHostToDevice, m->st));
     for (int i = 0; i < n_steps; i++) {
         int *tin = m->rs.tok + (size_t)i * n;
-        CK(qdb_launch_embed_rows(m->embed, tin, m->rs.X, n, m->cfg.hidden, m->st));
+        CK(qdb_launch_embed_rows(m->embed, tin, m->rs.X, n, m->cfg.hidden, m->cfg.vocab, m->st));
         if (run_rows(m, n, false, m->rs.rowkv, i, nullptr, 0) || batch_tail(m, n, tin + n)) return -1;
     }
     CK(cudaMemcpyAsync(tokens_out, m->rs.tok + n, sizeof(int) * (size_t)n * n_steps, cudaMemcpyDeviceToHost, m->st));

@@ -37,9 +37,9 @@ constexpr int NCW = 8;                    // consumer warps
 constexpr int NCT = NCW * 32;             // consumer threads
 constexpr int NTHREADS = NCT + 32;        // + producer warp
 constexpr int STAGE_BYTES = 16384;
-constexpr int NSTAGE = 11;
+constexpr int NSTAGE = 10;
+constexpr int MAX_LAYERS = 32;             // layer table kept in shared memory
 constexpr int ATT_KEYS = 8;               // keys per warp iteration
-constexpr int MAX_GQA = 8;
 constexpr int POLL = 24;                  // tagged words per consumer thread per vector load
 
 static_assert(NTHREADS == QDB_STEP_THREADS, "thread count mismatch");
@@ -65,9 +65,23 @@ __device__ __forceinline__ float tag_val(u64 w) { return __uint_as_float((unsign
 
 __device__ __forceinline__ bool timed_out(long long t0) { return clock64() - t0 > QDB_SPIN_LIMIT_CYCLES; }
 
-__device__ __forceinline__ void abort_now(const Ctl &c) {
+// A wait ran out: raise the CTA abort flag and record the first failure with
+// its location (err[1] = wait site, err[2] = CTA, err[3] = warp).
+__device__ __forceinline__ void abort_now(const Ctl &c, int site = 0) {
     *c.abort = 1;
-    set_error(c.err, QDB_ERR_BARRIER_TIMEOUT);
+    if (c.err && atomicCAS(c.err, 0, QDB_ERR_BARRIER_TIMEOUT) == 0) {
+        c.err[1] = site;
+        c.err[2] = blockIdx.x;
+        c.err[3] = threadIdx.x >> 5;
+    }
+}
+
+// Abort flag as one decision for the whole warp (lane 0's view), so no warp
+// ever splits between a collective and an early exit.
+__device__ __forceinline__ bool warp_aborted(const Ctl &c) {
+    int v = 0;
+    if ((threadIdx.x & 31) == 0) v = *c.abort;
+    return __shfl_sync(0xffffffffu, v, 0) != 0;
 }
 
 // Checks the CTA flag and, every so often, the global error word (so one
@@ -105,16 +119,35 @@ __device__ __forceinline__ bool mbar_try(u64 *bar, unsigned parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait; `check` = honour the abort flag.
-__device__ bool mbar_wait(u64 *bar, unsigned parity, const Ctl &c, bool check) {
+// Bounded wait by ONE thread (the producer); `check` = honour the abort flag.
+__device__ bool mbar_wait(u64 *bar, unsigned parity, const Ctl &c, bool check, int site) {
     const long long t0 = clock64();
     for (int it = 0;; it++) {
         if (mbar_try(bar, parity)) return true;
         if (check && should_stop(c, it)) return false;
         if (timed_out(t0)) {
-            abort_now(c);
+            abort_now(c, site);
             return false;
         }
+    }
+}
+
+// Bounded wait by a whole warp: every lane observes the phase completion
+// (so the bulk-copied bytes are visible to it) and the result is uniform.
+__device__ bool mbar_wait_warp(u64 *bar, unsigned parity, const Ctl &c, int site) {
+    const long long t0 = clock64();
+    for (int it = 0;; it++) {
+        const bool done = mbar_try(bar, parity);
+        if (__all_sync(0xffffffffu, done)) return true;
+        int stop = 0;
+        if ((threadIdx.x & 31) == 0) {
+            stop = should_stop(c, it) ? 1 : 0;
+            if (!stop && timed_out(t0)) {
+                abort_now(c, site);
+                stop = 1;
+            }
+        }
+        if (__shfl_sync(0xffffffffu, stop, 0)) return false;
     }
 }
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, u64 *bar) {
@@ -123,6 +156,20 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
+}
+
+// Asynchronous 16-byte global -> shared copies (no registers held while the
+// thread goes on polling); completed with cp_async_wait().
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// Consumer threads start copying n floats (n % 4 == 0, 16-byte aligned) to smem.
+__device__ __forceinline__ void prefetch_f32(float *dst, const float *src, int n) {
+    for (int i = threadIdx.x * 4; i < n; i += NCT * 4) cp_async16(dst + i, src + i);
+    cp_async_commit();
 }
 
 // ---------------------------------------------------------------- schedule
@@ -150,12 +197,12 @@ __device__ __forceinline__ Slice make_slice(const uint16_t *w, int R, int K, int
 }
 
 // Phase p (0..3 = QKV, O, GU, DOWN) of a layer, or the lm_head (p = 4).
-__device__ __forceinline__ Slice phase_slice(const QdbStepArgs &a, int layer, int p) {
+__device__ __forceinline__ Slice phase_slice(const QdbStepArgs &a, const QdbLayerW *layers, int layer, int p) {
     const QdbDims &d = a.d;
     const int qd = d.Hq * QDB_HD, kvd = d.Hkv * QDB_HD;
     const int c = blockIdx.x, G = gridDim.x;
     if (p == 4) return make_slice(a.embed, d.V, d.h, c, G, false);
-    const QdbLayerW &lw = a.layers[layer];
+    const QdbLayerW &lw = layers[layer];
     switch (p) {
         case 0: return make_slice(lw.qkv, qd + 2 * kvd, d.h, c, G, false);
         case 1: return make_slice(lw.o, d.h, qd, c, G, false);
@@ -165,7 +212,8 @@ __device__ __forceinline__ Slice phase_slice(const QdbStepArgs &a, int layer, in
 }
 
 // ---------------------------------------------------------------- producer
-__device__ __noinline__ void producer(const QdbStepArgs &a, unsigned char *ring, u64 *full, u64 *empty, const Ctl &c) {
+__device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *layers, unsigned char *ring, u64 *full,
+                                      u64 *empty, const Ctl &c) {
     const int lane = threadIdx.x & 31;
     if (lane != 0) return;
     unsigned it = 0;
@@ -173,18 +221,28 @@ __device__ __noinline__ void producer(const QdbStepArgs &a, unsigned char *ring,
     for (int layer = 0; layer <= a.d.L && ok; layer++) {
         const int p_end = layer < a.d.L ? 4 : 5;
         for (int p = layer < a.d.L ? 0 : 4; p < p_end && ok; p++) {
-            const Slice s = phase_slice(a, layer, p);
+            const Slice s = phase_slice(a, layers, layer, p);
             const size_t row_bytes = (size_t)s.K * 2;
             for (int r = s.r0; r < s.r1 && ok; r += s.ipr, it++) {
                 const int nr = min(s.ipr, s.r1 - r);
                 const unsigned st = it % NSTAGE;
-                if (it >= NSTAGE && !mbar_wait(&empty[st], ((it / NSTAGE) - 1) & 1, c, true)) {
+                if (it >= NSTAGE && !mbar_wait(&empty[st], ((it / NSTAGE) - 1) & 1, c, true, 1)) {
                     ok = false;
                     break;
                 }
                 const unsigned bytes = (unsigned)(nr * row_bytes);
+                const uint16_t *src = s.w + (size_t)r * s.K;
+                const bool in_w = (src >= a.w_lo && src + (size_t)bytes / 2 <= a.w_hi);
+                const bool in_e = (src >= a.embed && src + (size_t)bytes / 2 <= a.embed + (size_t)a.d.V * a.d.h);
+                if (!check_or_record(((uintptr_t)src & 15) == 0 && (bytes & 15) == 0 && bytes <= STAGE_BYTES &&
+                                         bytes > 0 && (in_w || in_e),
+                                     a.err, 1, (long long)r, (long long)bytes)) {
+                    *c.abort = 1;
+                    ok = false;
+                    break;
+                }
                 mbar_expect_tx(&full[st], bytes);
-                bulk_g2s(ring + (size_t)st * STAGE_BYTES, s.w + (size_t)r * s.K, bytes, &full[st]);
+                bulk_g2s(ring + (size_t)st * STAGE_BYTES, src, bytes, &full[st]);
             }
         }
     }
@@ -193,7 +251,7 @@ __device__ __noinline__ void producer(const QdbStepArgs &a, unsigned char *ring,
         // flight, i.e. the latest item issued into each stage.
         for (unsigned k = 0; k < NSTAGE && k < it; k++) {
             const unsigned i = it - 1 - k;
-            mbar_wait(&full[i % NSTAGE], (i / NSTAGE) & 1, c, false);
+            mbar_wait(&full[i % NSTAGE], (i / NSTAGE) & 1, c, false, 2);
         }
     }
 }
@@ -201,7 +259,7 @@ __device__ __noinline__ void producer(const QdbStepArgs &a, unsigned char *ring,
 // ---------------------------------------------------------------- consumer helpers
 // Fills dst[0..n) from tagged words src expecting epoch ep (n <= POLL*NCT).
 // All still-missing words are re-read together each round.
-__device__ __noinline__ bool load_tagged(const u64 *src, int n, unsigned ep, float *dst, const Ctl &c) {
+__device__ __noinline__ bool load_tagged(const u64 *src, int n, unsigned ep, float *dst, const Ctl &c, int site) {
     const int t = threadIdx.x;
     uint32_t pending = 0;
     u64 w[POLL];
@@ -226,7 +284,7 @@ __device__ __noinline__ bool load_tagged(const u64 *src, int n, unsigned ep, flo
         if (!pending) return true;
         if (should_stop(c, iter)) return false;
         if (timed_out(t0)) {
-            abort_now(c);
+            abort_now(c, site);
             return false;
         }
 #pragma unroll
@@ -249,8 +307,10 @@ __device__ float consumer_sum(float v, float *red) {
 }
 
 // act[i] = x[i] * (1/sqrtf(mean(x^2)+eps)) * w[i]  (qwen_rms_norm,
-// qwen_asr_kernels.c:750-809), x already in xraw.
+// qwen_asr_kernels.c:750-809), x in xraw, w prefetched into smem.
 __device__ void rmsnorm_smem(const float *xraw, const float *w, int h, float eps, float *act, float *red) {
+    cp_async_wait();
+    consumer_sync();
     float ss = 0.f;
     for (int i = threadIdx.x; i < h; i += NCT) ss += xraw[i] * xraw[i];
     ss = consumer_sum(ss, red);
@@ -287,18 +347,21 @@ __device__ __forceinline__ void stage_dots(const uint16_t *wst, int nr, int K, c
 }
 
 // ---------------------------------------------------------------- attention
+template <int R>
 struct AttnSmem {
-    float q[MAX_GQA][QDB_HD];
+    float q[R][QDB_HD];
     float knew[QDB_HD];
     float vnew[QDB_HD];
-    float m[NCW][MAX_GQA];
-    float l[NCW][MAX_GQA];
-    float o[NCW][MAX_GQA][QDB_HD];
+    float qn[QDB_HD], kn[QDB_HD];   // q_norm / k_norm weights (prefetched)
+    float2 rope[QDB_HD / 2];        // this position's (cos, sin) row (prefetched)
+    float m[NCW][R];
+    float l[NCW][R];
+    float o[NCW][R][QDB_HD];
 };
 
 // Per-head RMSNorm then NeoX rotation of one 128-float head in smem, one warp
 // (qwen_rms_norm_per_head :811-873, qwen_apply_rope_neox :1182-1247).
-__device__ void head_norm_rope(float *v, const float *w, const float2 *rope_row, float eps) {
+__device__ __forceinline__ void head_norm_rope(float *v, const float *w, const float2 *rope_row, float eps) {
     const int lane = threadIdx.x & 31;
     float e[4];
 #pragma unroll
@@ -320,8 +383,9 @@ __device__ void head_norm_rope(float *v, const float *w, const float2 *rope_row,
     __syncwarp();
 }
 
-// Polls one 128-word head (4 words per lane, all in flight) with one warp.
-__device__ bool warp_load_head(const u64 *src, unsigned ep, float *dst, const Ctl &c) {
+// Polls one 128-word head (4 words per lane, all in flight) with one warp;
+// the result is the same for every lane.
+__device__ __forceinline__ bool warp_load_head(const u64 *src, unsigned ep, float *dst, const Ctl &c, int site) {
     const int lane = threadIdx.x & 31;
     u64 w[4];
     uint32_t pending = 0xfu;
@@ -336,11 +400,15 @@ __device__ bool warp_load_head(const u64 *src, unsigned ep, float *dst, const Ct
                 pending &= ~(1u << j);
             }
         if (!__any_sync(0xffffffffu, pending != 0)) break;
-        if (should_stop(c, iter)) return false;
-        if (timed_out(t0)) {
-            abort_now(c);
-            return false;
+        int stop = 0;
+        if (lane == 0) {
+            stop = should_stop(c, iter) ? 1 : 0;
+            if (!stop && timed_out(t0)) {
+                abort_now(c, site);
+                stop = 1;
+            }
         }
+        if (__shfl_sync(0xffffffffu, stop, 0)) return false;
 #pragma unroll
         for (int j = 0; j < 4; j++)
             if ((pending >> j) & 1u) w[j] = ld_tag(src + lane + 32 * j);
@@ -349,10 +417,15 @@ __device__ bool warp_load_head(const u64 *src, unsigned ep, float *dst, const Ct
     return true;
 }
 
-// Attention unit (KV head g, split s of S) for this step's position.
+// Attention unit (KV head g, split s of S) for this step's position. Reads
+// q/k/v tagged ep_in (phase A); partials and the merged output are tagged
+// ep_in + 1. Everything that does not depend on this step's q/k/v (the
+// q/k norm weights, the RoPE row and the first cached K/V rows of each warp)
+// is requested before the q/k/v poll.
 template <int R>
-__device__ __noinline__ void attn_unit(const QdbStepArgs &a, int layer, int g, int s, int S, unsigned ep, AttnSmem *sm,
-                          const Ctl &c) {
+__device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw, int layer, int g, int s, int S,
+                                       unsigned ep_in, AttnSmem<R> *sm, const Ctl &c) {
+    const unsigned ep = ep_in + 1;
     const QdbDims &d = a.d;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int ctx = a.pos + 1;
@@ -360,26 +433,56 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, int layer, int g, i
     const int p0 = s * per;
     const int p1 = min(ctx, p0 + per);
     const int qd = d.Hq * QDB_HD, kvd = d.Hkv * QDB_HD;
-    const QdbLayerW &lw = a.layers[layer];
-    const float2 *rope_row = a.rope + (size_t)a.pos * (QDB_HD / 2);
     const size_t head_base = ((size_t)layer * d.Hkv + g) * (size_t)a.cap * QDB_HD;
     uint16_t *kc = a.kc + head_base;
     uint16_t *vc = a.vc + head_base;
     const bool owns_new = (p0 <= a.pos && a.pos < p1);
+    if (!check_or_record(a.pos < a.cap && a.pos < a.rope_cap &&
+                             (size_t)(d.Hq * S) * (2 + QDB_HD) <= (size_t)a.part_len,
+                         a.err, 2, a.pos, a.cap)) {
+        *c.abort = 1;
+        return;
+    }
+    // prefetch: norm weights + rope row to smem, first K/V rows to registers
+    if (threadIdx.x < 32) cp_async16(sm->qn + threadIdx.x * 4, lw.q_norm + threadIdx.x * 4);
+    else if (threadIdx.x < 64) cp_async16(sm->kn + (threadIdx.x - 32) * 4, lw.k_norm + (threadIdx.x - 32) * 4);
+    else if (threadIdx.x < 96)
+        cp_async16(&sm->rope[(threadIdx.x - 64) * 2], a.rope + (size_t)a.pos * (QDB_HD / 2) + (threadIdx.x - 64) * 2);
+    cp_async_commit();
+    const int sub = lane & 3, kk = lane >> 2;
+    const int base0 = p0 + warp * ATT_KEYS;
+    uint4 kv4[4];
+    uint2 vv[ATT_KEYS];
+    {
+        const int j = base0 + kk;
+        if (j < p1 && j != a.pos) {
+            const uint4 *kp = reinterpret_cast<const uint4 *>(kc + (size_t)j * QDB_HD + sub * 32);
+#pragma unroll
+            for (int u = 0; u < 4; u++) kv4[u] = __ldcg(kp + u);
+        }
+#pragma unroll
+        for (int t = 0; t < ATT_KEYS; t++) {
+            const int jt = base0 + t;
+            if (jt < p1 && jt != a.pos)
+                vv[t] = __ldcg(reinterpret_cast<const uint2 *>(vc + (size_t)jt * QDB_HD + lane * 4));
+        }
+    }
+    cp_async_wait();
+    consumer_sync();
 
     // q heads of this group (and the new K/V row for the owner), one warp each
     for (int h = warp; h < R + (owns_new ? 2 : 0); h += NCW) {
         if (h < R) {
-            if (warp_load_head(a.tqkv + (size_t)(g * R + h) * QDB_HD, ep, sm->q[h], c))
-                head_norm_rope(sm->q[h], lw.q_norm, rope_row, d.eps);
+            if (warp_load_head(a.tqkv + (size_t)(g * R + h) * QDB_HD, ep_in, sm->q[h], c, 10))
+                head_norm_rope(sm->q[h], sm->qn, sm->rope, d.eps);
         } else if (h == R) {
-            if (warp_load_head(a.tqkv + qd + (size_t)g * QDB_HD, ep, sm->knew, c)) {
-                head_norm_rope(sm->knew, lw.k_norm, rope_row, d.eps);
+            if (warp_load_head(a.tqkv + qd + (size_t)g * QDB_HD, ep_in, sm->knew, c, 11)) {
+                head_norm_rope(sm->knew, sm->kn, sm->rope, d.eps);
                 for (int i = lane; i < QDB_HD; i += 32)
                     kc[(size_t)a.pos * QDB_HD + i] = f32_to_kv(sm->knew[i]);
             }
         } else {
-            if (warp_load_head(a.tqkv + qd + kvd + (size_t)g * QDB_HD, ep, sm->vnew, c))
+            if (warp_load_head(a.tqkv + qd + kvd + (size_t)g * QDB_HD, ep_in, sm->vnew, c, 12))
                 for (int i = lane; i < QDB_HD; i += 32)
                     vc[(size_t)a.pos * QDB_HD + i] = f32_to_kv(sm->vnew[i]);
         }
@@ -387,7 +490,6 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, int layer, int g, i
     consumer_sync();  // new K/V row stored (global writes by this CTA are visible to it)
 
     const float scale = 1.0f / sqrtf((float)QDB_HD);
-    const int sub = lane & 3, kk = lane >> 2;
     float m[R], l[R], o[R][4];
 #pragma unroll
     for (int h = 0; h < R; h++) {
@@ -396,22 +498,22 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, int layer, int g, i
 #pragma unroll
         for (int e = 0; e < 4; e++) o[h][e] = 0.f;
     }
-    if (!*c.abort) {
-        for (int base = p0 + warp * ATT_KEYS; base < p1; base += NCW * ATT_KEYS) {
+    if (!warp_aborted(c)) {
+        for (int base = base0; base < p1; base += NCW * ATT_KEYS) {
             const int j = base + kk;
             const bool valid = j < p1;
-            uint4 kv4[4];
-            if (valid) {
+            const bool first = (base == base0);
+            if (valid && (!first || j == a.pos)) {
                 const uint4 *kp = reinterpret_cast<const uint4 *>(kc + (size_t)j * QDB_HD + sub * 32);
 #pragma unroll
                 for (int u = 0; u < 4; u++) kv4[u] = __ldcg(kp + u);
             }
-            uint2 vv[ATT_KEYS];
 #pragma unroll
             for (int t = 0; t < ATT_KEYS; t++) {
                 const int jt = base + t;
-                vv[t] = jt < p1 ? __ldcg(reinterpret_cast<const uint2 *>(vc + (size_t)jt * QDB_HD + lane * 4))
-                                : make_uint2(0u, 0u);
+                if (jt >= p1) vv[t] = make_uint2(0u, 0u);
+                else if (!first || jt == a.pos)
+                    vv[t] = __ldcg(reinterpret_cast<const uint2 *>(vc + (size_t)jt * QDB_HD + lane * 4));
             }
             float sc[R];
 #pragma unroll
@@ -510,7 +612,7 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, int layer, int g, i
                 }
                 if (should_stop(c, iter)) return;
                 if (timed_out(t0)) {
-                    abort_now(c);
+                    abort_now(c, 13);
                     return;
                 }
             }
@@ -531,22 +633,33 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, int layer, int g, i
 }
 
 // ---------------------------------------------------------------- the kernel
+// Dynamic shared memory: ring | xraw[h] | wn[h] (norm weights) | act (union
+// with the attention scratch).
+template <int R>
+__host__ __device__ constexpr int act_region_floats(int h, int qd, int I) {
+    int n = h > qd ? h : qd;
+    n = n > I ? n : I;
+    const int att = (int)(sizeof(AttnSmem<R>) / sizeof(float));
+    return n > att ? n : att;
+}
+
 template <int R>
 __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     __shared__ __align__(8) u64 full[NSTAGE], empty[NSTAGE];
+    __shared__ __align__(16) QdbLayerW layers[MAX_LAYERS];
     __shared__ float red[NCW];
     __shared__ float outs[NCW][32];
     __shared__ u64 wbest[NCW];
     __shared__ volatile int s_abort;
-    __shared__ int s_last;
 
     const QdbDims &d = a.d;
     const int h = d.h, qd = d.Hq * QDB_HD, I = d.I;
     unsigned char *ring = smem_raw;
     float *xraw = reinterpret_cast<float *>(smem_raw + (size_t)NSTAGE * STAGE_BYTES);
-    float *act = xraw + h;
-    AttnSmem *asm_ = reinterpret_cast<AttnSmem *>(act);
+    float *wn = xraw + h;
+    float *act = wn + h;
+    AttnSmem<R> *asm_ = reinterpret_cast<AttnSmem<R> *>(act);
 
     if (threadIdx.x == 0) {
         s_abort = 0;
@@ -556,14 +669,29 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) 
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    {  // layer table -> shared memory (no dependent global load per phase)
+        const int words = d.L * (int)(sizeof(QdbLayerW) / 8);
+        const u64 *src = reinterpret_cast<const u64 *>(a.layers);
+        u64 *dst = reinterpret_cast<u64 *>(layers);
+        for (int i = threadIdx.x; i < words; i += NTHREADS) dst[i] = src[i];
+    }
     __syncthreads();
     Ctl c{&s_abort, a.err};
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp == NCW) {
-        producer(a, ring, full, empty, c);
+        producer(a, layers, ring, full, empty, c);
         return;
     }
 
+    const int tstride = qdb_step_trace_events(d.L);
+    auto mark = [&](int idx) {
+        if (a.trace && threadIdx.x == 0) {
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            a.trace[(size_t)blockIdx.x * tstride + idx] = t;
+        }
+    };
+    mark(0);
     unsigned it = 0;  // ring item counter (same sequence as the producer)
     auto run_items = [&](const Slice &s, int mode, unsigned ep, u64 &best) {
         // mode 0: QKV store, 1: O + residual, 2: gate/up SwiGLU, 3: down + residual, 4: lm_head
@@ -571,7 +699,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) 
         for (int k = 0; k < n; k++, it++) {
             if ((int)(it % NCW) != warp) continue;
             const unsigned st = it % NSTAGE;
-            if (*c.abort || !mbar_wait(&full[st], (it / NSTAGE) & 1, c, true)) continue;
+            if (warp_aborted(c) || !mbar_wait_warp(&full[st], (it / NSTAGE) & 1, c, 3)) continue;
             const int r = s.r0 + k * s.ipr;
             const int nr = min(s.ipr, s.r1 - r);
             const uint16_t *wst = reinterpret_cast<const uint16_t *>(ring + (size_t)st * STAGE_BYTES);
@@ -606,59 +734,77 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) 
     u64 best = 0ull;
     for (int layer = 0; layer < d.L; layer++) {
         const unsigned epA = a.epoch + 5u * layer;
-        const QdbLayerW &lw = a.layers[layer];
+        const QdbLayerW &lw = layers[layer];
+        const int tb = 1 + 9 * layer;
         // ---- A: residual -> xraw, input norm -> act, QKV rows
         consumer_sync();
+        mark(tb + 0);
+        prefetch_f32(wn, lw.in_norm, h);
         if (layer == 0) {
             if (a.token_in) {
-                const uint16_t *e = a.embed + (size_t)(*a.token_in) * h;
+                int tok = *a.token_in;
+                if (tok < 0 || tok >= d.V) {  // never gather outside the table
+                    set_error(a.err, QDB_ERR_BAD_ARG);
+                    tok = 0;
+                }
+                const uint16_t *e = a.embed + (size_t)tok * h;
                 for (int i = threadIdx.x; i < h; i += NCT) xraw[i] = __uint_as_float(((uint32_t)e[i]) << 16);
             } else {
                 for (int i = threadIdx.x; i < h; i += NCT) xraw[i] = a.x_in[i];
             }
         } else if (!*c.abort) {
-            load_tagged(a.tx, h, epA - 1, xraw, c);  // written by E of the previous layer
+            load_tagged(a.tx, h, epA - 1, xraw, c, 4);  // written by E of the previous layer
         }
-        consumer_sync();
-        rmsnorm_smem(xraw, lw.in_norm, h, d.eps, act, red);
-        run_items(phase_slice(a, layer, 0), 0, epA, best);
+        rmsnorm_smem(xraw, wn, h, d.eps, act, red);
+        mark(tb + 1);
+        run_items(phase_slice(a, layers, layer, 0), 0, epA, best);
 
         // ---- B: attention units
         const int S = a.splits;
         if ((int)blockIdx.x < d.Hkv * S) {
             consumer_sync();
+            mark(tb + 2);
             const int u = blockIdx.x;
-            attn_unit<R>(a, layer, u / S, u % S, S, epA + 1, asm_, c);
+            attn_unit<R>(a, lw, layer, u / S, u % S, S, epA, asm_, c);
         }
 
         // ---- C: O-proj + residual
         consumer_sync();
-        if (!*c.abort) load_tagged(a.tattn, qd, epA + 1, act, c);
+        mark(tb + 3);
+        if (!*c.abort) load_tagged(a.tattn, qd, epA + 1, act, c, 5);
         consumer_sync();
-        run_items(phase_slice(a, layer, 1), 1, epA + 2, best);
+        mark(tb + 4);
+        run_items(phase_slice(a, layers, layer, 1), 1, epA + 2, best);
 
         // ---- D: post-attention norm + gate/up + SwiGLU
         consumer_sync();
-        if (!*c.abort) load_tagged(a.tx, h, epA + 2, xraw, c);
-        consumer_sync();
-        rmsnorm_smem(xraw, lw.post_norm, h, d.eps, act, red);
-        run_items(phase_slice(a, layer, 2), 2, epA + 3, best);
+        mark(tb + 5);
+        prefetch_f32(wn, lw.post_norm, h);
+        if (!*c.abort) load_tagged(a.tx, h, epA + 2, xraw, c, 6);
+        rmsnorm_smem(xraw, wn, h, d.eps, act, red);
+        mark(tb + 6);
+        run_items(phase_slice(a, layers, layer, 2), 2, epA + 3, best);
 
         // ---- E: down + residual
         consumer_sync();
-        if (!*c.abort) load_tagged(a.tact, I, epA + 3, act, c);
+        mark(tb + 7);
+        if (!*c.abort) load_tagged(a.tact, I, epA + 3, act, c, 7);
         consumer_sync();
-        run_items(phase_slice(a, layer, 3), 3, epA + 4, best);
+        mark(tb + 8);
+        run_items(phase_slice(a, layers, layer, 3), 3, epA + 4, best);
     }
     // ---- F: final norm + lm_head + argmax
     const unsigned epF = a.epoch + 5u * d.L;
+    const int tf = 1 + 9 * d.L;
     consumer_sync();
-    if (!*c.abort) load_tagged(a.tx, h, epF - 1, xraw, c);
-    consumer_sync();
-    rmsnorm_smem(xraw, a.final_norm, h, d.eps, act, red);
+    mark(tf);
+    prefetch_f32(wn, a.final_norm, h);
+    if (!*c.abort) load_tagged(a.tx, h, epF - 1, xraw, c, 8);
+    rmsnorm_smem(xraw, wn, h, d.eps, act, red);
+    mark(tf + 1);
     if (blockIdx.x == 0 && a.hidden_out)
         for (int i = threadIdx.x; i < h; i += NCT) a.hidden_out[i] = act[i];
-    run_items(phase_slice(a, 0, 4), 4, epF, best);
+    run_items(phase_slice(a, layers, 0, 4), 4, epF, best);
     // reduce this CTA's best, publish, elect the last CTA
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -667,17 +813,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) 
     }
     if (lane == 0) wbest[warp] = best;
     consumer_sync();
+    mark(tf + 2);
     if (threadIdx.x == 0) {
         u64 b = 0ull;
         for (int w = 0; w < NCW; w++) b = wbest[w] > b ? wbest[w] : b;
         if (b) atomicMax(a.best, b);
         __threadfence();
         const unsigned prev = atomicAdd(a.done, 1u);
-        s_last = (prev == gridDim.x - 1);
-        if (s_last) {
+        if (prev == gridDim.x - 1) {
             __threadfence();
             const u64 fin = atomicMax(a.best, 0ull);
-            *a.token_out = argmax_key_index(fin);
+            if (fin == 0ull) set_error(a.err, QDB_ERR_BAD_ARG);  // no candidate (aborted step)
+            *a.token_out = fin ? argmax_key_index(fin) : 0;
             atomicExch(a.best, 0ull);
             atomicExch(a.done, 0u);
         }
@@ -702,12 +849,14 @@ __global__ void rope_table_kernel(float2 *tab, int n_pos, float theta) {
 
 extern "C" int qdb_step_smem_bytes(const QdbDims &d) {
     const int qd = d.Hq * QDB_HD;
-    int n = d.h;
-    if (qd > n) n = qd;
-    if (d.I > n) n = d.I;
-    int act = n * (int)sizeof(float);
-    if ((int)sizeof(AttnSmem) > act) act = (int)sizeof(AttnSmem);
-    return NSTAGE * STAGE_BYTES + d.h * (int)sizeof(float) + act;
+    int act = 0;
+    switch (d.Hq / d.Hkv) {
+        case 1: act = act_region_floats<1>(d.h, qd, d.I); break;
+        case 2: act = act_region_floats<2>(d.h, qd, d.I); break;
+        case 4: act = act_region_floats<4>(d.h, qd, d.I); break;
+        default: act = act_region_floats<8>(d.h, qd, d.I); break;
+    }
+    return NSTAGE * STAGE_BYTES + (2 * d.h + act) * (int)sizeof(float);
 }
 
 extern "C" int qdb_step_max_splits(int grid, int kv_heads) {
@@ -727,6 +876,7 @@ static cudaError_t launch_r(const QdbStepArgs &a, int grid, cudaStream_t st) {
 
 extern "C" cudaError_t qdb_launch_step(const QdbStepArgs &a, int grid, cudaStream_t st) {
     if (a.d.h > POLL * NCT || a.d.I > POLL * NCT || a.d.Hq * QDB_HD > POLL * NCT) return cudaErrorInvalidValue;
+    if (a.d.L > MAX_LAYERS) return cudaErrorInvalidValue;
     if (a.splits < 1 || a.splits > 64 || a.d.Hkv * a.splits > grid) return cudaErrorInvalidValue;
     switch (a.d.Hq / a.d.Hkv) {
         case 1: return launch_r<1>(a, grid, st);
