@@ -33,16 +33,22 @@
 
 namespace {
 
-constexpr int NCW = 8;                    // consumer warps
+constexpr int NCW = 8;                    // consumer warps (= ring stages)
 constexpr int NCT = NCW * 32;             // consumer threads
 constexpr int NTHREADS = NCT + 32;        // + producer warp
-constexpr int STAGE_BYTES = 16384;
-constexpr int NSTAGE = 10;
+constexpr int STAGE_BYTES = 20480;
+// One ring stage per consumer warp: item `it` goes to warp it % NCW AND stage
+// it % NSTAGE, so a stage is only ever reused by the warp that consumed its
+// previous item. (With NSTAGE != NCW a fast warp could wait on a stage two
+// mbarrier phases ahead, which a parity wait cannot tell from "complete".)
+constexpr int NSTAGE = NCW;
+constexpr int L2_AHEAD = 24;              // items prefetched into L2 ahead of the ring
 constexpr int MAX_LAYERS = 32;             // layer table kept in shared memory
 constexpr int ATT_KEYS = 8;               // keys per warp iteration
 constexpr int POLL = 24;                  // tagged words per consumer thread per vector load
 
 static_assert(NTHREADS == QDB_STEP_THREADS, "thread count mismatch");
+static_assert(NSTAGE == NCW, "a ring stage must belong to exactly one consumer warp");
 
 typedef unsigned long long u64;
 
@@ -158,6 +164,10 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
         : "memory");
 }
 
+__device__ __forceinline__ void prefetch_l2(const void *src, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Asynchronous 16-byte global -> shared copies (no registers held while the
 // thread goes on polling); completed with cp_async_wait().
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
@@ -212,39 +222,78 @@ __device__ __forceinline__ Slice phase_slice(const QdbStepArgs &a, const QdbLaye
 }
 
 // ---------------------------------------------------------------- producer
+// Walks the step's weight schedule: layers 0..L-1 phases 0..3, then the
+// lm_head (layer L, phase 4), one item (<= ipr rows) at a time.
+struct Cursor {
+    int layer, p, r;
+    Slice s;
+    bool done;
+};
+
+__device__ __forceinline__ void cursor_settle(const QdbStepArgs &a, const QdbLayerW *layers, Cursor &q) {
+    while (!q.done && q.r >= q.s.r1) {
+        if (q.layer == a.d.L) {
+            q.done = true;
+            break;
+        }
+        if (++q.p == 4) {
+            q.layer++;
+            q.p = q.layer < a.d.L ? 0 : 4;
+        }
+        q.s = phase_slice(a, layers, q.layer, q.p);
+        q.r = q.s.r0;
+    }
+}
+
+__device__ __forceinline__ void cursor_init(const QdbStepArgs &a, const QdbLayerW *layers, Cursor &q) {
+    q.layer = 0;
+    q.p = 0;
+    q.done = false;
+    q.s = phase_slice(a, layers, 0, 0);
+    q.r = q.s.r0;
+    cursor_settle(a, layers, q);
+}
+
+__device__ __forceinline__ void cursor_next(const QdbStepArgs &a, const QdbLayerW *layers, Cursor &q) {
+    q.r += q.s.ipr;
+    cursor_settle(a, layers, q);
+}
+
 __device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *layers, unsigned char *ring, u64 *full,
                                       u64 *empty, const Ctl &c) {
     const int lane = threadIdx.x & 31;
     if (lane != 0) return;
-    unsigned it = 0;
+    Cursor ld, pf;
+    cursor_init(a, layers, ld);
+    cursor_init(a, layers, pf);
+    unsigned it = 0, pf_it = 0;
     bool ok = true;
-    for (int layer = 0; layer <= a.d.L && ok; layer++) {
-        const int p_end = layer < a.d.L ? 4 : 5;
-        for (int p = layer < a.d.L ? 0 : 4; p < p_end && ok; p++) {
-            const Slice s = phase_slice(a, layers, layer, p);
-            const size_t row_bytes = (size_t)s.K * 2;
-            for (int r = s.r0; r < s.r1 && ok; r += s.ipr, it++) {
-                const int nr = min(s.ipr, s.r1 - r);
-                const unsigned st = it % NSTAGE;
-                if (it >= NSTAGE && !mbar_wait(&empty[st], ((it / NSTAGE) - 1) & 1, c, true, 1)) {
-                    ok = false;
-                    break;
-                }
-                const unsigned bytes = (unsigned)(nr * row_bytes);
-                const uint16_t *src = s.w + (size_t)r * s.K;
-                const bool in_w = (src >= a.w_lo && src + (size_t)bytes / 2 <= a.w_hi);
-                const bool in_e = (src >= a.embed && src + (size_t)bytes / 2 <= a.embed + (size_t)a.d.V * a.d.h);
-                if (!check_or_record(((uintptr_t)src & 15) == 0 && (bytes & 15) == 0 && bytes <= STAGE_BYTES &&
-                                         bytes > 0 && (in_w || in_e),
-                                     a.err, 1, (long long)r, (long long)bytes)) {
-                    *c.abort = 1;
-                    ok = false;
-                    break;
-                }
-                mbar_expect_tx(&full[st], bytes);
-                bulk_g2s(ring + (size_t)st * STAGE_BYTES, src, bytes, &full[st]);
+    for (; !ld.done && ok; cursor_next(a, layers, ld), it++) {
+        // keep the L2 prefetch cursor L2_AHEAD items ahead (no smem, no waits)
+        for (; !pf.done && pf_it < it + L2_AHEAD; cursor_next(a, layers, pf), pf_it++)
+            if (pf_it >= it) {
+                const int nr = min(pf.s.ipr, pf.s.r1 - pf.r);
+                prefetch_l2(pf.s.w + (size_t)pf.r * pf.s.K, (unsigned)(nr * pf.s.K * 2));
             }
+        const int nr = min(ld.s.ipr, ld.s.r1 - ld.r);
+        const unsigned st = it % NSTAGE;
+        if (it >= NSTAGE && !mbar_wait(&empty[st], ((it / NSTAGE) - 1) & 1, c, true, 1)) {
+            ok = false;
+            break;
         }
+        const unsigned bytes = (unsigned)(nr * ld.s.K * 2);
+        const uint16_t *src = ld.s.w + (size_t)ld.r * ld.s.K;
+        const bool in_w = (src >= a.w_lo && src + (size_t)bytes / 2 <= a.w_hi);
+        const bool in_e = (src >= a.embed && src + (size_t)bytes / 2 <= a.embed + (size_t)a.d.V * a.d.h);
+        if (!check_or_record(((uintptr_t)src & 15) == 0 && (bytes & 15) == 0 && bytes <= STAGE_BYTES && bytes > 0 &&
+                                 (in_w || in_e),
+                             a.err, 1, (long long)ld.r, (long long)bytes)) {
+            *c.abort = 1;
+            ok = false;
+            break;
+        }
+        mbar_expect_tx(&full[st], bytes);
+        bulk_g2s(ring + (size_t)st * STAGE_BYTES, src, bytes, &full[st]);
     }
     if (!ok) {
         // Drain: wait (bounded, ignoring the abort flag) for the copies in
