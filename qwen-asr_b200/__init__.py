@@ -20,7 +20,9 @@ import os
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libqwen_asr_b200.so")
+# QWEN_ASR_B200_LIB selects another build of the same library (A/B runs of
+# compile-time variants); the default is the in-tree build.
+LIB_PATH = os.environ.get("QWEN_ASR_B200_LIB") or os.path.join(_HERE, "libqwen_asr_b200.so")
 
 QWEN_TOKEN_ENDOFTEXT = 151643
 QWEN_TOKEN_IM_END = 151645

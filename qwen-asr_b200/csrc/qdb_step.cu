@@ -33,22 +33,36 @@
 
 namespace {
 
-constexpr int NCW = 8;                    // consumer warps (= ring stages)
+constexpr int NCW = 8;                    // consumer warps
 constexpr int NCT = NCW * 32;             // consumer threads
 constexpr int NTHREADS = NCT + 32;        // + producer warp
-constexpr int STAGE_BYTES = 20480;
-// One ring stage per consumer warp: item `it` goes to warp it % NCW AND stage
-// it % NSTAGE, so a stage is only ever reused by the warp that consumed its
-// previous item. (With NSTAGE != NCW a fast warp could wait on a stage two
-// mbarrier phases ahead, which a parity wait cannot tell from "complete".)
-constexpr int NSTAGE = NCW;
-constexpr int L2_AHEAD = 24;              // items prefetched into L2 ahead of the ring
+#ifndef QDB_STAGE_BYTES
+#define QDB_STAGE_BYTES 12288
+#endif
+#ifndef QDB_STAGES_PER_WARP
+#define QDB_STAGES_PER_WARP 2
+#endif
+#ifndef QDB_L2_AHEAD
+#define QDB_L2_AHEAD 0
+#endif
+#ifndef QDB_POLL_SLEEP_NS
+#define QDB_POLL_SLEEP_NS 0
+#endif
+constexpr int STAGE_BYTES = QDB_STAGE_BYTES;
+// Ring stages are owned by warps: item `it` goes to warp it % NCW and stage
+// it % NSTAGE with NSTAGE a multiple of NCW, so a stage is only ever reused
+// by the warp that consumed its previous item. (Otherwise a fast warp could
+// wait on a stage two mbarrier phases ahead, which a parity wait cannot tell
+// from "complete".)
+constexpr int NSTAGE = NCW * QDB_STAGES_PER_WARP;
+constexpr int L2_AHEAD = QDB_L2_AHEAD;    // items prefetched into L2 ahead of the ring (0 = off)
+constexpr int OWN_ROWS = 64;              // residual rows one CTA may own
 constexpr int MAX_LAYERS = 32;             // layer table kept in shared memory
 constexpr int ATT_KEYS = 8;               // keys per warp iteration
 constexpr int POLL = 24;                  // tagged words per consumer thread per vector load
 
 static_assert(NTHREADS == QDB_STEP_THREADS, "thread count mismatch");
-static_assert(NSTAGE == NCW, "a ring stage must belong to exactly one consumer warp");
+static_assert(NSTAGE % NCW == 0, "a ring stage must belong to exactly one consumer warp");
 
 typedef unsigned long long u64;
 
@@ -270,7 +284,7 @@ __device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *lay
     bool ok = true;
     for (; !ld.done && ok; cursor_next(a, layers, ld), it++) {
         // keep the L2 prefetch cursor L2_AHEAD items ahead (no smem, no waits)
-        for (; !pf.done && pf_it < it + L2_AHEAD; cursor_next(a, layers, pf), pf_it++)
+        for (; L2_AHEAD > 0 && !pf.done && pf_it < it + L2_AHEAD; cursor_next(a, layers, pf), pf_it++)
             if (pf_it >= it) {
                 const int nr = min(pf.s.ipr, pf.s.r1 - pf.r);
                 prefetch_l2(pf.s.w + (size_t)pf.r * pf.s.K, (unsigned)(nr * pf.s.K * 2));
@@ -336,6 +350,7 @@ __device__ __noinline__ bool load_tagged(const u64 *src, int n, unsigned ep, flo
             abort_now(c, site);
             return false;
         }
+        if (QDB_POLL_SLEEP_NS) __nanosleep(QDB_POLL_SLEEP_NS);
 #pragma unroll
         for (int j = 0; j < POLL; j++)
             if ((pending >> j) & 1u) w[j] = ld_tag(src + t + j * NCT);
@@ -355,16 +370,19 @@ __device__ float consumer_sum(float v, float *red) {
     return s;
 }
 
-// act[i] = x[i] * (1/sqrtf(mean(x^2)+eps)) * w[i]  (qwen_rms_norm,
-// qwen_asr_kernels.c:750-809), x in xraw, w prefetched into smem.
-__device__ void rmsnorm_smem(const float *xraw, const float *w, int h, float eps, float *act, float *red) {
+// In place: x[i] = x[i] * (1/sqrtf(mean(x^2)+eps)) * w[i]  (qwen_rms_norm,
+// qwen_asr_kernels.c:750-809); x (raw) and w (prefetched) in smem. The raw
+// values of this CTA's residual rows [own0, own0+nown) are kept in xown first.
+__device__ void rmsnorm_smem(float *x, const float *w, int h, float eps, float *red, float *xown, int own0,
+                             int nown) {
     cp_async_wait();
     consumer_sync();
+    for (int i = threadIdx.x; i < nown; i += NCT) xown[i] = x[own0 + i];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < h; i += NCT) ss += xraw[i] * xraw[i];
+    for (int i = threadIdx.x; i < h; i += NCT) ss += x[i] * x[i];
     ss = consumer_sum(ss, red);
     const float inv = 1.0f / sqrtf(ss / (float)h + eps);
-    for (int i = threadIdx.x; i < h; i += NCT) act[i] = xraw[i] * inv * w[i];
+    for (int i = threadIdx.x; i < h; i += NCT) x[i] = x[i] * inv * w[i];
     consumer_sync();
 }
 
@@ -458,6 +476,7 @@ __device__ __forceinline__ bool warp_load_head(const u64 *src, unsigned ep, floa
             }
         }
         if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+        if (QDB_POLL_SLEEP_NS) __nanosleep(QDB_POLL_SLEEP_NS);
 #pragma unroll
         for (int j = 0; j < 4; j++)
             if ((pending >> j) & 1u) w[j] = ld_tag(src + lane + 32 * j);
@@ -664,6 +683,7 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
                     abort_now(c, 13);
                     return;
                 }
+                if (QDB_POLL_SLEEP_NS) __nanosleep(QDB_POLL_SLEEP_NS);
             }
             if (mq == -INFINITY) continue;
             if (mq > M) {
@@ -682,11 +702,13 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
 }
 
 // ---------------------------------------------------------------- the kernel
-// Dynamic shared memory: ring | xraw[h] | wn[h] (norm weights) | act (union
-// with the attention scratch).
+// Dynamic shared memory: ring | act. act holds the phase's input vector
+// (x while it is normalised in place with the norm weights at act[h..2h),
+// attn, or the SwiGLU activations) and, in attention CTAs, the attention
+// scratch.
 template <int R>
 __host__ __device__ constexpr int act_region_floats(int h, int qd, int I) {
-    int n = h > qd ? h : qd;
+    int n = 2 * h > qd ? 2 * h : qd;
     n = n > I ? n : I;
     const int att = (int)(sizeof(AttnSmem<R>) / sizeof(float));
     return n > att ? n : att;
@@ -703,11 +725,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) 
     __shared__ volatile int s_abort;
 
     const QdbDims &d = a.d;
+    // residual rows owned by this CTA in phases C and E (same slice of h rows)
+    const int own0 = (int)((long long)d.h * blockIdx.x / gridDim.x);
+    const int nown = (int)((long long)d.h * (blockIdx.x + 1) / gridDim.x) - own0;
     const int h = d.h, qd = d.Hq * QDB_HD, I = d.I;
     unsigned char *ring = smem_raw;
-    float *xraw = reinterpret_cast<float *>(smem_raw + (size_t)NSTAGE * STAGE_BYTES);
-    float *wn = xraw + h;
-    float *act = wn + h;
+    float *act = reinterpret_cast<float *>(smem_raw + (size_t)NSTAGE * STAGE_BYTES);
+    float *wn = act + h;
+    __shared__ float xown[OWN_ROWS];  // raw residual of this CTA's O/down rows
     AttnSmem<R> *asm_ = reinterpret_cast<AttnSmem<R> *>(act);
 
     if (threadIdx.x == 0) {
@@ -774,7 +799,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) 
                 const int row = r + lane;
                 const float v = outs[warp][lane];
                 if (mode == 0) st_tag(a.tqkv + row, v, ep);
-                else st_tag(a.tx + row, xraw[row] + v, ep);
+                else st_tag(a.tx + row, xown[row - own0] + v, ep);
             }
             __syncwarp();
         }
@@ -785,7 +810,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) 
         const unsigned epA = a.epoch + 5u * layer;
         const QdbLayerW &lw = layers[layer];
         const int tb = 1 + 9 * layer;
-        // ---- A: residual -> xraw, input norm -> act, QKV rows
+        // ---- A: residual -> act (own rows kept), input norm in place, QKV rows
         consumer_sync();
         mark(tb + 0);
         prefetch_f32(wn, lw.in_norm, h);
@@ -797,14 +822,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) 
                     tok = 0;
                 }
                 const uint16_t *e = a.embed + (size_t)tok * h;
-                for (int i = threadIdx.x; i < h; i += NCT) xraw[i] = __uint_as_float(((uint32_t)e[i]) << 16);
+                for (int i = threadIdx.x; i < h; i += NCT) act[i] = __uint_as_float(((uint32_t)e[i]) << 16);
             } else {
-                for (int i = threadIdx.x; i < h; i += NCT) xraw[i] = a.x_in[i];
+                for (int i = threadIdx.x; i < h; i += NCT) act[i] = a.x_in[i];
             }
         } else if (!*c.abort) {
-            load_tagged(a.tx, h, epA - 1, xraw, c, 4);  // written by E of the previous layer
+            load_tagged(a.tx, h, epA - 1, act, c, 4);  // written by E of the previous layer
         }
-        rmsnorm_smem(xraw, wn, h, d.eps, act, red);
+        rmsnorm_smem(act, wn, h, d.eps, red, xown, own0, nown);
         mark(tb + 1);
         run_items(phase_slice(a, layers, layer, 0), 0, epA, best);
 
@@ -829,8 +854,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) 
         consumer_sync();
         mark(tb + 5);
         prefetch_f32(wn, lw.post_norm, h);
-        if (!*c.abort) load_tagged(a.tx, h, epA + 2, xraw, c, 6);
-        rmsnorm_smem(xraw, wn, h, d.eps, act, red);
+        if (!*c.abort) load_tagged(a.tx, h, epA + 2, act, c, 6);
+        rmsnorm_smem(act, wn, h, d.eps, red, xown, own0, nown);
         mark(tb + 6);
         run_items(phase_slice(a, layers, layer, 2), 2, epA + 3, best);
 
@@ -848,8 +873,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) 
     consumer_sync();
     mark(tf);
     prefetch_f32(wn, a.final_norm, h);
-    if (!*c.abort) load_tagged(a.tx, h, epF - 1, xraw, c, 8);
-    rmsnorm_smem(xraw, wn, h, d.eps, act, red);
+    if (!*c.abort) load_tagged(a.tx, h, epF - 1, act, c, 8);
+    rmsnorm_smem(act, wn, h, d.eps, red, xown, own0, nown);
     mark(tf + 1);
     if (blockIdx.x == 0 && a.hidden_out)
         for (int i = threadIdx.x; i < h; i += NCT) a.hidden_out[i] = act[i];
@@ -905,7 +930,7 @@ extern "C" int qdb_step_smem_bytes(const QdbDims &d) {
         case 4: act = act_region_floats<4>(d.h, qd, d.I); break;
         default: act = act_region_floats<8>(d.h, qd, d.I); break;
     }
-    return NSTAGE * STAGE_BYTES + (2 * d.h + act) * (int)sizeof(float);
+    return NSTAGE * STAGE_BYTES + act * (int)sizeof(float);
 }
 
 extern "C" int qdb_step_max_splits(int grid, int kv_heads) {
@@ -926,6 +951,7 @@ static cudaError_t launch_r(const QdbStepArgs &a, int grid, cudaStream_t st) {
 extern "C" cudaError_t qdb_launch_step(const QdbStepArgs &a, int grid, cudaStream_t st) {
     if (a.d.h > POLL * NCT || a.d.I > POLL * NCT || a.d.Hq * QDB_HD > POLL * NCT) return cudaErrorInvalidValue;
     if (a.d.L > MAX_LAYERS) return cudaErrorInvalidValue;
+    if ((a.d.h + grid - 1) / grid > OWN_ROWS) return cudaErrorInvalidValue;
     if (a.splits < 1 || a.splits > 64 || a.d.Hkv * a.splits > grid) return cudaErrorInvalidValue;
     switch (a.d.Hq / a.d.Hkv) {
         case 1: return launch_r<1>(a, grid, st);
