@@ -276,7 +276,7 @@ def run_ours(args):
         "higher_is_better": True,
         "scaling": scaling,
         "vs_baseline": None,
-        "dtype": "bf16 weights x f32 activations (f32 accumulate), bf16 KV",
+        "dtype": "bf16 weights x f32 activations (f32 accumulate), fp16 KV cache",
         "data": "synthetic: seeded random-init weights of the real shape, seeded prompt embeddings",
         "config": {"workload": f"{args.config}: {preset} decoder, {n_utt} utterance(s) of {seconds:g} s "
                                f"-> prefill {P} positions + {n_dec} greedy tokens (EOS masked)",

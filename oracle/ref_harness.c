@@ -177,10 +177,15 @@ double refh_decode_loop(void *hp, int first_token, int n_steps, int mask_eos, in
     return ms;
 }
 
+/* Defined only by the drop-in decoder (qwen-asr_b200/dropin); absent when the
+ * reference's own qwen_asr_decoder.c is linked. */
+void qwen_decoder_release(qwen_ctx_t *ctx) __attribute__((weak));
+
 void refh_free(void *hp) {
     refh_t *h = (refh_t *)hp;
     if (!h) return;
     qwen_ctx_t *ctx = h->ctx;
+    if (qwen_decoder_release) qwen_decoder_release(ctx);
     for (int i = 0; i < ctx->config.dec_layers; i++) {
         qwen_dec_layer_t *l = &ctx->decoder.layers[i];
         free(l->q_norm_weight); free(l->k_norm_weight);

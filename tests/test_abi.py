@@ -67,3 +67,20 @@ def test_library_is_sm100a_only():
     out = subprocess.run([tool, "--list-elf", LIB], capture_output=True, text=True).stdout
     archs = set(re.findall(r"sm_\d+a?", out))
     assert archs == {"sm_100a"}, archs
+
+
+def test_dropin_adapter_exports_reference_symbols(pkg, synth):
+    """The drop-in decoder exports the reference's three decoder symbols and,
+    with no GPU, fails loudly inside the reference's qwen_decoder_load."""
+    from oracle.pyoracle import RefDecoder
+    p = os.path.join(REPO, "oracle", "_ref", "dropin", "libqwen_dropin.so")
+    if not os.path.exists(p):
+        pytest.skip("drop-in harness not built (needs the reference tree)")
+    lib = ctypes.CDLL(p)
+    for sym in ("qwen_decoder_load", "qwen_decoder_prefill", "qwen_decoder_forward", "qwen_decoder_release"):
+        assert hasattr(lib, sym)
+    if has_gpu():
+        return
+    ws = synth.WeightSet(synth.PRESETS["tiny"], seed=0)
+    with pytest.raises(RuntimeError, match="qwen_decoder_load failed"):
+        RefDecoder(ws, so_path=p)

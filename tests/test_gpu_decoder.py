@@ -212,3 +212,41 @@ def test_full_size_against_reference_golden(pkg, synth, name):
             assert tok == want, (step, tok, want)
         e = synth.embed_rows(ws, [int(want)])[0]
     model.close()
+
+
+def _dropin_so():
+    import os
+    from conftest import REPO
+    p = os.path.join(REPO, "oracle", "_ref", "dropin", "libqwen_dropin.so")
+    return p if os.path.exists(p) else None
+
+
+@pytest.mark.skipif(_dropin_so() is None, reason="drop-in harness not built (needs the reference tree)")
+@pytest.mark.parametrize("name", SMALL)
+def test_dropin_reference_api_matches_golden(synth, name, monkeypatch):
+    """The CUDA library behind the reference's own qwen_decoder_load /
+    qwen_decoder_prefill / qwen_decoder_forward (qwen-asr_b200/dropin), loaded
+    by the reference's safetensors loader, against the reference's golden
+    tokens and logits (logits from ctx->dec_x, as for the reference)."""
+    from oracle.pyoracle import RefDecoder
+    monkeypatch.setenv("QWEN_B200_MASK_EOS", "1")
+    g = golden(name)
+    cfg, ws, emb = _setup(synth, g)
+    d = RefDecoder(ws, so_path=_dropin_so())
+    d.kv_cache_len = 0
+    d.prefill(emb[:-1])
+    assert d.kv_cache_len == int(g["prefill_len"])
+    e = emb[-1]
+    for step, want in enumerate(g["tokens"]):
+        tok, _, lg = d.forward(e, mask_eos=True)
+        assert_logits_close(lg, g["logits"][step], f"dropin {name} step {step}")
+        if g["margins"][step] > MARGIN:
+            assert tok == want, (step, tok, want)
+        e = synth.embed_rows(ws, [int(want)])[0]
+    d.kv_cache_len = int(g["rewind_pos"])  # the streaming caller's rewind
+    e = synth.embed_rows(ws, [int(g["tokens"][1])])[0]
+    for step, want in enumerate(g["rewind_tokens"]):
+        tok, _, lg = d.forward(e, mask_eos=True)
+        assert_logits_close(lg, g["rewind_logits"][step], f"dropin {name} rewind {step}")
+        e = synth.embed_rows(ws, [int(want)])[0]
+    d.close()
