@@ -143,6 +143,28 @@ int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, const int *firs
  * (qwen_asr.c:606-607, :714-715) at the granularity of one step. */
 int qdb_trace_step(qdb_session *s, int token, int pos, unsigned long long *trace_out, int max_words);
 
+/* One decode step that allocates nothing. No counterpart in the reference.
+ *
+ * For callers that must not allocate GPU memory while decoding: code running
+ * under a memory budget enforced by a pool or arena they do not own, real-time
+ * loops where a cudaMalloc could stall on a device-wide synchronisation, or
+ * hosts that forbid allocation after start-up. It runs the same persistent
+ * step as qdb_forward, but the step's scratch (its inter-CTA vectors and the
+ * argmax / error words) lives in one fixed array inside the library instead
+ * of the model's own buffers: 512 KiB per GPU, held from library load to
+ * process exit, enough for both reference decoder shapes; larger models are
+ * refused with an error.
+ *
+ * embed_dev: DEVICE f32 [hidden] embedding of position pos; token_dev: DEVICE
+ * int receiving the greedy token. The session must already hold pos (use
+ * qdb_session_reserve beforehand): nothing is grown here. The call is
+ * synchronous on the model's stream. The first call on a device looks up the
+ * array's device address and clears it, so make that first call before any
+ * stream capture. Every call on a device shares the one array and leaves its
+ * contents behind; calls that overlap on the GPU (e.g. from two models on the
+ * same device driven concurrently) race and must not be issued. */
+int qdb_forward_noalloc(qdb_session *s, const float *embed_dev, int pos, int *token_dev);
+
 /* Waits for all queued work of the model's stream. */
 int qdb_model_sync(qdb_model *m);
 

@@ -60,6 +60,7 @@ ABI = {
     "qdb_decode_greedy_batch": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _i32p, _i32p,
                                                ctypes.c_int, _i32p]),
     "qdb_model_sync": (ctypes.c_int, [ctypes.c_void_p]),
+    "qdb_forward_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "qdb_model_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
     "qdb_trace_step": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                       ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]),

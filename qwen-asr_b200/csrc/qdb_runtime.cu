@@ -719,3 +719,77 @@ extern "C" int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, cons
     CK(cudaStreamSynchronize(m->st));
     return 0;
 }
+
+// ------------------------------------------------------------------ decode step without allocation
+// Scratch of qdb_forward_noalloc: the persistent step's tagged inter-CTA
+// vectors, followed by its argmax key, completion counter and error words.
+// Sized for the largest decoder this library runs (the 1.7B shape needs about
+// 52k words), 512 KiB in all; every GPU that loads the library holds it.
+#define QDB_NOALLOC_TAG_WORDS 65536
+static __device__ __align__(256) unsigned long long g_noalloc_scratch[QDB_NOALLOC_TAG_WORDS + 4];
+
+static unsigned long long *g_noalloc_ptr[64];  // device address of the array, per device
+static unsigned g_noalloc_epoch[64];           // next epoch for the array, per device
+
+extern "C" int qdb_forward_noalloc(qdb_session *s, const float *embed_dev, int pos, int *token_dev) {
+    g_err.clear();
+    if (!s || !embed_dev || !token_dev) return fail("null argument");
+    if (!s->m) return fail("session's model has been freed");
+    qdb_model *m = s->m;
+    if (m->device < 0 || m->device >= 64) return fail("device index %d out of range", m->device);
+    if (pos < 0) return fail("negative position");
+    // Nothing may grow here (growing allocates): the session and the RoPE
+    // table must already cover pos.
+    if (pos >= s->cap) return fail("position %d needs KV capacity %d (have %d); reserve it first", pos, pos + 1, s->cap);
+    if (pos >= m->rope_cap) return fail("position %d beyond the RoPE table (%d)", pos, m->rope_cap);
+    const size_t need = m->tags_len;
+    if (need > QDB_NOALLOC_TAG_WORDS)
+        return fail("model needs %zu scratch words, the no-allocation scratch holds %d", need, QDB_NOALLOC_TAG_WORDS);
+    if (set_dev(m)) return -1;
+    unsigned long long *base = g_noalloc_ptr[m->device];
+    if (!base) {  // set-up, once per device, with that device current
+        CK(cudaGetSymbolAddress((void **)&base, g_noalloc_scratch));
+        g_noalloc_ptr[m->device] = base;
+        g_noalloc_epoch[m->device] = 1;
+        CK(cudaMemsetAsync(base, 0, sizeof(unsigned long long) * (QDB_NOALLOC_TAG_WORDS + 4), m->st));
+    }
+    const unsigned span = qdb_step_epochs(m->cfg.layers);
+    unsigned &epoch = g_noalloc_epoch[m->device];
+    if (epoch > 0xffffffffu - 2 * span) {
+        CK(cudaMemsetAsync(base, 0, sizeof(unsigned long long) * QDB_NOALLOC_TAG_WORDS, m->st));
+        epoch = 1;
+    }
+    unsigned long long *tail = base + QDB_NOALLOC_TAG_WORDS;  // best | done, err[4]
+    // the argmax key, the completion counter and the error words start at zero
+    CK(cudaMemsetAsync(tail, 0, 4 * sizeof(unsigned long long), m->st));
+
+    QdbStepArgs a = step_args(s, pos);
+    const size_t n_x = m->cfg.hidden, n_qkv = m->qd + 2 * m->kvd, n_attn = m->qd, n_act = m->cfg.intermediate;
+    a.tx = base;
+    a.tqkv = a.tx + n_x;
+    a.tattn = a.tqkv + n_qkv;
+    a.tact = a.tattn + n_attn;
+    a.tpart = a.tact + n_act;
+    a.best = tail;
+    a.done = reinterpret_cast<unsigned *>(tail + 1);
+    a.err = reinterpret_cast<int *>(tail + 2);
+    a.x_in = embed_dev;
+    a.token_in = nullptr;
+    a.token_out = token_dev;
+    a.hidden_out = nullptr;
+    a.logits_out = nullptr;
+    a.epoch = epoch;
+    CK(qdb_launch_step(a, m->grid, m->st));
+    epoch += span;
+    int ev[4] = {0, 0, 0, 0};
+    CK(cudaMemcpyAsync(ev, a.err, sizeof(ev), cudaMemcpyDeviceToHost, m->st));
+    CK(cudaStreamSynchronize(m->st));
+    if (ev[0]) {
+        // a bounded wait ran out: forget the array's contents (epochs restart)
+        CK(cudaMemsetAsync(base, 0, sizeof(unsigned long long) * (QDB_NOALLOC_TAG_WORDS + 4), m->st));
+        CK(cudaStreamSynchronize(m->st));
+        epoch = 1;
+        return fail("device error code %d in the no-allocation step (check %d: %d %d)", ev[0], ev[1], ev[2], ev[3]);
+    }
+    return 0;
+}
