@@ -260,7 +260,7 @@ def run_ours(args):
     launch_s = (dec_ms / 1e3) / (args.steps * n_dec)
     achieved = bytes_per_step / launch_s / 1e9
     peak, peak_kind = measured_peaks()
-    kernel = "qdb_step" if n_local == 1 else "qdb_rows_decode"
+    kernel = "step_kernel" if n_local == 1 else "rows_decode"
     traffic = step_traffic_from_profile(kernel, args.config)
     launches_per_step = (L * 8) * n_local + (n_dec if n_local == 1 else n_dec * (L * 9 + 4))
     h2d = sum(e.numel() * 4 for e in pinned) - n_local * h * 4 + n_dec * n_local * h * 4
@@ -409,6 +409,22 @@ def run_reference(args):
     print(json.dumps(res), flush=True)
 
 
+def profile_step(args):
+    """Small fixed case for ncu captures of the decode step: the config's
+    model, a prefill of the config's prompt, then 3 device greedy steps."""
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    synth = ge.load_synth()
+    preset, seconds, n_dec, n_utt = CONFIGS[args.config]
+    ws = synth.WeightSet(synth.PRESETS[preset], seed=0)
+    emb = synth.utterance(ws, seconds, 1)
+    P = emb.shape[0] - 1
+    model = pkg.Model(ws, device=0, mask_eos=True)
+    s = model.session(P + 8)
+    s.prefill(emb[:-1], 0)
+    print(list(s.decode_greedy(synth.PROMPT_SUFFIX[-1], P, 3)))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -417,10 +433,13 @@ def main():
     ap.add_argument("--config", default="c1", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-step", action="store_true", help="small fixed case for ncu (no timing)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.profile_step:
+        profile_step(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

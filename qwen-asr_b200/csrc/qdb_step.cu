@@ -45,6 +45,9 @@ constexpr int NTHREADS = NCT + 32;        // + producer warp
 #ifndef QDB_L2_AHEAD
 #define QDB_L2_AHEAD 0
 #endif
+#ifndef QDB_PRODUCER_LSU
+#define QDB_PRODUCER_LSU 0  // 1: the producer warp fills stages with per-lane 16-byte cp.async
+#endif
 #ifndef QDB_POLL_SLEEP_NS
 #define QDB_POLL_SLEEP_NS 0
 #endif
@@ -273,10 +276,21 @@ __device__ __forceinline__ void cursor_next(const QdbStepArgs &a, const QdbLayer
     cursor_settle(a, layers, q);
 }
 
+#if QDB_PRODUCER_LSU
+__device__ __forceinline__ void cp_async16_cg(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_mbar_arrive(u64 *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+#endif
+
 __device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *layers, unsigned char *ring, u64 *full,
                                       u64 *empty, const Ctl &c) {
     const int lane = threadIdx.x & 31;
+#if !QDB_PRODUCER_LSU
     if (lane != 0) return;
+#endif
     Cursor ld, pf;
     cursor_init(a, layers, ld);
     cursor_init(a, layers, pf);
@@ -285,16 +299,25 @@ __device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *lay
     for (; !ld.done && ok; cursor_next(a, layers, ld), it++) {
         // keep the L2 prefetch cursor L2_AHEAD items ahead (no smem, no waits)
         for (; L2_AHEAD > 0 && !pf.done && pf_it < it + L2_AHEAD; cursor_next(a, layers, pf), pf_it++)
-            if (pf_it >= it) {
+            if (pf_it >= it && lane == 0) {
                 const int nr = min(pf.s.ipr, pf.s.r1 - pf.r);
                 prefetch_l2(pf.s.w + (size_t)pf.r * pf.s.K, (unsigned)(nr * pf.s.K * 2));
             }
         const int nr = min(ld.s.ipr, ld.s.r1 - ld.r);
         const unsigned st = it % NSTAGE;
+#if QDB_PRODUCER_LSU
+        int wok = 1;
+        if (lane == 0 && it >= NSTAGE) wok = mbar_wait(&empty[st], ((it / NSTAGE) - 1) & 1, c, true, 1) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, wok, 0)) {
+            ok = false;
+            break;
+        }
+#else
         if (it >= NSTAGE && !mbar_wait(&empty[st], ((it / NSTAGE) - 1) & 1, c, true, 1)) {
             ok = false;
             break;
         }
+#endif
         const unsigned bytes = (unsigned)(nr * ld.s.K * 2);
         const uint16_t *src = ld.s.w + (size_t)ld.r * ld.s.K;
         const bool in_w = (src >= a.w_lo && src + (size_t)bytes / 2 <= a.w_hi);
@@ -306,10 +329,19 @@ __device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *lay
             ok = false;
             break;
         }
+#if QDB_PRODUCER_LSU
+        {
+            unsigned char *dst = ring + (size_t)st * STAGE_BYTES;
+            const unsigned char *sb = reinterpret_cast<const unsigned char *>(src);
+            for (unsigned off = lane * 16; off < bytes; off += 32 * 16) cp_async16_cg(dst + off, sb + off);
+            cp_async_mbar_arrive(&full[st]);
+        }
+#else
         mbar_expect_tx(&full[st], bytes);
         bulk_g2s(ring + (size_t)st * STAGE_BYTES, src, bytes, &full[st]);
+#endif
     }
-    if (!ok) {
+    if (!ok && lane == 0) {
         // Drain: wait (bounded, ignoring the abort flag) for the copies in
         // flight, i.e. the latest item issued into each stage.
         for (unsigned k = 0; k < NSTAGE && k < it; k++) {
@@ -317,6 +349,9 @@ __device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *lay
             mbar_wait(&full[i % NSTAGE], (i / NSTAGE) & 1, c, false, 2);
         }
     }
+#if QDB_PRODUCER_LSU
+    asm volatile("cp.async.wait_all;" ::: "memory");
+#endif
 }
 
 // ---------------------------------------------------------------- consumer helpers
@@ -395,7 +430,9 @@ __device__ __forceinline__ void stage_dots(const uint16_t *wst, int nr, int K, c
         const bool two = r + 1 < nr;
         const uint4 *p0 = reinterpret_cast<const uint4 *>(wst + (size_t)r * K);
         const uint4 *p1 = reinterpret_cast<const uint4 *>(wst + (size_t)(r + (two ? 1 : 0)) * K);
-        float a0 = 0.f, a1 = 0.f;
+        // four independent accumulator chains per row (the FMA latency of a
+        // single chain is what this latency-bound loop would otherwise wait on)
+        float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
         for (int j = 0; j < nv; j++) {
             const int e = (j * 32 + lane);
@@ -403,13 +440,24 @@ __device__ __forceinline__ void stage_dots(const uint16_t *wst, int nr, int K, c
             const uint4 w1 = p1[e];
             const float4 xa = *reinterpret_cast<const float4 *>(act + e * 8);
             const float4 xb = *reinterpret_cast<const float4 *>(act + e * 8 + 4);
-            a0 = dot8(w0, xa, xb, a0);
-            a1 = dot8(w1, xa, xb, a1);
+            a[0] = fmaf(bf16lo(w0.x), xa.x, a[0]); a[1] = fmaf(bf16hi(w0.x), xa.y, a[1]);
+            a[2] = fmaf(bf16lo(w0.y), xa.z, a[2]); a[3] = fmaf(bf16hi(w0.y), xa.w, a[3]);
+            a[0] = fmaf(bf16lo(w0.z), xb.x, a[0]); a[1] = fmaf(bf16hi(w0.z), xb.y, a[1]);
+            a[2] = fmaf(bf16lo(w0.w), xb.z, a[2]); a[3] = fmaf(bf16hi(w0.w), xb.w, a[3]);
+            b[0] = fmaf(bf16lo(w1.x), xa.x, b[0]); b[1] = fmaf(bf16hi(w1.x), xa.y, b[1]);
+            b[2] = fmaf(bf16lo(w1.y), xa.z, b[2]); b[3] = fmaf(bf16hi(w1.y), xa.w, b[3]);
+            b[0] = fmaf(bf16lo(w1.z), xb.x, b[0]); b[1] = fmaf(bf16hi(w1.z), xb.y, b[1]);
+            b[2] = fmaf(bf16lo(w1.w), xb.z, b[2]); b[3] = fmaf(bf16hi(w1.w), xb.w, b[3]);
         }
-        a0 = warp_sum(a0);
-        a1 = warp_sum(a1);
-        out[r] = a0;
-        if (two) out[r + 1] = a1;
+        float s0 = (a[0] + a[1]) + (a[2] + a[3]);
+        float s1 = (b[0] + b[1]) + (b[2] + b[3]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        }
+        out[r] = s0;
+        if (two) out[r + 1] = s1;
     }
 }
 
@@ -738,7 +786,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) 
     if (threadIdx.x == 0) {
         s_abort = 0;
         for (int i = 0; i < NSTAGE; i++) {
-            mbar_init(&full[i], 1);
+            mbar_init(&full[i], QDB_PRODUCER_LSU ? 32 : 1);
             mbar_init(&empty[i], 1);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
