@@ -82,11 +82,9 @@ struct QdbRowKV {
     int cap, pos;
 };
 
-cudaError_t qdb_launch_rmsnorm_rows(const float *x, const float *w, float *out, int n, int h,
+// RMSNorm rows written as the bf16 hi/lo split consumed by the tensor-core GEMM.
+cudaError_t qdb_launch_rmsnorm_rows(const float *x, const float *w, uint16_t *hi, uint16_t *lo, int n, int h,
                                     float eps, cudaStream_t st);
-// Y = X W^T with epilogue: 0 store [n,N], 1 add into Y [n,N], 2 SwiGLU pairs -> Y [n,N/2]
-cudaError_t qdb_launch_gemm_rows(const float *X, const uint16_t *W, float *Y, int n, int N, int K,
-                                 int mode, cudaStream_t st);
 // Per-row targets: row b writes position rows[b].pos + row_pos_offset.
 cudaError_t qdb_launch_qk_rope_append(const float *qkv, float *q_out, const QdbRowKV *rows,
                                       int row_pos_offset, int layer, int n, int Hq, int Hkv,
@@ -105,6 +103,10 @@ cudaError_t qdb_launch_attn_prefill(const float *q, const uint16_t *kc, const ui
 cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
                                  int n, int Hq, int Hkv, int splits, float *part, float *out,
                                  cudaStream_t st);
+// Tensor-core GEMM (qdb_tcgemm.cu): Y (op)= X W^T with X given as bf16 hi/lo.
+cudaError_t qdb_launch_split_bf16(const float *x, uint16_t *hi, uint16_t *lo, size_t count, cudaStream_t st);
+cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,
+                               int mode, int *err, cudaStream_t st);
 cudaError_t qdb_launch_argmax_rows(const float *logits, int n, int V, int mask_eos, int *tokens,
                                    cudaStream_t st);
 cudaError_t qdb_launch_embed_rows(const uint16_t *embed, const int *tokens, float *x, int n, int h, int V,

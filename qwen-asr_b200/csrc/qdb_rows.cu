@@ -1,17 +1,19 @@
-// qdb_rows.cu - row-batched decoder kernels: prefill of one utterance
-// (qwen_decoder_prefill, qwen_asr_decoder.c:262-359) and one decode step of
-// many independent utterances. Every row is one position; the weight matrix
-// is streamed once per launch for all rows.
+// qdb_rows.cu - row-batched decoder kernels around the tensor-core GEMM
+// (qdb_tcgemm.cu): prefill of one utterance (qwen_decoder_prefill,
+// qwen_asr_decoder.c:262-359) and one decode step of many independent
+// utterances. Every row is one position.
 #include "qdb_common.cuh"
 #include "qdb_kernels.h"
 
 namespace {
 
 // ---------------------------------------------------------------- RMSNorm
-__global__ void rmsnorm_rows_kernel(const float *x, const float *w, float *out, int h, float eps) {
+// Per row: y = x * (1/sqrtf(mean(x^2)+eps)) * w (qwen_rms_norm,
+// qwen_asr_kernels.c:750-809), written as the bf16 hi/lo split the
+// tensor-core GEMM consumes (hi + lo ~= y to ~16 mantissa bits).
+__global__ void rmsnorm_rows_kernel(const float *x, const float *w, uint16_t *hi, uint16_t *lo, int h, float eps) {
     __shared__ float red[32];
     const float *xr = x + (size_t)blockIdx.x * h;
-    float *orow = out + (size_t)blockIdx.x * h;
     float ss = 0.f;
     for (int i = threadIdx.x; i < h; i += blockDim.x) ss += xr[i] * xr[i];
     ss = warp_sum(ss);
@@ -24,94 +26,12 @@ __global__ void rmsnorm_rows_kernel(const float *x, const float *w, float *out, 
     }
     __syncthreads();
     const float inv = 1.0f / sqrtf(red[0] / (float)h + eps);
-    for (int i = threadIdx.x; i < h; i += blockDim.x) orow[i] = xr[i] * inv * w[i];
-}
-
-// ---------------------------------------------------------------- GEMM
-// Y[n, N] (op)= X[n, K] (f32) * W[N, K]^T (bf16), f32 accumulation in
-// ascending k per output. Tile 64 rows x 128 weight rows x 32 k.
-constexpr int GB_M = 64, GB_N = 128, GB_K = 32;
-
-__global__ void __launch_bounds__(256) gemm_rows_kernel(const float *__restrict__ X,
-                                                        const uint16_t *__restrict__ W,
-                                                        float *__restrict__ Y, int n, int N, int K,
-                                                        int mode) {
-    __shared__ __align__(16) float As[GB_K][GB_M + 4];
-    __shared__ __align__(16) float Bs[GB_K][GB_N + 4];
-    const int tid = threadIdx.x;
-    const int tx = tid & 15, ty = tid >> 4;
-    const int m0 = blockIdx.y * GB_M, n0 = blockIdx.x * GB_N;
-    float acc[4][8];
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-#pragma unroll
-        for (int j = 0; j < 8; j++) acc[i][j] = 0.f;
-
-    for (int k0 = 0; k0 < K; k0 += GB_K) {
-        // X tile: 64 x 32 floats, 2 float4 per thread
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int idx = tid + u * 256;  // 0..511 float4 slots
-            const int r = idx >> 3, c4 = (idx & 7) * 4;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (m0 + r < n) v = *reinterpret_cast<const float4 *>(X + (size_t)(m0 + r) * K + k0 + c4);
-            As[c4 + 0][r] = v.x;
-            As[c4 + 1][r] = v.y;
-            As[c4 + 2][r] = v.z;
-            As[c4 + 3][r] = v.w;
-        }
-        // W tile: 128 x 32 bf16, 2 uint4 per thread
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int idx = tid + u * 256;  // 0..511 uint4 slots
-            const int r = idx >> 2, c8 = (idx & 3) * 8;
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (n0 + r < N) v = ldg_stream(W + (size_t)(n0 + r) * K + k0 + c8);
-            Bs[c8 + 0][r] = bf16lo(v.x);
-            Bs[c8 + 1][r] = bf16hi(v.x);
-            Bs[c8 + 2][r] = bf16lo(v.y);
-            Bs[c8 + 3][r] = bf16hi(v.y);
-            Bs[c8 + 4][r] = bf16lo(v.z);
-            Bs[c8 + 5][r] = bf16hi(v.z);
-            Bs[c8 + 6][r] = bf16lo(v.w);
-            Bs[c8 + 7][r] = bf16hi(v.w);
-        }
-        __syncthreads();
-#pragma unroll 8
-        for (int k = 0; k < GB_K; k++) {
-            const float4 a = *reinterpret_cast<const float4 *>(&As[k][ty * 4]);
-            const float4 b0 = *reinterpret_cast<const float4 *>(&Bs[k][tx * 8]);
-            const float4 b1 = *reinterpret_cast<const float4 *>(&Bs[k][tx * 8 + 4]);
-            const float av[4] = {a.x, a.y, a.z, a.w};
-            const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-            for (int i = 0; i < 4; i++)
-#pragma unroll
-                for (int j = 0; j < 8; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const int r = m0 + ty * 4 + i;
-        if (r >= n) continue;
-        if (mode == 2) {
-            const int NO = N / 2;
-#pragma unroll
-            for (int p = 0; p < 4; p++) {
-                const int c = n0 + tx * 8 + 2 * p;
-                if (c + 1 < N) Y[(size_t)r * NO + c / 2] = silu_mul(acc[i][2 * p], acc[i][2 * p + 1]);
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const int c = n0 + tx * 8 + j;
-                if (c < N) {
-                    float *dst = Y + (size_t)r * N + c;
-                    *dst = mode == 1 ? *dst + acc[i][j] : acc[i][j];
-                }
-            }
-        }
+    uint16_t *hr = hi + (size_t)blockIdx.x * h, *lr = lo + (size_t)blockIdx.x * h;
+    for (int i = threadIdx.x; i < h; i += blockDim.x) {
+        const float y = xr[i] * inv * w[i];
+        const uint16_t b = f32_to_bf16_rn(y);
+        hr[i] = b;
+        lr[i] = f32_to_bf16_rn(y - __uint_as_float((uint32_t)b << 16));
     }
 }
 
@@ -398,19 +318,10 @@ __global__ void embed_rows_kernel(const uint16_t *embed, const int *tokens, floa
 
 }  // namespace
 
-extern "C" cudaError_t qdb_launch_rmsnorm_rows(const float *x, const float *w, float *out, int n, int h, float eps,
-                                               cudaStream_t st) {
+extern "C" cudaError_t qdb_launch_rmsnorm_rows(const float *x, const float *w, uint16_t *hi, uint16_t *lo, int n, int h,
+                                               float eps, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
-    rmsnorm_rows_kernel<<<n, 256, 0, st>>>(x, w, out, h, eps);
-    return cudaGetLastError();
-}
-
-extern "C" cudaError_t qdb_launch_gemm_rows(const float *X, const uint16_t *W, float *Y, int n, int N, int K, int mode,
-                                            cudaStream_t st) {
-    if (n <= 0) return cudaSuccess;
-    if (K % GB_K) return cudaErrorInvalidValue;
-    dim3 grid((N + GB_N - 1) / GB_N, (n + GB_M - 1) / GB_M);
-    gemm_rows_kernel<<<grid, 256, 0, st>>>(X, W, Y, n, N, K, mode);
+    rmsnorm_rows_kernel<<<n, 256, 0, st>>>(x, w, hi, lo, h, eps);
     return cudaGetLastError();
 }
 

@@ -50,7 +50,9 @@ static int dev_alloc(T **p, size_t count) {
 
 struct RowScratch {
     int cap = 0;
-    float *X = nullptr, *XN = nullptr, *QKV = nullptr, *Q = nullptr, *ATT = nullptr, *ACT = nullptr;
+    float *X = nullptr, *QKV = nullptr, *Q = nullptr, *ATT = nullptr, *ACT = nullptr;
+    uint16_t *XH = nullptr, *XL = nullptr;  // bf16 hi/lo of the current GEMM input [cap, max(h, qd, I)]
+    int *err = nullptr;                     // [4] device error words of the tensor-core GEMMs
     float *LOG = nullptr;  // [cap, V] only for batched decode
     int log_cap = 0;
     float *part = nullptr;
@@ -243,8 +245,8 @@ extern "C" void qdb_model_free(qdb_model *m) {
     cudaFree(m->hidden_dev); cudaFree(m->logits_dev); cudaFree(m->done); cudaFree(m->best);
     cudaFree(m->err); cudaFree(m->tok_dev);
     RowScratch &r = m->rs;
-    cudaFree(r.X); cudaFree(r.XN); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT); cudaFree(r.LOG);
-    cudaFree(r.part); cudaFree(r.rowkv); cudaFree(r.tok);
+    cudaFree(r.X); cudaFree(r.XH); cudaFree(r.XL); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT);
+    cudaFree(r.LOG); cudaFree(r.part); cudaFree(r.rowkv); cudaFree(r.tok); cudaFree(r.err);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->h_tok) cudaFreeHost(m->h_tok);
     if (m->st) cudaStreamDestroy(m->st);
@@ -552,11 +554,14 @@ static int ensure_rows(qdb_model *m, int n, bool logits) {
     if (n > r.cap) {
         int cap = r.cap ? r.cap : 64;
         while (cap < n) cap *= 2;
-        cudaFree(r.X); cudaFree(r.XN); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT);
-        r.X = r.XN = r.QKV = r.Q = r.ATT = r.ACT = nullptr;
+        cudaFree(r.X); cudaFree(r.XH); cudaFree(r.XL); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT);
+        r.X = r.QKV = r.Q = r.ATT = r.ACT = nullptr;
+        r.XH = r.XL = nullptr;
         r.cap = 0;
-        if (dev_alloc(&r.X, cap * h) || dev_alloc(&r.XN, cap * h) || dev_alloc(&r.QKV, cap * (size_t)(m->qd + 2 * m->kvd)) ||
-            dev_alloc(&r.Q, cap * (size_t)m->qd) || dev_alloc(&r.ATT, cap * (size_t)m->qd) || dev_alloc(&r.ACT, cap * I))
+        const size_t kmax = std::max<size_t>(std::max<size_t>(h, (size_t)m->qd), I);
+        if (dev_alloc(&r.X, cap * h) || dev_alloc(&r.XH, cap * kmax) || dev_alloc(&r.XL, cap * kmax) ||
+            dev_alloc(&r.QKV, cap * (size_t)(m->qd + 2 * m->kvd)) || dev_alloc(&r.Q, cap * (size_t)m->qd) ||
+            dev_alloc(&r.ATT, cap * (size_t)m->qd) || dev_alloc(&r.ACT, cap * I))
             return -1;
         r.cap = cap;
     }
@@ -566,6 +571,10 @@ static int ensure_rows(qdb_model *m, int n, bool logits) {
         r.log_cap = 0;
         if (dev_alloc(&r.LOG, (size_t)n * m->cfg.vocab)) return -1;
         r.log_cap = n;
+    }
+    if (!r.err) {
+        if (dev_alloc(&r.err, 4)) return -1;
+        CK(cudaMemset(r.err, 0, 4 * sizeof(int)));
     }
     if (n > r.rowkv_cap) {
         cudaFree(r.rowkv);
@@ -602,8 +611,8 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
     }
     for (int l = 0; l < m->cfg.layers; l++) {
         const QdbLayerW &lw = m->layers_host[l];
-        CK(qdb_launch_rmsnorm_rows(r.X, lw.in_norm, r.XN, n, h, m->cfg.eps, m->st));
-        CK(qdb_launch_gemm_rows(r.XN, lw.qkv, r.QKV, n, qkvd, h, 0, m->st));
+        CK(qdb_launch_rmsnorm_rows(r.X, lw.in_norm, r.XH, r.XL, n, h, m->cfg.eps, m->st));
+        CK(qdb_launch_gemm_tc(lw.qkv, r.XH, r.XL, r.QKV, n, qkvd, h, 0, r.err, m->st));
         if (single) {
             CK(qdb_launch_qk_rope_append_single(r.QKV, r.Q, row0_dev, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
                                                 m->cfg.eps, m->st));
@@ -613,10 +622,23 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
                                          m->cfg.eps, m->st));
             CK(qdb_launch_attn_rows(r.Q, row0_dev, pos_off, l, n, Hq, Hkv, S, r.part, r.ATT, m->st));
         }
-        CK(qdb_launch_gemm_rows(r.ATT, lw.o, r.X, n, h, m->qd, 1, m->st));
-        CK(qdb_launch_rmsnorm_rows(r.X, lw.post_norm, r.XN, n, h, m->cfg.eps, m->st));
-        CK(qdb_launch_gemm_rows(r.XN, lw.gu, r.ACT, n, 2 * I, h, 2, m->st));
-        CK(qdb_launch_gemm_rows(r.ACT, lw.down, r.X, n, h, I, 1, m->st));
+        CK(qdb_launch_split_bf16(r.ATT, r.XH, r.XL, (size_t)n * m->qd, m->st));
+        CK(qdb_launch_gemm_tc(lw.o, r.XH, r.XL, r.X, n, h, m->qd, 1, r.err, m->st));
+        CK(qdb_launch_rmsnorm_rows(r.X, lw.post_norm, r.XH, r.XL, n, h, m->cfg.eps, m->st));
+        CK(qdb_launch_gemm_tc(lw.gu, r.XH, r.XL, r.ACT, n, 2 * I, h, 2, r.err, m->st));
+        CK(qdb_launch_split_bf16(r.ACT, r.XH, r.XL, (size_t)n * I, m->st));
+        CK(qdb_launch_gemm_tc(lw.down, r.XH, r.XL, r.X, n, h, I, 1, r.err, m->st));
+    }
+    return 0;
+}
+
+// Reads (and clears) the tensor-core GEMMs' device error words after a sync.
+static int check_rows_err(qdb_model *m) {
+    int ev[4] = {0, 0, 0, 0};
+    CK(cudaMemcpy(ev, m->rs.err, sizeof(ev), cudaMemcpyDeviceToHost));
+    if (ev[0]) {
+        cudaMemset(m->rs.err, 0, sizeof(ev));
+        return fail("device error code %d in a tensor-core GEMM (a bounded wait ran out)", ev[0]);
     }
     return 0;
 }
@@ -637,7 +659,7 @@ static int prefill_impl(qdb_session *s, const float *embeds, bool device_ptr, in
     CK(cudaMemcpyAsync(m->rs.rowkv, &rk, sizeof(rk), cudaMemcpyHostToDevice, m->st));
     if (run_rows(m, seq_len, true, m->rs.rowkv, 0, s, start_pos)) return -1;
     CK(cudaStreamSynchronize(m->st));
-    return 0;
+    return check_rows_err(m);
 }
 
 extern "C" int qdb_prefill(qdb_session *s, const float *embeds, int seq_len, int start_pos) {
@@ -670,8 +692,8 @@ static int batch_setup(qdb_session *const *ss, int n, const int *pos, int extra_
 
 static int batch_tail(qdb_model *m, int n, int *tok_dev) {
     RowScratch &r = m->rs;
-    CK(qdb_launch_rmsnorm_rows(r.X, m->final_norm, r.XN, n, m->cfg.hidden, m->cfg.eps, m->st));
-    CK(qdb_launch_gemm_rows(r.XN, m->embed, r.LOG, n, m->cfg.vocab, m->cfg.hidden, 0, m->st));
+    CK(qdb_launch_rmsnorm_rows(r.X, m->final_norm, r.XH, r.XL, n, m->cfg.hidden, m->cfg.eps, m->st));
+    CK(qdb_launch_gemm_tc(m->embed, r.XH, r.XL, r.LOG, n, m->cfg.vocab, m->cfg.hidden, 0, r.err, m->st));
     CK(qdb_launch_argmax_rows(r.LOG, n, m->cfg.vocab, m->mask_eos, tok_dev, m->st));
     return 0;
 }
@@ -697,7 +719,7 @@ extern "C" int qdb_forward_batch(qdb_session *const *sessions, int n, const floa
     if (run_rows(m, n, false, m->rs.rowkv, 0, nullptr, 0) || batch_tail(m, n, m->rs.tok)) return -1;
     CK(cudaMemcpyAsync(tokens_out, m->rs.tok, sizeof(int) * n, cudaMemcpyDeviceToHost, m->st));
     CK(cudaStreamSynchronize(m->st));
-    return 0;
+    return check_rows_err(m);
 }
 
 extern "C" int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, const int *first_tokens, const int *pos,
@@ -717,7 +739,7 @@ extern "C" int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, cons
     }
     CK(cudaMemcpyAsync(tokens_out, m->rs.tok + n, sizeof(int) * (size_t)n * n_steps, cudaMemcpyDeviceToHost, m->st));
     CK(cudaStreamSynchronize(m->st));
-    return 0;
+    return check_rows_err(m);
 }
 
 // ------------------------------------------------------------------ decode step without allocation
