@@ -106,7 +106,9 @@ cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_p
 // Tensor-core GEMM (qdb_tcgemm.cu): Y (op)= X W^T with X given as bf16 hi/lo.
 cudaError_t qdb_launch_split_bf16(const float *x, uint16_t *hi, uint16_t *lo, size_t count, cudaStream_t st);
 cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,
-                               int mode, int *err, cudaStream_t st);
+                               int mode, int splits, int *err, cudaStream_t st);
+cudaError_t qdb_launch_swiglu_split(const float *gu, uint16_t *hi, uint16_t *lo, size_t count, cudaStream_t st);
+int qdb_gemm_tc_splits(int n, int N, int K, int sms);
 cudaError_t qdb_launch_argmax_rows(const float *logits, int n, int V, int mask_eos, int *tokens,
                                    cudaStream_t st);
 cudaError_t qdb_launch_embed_rows(const uint16_t *embed, const int *tokens, float *x, int n, int h, int V,

@@ -195,71 +195,131 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float *q, const
 }
 
 // ---------------------------------------------------------------- independent-row attention
-// Unit = (row, KV head g, split s), one warp per query head of the group,
-// keys [p0, p1) of ctx = pos + 1; partial (m, l, o[128]) per query head.
-__global__ void attn_rows_partial_kernel(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
-                                         int Hq, int Hkv, int S, float *part) {
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int R = Hq / Hkv;
+// Unit = (row, KV head g, split s) = one CTA of 8 warps over keys [p0, p1)
+// of ctx = pos + 1 (at most 64 keys: one 8-key step per warp, every K/V load
+// in flight at once). Lanes: 4 per key over 32 dims for q.k, then 4 dims per
+// lane for p.V; the R query heads of the group share each K/V load. Writes
+// the unnormalised partial (m, l, o[128]) of each query head; the merge
+// kernel combines the splits (same online-softmax algebra as
+// qwen_causal_attention, qwen_asr_kernels.c:1050-1141).
+constexpr int AR_WARPS = 8, AR_KEYS = 8;
+
+template <int R>
+__global__ void __launch_bounds__(AR_WARPS * 32) attn_rows_partial_kernel(const float *q, const QdbRowKV *rows,
+                                                                          int row_pos_offset, int layer, int Hq,
+                                                                          int Hkv, int S, float *part) {
+    __shared__ __align__(16) float qs[R][QDB_HD];
+    __shared__ float sm_m[AR_WARPS][R], sm_l[AR_WARPS][R];
+    __shared__ __align__(16) float sm_o[AR_WARPS][R][QDB_HD];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int row = blockIdx.x / Hkv, g = blockIdx.x % Hkv, s = blockIdx.y;
-    if (w >= R) return;
     const QdbRowKV rk = rows[row];
     const int pos = rk.pos + row_pos_offset;
     const int ctx = pos + 1;
     const int per = (ctx + S - 1) / S;
     const int p0 = s * per, p1 = min(ctx, p0 + per);
-    const int h = g * R + w;
-    const float *qv = q + (size_t)row * Hq * QDB_HD + (size_t)h * QDB_HD;
-    float qr[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) qr[i] = qv[lane * 4 + i];
     const size_t head_base = ((size_t)layer * Hkv + g) * (size_t)rk.cap * QDB_HD;
     const uint16_t *kc = rk.kc + head_base, *vc = rk.vc + head_base;
+    for (int t = threadIdx.x; t < R * QDB_HD; t += blockDim.x)
+        qs[t / QDB_HD][t % QDB_HD] = q[(size_t)row * Hq * QDB_HD + (size_t)(g * R) * QDB_HD + t];
+    __syncthreads();
     const float scale = 1.0f / sqrtf((float)QDB_HD);
-    float m = -INFINITY, l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int j0 = p0; j0 < p1; j0 += 8) {
-        uint2 kk[8], vv[8];
+    const int sub = lane & 3, kk = lane >> 2;
+    float m[R], l[R], o[R][4];
 #pragma unroll
-        for (int t = 0; t < 8; t++) {
-            if (j0 + t < p1) {
-                kk[t] = *reinterpret_cast<const uint2 *>(kc + (size_t)(j0 + t) * QDB_HD + lane * 4);
-                vv[t] = *reinterpret_cast<const uint2 *>(vc + (size_t)(j0 + t) * QDB_HD + lane * 4);
-            } else {
-                kk[t] = make_uint2(0u, 0u);
-                vv[t] = kk[t];
-            }
+    for (int h = 0; h < R; h++) {
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; e++) o[h][e] = 0.f;
+    }
+    for (int base = p0 + warp * AR_KEYS; base < p1; base += AR_WARPS * AR_KEYS) {
+        const int j = base + kk;
+        const bool valid = j < p1;
+        uint4 kv4[4];
+        if (valid) {
+            const uint4 *kp = reinterpret_cast<const uint4 *>(kc + (size_t)j * QDB_HD + sub * 32);
+#pragma unroll
+            for (int u = 0; u < 4; u++) kv4[u] = __ldcg(kp + u);
         }
+        uint2 vv[AR_KEYS];
 #pragma unroll
-        for (int t = 0; t < 8; t++) {
-            if (j0 + t >= p1) break;
-            float sc = qr[0] * kvlo(kk[t].x) + qr[1] * kvhi(kk[t].x) + qr[2] * kvlo(kk[t].y) +
-                       qr[3] * kvhi(kk[t].y);
-            sc = warp_sum(sc) * scale;
-            if (sc > m) {
-                const float corr = expf(m - sc);
-                l = l * corr + 1.f;
-                o[0] = o[0] * corr + kvlo(vv[t].x);
-                o[1] = o[1] * corr + kvhi(vv[t].x);
-                o[2] = o[2] * corr + kvlo(vv[t].y);
-                o[3] = o[3] * corr + kvhi(vv[t].y);
-                m = sc;
-            } else {
-                const float p = expf(sc - m);
-                l += p;
-                o[0] = fmaf(p, kvlo(vv[t].x), o[0]);
-                o[1] = fmaf(p, kvhi(vv[t].x), o[1]);
-                o[2] = fmaf(p, kvlo(vv[t].y), o[2]);
-                o[3] = fmaf(p, kvhi(vv[t].y), o[3]);
+        for (int t = 0; t < AR_KEYS; t++)
+            vv[t] = base + t < p1 ? __ldcg(reinterpret_cast<const uint2 *>(vc + (size_t)(base + t) * QDB_HD + lane * 4))
+                                  : make_uint2(0u, 0u);
+#pragma unroll
+        for (int h = 0; h < R; h++) {
+            float a0 = 0.f, a1 = 0.f;
+            if (valid) {
+                const float *qv = qs[h] + sub * 32;
+#pragma unroll
+                for (int u = 0; u < 4; u += 2) {
+                    a0 = dot8_kv(kv4[u], *reinterpret_cast<const float4 *>(qv + u * 8),
+                                 *reinterpret_cast<const float4 *>(qv + u * 8 + 4), a0);
+                    a1 = dot8_kv(kv4[u + 1], *reinterpret_cast<const float4 *>(qv + u * 8 + 8),
+                                 *reinterpret_cast<const float4 *>(qv + u * 8 + 12), a1);
+                }
             }
+            float acc = a0 + a1;
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+            const float sc = valid ? acc * scale : -INFINITY;
+            float cm = sc;
+            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
+            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
+            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
+            const float mn = fmaxf(m[h], cm);
+            const float corr = expf(m[h] - mn);
+            const float p = valid ? expf(sc - mn) : 0.f;
+            float ps = p;
+            ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+            l[h] = l[h] * corr + ps;
+#pragma unroll
+            for (int e = 0; e < 4; e++) o[h][e] *= corr;
+#pragma unroll
+            for (int t = 0; t < AR_KEYS; t++) {
+                const float pt = __shfl_sync(0xffffffffu, p, t * 4);
+                o[h][0] = fmaf(pt, kvlo(vv[t].x), o[h][0]);
+                o[h][1] = fmaf(pt, kvhi(vv[t].x), o[h][1]);
+                o[h][2] = fmaf(pt, kvlo(vv[t].y), o[h][2]);
+                o[h][3] = fmaf(pt, kvhi(vv[t].y), o[h][3]);
+            }
+            m[h] = mn;
         }
     }
-    float *dst = part + (((size_t)row * Hq + h) * S + s) * (2 + QDB_HD);
-    if (lane == 0) {
-        dst[0] = m;
-        dst[1] = l;
-    }
 #pragma unroll
-    for (int i = 0; i < 4; i++) dst[2 + lane * 4 + i] = o[i];
+    for (int h = 0; h < R; h++) {
+        if (lane == 0) {
+            sm_m[warp][h] = m[h];
+            sm_l[warp][h] = l[h];
+        }
+#pragma unroll
+        for (int e = 0; e < 4; e++) sm_o[warp][h][lane * 4 + e] = o[h][e];
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < R * QDB_HD; t += blockDim.x) {
+        const int h = t / QDB_HD, dd = t % QDB_HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < AR_WARPS; w++) M = fmaxf(M, sm_m[w][h]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < AR_WARPS; w++) {
+                const float f = expf(sm_m[w][h] - M);
+                L += sm_l[w][h] * f;
+                O += sm_o[w][h][dd] * f;
+            }
+        }
+        float *dst = part + (((size_t)row * Hq + g * R + h) * S + s) * (2 + QDB_HD);
+        if (dd == 0) {
+            dst[0] = M;
+            dst[1] = L;
+        }
+        dst[2 + dd] = O;
+    }
 }
 
 __global__ void attn_rows_merge_kernel(const float *part, int S, int Hq, float *out) {
@@ -380,9 +440,14 @@ extern "C" cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows
                                             int n, int Hq, int Hkv, int S, float *part, float *out,
                                             cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
-    const int R = Hq / Hkv;
     dim3 grid(n * Hkv, S);
-    attn_rows_partial_kernel<<<grid, 32 * R, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part);
+    switch (Hq / Hkv) {
+        case 1: attn_rows_partial_kernel<1><<<grid, AR_WARPS * 32, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part); break;
+        case 2: attn_rows_partial_kernel<2><<<grid, AR_WARPS * 32, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part); break;
+        case 4: attn_rows_partial_kernel<4><<<grid, AR_WARPS * 32, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part); break;
+        case 8: attn_rows_partial_kernel<8><<<grid, AR_WARPS * 32, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part); break;
+        default: return cudaErrorInvalidValue;
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     attn_rows_merge_kernel<<<dim3(n, Hq), QDB_HD, 0, st>>>(part, S, Hq, out);

@@ -52,6 +52,7 @@ struct RowScratch {
     int cap = 0;
     float *X = nullptr, *QKV = nullptr, *Q = nullptr, *ATT = nullptr, *ACT = nullptr;
     uint16_t *XH = nullptr, *XL = nullptr;  // bf16 hi/lo of the current GEMM input [cap, max(h, qd, I)]
+    float *GU = nullptr;                    // [64, 2I] gate/up sums of split-K decode GEMMs
     int *err = nullptr;                     // [4] device error words of the tensor-core GEMMs
     float *LOG = nullptr;  // [cap, V] only for batched decode
     int log_cap = 0;
@@ -246,7 +247,7 @@ extern "C" void qdb_model_free(qdb_model *m) {
     cudaFree(m->err); cudaFree(m->tok_dev);
     RowScratch &r = m->rs;
     cudaFree(r.X); cudaFree(r.XH); cudaFree(r.XL); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT);
-    cudaFree(r.LOG); cudaFree(r.part); cudaFree(r.rowkv); cudaFree(r.tok); cudaFree(r.err);
+    cudaFree(r.LOG); cudaFree(r.part); cudaFree(r.rowkv); cudaFree(r.tok); cudaFree(r.err); cudaFree(r.GU);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->h_tok) cudaFreeHost(m->h_tok);
     if (m->st) cudaStreamDestroy(m->st);
@@ -572,6 +573,7 @@ static int ensure_rows(qdb_model *m, int n, bool logits) {
         if (dev_alloc(&r.LOG, (size_t)n * m->cfg.vocab)) return -1;
         r.log_cap = n;
     }
+    if (n <= 64 && !r.GU && dev_alloc(&r.GU, (size_t)64 * 2 * I)) return -1;
     if (!r.err) {
         if (dev_alloc(&r.err, 4)) return -1;
         CK(cudaMemset(r.err, 0, 4 * sizeof(int)));
@@ -590,15 +592,15 @@ static int ensure_rows(qdb_model *m, int n, bool logits) {
 // to one session and are consecutive positions (prefill); otherwise row b uses
 // rowkv[b] at position rowkv[b].pos + pos_off (multi-utterance decode).
 static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, int pos_off, const qdb_session *s1,
-                    int start_pos) {
+                    int start_pos, int max_ctx = 1) {
     RowScratch &r = m->rs;
     const int h = m->cfg.hidden, I = m->cfg.intermediate, Hq = m->cfg.heads, Hkv = m->cfg.kv_heads;
     const int qkvd = m->qd + 2 * m->kvd;
     int S = 1;
     if (!single) {
-        const int units = n * Hkv;
-        S = (2 * m->sms + units - 1) / units;
-        if (S > 16) S = 16;
+        // one attention unit per 64 keys of the longest row (one step per warp)
+        S = (max_ctx + 63) / 64;
+        if (S > 64) S = 64;
         if (S < 1) S = 1;
         const size_t need = (size_t)n * Hq * S * (2 + QDB_HD);
         if (need > r.part_cap) {
@@ -609,10 +611,23 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
             r.part_cap = need;
         }
     }
+    // Y (op)= X W^T from the bf16 split in XH/XL. Skinny problems (decode
+    // batches of <= 64 rows) use split-K with atomic accumulation: mode 0
+    // targets are zeroed first, mode 1 targets already hold the residual.
+    auto gemm = [&](const uint16_t *W, float *Y, int N, int K, int mode) -> int {
+        const int sp = n <= 64 ? qdb_gemm_tc_splits(n, N, K, m->sms) : 1;
+        if (sp > 1) {
+            if (mode == 0) CK(cudaMemsetAsync(Y, 0, sizeof(float) * (size_t)n * N, m->st));
+            CK(qdb_launch_gemm_tc(W, r.XH, r.XL, Y, n, N, K, 3, sp, r.err, m->st));
+        } else {
+            CK(qdb_launch_gemm_tc(W, r.XH, r.XL, Y, n, N, K, mode, 1, r.err, m->st));
+        }
+        return 0;
+    };
     for (int l = 0; l < m->cfg.layers; l++) {
         const QdbLayerW &lw = m->layers_host[l];
         CK(qdb_launch_rmsnorm_rows(r.X, lw.in_norm, r.XH, r.XL, n, h, m->cfg.eps, m->st));
-        CK(qdb_launch_gemm_tc(lw.qkv, r.XH, r.XL, r.QKV, n, qkvd, h, 0, r.err, m->st));
+        if (gemm(lw.qkv, r.QKV, qkvd, h, 0)) return -1;
         if (single) {
             CK(qdb_launch_qk_rope_append_single(r.QKV, r.Q, row0_dev, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
                                                 m->cfg.eps, m->st));
@@ -623,11 +638,17 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
             CK(qdb_launch_attn_rows(r.Q, row0_dev, pos_off, l, n, Hq, Hkv, S, r.part, r.ATT, m->st));
         }
         CK(qdb_launch_split_bf16(r.ATT, r.XH, r.XL, (size_t)n * m->qd, m->st));
-        CK(qdb_launch_gemm_tc(lw.o, r.XH, r.XL, r.X, n, h, m->qd, 1, r.err, m->st));
+        if (gemm(lw.o, r.X, h, m->qd, 1)) return -1;
         CK(qdb_launch_rmsnorm_rows(r.X, lw.post_norm, r.XH, r.XL, n, h, m->cfg.eps, m->st));
-        CK(qdb_launch_gemm_tc(lw.gu, r.XH, r.XL, r.ACT, n, 2 * I, h, 2, r.err, m->st));
-        CK(qdb_launch_split_bf16(r.ACT, r.XH, r.XL, (size_t)n * I, m->st));
-        CK(qdb_launch_gemm_tc(lw.down, r.XH, r.XL, r.X, n, h, I, 1, r.err, m->st));
+        if (n <= 64 && qdb_gemm_tc_splits(n, 2 * I, h, m->sms) > 1) {
+            // split-K: gate/up sums into GU, then SwiGLU straight into the bf16 split
+            if (gemm(lw.gu, r.GU, 2 * I, h, 0)) return -1;
+            CK(qdb_launch_swiglu_split(r.GU, r.XH, r.XL, (size_t)n * I, m->st));
+        } else {
+            CK(qdb_launch_gemm_tc(lw.gu, r.XH, r.XL, r.ACT, n, 2 * I, h, 2, 1, r.err, m->st));
+            CK(qdb_launch_split_bf16(r.ACT, r.XH, r.XL, (size_t)n * I, m->st));
+        }
+        if (gemm(lw.down, r.X, h, I, 1)) return -1;
     }
     return 0;
 }
@@ -670,7 +691,8 @@ extern "C" int qdb_prefill_device(qdb_session *s, const float *embeds_dev, int s
     return prefill_impl(s, embeds_dev, true, seq_len, start_pos);
 }
 
-static int batch_setup(qdb_session *const *ss, int n, const int *pos, int extra_steps, qdb_model **mo) {
+static int batch_setup(qdb_session *const *ss, int n, const int *pos, int extra_steps, qdb_model **mo,
+                       int *max_pos = nullptr) {
     if (!ss || n <= 0 || !pos) return fail("bad batch arguments");
     qdb_model *m = ss[0] ? ss[0]->m : nullptr;
     if (!m) return fail("null session or session's model has been freed");
@@ -684,6 +706,10 @@ static int batch_setup(qdb_session *const *ss, int n, const int *pos, int extra_
         if (prep_pos(ss[b], pos[b] + extra_steps)) return -1;
     }
     for (int b = 0; b < n; b++) rk[b] = QdbRowKV{ss[b]->kc, ss[b]->vc, ss[b]->cap, pos[b]};
+    if (max_pos) {
+        *max_pos = 0;
+        for (int b = 0; b < n; b++) *max_pos = std::max(*max_pos, pos[b]);
+    }
     CK(cudaMemcpyAsync(m->rs.rowkv, rk.data(), sizeof(QdbRowKV) * n, cudaMemcpyHostToDevice, m->st));
     CK(cudaStreamSynchronize(m->st));  // rk is a stack vector
     *mo = m;
@@ -693,7 +719,7 @@ static int batch_setup(qdb_session *const *ss, int n, const int *pos, int extra_
 static int batch_tail(qdb_model *m, int n, int *tok_dev) {
     RowScratch &r = m->rs;
     CK(qdb_launch_rmsnorm_rows(r.X, m->final_norm, r.XH, r.XL, n, m->cfg.hidden, m->cfg.eps, m->st));
-    CK(qdb_launch_gemm_tc(m->embed, r.XH, r.XL, r.LOG, n, m->cfg.vocab, m->cfg.hidden, 0, r.err, m->st));
+    CK(qdb_launch_gemm_tc(m->embed, r.XH, r.XL, r.LOG, n, m->cfg.vocab, m->cfg.hidden, 0, 1, r.err, m->st));
     CK(qdb_launch_argmax_rows(r.LOG, n, m->cfg.vocab, m->mask_eos, tok_dev, m->st));
     return 0;
 }
@@ -714,9 +740,10 @@ extern "C" int qdb_forward_batch(qdb_session *const *sessions, int n, const floa
     g_err.clear();
     qdb_model *m = nullptr;
     if (!embeds || !tokens_out) return fail("null argument");
-    if (batch_setup(sessions, n, pos, 0, &m) || ensure_tok(m, n)) return -1;
+    int maxp = 0;
+    if (batch_setup(sessions, n, pos, 0, &m, &maxp) || ensure_tok(m, n)) return -1;
     CK(cudaMemcpyAsync(m->rs.X, embeds, (size_t)n * m->cfg.hidden * 4, cudaMemcpyHostToDevice, m->st));
-    if (run_rows(m, n, false, m->rs.rowkv, 0, nullptr, 0) || batch_tail(m, n, m->rs.tok)) return -1;
+    if (run_rows(m, n, false, m->rs.rowkv, 0, nullptr, 0, maxp + 1) || batch_tail(m, n, m->rs.tok)) return -1;
     CK(cudaMemcpyAsync(tokens_out, m->rs.tok, sizeof(int) * n, cudaMemcpyDeviceToHost, m->st));
     CK(cudaStreamSynchronize(m->st));
     return check_rows_err(m);
@@ -728,14 +755,15 @@ extern "C" int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, cons
     qdb_model *m = nullptr;
     if (!first_tokens || (n_steps > 0 && !tokens_out)) return fail("null argument");
     if (n_steps <= 0) return 0;
-    if (batch_setup(sessions, n, pos, n_steps - 1, &m) || ensure_tok(m, (size_t)n * (n_steps + 1))) return -1;
+    int maxp = 0;
+    if (batch_setup(sessions, n, pos, n_steps - 1, &m, &maxp) || ensure_tok(m, (size_t)n * (n_steps + 1))) return -1;
     for (int b = 0; b < n; b++)
         if (first_tokens[b] < 0 || first_tokens[b] >= m->cfg.vocab) return fail("row %d: token out of range", b);
     CK(cudaMemcpyAsync(m->rs.tok, first_tokens, sizeof(int) * n, cudaMemcpyHostToDevice, m->st));
     for (int i = 0; i < n_steps; i++) {
         int *tin = m->rs.tok + (size_t)i * n;
         CK(qdb_launch_embed_rows(m->embed, tin, m->rs.X, n, m->cfg.hidden, m->cfg.vocab, m->st));
-        if (run_rows(m, n, false, m->rs.rowkv, i, nullptr, 0) || batch_tail(m, n, tin + n)) return -1;
+        if (run_rows(m, n, false, m->rs.rowkv, i, nullptr, 0, maxp + i + 1) || batch_tail(m, n, tin + n)) return -1;
     }
     CK(cudaMemcpyAsync(tokens_out, m->rs.tok + n, sizeof(int) * (size_t)n * n_steps, cudaMemcpyDeviceToHost, m->st));
     CK(cudaStreamSynchronize(m->st));

@@ -122,7 +122,7 @@ template <int BN, int S>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXh,
                    const __grid_constant__ CUtensorMap tmXl, float *__restrict__ Y, int n, int N, int K, int mode,
-                   int *err) {
+                   int kb_per, int *err) {
     constexpr int A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
     constexpr int B_BYTES = BN * TC_BK * 2;
     constexpr int STAGE = A_BYTES + 2 * B_BYTES;
@@ -132,7 +132,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * TC_BM, a0 = blockIdx.y * BN;
-    const int nk = K / TC_BK;
+    // split-K: this CTA takes k-blocks [kb0, kb0 + nk) (gridDim.z splits)
+    const int kb0 = blockIdx.z * kb_per;
+    const int nk = min(K / TC_BK - kb0, kb_per);
     // 128-byte swizzle atoms need 1024-byte aligned tiles: round the base up
     // (the launch reserves 1 KB of slack for this)
     unsigned char *smem = smem_dyn + ((1024u - (su32(smem_dyn) & 1023u)) & 1023u);
@@ -163,9 +165,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (kb >= S && !mb_wait(&empty[s], ((kb / S) - 1) & 1, err)) break;
             unsigned char *st = smem + (size_t)s * STAGE;
             mb_expect(&full[s], STAGE);
-            tma_load_2d(st, &tmW, kb * TC_BK, m0, &full[s]);
-            tma_load_2d(st + A_BYTES, &tmXh, kb * TC_BK, a0, &full[s]);
-            tma_load_2d(st + A_BYTES + B_BYTES, &tmXl, kb * TC_BK, a0, &full[s]);
+            const int kx = (kb0 + kb) * TC_BK;
+            tma_load_2d(st, &tmW, kx, m0, &full[s]);
+            tma_load_2d(st + A_BYTES, &tmXh, kx, a0, &full[s]);
+            tma_load_2d(st + A_BYTES + B_BYTES, &tmXl, kx, a0, &full[s]);
             issued = kb + 1;
         }
         // wait for the last copies of every stage to land before leaving
@@ -211,7 +214,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                             Y[(size_t)arow * (N / 2) + wrow / 2] = silu_mul(v[j], u);
                     } else if (arow < n && wrow < N) {
                         float *dst = Y + (size_t)arow * N + wrow;
-                        *dst = mode == 1 ? *dst + v[j] : v[j];
+                        if (mode == 3) atomicAdd(dst, v[j]);  // split-K partial (compiles to a reduction)
+                        else *dst = mode == 1 ? *dst + v[j] : v[j];
                     }
                 }
             }
@@ -223,6 +227,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
     }
+}
+
+// SwiGLU of interleaved (gate, up) f32 pairs [n, 2I] -> bf16 hi/lo [n, I]
+// (qwen_swiglu_multiply, qwen_asr_kernels.c:895-959, then the GEMM split).
+__global__ void swiglu_split_kernel(const float *__restrict__ gu, uint16_t *__restrict__ hi, uint16_t *__restrict__ lo,
+                                    size_t count) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    const float2 p = reinterpret_cast<const float2 *>(gu)[i];
+    const float v = silu_mul(p.x, p.y);
+    const uint16_t h = f32_to_bf16_rn(v);
+    hi[i] = h;
+    lo[i] = f32_to_bf16_rn(v - __uint_as_float((uint32_t)h << 16));
 }
 
 // f32 [n, K] -> bf16 hi [n, K] + bf16 lo [n, K] with hi + lo ~= x
@@ -263,7 +280,7 @@ bool make_map(CUtensorMap *m, const void *base, int rows, int cols, int box_rows
 
 template <int BN, int S>
 cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,
-                      int mode, int *err, cudaStream_t st) {
+                      int mode, int splits, int *err, cudaStream_t st) {
     CUtensorMap mw, mh, ml;
     if (!make_map(&mw, W, N, K, TC_BM) || !make_map(&mh, Xh, n, K, BN) || !make_map(&ml, Xl, n, K, BN))
         return cudaErrorInvalidValue;
@@ -272,7 +289,10 @@ cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl,
     cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid((N + TC_BM - 1) / TC_BM, (n + BN - 1) / BN);
-    tc_gemm_kernel<BN, S><<<grid, TC_THREADS, smem, st>>>(mw, mh, ml, Y, n, N, K, mode, err);
+    const int nk = K / TC_BK;
+    const int kb_per = (nk + splits - 1) / splits;
+    grid.z = (nk + kb_per - 1) / kb_per;
+    tc_gemm_kernel<BN, S><<<grid, TC_THREADS, smem, st>>>(mw, mh, ml, Y, n, N, K, mode, kb_per, err);
     return cudaGetLastError();
 }
 
@@ -285,14 +305,34 @@ extern "C" cudaError_t qdb_launch_split_bf16(const float *x, uint16_t *hi, uint1
     return cudaGetLastError();
 }
 
+extern "C" cudaError_t qdb_launch_swiglu_split(const float *gu, uint16_t *hi, uint16_t *lo, size_t count,
+                                               cudaStream_t st) {
+    if (!count) return cudaSuccess;
+    swiglu_split_kernel<<<(unsigned)((count + 255) / 256), 256, 0, st>>>(gu, hi, lo, count);
+    return cudaGetLastError();
+}
+
 // Y (op)= X W^T on tensor cores; X given as its bf16 split (Xh, Xl) [n, K].
-// mode: 0 store [n, N], 1 add into Y [n, N], 2 SwiGLU of row pairs -> Y [n, N/2].
+// mode: 0 store [n, N], 1 add into Y [n, N], 2 SwiGLU of row pairs -> Y [n, N/2],
+// 3 add with atomics (split-K allowed; Y must hold the starting value).
+// splits > 1 (mode 3 only) divides K across CTAs so that skinny problems
+// (few weight-row tiles) still spread the weight stream over the whole GPU.
 // K % 64 == 0; all base pointers 16-byte aligned; N even for mode 2.
 extern "C" cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n,
-                                          int N, int K, int mode, int *err, cudaStream_t st) {
+                                          int N, int K, int mode, int splits, int *err, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
-    if (K % TC_BK || (mode == 2 && (N & 1))) return cudaErrorInvalidValue;
+    if (K % TC_BK || (mode == 2 && (N & 1)) || mode < 0 || mode > 3) return cudaErrorInvalidValue;
+    if (splits < 1 || (splits > 1 && mode != 3)) return cudaErrorInvalidValue;
     if (((uintptr_t)W | (uintptr_t)Xh | (uintptr_t)Xl) & 15) return cudaErrorInvalidValue;
-    if (n <= 64) return launch_tc<64, 6>(W, Xh, Xl, Y, n, N, K, mode, err, st);
-    return launch_tc<128, 4>(W, Xh, Xl, Y, n, N, K, mode, err, st);
+    if (n <= 64) return launch_tc<64, 6>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st);
+    return launch_tc<128, 4>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st);
+}
+
+// Split count that spreads a GEMM of `tiles` output tiles over ~2 waves.
+extern "C" int qdb_gemm_tc_splits(int n, int N, int K, int sms) {
+    const int tiles = ((N + TC_BM - 1) / TC_BM) * ((n + (n <= 64 ? 63 : 127)) / (n <= 64 ? 64 : 128));
+    const int nk = K / TC_BK;
+    int s = (2 * sms + tiles - 1) / tiles;
+    if (s > nk) s = nk;
+    return s < 1 ? 1 : s;
 }
