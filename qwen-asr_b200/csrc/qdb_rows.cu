@@ -202,10 +202,13 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float *q, const
 // the unnormalised partial (m, l, o[128]) of each query head; the merge
 // kernel combines the splits (same online-softmax algebra as
 // qwen_causal_attention, qwen_asr_kernels.c:1050-1141).
+#ifndef QDB_AR_MINB
+#define QDB_AR_MINB 3  // resident CTAs per SM the attention kernel is register-capped for
+#endif
 constexpr int AR_WARPS = 8, AR_KEYS = 8;
 
 template <int R>
-__global__ void __launch_bounds__(AR_WARPS * 32) attn_rows_partial_kernel(const float *q, const QdbRowKV *rows,
+__global__ void __launch_bounds__(AR_WARPS * 32, QDB_AR_MINB) attn_rows_partial_kernel(const float *q, const QdbRowKV *rows,
                                                                           int row_pos_offset, int layer, int Hq,
                                                                           int Hkv, int S, float *part) {
     __shared__ __align__(16) float qs[R][QDB_HD];
