@@ -328,11 +328,19 @@ extern "C" cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh,
     return launch_tc<128, 4>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st);
 }
 
-// Split count that spreads a GEMM of `tiles` output tiles over ~2 waves.
+#ifndef QDB_SPLIT_WAVES
+#define QDB_SPLIT_WAVES 1    // CTAs targeted per SM by split-K
+#endif
+#ifndef QDB_SPLIT_MIN_KB
+#define QDB_SPLIT_MIN_KB 4   // fewest 64-wide k-blocks one split-K CTA takes
+#endif
+// Split count for a skinny GEMM: about QDB_SPLIT_WAVES CTAs per SM, each
+// with at least QDB_SPLIT_MIN_KB k-blocks (short CTAs are all set-up).
 extern "C" int qdb_gemm_tc_splits(int n, int N, int K, int sms) {
     const int tiles = ((N + TC_BM - 1) / TC_BM) * ((n + (n <= 64 ? 63 : 127)) / (n <= 64 ? 64 : 128));
     const int nk = K / TC_BK;
-    int s = (2 * sms + tiles - 1) / tiles;
-    if (s > nk) s = nk;
+    int s = (QDB_SPLIT_WAVES * sms + tiles - 1) / tiles;
+    const int smax = nk / QDB_SPLIT_MIN_KB;
+    if (s > smax) s = smax;
     return s < 1 ? 1 : s;
 }
