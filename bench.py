@@ -42,6 +42,7 @@ CONFIGS = {
     "c0": ("0.6b", 10.0, 128, 1),
     "c1": ("1.7b", 30.0, 256, 1),
     "c2": ("0.6b", 20.0, 200, 64),
+    "c3": ("1.7b", 300.0, 1024, 1),
 }
 KV_BYTES_PER_POS = 28 * 8 * 128 * 2 * 2  # bf16 K and V per cached position (all layers)
 
@@ -149,9 +150,9 @@ def run_ours(args):
     preset, seconds, n_dec, n_utt = CONFIGS[args.config]
     cfg = synth.PRESETS[preset]
     if n_utt > 1:
-        if n_utt % world:
-            raise SystemExit(f"{n_utt} utterances do not shard evenly over {world} GPUs")
-        n_local, first = n_utt // world, rank * (n_utt // world)
+        import importlib
+        shard = importlib.import_module("qwen_asr_b200.shard")
+        first, n_local = shard.shard_range(n_utt, world, rank)
         scaling = "strong"
     else:
         n_local, first = 1, 0
@@ -241,15 +242,14 @@ def run_ours(args):
     e2e_tot_ms = sum(e[0].elapsed_time(e[2]) for e in e2e_ev)
 
     # max over ranks
-    vals = torch.tensor([dec_ms, pre_ms, tot_ms, e2e_dec_ms, e2e_tot_ms], dtype=torch.float64,
-                        device=f"cuda:{local}")
-    if world > 1:
-        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    dec_ms, pre_ms, tot_ms, e2e_dec_ms, e2e_tot_ms = vals.tolist()
+    import importlib
+    shard = importlib.import_module("qwen_asr_b200.shard")
+    dec_ms, pre_ms, tot_ms, e2e_dec_ms, e2e_tot_ms = shard.max_over_ranks(
+        [dec_ms, pre_ms, tot_ms, e2e_dec_ms, e2e_tot_ms], device=f"cuda:{local}")
 
-    tokens_total = args.steps * n_dec * n_local * world
+    tokens_total = args.steps * n_dec * (n_utt if n_utt > 1 else world)
     value = tokens_total / (dec_ms / 1e3)
-    e2e_value = (n_e2e * n_dec * n_local * world) / (e2e_dec_ms / 1e3)
+    e2e_value = (n_e2e * n_dec * (n_utt if n_utt > 1 else world)) / (e2e_dec_ms / 1e3)
     # roofline of the dominant kernel (the persistent decode step at b=1; the
     # batched decode step for c2): algorithmic bytes per launch / launch time
     h, L, V, I = cfg.hidden, cfg.layers, cfg.vocab, cfg.intermediate
