@@ -63,14 +63,25 @@ __host__ __device__ static inline int qdb_step_trace_events(int layers) { return
 // Epochs one decode step consumes (host advances the base by this much).
 __host__ __device__ static inline unsigned qdb_step_epochs(int layers) { return 5u * (unsigned)layers + 1u; }
 
-#define QDB_STEP_THREADS 288
+// One compiled build of the persistent step (qdb_step.cu is built twice:
+// consumer-warp count and ring-stage size are compile-time constants).
+struct QdbStepKernel {
+    const char *name;
+    int consumer_warps;  // also sets the attention split size: 8 keys per warp
+    int stage_bytes;     // bytes of one weight stage of the shared-memory ring
+    int max_vector;      // longest activation vector (h, heads*head_dim, I) it loads
+    int (*smem_bytes)(const QdbDims &d);
+    // Launches one persistent step. grid = co-resident CTAs (one per SM).
+    cudaError_t (*launch)(const QdbStepArgs &a, int grid, cudaStream_t st);
+};
 
 extern "C" {
-// Launches one persistent step. grid = co-resident CTAs (one per SM).
-cudaError_t qdb_launch_step(const QdbStepArgs &a, int grid, cudaStream_t st);
+// 6 consumer warps, 16 KB stages (even row counts for hidden 2048)
+const QdbStepKernel *qdb_step_kernel_w6(void);
+// 7 consumer warps, 12 KB stages (hidden 1024)
+const QdbStepKernel *qdb_step_kernel_w7(void);
 int qdb_step_max_grid(int device);
 int qdb_step_max_splits(int grid, int kv_heads);
-int qdb_step_smem_bytes(const QdbDims &d);
 
 // RoPE table: tab[p][i] = (cos, sin) of (float)p * inv_freq[i], p < n_pos.
 cudaError_t qdb_launch_rope_table(float2 *tab, int n_pos, float theta, cudaStream_t st);

@@ -102,6 +102,7 @@ struct qdb_model {
     int *tok_dev = nullptr;
     int tok_cap = 0;
     int max_splits = 1;
+    const QdbStepKernel *step_k = nullptr;  // the step build this model uses
     float *h_stage = nullptr;  // pinned [max(h, V)]
     int *h_tok = nullptr;      // pinned
     RowScratch rs;
@@ -157,11 +158,30 @@ extern "C" qdb_model *qdb_model_create(const qdb_config *cfg, int device) {
     if (R != 1 && R != 2 && R != 4 && R != 8) { fail("heads/kv_heads must be 1, 2, 4 or 8"); return nullptr; }
     if (cfg->layers <= 0 || cfg->layers > 32 || cfg->vocab <= 0) { fail("layers must be 1..32 and vocab > 0"); return nullptr; }
     if (cfg->heads * QDB_HD % 256) { fail("heads*head_dim must be a multiple of 256"); return nullptr; }
+    // Step build: 16 KB stages for hidden >= 2048 (even rows per item), the
+    // 7-warp 12 KB build below that; either one if the other cannot hold the
+    // model. A ring stage must hold a gate/up row pair and one row of the
+    // longest K, and the step loads vectors of at most max_vector floats.
+    const QdbStepKernel *step_k = nullptr;
+    {
+        const long long kmax = std::max<long long>(std::max<long long>(2LL * cfg->hidden, cfg->intermediate),
+                                                   (long long)cfg->heads * QDB_HD);
+        const int vmax = std::max(cfg->hidden, std::max(cfg->intermediate, cfg->heads * QDB_HD));
+        const QdbStepKernel *pref[2] = {qdb_step_kernel_w6(), qdb_step_kernel_w7()};
+        if (cfg->hidden < 2048) std::swap(pref[0], pref[1]);
+        for (const QdbStepKernel *k : pref)
+            if (!step_k && kmax * 2 <= k->stage_bytes && vmax <= k->max_vector) step_k = k;
+        if (!step_k) {
+            fail("rows of %lld bf16 / vectors of %d floats exceed the decode step's stages", kmax, vmax);
+            return nullptr;
+        }
+    }
     int ndev = qdb_device_count();
     if (device < 0 || device >= ndev) { fail("CUDA device %d not available (%d visible)", device, ndev); return nullptr; }
 
     qdb_model *m = new qdb_model();
     m->cfg = *cfg;
+    m->step_k = step_k;
     m->device = device;
     m->d = QdbDims{cfg->hidden, cfg->layers, cfg->heads, cfg->kv_heads, cfg->intermediate, cfg->vocab, cfg->eps};
     m->qd = cfg->heads * QDB_HD;
@@ -423,9 +443,11 @@ static QdbStepArgs step_args(qdb_session *s, int pos) {
     a.tattn = m->tattn;
     a.tact = m->tact;
     a.tpart = m->tpart;
-    // attention splits: about 64 keys per unit, at most grid / Hkv units per head
+    // attention splits: one key-loop iteration per unit (8 keys per consumer
+    // warp), at most grid / Hkv units per head
     const int ctx = pos + 1;
-    int S = (ctx + 63) / 64;
+    const int keys_per_unit = m->step_k->consumer_warps * 8;
+    int S = (ctx + keys_per_unit - 1) / keys_per_unit;
     if (S > m->max_splits) S = m->max_splits;
     if (S < 1) S = 1;
     a.splits = S;
@@ -447,7 +469,7 @@ static int launch_step(qdb_model *m, QdbStepArgs &a) {
         m->epoch = 1;
     }
     a.epoch = m->epoch;
-    CK(qdb_launch_step(a, m->grid, m->st));
+    CK(m->step_k->launch(a, m->grid, m->st));
     m->epoch += span;
     return 0;
 }
@@ -829,7 +851,7 @@ extern "C" int qdb_forward_noalloc(qdb_session *s, const float *embed_dev, int p
     a.hidden_out = nullptr;
     a.logits_out = nullptr;
     a.epoch = epoch;
-    CK(qdb_launch_step(a, m->grid, m->st));
+    CK(m->step_k->launch(a, m->grid, m->st));
     epoch += span;
     int ev[4] = {0, 0, 0, 0};
     CK(cudaMemcpyAsync(ev, a.err, sizeof(ev), cudaMemcpyDeviceToHost, m->st));

@@ -31,14 +31,24 @@
 #include "qdb_common.cuh"
 #include "qdb_kernels.h"
 
+// Build constants (qdb_step_w7.cu includes this file with its own).
+#ifndef QDB_NCW
+#define QDB_NCW 6
+#endif
+#ifndef QDB_STAGE_BYTES
+#define QDB_STAGE_BYTES 16384
+#endif
+#ifndef QDB_STEP_ENTRY
+#define QDB_STEP_ENTRY qdb_step_kernel_w6
+#define QDB_STEP_NAME "w6s16"
+#define QDB_STEP_COMMON 1  // this build also defines the variant-independent helpers
+#endif
+
 namespace {
 
-constexpr int NCW = 8;                    // consumer warps
+constexpr int NCW = QDB_NCW;              // consumer warps
 constexpr int NCT = NCW * 32;             // consumer threads
 constexpr int NTHREADS = NCT + 32;        // + producer warp
-#ifndef QDB_STAGE_BYTES
-#define QDB_STAGE_BYTES 12288
-#endif
 #ifndef QDB_STAGES_PER_WARP
 #define QDB_STAGES_PER_WARP 2
 #endif
@@ -62,9 +72,8 @@ constexpr int L2_AHEAD = QDB_L2_AHEAD;    // items prefetched into L2 ahead of t
 constexpr int OWN_ROWS = 64;              // residual rows one CTA may own
 constexpr int MAX_LAYERS = 32;             // layer table kept in shared memory
 constexpr int ATT_KEYS = 8;               // keys per warp iteration
-constexpr int POLL = 24;                  // tagged words per consumer thread per vector load
+constexpr int POLL = (6144 + NCT - 1) / NCT;  // tagged words per consumer thread per vector load
 
-static_assert(NTHREADS == QDB_STEP_THREADS, "thread count mismatch");
 static_assert(NSTAGE % NCW == 0, "a ring stage must belong to exactly one consumer warp");
 
 typedef unsigned long long u64;
@@ -422,42 +431,62 @@ __device__ void rmsnorm_smem(float *x, const float *w, int h, float eps, float *
 }
 
 // Dot products of nr rows (bf16, row length K, in smem) with act (smem f32).
-// out[r] for r < nr (nr <= 32). Two rows at a time; lanes stride 8 elements.
-__device__ __forceinline__ void stage_dots(const uint16_t *wst, int nr, int K, const float *act, float *out) {
+// out[r] for r < nr (nr <= 32). Two dot streams at a time, lanes stride 8
+// elements: row pairs share the activation loads; an odd last row is split
+// into its two halves (when K is a multiple of 512) instead of being paired
+// with a duplicate of itself.
+// HALVES: the second stream reads act at +x1off (a half row); otherwise both
+// streams share one activation load.
+template <bool HALVES>
+__device__ __forceinline__ void dots2(const uint4 *p0, const uint4 *p1, const float *x0, int x1off, int nv,
+                                      float &s0, float &s1) {
     const int lane = threadIdx.x & 31;
+    // four independent accumulator chains per stream (the FMA latency of a
+    // single chain is what this latency-bound loop would otherwise wait on)
+    float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+    for (int j = 0; j < nv; j++) {
+        const int e = (j * 32 + lane);
+        const uint4 w0 = p0[e];
+        const uint4 w1 = p1[e];
+        const float4 xa = *reinterpret_cast<const float4 *>(x0 + e * 8);
+        const float4 xb = *reinterpret_cast<const float4 *>(x0 + e * 8 + 4);
+        const float4 ya = HALVES ? *reinterpret_cast<const float4 *>(x0 + x1off + e * 8) : xa;
+        const float4 yb = HALVES ? *reinterpret_cast<const float4 *>(x0 + x1off + e * 8 + 4) : xb;
+        a[0] = fmaf(bf16lo(w0.x), xa.x, a[0]); a[1] = fmaf(bf16hi(w0.x), xa.y, a[1]);
+        a[2] = fmaf(bf16lo(w0.y), xa.z, a[2]); a[3] = fmaf(bf16hi(w0.y), xa.w, a[3]);
+        a[0] = fmaf(bf16lo(w0.z), xb.x, a[0]); a[1] = fmaf(bf16hi(w0.z), xb.y, a[1]);
+        a[2] = fmaf(bf16lo(w0.w), xb.z, a[2]); a[3] = fmaf(bf16hi(w0.w), xb.w, a[3]);
+        b[0] = fmaf(bf16lo(w1.x), ya.x, b[0]); b[1] = fmaf(bf16hi(w1.x), ya.y, b[1]);
+        b[2] = fmaf(bf16lo(w1.y), ya.z, b[2]); b[3] = fmaf(bf16hi(w1.y), ya.w, b[3]);
+        b[0] = fmaf(bf16lo(w1.z), yb.x, b[0]); b[1] = fmaf(bf16hi(w1.z), yb.y, b[1]);
+        b[2] = fmaf(bf16lo(w1.w), yb.z, b[2]); b[3] = fmaf(bf16hi(w1.w), yb.w, b[3]);
+    }
+    s0 = (a[0] + a[1]) + (a[2] + a[3]);
+    s1 = (b[0] + b[1]) + (b[2] + b[3]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    }
+}
+
+__device__ __forceinline__ void stage_dots(const uint16_t *wst, int nr, int K, const float *act, float *out) {
     const int nv = K >> 8;
     for (int r = 0; r < nr; r += 2) {
-        const bool two = r + 1 < nr;
         const uint4 *p0 = reinterpret_cast<const uint4 *>(wst + (size_t)r * K);
-        const uint4 *p1 = reinterpret_cast<const uint4 *>(wst + (size_t)(r + (two ? 1 : 0)) * K);
-        // four independent accumulator chains per row (the FMA latency of a
-        // single chain is what this latency-bound loop would otherwise wait on)
-        float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-        for (int j = 0; j < nv; j++) {
-            const int e = (j * 32 + lane);
-            const uint4 w0 = p0[e];
-            const uint4 w1 = p1[e];
-            const float4 xa = *reinterpret_cast<const float4 *>(act + e * 8);
-            const float4 xb = *reinterpret_cast<const float4 *>(act + e * 8 + 4);
-            a[0] = fmaf(bf16lo(w0.x), xa.x, a[0]); a[1] = fmaf(bf16hi(w0.x), xa.y, a[1]);
-            a[2] = fmaf(bf16lo(w0.y), xa.z, a[2]); a[3] = fmaf(bf16hi(w0.y), xa.w, a[3]);
-            a[0] = fmaf(bf16lo(w0.z), xb.x, a[0]); a[1] = fmaf(bf16hi(w0.z), xb.y, a[1]);
-            a[2] = fmaf(bf16lo(w0.w), xb.z, a[2]); a[3] = fmaf(bf16hi(w0.w), xb.w, a[3]);
-            b[0] = fmaf(bf16lo(w1.x), xa.x, b[0]); b[1] = fmaf(bf16hi(w1.x), xa.y, b[1]);
-            b[2] = fmaf(bf16lo(w1.y), xa.z, b[2]); b[3] = fmaf(bf16hi(w1.y), xa.w, b[3]);
-            b[0] = fmaf(bf16lo(w1.z), xb.x, b[0]); b[1] = fmaf(bf16hi(w1.z), xb.y, b[1]);
-            b[2] = fmaf(bf16lo(w1.w), xb.z, b[2]); b[3] = fmaf(bf16hi(w1.w), xb.w, b[3]);
+        float s0, s1;
+        if (r + 1 < nr) {
+            dots2<false>(p0, reinterpret_cast<const uint4 *>(wst + (size_t)(r + 1) * K), act, 0, nv, s0, s1);
+            out[r] = s0;
+            out[r + 1] = s1;
+        } else if ((nv & 1) == 0) {
+            dots2<true>(p0, p0 + (K >> 4), act, K >> 1, nv >> 1, s0, s1);
+            out[r] = s0 + s1;
+        } else {
+            dots2<false>(p0, p0, act, 0, nv, s0, s1);
+            out[r] = s0;
         }
-        float s0 = (a[0] + a[1]) + (a[2] + a[3]);
-        float s1 = (b[0] + b[1]) + (b[2] + b[3]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-        }
-        out[r] = s0;
-        if (two) out[r + 1] = s1;
     }
 }
 
@@ -967,9 +996,8 @@ __global__ void rope_table_kernel(float2 *tab, int n_pos, float theta) {
     tab[i] = make_float2((float)cos((double)angle), (float)sin((double)angle));
 }
 
-}  // namespace
 
-extern "C" int qdb_step_smem_bytes(const QdbDims &d) {
+int step_smem_bytes(const QdbDims &d) {
     const int qd = d.Hq * QDB_HD;
     int act = 0;
     switch (d.Hq / d.Hkv) {
@@ -981,14 +1009,9 @@ extern "C" int qdb_step_smem_bytes(const QdbDims &d) {
     return NSTAGE * STAGE_BYTES + act * (int)sizeof(float);
 }
 
-extern "C" int qdb_step_max_splits(int grid, int kv_heads) {
-    int s = grid / kv_heads;
-    return s < 1 ? 1 : (s > 64 ? 64 : s);
-}
-
 template <int R>
-static cudaError_t launch_r(const QdbStepArgs &a, int grid, cudaStream_t st) {
-    const int smem = qdb_step_smem_bytes(a.d);
+cudaError_t launch_r(const QdbStepArgs &a, int grid, cudaStream_t st) {
+    const int smem = step_smem_bytes(a.d);
     cudaError_t e = cudaFuncSetAttribute(step_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     void *args[] = {const_cast<QdbStepArgs *>(&a)};
@@ -996,7 +1019,7 @@ static cudaError_t launch_r(const QdbStepArgs &a, int grid, cudaStream_t st) {
                                        (size_t)smem, st);
 }
 
-extern "C" cudaError_t qdb_launch_step(const QdbStepArgs &a, int grid, cudaStream_t st) {
+cudaError_t launch_step(const QdbStepArgs &a, int grid, cudaStream_t st) {
     if (a.d.h > POLL * NCT || a.d.I > POLL * NCT || a.d.Hq * QDB_HD > POLL * NCT) return cudaErrorInvalidValue;
     if (a.d.L > MAX_LAYERS) return cudaErrorInvalidValue;
     if ((a.d.h + grid - 1) / grid > OWN_ROWS) return cudaErrorInvalidValue;
@@ -1010,6 +1033,18 @@ extern "C" cudaError_t qdb_launch_step(const QdbStepArgs &a, int grid, cudaStrea
     }
 }
 
+const QdbStepKernel k_entry = {QDB_STEP_NAME, NCW, STAGE_BYTES, POLL * NCT, step_smem_bytes, launch_step};
+
+}  // namespace
+
+extern "C" const QdbStepKernel *QDB_STEP_ENTRY(void) { return &k_entry; }
+
+#if QDB_STEP_COMMON
+extern "C" int qdb_step_max_splits(int grid, int kv_heads) {
+    int s = grid / kv_heads;
+    return s < 1 ? 1 : (s > 64 ? 64 : s);
+}
+
 extern "C" int qdb_step_max_grid(int device) {
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
@@ -1021,3 +1056,4 @@ extern "C" cudaError_t qdb_launch_rope_table(float2 *tab, int n_pos, float theta
     rope_table_kernel<<<(n + 255) / 256, 256, 0, st>>>(tab, n_pos, theta);
     return cudaGetLastError();
 }
+#endif
