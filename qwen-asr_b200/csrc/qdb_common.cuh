@@ -104,6 +104,11 @@ __device__ __forceinline__ uint16_t f32_to_kv(float f) {
 __device__ __forceinline__ float kvlo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu))); }
 __device__ __forceinline__ float kvhi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
 
+// Two f32 rounded to the cache format, packed as kvlo / kvhi read them.
+__device__ __forceinline__ uint32_t kv_pack2(float lo, float hi) {
+    return (uint32_t)f32_to_kv(lo) | ((uint32_t)f32_to_kv(hi) << 16);
+}
+
 // 8 fp16 (one 16-byte vector) times 8 f32, accumulated in order into acc.
 __device__ __forceinline__ float dot8_kv(const uint4 w, const float4 a, const float4 b, float acc) {
     acc = fmaf(kvlo(w.x), a.x, acc);

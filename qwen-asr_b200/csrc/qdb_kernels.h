@@ -58,7 +58,12 @@ struct QdbStepArgs {
 // Trace events of one step per CTA: start, then per layer A entered, A data
 // ready, B entered, C entered, C ready, D entered, D ready, E entered,
 // E ready; then F entered, F ready, end.
-__host__ __device__ static inline int qdb_step_trace_events(int layers) { return 1 + 9 * layers + 3; }
+#ifndef QDB_ATTN_STAMPS
+#define QDB_ATTN_STAMPS 0  // 1: six more stamps per layer inside attention units (debug builds)
+#endif
+__host__ __device__ static inline int qdb_step_trace_events(int layers) {
+    return 1 + 9 * layers + 3 + (QDB_ATTN_STAMPS ? 6 * layers : 0);
+}
 
 // Epochs one decode step consumes (host advances the base by this much).
 __host__ __device__ static inline unsigned qdb_step_epochs(int layers) { return 5u * (unsigned)layers + 1u; }

@@ -501,6 +501,8 @@ struct AttnSmem {
     float m[NCW][R];
     float l[NCW][R];
     float o[NCW][R][QDB_HD];
+    float wq[R][64];                // split-0 merge: weight of each split's partial
+    float invl[R];                  //   and 1 / the merged softmax denominator
 };
 
 // Per-head RMSNorm then NeoX rotation of one 128-float head in smem, one warp
@@ -572,6 +574,14 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
                                        unsigned ep_in, AttnSmem<R> *sm, const Ctl &c) {
     const unsigned ep = ep_in + 1;
     const QdbDims &d = a.d;
+    auto astamp = [&](int k) {
+        if (QDB_ATTN_STAMPS && a.trace && threadIdx.x == 0) {
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            a.trace[(size_t)blockIdx.x * qdb_step_trace_events(d.L) + 1 + 9 * d.L + 3 + 6 * layer + k] = t;
+        }
+    };
+    astamp(0);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int ctx = a.pos + 1;
     const int per = (ctx + S - 1) / S;
@@ -614,6 +624,7 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
     }
     cp_async_wait();
     consumer_sync();
+    astamp(1);
 
     // q heads of this group (and the new K/V row for the owner), one warp each
     for (int h = warp; h < R + (owns_new ? 2 : 0); h += NCW) {
@@ -633,6 +644,7 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
         }
     }
     consumer_sync();  // new K/V row stored (global writes by this CTA are visible to it)
+    astamp(2);
 
     const float scale = 1.0f / sqrtf((float)QDB_HD);
     float m[R], l[R], o[R][4];
@@ -648,17 +660,27 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
             const int j = base + kk;
             const bool valid = j < p1;
             const bool first = (base == base0);
-            if (valid && (!first || j == a.pos)) {
+            if (valid && !first) {
                 const uint4 *kp = reinterpret_cast<const uint4 *>(kc + (size_t)j * QDB_HD + sub * 32);
 #pragma unroll
                 for (int u = 0; u < 4; u++) kv4[u] = __ldcg(kp + u);
+            }
+            if (first && j == a.pos) {  // this step's row: the rounded values stored above, from smem
+                const float *kn = sm->knew + sub * 32;
+#pragma unroll
+                for (int u = 0; u < 4; u++)
+                    kv4[u] = make_uint4(kv_pack2(kn[u * 8 + 0], kn[u * 8 + 1]), kv_pack2(kn[u * 8 + 2], kn[u * 8 + 3]),
+                                        kv_pack2(kn[u * 8 + 4], kn[u * 8 + 5]), kv_pack2(kn[u * 8 + 6], kn[u * 8 + 7]));
             }
 #pragma unroll
             for (int t = 0; t < ATT_KEYS; t++) {
                 const int jt = base + t;
                 if (jt >= p1) vv[t] = make_uint2(0u, 0u);
-                else if (!first || jt == a.pos)
+                else if (!first)
                     vv[t] = __ldcg(reinterpret_cast<const uint2 *>(vc + (size_t)jt * QDB_HD + lane * 4));
+                else if (jt == a.pos)
+                    vv[t] = make_uint2(kv_pack2(sm->vnew[lane * 4], sm->vnew[lane * 4 + 1]),
+                                       kv_pack2(sm->vnew[lane * 4 + 2], sm->vnew[lane * 4 + 3]));
             }
             float sc[R];
 #pragma unroll
@@ -715,6 +737,7 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
         for (int e = 0; e < 4; e++) sm->o[warp][h][lane * 4 + e] = o[h][e];
     }
     consumer_sync();
+    astamp(3);
     // merge the warps; write the unit partial (m, l, o) tagged
     for (int t = threadIdx.x; t < R * QDB_HD; t += NCT) {
         const int h = t / QDB_HD, dd = t % QDB_HD;
@@ -737,44 +760,106 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
         }
         st_tag(dst + 2 + dd, O, ep);
     }
+    astamp(4);
     if (s != 0) return;
-    // split 0 merges all splits of its KV head into attn (running max merge)
-    for (int t = threadIdx.x; t < R * QDB_HD; t += NCT) {
-        const int h = t / QDB_HD, dd = t % QDB_HD;
+    // Split 0 merges all S partials of its KV head into attn. First one warp
+    // per head polls every split's (m, l) at once and turns them into
+    // weights; then each thread merges its output elements with the O words
+    // of MERGE_CHUNK splits in flight per round trip.
+    for (int h = warp; h < R; h += NCW) {
         const u64 *src = a.tpart + (size_t)(g * R + h) * S * (2 + QDB_HD);
-        float M = -INFINITY, L = 0.f, O = 0.f;
-        const long long t0 = clock64();
-        for (int q = 0; q < S; q++) {
-            const u64 *e = src + (size_t)q * (2 + QDB_HD);
-            float mq, lq, oq;
-            for (int iter = 0;; iter++) {
-                const u64 w0 = ld_tag(e), w1 = ld_tag(e + 1), w2 = ld_tag(e + 2 + dd);
-                if (tag_ep(w0) == ep && tag_ep(w1) == ep && tag_ep(w2) == ep) {
-                    mq = tag_val(w0);
-                    lq = tag_val(w1);
-                    oq = tag_val(w2);
-                    break;
-                }
-                if (should_stop(c, iter)) return;
-                if (timed_out(t0)) {
-                    abort_now(c, 13);
-                    return;
-                }
-                if (QDB_POLL_SLEEP_NS) __nanosleep(QDB_POLL_SLEEP_NS);
-            }
-            if (mq == -INFINITY) continue;
-            if (mq > M) {
-                const float f = expf(M - mq);
-                L = L * f + lq;
-                O = O * f + oq;
-                M = mq;
-            } else {
-                const float f = expf(mq - M);
-                L += lq * f;
-                O += oq * f;
+        float mq[2], lq[2];
+        uint32_t pending = 0;
+        u64 w[4];
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            const int q = lane + 32 * k;
+            mq[k] = -INFINITY;
+            lq[k] = 0.f;
+            if (q < S) {
+                pending |= 3u << (2 * k);
+                w[2 * k] = ld_tag(src + (size_t)q * (2 + QDB_HD));
+                w[2 * k + 1] = ld_tag(src + (size_t)q * (2 + QDB_HD) + 1);
             }
         }
-        st_tag(a.tattn + (size_t)(g * R + h) * QDB_HD + dd, L > 0.f ? O / L : 0.f, ep);
+        const long long t0 = clock64();
+        bool ok = true;
+        for (int iter = 0;; iter++) {
+#pragma unroll
+            for (int b = 0; b < 4; b++)
+                if (((pending >> b) & 1u) && tag_ep(w[b]) == ep) pending &= ~(1u << b);
+            const bool stop = should_stop(c, iter);
+            const bool late = !stop && timed_out(t0);
+            if (__all_sync(0xffffffffu, pending == 0)) break;
+            if (__any_sync(0xffffffffu, stop || late)) {
+                if (__any_sync(0xffffffffu, late) && lane == 0) abort_now(c, 13);
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int b = 0; b < 4; b++)
+                if ((pending >> b) & 1u)
+                    w[b] = ld_tag(src + (size_t)(lane + 32 * (b >> 1)) * (2 + QDB_HD) + (b & 1));
+        }
+        if (!ok) continue;
+#pragma unroll
+        for (int k = 0; k < 2; k++)
+            if (lane + 32 * k < S) {
+                mq[k] = tag_val(w[2 * k]);
+                lq[k] = tag_val(w[2 * k + 1]);
+            }
+        float M = fmaxf(mq[0], mq[1]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float f[2], L = 0.f;
+#pragma unroll
+        for (int k = 0; k < 2; k++) {
+            f[k] = (M == -INFINITY || mq[k] == -INFINITY) ? 0.f : expf(mq[k] - M);
+            L += lq[k] * f[k];
+        }
+        L = warp_sum(L);
+#pragma unroll
+        for (int k = 0; k < 2; k++)
+            if (lane + 32 * k < 64) sm->wq[h][lane + 32 * k] = f[k];
+        if (lane == 0) sm->invl[h] = L > 0.f ? 1.0f / L : 0.f;
+    }
+    consumer_sync();
+    astamp(5);
+    if (warp_aborted(c)) return;
+    constexpr int MERGE_CHUNK = 16;
+    for (int t = threadIdx.x; t < R * QDB_HD; t += NCT) {
+        const int h = t / QDB_HD, dd = t % QDB_HD;
+        const u64 *src = a.tpart + (size_t)(g * R + h) * S * (2 + QDB_HD) + 2 + dd;
+        float O = 0.f;
+        for (int q0 = 0; q0 < S; q0 += MERGE_CHUNK) {
+            u64 w[MERGE_CHUNK];
+            uint32_t pending = 0;
+#pragma unroll
+            for (int k = 0; k < MERGE_CHUNK; k++)
+                if (q0 + k < S) {
+                    pending |= 1u << k;
+                    w[k] = ld_tag(src + (size_t)(q0 + k) * (2 + QDB_HD));
+                }
+            const long long t0 = clock64();
+            for (int iter = 0;; iter++) {
+#pragma unroll
+                for (int k = 0; k < MERGE_CHUNK; k++)
+                    if (((pending >> k) & 1u) && tag_ep(w[k]) == ep) pending &= ~(1u << k);
+                if (!pending) break;
+                if (should_stop(c, iter)) return;
+                if (timed_out(t0)) {
+                    abort_now(c, 14);
+                    return;
+                }
+#pragma unroll
+                for (int k = 0; k < MERGE_CHUNK; k++)
+                    if ((pending >> k) & 1u) w[k] = ld_tag(src + (size_t)(q0 + k) * (2 + QDB_HD));
+            }
+#pragma unroll
+            for (int k = 0; k < MERGE_CHUNK; k++)
+                if (q0 + k < S) O = fmaf(sm->wq[h][q0 + k], tag_val(w[k]), O);
+        }
+        st_tag(a.tattn + (size_t)(g * R + h) * QDB_HD + dd, O * sm->invl[h], ep);
     }
 }
 
