@@ -435,12 +435,52 @@ __device__ void rmsnorm_smem(float *x, const float *w, int h, float eps, float *
 // elements: row pairs share the activation loads; an odd last row is split
 // into its two halves (when K is a multiple of 512) instead of being paired
 // with a duplicate of itself.
+#ifndef QDB_FFMA2
+#define QDB_FFMA2 1  // packed f32x2 FMAs (two weights per instruction)
+#endif
+typedef unsigned long long f32x2_t;  // two f32 in one 64-bit register pair
+__device__ __forceinline__ f32x2_t pk2(float lo, float hi) {
+    f32x2_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void fma2(f32x2_t &acc, f32x2_t a, f32x2_t b) {
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ float sum2(f32x2_t v) {
+    float lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+    return lo + hi;
+}
+// bf16 pair (low half = even column) -> f32 pair
+__device__ __forceinline__ f32x2_t bf2(uint32_t w) { return pk2(bf16lo(w), bf16hi(w)); }
+
 // HALVES: the second stream reads act at +x1off (a half row); otherwise both
 // streams share one activation load.
 template <bool HALVES>
 __device__ __forceinline__ void dots2(const uint4 *p0, const uint4 *p1, const float *x0, int x1off, int nv,
                                       float &s0, float &s1) {
     const int lane = threadIdx.x & 31;
+#if QDB_FFMA2
+    // two independent packed chains per stream (each FMA2 = two columns)
+    f32x2_t a[2] = {0ull, 0ull}, b[2] = {0ull, 0ull};
+#pragma unroll 4
+    for (int j = 0; j < nv; j++) {
+        const int e = (j * 32 + lane);
+        const uint4 w0 = p0[e];
+        const uint4 w1 = p1[e];
+        const ulonglong2 xa = *reinterpret_cast<const ulonglong2 *>(x0 + e * 8);
+        const ulonglong2 xb = *reinterpret_cast<const ulonglong2 *>(x0 + e * 8 + 4);
+        const ulonglong2 ya = HALVES ? *reinterpret_cast<const ulonglong2 *>(x0 + x1off + e * 8) : xa;
+        const ulonglong2 yb = HALVES ? *reinterpret_cast<const ulonglong2 *>(x0 + x1off + e * 8 + 4) : xb;
+        fma2(a[0], bf2(w0.x), xa.x); fma2(a[1], bf2(w0.y), xa.y);
+        fma2(a[0], bf2(w0.z), xb.x); fma2(a[1], bf2(w0.w), xb.y);
+        fma2(b[0], bf2(w1.x), ya.x); fma2(b[1], bf2(w1.y), ya.y);
+        fma2(b[0], bf2(w1.z), yb.x); fma2(b[1], bf2(w1.w), yb.y);
+    }
+    s0 = sum2(a[0]) + sum2(a[1]);
+    s1 = sum2(b[0]) + sum2(b[1]);
+#else
     // four independent accumulator chains per stream (the FMA latency of a
     // single chain is what this latency-bound loop would otherwise wait on)
     float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
@@ -464,6 +504,7 @@ __device__ __forceinline__ void dots2(const uint4 *p0, const uint4 *p1, const fl
     }
     s0 = (a[0] + a[1]) + (a[2] + a[3]);
     s1 = (b[0] + b[1]) + (b[2] + b[3]);
+#endif
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         s0 += __shfl_xor_sync(0xffffffffu, s0, o);
@@ -471,7 +512,70 @@ __device__ __forceinline__ void dots2(const uint4 *p0, const uint4 *p1, const fl
     }
 }
 
+#ifndef QDB_DOT_GROUP
+#define QDB_DOT_GROUP 4  // rows per pass over K (activation loads are shared by the group)
+#endif
+// Dot products of NR consecutive rows (stride K) with act, all lanes end
+// with the sums in out[0..NR). One f32x2 chain per row, lanes stride 8.
+template <int NR>
+__device__ __forceinline__ void dots_rows(const uint16_t *w, int K, const float *act, float *out) {
+    const int lane = threadIdx.x & 31;
+    const int nv = K >> 8;
+    f32x2_t acc[NR][2];
+#pragma unroll
+    for (int r = 0; r < NR; r++) acc[r][0] = acc[r][1] = 0ull;
+#pragma unroll 2
+    for (int j = 0; j < nv; j++) {
+        const int e = (j * 32 + lane);
+        const ulonglong2 xa = *reinterpret_cast<const ulonglong2 *>(act + e * 8);
+        const ulonglong2 xb = *reinterpret_cast<const ulonglong2 *>(act + e * 8 + 4);
+#pragma unroll
+        for (int r = 0; r < NR; r++) {
+            const uint4 wv = reinterpret_cast<const uint4 *>(w + (size_t)r * K)[e];
+            fma2(acc[r][0], bf2(wv.x), xa.x);
+            fma2(acc[r][1], bf2(wv.y), xa.y);
+            fma2(acc[r][0], bf2(wv.z), xb.x);
+            fma2(acc[r][1], bf2(wv.w), xb.y);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < NR; r++) {
+        float v = sum2(acc[r][0]) + sum2(acc[r][1]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        out[r] = v;
+    }
+}
+
 __device__ __forceinline__ void stage_dots(const uint16_t *wst, int nr, int K, const float *act, float *out) {
+#if QDB_DOT_GROUP > 2
+    int r = 0;
+    for (; r + QDB_DOT_GROUP <= nr; r += QDB_DOT_GROUP)
+        dots_rows<QDB_DOT_GROUP>(wst + (size_t)r * K, K, act, out + r);
+#if QDB_DOT_GROUP == 8
+    if (r + 4 <= nr) {
+        dots_rows<4>(wst + (size_t)r * K, K, act, out + r);
+        r += 4;
+    }
+#endif
+    if (r + 2 <= nr) {
+        dots_rows<2>(wst + (size_t)r * K, K, act, out + r);
+        r += 2;
+    }
+    if (r < nr) {
+        const uint4 *p0 = reinterpret_cast<const uint4 *>(wst + (size_t)r * K);
+        const int nv = K >> 8;
+        float s0, s1;
+        if ((nv & 1) == 0) {  // an odd last row: its two halves as two streams
+            dots2<true>(p0, p0 + (K >> 4), act, K >> 1, nv >> 1, s0, s1);
+            out[r] = s0 + s1;
+        } else {
+            dots2<false>(p0, p0, act, 0, nv, s0, s1);
+            out[r] = s0;
+        }
+    }
+#else
+
     const int nv = K >> 8;
     for (int r = 0; r < nr; r += 2) {
         const uint4 *p0 = reinterpret_cast<const uint4 *>(wst + (size_t)r * K);
@@ -488,6 +592,7 @@ __device__ __forceinline__ void stage_dots(const uint16_t *wst, int nr, int K, c
             out[r] = s0;
         }
     }
+#endif
 }
 
 // ---------------------------------------------------------------- attention
@@ -863,6 +968,58 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
     }
 }
 
+#ifndef QDB_ITEMS_NOINLINE
+#define QDB_ITEMS_NOINLINE 0
+#endif
+// One phase's ring items for this warp (items it % NCW == warp): row dots,
+// then the phase's epilogue. mode 0: QKV store, 1: O + residual, 2: gate/up
+// SwiGLU, 3: down + residual, 4: lm_head + running argmax. One out-of-line
+// copy serves every phase, which keeps the kernel's code small.
+#if QDB_ITEMS_NOINLINE
+__device__ __noinline__
+#else
+__device__ __forceinline__
+#endif
+void items_phase(const QdbStepArgs &a, const Slice &s, int mode, unsigned ep, u64 &best, unsigned &it,
+                 unsigned char *ring, u64 *full, u64 *empty, const float *act, const float *xown, int own0,
+                 float *outw, const Ctl &c) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = s.items();
+    for (int k = 0; k < n; k++, it++) {
+        if ((int)(it % NCW) != warp) continue;
+        const unsigned st = it % NSTAGE;
+        if (warp_aborted(c) || !mbar_wait_warp(&full[st], (it / NSTAGE) & 1, c, 3)) continue;
+        const int r = s.r0 + k * s.ipr;
+        const int nr = min(s.ipr, s.r1 - r);
+        const uint16_t *wst = reinterpret_cast<const uint16_t *>(ring + (size_t)st * STAGE_BYTES);
+        stage_dots(wst, nr, s.K, act, outw);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        if (mode == 4) {
+            if (lane < nr) {
+                const int row = r + lane;
+                const float v = outw[lane];
+                if (a.logits_out) a.logits_out[row] = v;
+                if (!(a.mask_eos && (row == QDB_ENDOFTEXT || row == QDB_IM_END)) && !isnan(v)) {
+                    const u64 key = argmax_key(v, row);
+                    best = key > best ? key : best;
+                }
+            }
+        } else if (mode == 2) {
+            if (lane < nr / 2) {
+                const int pr = r / 2 + lane;
+                st_tag(a.tact + pr, silu_mul(outw[2 * lane], outw[2 * lane + 1]), ep);
+            }
+        } else if (lane < nr) {
+            const int row = r + lane;
+            const float v = outw[lane];
+            if (mode == 0) st_tag(a.tqkv + row, v, ep);
+            else st_tag(a.tx + row, xown[row - own0] + v, ep);
+        }
+        __syncwarp();
+    }
+}
+
 // ---------------------------------------------------------------- the kernel
 // Dynamic shared memory: ring | act. act holds the phase's input vector
 // (x while it is normalised in place with the norm weights at act[h..2h),
@@ -930,41 +1087,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) 
     mark(0);
     unsigned it = 0;  // ring item counter (same sequence as the producer)
     auto run_items = [&](const Slice &s, int mode, unsigned ep, u64 &best) {
-        // mode 0: QKV store, 1: O + residual, 2: gate/up SwiGLU, 3: down + residual, 4: lm_head
-        const int n = s.items();
-        for (int k = 0; k < n; k++, it++) {
-            if ((int)(it % NCW) != warp) continue;
-            const unsigned st = it % NSTAGE;
-            if (warp_aborted(c) || !mbar_wait_warp(&full[st], (it / NSTAGE) & 1, c, 3)) continue;
-            const int r = s.r0 + k * s.ipr;
-            const int nr = min(s.ipr, s.r1 - r);
-            const uint16_t *wst = reinterpret_cast<const uint16_t *>(ring + (size_t)st * STAGE_BYTES);
-            stage_dots(wst, nr, s.K, act, outs[warp]);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
-            if (mode == 4) {
-                if (lane < nr) {
-                    const int row = r + lane;
-                    const float v = outs[warp][lane];
-                    if (a.logits_out) a.logits_out[row] = v;
-                    if (!(a.mask_eos && (row == QDB_ENDOFTEXT || row == QDB_IM_END)) && !isnan(v)) {
-                        const u64 key = argmax_key(v, row);
-                        best = key > best ? key : best;
-                    }
-                }
-            } else if (mode == 2) {
-                if (lane < nr / 2) {
-                    const int pr = r / 2 + lane;
-                    st_tag(a.tact + pr, silu_mul(outs[warp][2 * lane], outs[warp][2 * lane + 1]), ep);
-                }
-            } else if (lane < nr) {
-                const int row = r + lane;
-                const float v = outs[warp][lane];
-                if (mode == 0) st_tag(a.tqkv + row, v, ep);
-                else st_tag(a.tx + row, xown[row - own0] + v, ep);
-            }
-            __syncwarp();
-        }
+        items_phase(a, s, mode, ep, best, it, ring, full, empty, act, xown, own0, outs[warp], c);
     };
 
     u64 best = 0ull;
