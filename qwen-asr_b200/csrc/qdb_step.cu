@@ -190,6 +190,18 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
         : "memory");
 }
 
+#ifndef QDB_W_EVICT_FIRST
+#define QDB_W_EVICT_FIRST 1  // weights stream through L2 with an evict-first policy
+#endif
+// Same copy with an L2 cache policy (createpolicy) on the global reads.
+__device__ __forceinline__ void bulk_g2s_pol(void *dst, const void *src, unsigned bytes, u64 *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+
 __device__ __forceinline__ void prefetch_l2(const void *src, unsigned bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
@@ -300,6 +312,8 @@ __device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *lay
 #if !QDB_PRODUCER_LSU
     if (lane != 0) return;
 #endif
+    uint64_t pol_w = 0;
+    if (QDB_W_EVICT_FIRST) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_w));
     Cursor ld, pf;
     cursor_init(a, layers, ld);
     cursor_init(a, layers, pf);
@@ -347,7 +361,12 @@ __device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *lay
         }
 #else
         mbar_expect_tx(&full[st], bytes);
-        bulk_g2s(ring + (size_t)st * STAGE_BYTES, src, bytes, &full[st]);
+        if (QDB_W_EVICT_FIRST)
+            // each weight byte is read once per step: keep it from evicting the
+            // KV cache and the small per-layer vectors the latency chain reads
+            bulk_g2s_pol(ring + (size_t)st * STAGE_BYTES, src, bytes, &full[st], pol_w);
+        else
+            bulk_g2s(ring + (size_t)st * STAGE_BYTES, src, bytes, &full[st]);
 #endif
     }
     if (!ok && lane == 0) {
