@@ -202,9 +202,10 @@ __device__ __forceinline__ void bulk_g2s_pol(void *dst, const void *src, unsigne
         : "memory");
 }
 
-__device__ __forceinline__ void prefetch_l2(const void *src, unsigned bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+__device__ __forceinline__ void prefetch_l2_pol(const void *src, unsigned bytes, uint64_t pol) {
+    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(src), "r"(bytes), "l"(pol) : "memory");
 }
+
 
 // Asynchronous 16-byte global -> shared copies (no registers held while the
 // thread goes on polling); completed with cp_async_wait().
@@ -324,7 +325,7 @@ __device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *lay
         for (; L2_AHEAD > 0 && !pf.done && pf_it < it + L2_AHEAD; cursor_next(a, layers, pf), pf_it++)
             if (pf_it >= it && lane == 0) {
                 const int nr = min(pf.s.ipr, pf.s.r1 - pf.r);
-                prefetch_l2(pf.s.w + (size_t)pf.r * pf.s.K, (unsigned)(nr * pf.s.K * 2));
+                prefetch_l2_pol(pf.s.w + (size_t)pf.r * pf.s.K, (unsigned)(nr * pf.s.K * 2), pol_w);
             }
         const int nr = min(ld.s.ipr, ld.s.r1 - ld.r);
         const unsigned st = it % NSTAGE;
