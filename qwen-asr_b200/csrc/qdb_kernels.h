@@ -112,6 +112,9 @@ cudaError_t qdb_launch_qk_rope_append_single(const float *qkv, float *q_out, con
                                              const float *k_norm, const float2 *rope, float eps,
                                              cudaStream_t st);
 // Causal attention of n query rows of ONE session (rows at start_pos + i).
+// Same on the tensor cores (tcgen05); err: device error words (bounded waits).
+cudaError_t qdb_launch_attn_prefill_tc(const float *q, const uint16_t *kc, const uint16_t *vc, int cap, int layer,
+                                       int start_pos, int n, int Hq, int Hkv, float *out, int *err, cudaStream_t st);
 cudaError_t qdb_launch_attn_prefill(const float *q, const uint16_t *kc, const uint16_t *vc, int cap,
                                     int layer, int start_pos, int n, int Hq, int Hkv, float *out,
                                     cudaStream_t st);

@@ -11,6 +11,13 @@
 #include <string.h>
 
 #include <algorithm>
+
+#ifndef QDB_ATTN_TC
+#define QDB_ATTN_TC 1  // prefill attention on tcgen05 (0: the CUDA-core flash kernel)
+#endif
+#ifndef QDB_ATT_ITERS
+#define QDB_ATT_ITERS 1  // key-loop iterations per decode attention unit
+#endif
 #include <string>
 #include <vector>
 
@@ -446,7 +453,7 @@ static QdbStepArgs step_args(qdb_session *s, int pos) {
     // attention splits: one key-loop iteration per unit (8 keys per consumer
     // warp), at most grid / Hkv units per head
     const int ctx = pos + 1;
-    const int keys_per_unit = m->step_k->consumer_warps * 8;
+    const int keys_per_unit = m->step_k->consumer_warps * 8 * QDB_ATT_ITERS;
     int S = (ctx + keys_per_unit - 1) / keys_per_unit;
     if (S > m->max_splits) S = m->max_splits;
     if (S < 1) S = 1;
@@ -653,7 +660,11 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
         if (single) {
             CK(qdb_launch_qk_rope_append_single(r.QKV, r.Q, row0_dev, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
                                                 m->cfg.eps, m->st));
-            CK(qdb_launch_attn_prefill(r.Q, s1->kc, s1->vc, s1->cap, l, start_pos, n, Hq, Hkv, r.ATT, m->st));
+            if (QDB_ATTN_TC)
+                CK(qdb_launch_attn_prefill_tc(r.Q, s1->kc, s1->vc, s1->cap, l, start_pos, n, Hq, Hkv, r.ATT, r.err,
+                                              m->st));
+            else
+                CK(qdb_launch_attn_prefill(r.Q, s1->kc, s1->vc, s1->cap, l, start_pos, n, Hq, Hkv, r.ATT, m->st));
         } else {
             CK(qdb_launch_qk_rope_append(r.QKV, r.Q, row0_dev, pos_off, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
                                          m->cfg.eps, m->st));
