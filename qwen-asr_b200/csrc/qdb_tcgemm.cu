@@ -69,6 +69,19 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
+// Same load with an L2 cache policy on the global reads.
+__device__ __forceinline__ void tma_load_2d_pol(void *dst, const CUtensorMap *map, int x, int y, u64 *bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+        "%3}], [%4], %5;" ::"r"(su32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(su32(bar)), "l"(pol)
+        : "memory");
+}
+
+#ifndef QDB_GEMM_W_EVICT_FIRST
+#define QDB_GEMM_W_EVICT_FIRST 1
+#endif
+
 // Shared-memory matrix descriptor: K-major operand, rows of 128 bytes in
 // 1024-byte 8-row swizzle atoms (128-byte swizzle). start >> 4 in bits 0-13,
 // leading offset 16 B (unused for this layout) in 16-29, stride between
@@ -158,7 +171,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t tmem = tmem_slot;
 
     if (warp == 0 && lane == 0) {
-        // ---- TMA producer
+        // ---- TMA producer. With one activation tile (decode batches) every
+        // weight tile is read exactly once: stream it evict-first so the KV
+        // caches the attention kernels read stay in L2.
+        const bool w_once = QDB_GEMM_W_EVICT_FIRST && gridDim.y == 1;
+        uint64_t pol = 0;
+        if (w_once) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
         int issued = 0;
         for (int kb = 0; kb < nk; kb++) {
             const int s = kb % S;
@@ -166,7 +184,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             unsigned char *st = smem + (size_t)s * STAGE;
             mb_expect(&full[s], STAGE);
             const int kx = (kb0 + kb) * TC_BK;
-            tma_load_2d(st, &tmW, kx, m0, &full[s]);
+            if (w_once) tma_load_2d_pol(st, &tmW, kx, m0, &full[s], pol);
+            else tma_load_2d(st, &tmW, kx, m0, &full[s]);
             tma_load_2d(st + A_BYTES, &tmXh, kx, a0, &full[s]);
             tma_load_2d(st + A_BYTES + B_BYTES, &tmXl, kx, a0, &full[s]);
             issued = kb + 1;

@@ -250,3 +250,28 @@ def test_dropin_reference_api_matches_golden(synth, name, monkeypatch):
         assert_logits_close(lg, g["rewind_logits"][step], f"dropin {name} rewind {step}")
         e = synth.embed_rows(ws, [int(want)])[0]
     d.close()
+
+
+@pytest.mark.parametrize("heads,kv_heads,chunks", [(4, 4, [200, 150]), (8, 1, [130, 1, 97]), (8, 2, [300])])
+def test_prefill_attention_groupings(pkg, synth, heads, kv_heads, chunks):
+    """Prefill attention for every GQA grouping the tensor-core kernel is
+    built for (1, 8 and 4 query heads per KV head here; 2 in the tests
+    above), over several 128-key tiles and query tiles, with prefill calls
+    that start mid-tile, against the oracle."""
+    cfg = synth.Config(256, 2, heads, kv_heads, 128, 512, 600)
+    ws = synth.WeightSet(cfg, seed=9, norm_jitter=0.1)
+    n = sum(chunks)
+    emb = synth.audio_embeddings(cfg, n + 2, seed=13)
+    model = pkg.Model(ws, device=0)
+    s = model.session(n + 8)
+    o = Oracle(ws, max_pos=n + 8)
+    at = 0
+    for c in chunks:
+        s.prefill(emb[at:at + c], at)
+        o.prefill(emb[at:at + c])
+        at += c
+    for i in range(at, at + 2):
+        tok, _, lg = s.forward(emb[i], i, want_logits=True)
+        otok, _, olg = o.forward(emb[i])
+        assert_logits_close(lg, olg, f"R={heads // kv_heads} pos {i}")
+        assert tok == otok or margin_top2(olg) <= MARGIN
