@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(const float *q, const
 // kernel combines the splits (same online-softmax algebra as
 // qwen_causal_attention, qwen_asr_kernels.c:1050-1141).
 #ifndef QDB_AR_MINB
-#define QDB_AR_MINB 3  // resident CTAs per SM the attention kernel is register-capped for
+#define QDB_AR_MINB 2  // resident CTAs per SM the attention kernel is register-capped for
 #endif
 constexpr int AR_WARPS = 8, AR_KEYS = 8;
 
@@ -236,20 +236,31 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AR_MINB) attn_rows_partial_
 #pragma unroll
         for (int e = 0; e < 4; e++) o[h][e] = 0.f;
     }
-    for (int base = p0 + warp * AR_KEYS; base < p1; base += AR_WARPS * AR_KEYS) {
+    // K/V of this warp's next 8-key step are loaded into registers before
+    // the current step's math (double buffering: loads stay in flight)
+    auto load_step = [&](int base, uint4 (&kv4)[4], uint2 (&vv)[AR_KEYS]) {
         const int j = base + kk;
-        const bool valid = j < p1;
-        uint4 kv4[4];
-        if (valid) {
+        if (j < p1) {
             const uint4 *kp = reinterpret_cast<const uint4 *>(kc + (size_t)j * QDB_HD + sub * 32);
 #pragma unroll
-            for (int u = 0; u < 4; u++) kv4[u] = __ldcg(kp + u);
+            for (int u = 0; u < 4; u++) kv4[u] = __ldcs(kp + u);
         }
-        uint2 vv[AR_KEYS];
 #pragma unroll
         for (int t = 0; t < AR_KEYS; t++)
-            vv[t] = base + t < p1 ? __ldcg(reinterpret_cast<const uint2 *>(vc + (size_t)(base + t) * QDB_HD + lane * 4))
+            vv[t] = base + t < p1 ? __ldcs(reinterpret_cast<const uint2 *>(vc + (size_t)(base + t) * QDB_HD + lane * 4))
                                   : make_uint2(0u, 0u);
+    };
+    uint4 kvA[4], kvB[4];
+    uint2 vvA[AR_KEYS], vvB[AR_KEYS];
+    int base = p0 + warp * AR_KEYS;
+    if (base < p1) load_step(base, kvA, vvA);
+    for (; base < p1; base += AR_WARPS * AR_KEYS) {
+        const int nb = base + AR_WARPS * AR_KEYS;
+        if (nb < p1) load_step(nb, kvB, vvB);
+        const uint4 *kv4 = kvA;
+        const uint2 *vv = vvA;
+        const int j = base + kk;
+        const bool valid = j < p1;
 #pragma unroll
         for (int h = 0; h < R; h++) {
             float a0 = 0.f, a1 = 0.f;
@@ -291,6 +302,10 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AR_MINB) attn_rows_partial_
             }
             m[h] = mn;
         }
+#pragma unroll
+        for (int u = 0; u < 4; u++) kvA[u] = kvB[u];
+#pragma unroll
+        for (int t = 0; t < AR_KEYS; t++) vvA[t] = vvB[t];
     }
 #pragma unroll
     for (int h = 0; h < R; h++) {

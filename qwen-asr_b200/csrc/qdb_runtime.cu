@@ -15,6 +15,9 @@
 #ifndef QDB_ATTN_TC
 #define QDB_ATTN_TC 1  // prefill attention on tcgen05 (0: the CUDA-core flash kernel)
 #endif
+#ifndef QDB_AR_ITERS
+#define QDB_AR_ITERS 8  // 8-key steps per warp of a batched-decode attention unit
+#endif
 #ifndef QDB_ATT_ITERS
 #define QDB_ATT_ITERS 1  // key-loop iterations per decode attention unit
 #endif
@@ -627,8 +630,9 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
     const int qkvd = m->qd + 2 * m->kvd;
     int S = 1;
     if (!single) {
-        // one attention unit per 64 keys of the longest row (one step per warp)
-        S = (max_ctx + 63) / 64;
+        // one attention unit per QDB_AR_ITERS x 64 keys of the longest row
+        // (8-key steps per warp, double-buffered)
+        S = (max_ctx + 64 * QDB_AR_ITERS - 1) / (64 * QDB_AR_ITERS);
         if (S > 64) S = 64;
         if (S < 1) S = 1;
         const size_t need = (size_t)n * Hq * S * (2 + QDB_HD);
