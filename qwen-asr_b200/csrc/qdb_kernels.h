@@ -99,8 +99,9 @@ struct QdbRowKV {
 };
 
 // RMSNorm rows written as the bf16 hi/lo split consumed by the tensor-core GEMM.
+// zero (optional): [n, zero_len] f32 target of the next split-K GEMM, cleared row by row.
 cudaError_t qdb_launch_rmsnorm_rows(const float *x, const float *w, uint16_t *hi, uint16_t *lo, int n, int h,
-                                    float eps, cudaStream_t st);
+                                    float eps, cudaStream_t st, float *zero = nullptr, int zero_len = 0);
 // Per-row targets: row b writes position rows[b].pos + row_pos_offset.
 cudaError_t qdb_launch_qk_rope_append(const float *qkv, float *q_out, const QdbRowKV *rows,
                                       int row_pos_offset, int layer, int n, int Hq, int Hkv,

@@ -11,27 +11,56 @@ namespace {
 // Per row: y = x * (1/sqrtf(mean(x^2)+eps)) * w (qwen_rms_norm,
 // qwen_asr_kernels.c:750-809), written as the bf16 hi/lo split the
 // tensor-core GEMM consumes (hi + lo ~= y to ~16 mantissa bits).
-__global__ void rmsnorm_rows_kernel(const float *x, const float *w, uint16_t *hi, uint16_t *lo, int h, float eps) {
-    __shared__ float red[32];
-    const float *xr = x + (size_t)blockIdx.x * h;
+// The row is read once into registers (up to RN_VEC float4 per thread).
+// zero/zero_len: optionally clears this row of the next split-K GEMM's
+// target (zero_len floats per row), which saves a memset launch.
+constexpr int RN_THREADS = 256, RN_VEC = 8;  // h <= 8192
+__global__ void __launch_bounds__(RN_THREADS) rmsnorm_rows_kernel(const float *x, const float *w, uint16_t *hi,
+                                                                 uint16_t *lo, int h, float eps, float *zero,
+                                                                 int zero_len) {
+    __shared__ float red[RN_THREADS / 32];
+    const int t = threadIdx.x;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)blockIdx.x * h);
+    const int h4 = h >> 2;
+    float4 v[RN_VEC];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < h; i += blockDim.x) ss += xr[i] * xr[i];
-    ss = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-        t = warp_sum(t);
-        if (threadIdx.x == 0) red[0] = t;
+#pragma unroll
+    for (int k = 0; k < RN_VEC; k++) {
+        const int i = t + k * RN_THREADS;
+        if (i < h4) {
+            v[k] = xr[i];
+            ss += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z + v[k].w * v[k].w;
+        }
     }
+    if (zero) {
+        float4 *zr = reinterpret_cast<float4 *>(zero + (size_t)blockIdx.x * zero_len);
+        for (int i = t; i < (zero_len >> 2); i += RN_THREADS) zr[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    ss = warp_sum(ss);
+    if ((t & 31) == 0) red[t >> 5] = ss;
     __syncthreads();
-    const float inv = 1.0f / sqrtf(red[0] / (float)h + eps);
-    uint16_t *hr = hi + (size_t)blockIdx.x * h, *lr = lo + (size_t)blockIdx.x * h;
-    for (int i = threadIdx.x; i < h; i += blockDim.x) {
-        const float y = xr[i] * inv * w[i];
-        const uint16_t b = f32_to_bf16_rn(y);
-        hr[i] = b;
-        lr[i] = f32_to_bf16_rn(y - __uint_as_float((uint32_t)b << 16));
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < RN_THREADS / 32; k++) tot += red[k];
+    const float inv = 1.0f / sqrtf(tot / (float)h + eps);
+    uint2 *hr = reinterpret_cast<uint2 *>(hi + (size_t)blockIdx.x * h);
+    uint2 *lr = reinterpret_cast<uint2 *>(lo + (size_t)blockIdx.x * h);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w);
+#pragma unroll
+    for (int k = 0; k < RN_VEC; k++) {
+        const int i = t + k * RN_THREADS;
+        if (i < h4) {
+            const float4 ww = w4[i];
+            const float y[4] = {v[k].x * inv * ww.x, v[k].y * inv * ww.y, v[k].z * inv * ww.z, v[k].w * inv * ww.w};
+            uint16_t b[4], c[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                b[e] = f32_to_bf16_rn(y[e]);
+                c[e] = f32_to_bf16_rn(y[e] - __uint_as_float((uint32_t)b[e] << 16));
+            }
+            hr[i] = make_uint2((uint32_t)b[0] | ((uint32_t)b[1] << 16), (uint32_t)b[2] | ((uint32_t)b[3] << 16));
+            lr[i] = make_uint2((uint32_t)c[0] | ((uint32_t)c[1] << 16), (uint32_t)c[2] | ((uint32_t)c[3] << 16));
+        }
     }
 }
 
@@ -397,9 +426,10 @@ __global__ void embed_rows_kernel(const uint16_t *embed, const int *tokens, floa
 }  // namespace
 
 extern "C" cudaError_t qdb_launch_rmsnorm_rows(const float *x, const float *w, uint16_t *hi, uint16_t *lo, int n, int h,
-                                               float eps, cudaStream_t st) {
+                                               float eps, cudaStream_t st, float *zero, int zero_len) {
     if (n <= 0) return cudaSuccess;
-    rmsnorm_rows_kernel<<<n, 256, 0, st>>>(x, w, hi, lo, h, eps);
+    if (h % 4 || h > 4 * RN_VEC * RN_THREADS || (zero && zero_len % 4)) return cudaErrorInvalidValue;
+    rmsnorm_rows_kernel<<<n, RN_THREADS, 0, st>>>(x, w, hi, lo, h, eps, zero, zero_len);
     return cudaGetLastError();
 }
 

@@ -647,10 +647,12 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
     // Y (op)= X W^T from the bf16 split in XH/XL. Skinny problems (decode
     // batches of <= 64 rows) use split-K with atomic accumulation: mode 0
     // targets are zeroed first, mode 1 targets already hold the residual.
-    auto gemm = [&](const uint16_t *W, float *Y, int N, int K, int mode) -> int {
-        const int sp = n <= 64 ? qdb_gemm_tc_splits(n, N, K, m->sms) : 1;
+    // (the norm before a mode-0 split GEMM clears its target: zeroed = true)
+    auto splits_of = [&](int N, int K) { return n <= 64 ? qdb_gemm_tc_splits(n, N, K, m->sms) : 1; };
+    auto gemm = [&](const uint16_t *W, float *Y, int N, int K, int mode, bool zeroed = false) -> int {
+        const int sp = splits_of(N, K);
         if (sp > 1) {
-            if (mode == 0) CK(cudaMemsetAsync(Y, 0, sizeof(float) * (size_t)n * N, m->st));
+            if (mode == 0 && !zeroed) CK(cudaMemsetAsync(Y, 0, sizeof(float) * (size_t)n * N, m->st));
             CK(qdb_launch_gemm_tc(W, r.XH, r.XL, Y, n, N, K, 3, sp, r.err, m->st));
         } else {
             CK(qdb_launch_gemm_tc(W, r.XH, r.XL, Y, n, N, K, mode, 1, r.err, m->st));
@@ -659,8 +661,10 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
     };
     for (int l = 0; l < m->cfg.layers; l++) {
         const QdbLayerW &lw = m->layers_host[l];
-        CK(qdb_launch_rmsnorm_rows(r.X, lw.in_norm, r.XH, r.XL, n, h, m->cfg.eps, m->st));
-        if (gemm(lw.qkv, r.QKV, qkvd, h, 0)) return -1;
+        const bool qkv_split = splits_of(qkvd, h) > 1;
+        CK(qdb_launch_rmsnorm_rows(r.X, lw.in_norm, r.XH, r.XL, n, h, m->cfg.eps, m->st, qkv_split ? r.QKV : nullptr,
+                                   qkvd));
+        if (gemm(lw.qkv, r.QKV, qkvd, h, 0, qkv_split)) return -1;
         if (single) {
             CK(qdb_launch_qk_rope_append_single(r.QKV, r.Q, row0_dev, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
                                                 m->cfg.eps, m->st));
@@ -676,10 +680,12 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
         }
         CK(qdb_launch_split_bf16(r.ATT, r.XH, r.XL, (size_t)n * m->qd, m->st));
         if (gemm(lw.o, r.X, h, m->qd, 1)) return -1;
-        CK(qdb_launch_rmsnorm_rows(r.X, lw.post_norm, r.XH, r.XL, n, h, m->cfg.eps, m->st));
-        if (n <= 64 && qdb_gemm_tc_splits(n, 2 * I, h, m->sms) > 1) {
+        const bool gu_split = splits_of(2 * I, h) > 1;
+        CK(qdb_launch_rmsnorm_rows(r.X, lw.post_norm, r.XH, r.XL, n, h, m->cfg.eps, m->st, gu_split ? r.GU : nullptr,
+                                   2 * I));
+        if (gu_split) {
             // split-K: gate/up sums into GU, then SwiGLU straight into the bf16 split
-            if (gemm(lw.gu, r.GU, 2 * I, h, 0)) return -1;
+            if (gemm(lw.gu, r.GU, 2 * I, h, 0, true)) return -1;
             CK(qdb_launch_swiglu_split(r.GU, r.XH, r.XL, (size_t)n * I, m->st));
         } else {
             CK(qdb_launch_gemm_tc(lw.gu, r.XH, r.XL, r.ACT, n, 2 * I, h, 2, 1, r.err, m->st));
