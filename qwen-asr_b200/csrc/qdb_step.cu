@@ -386,6 +386,9 @@ __device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *lay
 // ---------------------------------------------------------------- consumer helpers
 // Fills dst[0..n) from tagged words src expecting epoch ep (n <= POLL*NCT).
 // All still-missing words are re-read together each round.
+#ifndef QDB_POLL_WAVES
+#define QDB_POLL_WAVES 1  // poll rounds in flight per word (2: the next round is issued before this one is checked)
+#endif
 __device__ __noinline__ bool load_tagged(const u64 *src, int n, unsigned ep, float *dst, const Ctl &c, int site) {
     const int t = threadIdx.x;
     uint32_t pending = 0;
@@ -399,6 +402,37 @@ __device__ __noinline__ bool load_tagged(const u64 *src, int n, unsigned ep, flo
         }
     }
     const long long t0 = clock64();
+#if QDB_POLL_WAVES == 2
+    // Two rounds in flight: round k+1 is issued for the words still pending
+    // before round k is checked, so a word is seen about one L2 round trip
+    // after it lands instead of one and a half.
+    u64 w2[POLL];
+    auto check = [&](const u64 (&b)[POLL]) {
+#pragma unroll
+        for (int j = 0; j < POLL; j++)
+            if (((pending >> j) & 1u) && tag_ep(b[j]) == ep) {
+                dst[t + j * NCT] = tag_val(b[j]);
+                pending &= ~(1u << j);
+            }
+    };
+    for (int iter = 0;; iter += 2) {
+#pragma unroll
+        for (int j = 0; j < POLL; j++)
+            if ((pending >> j) & 1u) w2[j] = ld_tag(src + t + j * NCT);
+        check(w);
+        if (!pending) return true;
+#pragma unroll
+        for (int j = 0; j < POLL; j++)
+            if ((pending >> j) & 1u) w[j] = ld_tag(src + t + j * NCT);
+        check(w2);
+        if (!pending) return true;
+        if (should_stop(c, iter | 1)) return false;
+        if (timed_out(t0)) {
+            abort_now(c, site);
+            return false;
+        }
+    }
+#else
     for (int iter = 0;; iter++) {
 #pragma unroll
         for (int j = 0; j < POLL; j++)
@@ -419,6 +453,7 @@ __device__ __noinline__ bool load_tagged(const u64 *src, int n, unsigned ep, flo
         for (int j = 0; j < POLL; j++)
             if ((pending >> j) & 1u) w[j] = ld_tag(src + t + j * NCT);
     }
+#endif
 }
 
 // Consumer-wide sum; red has NCW floats.
