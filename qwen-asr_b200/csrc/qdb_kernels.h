@@ -122,7 +122,7 @@ cudaError_t qdb_launch_attn_prefill(const float *q, const uint16_t *kc, const ui
 // Independent rows (one query each) over per-row caches.
 cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
                                  int n, int Hq, int Hkv, int splits, float *part, float *out,
-                                 cudaStream_t st);
+                                 cudaStream_t st, int *err = nullptr);
 // Tensor-core GEMM (qdb_tcgemm.cu): Y (op)= X W^T with X given as bf16 hi/lo.
 cudaError_t qdb_launch_split_bf16(const float *x, uint16_t *hi, uint16_t *lo, size_t count, cudaStream_t st);
 cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,

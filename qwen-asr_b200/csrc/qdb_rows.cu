@@ -369,6 +369,184 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AR_MINB) attn_rows_partial_
     }
 }
 
+// Same unit computed from a shared-memory ring: the unit's K and V rows are
+// contiguous in the cache, so thread 0 streams them in 64-key chunks with
+// cp.async.bulk (3 stages x 32 KB, 2 CTAs per SM: ~190 KB in flight per SM)
+// and the 8 warps take 8 keys each per chunk. K chunks are read with the
+// 16-byte piece order rotated per lane, which keeps the quarter-warp
+// LDS.128 phases free of bank conflicts.
+constexpr int AB_STAGES = 3, AB_KEYS = 64, AB_HALF = AB_KEYS * QDB_HD * 2, AB_STAGE = 2 * AB_HALF;
+typedef unsigned long long u64r;
+__device__ __forceinline__ uint32_t su32r(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+template <int R>
+__global__ void __launch_bounds__(AR_WARPS * 32, 2) attn_rows_bulk_kernel(const float *q, const QdbRowKV *rows,
+                                                                         int row_pos_offset, int layer, int Hq,
+                                                                         int Hkv, int S, float *part, int *err) {
+    extern __shared__ __align__(128) unsigned char ring[];
+    __shared__ __align__(16) float qs[R][QDB_HD];
+    __shared__ float sm_m[AR_WARPS][R], sm_l[AR_WARPS][R];
+    __shared__ __align__(16) float sm_o[AR_WARPS][R][QDB_HD];
+    __shared__ __align__(8) u64r full[AB_STAGES];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int row = blockIdx.x / Hkv, g = blockIdx.x % Hkv, s = blockIdx.y;
+    const QdbRowKV rk = rows[row];
+    const int pos = rk.pos + row_pos_offset;
+    const int ctx = pos + 1;
+    const int per = (ctx + S - 1) / S;
+    const int p0 = s * per, p1 = min(ctx, p0 + per);
+    const int nch = p1 > p0 ? (p1 - p0 + AB_KEYS - 1) / AB_KEYS : 0;
+    const size_t head_base = ((size_t)layer * Hkv + g) * (size_t)rk.cap * QDB_HD;
+    const uint16_t *kc = rk.kc + head_base, *vc = rk.vc + head_base;
+    auto issue = [&](int c) {
+        const int k0 = p0 + c * AB_KEYS;
+        const unsigned bytes = (unsigned)(min(AB_KEYS, p1 - k0) * QDB_HD * 2);
+        unsigned char *st = ring + (size_t)(c % AB_STAGES) * AB_STAGE;
+        u64r *bar = &full[c % AB_STAGES];
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32r(bar)), "r"(2 * bytes)
+                     : "memory");
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(su32r(st)),
+            "l"(kc + (size_t)k0 * QDB_HD), "r"(bytes), "r"(su32r(bar))
+            : "memory");
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                su32r(st + AB_HALF)),
+            "l"(vc + (size_t)k0 * QDB_HD), "r"(bytes), "r"(su32r(bar))
+            : "memory");
+    };
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < AB_STAGES; i++)
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32r(&full[i])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int c = 0; c < nch && c < AB_STAGES; c++) issue(c);
+    }
+    for (int t = threadIdx.x; t < R * QDB_HD; t += blockDim.x)
+        qs[t / QDB_HD][t % QDB_HD] = q[(size_t)row * Hq * QDB_HD + (size_t)(g * R) * QDB_HD + t];
+    __syncthreads();
+    const float scale = 1.0f / sqrtf((float)QDB_HD);
+    const int sub = lane & 3, kk = lane >> 2;
+    float m[R], l[R], o[R][4];
+#pragma unroll
+    for (int h = 0; h < R; h++) {
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; e++) o[h][e] = 0.f;
+    }
+    for (int c = 0; c < nch; c++) {
+        const unsigned char *st = ring + (size_t)(c % AB_STAGES) * AB_STAGE;
+        {  // bounded wait for this chunk (every thread observes the phase)
+            const unsigned par = (unsigned)(c / AB_STAGES) & 1u;
+            const long long t0 = clock64();
+            for (;;) {
+                uint32_t ok;
+                asm volatile(
+                    "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                    : "=r"(ok)
+                    : "r"(su32r(&full[c % AB_STAGES])), "r"(par)
+                    : "memory");
+                if (ok) break;
+                if (clock64() - t0 > QDB_SPIN_LIMIT_CYCLES) {
+                    set_error(err, QDB_ERR_BARRIER_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        const int base = p0 + c * AB_KEYS + warp * AR_KEYS;  // this warp's 8 keys
+        const int j = base + kk;
+        const bool valid = j < p1;
+        uint4 kv4[4];
+        const int rot = (sub + kk) & 3;
+        if (valid) {
+            const uint4 *kp = reinterpret_cast<const uint4 *>(st + (size_t)(warp * AR_KEYS + kk) * QDB_HD * 2) + sub * 4;
+#pragma unroll
+            for (int u = 0; u < 4; u++) kv4[u] = kp[(u + rot) & 3];
+        }
+        uint2 vv[AR_KEYS];
+#pragma unroll
+        for (int t = 0; t < AR_KEYS; t++)
+            vv[t] = base + t < p1
+                        ? *reinterpret_cast<const uint2 *>(st + AB_HALF + (size_t)(warp * AR_KEYS + t) * QDB_HD * 2 + lane * 8)
+                        : make_uint2(0u, 0u);
+#pragma unroll
+        for (int h = 0; h < R; h++) {
+            float a0 = 0.f, a1 = 0.f;
+            if (valid) {
+                const float *qv = qs[h] + sub * 32;
+#pragma unroll
+                for (int u = 0; u < 4; u += 2) {
+                    const int ua = (u + rot) & 3, ub = (u + 1 + rot) & 3;
+                    a0 = dot8_kv(kv4[u], *reinterpret_cast<const float4 *>(qv + ua * 8),
+                                 *reinterpret_cast<const float4 *>(qv + ua * 8 + 4), a0);
+                    a1 = dot8_kv(kv4[u + 1], *reinterpret_cast<const float4 *>(qv + ub * 8),
+                                 *reinterpret_cast<const float4 *>(qv + ub * 8 + 4), a1);
+                }
+            }
+            float acc = a0 + a1;
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+            const float sc = valid ? acc * scale : -INFINITY;
+            float cm = sc;
+            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
+            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
+            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
+            const float mn = fmaxf(m[h], cm);
+            const float corr = (mn == -INFINITY) ? 1.f : expf(m[h] - mn);
+            const float p = valid ? expf(sc - mn) : 0.f;
+            float ps = p;
+            ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+            ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+            l[h] = l[h] * corr + ps;
+#pragma unroll
+            for (int e = 0; e < 4; e++) o[h][e] *= corr;
+#pragma unroll
+            for (int t = 0; t < AR_KEYS; t++) {
+                const float pt = __shfl_sync(0xffffffffu, p, t * 4);
+                o[h][0] = fmaf(pt, kvlo(vv[t].x), o[h][0]);
+                o[h][1] = fmaf(pt, kvhi(vv[t].x), o[h][1]);
+                o[h][2] = fmaf(pt, kvlo(vv[t].y), o[h][2]);
+                o[h][3] = fmaf(pt, kvhi(vv[t].y), o[h][3]);
+            }
+            m[h] = mn;
+        }
+        __syncthreads();  // every warp is done with this stage
+        if (threadIdx.x == 0 && c + AB_STAGES < nch) issue(c + AB_STAGES);
+    }
+#pragma unroll
+    for (int h = 0; h < R; h++) {
+        if (lane == 0) {
+            sm_m[warp][h] = m[h];
+            sm_l[warp][h] = l[h];
+        }
+#pragma unroll
+        for (int e = 0; e < 4; e++) sm_o[warp][h][lane * 4 + e] = o[h][e];
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < R * QDB_HD; t += blockDim.x) {
+        const int h = t / QDB_HD, dd = t % QDB_HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < AR_WARPS; w++) M = fmaxf(M, sm_m[w][h]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < AR_WARPS; w++) {
+                const float f = expf(sm_m[w][h] - M);
+                L += sm_l[w][h] * f;
+                O += sm_o[w][h][dd] * f;
+            }
+        }
+        float *dst = part + (((size_t)row * Hq + g * R + h) * S + s) * (2 + QDB_HD);
+        if (dd == 0) {
+            dst[0] = M;
+            dst[1] = L;
+        }
+        dst[2 + dd] = O;
+    }
+}
+
 __global__ void attn_rows_merge_kernel(const float *part, int S, int Hq, float *out) {
     const int row = blockIdx.x, h = blockIdx.y, dd = threadIdx.x;
     const float *src = part + ((size_t)row * Hq + h) * S * (2 + QDB_HD);
@@ -484,18 +662,38 @@ extern "C" cudaError_t qdb_launch_attn_prefill(const float *q, const uint16_t *k
     }
 }
 
+#ifndef QDB_AR_BULK
+#define QDB_AR_BULK 1  // batched-decode attention from the bulk-copy ring (0: register-loading kernel)
+#endif
+template <int R>
+static cudaError_t attn_rows_launch(dim3 grid, const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
+                                    int Hq, int Hkv, int S, float *part, int *err, cudaStream_t st) {
+    if (QDB_AR_BULK) {
+        const int smem = AB_STAGES * AB_STAGE;
+        cudaError_t e = cudaFuncSetAttribute(attn_rows_bulk_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        attn_rows_bulk_kernel<R><<<grid, AR_WARPS * 32, smem, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part,
+                                                                    err);
+    } else {
+        attn_rows_partial_kernel<R><<<grid, AR_WARPS * 32, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part);
+    }
+    return cudaGetLastError();
+}
+
 extern "C" cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
                                             int n, int Hq, int Hkv, int S, float *part, float *out,
-                                            cudaStream_t st) {
+                                            cudaStream_t st, int *err) {
     if (n <= 0) return cudaSuccess;
     dim3 grid(n * Hkv, S);
+    cudaError_t e0;
     switch (Hq / Hkv) {
-        case 1: attn_rows_partial_kernel<1><<<grid, AR_WARPS * 32, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part); break;
-        case 2: attn_rows_partial_kernel<2><<<grid, AR_WARPS * 32, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part); break;
-        case 4: attn_rows_partial_kernel<4><<<grid, AR_WARPS * 32, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part); break;
-        case 8: attn_rows_partial_kernel<8><<<grid, AR_WARPS * 32, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part); break;
+        case 1: e0 = attn_rows_launch<1>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st); break;
+        case 2: e0 = attn_rows_launch<2>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st); break;
+        case 4: e0 = attn_rows_launch<4>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st); break;
+        case 8: e0 = attn_rows_launch<8>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st); break;
         default: return cudaErrorInvalidValue;
     }
+    if (e0 != cudaSuccess) return e0;
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     attn_rows_merge_kernel<<<dim3(n, Hq), QDB_HD, 0, st>>>(part, S, Hq, out);

@@ -681,7 +681,7 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
         } else {
             CK(qdb_launch_qk_rope_append(r.QKV, r.Q, row0_dev, pos_off, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
                                          m->cfg.eps, m->st));
-            CK(qdb_launch_attn_rows(r.Q, row0_dev, pos_off, l, n, Hq, Hkv, S, r.part, r.ATT, m->st));
+            CK(qdb_launch_attn_rows(r.Q, row0_dev, pos_off, l, n, Hq, Hkv, S, r.part, r.ATT, m->st, r.err));
         }
         CK(qdb_launch_split_bf16(r.ATT, r.XH, r.XL, (size_t)n * m->qd, m->st));
         if (gemm(lw.o, r.X, h, m->qd, 1)) return -1;
