@@ -106,7 +106,7 @@ cudaError_t qdb_launch_rmsnorm_rows(const float *x, const float *w, uint16_t *hi
 cudaError_t qdb_launch_qk_rope_append(const float *qkv, float *q_out, const QdbRowKV *rows,
                                       int row_pos_offset, int layer, int n, int Hq, int Hkv,
                                       const float *q_norm, const float *k_norm, const float2 *rope,
-                                      float eps, cudaStream_t st);
+                                      float eps, cudaStream_t st, const int *step = nullptr);
 // One session: row i writes position row0->pos + i.
 cudaError_t qdb_launch_qk_rope_append_single(const float *qkv, float *q_out, const QdbRowKV *row0,
                                              int layer, int n, int Hq, int Hkv, const float *q_norm,
@@ -122,15 +122,19 @@ cudaError_t qdb_launch_attn_prefill(const float *q, const uint16_t *kc, const ui
 // Independent rows (one query each) over per-row caches.
 cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
                                  int n, int Hq, int Hkv, int splits, float *part, float *out,
-                                 cudaStream_t st, int *err = nullptr);
+                                 cudaStream_t st, int *err = nullptr, const int *step = nullptr);
 // Tensor-core GEMM (qdb_tcgemm.cu): Y (op)= X W^T with X given as bf16 hi/lo.
 cudaError_t qdb_launch_split_bf16(const float *x, uint16_t *hi, uint16_t *lo, size_t count, cudaStream_t st);
 cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,
                                int mode, int splits, int *err, cudaStream_t st);
 cudaError_t qdb_launch_swiglu_split(const float *gu, uint16_t *hi, uint16_t *lo, size_t count, cudaStream_t st);
 int qdb_gemm_tc_splits(int n, int N, int K, int sms);
+// step (optional, device): the rows' tokens are read at tokens + *step * n
+// (embed) / written at tokens + *step * n (argmax), and positions advance by
+// *step (qk_rope_append, attn_rows): the form a captured decode step replays.
 cudaError_t qdb_launch_argmax_rows(const float *logits, int n, int V, int mask_eos, int *tokens,
-                                   cudaStream_t st);
+                                   cudaStream_t st, const int *step = nullptr);
 cudaError_t qdb_launch_embed_rows(const uint16_t *embed, const int *tokens, float *x, int n, int h, int V,
-                                  cudaStream_t st);
+                                  cudaStream_t st, const int *step = nullptr);
+cudaError_t qdb_launch_step_advance(int *step, cudaStream_t st);
 }

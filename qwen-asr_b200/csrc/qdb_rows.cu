@@ -69,14 +69,15 @@ __global__ void __launch_bounds__(RN_THREADS) rmsnorm_rows_kernel(const float *x
 // [Hq, Hq+Hkv) key heads -> cache K, [Hq+Hkv, Hq+2Hkv) value heads -> cache V.
 __global__ void qk_rope_append_kernel(const float *qkv, float *q_out, const QdbRowKV *rows, int n_rowkv,
                                       int row_pos_offset, int layer, int n, int Hq, int Hkv,
-                                      const float *q_norm, const float *k_norm, const float2 *rope, float eps) {
+                                      const float *q_norm, const float *k_norm, const float2 *rope, float eps,
+                                      const int *step) {
     const int lane = threadIdx.x & 31;
     const int slot = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int row = blockIdx.x;
     if (slot >= Hq + 2 * Hkv || row >= n) return;
     const bool single = (n_rowkv == 1);
     const QdbRowKV rk = rows[single ? 0 : row];
-    const int pos = rk.pos + (single ? row : 0) + row_pos_offset;
+    const int pos = rk.pos + (single ? row : 0) + row_pos_offset + (step ? *step : 0);
     const int width = (Hq + 2 * Hkv) * QDB_HD;
     const float *src = qkv + (size_t)row * width + (size_t)slot * QDB_HD;
     float e[4];
@@ -239,14 +240,15 @@ constexpr int AR_WARPS = 8, AR_KEYS = 8;
 template <int R>
 __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AR_MINB) attn_rows_partial_kernel(const float *q, const QdbRowKV *rows,
                                                                           int row_pos_offset, int layer, int Hq,
-                                                                          int Hkv, int S, float *part) {
+                                                                          int Hkv, int S, float *part,
+                                                                          const int *step) {
     __shared__ __align__(16) float qs[R][QDB_HD];
     __shared__ float sm_m[AR_WARPS][R], sm_l[AR_WARPS][R];
     __shared__ __align__(16) float sm_o[AR_WARPS][R][QDB_HD];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int row = blockIdx.x / Hkv, g = blockIdx.x % Hkv, s = blockIdx.y;
     const QdbRowKV rk = rows[row];
-    const int pos = rk.pos + row_pos_offset;
+    const int pos = rk.pos + row_pos_offset + (step ? *step : 0);
     const int ctx = pos + 1;
     const int per = (ctx + S - 1) / S;
     const int p0 = s * per, p1 = min(ctx, p0 + per);
@@ -382,7 +384,8 @@ __device__ __forceinline__ uint32_t su32r(const void *p) { return (uint32_t)__cv
 template <int R>
 __global__ void __launch_bounds__(AR_WARPS * 32, 2) attn_rows_bulk_kernel(const float *q, const QdbRowKV *rows,
                                                                          int row_pos_offset, int layer, int Hq,
-                                                                         int Hkv, int S, float *part, int *err) {
+                                                                         int Hkv, int S, float *part, int *err,
+                                                                         const int *step) {
     extern __shared__ __align__(128) unsigned char ring[];
     __shared__ __align__(16) float qs[R][QDB_HD];
     __shared__ float sm_m[AR_WARPS][R], sm_l[AR_WARPS][R];
@@ -391,7 +394,7 @@ __global__ void __launch_bounds__(AR_WARPS * 32, 2) attn_rows_bulk_kernel(const 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int row = blockIdx.x / Hkv, g = blockIdx.x % Hkv, s = blockIdx.y;
     const QdbRowKV rk = rows[row];
-    const int pos = rk.pos + row_pos_offset;
+    const int pos = rk.pos + row_pos_offset + (step ? *step : 0);
     const int ctx = pos + 1;
     const int per = (ctx + S - 1) / S;
     const int p0 = s * per, p1 = min(ctx, p0 + per);
@@ -564,7 +567,7 @@ __global__ void attn_rows_merge_kernel(const float *part, int S, int Hq, float *
 }
 
 // ---------------------------------------------------------------- argmax / embed
-__global__ void argmax_rows_kernel(const float *logits, int V, int mask_eos, int *tokens) {
+__global__ void argmax_rows_kernel(const float *logits, int V, int mask_eos, int *tokens, const int *step) {
     __shared__ unsigned long long red[32];
     const float *lr = logits + (size_t)blockIdx.x * V;
     unsigned long long best = 0ull;
@@ -589,19 +592,27 @@ __global__ void argmax_rows_kernel(const float *logits, int V, int mask_eos, int
             const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
             best = t > best ? t : best;
         }
-        if (threadIdx.x == 0) tokens[blockIdx.x] = best ? argmax_key_index(best) : 0;
+        if (threadIdx.x == 0) tokens[(step ? (size_t)*step * gridDim.x : 0) + blockIdx.x] = best ? argmax_key_index(best) : 0;
     }
 }
 
-__global__ void embed_rows_kernel(const uint16_t *embed, const int *tokens, float *x, int h, int V) {
+__global__ void embed_rows_kernel(const uint16_t *embed, const int *tokens, float *x, int h, int V, const int *step) {
     const int row = blockIdx.x;
-    int tok = tokens[row];
+    int tok = tokens[(step ? (size_t)*step * gridDim.x : 0) + row];
     if (tok < 0 || tok >= V) tok = 0;  // never gather outside the table
     const uint16_t *src = embed + (size_t)tok * h;
     for (int i = threadIdx.x; i < h; i += blockDim.x) x[(size_t)row * h + i] = __uint_as_float(((uint32_t)src[i]) << 16);
 }
 
+// One thread: the device-side step counter of a captured decode step.
+__global__ void step_advance_kernel(int *step) { *step += 1; }
+
 }  // namespace
+
+extern "C" cudaError_t qdb_launch_step_advance(int *step, cudaStream_t st) {
+    step_advance_kernel<<<1, 1, 0, st>>>(step);
+    return cudaGetLastError();
+}
 
 extern "C" cudaError_t qdb_launch_rmsnorm_rows(const float *x, const float *w, uint16_t *hi, uint16_t *lo, int n, int h,
                                                float eps, cudaStream_t st, float *zero, int zero_len) {
@@ -614,13 +625,13 @@ extern "C" cudaError_t qdb_launch_rmsnorm_rows(const float *x, const float *w, u
 extern "C" cudaError_t qdb_launch_qk_rope_append(const float *qkv, float *q_out, const QdbRowKV *rows, int row_pos_offset,
                                                  int layer, int n, int Hq, int Hkv, const float *q_norm,
                                                  const float *k_norm, const float2 *rope, float eps,
-                                                 cudaStream_t st) {
+                                                 cudaStream_t st, const int *step) {
     if (n <= 0) return cudaSuccess;
     const int slots = Hq + 2 * Hkv;
     dim3 grid(n, (slots + 3) / 4);
     // n_rowkv: callers pass a single-entry array for one session (rows[0].pos is the first row's position)
     qk_rope_append_kernel<<<grid, 128, 0, st>>>(qkv, q_out, rows, 0, row_pos_offset, layer, n, Hq, Hkv, q_norm,
-                                                k_norm, rope, eps);
+                                                k_norm, rope, eps, step);
     return cudaGetLastError();
 }
 
@@ -632,7 +643,7 @@ extern "C" cudaError_t qdb_launch_qk_rope_append_single(const float *qkv, float 
     const int slots = Hq + 2 * Hkv;
     dim3 grid(n, (slots + 3) / 4);
     qk_rope_append_kernel<<<grid, 128, 0, st>>>(qkv, q_out, row0, 1, 0, layer, n, Hq, Hkv, q_norm, k_norm, rope,
-                                                eps);
+                                                eps, nullptr);
     return cudaGetLastError();
 }
 
@@ -667,30 +678,31 @@ extern "C" cudaError_t qdb_launch_attn_prefill(const float *q, const uint16_t *k
 #endif
 template <int R>
 static cudaError_t attn_rows_launch(dim3 grid, const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
-                                    int Hq, int Hkv, int S, float *part, int *err, cudaStream_t st) {
+                                    int Hq, int Hkv, int S, float *part, int *err, cudaStream_t st, const int *step) {
     if (QDB_AR_BULK) {
         const int smem = AB_STAGES * AB_STAGE;
         cudaError_t e = cudaFuncSetAttribute(attn_rows_bulk_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         attn_rows_bulk_kernel<R><<<grid, AR_WARPS * 32, smem, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part,
-                                                                    err);
+                                                                    err, step);
     } else {
-        attn_rows_partial_kernel<R><<<grid, AR_WARPS * 32, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part);
+        attn_rows_partial_kernel<R><<<grid, AR_WARPS * 32, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part,
+                                                                      step);
     }
     return cudaGetLastError();
 }
 
 extern "C" cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
                                             int n, int Hq, int Hkv, int S, float *part, float *out,
-                                            cudaStream_t st, int *err) {
+                                            cudaStream_t st, int *err, const int *step) {
     if (n <= 0) return cudaSuccess;
     dim3 grid(n * Hkv, S);
     cudaError_t e0;
     switch (Hq / Hkv) {
-        case 1: e0 = attn_rows_launch<1>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st); break;
-        case 2: e0 = attn_rows_launch<2>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st); break;
-        case 4: e0 = attn_rows_launch<4>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st); break;
-        case 8: e0 = attn_rows_launch<8>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st); break;
+        case 1: e0 = attn_rows_launch<1>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step); break;
+        case 2: e0 = attn_rows_launch<2>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step); break;
+        case 4: e0 = attn_rows_launch<4>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step); break;
+        case 8: e0 = attn_rows_launch<8>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step); break;
         default: return cudaErrorInvalidValue;
     }
     if (e0 != cudaSuccess) return e0;
@@ -701,15 +713,15 @@ extern "C" cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows
 }
 
 extern "C" cudaError_t qdb_launch_argmax_rows(const float *logits, int n, int V, int mask_eos, int *tokens,
-                                              cudaStream_t st) {
+                                              cudaStream_t st, const int *step) {
     if (n <= 0) return cudaSuccess;
-    argmax_rows_kernel<<<n, 1024, 0, st>>>(logits, V, mask_eos, tokens);
+    argmax_rows_kernel<<<n, 1024, 0, st>>>(logits, V, mask_eos, tokens, step);
     return cudaGetLastError();
 }
 
 extern "C" cudaError_t qdb_launch_embed_rows(const uint16_t *embed, const int *tokens, float *x, int n, int h,
-                                             int V, cudaStream_t st) {
+                                             int V, cudaStream_t st, const int *step) {
     if (n <= 0) return cudaSuccess;
-    embed_rows_kernel<<<n, 256, 0, st>>>(embed, tokens, x, h, V);
+    embed_rows_kernel<<<n, 256, 0, st>>>(embed, tokens, x, h, V, step);
     return cudaGetLastError();
 }

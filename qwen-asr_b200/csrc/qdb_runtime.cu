@@ -64,6 +64,7 @@ struct RowScratch {
     uint16_t *XH = nullptr, *XL = nullptr;  // bf16 hi/lo of the current GEMM input [cap, max(h, qd, I)]
     float *GU = nullptr;                    // [64, 2I] gate/up sums of split-K decode GEMMs
     int *err = nullptr;                     // [4] device error words of the tensor-core GEMMs
+    int *step = nullptr;                    // [1] step counter of a captured batched decode step
     float *LOG = nullptr;  // [cap, V] only for batched decode
     int log_cap = 0;
     float *part = nullptr;
@@ -282,7 +283,7 @@ extern "C" void qdb_model_free(qdb_model *m) {
     cudaFree(m->err); cudaFree(m->tok_dev);
     RowScratch &r = m->rs;
     cudaFree(r.X); cudaFree(r.XH); cudaFree(r.XL); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT);
-    cudaFree(r.LOG); cudaFree(r.part); cudaFree(r.rowkv); cudaFree(r.tok); cudaFree(r.err); cudaFree(r.GU);
+    cudaFree(r.LOG); cudaFree(r.part); cudaFree(r.rowkv); cudaFree(r.tok); cudaFree(r.err); cudaFree(r.GU); cudaFree(r.step);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->h_tok) cudaFreeHost(m->h_tok);
     if (m->st) cudaStreamDestroy(m->st);
@@ -615,6 +616,7 @@ static int ensure_rows(qdb_model *m, int n, bool logits) {
         if (dev_alloc(&r.err, 4)) return -1;
         CK(cudaMemset(r.err, 0, 4 * sizeof(int)));
     }
+    if (!r.step && dev_alloc(&r.step, 1)) return -1;
     if (n > r.rowkv_cap) {
         cudaFree(r.rowkv);
         r.rowkv = nullptr;
@@ -629,7 +631,7 @@ static int ensure_rows(qdb_model *m, int n, bool logits) {
 // to one session and are consecutive positions (prefill); otherwise row b uses
 // rowkv[b] at position rowkv[b].pos + pos_off (multi-utterance decode).
 static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, int pos_off, const qdb_session *s1,
-                    int start_pos, int max_ctx = 1) {
+                    int start_pos, int max_ctx = 1, const int *step = nullptr) {
     RowScratch &r = m->rs;
     const int h = m->cfg.hidden, I = m->cfg.intermediate, Hq = m->cfg.heads, Hkv = m->cfg.kv_heads;
     const int qkvd = m->qd + 2 * m->kvd;
@@ -680,8 +682,8 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
                 CK(qdb_launch_attn_prefill(r.Q, s1->kc, s1->vc, s1->cap, l, start_pos, n, Hq, Hkv, r.ATT, m->st));
         } else {
             CK(qdb_launch_qk_rope_append(r.QKV, r.Q, row0_dev, pos_off, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
-                                         m->cfg.eps, m->st));
-            CK(qdb_launch_attn_rows(r.Q, row0_dev, pos_off, l, n, Hq, Hkv, S, r.part, r.ATT, m->st, r.err));
+                                         m->cfg.eps, m->st, step));
+            CK(qdb_launch_attn_rows(r.Q, row0_dev, pos_off, l, n, Hq, Hkv, S, r.part, r.ATT, m->st, r.err, step));
         }
         CK(qdb_launch_split_bf16(r.ATT, r.XH, r.XL, (size_t)n * m->qd, m->st));
         if (gemm(lw.o, r.X, h, m->qd, 1)) return -1;
@@ -764,11 +766,11 @@ static int batch_setup(qdb_session *const *ss, int n, const int *pos, int extra_
     return 0;
 }
 
-static int batch_tail(qdb_model *m, int n, int *tok_dev) {
+static int batch_tail(qdb_model *m, int n, int *tok_dev, const int *step = nullptr) {
     RowScratch &r = m->rs;
     CK(qdb_launch_rmsnorm_rows(r.X, m->final_norm, r.XH, r.XL, n, m->cfg.hidden, m->cfg.eps, m->st));
     CK(qdb_launch_gemm_tc(m->embed, r.XH, r.XL, r.LOG, n, m->cfg.vocab, m->cfg.hidden, 0, 1, r.err, m->st));
-    CK(qdb_launch_argmax_rows(r.LOG, n, m->cfg.vocab, m->mask_eos, tok_dev, m->st));
+    CK(qdb_launch_argmax_rows(r.LOG, n, m->cfg.vocab, m->mask_eos, tok_dev, m->st, step));
     return 0;
 }
 
@@ -808,10 +810,38 @@ extern "C" int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, cons
     for (int b = 0; b < n; b++)
         if (first_tokens[b] < 0 || first_tokens[b] >= m->cfg.vocab) return fail("row %d: token out of range", b);
     CK(cudaMemcpyAsync(m->rs.tok, first_tokens, sizeof(int) * n, cudaMemcpyHostToDevice, m->st));
-    for (int i = 0; i < n_steps; i++) {
-        int *tin = m->rs.tok + (size_t)i * n;
-        CK(qdb_launch_embed_rows(m->embed, tin, m->rs.X, n, m->cfg.hidden, m->cfg.vocab, m->st));
-        if (run_rows(m, n, false, m->rs.rowkv, i, nullptr, 0, maxp + i + 1) || batch_tail(m, n, tin + n)) return -1;
+    // One step reads its tokens and position offset from the device step
+    // counter, so the same launch sequence serves every step: step 0 runs
+    // directly (it also sizes the scratch), the rest replay a CUDA graph of
+    // one step (~11 launches per layer), which removes the launch gaps. The
+    // attention split count is fixed for the call (sized for its last step).
+    RowScratch &r = m->rs;
+    const int ctx_last = maxp + n_steps;
+    CK(cudaMemsetAsync(r.step, 0, sizeof(int), m->st));
+    auto one_step = [&]() -> int {
+        CK(qdb_launch_embed_rows(m->embed, r.tok, r.X, n, m->cfg.hidden, m->cfg.vocab, m->st, r.step));
+        if (run_rows(m, n, false, r.rowkv, 0, nullptr, 0, ctx_last, r.step) || batch_tail(m, n, r.tok + n, r.step))
+            return -1;
+        CK(qdb_launch_step_advance(r.step, m->st));
+        return 0;
+    };
+    if (one_step()) return -1;
+    if (n_steps > 1) {
+        cudaGraph_t graph = nullptr;
+        cudaGraphExec_t exec = nullptr;
+        CK(cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal));
+        const int rc = one_step();
+        const cudaError_t ce = cudaStreamEndCapture(m->st, &graph);
+        if (rc || ce != cudaSuccess) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc ? -1 : fail("decode step capture: %s", cudaGetErrorString(ce));
+        }
+        cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return fail("decode step graph: %s", cudaGetErrorString(e));
+        for (int i = 1; i < n_steps && e == cudaSuccess; i++) e = cudaGraphLaunch(exec, m->st);
+        cudaGraphExecDestroy(exec);
+        if (e != cudaSuccess) return fail("decode step graph launch: %s", cudaGetErrorString(e));
     }
     CK(cudaMemcpyAsync(tokens_out, m->rs.tok + n, sizeof(int) * (size_t)n * n_steps, cudaMemcpyDeviceToHost, m->st));
     CK(cudaStreamSynchronize(m->st));
