@@ -77,6 +77,10 @@ struct RowScratch {
 
 struct qdb_model {
     qdb_config cfg;
+    // captured step of qdb_forward_batch, valid while its key (row count,
+    // split count and every scratch pointer it uses) is unchanged
+    cudaGraphExec_t fb_exec = nullptr;
+    std::vector<const void *> fb_key;
     QdbDims d;
     int device = 0;
     int sms = 0;
@@ -267,6 +271,7 @@ extern "C" void qdb_model_free(qdb_model *m) {
     if (!m) return;
     cudaSetDevice(m->device);
     if (m->st) cudaStreamSynchronize(m->st);
+    if (m->fb_exec) cudaGraphExecDestroy(m->fb_exec);
     // Sessions still alive are detached: their device KV is released here and
     // a later qdb_session_free only deletes the handle.
     for (qdb_session *s : m->sessions) {
@@ -793,7 +798,37 @@ extern "C" int qdb_forward_batch(qdb_session *const *sessions, int n, const floa
     int maxp = 0;
     if (batch_setup(sessions, n, pos, 0, &m, &maxp) || ensure_tok(m, n)) return -1;
     CK(cudaMemcpyAsync(m->rs.X, embeds, (size_t)n * m->cfg.hidden * 4, cudaMemcpyHostToDevice, m->st));
-    if (run_rows(m, n, false, m->rs.rowkv, 0, nullptr, 0, maxp + 1) || batch_tail(m, n, m->rs.tok)) return -1;
+    RowScratch &r = m->rs;
+    auto step = [&]() { return run_rows(m, n, false, r.rowkv, 0, nullptr, 0, maxp + 1) || batch_tail(m, n, r.tok); };
+    const int S = std::min(64, std::max(1, (maxp + 1 + 64 * QDB_AR_ITERS - 1) / (64 * QDB_AR_ITERS)));
+    const std::vector<const void *> key = {(const void *)(intptr_t)n, (const void *)(intptr_t)S, r.X, r.XH, r.XL,
+                                           r.QKV, r.Q, r.ATT, r.ACT, r.LOG, r.part, r.GU, r.tok, r.err, r.rowkv};
+    if (m->fb_exec && key == m->fb_key) {
+        CK(cudaGraphLaunch(m->fb_exec, m->st));
+    } else {
+        // run directly (this sizes the scratch), then capture the same launch
+        // sequence for the calls that follow
+        if (step()) return -1;
+        if (m->fb_exec) cudaGraphExecDestroy(m->fb_exec);
+        m->fb_exec = nullptr;
+        m->fb_key.clear();
+        const std::vector<const void *> key2 = {(const void *)(intptr_t)n, (const void *)(intptr_t)S, r.X, r.XH, r.XL,
+                                                r.QKV, r.Q, r.ATT, r.ACT, r.LOG, r.part, r.GU, r.tok, r.err, r.rowkv};
+        cudaGraph_t graph = nullptr;
+        if (cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            const bool bad = step();
+            if (cudaStreamEndCapture(m->st, &graph) == cudaSuccess && !bad && graph &&
+                cudaGraphInstantiate(&m->fb_exec, graph, 0) == cudaSuccess)
+                m->fb_key = key2;
+            else
+                m->fb_exec = nullptr;
+            if (graph) cudaGraphDestroy(graph);
+            if (!m->fb_exec) {  // a failed capture only means no graph: the step above already ran
+                cudaGetLastError();
+                g_err.clear();
+            }
+        }
+    }
     CK(cudaMemcpyAsync(tokens_out, m->rs.tok, sizeof(int) * n, cudaMemcpyDeviceToHost, m->st));
     CK(cudaStreamSynchronize(m->st));
     return check_rows_err(m);
