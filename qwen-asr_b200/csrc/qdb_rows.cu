@@ -19,6 +19,7 @@ __global__ void __launch_bounds__(RN_THREADS) rmsnorm_rows_kernel(const float *x
                                                                  uint16_t *lo, int h, float eps, float *zero,
                                                                  int zero_len) {
     __shared__ float red[RN_THREADS / 32];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the next GEMM may start its weight stream
     const int t = threadIdx.x;
     const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)blockIdx.x * h);
     const int h4 = h >> 2;

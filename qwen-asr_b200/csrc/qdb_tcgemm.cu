@@ -78,6 +78,9 @@ __device__ __forceinline__ void tma_load_2d_pol(void *dst, const CUtensorMap *ma
         : "memory");
 }
 
+#ifndef QDB_GEMM_PDL
+#define QDB_GEMM_PDL 1  // programmatic dependent launch: weight prefetch overlaps the previous kernel
+#endif
 #ifndef QDB_GEMM_W_EVICT_FIRST
 #define QDB_GEMM_W_EVICT_FIRST 1
 #endif
@@ -177,15 +180,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const bool w_once = QDB_GEMM_W_EVICT_FIRST && gridDim.y == 1;
         uint64_t pol = 0;
         if (w_once) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+        // Weights do not depend on the kernels before this one: the first S
+        // weight tiles are requested before griddepcontrol.wait (launched
+        // with programmatic dependent launch, this overlaps the previous
+        // kernel); activation tiles only after it.
+        const int pre = nk < S ? nk : S;
+        for (int kb = 0; kb < pre; kb++) {
+            unsigned char *st = smem + (size_t)kb * STAGE;
+            mb_expect(&full[kb], STAGE);
+            const int kx = (kb0 + kb) * TC_BK;
+            if (w_once) tma_load_2d_pol(st, &tmW, kx, m0, &full[kb], pol);
+            else tma_load_2d(st, &tmW, kx, m0, &full[kb]);
+        }
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         int issued = 0;
         for (int kb = 0; kb < nk; kb++) {
             const int s = kb % S;
             if (kb >= S && !mb_wait(&empty[s], ((kb / S) - 1) & 1, err)) break;
             unsigned char *st = smem + (size_t)s * STAGE;
-            mb_expect(&full[s], STAGE);
             const int kx = (kb0 + kb) * TC_BK;
-            if (w_once) tma_load_2d_pol(st, &tmW, kx, m0, &full[s], pol);
-            else tma_load_2d(st, &tmW, kx, m0, &full[s]);
+            if (kb >= pre) {
+                mb_expect(&full[s], STAGE);
+                if (w_once) tma_load_2d_pol(st, &tmW, kx, m0, &full[s], pol);
+                else tma_load_2d(st, &tmW, kx, m0, &full[s]);
+            }
             tma_load_2d(st + A_BYTES, &tmXh, kx, a0, &full[s]);
             tma_load_2d(st + A_BYTES + B_BYTES, &tmXl, kx, a0, &full[s]);
             issued = kb + 1;
@@ -214,6 +232,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     } else if (warp >= 2) {
         // ---- epilogue: warp q reads TMEM lanes [32q, 32q+32) = weight rows
         const int q = warp & 3;
+        asm volatile("griddepcontrol.wait;" ::: "memory");  // Y (residual / zeroed target) is the predecessors' output
         bool ok = true;
         if (lane == 0) ok = mb_wait(&accum, 0, err);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -252,6 +271,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // (qwen_swiglu_multiply, qwen_asr_kernels.c:895-959, then the GEMM split).
 __global__ void swiglu_split_kernel(const float *__restrict__ gu, uint16_t *__restrict__ hi, uint16_t *__restrict__ lo,
                                     size_t count) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the next GEMM may start its weight stream
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= count) return;
     const float2 p = reinterpret_cast<const float2 *>(gu)[i];
@@ -264,6 +284,7 @@ __global__ void swiglu_split_kernel(const float *__restrict__ gu, uint16_t *__re
 // f32 [n, K] -> bf16 hi [n, K] + bf16 lo [n, K] with hi + lo ~= x
 __global__ void split_bf16_kernel(const float *__restrict__ x, uint16_t *__restrict__ hi, uint16_t *__restrict__ lo,
                                   size_t count) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the next GEMM may start its weight stream
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= count) return;
     const float v = x[i];
@@ -311,8 +332,17 @@ cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl,
     const int nk = K / TC_BK;
     const int kb_per = (nk + splits - 1) / splits;
     grid.z = (nk + kb_per - 1) / kb_per;
-    tc_gemm_kernel<BN, S><<<grid, TC_THREADS, smem, st>>>(mw, mh, ml, Y, n, N, K, mode, kb_per, err);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = QDB_GEMM_PDL;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, S>, mw, mh, ml, Y, n, N, K, mode, kb_per, err);
 }
 
 }  // namespace
