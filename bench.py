@@ -425,6 +425,32 @@ def profile_step(args):
     print(list(s.decode_greedy(synth.PROMPT_SUFFIX[-1], P, 3)))
 
 
+def profile_batch(args):
+    """Fixed case for ncu captures of the batched decode kernels: 64 sessions
+    of the 0.6B synthetic model, a 270-position prefill each, then one
+    forward_batch step inside the NVTX range "decode" (ncu --nvtx
+    --nvtx-include "decode/")."""
+    import torch
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    synth = ge.load_synth()
+    cfg = synth.PRESETS["0.6b"]
+    ws = synth.WeightSet(cfg, seed=0)
+    B, P = 64, 270
+    model = pkg.Model(ws, device=0, mask_eos=True)
+    sess = [model.session(P + 16) for _ in range(B)]
+    emb = synth.audio_embeddings(cfg, P, seed=1)
+    for s in sess:
+        s.prefill(emb, 0)
+    pos = np.full(B, P, np.int32)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("decode")
+    toks = pkg.forward_batch(sess, np.tile(emb[:1], (B, 1)), pos)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    print(toks[:4].tolist())
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -434,9 +460,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-step", action="store_true", help="small fixed case for ncu (no timing)")
+    ap.add_argument("--profile-batch", action="store_true", help="batched-decode case for ncu (no timing)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.profile_batch:
+        profile_batch(args)
+        return
     if args.profile_step:
         profile_step(args)
     elif args.impl == "reference":
