@@ -121,3 +121,32 @@ __device__ __forceinline__ float dot8_kv(const uint4 w, const float4 a, const fl
     acc = fmaf(kvhi(w.w), b.w, acc);
     return acc;
 }
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// Row-path kernels are launched with programmatic stream serialization: a
+// kernel may become resident while its predecessor is still running. On
+// entry it lets its own successor do the same, then waits for the
+// predecessor grid to complete (and its writes to be visible) before it
+// touches any memory, so the only overlap is launch latency and set-up.
+#ifndef QDB_PDL
+#define QDB_PDL 1
+#endif
+__device__ __forceinline__ void pdl_enter() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+template <typename... KArgs, typename... Args>
+static inline cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                     Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = QDB_PDL;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}

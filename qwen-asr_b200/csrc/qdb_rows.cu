@@ -19,7 +19,7 @@ __global__ void __launch_bounds__(RN_THREADS) rmsnorm_rows_kernel(const float *x
                                                                  uint16_t *lo, int h, float eps, float *zero,
                                                                  int zero_len) {
     __shared__ float red[RN_THREADS / 32];
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the next GEMM may start its weight stream
+    pdl_enter();
     const int t = threadIdx.x;
     const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)blockIdx.x * h);
     const int h4 = h >> 2;
@@ -72,6 +72,7 @@ __global__ void qk_rope_append_kernel(const float *qkv, float *q_out, const QdbR
                                       int row_pos_offset, int layer, int n, int Hq, int Hkv,
                                       const float *q_norm, const float *k_norm, const float2 *rope, float eps,
                                       const int *step) {
+    pdl_enter();
     const int lane = threadIdx.x & 31;
     const int slot = blockIdx.y * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int row = blockIdx.x;
@@ -243,6 +244,7 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AR_MINB) attn_rows_partial_
                                                                           int row_pos_offset, int layer, int Hq,
                                                                           int Hkv, int S, float *part,
                                                                           const int *step) {
+    pdl_enter();
     __shared__ __align__(16) float qs[R][QDB_HD];
     __shared__ float sm_m[AR_WARPS][R], sm_l[AR_WARPS][R];
     __shared__ __align__(16) float sm_o[AR_WARPS][R][QDB_HD];
@@ -387,6 +389,7 @@ __global__ void __launch_bounds__(AR_WARPS * 32, 2) attn_rows_bulk_kernel(const 
                                                                          int row_pos_offset, int layer, int Hq,
                                                                          int Hkv, int S, float *part, int *err,
                                                                          const int *step) {
+    pdl_enter();
     extern __shared__ __align__(128) unsigned char ring[];
     __shared__ __align__(16) float qs[R][QDB_HD];
     __shared__ float sm_m[AR_WARPS][R], sm_l[AR_WARPS][R];
@@ -552,6 +555,7 @@ __global__ void __launch_bounds__(AR_WARPS * 32, 2) attn_rows_bulk_kernel(const 
 }
 
 __global__ void attn_rows_merge_kernel(const float *part, int S, int Hq, float *out) {
+    pdl_enter();
     const int row = blockIdx.x, h = blockIdx.y, dd = threadIdx.x;
     const float *src = part + ((size_t)row * Hq + h) * S * (2 + QDB_HD);
     float M = -INFINITY;
@@ -569,6 +573,7 @@ __global__ void attn_rows_merge_kernel(const float *part, int S, int Hq, float *
 
 // ---------------------------------------------------------------- argmax / embed
 __global__ void argmax_rows_kernel(const float *logits, int V, int mask_eos, int *tokens, const int *step) {
+    pdl_enter();
     __shared__ unsigned long long red[32];
     const float *lr = logits + (size_t)blockIdx.x * V;
     unsigned long long best = 0ull;
@@ -598,6 +603,7 @@ __global__ void argmax_rows_kernel(const float *logits, int V, int mask_eos, int
 }
 
 __global__ void embed_rows_kernel(const uint16_t *embed, const int *tokens, float *x, int h, int V, const int *step) {
+    pdl_enter();
     const int row = blockIdx.x;
     int tok = tokens[(step ? (size_t)*step * gridDim.x : 0) + row];
     if (tok < 0 || tok >= V) tok = 0;  // never gather outside the table
@@ -606,21 +612,22 @@ __global__ void embed_rows_kernel(const uint16_t *embed, const int *tokens, floa
 }
 
 // One thread: the device-side step counter of a captured decode step.
-__global__ void step_advance_kernel(int *step) { *step += 1; }
+__global__ void step_advance_kernel(int *step) {
+    pdl_enter();
+    *step += 1;
+}
 
 }  // namespace
 
 extern "C" cudaError_t qdb_launch_step_advance(int *step, cudaStream_t st) {
-    step_advance_kernel<<<1, 1, 0, st>>>(step);
-    return cudaGetLastError();
+    return pdl_launch(step_advance_kernel, dim3(1), dim3(1), 0, st, step);
 }
 
 extern "C" cudaError_t qdb_launch_rmsnorm_rows(const float *x, const float *w, uint16_t *hi, uint16_t *lo, int n, int h,
                                                float eps, cudaStream_t st, float *zero, int zero_len) {
     if (n <= 0) return cudaSuccess;
     if (h % 4 || h > 4 * RN_VEC * RN_THREADS || (zero && zero_len % 4)) return cudaErrorInvalidValue;
-    rmsnorm_rows_kernel<<<n, RN_THREADS, 0, st>>>(x, w, hi, lo, h, eps, zero, zero_len);
-    return cudaGetLastError();
+    return pdl_launch(rmsnorm_rows_kernel, dim3(n), dim3(RN_THREADS), 0, st, x, w, hi, lo, h, eps, zero, zero_len);
 }
 
 extern "C" cudaError_t qdb_launch_qk_rope_append(const float *qkv, float *q_out, const QdbRowKV *rows, int row_pos_offset,
@@ -631,9 +638,8 @@ extern "C" cudaError_t qdb_launch_qk_rope_append(const float *qkv, float *q_out,
     const int slots = Hq + 2 * Hkv;
     dim3 grid(n, (slots + 3) / 4);
     // n_rowkv: callers pass a single-entry array for one session (rows[0].pos is the first row's position)
-    qk_rope_append_kernel<<<grid, 128, 0, st>>>(qkv, q_out, rows, 0, row_pos_offset, layer, n, Hq, Hkv, q_norm,
-                                                k_norm, rope, eps, step);
-    return cudaGetLastError();
+    return pdl_launch(qk_rope_append_kernel, grid, dim3(128), 0, st, qkv, q_out, rows, 0, row_pos_offset, layer, n, Hq,
+                      Hkv, q_norm, k_norm, rope, eps, step);
 }
 
 extern "C" cudaError_t qdb_launch_qk_rope_append_single(const float *qkv, float *q_out, const QdbRowKV *row0,
@@ -684,8 +690,8 @@ static cudaError_t attn_rows_launch(dim3 grid, const float *q, const QdbRowKV *r
         const int smem = AB_STAGES * AB_STAGE;
         cudaError_t e = cudaFuncSetAttribute(attn_rows_bulk_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        attn_rows_bulk_kernel<R><<<grid, AR_WARPS * 32, smem, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part,
-                                                                    err, step);
+        return pdl_launch(attn_rows_bulk_kernel<R>, grid, dim3(AR_WARPS * 32), (size_t)smem, st, q, rows,
+                          row_pos_offset, layer, Hq, Hkv, S, part, err, step);
     } else {
         attn_rows_partial_kernel<R><<<grid, AR_WARPS * 32, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part,
                                                                       step);
@@ -709,20 +715,17 @@ extern "C" cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows
     if (e0 != cudaSuccess) return e0;
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    attn_rows_merge_kernel<<<dim3(n, Hq), QDB_HD, 0, st>>>(part, S, Hq, out);
-    return cudaGetLastError();
+    return pdl_launch(attn_rows_merge_kernel, dim3(n, Hq), dim3(QDB_HD), 0, st, part, S, Hq, out);
 }
 
 extern "C" cudaError_t qdb_launch_argmax_rows(const float *logits, int n, int V, int mask_eos, int *tokens,
                                               cudaStream_t st, const int *step) {
     if (n <= 0) return cudaSuccess;
-    argmax_rows_kernel<<<n, 1024, 0, st>>>(logits, V, mask_eos, tokens, step);
-    return cudaGetLastError();
+    return pdl_launch(argmax_rows_kernel, dim3(n), dim3(1024), 0, st, logits, V, mask_eos, tokens, step);
 }
 
 extern "C" cudaError_t qdb_launch_embed_rows(const uint16_t *embed, const int *tokens, float *x, int n, int h,
                                              int V, cudaStream_t st, const int *step) {
     if (n <= 0) return cudaSuccess;
-    embed_rows_kernel<<<n, 256, 0, st>>>(embed, tokens, x, h, V, step);
-    return cudaGetLastError();
+    return pdl_launch(embed_rows_kernel, dim3(n), dim3(256), 0, st, embed, tokens, x, h, V, step);
 }

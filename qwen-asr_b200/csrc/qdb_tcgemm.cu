@@ -146,6 +146,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __shared__ __align__(8) u64 full[S], empty[S], accum;
     __shared__ uint32_t tmem_slot;
 
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // successors may become resident
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * TC_BM, a0 = blockIdx.y * BN;
     // split-K: this CTA takes k-blocks [kb0, kb0 + nk) (gridDim.z splits)
@@ -271,7 +272,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // (qwen_swiglu_multiply, qwen_asr_kernels.c:895-959, then the GEMM split).
 __global__ void swiglu_split_kernel(const float *__restrict__ gu, uint16_t *__restrict__ hi, uint16_t *__restrict__ lo,
                                     size_t count) {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the next GEMM may start its weight stream
+    pdl_enter();
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= count) return;
     const float2 p = reinterpret_cast<const float2 *>(gu)[i];
@@ -284,7 +285,7 @@ __global__ void swiglu_split_kernel(const float *__restrict__ gu, uint16_t *__re
 // f32 [n, K] -> bf16 hi [n, K] + bf16 lo [n, K] with hi + lo ~= x
 __global__ void split_bf16_kernel(const float *__restrict__ x, uint16_t *__restrict__ hi, uint16_t *__restrict__ lo,
                                   size_t count) {
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // the next GEMM may start its weight stream
+    pdl_enter();
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= count) return;
     const float v = x[i];
@@ -350,15 +351,13 @@ cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl,
 extern "C" cudaError_t qdb_launch_split_bf16(const float *x, uint16_t *hi, uint16_t *lo, size_t count,
                                              cudaStream_t st) {
     if (!count) return cudaSuccess;
-    split_bf16_kernel<<<(unsigned)((count + 255) / 256), 256, 0, st>>>(x, hi, lo, count);
-    return cudaGetLastError();
+    return pdl_launch(split_bf16_kernel, dim3((unsigned)((count + 255) / 256)), dim3(256), 0, st, x, hi, lo, count);
 }
 
 extern "C" cudaError_t qdb_launch_swiglu_split(const float *gu, uint16_t *hi, uint16_t *lo, size_t count,
                                                cudaStream_t st) {
     if (!count) return cudaSuccess;
-    swiglu_split_kernel<<<(unsigned)((count + 255) / 256), 256, 0, st>>>(gu, hi, lo, count);
-    return cudaGetLastError();
+    return pdl_launch(swiglu_split_kernel, dim3((unsigned)((count + 255) / 256)), dim3(256), 0, st, gu, hi, lo, count);
 }
 
 // Y (op)= X W^T on tensor cores; X given as its bf16 split (Xh, Xl) [n, K].
