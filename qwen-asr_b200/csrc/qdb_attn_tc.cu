@@ -150,7 +150,8 @@ __device__ __forceinline__ void put8_split(unsigned char *hi, unsigned char *lo,
 template <int R>
 __global__ void __launch_bounds__(AT_THREADS, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const float *__restrict__ q, const uint16_t *__restrict__ vc,
-                   int cap, int start_pos, int n, int Hq, float *__restrict__ out, int *err) {
+                   int cap, int start_pos, int n, int Hq, float *__restrict__ out, int *err, uint16_t *hi,
+                   uint16_t *lo) {
     constexpr int QT = AT_M / R;  // query positions per CTA
     extern __shared__ __align__(1024) unsigned char smem_dyn[];
     __shared__ __align__(8) u64 barK, barS, barO;
@@ -326,15 +327,27 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     // ---- epilogue: O row -> out
     if (s_ok && ntiles > 0) {
         tc_fence_after();
-        float *dst = out + (size_t)(i0 + p) * Hq * QDB_HD + (size_t)(g * R + h) * QDB_HD;
+        const size_t at = (size_t)(i0 + p) * Hq * QDB_HD + (size_t)(g * R + h) * QDB_HD;
+        float *dst = out + at;
 #pragma unroll 1
         for (int c0 = 0; c0 < QDB_HD; c0 += 32) {
             float v[32];
             tmem_ld32(tO + lane_base + c0, v);
-            if (row_ok)
+            if (!row_ok) continue;
+            if (hi) {  // the bf16 split the O-projection GEMM reads
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const uint16_t b0 = f32_to_bf16_rn(v[j]), b1 = f32_to_bf16_rn(v[j + 1]);
+                    const uint16_t l0 = f32_to_bf16_rn(v[j] - __uint_as_float((uint32_t)b0 << 16));
+                    const uint16_t l1 = f32_to_bf16_rn(v[j + 1] - __uint_as_float((uint32_t)b1 << 16));
+                    *reinterpret_cast<uint32_t *>(hi + at + c0 + j) = (uint32_t)b0 | ((uint32_t)b1 << 16);
+                    *reinterpret_cast<uint32_t *>(lo + at + c0 + j) = (uint32_t)l0 | ((uint32_t)l1 << 16);
+                }
+            } else {
 #pragma unroll
                 for (int j = 0; j < 32; j += 4)
                     *reinterpret_cast<float4 *>(dst + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            }
         }
     }
     tc_fence_before();
@@ -359,13 +372,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn_at() {
 
 template <int R>
 cudaError_t launch_at(const CUtensorMap &mk, const float *q, const uint16_t *vl, int cap, int start_pos, int n,
-                      int Hq, int Hkv, float *out, int *err, cudaStream_t st) {
+                      int Hq, int Hkv, float *out, int *err, cudaStream_t st, uint16_t *hi, uint16_t *lo) {
     const int smem = 12 * AT_TILE + 1024;  // Q hi/lo, K, P hi/lo, V^T + alignment slack
     cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     constexpr int QT = AT_M / R;
     dim3 grid((n + QT - 1) / QT, Hkv);
-    attn_tc_kernel<R><<<grid, AT_THREADS, smem, st>>>(mk, q, vl, cap, start_pos, n, Hq, out, err);
+    attn_tc_kernel<R><<<grid, AT_THREADS, smem, st>>>(mk, q, vl, cap, start_pos, n, Hq, out, err, hi, lo);
     return cudaGetLastError();
 }
 
@@ -377,7 +390,7 @@ cudaError_t launch_at(const CUtensorMap &mk, const float *q, const uint16_t *vl,
 // [0, start_pos + n) of this layer; out: f32 [n, Hq*128].
 extern "C" cudaError_t qdb_launch_attn_prefill_tc(const float *q, const uint16_t *kc, const uint16_t *vc, int cap,
                                                   int layer, int start_pos, int n, int Hq, int Hkv, float *out,
-                                                  int *err, cudaStream_t st) {
+                                                  int *err, cudaStream_t st, uint16_t *hi, uint16_t *lo) {
     if (n <= 0) return cudaSuccess;
     if (Hkv <= 0 || Hq % Hkv || cap <= 0 || start_pos + n > cap) return cudaErrorInvalidValue;
     if (((uintptr_t)q | (uintptr_t)kc | (uintptr_t)vc | (uintptr_t)out) & 15) return cudaErrorInvalidValue;
@@ -395,10 +408,10 @@ extern "C" cudaError_t qdb_launch_attn_prefill_tc(const float *q, const uint16_t
         return cudaErrorInvalidValue;
     const uint16_t *vl = vc + layer_off;
     switch (Hq / Hkv) {
-        case 1: return launch_at<1>(mk, q, vl, cap, start_pos, n, Hq, Hkv, out, err, st);
-        case 2: return launch_at<2>(mk, q, vl, cap, start_pos, n, Hq, Hkv, out, err, st);
-        case 4: return launch_at<4>(mk, q, vl, cap, start_pos, n, Hq, Hkv, out, err, st);
-        case 8: return launch_at<8>(mk, q, vl, cap, start_pos, n, Hq, Hkv, out, err, st);
+        case 1: return launch_at<1>(mk, q, vl, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
+        case 2: return launch_at<2>(mk, q, vl, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
+        case 4: return launch_at<4>(mk, q, vl, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
+        case 8: return launch_at<8>(mk, q, vl, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
         default: return cudaErrorInvalidValue;
     }
 }

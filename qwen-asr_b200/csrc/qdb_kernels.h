@@ -114,15 +114,18 @@ cudaError_t qdb_launch_qk_rope_append_single(const float *qkv, float *q_out, con
                                              cudaStream_t st);
 // Causal attention of n query rows of ONE session (rows at start_pos + i).
 // Same on the tensor cores (tcgen05); err: device error words (bounded waits).
+// hi/lo (optional): write the output as its bf16 split [n, Hq*128] instead of f32 out.
 cudaError_t qdb_launch_attn_prefill_tc(const float *q, const uint16_t *kc, const uint16_t *vc, int cap, int layer,
-                                       int start_pos, int n, int Hq, int Hkv, float *out, int *err, cudaStream_t st);
+                                       int start_pos, int n, int Hq, int Hkv, float *out, int *err, cudaStream_t st,
+                                       uint16_t *hi = nullptr, uint16_t *lo = nullptr);
 cudaError_t qdb_launch_attn_prefill(const float *q, const uint16_t *kc, const uint16_t *vc, int cap,
                                     int layer, int start_pos, int n, int Hq, int Hkv, float *out,
                                     cudaStream_t st);
 // Independent rows (one query each) over per-row caches.
 cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
                                  int n, int Hq, int Hkv, int splits, float *part, float *out,
-                                 cudaStream_t st, int *err = nullptr, const int *step = nullptr);
+                                 cudaStream_t st, int *err = nullptr, const int *step = nullptr,
+                                 uint16_t *hi = nullptr, uint16_t *lo = nullptr);
 // Tensor-core GEMM (qdb_tcgemm.cu): Y (op)= X W^T with X given as bf16 hi/lo.
 cudaError_t qdb_launch_split_bf16(const float *x, uint16_t *hi, uint16_t *lo, size_t count, cudaStream_t st);
 cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,

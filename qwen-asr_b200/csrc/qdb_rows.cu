@@ -554,7 +554,8 @@ __global__ void __launch_bounds__(AR_WARPS * 32, 2) attn_rows_bulk_kernel(const 
     }
 }
 
-__global__ void attn_rows_merge_kernel(const float *part, int S, int Hq, float *out) {
+// hi/lo (optional): write the bf16 split the O-projection GEMM reads instead of f32 out.
+__global__ void attn_rows_merge_kernel(const float *part, int S, int Hq, float *out, uint16_t *hi, uint16_t *lo) {
     pdl_enter();
     const int row = blockIdx.x, h = blockIdx.y, dd = threadIdx.x;
     const float *src = part + ((size_t)row * Hq + h) * S * (2 + QDB_HD);
@@ -568,7 +569,15 @@ __global__ void attn_rows_merge_kernel(const float *part, int S, int Hq, float *
         L += src[s * (2 + QDB_HD) + 1] * f;
         O += src[s * (2 + QDB_HD) + 2 + dd] * f;
     }
-    out[(size_t)row * Hq * QDB_HD + (size_t)h * QDB_HD + dd] = L > 0.f ? O / L : 0.f;
+    const float v = L > 0.f ? O / L : 0.f;
+    const size_t at = (size_t)row * Hq * QDB_HD + (size_t)h * QDB_HD + dd;
+    if (hi) {
+        const uint16_t b = f32_to_bf16_rn(v);
+        hi[at] = b;
+        lo[at] = f32_to_bf16_rn(v - __uint_as_float((uint32_t)b << 16));
+    } else {
+        out[at] = v;
+    }
 }
 
 // ---------------------------------------------------------------- argmax / embed
@@ -701,7 +710,8 @@ static cudaError_t attn_rows_launch(dim3 grid, const float *q, const QdbRowKV *r
 
 extern "C" cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
                                             int n, int Hq, int Hkv, int S, float *part, float *out,
-                                            cudaStream_t st, int *err, const int *step) {
+                                            cudaStream_t st, int *err, const int *step, uint16_t *hi,
+                                            uint16_t *lo) {
     if (n <= 0) return cudaSuccess;
     dim3 grid(n * Hkv, S);
     cudaError_t e0;
@@ -715,7 +725,7 @@ extern "C" cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows
     if (e0 != cudaSuccess) return e0;
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    return pdl_launch(attn_rows_merge_kernel, dim3(n, Hq), dim3(QDB_HD), 0, st, part, S, Hq, out);
+    return pdl_launch(attn_rows_merge_kernel, dim3(n, Hq), dim3(QDB_HD), 0, st, part, S, Hq, out, hi, lo);
 }
 
 extern "C" cudaError_t qdb_launch_argmax_rows(const float *logits, int n, int V, int mask_eos, int *tokens,

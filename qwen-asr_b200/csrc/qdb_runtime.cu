@@ -680,17 +680,20 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
         if (single) {
             CK(qdb_launch_qk_rope_append_single(r.QKV, r.Q, row0_dev, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
                                                 m->cfg.eps, m->st));
-            if (QDB_ATTN_TC)
+            if (QDB_ATTN_TC) {
                 CK(qdb_launch_attn_prefill_tc(r.Q, s1->kc, s1->vc, s1->cap, l, start_pos, n, Hq, Hkv, r.ATT, r.err,
-                                              m->st));
-            else
+                                              m->st, r.XH, r.XL));
+            } else {
                 CK(qdb_launch_attn_prefill(r.Q, s1->kc, s1->vc, s1->cap, l, start_pos, n, Hq, Hkv, r.ATT, m->st));
+                CK(qdb_launch_split_bf16(r.ATT, r.XH, r.XL, (size_t)n * m->qd, m->st));
+            }
         } else {
             CK(qdb_launch_qk_rope_append(r.QKV, r.Q, row0_dev, pos_off, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
                                          m->cfg.eps, m->st, step));
-            CK(qdb_launch_attn_rows(r.Q, row0_dev, pos_off, l, n, Hq, Hkv, S, r.part, r.ATT, m->st, r.err, step));
+            CK(qdb_launch_attn_rows(r.Q, row0_dev, pos_off, l, n, Hq, Hkv, S, r.part, r.ATT, m->st, r.err, step,
+                                    r.XH, r.XL));
         }
-        CK(qdb_launch_split_bf16(r.ATT, r.XH, r.XL, (size_t)n * m->qd, m->st));
+        // (both attention paths write the O-projection's bf16 split directly)
         if (gemm(lw.o, r.X, h, m->qd, 1)) return -1;
         const bool gu_split = splits_of(2 * I, h) > 1;
         CK(qdb_launch_rmsnorm_rows(r.X, lw.post_norm, r.XH, r.XL, n, h, m->cfg.eps, m->st, gu_split ? r.GU : nullptr,
