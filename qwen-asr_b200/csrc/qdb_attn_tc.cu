@@ -30,7 +30,7 @@
 
 namespace {
 
-constexpr int AT_THREADS = 128;
+constexpr int AT_THREADS = 256;  // two threads per MMA row: warps w and w + 4 share TMEM lanes, split the columns
 constexpr int AT_M = 128;          // MMA rows per CTA (query vectors)
 constexpr int AT_N = 128;          // keys per tile
 constexpr int AT_TILE = 128 * 128; // bytes of one 128-row x 64-column fp16 swizzled tile (16 KB)
@@ -149,7 +149,8 @@ __device__ __forceinline__ void put8_split(unsigned char *hi, unsigned char *lo,
 
 template <int R>
 __global__ void __launch_bounds__(AT_THREADS, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const float *__restrict__ q, const uint16_t *__restrict__ vc,
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                   const float *__restrict__ q,
                    int cap, int start_pos, int n, int Hq, float *__restrict__ out, int *err, uint16_t *hi,
                    uint16_t *lo) {
     constexpr int QT = AT_M / R;  // query positions per CTA
@@ -165,7 +166,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 
     const int t = threadIdx.x, warp = t >> 5;
     const int g = blockIdx.y, i0 = blockIdx.x * QT;
-    const int r = t, p = r / R, h = r % R;  // this thread's MMA row: position i0 + p, head g*R + h
+    const int half = warp >> 2;                     // this thread's half of the row's columns
+    const int r = 32 * (warp & 3) + (t & 31), p = r / R, h = r % R;  // MMA row: position i0 + p, head g*R + h
     const bool row_ok = i0 + p < n;
     const int qpos = start_pos + i0 + p;
     const int kend = start_pos + min(n, i0 + QT);  // keys this tile needs
@@ -189,7 +191,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     {
         const float *src = q + (size_t)(i0 + p) * Hq * QDB_HD + (size_t)(g * R + h) * QDB_HD;
 #pragma unroll 1
-        for (int c = 0; c < QDB_HD / 8; c++) {
+        for (int c = half * 8; c < half * 8 + 8; c++) {
             float v[8];
             if (row_ok) {
                 const float4 a = *reinterpret_cast<const float4 *>(src + c * 8);
@@ -207,7 +209,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot, tS = tmem, tO = tmem + 128;
-    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
     constexpr uint32_t idesc = idesc_f16(AT_M, AT_N);
     unsigned phK = 0, phS = 0, phO = 0;
 
@@ -243,7 +245,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         if (!s_ok) break;
         tc_fence_after();
 #pragma unroll 1
-        for (int c0 = 0; c0 < AT_N; c0 += 32) {
+        for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
             float v[32];
             tmem_ld32(tS + lane_base + c0, v);
             float cm = -INFINITY;
@@ -265,33 +267,40 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         tc_fence_before();
         __syncthreads();
     }
+    {  // combine the two column halves of each row
+        __shared__ float cm_m[AT_THREADS], cm_l[AT_THREADS];
+        cm_m[t] = m;
+        cm_l[t] = l;
+        __syncthreads();
+        const float m2 = cm_m[t ^ 128], l2 = cm_l[t ^ 128];
+        const float mn = fmaxf(m, m2);
+        if (mn != -INFINITY) {
+            l = (m == -INFINITY ? 0.f : l * expf(m - mn)) + (m2 == -INFINITY ? 0.f : l2 * expf(m2 - mn));
+            m = mn;
+        }
+    }
     const float inv_l = l > 0.f ? 1.0f / l : 0.f;
 
     // ---- pass 2: P = softmax row (exact m, l), O += P V
-    const uint16_t *vhead = vc + (size_t)g * cap * QDB_HD;
+    // Once S of a tile is computed the K buffer is free: the V tile is loaded
+    // into it by TMA while the threads write P, then transposed smem -> smem.
 #pragma unroll 1
     for (int kt = 0; kt < ntiles && s_ok; kt++) {
         const int k0 = kt * AT_N;
-        if (t == 0 && !s_tile(k0)) s_ok = 0;
-        // V^T: thread t owns dim t; 8 keys per 16-byte chunk; keys past kend -> 0
-        // (the previous P V MMAs finished before the barrier that ended the last round)
-#pragma unroll 1
-        for (int c = 0; c < AT_N / 8; c++) {
-            uint32_t w[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int ka = k0 + c * 8 + 2 * i, kb = ka + 1;
-                const uint32_t lo = ka < kend ? vhead[(size_t)ka * QDB_HD + t] : 0u;
-                const uint32_t hi = kb < kend ? vhead[(size_t)kb * QDB_HD + t] : 0u;
-                w[i] = lo | (hi << 16);
+        if (t == 0) {
+            if (!s_tile(k0)) {
+                s_ok = 0;
+            } else {
+                mb_expect(&barK, 2 * AT_TILE);
+                tma_load_2d(Kt, &tmV, 0, g * cap + k0, &barK);
+                tma_load_2d(Kt + AT_TILE, &tmV, 64, g * cap + k0, &barK);
             }
-            *reinterpret_cast<uint4 *>(Vt + (c >> 3) * AT_TILE + swz(t, c & 7)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
         __syncthreads();
         if (!s_ok) break;
         tc_fence_after();
 #pragma unroll 1
-        for (int c0 = 0; c0 < AT_N; c0 += 32) {
+        for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
             float v[32];
             tmem_ld32(tS + lane_base + c0, v);
 #pragma unroll
@@ -305,10 +314,34 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 put8_split(Ph + (col >> 6) * AT_TILE, Pl + (col >> 6) * AT_TILE, r, (col & 63) >> 3, v + q8 * 8);
             }
         }
+        // V^T: thread t owns dim t; 8 keys per 16-byte chunk; keys past kend -> 0
+        if (t == 0 && s_ok) {
+            if (!mb_wait(&barK, phK, err)) s_ok = 0;
+            phK ^= 1;
+        }
+        __syncthreads();
+        if (s_ok) {
+            const int d = t & 127;  // dim; keys of half t >> 7
+            const unsigned char *vsrc = Kt + (d >> 6) * AT_TILE;
+            const int vc8 = (d & 63) >> 3, ve = d & 7;
+#pragma unroll 2
+            for (int c = (t >> 7) * 8; c < (t >> 7) * 8 + 8; c++) {
+                uint32_t w[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int ka = c * 8 + 2 * i;
+                    const uint32_t lo = k0 + ka < kend ? *reinterpret_cast<const uint16_t *>(vsrc + swz(ka, vc8) + ve * 2) : 0u;
+                    const uint32_t hi =
+                        k0 + ka + 1 < kend ? *reinterpret_cast<const uint16_t *>(vsrc + swz(ka + 1, vc8) + ve * 2) : 0u;
+                    w[i] = lo | (hi << 16);
+                }
+                *reinterpret_cast<uint4 *>(Vt + (c >> 3) * AT_TILE + swz(d, c & 7)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
-        if (t == 0) {
+        if (t == 0 && s_ok) {
             tc_fence_after();
 #pragma unroll
             for (int kb = 0; kb < 2; kb++)
@@ -330,7 +363,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         const size_t at = (size_t)(i0 + p) * Hq * QDB_HD + (size_t)(g * R + h) * QDB_HD;
         float *dst = out + at;
 #pragma unroll 1
-        for (int c0 = 0; c0 < QDB_HD; c0 += 32) {
+        for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
             float v[32];
             tmem_ld32(tO + lane_base + c0, v);
             if (!row_ok) continue;
@@ -371,14 +404,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn_at() {
 }
 
 template <int R>
-cudaError_t launch_at(const CUtensorMap &mk, const float *q, const uint16_t *vl, int cap, int start_pos, int n,
+cudaError_t launch_at(const CUtensorMap &mk, const CUtensorMap &mv, const float *q, int cap, int start_pos, int n,
                       int Hq, int Hkv, float *out, int *err, cudaStream_t st, uint16_t *hi, uint16_t *lo) {
     const int smem = 12 * AT_TILE + 1024;  // Q hi/lo, K, P hi/lo, V^T + alignment slack
     cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     constexpr int QT = AT_M / R;
     dim3 grid((n + QT - 1) / QT, Hkv);
-    attn_tc_kernel<R><<<grid, AT_THREADS, smem, st>>>(mk, q, vl, cap, start_pos, n, Hq, out, err, hi, lo);
+    attn_tc_kernel<R><<<grid, AT_THREADS, smem, st>>>(mk, mv, q, cap, start_pos, n, Hq, out, err, hi, lo);
     return cudaGetLastError();
 }
 
@@ -397,21 +430,22 @@ extern "C" cudaError_t qdb_launch_attn_prefill_tc(const float *q, const uint16_t
     auto fn = encode_fn_at();
     if (!fn) return cudaErrorNotSupported;
     const size_t layer_off = (size_t)layer * Hkv * cap * QDB_HD;
-    CUtensorMap mk;
+    // K and V of this layer: [Hkv * cap rows][128] fp16, 64-column x 128-row boxes, 128-byte swizzle
+    CUtensorMap mk, mv;
     cuuint64_t dims[2] = {(cuuint64_t)QDB_HD, (cuuint64_t)Hkv * (cuuint64_t)cap};
     cuuint64_t strides[1] = {(cuuint64_t)QDB_HD * 2};
     cuuint32_t box[2] = {64, (cuuint32_t)AT_N};
     cuuint32_t es[2] = {1, 1};
-    if (fn(&mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t *>(kc + layer_off), dims, strides, box, es,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return cudaErrorInvalidValue;
-    const uint16_t *vl = vc + layer_off;
+    for (int i = 0; i < 2; i++)
+        if (fn(i ? &mv : &mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t *>((i ? vc : kc) + layer_off), dims,
+               strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
     switch (Hq / Hkv) {
-        case 1: return launch_at<1>(mk, q, vl, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
-        case 2: return launch_at<2>(mk, q, vl, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
-        case 4: return launch_at<4>(mk, q, vl, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
-        case 8: return launch_at<8>(mk, q, vl, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
+        case 1: return launch_at<1>(mk, mv, q, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
+        case 2: return launch_at<2>(mk, mv, q, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
+        case 4: return launch_at<4>(mk, mv, q, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
+        case 8: return launch_at<8>(mk, mv, q, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
         default: return cudaErrorInvalidValue;
     }
 }
