@@ -319,6 +319,151 @@ bool make_map(CUtensorMap *m, const void *base, int rows, int cols, int box_rows
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Accumulator tile -> Y: warp q of the epilogue reads TMEM lanes [32q, 32q+32)
+// (weight rows m0 + 32q + lane), columns [col0, col0 + BN) (activation rows a0..).
+template <int BN>
+__device__ __forceinline__ void epilogue_tile(uint32_t tcol, int q, int lane, int m0, int a0, float *__restrict__ Y,
+                                              int n, int N, int mode) {
+    const int wrow = m0 + 32 * q + lane;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_ld32(tcol + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int arow = a0 + c0 + j;
+            if (mode == 2) {
+                const float u = __shfl_down_sync(0xffffffffu, v[j], 1);
+                if (arow < n && (lane & 1) == 0 && wrow + 1 < N) Y[(size_t)arow * (N / 2) + wrow / 2] = silu_mul(v[j], u);
+            } else if (arow < n && wrow < N) {
+                float *dst = Y + (size_t)arow * N + wrow;
+                if (mode == 3) atomicAdd(dst, v[j]);
+                else *dst = mode == 1 ? *dst + v[j] : v[j];
+            }
+        }
+    }
+}
+
+// Persistent form for the prefill shapes (no split-K): one CTA per SM walks
+// the output tiles (tile t -> weight tile t / ny, activation tile t % ny, so
+// the CTAs of a wave share weight tiles in L2). The TMA ring runs on across
+// tiles, and the accumulator is double-buffered in TMEM (2 x BN columns):
+// the MMA warp fills one buffer while the epilogue warps drain the other.
+template <int BN, int S>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_persist_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXh,
+                           const __grid_constant__ CUtensorMap tmXl, float *__restrict__ Y, int n, int N, int K,
+                           int mode, int *err) {
+    constexpr int A_BYTES = TC_BM * TC_BK * 2;
+    constexpr int B_BYTES = BN * TC_BK * 2;
+    constexpr int STAGE = A_BYTES + 2 * B_BYTES;
+    extern __shared__ __align__(1024) unsigned char smem_dyn[];
+    __shared__ __align__(8) u64 full[S], empty[S], acc_full[2], acc_empty[2];
+    __shared__ uint32_t tmem_slot;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nx = (N + TC_BM - 1) / TC_BM, ny = (n + BN - 1) / BN, ntile = nx * ny;
+    const int nk = K / TC_BK;
+    unsigned char *smem = smem_dyn + ((1024u - (su32(smem_dyn) & 1023u)) & 1023u);
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; i++) {
+            mb_init(&full[i], 1);
+            mb_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mb_init(&acc_full[i], 1);
+            mb_init(&acc_empty[i], 4);  // one arrival per epilogue warp
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_slot)),
+                     "r"(2 * BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // ---- TMA producer: every k-block of every tile of this CTA, one ring
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        unsigned it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < ntile && ok; tile += gridDim.x) {
+            const int m0 = (tile / ny) * TC_BM, a0 = (tile % ny) * BN;
+            for (int kb = 0; kb < nk; kb++, it++) {
+                const int s = it % S;
+                if (it >= (unsigned)S && !mb_wait(&empty[s], ((it / S) - 1) & 1, err)) {
+                    ok = false;
+                    break;
+                }
+                unsigned char *st = smem + (size_t)s * STAGE;
+                mb_expect(&full[s], STAGE);
+                const int kx = kb * TC_BK;
+                tma_load_2d(st, &tmW, kx, m0, &full[s]);
+                tma_load_2d(st + A_BYTES, &tmXh, kx, a0, &full[s]);
+                tma_load_2d(st + A_BYTES + B_BYTES, &tmXl, kx, a0, &full[s]);
+            }
+        }
+        // the copies of the last round of every stage land before leaving
+        for (unsigned i = it > (unsigned)S ? it - S : 0; i < it; i++) mb_wait(&full[i % S], (i / S) & 1, err);
+    } else if (warp == 1 && lane == 0) {
+        // ---- MMA issuer
+        constexpr uint32_t idesc = instr_desc(TC_BM, BN);
+        unsigned it = 0, tl = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < ntile && ok; tile += gridDim.x, tl++) {
+            const int b = tl & 1;
+            // the epilogue has drained this accumulator buffer (its previous use)
+            if (tl >= 2 && !mb_wait(&acc_empty[b], ((tl >> 1) - 1) & 1, err)) break;
+            tc_fence_after();
+            const uint32_t acc = tmem + (uint32_t)(b * BN);
+            for (int kb = 0; kb < nk; kb++, it++) {
+                const int s = it % S;
+                if (!mb_wait(&full[s], (it / S) & 1, err)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t base = su32(smem + (size_t)s * STAGE);
+#pragma unroll
+                for (int k = 0; k < TC_BK / 16; k++) {
+                    const u64 ad = sm_desc(base + k * 32);
+                    mma_bf16(acc, ad, sm_desc(base + A_BYTES + k * 32), idesc, (kb | k) ? 1u : 0u);
+                    mma_bf16(acc, ad, sm_desc(base + A_BYTES + B_BYTES + k * 32), idesc, 1u);
+                }
+                mma_commit(&empty[s]);
+            }
+            mma_commit(&acc_full[b]);
+        }
+    } else if (warp >= 2) {
+        // ---- epilogue (warp q = warp & 3 owns TMEM lanes [32q, 32q+32))
+        const int q = warp & 3;
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        unsigned tl = 0;
+        for (int tile = blockIdx.x; tile < ntile; tile += gridDim.x, tl++) {
+            const int b = tl & 1;
+            bool ok = true;
+            if (lane == 0) ok = mb_wait(&acc_full[b], (tl >> 1) & 1, err);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            tc_fence_after();
+            epilogue_tile<BN>(tmem + (uint32_t)(b * BN), q, lane, (tile / ny) * TC_BM, (tile % ny) * BN, Y, n, N, mode);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&acc_empty[b])) : "memory");
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN) : "memory");
+    }
+}
+
 template <int BN, int S>
 cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,
                       int mode, int splits, int *err, cudaStream_t st) {
@@ -344,6 +489,38 @@ cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl,
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, S>, mw, mh, ml, Y, n, N, K, mode, kb_per, err);
+}
+
+
+#ifndef QDB_GEMM_PERSIST
+#define QDB_GEMM_PERSIST 1  // prefill shapes: persistent CTAs with a double-buffered TMEM accumulator
+#endif
+template <int BN, int S>
+cudaError_t launch_persist(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,
+                           int mode, int *err, cudaStream_t st) {
+    CUtensorMap mw, mh, ml;
+    if (!make_map(&mw, W, N, K, TC_BM) || !make_map(&mh, Xh, n, K, BN) || !make_map(&ml, Xl, n, K, BN))
+        return cudaErrorInvalidValue;
+    constexpr int STAGE = TC_BM * TC_BK * 2 + 2 * BN * TC_BK * 2;
+    const int smem = S * STAGE + 1024;
+    cudaError_t e =
+        cudaFuncSetAttribute(tc_gemm_persist_kernel<BN, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return cudaErrorInvalidValue;
+    const int tiles = ((N + TC_BM - 1) / TC_BM) * ((n + BN - 1) / BN);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(tiles < sms ? tiles : sms);
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = QDB_GEMM_PDL;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tc_gemm_persist_kernel<BN, S>, mw, mh, ml, Y, n, N, K, mode, err);
 }
 
 }  // namespace
@@ -373,6 +550,7 @@ extern "C" cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh,
     if (splits < 1 || (splits > 1 && mode != 3)) return cudaErrorInvalidValue;
     if (((uintptr_t)W | (uintptr_t)Xh | (uintptr_t)Xl) & 15) return cudaErrorInvalidValue;
     if (n <= 64) return launch_tc<64, 6>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st);
+    if (QDB_GEMM_PERSIST && splits == 1) return launch_persist<128, 4>(W, Xh, Xl, Y, n, N, K, mode, err, st);
     return launch_tc<128, 4>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st);
 }
 
