@@ -262,7 +262,11 @@ def run_ours(args):
     peak, peak_kind = measured_peaks()
     kernel = "step_kernel" if n_local == 1 else "rows_decode"
     traffic = step_traffic_from_profile(kernel, args.config)
-    launches_per_step = (L * 8) * n_local + (n_dec if n_local == 1 else n_dec * (L * 9 + 4))
+    # per prefill, per layer: 2 norms, 4 GEMMs, q/k RoPE + KV append, attention, bf16 split of the
+    # SwiGLU output; per batched decode step: embed, 10 per layer (2 norms, 4 GEMMs, RoPE/append,
+    # attention units, split merge, SwiGLU split), final norm, lm_head GEMM, argmax, step advance;
+    # b=1 decode: one persistent step kernel per token
+    launches_per_step = (L * 9) * n_local + (n_dec if n_local == 1 else n_dec * (L * 10 + 5))
     h2d = sum(e.numel() * 4 for e in pinned) - n_local * h * 4 + n_dec * n_local * h * 4
     d2h = n_dec * n_local * 4
     result = {
