@@ -423,9 +423,12 @@ extern "C" int qdb_session_reserve(qdb_session *s, int positions) {
 }
 
 // ------------------------------------------------------------------ single-utterance step
-static int check_err(qdb_model *m) {
+// fetched: the error words already copied to the host (after the caller's
+// stream sync), or null to read them here.
+static int check_err(qdb_model *m, const int *fetched = nullptr) {
     int ev[4] = {0, 0, 0, 0};
-    CK(cudaMemcpy(ev, m->err, sizeof(ev), cudaMemcpyDeviceToHost));
+    if (fetched) memcpy(ev, fetched, sizeof(ev));
+    else CK(cudaMemcpy(ev, m->err, sizeof(ev), cudaMemcpyDeviceToHost));
     const int e = ev[0];
     if (e) {
         // A bounded wait ran out or a check refused an access: reset the
@@ -520,12 +523,15 @@ extern "C" int qdb_forward(qdb_session *s, const float *embed, int pos, float *h
     a.hidden_out = hidden_out ? m->hidden_dev : nullptr;
     a.logits_out = logits_out ? m->logits_dev : nullptr;
     if (launch_step(m, a)) return -1;
+    // token and error words into pinned memory with the outputs: one stream
+    // sync per call, no second round trip for the error check
     CK(cudaMemcpyAsync(m->h_tok, m->tok_dev, sizeof(int), cudaMemcpyDeviceToHost, m->st));
+    CK(cudaMemcpyAsync(m->h_tok + 8, m->err, 4 * sizeof(int), cudaMemcpyDeviceToHost, m->st));
     if (hidden_out) CK(cudaMemcpyAsync(hidden_out, m->hidden_dev, h * 4, cudaMemcpyDeviceToHost, m->st));
     if (logits_out)
         CK(cudaMemcpyAsync(logits_out, m->logits_dev, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->st));
     CK(cudaStreamSynchronize(m->st));
-    if (check_err(m)) return -1;
+    if (check_err(m, m->h_tok + 8)) return -1;
     return m->h_tok[0];
 }
 
