@@ -329,6 +329,20 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tcol, int q, int lane, in
     for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
         tmem_ld32(tcol + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+        if (mode == 1) {  // residual add: all 32 loads in flight before the stores
+            float y[32];
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                const int arow = a0 + c0 + j;
+                y[j] = (arow < n && wrow < N) ? Y[(size_t)arow * N + wrow] : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                const int arow = a0 + c0 + j;
+                if (arow < n && wrow < N) Y[(size_t)arow * N + wrow] = y[j] + v[j];
+            }
+            continue;
+        }
 #pragma unroll
         for (int j = 0; j < 32; j++) {
             const int arow = a0 + c0 + j;
