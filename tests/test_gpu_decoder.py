@@ -168,6 +168,34 @@ def test_batched_decode_matches_single(pkg, synth):
             assert got[b] == want or margin_top2(lg, mask_eos=True) <= MARGIN, (step, b)
 
 
+def test_forward_batch_graph_reuse_across_session_groups(pkg, synth):
+    """qdb_forward_batch replays one captured step for every call with the same
+    row count: two disjoint groups of sessions (other KV caches, other
+    positions) alternate through it, and each step still equals per-session
+    qdb_forward."""
+    cfg = synth.PRESETS["small"]
+    ws = synth.WeightSet(cfg, seed=8, norm_jitter=0.1)
+    model = pkg.Model(ws, device=0, mask_eos=True)
+    n = 4
+    groups = []
+    for gi, lens in enumerate([[5, 21, 40, 12], [33, 2, 17, 60]]):
+        embs = [synth.audio_embeddings(cfg, L + 4, seed=300 + 10 * gi + b) for b, L in enumerate(lens)]
+        sb = [model.session(80) for _ in range(n)]
+        ss = [model.session(80) for _ in range(n)]
+        for b in range(n):
+            sb[b].prefill(embs[b][:lens[b]], 0)
+            ss[b].prefill(embs[b][:lens[b]], 0)
+        groups.append((lens, embs, sb, ss))
+    for step in range(3):
+        for gi, (lens, embs, sb, ss) in enumerate(groups):
+            x = np.stack([embs[b][lens[b] + step] for b in range(n)])
+            pos = [lens[b] + step for b in range(n)]
+            got = pkg.forward_batch(sb, x, pos)
+            for b in range(n):
+                want, _, lg = ss[b].forward(x[b], pos[b], want_logits=True)
+                assert got[b] == want or margin_top2(lg, mask_eos=True) <= MARGIN, (step, gi, b)
+
+
 def test_batched_greedy_loop_matches_oracle(pkg, synth):
     cfg = synth.PRESETS["tiny"]
     ws = synth.WeightSet(cfg, seed=8, norm_jitter=0.1)
