@@ -185,10 +185,8 @@ extern "C" qdb_model *qdb_model_create(const qdb_config *cfg, int device) {
         const QdbStepKernel *pref[2] = {qdb_step_kernel_w6(), qdb_step_kernel_w7()};
         if (cfg->hidden < 2048) std::swap(pref[0], pref[1]);
         // QWEN_ASR_B200_STEP=w6|w7 forces a build (tuning; falls back if it cannot hold the model)
-        if (const char *ov = getenv("QWEN_ASR_B200_STEP")) {
-            if (!strcmp(ov, pref[1]->name + 0) || (ov[0] == 'w' && ov[1] == pref[1]->name[1]))
-                std::swap(pref[0], pref[1]);
-        }
+        if (const char *ov = getenv("QWEN_ASR_B200_STEP"))  // "w6" / "w7": leading part of a build name
+            if (ov[0] && !strncmp(ov, pref[1]->name, strlen(ov))) std::swap(pref[0], pref[1]);
         for (const QdbStepKernel *k : pref)
             if (!step_k && kmax * 2 <= k->stage_bytes && vmax <= k->max_vector) step_k = k;
         if (!step_k) {
