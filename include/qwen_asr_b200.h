@@ -123,12 +123,15 @@ int qdb_decode_greedy(qdb_session *s, int first_token, int pos, int n_steps, int
 /* ---- Batched decode of independent utterances (no reference counterpart:
  * the reference decodes one utterance per process). Row b runs session
  * sessions[b] at position pos[b] with embedding row b of embeds (host f32
- * [n, hidden]); tokens_out[b] receives its greedy token. */
+ * [n, hidden]); tokens_out[b] receives its greedy token. The model keeps a
+ * CUDA graph of this step and replays it while n and its scratch are
+ * unchanged; sessions and positions may differ from call to call. */
 int qdb_forward_batch(qdb_session *const *sessions, int n, const float *embeds,
                       const int *pos, int *tokens_out);
 
 /* Batched device-resident greedy loop over n sessions: row b starts from
- * first_tokens[b] at pos[b]; tokens_out is [n_steps, n] (host). */
+ * first_tokens[b] at pos[b]; tokens_out is [n_steps, n] (host). Steps after
+ * the first replay a CUDA graph captured on the model's stream. */
 int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, const int *first_tokens,
                             const int *pos, int n_steps, int *tokens_out);
 
