@@ -1,10 +1,10 @@
 """Benchmark of the B200 decoder hot path (qwen-asr decoder token loop + prefill).
 
-Metric: decode tok/s per GPU as a fraction of the HBM roofline,
-plus end-to-end x-realtime of the decoder stage. Default workload = config c1
+Metric: decode tok/s per GPU as a fraction of the HBM roofline, plus
+end-to-end x-realtime of the decoder stage. Default workload = config c1
 (1.7B-shaped, batch 1, 30 s utterance -> 404-position prefill, 256 greedy
-tokens with EOS masked); --config c0 / c2 select the 0.6B batch-1 and 0.6B
-64-utterance configurations.
+tokens with EOS masked); --config c0 / c2 / c3 select the 0.6B batch-1, the
+0.6B 64-utterance and the 1.7B long-context (300 s) configurations.
 
 One timed step = one utterance per rank (c2: this rank's shard of the 64
 utterances): prefill over the prompt embeddings followed by the greedy decode
