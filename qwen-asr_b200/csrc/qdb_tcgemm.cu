@@ -572,7 +572,7 @@ extern "C" cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh,
 #define QDB_SPLIT_WAVES 1    // CTAs targeted per SM by split-K
 #endif
 #ifndef QDB_SPLIT_MIN_KB
-#define QDB_SPLIT_MIN_KB 4   // fewest 64-wide k-blocks one split-K CTA takes
+#define QDB_SPLIT_MIN_KB 2   // fewest 64-wide k-blocks one split-K CTA takes
 #endif
 // Split count for a skinny GEMM: about QDB_SPLIT_WAVES CTAs per SM, each
 // with at least QDB_SPLIT_MIN_KB k-blocks (short CTAs are all set-up).
