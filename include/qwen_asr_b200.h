@@ -123,11 +123,14 @@ int qdb_decode_greedy(qdb_session *s, int first_token, int pos, int n_steps, int
 /* ---- Batched decode of independent utterances (no reference counterpart:
  * the reference decodes one utterance per process). Row b runs session
  * sessions[b] at position pos[b] with embedding row b of embeds (host f32
- * [n, hidden]); tokens_out[b] receives its greedy token. The model keeps a
- * CUDA graph of this step and replays it while n and its scratch are
- * unchanged; sessions and positions may differ from call to call. */
+ * [n, hidden]); tokens_out[b] receives its greedy token and logits_out
+ * (nullable, host f32 [n, vocab]) its final-layer logits. The model keeps a
+ * CUDA graph of this step and replays it while n, its scratch, the RoPE table
+ * and the EOS mask are unchanged; sessions and positions may differ from call
+ * to call. The projections accumulate split-K partials with atomics, so
+ * logits may differ between runs in the last bits (about 1e-6 relative). */
 int qdb_forward_batch(qdb_session *const *sessions, int n, const float *embeds,
-                      const int *pos, int *tokens_out);
+                      const int *pos, int *tokens_out, float *logits_out);
 
 /* Batched device-resident greedy loop over n sessions: row b starts from
  * first_tokens[b] at pos[b]; tokens_out is [n_steps, n] (host). Steps after

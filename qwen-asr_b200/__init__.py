@@ -56,7 +56,7 @@ ABI = {
     "qdb_prefill_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int]),
     "qdb_forward": (ctypes.c_int, [ctypes.c_void_p, _f32p, ctypes.c_int, _f32p, _f32p]),
     "qdb_decode_greedy": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _i32p]),
-    "qdb_forward_batch": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _f32p, _i32p, _i32p]),
+    "qdb_forward_batch": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _f32p, _i32p, _i32p, _f32p]),
     "qdb_decode_greedy_batch": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _i32p, _i32p,
                                                ctypes.c_int, _i32p]),
     "qdb_model_sync": (ctypes.c_int, [ctypes.c_void_p]),
@@ -227,14 +227,18 @@ def _handles(sessions):
     return arr
 
 
-def forward_batch(sessions, embeds: np.ndarray, pos) -> np.ndarray:
+def forward_batch(sessions, embeds: np.ndarray, pos, want_logits: bool = False):
+    """One decode step of independent sessions; returns the tokens, or
+    (tokens, logits [n, vocab]) with want_logits."""
     n = len(sessions)
     e = np.ascontiguousarray(embeds, dtype=np.float32)
     p = np.ascontiguousarray(pos, dtype=np.int32)
     out = np.empty(n, np.int32)
-    if lib.qdb_forward_batch(_handles(sessions), n, _ptr(e, _f32p), _ptr(p, _i32p), _ptr(out, _i32p)):
+    log = np.empty((n, sessions[0].model.cfg.vocab), np.float32) if want_logits else None
+    if lib.qdb_forward_batch(_handles(sessions), n, _ptr(e, _f32p), _ptr(p, _i32p), _ptr(out, _i32p),
+                             _ptr(log, _f32p) if log is not None else None):
         raise _err("qdb_forward_batch")
-    return out
+    return (out, log) if want_logits else out
 
 
 def decode_greedy_batch(sessions, first_tokens, pos, n_steps: int) -> np.ndarray:

@@ -58,12 +58,7 @@ struct QdbStepArgs {
 // Trace events of one step per CTA: start, then per layer A entered, A data
 // ready, B entered, C entered, C ready, D entered, D ready, E entered,
 // E ready; then F entered, F ready, end.
-#ifndef QDB_ATTN_STAMPS
-#define QDB_ATTN_STAMPS 0  // 1: six more stamps per layer inside attention units (debug builds)
-#endif
-__host__ __device__ static inline int qdb_step_trace_events(int layers) {
-    return 1 + 9 * layers + 3 + (QDB_ATTN_STAMPS ? 6 * layers : 0);
-}
+__host__ __device__ static inline int qdb_step_trace_events(int layers) { return 1 + 9 * layers + 3; }
 
 // Epochs one decode step consumes (host advances the base by this much).
 __host__ __device__ static inline unsigned qdb_step_epochs(int layers) { return 5u * (unsigned)layers + 1u; }
@@ -112,15 +107,12 @@ cudaError_t qdb_launch_qk_rope_append_single(const float *qkv, float *q_out, con
                                              int layer, int n, int Hq, int Hkv, const float *q_norm,
                                              const float *k_norm, const float2 *rope, float eps,
                                              cudaStream_t st);
-// Causal attention of n query rows of ONE session (rows at start_pos + i).
-// Same on the tensor cores (tcgen05); err: device error words (bounded waits).
+// Causal attention of n query rows of ONE session (rows at start_pos + i) on
+// the tensor cores (tcgen05); err: device error words (bounded waits).
 // hi/lo (optional): write the output as its bf16 split [n, Hq*128] instead of f32 out.
 cudaError_t qdb_launch_attn_prefill_tc(const float *q, const uint16_t *kc, const uint16_t *vc, int cap, int layer,
                                        int start_pos, int n, int Hq, int Hkv, float *out, int *err, cudaStream_t st,
                                        uint16_t *hi = nullptr, uint16_t *lo = nullptr);
-cudaError_t qdb_launch_attn_prefill(const float *q, const uint16_t *kc, const uint16_t *vc, int cap,
-                                    int layer, int start_pos, int n, int Hq, int Hkv, float *out,
-                                    cudaStream_t st);
 // Independent rows (one query each) over per-row caches.
 cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
                                  int n, int Hq, int Hkv, int splits, float *part, float *out,

@@ -114,267 +114,16 @@ __global__ void qk_rope_append_kernel(const float *qkv, float *q_out, const QdbR
     }
 }
 
-// ---------------------------------------------------------------- prefill attention
-// Causal GQA attention for n query rows of one session at positions
-// start_pos + i over keys [0, start_pos + i] (qwen_causal_attention with
-// q_offset = start_pos, qwen_asr_kernels.c:1050-1141). CTA = (query tile of
-// AQ rows, KV head g); its R*AQ query vectors share each K/V tile in smem.
-// Online softmax per query row over 64-key tiles.
-constexpr int AQ = 16;   // query rows per CTA
-constexpr int AK = 64;   // keys per tile
-
-template <int R>
-__global__ void __launch_bounds__(256) attn_prefill_kernel(const float *q, const uint16_t *kc, const uint16_t *vc,
-                                                           int cap, int layer, int start_pos, int n, int Hq,
-                                                           int Hkv, float *out) {
-    constexpr int NQ = R * AQ;         // query vectors per CTA
-    constexpr int TPQ = 256 / NQ;      // threads per query vector
-    extern __shared__ __align__(16) float sm[];
-    float *Qs = sm;                            // [NQ][128]
-    float *Ks = Qs + NQ * QDB_HD;              // [AK][129]
-    float *Vs = Ks + AK * (QDB_HD + 1);        // [AK][128]
-    float *Ps = Vs + AK * QDB_HD;              // [NQ][AK]
-    const int tid = threadIdx.x;
-    const int g = blockIdx.y;
-    const int i0 = blockIdx.x * AQ;
-    const int qv = tid / TPQ, sub = tid % TPQ;  // this thread's query vector and lane within it
-    const int qi = qv / R, hh = qv % R;         // row within tile, head within group
-    const int row = i0 + qi;
-    const bool row_ok = row < n;
-    const int qpos = start_pos + row;
-    const float scale = 1.0f / sqrtf((float)QDB_HD);
-
-    for (int t = tid; t < NQ * QDB_HD; t += 256) {
-        const int v = t / QDB_HD, dd = t % QDB_HD;
-        const int r = i0 + v / R, h = g * R + v % R;
-        Qs[t] = r < n ? q[(size_t)r * Hq * QDB_HD + (size_t)h * QDB_HD + dd] : 0.f;
-    }
-    constexpr int DPT = QDB_HD / TPQ;   // output dims per thread
-    constexpr int KPT = AK / TPQ;       // keys per thread per tile
-    float o[DPT];
-#pragma unroll
-    for (int e = 0; e < DPT; e++) o[e] = 0.f;
-    float m = -INFINITY, l = 0.f;
-
-    const size_t head_base = ((size_t)layer * Hkv + g) * (size_t)cap * QDB_HD;
-    const int last_row = min(n, i0 + AQ) - 1;
-    const int kend = start_pos + last_row + 1;  // keys needed by this tile
-    for (int k0 = 0; k0 < kend; k0 += AK) {
-        __syncthreads();
-        for (int t = tid; t < AK * QDB_HD / 8; t += 256) {
-            const int kr = t / (QDB_HD / 8), c8 = (t % (QDB_HD / 8)) * 8;
-            uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
-            if (k0 + kr < kend) {
-                kv = *reinterpret_cast<const uint4 *>(kc + head_base + (size_t)(k0 + kr) * QDB_HD + c8);
-                vv = *reinterpret_cast<const uint4 *>(vc + head_base + (size_t)(k0 + kr) * QDB_HD + c8);
-            }
-            float *kd = Ks + kr * (QDB_HD + 1) + c8;
-            kd[0] = kvlo(kv.x); kd[1] = kvhi(kv.x); kd[2] = kvlo(kv.y); kd[3] = kvhi(kv.y);
-            kd[4] = kvlo(kv.z); kd[5] = kvhi(kv.z); kd[6] = kvlo(kv.w); kd[7] = kvhi(kv.w);
-            float *vd = Vs + kr * QDB_HD + c8;
-            vd[0] = kvlo(vv.x); vd[1] = kvhi(vv.x); vd[2] = kvlo(vv.y); vd[3] = kvhi(vv.y);
-            vd[4] = kvlo(vv.z); vd[5] = kvhi(vv.z); vd[6] = kvlo(vv.w); vd[7] = kvhi(vv.w);
-        }
-        __syncthreads();
-        // scores for keys sub, sub+TPQ, ... of this tile
-        float sc[KPT];
-        float cmax = -INFINITY;
-        const float *qrow = Qs + qv * QDB_HD;
-#pragma unroll
-        for (int u = 0; u < KPT; u++) {
-            const int kr = sub + u * TPQ;
-            const float *krow = Ks + kr * (QDB_HD + 1);
-            float acc = 0.f;
-#pragma unroll 16
-            for (int dd = 0; dd < QDB_HD; dd++) acc = fmaf(qrow[dd], krow[dd], acc);
-            const bool ok = row_ok && (k0 + kr <= qpos);
-            sc[u] = ok ? acc * scale : -INFINITY;
-            cmax = fmaxf(cmax, sc[u]);
-        }
-#pragma unroll
-        for (int off = TPQ / 2; off > 0; off >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, off));
-        const float mn = fmaxf(m, cmax);
-        float psum = 0.f;
-#pragma unroll
-        for (int u = 0; u < KPT; u++) {
-            const float p = (sc[u] == -INFINITY) ? 0.f : expf(sc[u] - mn);
-            Ps[qv * AK + sub + u * TPQ] = p;
-            psum += p;
-        }
-#pragma unroll
-        for (int off = TPQ / 2; off > 0; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
-        const float corr = (m == -INFINITY) ? 0.f : expf(m - mn);
-        if (mn != -INFINITY) {
-            l = l * corr + psum;
-            m = mn;
-        }
-        __syncwarp();
-#pragma unroll
-        for (int e = 0; e < DPT; e++) o[e] *= (mn != -INFINITY ? corr : 1.f);
-        for (int kr = 0; kr < AK; kr++) {
-            const float p = Ps[qv * AK + kr];
-            const float *vrow = Vs + kr * QDB_HD + sub * DPT;
-#pragma unroll
-            for (int e = 0; e < DPT; e++) o[e] = fmaf(p, vrow[e], o[e]);
-        }
-    }
-    if (row_ok) {
-        const float inv = l > 0.f ? 1.0f / l : 0.f;
-        float *dst = out + (size_t)row * Hq * QDB_HD + (size_t)(g * R + hh) * QDB_HD + sub * DPT;
-#pragma unroll
-        for (int e = 0; e < DPT; e++) dst[e] = o[e] * inv;
-    }
-}
-
 // ---------------------------------------------------------------- independent-row attention
 // Unit = (row, KV head g, split s) = one CTA of 8 warps over keys [p0, p1)
-// of ctx = pos + 1 (at most 64 keys: one 8-key step per warp, every K/V load
-// in flight at once). Lanes: 4 per key over 32 dims for q.k, then 4 dims per
+// of ctx = pos + 1. Lanes: 4 per key over 32 dims for q.k, then 4 dims per
 // lane for p.V; the R query heads of the group share each K/V load. Writes
 // the unnormalised partial (m, l, o[128]) of each query head; the merge
 // kernel combines the splits (same online-softmax algebra as
 // qwen_causal_attention, qwen_asr_kernels.c:1050-1141).
-#ifndef QDB_AR_MINB
-#define QDB_AR_MINB 2  // resident CTAs per SM the attention kernel is register-capped for
-#endif
 constexpr int AR_WARPS = 8, AR_KEYS = 8;
 
-template <int R>
-__global__ void __launch_bounds__(AR_WARPS * 32, QDB_AR_MINB) attn_rows_partial_kernel(const float *q, const QdbRowKV *rows,
-                                                                          int row_pos_offset, int layer, int Hq,
-                                                                          int Hkv, int S, float *part,
-                                                                          const int *step) {
-    pdl_enter();
-    __shared__ __align__(16) float qs[R][QDB_HD];
-    __shared__ float sm_m[AR_WARPS][R], sm_l[AR_WARPS][R];
-    __shared__ __align__(16) float sm_o[AR_WARPS][R][QDB_HD];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int row = blockIdx.x / Hkv, g = blockIdx.x % Hkv, s = blockIdx.y;
-    const QdbRowKV rk = rows[row];
-    const int pos = rk.pos + row_pos_offset + (step ? *step : 0);
-    const int ctx = pos + 1;
-    const int per = (ctx + S - 1) / S;
-    const int p0 = s * per, p1 = min(ctx, p0 + per);
-    const size_t head_base = ((size_t)layer * Hkv + g) * (size_t)rk.cap * QDB_HD;
-    const uint16_t *kc = rk.kc + head_base, *vc = rk.vc + head_base;
-    for (int t = threadIdx.x; t < R * QDB_HD; t += blockDim.x)
-        qs[t / QDB_HD][t % QDB_HD] = q[(size_t)row * Hq * QDB_HD + (size_t)(g * R) * QDB_HD + t];
-    __syncthreads();
-    const float scale = 1.0f / sqrtf((float)QDB_HD);
-    const int sub = lane & 3, kk = lane >> 2;
-    float m[R], l[R], o[R][4];
-#pragma unroll
-    for (int h = 0; h < R; h++) {
-        m[h] = -INFINITY;
-        l[h] = 0.f;
-#pragma unroll
-        for (int e = 0; e < 4; e++) o[h][e] = 0.f;
-    }
-    // K/V of this warp's next 8-key step are loaded into registers before
-    // the current step's math (double buffering: loads stay in flight)
-    auto load_step = [&](int base, uint4 (&kv4)[4], uint2 (&vv)[AR_KEYS]) {
-        const int j = base + kk;
-        if (j < p1) {
-            const uint4 *kp = reinterpret_cast<const uint4 *>(kc + (size_t)j * QDB_HD + sub * 32);
-#pragma unroll
-            for (int u = 0; u < 4; u++) kv4[u] = __ldcs(kp + u);
-        }
-#pragma unroll
-        for (int t = 0; t < AR_KEYS; t++)
-            vv[t] = base + t < p1 ? __ldcs(reinterpret_cast<const uint2 *>(vc + (size_t)(base + t) * QDB_HD + lane * 4))
-                                  : make_uint2(0u, 0u);
-    };
-    uint4 kvA[4], kvB[4];
-    uint2 vvA[AR_KEYS], vvB[AR_KEYS];
-    int base = p0 + warp * AR_KEYS;
-    if (base < p1) load_step(base, kvA, vvA);
-    for (; base < p1; base += AR_WARPS * AR_KEYS) {
-        const int nb = base + AR_WARPS * AR_KEYS;
-        if (nb < p1) load_step(nb, kvB, vvB);
-        const uint4 *kv4 = kvA;
-        const uint2 *vv = vvA;
-        const int j = base + kk;
-        const bool valid = j < p1;
-#pragma unroll
-        for (int h = 0; h < R; h++) {
-            float a0 = 0.f, a1 = 0.f;
-            if (valid) {
-                const float *qv = qs[h] + sub * 32;
-#pragma unroll
-                for (int u = 0; u < 4; u += 2) {
-                    a0 = dot8_kv(kv4[u], *reinterpret_cast<const float4 *>(qv + u * 8),
-                                 *reinterpret_cast<const float4 *>(qv + u * 8 + 4), a0);
-                    a1 = dot8_kv(kv4[u + 1], *reinterpret_cast<const float4 *>(qv + u * 8 + 8),
-                                 *reinterpret_cast<const float4 *>(qv + u * 8 + 12), a1);
-                }
-            }
-            float acc = a0 + a1;
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-            const float sc = valid ? acc * scale : -INFINITY;
-            float cm = sc;
-            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
-            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
-            cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
-            const float mn = fmaxf(m[h], cm);
-            const float corr = expf(m[h] - mn);
-            const float p = valid ? expf(sc - mn) : 0.f;
-            float ps = p;
-            ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-            ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-            ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-            l[h] = l[h] * corr + ps;
-#pragma unroll
-            for (int e = 0; e < 4; e++) o[h][e] *= corr;
-#pragma unroll
-            for (int t = 0; t < AR_KEYS; t++) {
-                const float pt = __shfl_sync(0xffffffffu, p, t * 4);
-                o[h][0] = fmaf(pt, kvlo(vv[t].x), o[h][0]);
-                o[h][1] = fmaf(pt, kvhi(vv[t].x), o[h][1]);
-                o[h][2] = fmaf(pt, kvlo(vv[t].y), o[h][2]);
-                o[h][3] = fmaf(pt, kvhi(vv[t].y), o[h][3]);
-            }
-            m[h] = mn;
-        }
-#pragma unroll
-        for (int u = 0; u < 4; u++) kvA[u] = kvB[u];
-#pragma unroll
-        for (int t = 0; t < AR_KEYS; t++) vvA[t] = vvB[t];
-    }
-#pragma unroll
-    for (int h = 0; h < R; h++) {
-        if (lane == 0) {
-            sm_m[warp][h] = m[h];
-            sm_l[warp][h] = l[h];
-        }
-#pragma unroll
-        for (int e = 0; e < 4; e++) sm_o[warp][h][lane * 4 + e] = o[h][e];
-    }
-    __syncthreads();
-    for (int t = threadIdx.x; t < R * QDB_HD; t += blockDim.x) {
-        const int h = t / QDB_HD, dd = t % QDB_HD;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < AR_WARPS; w++) M = fmaxf(M, sm_m[w][h]);
-        float L = 0.f, O = 0.f;
-        if (M != -INFINITY) {
-#pragma unroll
-            for (int w = 0; w < AR_WARPS; w++) {
-                const float f = expf(sm_m[w][h] - M);
-                L += sm_l[w][h] * f;
-                O += sm_o[w][h][dd] * f;
-            }
-        }
-        float *dst = part + (((size_t)row * Hq + g * R + h) * S + s) * (2 + QDB_HD);
-        if (dd == 0) {
-            dst[0] = M;
-            dst[1] = L;
-        }
-        dst[2 + dd] = O;
-    }
-}
-
-// Same unit computed from a shared-memory ring: the unit's K and V rows are
+// The unit is computed from a shared-memory ring: the unit's K and V rows are
 // contiguous in the cache, so thread 0 streams them in 64-key chunks with
 // cp.async.bulk (3 stages x 32 KB, 2 CTAs per SM: ~190 KB in flight per SM)
 // and the 8 warps take 8 keys each per chunk. K chunks are read with the
@@ -664,48 +413,13 @@ extern "C" cudaError_t qdb_launch_qk_rope_append_single(const float *qkv, float 
 }
 
 template <int R>
-static cudaError_t attn_prefill_r(const float *q, const uint16_t *kc, const uint16_t *vc, int cap, int layer,
-                                  int start_pos, int n, int Hq, int Hkv, float *out, cudaStream_t st) {
-    constexpr int NQ = R * AQ;
-    const size_t smem = sizeof(float) * (NQ * QDB_HD + AK * (QDB_HD + 1) + AK * QDB_HD + NQ * AK);
-    cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-    dim3 grid((n + AQ - 1) / AQ, Hkv);
-    attn_prefill_kernel<R><<<grid, 256, smem, st>>>(q, kc, vc, cap, layer, start_pos, n, Hq, Hkv, out);
-    return cudaGetLastError();
-}
-
-extern "C" cudaError_t qdb_launch_attn_prefill(const float *q, const uint16_t *kc, const uint16_t *vc, int cap,
-                                               int layer, int start_pos, int n, int Hq, int Hkv, float *out,
-                                               cudaStream_t st) {
-    if (n <= 0) return cudaSuccess;
-    switch (Hq / Hkv) {
-        case 1: return attn_prefill_r<1>(q, kc, vc, cap, layer, start_pos, n, Hq, Hkv, out, st);
-        case 2: return attn_prefill_r<2>(q, kc, vc, cap, layer, start_pos, n, Hq, Hkv, out, st);
-        case 4: return attn_prefill_r<4>(q, kc, vc, cap, layer, start_pos, n, Hq, Hkv, out, st);
-        case 8: return attn_prefill_r<8>(q, kc, vc, cap, layer, start_pos, n, Hq, Hkv, out, st);
-        default: return cudaErrorInvalidValue;
-    }
-}
-
-#ifndef QDB_AR_BULK
-#define QDB_AR_BULK 1  // batched-decode attention from the bulk-copy ring (0: register-loading kernel)
-#endif
-template <int R>
 static cudaError_t attn_rows_launch(dim3 grid, const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
                                     int Hq, int Hkv, int S, float *part, int *err, cudaStream_t st, const int *step) {
-    if (QDB_AR_BULK) {
-        const int smem = AB_STAGES * AB_STAGE;
-        cudaError_t e = cudaFuncSetAttribute(attn_rows_bulk_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        return pdl_launch(attn_rows_bulk_kernel<R>, grid, dim3(AR_WARPS * 32), (size_t)smem, st, q, rows,
-                          row_pos_offset, layer, Hq, Hkv, S, part, err, step);
-    } else {
-        attn_rows_partial_kernel<R><<<grid, AR_WARPS * 32, 0, st>>>(q, rows, row_pos_offset, layer, Hq, Hkv, S, part,
-                                                                      step);
-    }
-    return cudaGetLastError();
+    const int smem = AB_STAGES * AB_STAGE;
+    cudaError_t e = cudaFuncSetAttribute(attn_rows_bulk_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    return pdl_launch(attn_rows_bulk_kernel<R>, grid, dim3(AR_WARPS * 32), (size_t)smem, st, q, rows, row_pos_offset,
+                      layer, Hq, Hkv, S, part, err, step);
 }
 
 extern "C" cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,

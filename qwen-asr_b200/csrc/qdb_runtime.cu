@@ -12,9 +12,6 @@
 
 #include <algorithm>
 
-#ifndef QDB_ATTN_TC
-#define QDB_ATTN_TC 1  // prefill attention on tcgen05 (0: the CUDA-core flash kernel)
-#endif
 #ifndef QDB_AR_ITERS
 #define QDB_AR_ITERS 8  // 8-key steps per warp of a batched-decode attention unit
 #endif
@@ -684,13 +681,8 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
         if (single) {
             CK(qdb_launch_qk_rope_append_single(r.QKV, r.Q, row0_dev, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
                                                 m->cfg.eps, m->st));
-            if (QDB_ATTN_TC) {
-                CK(qdb_launch_attn_prefill_tc(r.Q, s1->kc, s1->vc, s1->cap, l, start_pos, n, Hq, Hkv, r.ATT, r.err,
-                                              m->st, r.XH, r.XL));
-            } else {
-                CK(qdb_launch_attn_prefill(r.Q, s1->kc, s1->vc, s1->cap, l, start_pos, n, Hq, Hkv, r.ATT, m->st));
-                CK(qdb_launch_split_bf16(r.ATT, r.XH, r.XL, (size_t)n * m->qd, m->st));
-            }
+            CK(qdb_launch_attn_prefill_tc(r.Q, s1->kc, s1->vc, s1->cap, l, start_pos, n, Hq, Hkv, r.ATT, r.err, m->st,
+                                          r.XH, r.XL));
         } else {
             CK(qdb_launch_qk_rope_append(r.QKV, r.Q, row0_dev, pos_off, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
                                          m->cfg.eps, m->st, step));
@@ -798,7 +790,7 @@ static int ensure_tok(qdb_model *m, size_t count) {
 }
 
 extern "C" int qdb_forward_batch(qdb_session *const *sessions, int n, const float *embeds, const int *pos,
-                                 int *tokens_out) {
+                                 int *tokens_out, float *logits_out) {
     g_err.clear();
     qdb_model *m = nullptr;
     if (!embeds || !tokens_out) return fail("null argument");
@@ -808,8 +800,15 @@ extern "C" int qdb_forward_batch(qdb_session *const *sessions, int n, const floa
     RowScratch &r = m->rs;
     auto step = [&]() { return run_rows(m, n, false, r.rowkv, 0, nullptr, 0, maxp + 1) || batch_tail(m, n, r.tok); };
     const int S = std::min(64, std::max(1, (maxp + 1 + 64 * QDB_AR_ITERS - 1) / (64 * QDB_AR_ITERS)));
-    const std::vector<const void *> key = {(const void *)(intptr_t)n, (const void *)(intptr_t)S, r.X, r.XH, r.XL,
-                                           r.QKV, r.Q, r.ATT, r.ACT, r.LOG, r.part, r.GU, r.tok, r.err, r.rowkv};
+    // the captured launches bake in the row count, the split count, every
+    // scratch pointer, the RoPE table (reallocated when a session grows past
+    // it) and the EOS mask
+    auto graph_key = [&]() {
+        return std::vector<const void *>{(const void *)(intptr_t)n, (const void *)(intptr_t)S,
+                                         (const void *)(intptr_t)m->mask_eos, m->rope, r.X, r.XH, r.XL, r.QKV, r.Q,
+                                         r.ATT, r.ACT, r.LOG, r.part, r.GU, r.tok, r.err, r.rowkv};
+    };
+    const std::vector<const void *> key = graph_key();
     if (m->fb_exec && key == m->fb_key) {
         CK(cudaGraphLaunch(m->fb_exec, m->st));
     } else {
@@ -819,8 +818,7 @@ extern "C" int qdb_forward_batch(qdb_session *const *sessions, int n, const floa
         if (m->fb_exec) cudaGraphExecDestroy(m->fb_exec);
         m->fb_exec = nullptr;
         m->fb_key.clear();
-        const std::vector<const void *> key2 = {(const void *)(intptr_t)n, (const void *)(intptr_t)S, r.X, r.XH, r.XL,
-                                                r.QKV, r.Q, r.ATT, r.ACT, r.LOG, r.part, r.GU, r.tok, r.err, r.rowkv};
+        const std::vector<const void *> key2 = graph_key();
         cudaGraph_t graph = nullptr;
         if (cudaStreamBeginCapture(m->st, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
             const bool bad = step();
@@ -837,6 +835,9 @@ extern "C" int qdb_forward_batch(qdb_session *const *sessions, int n, const floa
         }
     }
     CK(cudaMemcpyAsync(tokens_out, m->rs.tok, sizeof(int) * n, cudaMemcpyDeviceToHost, m->st));
+    if (logits_out)
+        CK(cudaMemcpyAsync(logits_out, m->rs.LOG, sizeof(float) * (size_t)n * m->cfg.vocab, cudaMemcpyDeviceToHost,
+                           m->st));
     CK(cudaStreamSynchronize(m->st));
     return check_rows_err(m);
 }

@@ -52,15 +52,6 @@ constexpr int NTHREADS = NCT + 32;        // + producer warp
 #ifndef QDB_STAGES_PER_WARP
 #define QDB_STAGES_PER_WARP 2
 #endif
-#ifndef QDB_L2_AHEAD
-#define QDB_L2_AHEAD 0
-#endif
-#ifndef QDB_PRODUCER_LSU
-#define QDB_PRODUCER_LSU 0  // 1: the producer warp fills stages with per-lane 16-byte cp.async
-#endif
-#ifndef QDB_POLL_SLEEP_NS
-#define QDB_POLL_SLEEP_NS 0
-#endif
 constexpr int STAGE_BYTES = QDB_STAGE_BYTES;
 // Ring stages are owned by warps: item `it` goes to warp it % NCW and stage
 // it % NSTAGE with NSTAGE a multiple of NCW, so a stage is only ever reused
@@ -68,7 +59,6 @@ constexpr int STAGE_BYTES = QDB_STAGE_BYTES;
 // wait on a stage two mbarrier phases ahead, which a parity wait cannot tell
 // from "complete".)
 constexpr int NSTAGE = NCW * QDB_STAGES_PER_WARP;
-constexpr int L2_AHEAD = QDB_L2_AHEAD;    // items prefetched into L2 ahead of the ring (0 = off)
 constexpr int OWN_ROWS = 64;              // residual rows one CTA may own
 constexpr int MAX_LAYERS = 32;             // layer table kept in shared memory
 constexpr int ATT_KEYS = 8;               // keys per warp iteration
@@ -202,10 +192,6 @@ __device__ __forceinline__ void bulk_g2s_pol(void *dst, const void *src, unsigne
         : "memory");
 }
 
-__device__ __forceinline__ void prefetch_l2_pol(const void *src, unsigned bytes, uint64_t pol) {
-    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(src), "r"(bytes), "l"(pol) : "memory");
-}
-
 
 // Asynchronous 16-byte global -> shared copies (no registers held while the
 // thread goes on polling); completed with cp_async_wait().
@@ -298,50 +284,22 @@ __device__ __forceinline__ void cursor_next(const QdbStepArgs &a, const QdbLayer
     cursor_settle(a, layers, q);
 }
 
-#if QDB_PRODUCER_LSU
-__device__ __forceinline__ void cp_async16_cg(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_mbar_arrive(u64 *bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-#endif
-
 __device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *layers, unsigned char *ring, u64 *full,
                                       u64 *empty, const Ctl &c) {
-    const int lane = threadIdx.x & 31;
-#if !QDB_PRODUCER_LSU
-    if (lane != 0) return;
-#endif
+    if ((threadIdx.x & 31) != 0) return;
     uint64_t pol_w = 0;
     if (QDB_W_EVICT_FIRST) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_w));
-    Cursor ld, pf;
+    Cursor ld;
     cursor_init(a, layers, ld);
-    cursor_init(a, layers, pf);
-    unsigned it = 0, pf_it = 0;
+    unsigned it = 0;
     bool ok = true;
     for (; !ld.done && ok; cursor_next(a, layers, ld), it++) {
-        // keep the L2 prefetch cursor L2_AHEAD items ahead (no smem, no waits)
-        for (; L2_AHEAD > 0 && !pf.done && pf_it < it + L2_AHEAD; cursor_next(a, layers, pf), pf_it++)
-            if (pf_it >= it && lane == 0) {
-                const int nr = min(pf.s.ipr, pf.s.r1 - pf.r);
-                prefetch_l2_pol(pf.s.w + (size_t)pf.r * pf.s.K, (unsigned)(nr * pf.s.K * 2), pol_w);
-            }
         const int nr = min(ld.s.ipr, ld.s.r1 - ld.r);
         const unsigned st = it % NSTAGE;
-#if QDB_PRODUCER_LSU
-        int wok = 1;
-        if (lane == 0 && it >= NSTAGE) wok = mbar_wait(&empty[st], ((it / NSTAGE) - 1) & 1, c, true, 1) ? 1 : 0;
-        if (!__shfl_sync(0xffffffffu, wok, 0)) {
-            ok = false;
-            break;
-        }
-#else
         if (it >= NSTAGE && !mbar_wait(&empty[st], ((it / NSTAGE) - 1) & 1, c, true, 1)) {
             ok = false;
             break;
         }
-#endif
         const unsigned bytes = (unsigned)(nr * ld.s.K * 2);
         const uint16_t *src = ld.s.w + (size_t)ld.r * ld.s.K;
         const bool in_w = (src >= a.w_lo && src + (size_t)bytes / 2 <= a.w_hi);
@@ -353,14 +311,6 @@ __device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *lay
             ok = false;
             break;
         }
-#if QDB_PRODUCER_LSU
-        {
-            unsigned char *dst = ring + (size_t)st * STAGE_BYTES;
-            const unsigned char *sb = reinterpret_cast<const unsigned char *>(src);
-            for (unsigned off = lane * 16; off < bytes; off += 32 * 16) cp_async16_cg(dst + off, sb + off);
-            cp_async_mbar_arrive(&full[st]);
-        }
-#else
         mbar_expect_tx(&full[st], bytes);
         if (QDB_W_EVICT_FIRST)
             // each weight byte is read once per step: keep it from evicting the
@@ -368,9 +318,8 @@ __device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *lay
             bulk_g2s_pol(ring + (size_t)st * STAGE_BYTES, src, bytes, &full[st], pol_w);
         else
             bulk_g2s(ring + (size_t)st * STAGE_BYTES, src, bytes, &full[st]);
-#endif
     }
-    if (!ok && lane == 0) {
+    if (!ok) {
         // Drain: wait (bounded, ignoring the abort flag) for the copies in
         // flight, i.e. the latest item issued into each stage.
         for (unsigned k = 0; k < NSTAGE && k < it; k++) {
@@ -378,17 +327,11 @@ __device__ __noinline__ void producer(const QdbStepArgs &a, const QdbLayerW *lay
             mbar_wait(&full[i % NSTAGE], (i / NSTAGE) & 1, c, false, 2);
         }
     }
-#if QDB_PRODUCER_LSU
-    asm volatile("cp.async.wait_all;" ::: "memory");
-#endif
 }
 
 // ---------------------------------------------------------------- consumer helpers
 // Fills dst[0..n) from tagged words src expecting epoch ep (n <= POLL*NCT).
 // All still-missing words are re-read together each round.
-#ifndef QDB_POLL_WAVES
-#define QDB_POLL_WAVES 1  // poll rounds in flight per word (2: the next round is issued before this one is checked)
-#endif
 __device__ __noinline__ bool load_tagged(const u64 *src, int n, unsigned ep, float *dst, const Ctl &c, int site) {
     const int t = threadIdx.x;
     uint32_t pending = 0;
@@ -402,37 +345,6 @@ __device__ __noinline__ bool load_tagged(const u64 *src, int n, unsigned ep, flo
         }
     }
     const long long t0 = clock64();
-#if QDB_POLL_WAVES == 2
-    // Two rounds in flight: round k+1 is issued for the words still pending
-    // before round k is checked, so a word is seen about one L2 round trip
-    // after it lands instead of one and a half.
-    u64 w2[POLL];
-    auto check = [&](const u64 (&b)[POLL]) {
-#pragma unroll
-        for (int j = 0; j < POLL; j++)
-            if (((pending >> j) & 1u) && tag_ep(b[j]) == ep) {
-                dst[t + j * NCT] = tag_val(b[j]);
-                pending &= ~(1u << j);
-            }
-    };
-    for (int iter = 0;; iter += 2) {
-#pragma unroll
-        for (int j = 0; j < POLL; j++)
-            if ((pending >> j) & 1u) w2[j] = ld_tag(src + t + j * NCT);
-        check(w);
-        if (!pending) return true;
-#pragma unroll
-        for (int j = 0; j < POLL; j++)
-            if ((pending >> j) & 1u) w[j] = ld_tag(src + t + j * NCT);
-        check(w2);
-        if (!pending) return true;
-        if (should_stop(c, iter | 1)) return false;
-        if (timed_out(t0)) {
-            abort_now(c, site);
-            return false;
-        }
-    }
-#else
     for (int iter = 0;; iter++) {
 #pragma unroll
         for (int j = 0; j < POLL; j++)
@@ -448,12 +360,10 @@ __device__ __noinline__ bool load_tagged(const u64 *src, int n, unsigned ep, flo
             abort_now(c, site);
             return false;
         }
-        if (QDB_POLL_SLEEP_NS) __nanosleep(QDB_POLL_SLEEP_NS);
 #pragma unroll
         for (int j = 0; j < POLL; j++)
             if ((pending >> j) & 1u) w[j] = ld_tag(src + t + j * NCT);
     }
-#endif
 }
 
 // Consumer-wide sum; red has NCW floats.
@@ -490,9 +400,6 @@ __device__ void rmsnorm_smem(float *x, const float *w, int h, float eps, float *
 // elements: row pairs share the activation loads; an odd last row is split
 // into its two halves (when K is a multiple of 512) instead of being paired
 // with a duplicate of itself.
-#ifndef QDB_FFMA2
-#define QDB_FFMA2 1  // packed f32x2 FMAs (two weights per instruction)
-#endif
 typedef unsigned long long f32x2_t;  // two f32 in one 64-bit register pair
 __device__ __forceinline__ f32x2_t pk2(float lo, float hi) {
     f32x2_t r;
@@ -516,7 +423,6 @@ template <bool HALVES>
 __device__ __forceinline__ void dots2(const uint4 *p0, const uint4 *p1, const float *x0, int x1off, int nv,
                                       float &s0, float &s1) {
     const int lane = threadIdx.x & 31;
-#if QDB_FFMA2
     // two independent packed chains per stream (each FMA2 = two columns)
     f32x2_t a[2] = {0ull, 0ull}, b[2] = {0ull, 0ull};
 #pragma unroll 4
@@ -535,31 +441,6 @@ __device__ __forceinline__ void dots2(const uint4 *p0, const uint4 *p1, const fl
     }
     s0 = sum2(a[0]) + sum2(a[1]);
     s1 = sum2(b[0]) + sum2(b[1]);
-#else
-    // four independent accumulator chains per stream (the FMA latency of a
-    // single chain is what this latency-bound loop would otherwise wait on)
-    float a[4] = {0.f, 0.f, 0.f, 0.f}, b[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-    for (int j = 0; j < nv; j++) {
-        const int e = (j * 32 + lane);
-        const uint4 w0 = p0[e];
-        const uint4 w1 = p1[e];
-        const float4 xa = *reinterpret_cast<const float4 *>(x0 + e * 8);
-        const float4 xb = *reinterpret_cast<const float4 *>(x0 + e * 8 + 4);
-        const float4 ya = HALVES ? *reinterpret_cast<const float4 *>(x0 + x1off + e * 8) : xa;
-        const float4 yb = HALVES ? *reinterpret_cast<const float4 *>(x0 + x1off + e * 8 + 4) : xb;
-        a[0] = fmaf(bf16lo(w0.x), xa.x, a[0]); a[1] = fmaf(bf16hi(w0.x), xa.y, a[1]);
-        a[2] = fmaf(bf16lo(w0.y), xa.z, a[2]); a[3] = fmaf(bf16hi(w0.y), xa.w, a[3]);
-        a[0] = fmaf(bf16lo(w0.z), xb.x, a[0]); a[1] = fmaf(bf16hi(w0.z), xb.y, a[1]);
-        a[2] = fmaf(bf16lo(w0.w), xb.z, a[2]); a[3] = fmaf(bf16hi(w0.w), xb.w, a[3]);
-        b[0] = fmaf(bf16lo(w1.x), ya.x, b[0]); b[1] = fmaf(bf16hi(w1.x), ya.y, b[1]);
-        b[2] = fmaf(bf16lo(w1.y), ya.z, b[2]); b[3] = fmaf(bf16hi(w1.y), ya.w, b[3]);
-        b[0] = fmaf(bf16lo(w1.z), yb.x, b[0]); b[1] = fmaf(bf16hi(w1.z), yb.y, b[1]);
-        b[2] = fmaf(bf16lo(w1.w), yb.z, b[2]); b[3] = fmaf(bf16hi(w1.w), yb.w, b[3]);
-    }
-    s0 = (a[0] + a[1]) + (a[2] + a[3]);
-    s1 = (b[0] + b[1]) + (b[2] + b[3]);
-#endif
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         s0 += __shfl_xor_sync(0xffffffffu, s0, o);
@@ -567,9 +448,7 @@ __device__ __forceinline__ void dots2(const uint4 *p0, const uint4 *p1, const fl
     }
 }
 
-#ifndef QDB_DOT_GROUP
-#define QDB_DOT_GROUP 4  // rows per pass over K (activation loads are shared by the group)
-#endif
+constexpr int DOT_GROUP = 4;  // rows per pass over K (activation loads are shared by the group)
 // Dot products of NR consecutive rows (stride K) with act, all lanes end
 // with the sums in out[0..NR). One f32x2 chain per row, lanes stride 8.
 template <int NR>
@@ -603,16 +482,8 @@ __device__ __forceinline__ void dots_rows(const uint16_t *w, int K, const float 
 }
 
 __device__ __forceinline__ void stage_dots(const uint16_t *wst, int nr, int K, const float *act, float *out) {
-#if QDB_DOT_GROUP > 2
     int r = 0;
-    for (; r + QDB_DOT_GROUP <= nr; r += QDB_DOT_GROUP)
-        dots_rows<QDB_DOT_GROUP>(wst + (size_t)r * K, K, act, out + r);
-#if QDB_DOT_GROUP == 8
-    if (r + 4 <= nr) {
-        dots_rows<4>(wst + (size_t)r * K, K, act, out + r);
-        r += 4;
-    }
-#endif
+    for (; r + DOT_GROUP <= nr; r += DOT_GROUP) dots_rows<DOT_GROUP>(wst + (size_t)r * K, K, act, out + r);
     if (r + 2 <= nr) {
         dots_rows<2>(wst + (size_t)r * K, K, act, out + r);
         r += 2;
@@ -629,25 +500,6 @@ __device__ __forceinline__ void stage_dots(const uint16_t *wst, int nr, int K, c
             out[r] = s0;
         }
     }
-#else
-
-    const int nv = K >> 8;
-    for (int r = 0; r < nr; r += 2) {
-        const uint4 *p0 = reinterpret_cast<const uint4 *>(wst + (size_t)r * K);
-        float s0, s1;
-        if (r + 1 < nr) {
-            dots2<false>(p0, reinterpret_cast<const uint4 *>(wst + (size_t)(r + 1) * K), act, 0, nv, s0, s1);
-            out[r] = s0;
-            out[r + 1] = s1;
-        } else if ((nv & 1) == 0) {
-            dots2<true>(p0, p0 + (K >> 4), act, K >> 1, nv >> 1, s0, s1);
-            out[r] = s0 + s1;
-        } else {
-            dots2<false>(p0, p0, act, 0, nv, s0, s1);
-            out[r] = s0;
-        }
-    }
-#endif
 }
 
 // ---------------------------------------------------------------- attention
@@ -715,7 +567,6 @@ __device__ __forceinline__ bool warp_load_head(const u64 *src, unsigned ep, floa
             }
         }
         if (__shfl_sync(0xffffffffu, stop, 0)) return false;
-        if (QDB_POLL_SLEEP_NS) __nanosleep(QDB_POLL_SLEEP_NS);
 #pragma unroll
         for (int j = 0; j < 4; j++)
             if ((pending >> j) & 1u) w[j] = ld_tag(src + lane + 32 * j);
@@ -734,14 +585,6 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
                                        unsigned ep_in, AttnSmem<R> *sm, const Ctl &c) {
     const unsigned ep = ep_in + 1;
     const QdbDims &d = a.d;
-    auto astamp = [&](int k) {
-        if (QDB_ATTN_STAMPS && a.trace && threadIdx.x == 0) {
-            unsigned long long t;
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-            a.trace[(size_t)blockIdx.x * qdb_step_trace_events(d.L) + 1 + 9 * d.L + 3 + 6 * layer + k] = t;
-        }
-    };
-    astamp(0);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int ctx = a.pos + 1;
     const int per = (ctx + S - 1) / S;
@@ -784,7 +627,6 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
     }
     cp_async_wait();
     consumer_sync();
-    astamp(1);
 
     // q heads of this group (and the new K/V row for the owner), one warp each
     for (int h = warp; h < R + (owns_new ? 2 : 0); h += NCW) {
@@ -804,7 +646,6 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
         }
     }
     consumer_sync();  // new K/V row stored (global writes by this CTA are visible to it)
-    astamp(2);
 
     const float scale = 1.0f / sqrtf((float)QDB_HD);
     float m[R], l[R], o[R][4];
@@ -897,7 +738,6 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
         for (int e = 0; e < 4; e++) sm->o[warp][h][lane * 4 + e] = o[h][e];
     }
     consumer_sync();
-    astamp(3);
     // merge the warps; write the unit partial (m, l, o) tagged
     for (int t = threadIdx.x; t < R * QDB_HD; t += NCT) {
         const int h = t / QDB_HD, dd = t % QDB_HD;
@@ -920,7 +760,6 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
         }
         st_tag(dst + 2 + dd, O, ep);
     }
-    astamp(4);
     if (s != 0) return;
     // Split 0 merges all S partials of its KV head into attn. First one warp
     // per head polls every split's (m, l) at once and turns them into
@@ -984,7 +823,6 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
         if (lane == 0) sm->invl[h] = L > 0.f ? 1.0f / L : 0.f;
     }
     consumer_sync();
-    astamp(5);
     if (warp_aborted(c)) return;
     constexpr int MERGE_CHUNK = 16;
     for (int t = threadIdx.x; t < R * QDB_HD; t += NCT) {
@@ -1023,19 +861,11 @@ __device__ __noinline__ void attn_unit(const QdbStepArgs &a, const QdbLayerW &lw
     }
 }
 
-#ifndef QDB_ITEMS_NOINLINE
-#define QDB_ITEMS_NOINLINE 0
-#endif
 // One phase's ring items for this warp (items it % NCW == warp): row dots,
 // then the phase's epilogue. mode 0: QKV store, 1: O + residual, 2: gate/up
 // SwiGLU, 3: down + residual, 4: lm_head + running argmax. One out-of-line
 // copy serves every phase, which keeps the kernel's code small.
-#if QDB_ITEMS_NOINLINE
-__device__ __noinline__
-#else
-__device__ __forceinline__
-#endif
-void items_phase(const QdbStepArgs &a, const Slice &s, int mode, unsigned ep, u64 &best, unsigned &it,
+__device__ __forceinline__ void items_phase(const QdbStepArgs &a, const Slice &s, int mode, unsigned ep, u64 &best, unsigned &it,
                  unsigned char *ring, u64 *full, u64 *empty, const float *act, const float *xown, int own0,
                  float *outw, const Ctl &c) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1112,7 +942,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) step_kernel(const QdbStepArgs a) 
     if (threadIdx.x == 0) {
         s_abort = 0;
         for (int i = 0; i < NSTAGE; i++) {
-            mbar_init(&full[i], QDB_PRODUCER_LSU ? 32 : 1);
+            mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");

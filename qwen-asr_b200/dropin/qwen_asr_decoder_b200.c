@@ -5,8 +5,12 @@
  *
  * Build it INSTEAD of qwen_asr_decoder.c, against the reference's own
  * headers (qwen_asr.h, qwen_asr_safetensors.h), and link
- * libqwen_asr_b200.so. qwen_asr.c, main.c, the encoder, audio, tokenizer and
- * safetensors code are unchanged.
+ * libqwen_asr_b200.so. main.c, the encoder, audio, tokenizer and safetensors
+ * code are unchanged; qwen_asr.c needs one added line, a call of
+ * qwen_decoder_release(ctx) at the top of qwen_free (qwen_asr.c:253). Without
+ * that call every qwen_load / qwen_free cycle leaks the context's device model
+ * (about 1.2 GB at 0.6B, 3.4 GB at 1.7B) and one of the 16 binding slots;
+ * after 16 such cycles qwen_decoder_load fails ("too many live contexts").
  *
  *  qwen_decoder_load    (qwen_asr_decoder.c:45-116)  weights -> device once
  *  qwen_decoder_prefill (qwen_asr_decoder.c:262-359) appends at kv_cache_len
