@@ -1,31 +1,42 @@
 """Benchmark of the B200 decoder hot path (qwen-asr decoder token loop + prefill).
 
-Metric: decode tok/s per GPU as a fraction of the HBM roofline, plus
-end-to-end x-realtime of the decoder stage. Default workload = config c1
-(1.7B-shaped, batch 1, 30 s utterance -> 404-position prefill, 256 greedy
-tokens with EOS masked); --config c0 / c2 / c3 select the 0.6B batch-1, the
-0.6B 64-utterance and the 1.7B long-context (300 s) configurations.
+Metric: decode tok/s per GPU (b=1 and batched) as a fraction of
+the HBM roofline, plus end-to-end x-realtime of the decoder stage.
 
-One timed step = one utterance per rank (c2: this rank's shard of the 64
-utterances): prefill over the prompt embeddings followed by the greedy decode
-loop. `value` = decoded tokens / decode time, inputs resident in HBM (device
-embedding lookup, device greedy loop). `e2e` = the same metric through the
-reference-facing C ABI with host buffers: host f32 prompt embeddings (pinned),
-one host embedding in and one token out per decode step, exactly the
-qwen_asr.c:729-759 caller loop.
+Default workload = config c2: the 0.6B-shaped decoder, 64 independent
+utterances of 20 s (274-position prompts), 200 greedy tokens each with EOS
+masked, decoded as one batch and sharded evenly over the ranks (strong
+scaling: 64/N utterances per GPU, no collective on the data path). At N=1 the
+same JSON line carries a `b1` object with the batch-1 configs c0 (0.6B, 10 s,
+128 tokens) and c1 (1.7B, 30 s, 256 tokens) measured in the same run.
+`--config c0|c1|c3` makes a batch-1 config the headline instead (replicas on
+N>1, weak scaling).
+
+One timed step = this rank's utterances: prefill of every prompt followed by
+the greedy decode loop. `value` = decoded tokens (all ranks) / decode time
+(max over ranks), inputs resident in HBM (device embedding lookup, device
+greedy loop). `e2e` = the same metric through the reference-facing C ABI with
+host buffers: host f32 prompt embeddings (pinned) through qdb_prefill, then
+one host embedding row in and one token out per utterance per decode step
+(the qwen_asr.c:729-759 caller loop; qdb_forward_batch for batches).
 
 Weights and inputs are seeded synthetic data of the real shapes (no
 checkpoints offline). Weights (1.2 / 3.4 GB) exceed the 126 MB L2, so every
 step streams them from HBM; no flush is needed.
 
 --impl reference times the reference's own CPU decoder (oracle/_ref, built
-from the reference sources) on this host, bounded samples of the same workload.
+from the reference sources) on this host for the same config: the decode of
+one utterance (the reference decodes utterances one after another), sampled
+evenly over the whole decode context range of the config at every step. This
+arm never loads the CUDA library.
 """
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
 import os
+import socket
 import statistics
 import subprocess
 import sys
@@ -44,7 +55,9 @@ CONFIGS = {
     "c2": ("0.6b", 20.0, 200, 64),
     "c3": ("1.7b", 300.0, 1024, 1),
 }
-KV_BYTES_PER_POS = 28 * 8 * 128 * 2 * 2  # bf16 K and V per cached position (all layers)
+KV_BYTES_PER_POS = 28 * 8 * 128 * 2 * 2  # fp16 K and V per cached position (all layers)
+METRIC = "decode tok/s/GPU (b=1, b=64) as % of 8 TB/s HBM; end-to-end x-realtime"
+REF_WINDOWS = 8  # reference sample: windows spread evenly over the decode range
 
 
 def dist_env():
@@ -52,6 +65,19 @@ def dist_env():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return ws, rank, local
+
+
+def load_synth_standalone():
+    """synth.py by file path: the seeded weights and inputs without importing
+    the package (which loads the CUDA library)."""
+    name = "qdb_bench_synth"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, os.path.join(REPO, "qwen-asr_b200", "synth.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
 
 
 def measured_peaks():
@@ -126,44 +152,50 @@ def step_traffic_from_profile(kernel, workload):
     return None
 
 
-def build_inputs(synth, ws, cfg_name, rank, n_local, first_utt):
-    preset, seconds, steps, n_utt = CONFIGS[cfg_name]
-    embs = []
-    for u in range(first_utt, first_utt + n_local):
-        seed = 1 if n_utt == 1 else 100 + u
-        embs.append(synth.utterance(ws, seconds, seed))
-    return embs
+def utterance_seed(cfg_name, u):
+    return 1 if CONFIGS[cfg_name][3] == 1 else 100 + u
 
 
-def run_ours(args):
+def config_block(cfg_name, world, n_local, P):
+    preset, seconds, n_dec, n_utt = CONFIGS[cfg_name]
+    if n_utt > 1:
+        par = f"dp{world}: {n_utt} utterances split into contiguous blocks, no collective" if world > 1 else \
+            "single GPU"
+    else:
+        par = f"{world} independent replicas (one utterance does not shard)" if world > 1 else "single GPU"
+    return {"workload": f"{cfg_name}: {preset} decoder, {n_utt} utterance(s) of {seconds:g} s "
+                        f"-> prefill {P} positions + {n_dec} greedy tokens each (EOS masked)",
+            "global_batch": n_utt if n_utt > 1 else world, "per_gpu_batch": n_local, "prefill_len": P,
+            "decode_tokens": n_dec, "parallelism": par,
+            "l2": "weights (> 1 GB) exceed the 126 MB L2; no flush needed"}
+
+
+def weight_bytes(cfg):
+    h, L, V, I = cfg.hidden, cfg.layers, cfg.vocab, cfg.intermediate
+    qd, kvd = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
+    return 2 * (L * ((qd + 2 * kvd) * h + h * qd + 2 * I * h + h * I) + V * h)
+
+
+def measure(pkg, synth, cfg_name, world, rank, local, steps, warmup, clocks=None, e2e_steps=3):
+    """Times `steps` steps of cfg_name on this rank; returns a dict of device
+    times (ms, this rank) and what the JSON line needs."""
     import torch
-    import torch.distributed as dist
 
-    world, rank, local = dist_env()
-    if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    torch.cuda.set_device(local)
-    import __graft_entry__ as ge
-    pkg = ge.load_package()
-    synth = ge.load_synth()
-
-    preset, seconds, n_dec, n_utt = CONFIGS[args.config]
+    preset, seconds, n_dec, n_utt = CONFIGS[cfg_name]
     cfg = synth.PRESETS[preset]
     if n_utt > 1:
         import importlib
         shard = importlib.import_module("qwen_asr_b200.shard")
         first, n_local = shard.shard_range(n_utt, world, rank)
-        scaling = "strong"
     else:
-        n_local, first = 1, 0
-        scaling = "weak"  # batch-1 configs run one replica per GPU
+        first, n_local = 0, 1
     t0 = time.time()
     ws = synth.WeightSet(cfg, seed=0)
-    embs = build_inputs(synth, ws, args.config, rank, n_local, first)
+    embs = [synth.utterance(ws, seconds, utterance_seed(cfg_name, u)) for u in range(first, first + n_local)]
     P = embs[0].shape[0] - 1  # prefill length; the last prompt position is token 198
     last_tok = synth.PROMPT_SUFFIX[-1]
     model = pkg.Model(ws, device=local, mask_eos=True)
-    gen_s = time.time() - t0
+    setup_s = time.time() - t0
     stream = torch.cuda.ExternalStream(model.stream_handle, device=torch.device("cuda", local))
     cap = P + n_dec + 8
     sessions = [model.session(cap) for _ in range(n_local)]
@@ -184,21 +216,22 @@ def run_ours(args):
         timing.append(ev)
         return toks
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         one_step([])
     torch.cuda.synchronize()
     if world > 1:
+        import torch.distributed as dist
         dist.barrier()
     torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    clocks.start()
+    if clocks:
+        clocks.start()
     timing = []
     t_wall = time.time()
-    for _ in range(args.steps):
+    for _ in range(steps):
         one_step(timing)
     torch.cuda.synchronize()
     wall = time.time() - t_wall
-    clk = clocks.stop()
+    clk = clocks.stop() if clocks else None
     pre_ms = sum(e[0].elapsed_time(e[1]) for e in timing)
     dec_ms = sum(e[1].elapsed_time(e[2]) for e in timing)
     tot_ms = sum(e[0].elapsed_time(e[2]) for e in timing)
@@ -211,19 +244,15 @@ def run_ours(args):
     def e2e_step():
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         ev[0].record(stream)
-        toks_all = []
         for s, e in zip(sessions, pinned):
             s.prefill(e.numpy()[:-1], 0)
         ev[1].record(stream)
         if n_local == 1:
             s = sessions[0]
             x = pinned[0].numpy()[-1]
-            out = []
             for i in range(n_dec):
                 t, _, _ = s.forward(x, P + i)
-                out.append(t)
                 x = synth.bf16_to_f32(emb_tab[t])
-            toks_all.append(out)
         else:
             x = np.stack([p.numpy()[-1] for p in pinned])
             for i in range(n_dec):
@@ -234,82 +263,117 @@ def run_ours(args):
 
     e2e_step()  # warm
     e2e_ev.clear()
-    n_e2e = max(1, min(args.steps, 3))
-    for _ in range(n_e2e):
+    for _ in range(e2e_steps):
         e2e_step()
     torch.cuda.synchronize()
     e2e_dec_ms = sum(e[1].elapsed_time(e[2]) for e in e2e_ev)
     e2e_tot_ms = sum(e[0].elapsed_time(e[2]) for e in e2e_ev)
+    h = cfg.hidden
+    h2d = sum(e.numel() * 4 for e in pinned) - n_local * h * 4 + n_dec * n_local * h * 4
+    d2h = n_dec * n_local * 4
+    for s in sessions:
+        s.close()
+    model.close()
+    del emb_dev
+    torch.cuda.synchronize()
+    return dict(cfg=cfg, ws=ws, embs=embs, P=P, n_dec=n_dec, n_utt=n_utt, n_local=n_local, seconds=seconds,
+                pre_ms=pre_ms, dec_ms=dec_ms, tot_ms=tot_ms, e2e_dec_ms=e2e_dec_ms, e2e_tot_ms=e2e_tot_ms,
+                e2e_steps=e2e_steps, h2d=h2d, d2h=d2h, clk=clk, wall=wall, setup_s=setup_s)
 
-    # max over ranks
-    import importlib
-    shard = importlib.import_module("qwen_asr_b200.shard")
-    dec_ms, pre_ms, tot_ms, e2e_dec_ms, e2e_tot_ms = shard.max_over_ranks(
-        [dec_ms, pre_ms, tot_ms, e2e_dec_ms, e2e_tot_ms], device=f"cuda:{local}")
 
-    tokens_total = args.steps * n_dec * (n_utt if n_utt > 1 else world)
-    value = tokens_total / (dec_ms / 1e3)
-    e2e_value = (n_e2e * n_dec * (n_utt if n_utt > 1 else world)) / (e2e_dec_ms / 1e3)
-    # roofline of the dominant kernel (the persistent decode step at b=1; the
-    # batched decode step for c2): algorithmic bytes per launch / launch time
-    h, L, V, I = cfg.hidden, cfg.layers, cfg.vocab, cfg.intermediate
-    qd, kvd = cfg.heads * cfg.head_dim, cfg.kv_heads * cfg.head_dim
-    w_bytes = 2 * (L * ((qd + 2 * kvd) * h + h * qd + 2 * I * h + h * I) + V * h)
+def summarize(m, cfg_name, world, steps):
+    """Rates and roofline of one measure() result whose times are already the
+    max over ranks."""
+    n_dec, n_utt, n_local, P = m["n_dec"], m["n_utt"], m["n_local"], m["P"]
+    per_step_tokens = n_dec * (n_utt if n_utt > 1 else world)
+    value = steps * per_step_tokens / (m["dec_ms"] / 1e3)
+    e2e_value = m["e2e_steps"] * per_step_tokens / (m["e2e_dec_ms"] / 1e3)
     ctx_avg = P + (n_dec + 1) / 2.0
-    bytes_per_step = w_bytes + n_local * KV_BYTES_PER_POS * ctx_avg
-    launch_s = (dec_ms / 1e3) / (args.steps * n_dec)
+    bytes_per_step = weight_bytes(m["cfg"]) + n_local * KV_BYTES_PER_POS * ctx_avg
+    launch_s = (m["dec_ms"] / 1e3) / (steps * n_dec)
     achieved = bytes_per_step / launch_s / 1e9
     peak, peak_kind = measured_peaks()
     kernel = "step_kernel" if n_local == 1 else "rows_decode"
-    traffic = step_traffic_from_profile(kernel, args.config)
+    return dict(value=value, e2e_value=e2e_value, achieved=achieved, peak=peak, peak_kind=peak_kind,
+                frac=achieved / peak, kernel=kernel, bytes_per_step=bytes_per_step,
+                traffic=step_traffic_from_profile(kernel, cfg_name))
+
+
+def launches_per_step(cfg, n_local, n_dec):
     # per prefill, per layer: 2 norms, 4 GEMMs, q/k RoPE + KV append, attention, bf16 split of the
     # SwiGLU output; per batched decode step: embed, 10 per layer (2 norms, 4 GEMMs, RoPE/append,
     # attention units, split merge, SwiGLU split), final norm, lm_head GEMM, argmax, step advance;
     # b=1 decode: one persistent step kernel per token
-    launches_per_step = (L * 9) * n_local + (n_dec if n_local == 1 else n_dec * (L * 10 + 5))
-    h2d = sum(e.numel() * 4 for e in pinned) - n_local * h * 4 + n_dec * n_local * h * 4
-    d2h = n_dec * n_local * 4
+    L = cfg.layers
+    return (L * 9) * n_local + (n_dec if n_local == 1 else n_dec * (L * 10 + 5))
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_env()
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    torch.cuda.set_device(local)
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    synth = ge.load_synth()
+    import importlib
+    shard = importlib.import_module("qwen_asr_b200.shard")
+
+    m = measure(pkg, synth, args.config, world, rank, local, args.steps, args.warmup, clocks=ClockSampler(local))
+    keys = ["dec_ms", "pre_ms", "tot_ms", "e2e_dec_ms", "e2e_tot_ms"]
+    for k, v in zip(keys, shard.max_over_ranks([m[k] for k in keys], device=f"cuda:{local}")):
+        m[k] = v
+    r = summarize(m, args.config, world, args.steps)
+    n_local, seconds, steps = m["n_local"], m["seconds"], args.steps
+    n_utt = m["n_utt"]
     result = {
-        "metric": "decode tok/s/GPU (b=1, b=64) as % of HBM; end-to-end x-realtime",
-        "value": round(value, 2),
+        "metric": METRIC,
+        "value": round(r["value"], 2),
         "unit": "tok/s",
         "n_gpus": world,
-        "steps": args.steps,
+        "steps": steps,
         "warmup": args.warmup,
-        "ms_per_step": round(tot_ms / args.steps, 3),
+        "ms_per_step": round(m["tot_ms"] / steps, 3),
         "higher_is_better": True,
-        "scaling": scaling,
+        "scaling": "strong" if n_utt > 1 else "weak",
         "vs_baseline": None,
         "dtype": "bf16 weights x f32 activations (f32 accumulate), fp16 KV cache",
         "data": "synthetic: seeded random-init weights of the real shape, seeded prompt embeddings",
-        "config": {"workload": f"{args.config}: {preset} decoder, {n_utt} utterance(s) of {seconds:g} s "
-                               f"-> prefill {P} positions + {n_dec} greedy tokens (EOS masked)",
-                   "global_batch": n_utt, "per_gpu_batch": n_local, "prefill_len": P, "decode_tokens": n_dec,
-                   "parallelism": f"dp{world} (independent utterances, no collective)" if world > 1 else "single GPU",
-                   "l2": "weights (> 1 GB) exceed the 126 MB L2; no flush needed"},
-        "prefill_ms": round(pre_ms / args.steps, 3),
-        "decode_ms": round(dec_ms / args.steps, 3),
-        "decoder_x_realtime": round(seconds * n_local * args.steps / (tot_ms / 1e3), 2),
-        "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
-                "d2h_bytes_per_step": int(d2h),
-                "decoder_x_realtime": round(seconds * n_local * n_e2e / (e2e_tot_ms / 1e3), 2),
-                "path": "qdb_prefill + qdb_forward/qdb_forward_batch with host buffers"},
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": kernel, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                     "bytes_per_launch": int(bytes_per_step)},
-        "gpu_launches": int(launches_per_step * args.steps),
-        "clocks": clk,
-        "wall_s": round(wall, 3),
-        "setup_s": round(gen_s, 1),
+        "config": config_block(args.config, world, n_local, m["P"]),
+        "prefill_ms": round(m["pre_ms"] / steps, 3),
+        "decode_ms": round(m["dec_ms"] / steps, 3),
+        "decoder_x_realtime": round(seconds * (n_utt if n_utt > 1 else world) * steps / (m["tot_ms"] / 1e3), 2),
+        "e2e": {"value": round(r["e2e_value"], 2), "unit": "tok/s", "h2d_bytes_per_step": int(m["h2d"]),
+                "d2h_bytes_per_step": int(m["d2h"]),
+                "decoder_x_realtime": round(seconds * (n_utt if n_utt > 1 else world) * m["e2e_steps"]
+                                            / (m["e2e_tot_ms"] / 1e3), 2),
+                "path": "qdb_prefill + qdb_forward (b=1) / qdb_forward_batch (batches) with host buffers"},
+        "roofline": {"bound": "hbm", "achieved": round(r["achieved"], 1), "peak": r["peak"], "unit": "GB/s",
+                     "frac": round(r["frac"], 4), "traffic": r["traffic"], "kernel": r["kernel"],
+                     "peak_kind": f"{r['peak_kind']} (MEASURED_PEAKS.json hbm_gbs)",
+                     "bytes_per_launch": int(r["bytes_per_step"])},
+        "gpu_launches": int(launches_per_step(m["cfg"], n_local, m["n_dec"]) * steps),
+        "clocks": m["clk"],
+        "wall_s": round(m["wall"], 3),
+        "setup_s": round(m["setup_s"], 1),
     }
+    if rank == 0 and world == 1 and not args.no_b1 and args.config == "c2":
+        b1 = {}
+        for name in ("c0", "c1"):
+            mb = measure(pkg, synth, name, 1, 0, local, min(steps, 5), args.warmup, e2e_steps=2)
+            rb = summarize(mb, name, 1, min(steps, 5))
+            b1[name] = {"value": round(rb["value"], 2), "unit": "tok/s", "roofline_frac": round(rb["frac"], 4),
+                        "achieved_gbs": round(rb["achieved"], 1), "e2e": round(rb["e2e_value"], 2),
+                        "prefill_ms": round(mb["pre_ms"] / min(steps, 5), 3),
+                        "steps": min(steps, 5), "workload": config_block(name, 1, 1, mb["P"])["workload"]}
+        result["b1"] = b1
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(ws, embs[0], n_dec, args.config)
+        result["cpu_baseline"] = cpu_baseline(synth, m["ws"], m["embs"][0], args.config)
     if rank == 0:
         print(json.dumps(result), flush=True)
-    for s in sessions:
-        s.close()
-    model.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -319,97 +383,118 @@ def ref_threads():
     return max(1, min(os.cpu_count() or 1, 16))
 
 
-def cpu_baseline(ws, emb, n_dec, cfg_name, sample_tokens=24):
-    """Reference CPU decoder on this host: prefill + a bounded decode sample."""
-    from oracle.pyoracle import RefDecoder, Oracle
-    th = ref_threads()
-    try:
-        ref = RefDecoder(ws, threads=th)
-        kind = "reference"
-    except (FileNotFoundError, OSError):
-        ref = Oracle(ws, max_pos=emb.shape[0] + sample_tokens + 8, threads=th)
-        kind = "port"
-    P = emb.shape[0] - 1
-    t0 = time.perf_counter()
-    ref.prefill(emb[:-1])
-    pre_s = time.perf_counter() - t0
-    if kind == "reference":
-        _, ms = ref.decode_loop(198, sample_tokens, mask_eos=True)
-        dec_s = ms / 1e3
-    else:
+class RefSampler:
+    """The reference's own CPU decoder (oracle/_ref) on one utterance of the
+    config. Set-up (untimed): prefill, then the full greedy decode, which
+    fills the KV cache over the whole decode range and records the tokens.
+    A sample then re-decodes REF_WINDOWS windows of `per_window` tokens spread
+    evenly over that range (kv_cache_len rewound to each window's start, fed
+    the token the full decode produced there), so every timed token repeats a
+    step of the real run at its real context length."""
+
+    def __init__(self, synth, ws, emb, n_dec, threads):
+        from oracle.pyoracle import Oracle, RefDecoder
+        try:
+            self.ref = RefDecoder(ws, threads=threads)
+            self.kind = "reference"
+        except (FileNotFoundError, OSError):
+            self.ref = Oracle(ws, max_pos=emb.shape[0] + n_dec + 8, threads=threads)
+            self.kind = "port"
+        self.ws, self.n_dec = ws, n_dec
+        self.P = emb.shape[0] - 1
         t0 = time.perf_counter()
-        x = emb[-1]
-        for _ in range(sample_tokens):
-            t, _, _ = ref.forward(x, mask_eos=True, want_logits=False)
-            x = (ws.embed[t].astype(np.uint32) << 16).view(np.float32)
-        dec_s = time.perf_counter() - t0
-    ref.close()
-    return {"value": round(sample_tokens / dec_s, 3), "unit": "tok/s", "cores": th, "kind": kind,
-            "sample": f"{cfg_name}: prefill {P} positions ({pre_s:.2f} s) then {sample_tokens} greedy decode "
-                      f"tokens from position {P}; value = decode tokens / decode wall time",
-            "prefill_s": round(pre_s, 3), "host_nproc": os.cpu_count()}
+        self.ref.prefill(emb[:-1])
+        self.prefill_s = time.perf_counter() - t0
+        self.first = int(synth.PROMPT_SUFFIX[-1])
+        t0 = time.perf_counter()
+        self.tokens = self._decode(self.first, n_dec)
+        self.full_decode_s = time.perf_counter() - t0
+
+    def _decode(self, first, n):
+        if self.kind == "reference":
+            out, _ = self.ref.decode_loop(first, n, mask_eos=True)
+            return [int(t) for t in out]
+        out, tok = [], first
+        for _ in range(n):
+            x = (self.ws.embed[tok].astype(np.uint32) << 16).view(np.float32)
+            tok, _, _ = self.ref.forward(x, mask_eos=True, want_logits=False)
+            out.append(int(tok))
+        return out
+
+    def sample(self, per_window):
+        """Seconds for REF_WINDOWS x per_window decode tokens."""
+        total = 0.0
+        for w in range(REF_WINDOWS):
+            start = (w * self.n_dec) // REF_WINDOWS
+            self.ref.kv_cache_len = self.P + start
+            first = self.first if start == 0 else self.tokens[start - 1]
+            if self.kind == "reference":
+                _, ms = self.ref.decode_loop(first, per_window, mask_eos=True)
+                total += ms / 1e3
+            else:
+                t0 = time.perf_counter()
+                self._decode(first, per_window)
+                total += time.perf_counter() - t0
+        return total
+
+    def describe(self, steps, per_window):
+        return (f"one utterance (prefill {self.P} positions, {self.prefill_s:.2f} s, then the full {self.n_dec}-token "
+                f"greedy decode untimed); each step re-decodes {REF_WINDOWS} windows x {per_window} tokens spread "
+                f"evenly over decode positions {self.P}..{self.P + self.n_dec - 1}; {steps} steps timed")
+
+    def close(self):
+        self.ref.close()
+
+
+def cpu_baseline(synth, ws, emb, cfg_name, steps=2, per_window=3):
+    """Reference CPU decoder on this host: a bounded sample of the config."""
+    th = ref_threads()
+    n_dec = CONFIGS[cfg_name][2]
+    rs = RefSampler(synth, ws, emb, n_dec, th)
+    secs = sum(rs.sample(per_window) for _ in range(steps))
+    value = steps * REF_WINDOWS * per_window / secs
+    out = {"value": round(value, 3), "unit": "tok/s", "cores": th, "kind": rs.kind,
+           "sample": rs.describe(steps, per_window) + "; value = timed tokens / their decode wall time "
+                                                      "(one utterance at a time, the reference's mode)",
+           "prefill_s": round(rs.prefill_s, 3), "host_nproc": os.cpu_count()}
+    rs.close()
+    return out
 
 
 def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    import __graft_entry__ as ge
-    synth = ge.load_synth()
-    from oracle.pyoracle import RefDecoder, Oracle
+    synth = load_synth_standalone()
     preset, seconds, n_dec, n_utt = CONFIGS[args.config]
     cfg = synth.PRESETS[preset]
     ws = synth.WeightSet(cfg, seed=0)
-    emb = synth.utterance(ws, seconds, 1 if n_utt == 1 else 100)
+    # same per-GPU block as the GPU arm's rank 0 at this world size
+    n_local = -(-n_utt // world) if n_utt > 1 else 1
+    emb = synth.utterance(ws, seconds, utterance_seed(args.config, 0))
     th = ref_threads()
-    try:
-        ref = RefDecoder(ws, threads=th)
-        kind = "reference"
-    except (FileNotFoundError, OSError) as ex:
-        ref = Oracle(ws, max_pos=emb.shape[0] + 4096, threads=th)
-        kind = "port"
-    P = emb.shape[0] - 1
-    t0 = time.perf_counter()
-    ref.prefill(emb[:-1])
-    pre_s = time.perf_counter() - t0
-    per_step = 8  # decode tokens per timed step (bounded sample)
-    tok = 198
-    pos = P
-
-    def step():
-        nonlocal tok, pos
-        if kind == "reference":
-            ref.kv_cache_len = pos
-            out, ms = ref.decode_loop(tok, per_step, mask_eos=True)
-            return ms / 1e3
-        t0 = time.perf_counter()
-        x = (ws.embed[tok].astype(np.uint32) << 16).view(np.float32)
-        for _ in range(per_step):
-            t, _, _ = ref.forward(x, mask_eos=True, want_logits=False)
-            x = (ws.embed[t].astype(np.uint32) << 16).view(np.float32)
-        return time.perf_counter() - t0
-
+    per_window = 3
+    rs = RefSampler(synth, ws, emb, n_dec, th)
     for _ in range(args.warmup):
-        step()
-    times = [step() for _ in range(args.steps)]
+        rs.sample(per_window)
+    times = [rs.sample(per_window) for _ in range(args.steps)]
     dec_s = sum(times)
-    value = args.steps * per_step / dec_s
+    value = args.steps * REF_WINDOWS * per_window / dec_s
     res = {
         "impl": "reference",
-        "metric": "decode tok/s/GPU (b=1, b=64) as % of HBM; end-to-end x-realtime",
+        "metric": METRIC,
         "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(dec_s / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(dec_s / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong" if n_utt > 1 else "weak",
         "vs_baseline": None, "dtype": "f32 activations x bf16 weights (reference CPU path)",
         "data": "synthetic: seeded random-init weights of the real shape, seeded prompt embeddings",
-        "config": {"workload": f"{args.config}: {preset} decoder, reference CPU path, each step = {per_step} "
-                               f"greedy decode tokens continuing after a {P}-position prefill",
-                   "global_batch": 1, "prefill_len": P},
-        "prefill_ms": round(pre_s * 1e3, 1),
-        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": th, "kind": kind,
-                         "sample": f"{args.steps} steps x {per_step} tokens after a {P}-position prefill"},
+        "config": config_block(args.config, world, n_local, rs.P),
+        "prefill_ms": round(rs.prefill_s * 1e3, 1),
+        "cpu_baseline": {"value": round(value, 3), "unit": "tok/s", "cores": th, "kind": rs.kind,
+                         "sample": rs.describe(args.steps, per_window)},
         "e2e": {"value": round(value, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    ref.close()
+    rs.close()
     print(json.dumps(res), flush=True)
 
 
@@ -455,19 +540,34 @@ def profile_batch(args):
     print(toks[:4].tolist())
 
 
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="c1", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-b1", action="store_true", help="skip the in-line batch-1 (c0, c1) measurements")
     ap.add_argument("--profile-step", action="store_true", help="small fixed case for ncu (no timing)")
     ap.add_argument("--profile-batch", action="store_true", help="batched-decode case for ncu (no timing)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "0"))
+    if args.gpus > 1 and world == 0:
+        # --gpus N without a launcher: start one rank per GPU on this node
+        cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={args.gpus}",
+               "--master-addr=127.0.0.1", f"--master-port={free_port()}", os.path.abspath(__file__)] + sys.argv[1:]
+        sys.exit(subprocess.call(cmd))
+    if world and world != args.gpus:
+        print(f"bench.py: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE", file=sys.stderr)
     if args.profile_batch:
         profile_batch(args)
         return
