@@ -171,6 +171,24 @@ int qdb_trace_step(qdb_session *s, int token, int pos, unsigned long long *trace
  * same device driven concurrently) race and must not be issued. */
 int qdb_forward_noalloc(qdb_session *s, const float *embed_dev, int pos, int *token_dev);
 
+/* Bound on the kernels' data waits, in SM clock cycles (default about one
+ * second; cycles < 0 restores it). A kernel whose wait runs out records an
+ * error, stops and returns; the call then fails with "a bounded wait ... ran
+ * out" and the model stays usable. It applies to the waits of the persistent
+ * decode step (one CTA waiting for another CTA's results or for its weight
+ * copies) and of the tensor-core GEMMs (a stage's copies, a free stage); the
+ * waits that drain a CTA's own copies or MMAs before it exits keep the fixed
+ * one-second bound. The setting is per device (every model on the device of
+ * m), so it exists for tests of the error path and for callers that want a
+ * stuck step reported sooner. cycles = 0 makes a wait give up at its first
+ * unsuccessful check.
+ *
+ * Host-side failure injection, for tests of the callers' error handling: the
+ * environment variable QWEN_ASR_B200_FAULT (read at each call) holds a comma
+ * list of "alloc" (every device allocation of the library fails) and "launch"
+ * (every prefill / decode call fails before its first kernel launch). */
+int qdb_model_set_wait_limit(qdb_model *m, long long cycles);
+
 /* Waits for all queued work of the model's stream. */
 int qdb_model_sync(qdb_model *m);
 

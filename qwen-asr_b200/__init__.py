@@ -62,6 +62,7 @@ ABI = {
     "qdb_model_sync": (ctypes.c_int, [ctypes.c_void_p]),
     "qdb_forward_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "qdb_model_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
+    "qdb_model_set_wait_limit": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_longlong]),
     "qdb_trace_step": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                       ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]),
 }
@@ -134,6 +135,12 @@ class Model:
 
     def set_mask_eos(self, on: bool):
         lib.qdb_model_set_mask_eos(self.h, 1 if on else 0)
+
+    def set_wait_limit(self, cycles: int):
+        """Bound (SM cycles) on the kernels' data waits on this model's device;
+        negative restores the default (about one second)."""
+        if lib.qdb_model_set_wait_limit(self.h, int(cycles)):
+            raise _err("qdb_model_set_wait_limit")
 
     @property
     def stream_handle(self) -> int:

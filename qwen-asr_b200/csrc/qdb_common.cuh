@@ -16,8 +16,20 @@ enum {
     QDB_ERR_BOUNDS = 3,  // a self-check refused an access (details in err[1..3])
 };
 
-// About one second at the B200's ~1.9 GHz SM clock: the bound on every spin.
+// About one second at the B200's ~1.9 GHz SM clock: the default bound on
+// every spin, and the fixed bound on the waits that must not be cut short
+// (draining a CTA's own copies in flight, or its MMAs, before it exits).
 #define QDB_SPIN_LIMIT_CYCLES (2000000000ll)
+
+// Bound on the data waits (a CTA waiting for another CTA's results, or for
+// its own weight/activation copies to land), settable at run time per device
+// (qdb_model_set_wait_limit). Each translation unit holds its own copy in
+// constant memory and exports a setter (QDB_WAIT_LIMIT_SETTER).
+static __constant__ long long qdb_wait_limit_c = QDB_SPIN_LIMIT_CYCLES;
+#define QDB_WAIT_LIMIT_SETTER(name)                                               \
+    extern "C" cudaError_t name(long long cycles) {                               \
+        return cudaMemcpyToSymbol(qdb_wait_limit_c, &cycles, sizeof(cycles));     \
+    }
 
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }

@@ -73,6 +73,8 @@ struct QdbStepKernel {
     int (*smem_bytes)(const QdbDims &d);
     // Launches one persistent step. grid = co-resident CTAs (one per SM).
     cudaError_t (*launch)(const QdbStepArgs &a, int grid, cudaStream_t st);
+    // Sets this build's bound on data waits (cycles) on the current device.
+    cudaError_t (*set_wait_limit)(long long cycles);
 };
 
 extern "C" {
@@ -124,6 +126,8 @@ cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh, const uint
                                int mode, int splits, int *err, cudaStream_t st);
 cudaError_t qdb_launch_swiglu_split(const float *gu, uint16_t *hi, uint16_t *lo, size_t count, cudaStream_t st);
 int qdb_gemm_tc_splits(int n, int N, int K, int sms);
+// Bound (cycles) on the tensor-core GEMMs' data waits, current device.
+cudaError_t qdb_set_wait_limit_tcgemm(long long cycles);
 // step (optional, device): the rows' tokens are read at tokens + *step * n
 // (embed) / written at tokens + *step * n (argmax), and positions advance by
 // *step (qk_rope_append, attn_rows): the form a captured decode step replays.

@@ -46,9 +46,28 @@ static int fail(const char *fmt, ...) {
                                            __FILE__, __LINE__);                              \
     } while (0)
 
+// Host-side failure injection (tests of the error paths; no GPU fault is
+// involved): QWEN_ASR_B200_FAULT holds a comma list of "alloc" (every device
+// allocation of the library fails) and "launch" (every decode / prefill call
+// fails before its first kernel launch). Read at each call.
+static bool injected(const char *kind) {
+    const char *v = getenv("QWEN_ASR_B200_FAULT");
+    if (!v || !*v) return false;
+    const size_t n = strlen(kind);
+    for (const char *p = v; (p = strstr(p, kind)) != nullptr; p += n)
+        if ((p == v || p[-1] == ',') && (p[n] == 0 || p[n] == ',')) return true;
+    return false;
+}
+
+static int launch_gate() {
+    if (injected("launch")) return fail("injected launch failure (QWEN_ASR_B200_FAULT)");
+    return 0;
+}
+
 template <typename T>
 static int dev_alloc(T **p, size_t count) {
     *p = nullptr;
+    if (injected("alloc")) return fail("injected allocation failure (QWEN_ASR_B200_FAULT)");
     if (count == 0) count = 1;
     cudaError_t e = cudaMalloc((void **)p, count * sizeof(T));
     if (e != cudaSuccess) return fail("cudaMalloc(%zu bytes): %s", count * sizeof(T), cudaGetErrorString(e));
@@ -348,6 +367,17 @@ extern "C" int qdb_model_set_mask_eos(qdb_model *m, int enable) {
     return 0;
 }
 
+extern "C" int qdb_model_set_wait_limit(qdb_model *m, long long cycles) {
+    g_err.clear();
+    if (!m) return fail("null model");
+    if (set_dev(m)) return -1;
+    if (cycles < 0) cycles = 2000000000LL;  // the default: about one second of SM clock
+    CK(qdb_step_kernel_w6()->set_wait_limit(cycles));
+    CK(qdb_step_kernel_w7()->set_wait_limit(cycles));
+    CK(qdb_set_wait_limit_tcgemm(cycles));
+    return 0;
+}
+
 extern "C" void *qdb_model_stream(qdb_model *m) { return m ? (void *)m->st : nullptr; }
 
 extern "C" int qdb_model_sync(qdb_model *m) {
@@ -482,6 +512,7 @@ static QdbStepArgs step_args(qdb_session *s, int pos) {
 }
 
 static int launch_step(qdb_model *m, QdbStepArgs &a) {
+    if (launch_gate()) return -1;
     const unsigned span = qdb_step_epochs(m->cfg.layers);
     if (m->epoch > 0xffffffffu - 2 * span) {  // epoch wrap: clear the tags and restart
         CK(cudaMemsetAsync(m->tags, 0, m->tags_len * 8, m->st));
@@ -638,6 +669,7 @@ static int ensure_rows(qdb_model *m, int n, bool logits) {
 // rowkv[b] at position rowkv[b].pos + pos_off (multi-utterance decode).
 static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, int pos_off, const qdb_session *s1,
                     int start_pos, int max_ctx = 1, const int *step = nullptr) {
+    if (launch_gate()) return -1;
     RowScratch &r = m->rs;
     const int h = m->cfg.hidden, I = m->cfg.intermediate, Hq = m->cfg.heads, Hkv = m->cfg.kv_heads;
     const int qkvd = m->qd + 2 * m->kvd;
@@ -934,6 +966,7 @@ extern "C" int qdb_forward_noalloc(qdb_session *s, const float *embed_dev, int p
     // the argmax key, the completion counter and the error words start at zero
     CK(cudaMemsetAsync(tail, 0, 4 * sizeof(unsigned long long), m->st));
 
+    if (launch_gate()) return -1;
     QdbStepArgs a = step_args(s, pos);
     const size_t n_x = m->cfg.hidden, n_qkv = m->qd + 2 * m->kvd, n_attn = m->qd, n_act = m->cfg.intermediate;
     a.tx = base;

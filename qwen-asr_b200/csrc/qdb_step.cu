@@ -85,7 +85,9 @@ __device__ __forceinline__ u64 ld_tag(const u64 *p) {
 __device__ __forceinline__ unsigned tag_ep(u64 w) { return (unsigned)(w >> 32); }
 __device__ __forceinline__ float tag_val(u64 w) { return __uint_as_float((unsigned)w); }
 
-__device__ __forceinline__ bool timed_out(long long t0) { return clock64() - t0 > QDB_SPIN_LIMIT_CYCLES; }
+__device__ __forceinline__ bool timed_out(long long t0) { return clock64() - t0 > qdb_wait_limit_c; }
+// Drain waits (the producer's own copies in flight) keep the fixed bound.
+__device__ __forceinline__ bool drain_timed_out(long long t0) { return clock64() - t0 > QDB_SPIN_LIMIT_CYCLES; }
 
 // A wait ran out: raise the CTA abort flag and record the first failure with
 // its location (err[1] = wait site, err[2] = CTA, err[3] = warp).
@@ -141,13 +143,15 @@ __device__ __forceinline__ bool mbar_try(u64 *bar, unsigned parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait by ONE thread (the producer); `check` = honour the abort flag.
+// Bounded wait by ONE thread (the producer); `check` = honour the abort flag
+// and the run-time wait limit (a drain passes false: it ignores the abort flag
+// and waits up to the fixed bound).
 __device__ bool mbar_wait(u64 *bar, unsigned parity, const Ctl &c, bool check, int site) {
     const long long t0 = clock64();
     for (int it = 0;; it++) {
         if (mbar_try(bar, parity)) return true;
         if (check && should_stop(c, it)) return false;
-        if (timed_out(t0)) {
+        if (check ? timed_out(t0) : drain_timed_out(t0)) {
             abort_now(c, site);
             return false;
         }
@@ -1126,7 +1130,12 @@ cudaError_t launch_step(const QdbStepArgs &a, int grid, cudaStream_t st) {
     }
 }
 
-const QdbStepKernel k_entry = {QDB_STEP_NAME, NCW, STAGE_BYTES, POLL * NCT, step_smem_bytes, launch_step};
+cudaError_t set_wait_limit(long long cycles) {
+    return cudaMemcpyToSymbol(qdb_wait_limit_c, &cycles, sizeof(cycles));
+}
+
+const QdbStepKernel k_entry = {QDB_STEP_NAME, NCW, STAGE_BYTES, POLL * NCT, step_smem_bytes, launch_step,
+                               set_wait_limit};
 
 }  // namespace
 

@@ -49,11 +49,15 @@ __device__ __forceinline__ bool mb_try(u64 *b, unsigned par) {
                  : "memory");
     return ok != 0;
 }
-// Bounded wait of one thread; false = ran out (error recorded).
-__device__ bool mb_wait(u64 *b, unsigned par, int *err) {
+// Bounded wait of one thread; false = ran out (error recorded). Data waits
+// (a stage's copies, a free stage) use the run-time limit; the waits that must
+// not be cut short (the accumulator before TMEM is read and released, the
+// producer's copies in flight before it exits) pass fixed = true.
+__device__ bool mb_wait(u64 *b, unsigned par, int *err, bool fixed = false) {
     const long long t0 = clock64();
+    const long long limit = fixed ? QDB_SPIN_LIMIT_CYCLES : qdb_wait_limit_c;
     while (!mb_try(b, par)) {
-        if (clock64() - t0 > QDB_SPIN_LIMIT_CYCLES) {
+        if (clock64() - t0 > limit) {
             set_error(err, QDB_ERR_BARRIER_TIMEOUT);
             return false;
         }
@@ -210,7 +214,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             issued = kb + 1;
         }
         // wait for the last copies of every stage to land before leaving
-        for (int kb = issued > S ? issued - S : 0; kb < issued; kb++) mb_wait(&full[kb % S], (kb / S) & 1, err);
+        for (int kb = issued > S ? issued - S : 0; kb < issued; kb++) mb_wait(&full[kb % S], (kb / S) & 1, err, true);
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer
         constexpr uint32_t idesc = instr_desc(TC_BM, BN);
@@ -235,7 +239,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int q = warp & 3;
         asm volatile("griddepcontrol.wait;" ::: "memory");  // Y (residual / zeroed target) is the predecessors' output
         bool ok = true;
-        if (lane == 0) ok = mb_wait(&accum, 0, err);
+        if (lane == 0) ok = mb_wait(&accum, 0, err, true);
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         tc_fence_after();
         const int wrow = m0 + 32 * q + lane;
@@ -423,7 +427,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             }
         }
         // the copies of the last round of every stage land before leaving
-        for (unsigned i = it > (unsigned)S ? it - S : 0; i < it; i++) mb_wait(&full[i % S], (i / S) & 1, err);
+        for (unsigned i = it > (unsigned)S ? it - S : 0; i < it; i++) mb_wait(&full[i % S], (i / S) & 1, err, true);
     } else if (warp == 1 && lane == 0) {
         // ---- MMA issuer
         constexpr uint32_t idesc = instr_desc(TC_BM, BN);
@@ -461,7 +465,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         for (int tile = blockIdx.x; tile < ntile; tile += gridDim.x, tl++) {
             const int b = tl & 1;
             bool ok = true;
-            if (lane == 0) ok = mb_wait(&acc_full[b], (tl >> 1) & 1, err);
+            if (lane == 0) ok = mb_wait(&acc_full[b], (tl >> 1) & 1, err, true);
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             tc_fence_after();
@@ -538,6 +542,8 @@ cudaError_t launch_persist(const uint16_t *W, const uint16_t *Xh, const uint16_t
 }
 
 }  // namespace
+
+QDB_WAIT_LIMIT_SETTER(qdb_set_wait_limit_tcgemm)
 
 extern "C" cudaError_t qdb_launch_split_bf16(const float *x, uint16_t *hi, uint16_t *lo, size_t count,
                                              cudaStream_t st) {

@@ -9,6 +9,12 @@ can pin both the oracle restatement and the CUDA path on a machine without the
 reference tree.
 
 Run here (needs oracle/_ref built):  python tests/golden/make_golden.py
+  --small-only        only the three small shapes
+  --bench=c0,c1,...   only the named benchmark-length cases (c0 c1 c3 c2set)
+
+The benchmark-length cases record the reference's own prefill time
+(ref_prefill_s, with ref_threads threads): c3's 3914-position 1.7B prefill is
+the long one.
 """
 from __future__ import annotations
 
@@ -39,6 +45,18 @@ FULL_CASES = [
     ("1.7b", 0.0, 24, 1, 3),
 ]
 TOPK = 64
+# The benchmark configurations at their own prompt lengths (bench.py CONFIGS):
+# c0 = 0.6B, 10 s (130 audio rows); c1 = 1.7B, 30 s (390 rows); c3 = 1.7B,
+# 300 s (3900 rows). Tokens, top-64 logits and checksums of every step.
+BENCH_CASES = [
+    ("c0", "0.6b", 130, 1, 16),
+    ("c1", "1.7b", 390, 1, 16),
+    ("c3", "1.7b", 3900, 1, 4),
+]
+# A c2-shaped set: 8 independent 0.6B utterances of different lengths
+# (audio seeds 100..107, as bench.py's c2 seeds), 8 steps each.
+C2SET_AUDIO = [260, 200, 130, 65, 240, 100, 180, 30]
+C2SET_STEPS = 8
 
 
 def run_case(preset, jitter, n_audio, seed, steps, full_logits, threads):
@@ -85,18 +103,81 @@ def run_case(preset, jitter, n_audio, seed, steps, full_logits, threads):
     return out
 
 
+def summarize_steps(ref, ws, e, steps):
+    toks, tops, topi, sums, sqs, margins = [], [], [], [], [], []
+    for _ in range(steps):
+        tok, _, lg = ref.forward(e, mask_eos=True)
+        toks.append(tok)
+        margins.append(margin_top2(lg, mask_eos=True))
+        idx = np.argsort(-lg, kind="stable")[:TOPK]
+        topi.append(idx.astype(np.int32))
+        tops.append(lg[idx])
+        sums.append(float(lg.astype(np.float64).sum()))
+        sqs.append(float((lg.astype(np.float64) ** 2).sum()))
+        e = synth.embed_rows(ws, [tok])[0]
+    return dict(tokens=np.array(toks, np.int32), margins=np.array(margins), top_idx=np.array(topi),
+                top_val=np.array(tops, np.float32), logit_sum=np.array(sums), logit_sumsq=np.array(sqs))
+
+
+def run_bench_case(name, preset, n_audio, seed, steps, threads):
+    import time
+    cfg = synth.PRESETS[preset]
+    ws = synth.WeightSet(cfg, seed=0)
+    emb = synth.prompt_embeddings(ws, synth.audio_embeddings(cfg, n_audio, seed))
+    ref = RefDecoder(ws, threads=threads)
+    ref.kv_cache_len = 0
+    t0 = time.perf_counter()
+    ref.prefill(emb[:-1])
+    prefill_s = time.perf_counter() - t0
+    out = summarize_steps(ref, ws, emb[-1], steps)
+    ref.close()
+    out.update(preset=preset, norm_jitter=0.0, n_audio=n_audio, audio_seed=seed, weight_seed=0,
+               prefill_len=emb.shape[0] - 1, ref_prefill_s=prefill_s, ref_threads=threads)
+    return out
+
+
+def run_c2set(threads):
+    cfg = synth.PRESETS["0.6b"]
+    ws = synth.WeightSet(cfg, seed=0)
+    ref = RefDecoder(ws, threads=threads)
+    per = []
+    for b, n_audio in enumerate(C2SET_AUDIO):
+        emb = synth.prompt_embeddings(ws, synth.audio_embeddings(cfg, n_audio, 100 + b))
+        ref.kv_cache_len = 0
+        ref.prefill(emb[:-1])
+        per.append(summarize_steps(ref, ws, emb[-1], C2SET_STEPS))
+    ref.close()
+    out = {k: np.stack([p[k] for p in per]) for k in per[0]}
+    out.update(preset="0.6b", weight_seed=0, n_audio=np.array(C2SET_AUDIO, np.int32),
+               audio_seed=np.arange(100, 100 + len(C2SET_AUDIO), dtype=np.int32))
+    return out
+
+
 def main():
     threads = min(os.cpu_count() or 1, 16)
-    for case in SMALL_CASES:
+    for case in ([] if any(a.startswith("--bench=") for a in sys.argv) else SMALL_CASES):
         d = run_case(*case, full_logits=True, threads=threads)
         np.savez_compressed(os.path.join(HERE, f"ref_{case[0]}.npz"), **d)
         print("wrote", case[0], d["tokens"], d["margins"].round(4))
     if "--small-only" in sys.argv:
         return
-    for case in FULL_CASES:
+    only = [x for a in sys.argv if a.startswith("--bench=") for x in a.split("=", 1)[1].split(",")]
+    for case in ([] if only else FULL_CASES):
         d = run_case(*case, full_logits=False, threads=threads)
         np.savez_compressed(os.path.join(HERE, f"ref_{case[0]}.npz"), **d)
         print("wrote", case[0], d["tokens"], d["margins"].round(4))
+    if "--full-only" in sys.argv:
+        return
+    for case in BENCH_CASES:
+        if only and case[0] not in only:
+            continue
+        d = run_bench_case(*case, threads=threads)
+        np.savez_compressed(os.path.join(HERE, f"ref_{case[0]}.npz"), **d)
+        print("wrote", case[0], d["tokens"], d["margins"].round(4), "prefill %.1f s" % d["ref_prefill_s"])
+    if not only or "c2set" in only:
+        d = run_c2set(threads)
+        np.savez_compressed(os.path.join(HERE, "ref_c2set.npz"), **d)
+        print("wrote c2set", d["tokens"][:, :4])
 
 
 if __name__ == "__main__":

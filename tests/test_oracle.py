@@ -143,3 +143,25 @@ def test_kv_cache_format_against_reference_1p7b(synth, mode, within):
         worst = max(worst, float(np.abs(lg[g["top_idx"][step]] - g["top_val"][step]).max()))
         e = synth.embed_rows(ws, [int(want_tok)])[0]
     assert (worst <= 0.5 * 2e-2) == within, worst
+
+
+def test_oracle_at_bench_length_c0(synth):
+    """The C restatement against the reference at config c0's own length
+    (0.6B, 144-position prompt, 16 teacher-forced steps)."""
+    from conftest import MARGIN
+    from oracle.pyoracle import Oracle
+    g = golden("c0")
+    cfg = synth.PRESETS["0.6b"]
+    ws = synth.WeightSet(cfg, seed=0)
+    emb = synth.prompt_embeddings(ws, synth.audio_embeddings(cfg, int(g["n_audio"]), int(g["audio_seed"])))
+    o = Oracle(ws, max_pos=emb.shape[0] + 32)
+    o.prefill(emb[:-1])
+    e = emb[-1]
+    for step, want in enumerate(g["tokens"]):
+        tok, _, lg = o.forward(e, mask_eos=True)
+        d = np.abs(lg[g["top_idx"][step]] - g["top_val"][step]).max()
+        assert d <= 1e-3, (step, d)
+        if g["margins"][step] > MARGIN:
+            assert tok == want
+        e = synth.embed_rows(ws, [int(want)])[0]
+    o.close()

@@ -15,7 +15,7 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
-def test_noalloc_step_matches_forward_twice(pkg, synth):
+def test_noalloc_step_matches_forward_twice(pkg, synth, monkeypatch):
     import torch
 
     cfg = synth.PRESETS["small"]
@@ -27,14 +27,21 @@ def test_noalloc_step_matches_forward_twice(pkg, synth):
     ref.prefill(emb[:P], 0)
     nal.prefill(emb[:P], 0)
     tok_dev = torch.zeros(1, dtype=torch.int32, device="cuda:0")
-    for pos in (P, P + 1):  # two calls in a row: the shared scratch is reused
-        want, _, _ = ref.forward(emb[pos], pos)
-        e_dev = torch.from_numpy(np.ascontiguousarray(emb[pos])).to("cuda:0")
-        torch.cuda.synchronize()
-        rc = pkg.lib.qdb_forward_noalloc(nal.h, ctypes.c_void_p(e_dev.data_ptr()), pos,
+    wants = [ref.forward(emb[pos], pos)[0] for pos in (P, P + 1, P + 2)]
+    e_devs = [torch.from_numpy(np.ascontiguousarray(emb[pos])).to("cuda:0") for pos in (P, P + 1, P + 2)]
+    torch.cuda.synchronize()
+    for i, pos in enumerate((P, P + 1, P + 2)):  # calls in a row: the shared scratch is reused
+        free_before = torch.cuda.mem_get_info(0)[0]
+        if i:  # after the first call (its one-time set-up): any library allocation would now fail
+            monkeypatch.setenv("QWEN_ASR_B200_FAULT", "alloc")
+        rc = pkg.lib.qdb_forward_noalloc(nal.h, ctypes.c_void_p(e_devs[i].data_ptr()), pos,
                                          ctypes.c_void_p(tok_dev.data_ptr()))
+        monkeypatch.delenv("QWEN_ASR_B200_FAULT", raising=False)
         assert rc == 0, pkg.lib.qdb_last_error()
-        assert int(tok_dev.item()) == want, (pos, int(tok_dev.item()), want)
+        if i:
+            assert torch.cuda.mem_get_info(0)[0] == free_before, "device memory changed across the call"
+        assert int(tok_dev.item()) == wants[i], (pos, int(tok_dev.item()), wants[i])
+    e_dev = e_devs[0]
     # sizes the array cannot serve are refused with a clear error, not run
     rc = pkg.lib.qdb_forward_noalloc(nal.h, ctypes.c_void_p(e_dev.data_ptr()), 10_000,
                                      ctypes.c_void_p(tok_dev.data_ptr()))
