@@ -1,0 +1,1128 @@
+// qdb_bstep.cu - persistent batched decode step: one decode position of B
+// independent utterances (B <= 64) in ONE cooperative launch, the row dots on
+// the 5th-generation tensor cores. Per utterance it computes what
+// qwen_decoder_forward does (qwen_asr_decoder.c:388-476): 28 layers of
+// RMSNorm -> QKV -> per-head QK-norm + NeoX RoPE + KV append -> causal GQA
+// attention -> O + residual -> RMSNorm -> gate/up + SwiGLU -> down + residual,
+// then the final norm, the tied lm_head and the greedy argmax (lowest index
+// on exact ties, qwen_asr_kernels.c:518-543).
+//
+// One CTA per SM (cooperative: all CTAs co-resident). Warp roles:
+//   warp 0       producer: streams this CTA's slice of every weight matrix of
+//                the step (128-row x 64-column bf16 tiles, TMA with 128-byte
+//                swizzle, L2 evict-first) through a ring of W stages. It never
+//                waits for activations, so weights run ahead across phases.
+//   warp 1       allocates TMEM; one thread issues tcgen05.mma: D[128 weight
+//                rows, Bp utterances] += W[128, 64] . X[Bp, 64]^T, twice per
+//                k-step (X as bf16 hi + lo: ~16 mantissa bits of the f32
+//                activation), f32 accumulators in TMEM (8 slots of Bp columns).
+//   warps 2..5   epilogue: tcgen05.ld of a finished accumulator (warp q holds
+//                TMEM lanes 32q..32q+31 = weight rows), red.global.add.v4 of the
+//                split-K partial into the phase output (layout [row][Bp], so a
+//                thread's utterances are consecutive addresses), or, for the
+//                lm_head, scaled logits and a running (value, index) argmax.
+//                They also compute the per-utterance RMS statistics.
+//   warps 6..13  builders: turn the phase's f32 activations into the X tiles
+//                of the ring (bf16 hi/lo, 128-byte swizzle, written by threads,
+//                fence.proxy.async before the MMA reads them), and run the
+//                attention units between the QKV and O phases.
+//
+// Phases of a layer (each CTA takes an equal contiguous share of every
+// matrix's (tile, k-block) items; split-K partials meet in red.add targets):
+//   QKV   X = x * w_in (the 1/rms factor of the input norm is applied by the
+//         attention units: the projections are linear in it) -> qkv [qkvd][Bp]
+//   ATT   unit = (utterance, KV head, key split): q/k/v scaled by 1/rms, q/k
+//         RMSNorm + RoPE, fp16 K/V append at the position, online-softmax
+//         partial (m, l, o) over the split's keys
+//   O     X = merged attention output -> red.add into the residual x [h][Bp]
+//   GU    X = x * w_post -> gu [2I][Bp]
+//   DOWN  X = silu(r g) * (r u) (r = 1/rms of x after O) -> red.add into x
+// then LM: X = x * w_final, whole 128-row vocabulary tiles per CTA (no
+// split-K, kb-outer so one X tile serves up to 8 accumulators), logits scaled
+// by the final 1/rms, argmax per utterance.
+//
+// Phase completion is a counter per (phase, layer) that every CTA increments
+// once after its part (fence first); a reader polls it until it reaches the
+// grid size. RMS statistics are epoch-tagged 64-bit words. The last CTA to
+// finish clears the counters and the argmax keys and advances the step
+// counter, so the next launch (or graph replay) starts clean.
+//
+// Every wait is bounded (run-time limit); a wait that runs out records an
+// error, raises the CTA abort flag, and every role winds down: the producer
+// drains its copies in flight, the MMA thread waits for its MMAs before TMEM
+// is released (fixed bound), and the kernel returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "qdb_common.cuh"
+#include "qdb_kernels.h"
+
+namespace {
+
+typedef unsigned long long u64;
+
+constexpr int NWARPS = 14;
+constexpr int NTHREADS = NWARPS * 32;
+constexpr int EPI0 = 2, NEPI = 4;      // epilogue warps 2..5
+constexpr int BLD0 = 6, NBLD = 8;      // builder warps 6..13
+constexpr int NACC = 8;                // accumulator slots in TMEM
+constexpr int W_TILE = 128 * 64 * 2;   // one weight tile (16 KB)
+constexpr int MAX_NSW = 8;             // W ring stages (at most)
+constexpr int NSX = 4;                 // X ring stages
+constexpr int MAX_LAYERS = 32;
+constexpr int ATT_KEYS = 8;            // keys per builder warp per attention step
+constexpr int MAX_SPLITS = 8;          // key splits per (utterance, KV head)
+
+// ---------------------------------------------------------------- small helpers
+__device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+struct Ctl {
+    volatile int *abort;  // CTA-local
+    int *err;             // global [4]
+};
+
+__device__ __forceinline__ bool timed_out(long long t0) { return clock64() - t0 > qdb_wait_limit_c; }
+
+__device__ __forceinline__ void abort_now(const Ctl &c, int site) {
+    *c.abort = 1;
+    if (atomicCAS(c.err, 0, QDB_ERR_BARRIER_TIMEOUT) == 0) {
+        c.err[1] = site;
+        c.err[2] = blockIdx.x;
+        c.err[3] = threadIdx.x >> 5;
+    }
+}
+
+__device__ __forceinline__ bool should_stop(const Ctl &c, int iter) {
+    if (*c.abort) return true;
+    if ((iter & 255) == 255 && *(volatile int *)c.err) {
+        *c.abort = 1;
+        return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ bool warp_aborted(const Ctl &c) {
+    int v = 0;
+    if ((threadIdx.x & 31) == 0) v = *c.abort;
+    return __shfl_sync(0xffffffffu, v, 0) != 0;
+}
+
+__device__ __forceinline__ void mb_init(u64 *b, unsigned n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mb_arrive(u64 *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void mb_expect(u64 *b, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mb_try(u64 *b, unsigned par) {
+    uint32_t ok;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(ok)
+                 : "r"(su32(b)), "r"(par)
+                 : "memory");
+    return ok != 0;
+}
+// One thread. check: honour the abort flag and the run-time limit; otherwise
+// (drains) wait up to the fixed bound.
+__device__ bool mb_wait(u64 *b, unsigned par, const Ctl &c, bool check, int site) {
+    const long long t0 = clock64();
+    for (int it = 0;; it++) {
+        if (mb_try(b, par)) return true;
+        if (check && should_stop(c, it)) return false;
+        if (check ? timed_out(t0) : (clock64() - t0 > QDB_SPIN_LIMIT_CYCLES)) {
+            abort_now(c, site);
+            return false;
+        }
+    }
+}
+// Whole warp, uniform result; every lane observes the phase.
+__device__ bool mb_wait_warp(u64 *b, unsigned par, const Ctl &c, int site) {
+    const long long t0 = clock64();
+    for (int it = 0;; it++) {
+        const bool done = mb_try(b, par);
+        if (__all_sync(0xffffffffu, done)) return true;
+        int stop = 0;
+        if ((threadIdx.x & 31) == 0) {
+            stop = should_stop(c, it) ? 1 : 0;
+            if (!stop && timed_out(t0)) {
+                abort_now(c, site);
+                stop = 1;
+            }
+        }
+        if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+    }
+}
+
+// Phase counter: this CTA's part is done (the caller fenced its writes).
+__device__ __forceinline__ void signal(unsigned *cnt) { atomicAdd(cnt, 1u); }
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Warp-uniform bounded wait until *cnt >= target (lane 0 polls).
+__device__ bool wait_count_warp(const unsigned *cnt, unsigned target, const Ctl &c, int site) {
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0) {
+        const long long t0 = clock64();
+        for (int it = 0;; it++) {
+            if (ld_acquire(cnt) >= target) break;
+            if (should_stop(c, it) || (timed_out(t0) && (abort_now(c, site), true))) {
+                ok = 0;
+                break;
+            }
+        }
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    __syncwarp();
+    return ok != 0;
+}
+
+__device__ __forceinline__ void st_tag(u64 *p, float v, unsigned ep) {
+    const u64 w = ((u64)ep << 32) | (u64)__float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ u64 ld_tag(const u64 *p) {
+    u64 w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+// One lane polls one tagged word (bounded); returns the value, or 0 with the
+// abort flag raised.
+__device__ float poll_tag(const u64 *p, unsigned ep, const Ctl &c, int site) {
+    const long long t0 = clock64();
+    for (int it = 0;; it++) {
+        const u64 w = ld_tag(p);
+        if ((unsigned)(w >> 32) == ep) return __uint_as_float((unsigned)w);
+        if (should_stop(c, it)) return 0.f;
+        if (timed_out(t0)) {
+            abort_now(c, site);
+            return 0.f;
+        }
+    }
+}
+
+__device__ __forceinline__ void red_add_v4(float *p, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05 pieces
+__device__ __forceinline__ void tma_load_2d_pol(void *dst, const CUtensorMap *map, int x, int y, u64 *bar,
+                                                uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+        "%3}], [%4], %5;" ::"r"(su32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(su32(bar)), "l"(pol)
+        : "memory");
+}
+
+// K-major operand, rows of 128 bytes in 1024-byte 8-row atoms, 128-byte
+// swizzle (the layout the TMA writes for W and the builders write for X).
+__device__ __forceinline__ u64 sm_desc(uint32_t saddr) {
+    u64 d = 0;
+    d |= (u64)((saddr >> 4) & 0x3fffu);
+    d |= (u64)1 << 16;
+    d |= (u64)(1024 >> 4) << 32;
+    d |= (u64)1 << 46;
+    d |= (u64)2 << 61;
+    return d;
+}
+// kind::f16 instruction descriptor: D f32, A and B bf16, both K-major, N>>3 at
+// bit 17, M>>4 at bit 24.
+__device__ __forceinline__ uint32_t instr_desc(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ void mma_bf16(uint32_t tmem, u64 a, u64 b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(u64 *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 16 consecutive accumulator columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// ---------------------------------------------------------------- the work schedule
+// Matrix m of the step: 0..3 = QKV, O, GU, DOWN of a layer, 4 = lm_head.
+struct Mat {
+    int N, K, T, KB;
+};
+
+__device__ __forceinline__ Mat mat_of(const QdbDims &d, int m) {
+    const int qd = d.Hq * QDB_HD, kvd = d.Hkv * QDB_HD;
+    Mat r;
+    switch (m) {
+        case 0: r.N = qd + 2 * kvd; r.K = d.h; break;
+        case 1: r.N = d.h; r.K = qd; break;
+        case 2: r.N = 2 * d.I; r.K = d.h; break;
+        case 3: r.N = d.h; r.K = d.I; break;
+        default: r.N = d.V; r.K = d.h; break;
+    }
+    r.T = (r.N + 127) / 128;
+    r.KB = r.K / 64;
+    return r;
+}
+
+// This CTA's share of a split-K matrix: items [i0, i1) of T*KB (tile-major).
+__device__ __forceinline__ void share(const Mat &M, int &i0, int &i1) {
+    const long long n = (long long)M.T * M.KB;
+    i0 = (int)(n * blockIdx.x / gridDim.x);
+    i1 = (int)(n * (blockIdx.x + 1) / gridDim.x);
+}
+// lm_head: whole tiles [t0, t1).
+__device__ __forceinline__ void share_tiles(const Mat &M, int &t0, int &t1) {
+    t0 = (int)((long long)M.T * blockIdx.x / gridDim.x);
+    t1 = (int)((long long)M.T * (blockIdx.x + 1) / gridDim.x);
+}
+
+// Counter index of (layer, phase); phase 0..4 = QKV, ATT, O, GU, DOWN. Slot 0
+// is the set-up phase (embedding + clears).
+__device__ __forceinline__ int cidx(int layer, int ph) { return 1 + layer * 5 + ph; }
+
+struct Smem {
+    u64 wfull[MAX_NSW], wempty[MAX_NSW];
+    u64 xfull[NSX], xempty[NSX];
+    u64 accfull[NACC], accempty[NACC];
+    u64 mma_done;
+    uint32_t tmem;
+    int abort;
+};
+
+// ---------------------------------------------------------------- builders: X tiles
+// Writes the X tile (Bp rows = utterances, 64 columns = k0..k0+63) into the
+// stage as bf16 hi and lo with the 128-byte swizzle: element (b, k) at byte
+// (b/8)*1024 + (b%8)*128 + (((k/8) ^ (b%8)) * 16) + (k%8)*2. One warp per tile:
+// lane = utterance b (and b + 32). The f32 source value of (b, k0 + k) is
+// `fetch(k, b)`; for a fixed k the lanes read consecutive utterances, which the
+// [feature][Bp] layout of every activation buffer makes one coalesced access.
+template <typename F>
+__device__ __forceinline__ void build_tile(unsigned char *xs, int Bp, int B, F fetch) {
+    const int lane = threadIdx.x & 31;
+    unsigned char *hi = xs, *lo = xs + Bp * 128;
+    for (int b = lane; b < Bp; b += 32) {
+        const uint32_t rb = (uint32_t)(b >> 3) * 1024u + (uint32_t)(b & 7) * 128u;
+        float v[64];  // all 64 loads in flight before the first conversion
+        if (b < B) {
+#pragma unroll
+            for (int k = 0; k < 64; k++) v[k] = fetch(k, b);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 64; k++) v[k] = 0.f;
+        }
+#pragma unroll
+        for (int cc = 0; cc < 8; cc++) {
+            uint32_t h[4], l[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float v0 = v[cc * 8 + 2 * i], v1 = v[cc * 8 + 2 * i + 1];
+                const uint16_t h0 = f32_to_bf16_rn(v0), h1 = f32_to_bf16_rn(v1);
+                const uint16_t l0 = f32_to_bf16_rn(v0 - __uint_as_float((uint32_t)h0 << 16));
+                const uint16_t l1 = f32_to_bf16_rn(v1 - __uint_as_float((uint32_t)h1 << 16));
+                h[i] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+                l[i] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+            }
+            const uint32_t off = rb + (uint32_t)((cc ^ (b & 7)) * 16);
+            *reinterpret_cast<uint4 *>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<uint4 *>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+        }
+    }
+    // generic-proxy writes -> visible to the tensor core's async proxy
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+}
+
+// ---------------------------------------------------------------- attention scratch
+struct AttnSm {
+    float q[8][QDB_HD];      // up to R = 8 query heads of the group
+    float knew[QDB_HD], vnew[QDB_HD];
+    float qn[QDB_HD], kn[QDB_HD];
+    float2 rope[QDB_HD / 2];
+    float m[NBLD][8], l[NBLD][8];
+    float r1;
+};
+
+// Per-head RMSNorm then NeoX rotation of one 128-float head in smem, one warp
+// (qwen_rms_norm_per_head, qwen_asr_kernels.c:811-873; qwen_apply_rope_neox,
+// :1182-1247).
+__device__ __forceinline__ void head_norm_rope(float *v, const float *w, const float2 *rope_row, float eps) {
+    const int lane = threadIdx.x & 31;
+    float e[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) e[i] = v[lane + 32 * i];
+    const float ss = warp_sum(e[0] * e[0] + e[1] * e[1] + e[2] * e[2] + e[3] * e[3]);
+    const float inv = 1.0f / sqrtf(ss / (float)QDB_HD + eps);
+#pragma unroll
+    for (int i = 0; i < 4; i++) e[i] = e[i] * inv * w[lane + 32 * i];
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const float2 cs = rope_row[lane + 32 * i];
+        const float x1 = e[i], x2 = e[i + 2];
+        e[i] = x1 * cs.x - x2 * cs.y;
+        e[i + 2] = x2 * cs.x + x1 * cs.y;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[lane + 32 * i] = e[i];
+    __syncwarp();
+}
+
+__device__ __forceinline__ void bld_sync() { asm volatile("bar.sync 1, %0;" ::"n"(NBLD * 32) : "memory"); }
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 2, %0;" ::"n"(NEPI * 32) : "memory"); }
+__device__ __forceinline__ void work_sync() {  // builders + epilogue
+    asm volatile("bar.sync 3, %0;" ::"n"((NBLD + NEPI) * 32) : "memory");
+}
+
+// One attention unit (utterance b, KV head g, split s of S) by the 8 builder
+// warps: partial (m, l, o[128]) of each of the R query heads into part.
+template <int R>
+__device__ void attn_unit(const QdbBatchArgs &a, const QdbLayerW &lw, int layer, int b, int g, int s, int S,
+                          float r1, AttnSm *sm, float *obuf, const Ctl &c) {
+    const QdbDims &d = a.d;
+    const int lane = threadIdx.x & 31, warp = (threadIdx.x >> 5) - BLD0, t = threadIdx.x - BLD0 * 32;
+    const QdbRowKV rk = a.rows[b];
+    const int pos = rk.pos + a.step_base;
+    const int ctx = pos + 1;
+    const int per = (ctx + S - 1) / S;
+    const int p0 = s * per, p1 = min(ctx, p0 + per);
+    const int qd = d.Hq * QDB_HD, kvd = d.Hkv * QDB_HD;
+    const int Bp = a.Bp;
+    const size_t head_base = ((size_t)layer * d.Hkv + g) * (size_t)rk.cap * QDB_HD;
+    uint16_t *kc = rk.kc + head_base;
+    uint16_t *vc = rk.vc + head_base;
+    const bool owns_new = (p0 <= pos && pos < p1);
+    // q/k/v of this utterance (column b of qkv), times the input-norm factor
+    for (int i = t; i < (R + 2) * QDB_HD; i += NBLD * 32) {
+        const int hh = i / QDB_HD, dd = i % QDB_HD;
+        int row;
+        float *dst;
+        if (hh < R) {
+            row = (g * R + hh) * QDB_HD + dd;
+            dst = &sm->q[hh][dd];
+        } else if (hh == R) {
+            row = qd + g * QDB_HD + dd;
+            dst = &sm->knew[dd];
+        } else {
+            row = qd + kvd + g * QDB_HD + dd;
+            dst = &sm->vnew[dd];
+        }
+        *dst = __ldcg(a.qkv + (size_t)row * Bp + b) * r1;
+    }
+    for (int i = t; i < QDB_HD; i += NBLD * 32) {
+        sm->qn[i] = lw.q_norm[i];
+        sm->kn[i] = lw.k_norm[i];
+    }
+    for (int i = t; i < QDB_HD / 2; i += NBLD * 32) sm->rope[i] = a.rope[(size_t)pos * (QDB_HD / 2) + i];
+    bld_sync();
+    for (int hh = warp; hh < R + 1; hh += NBLD) {
+        if (hh < R) head_norm_rope(sm->q[hh], sm->qn, sm->rope, d.eps);
+        else head_norm_rope(sm->knew, sm->kn, sm->rope, d.eps);
+    }
+    bld_sync();
+    if (owns_new) {  // the new K/V row, rounded to the cache format
+        for (int i = t; i < QDB_HD; i += NBLD * 32) {
+            kc[(size_t)pos * QDB_HD + i] = f32_to_kv(sm->knew[i]);
+            vc[(size_t)pos * QDB_HD + i] = f32_to_kv(sm->vnew[i]);
+        }
+    }
+    const float scale = 1.0f / sqrtf((float)QDB_HD);
+    const int sub = lane & 3, kk = lane >> 2;
+    float m[R], l[R], o[R][4];
+#pragma unroll
+    for (int h = 0; h < R; h++) {
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; e++) o[h][e] = 0.f;
+    }
+    if (!warp_aborted(c)) {
+        for (int base = p0 + warp * ATT_KEYS; base < p1; base += NBLD * ATT_KEYS) {
+            const int j = base + kk;
+            const bool valid = j < p1;
+            uint4 kv4[4];
+            if (valid) {
+                if (j == pos) {  // this step's row, from smem (same rounding as the cache)
+                    const float *kn = sm->knew + sub * 32;
+#pragma unroll
+                    for (int u = 0; u < 4; u++)
+                        kv4[u] = make_uint4(kv_pack2(kn[u * 8 + 0], kn[u * 8 + 1]), kv_pack2(kn[u * 8 + 2], kn[u * 8 + 3]),
+                                            kv_pack2(kn[u * 8 + 4], kn[u * 8 + 5]), kv_pack2(kn[u * 8 + 6], kn[u * 8 + 7]));
+                } else {
+                    const uint4 *kp = reinterpret_cast<const uint4 *>(kc + (size_t)j * QDB_HD + sub * 32);
+#pragma unroll
+                    for (int u = 0; u < 4; u++) kv4[u] = __ldcg(kp + u);
+                }
+            }
+            uint2 vv[ATT_KEYS];
+#pragma unroll
+            for (int tt = 0; tt < ATT_KEYS; tt++) {
+                const int jt = base + tt;
+                if (jt >= p1) vv[tt] = make_uint2(0u, 0u);
+                else if (jt == pos)
+                    vv[tt] = make_uint2(kv_pack2(sm->vnew[lane * 4], sm->vnew[lane * 4 + 1]),
+                                        kv_pack2(sm->vnew[lane * 4 + 2], sm->vnew[lane * 4 + 3]));
+                else
+                    vv[tt] = __ldcg(reinterpret_cast<const uint2 *>(vc + (size_t)jt * QDB_HD + lane * 4));
+            }
+            float sc[R];
+#pragma unroll
+            for (int h = 0; h < R; h++) {
+                float acc = 0.f;
+                if (valid) {
+                    const float *qv = sm->q[h] + sub * 32;
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const float4 qa = *reinterpret_cast<const float4 *>(qv + u * 8);
+                        const float4 qb = *reinterpret_cast<const float4 *>(qv + u * 8 + 4);
+                        acc = dot8_kv(kv4[u], qa, qb, acc);
+                    }
+                }
+                acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+                acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+                sc[h] = valid ? acc * scale : -INFINITY;
+            }
+#pragma unroll
+            for (int h = 0; h < R; h++) {
+                float cm = sc[h];
+                cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 4));
+                cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 8));
+                cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, 16));
+                const float mn = fmaxf(m[h], cm);
+                const float corr = (mn == -INFINITY) ? 1.f : expf(m[h] - mn);
+                const float p = valid ? expf(sc[h] - mn) : 0.f;
+                float ps = p;
+                ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+                ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+                ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+                l[h] = l[h] * corr + ps;
+#pragma unroll
+                for (int e = 0; e < 4; e++) o[h][e] *= corr;
+#pragma unroll
+                for (int tt = 0; tt < ATT_KEYS; tt++) {
+                    const float pt = __shfl_sync(0xffffffffu, p, tt * 4);
+                    o[h][0] = fmaf(pt, kvlo(vv[tt].x), o[h][0]);
+                    o[h][1] = fmaf(pt, kvhi(vv[tt].x), o[h][1]);
+                    o[h][2] = fmaf(pt, kvlo(vv[tt].y), o[h][2]);
+                    o[h][3] = fmaf(pt, kvhi(vv[tt].y), o[h][3]);
+                }
+                m[h] = mn;
+            }
+        }
+    }
+    // merge the warps' partials; write the unit's partial of each query head
+#pragma unroll
+    for (int h = 0; h < R; h++) {
+        if (lane == 0) {
+            sm->m[warp][h] = m[h];
+            sm->l[warp][h] = l[h];
+        }
+#pragma unroll
+        for (int e = 0; e < 4; e++) obuf[((size_t)warp * R + h) * QDB_HD + lane * 4 + e] = o[h][e];
+    }
+    bld_sync();
+    for (int i = t; i < R * QDB_HD; i += NBLD * 32) {
+        const int h = i / QDB_HD, dd = i % QDB_HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NBLD; w++) M = fmaxf(M, sm->m[w][h]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < NBLD; w++) {
+                const float f = expf(sm->m[w][h] - M);
+                L += sm->l[w][h] * f;
+                O += obuf[((size_t)w * R + h) * QDB_HD + dd] * f;
+            }
+        }
+        float *dst = a.part + (((size_t)b * d.Hq + g * R + h) * S + s) * (2 + QDB_HD);
+        if (dd == 0) {
+            dst[0] = M;
+            dst[1] = L;
+        }
+        dst[2 + dd] = O;
+    }
+    bld_sync();  // smem reused by the next unit
+}
+
+// 1/rms of utterance b's residual column (h values, stride Bp), by one warp.
+__device__ float row_inv_rms(const float *x, int h, int Bp, int b, float eps) {
+    const int lane = threadIdx.x & 31;
+    float ss = 0.f;
+    for (int k = lane; k < h; k += 32) {
+        const float v = __ldcg(x + (size_t)k * Bp + b);
+        ss += v * v;
+    }
+    ss = warp_sum(ss);
+    return 1.0f / sqrtf(ss / (float)h + eps);
+}
+
+// ---------------------------------------------------------------- the kernel
+template <int R>
+__global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_dyn[];
+    __shared__ Smem S_;
+    __shared__ __align__(16) QdbLayerW layers[MAX_LAYERS];
+    __shared__ u64 lm_best[NEPI][64];  // per epilogue warp: best key per utterance (lm_head)
+    __shared__ float lm_r3[64];
+
+    const QdbDims &d = a.d;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int Bp = a.Bp, B = a.B, G = gridDim.x;
+    const int NSW = a.nsw;
+    unsigned char *smem = smem_dyn + ((1024u - (su32(smem_dyn) & 1023u)) & 1023u);
+    unsigned char *wring = smem;
+    unsigned char *xring = wring + (size_t)NSW * W_TILE;
+    const int XST = 2 * Bp * 128;  // one X stage: hi + lo
+    AttnSm *asm_ = reinterpret_cast<AttnSm *>(xring + (size_t)NSX * XST);
+    float *obuf = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(asm_) + sizeof(AttnSm));
+    const Ctl c{&S_.abort, a.err};
+    const unsigned ep = a.epoch;
+    const int step = a.step_base;
+
+    if (threadIdx.x == 0) {
+        S_.abort = 0;
+        for (int i = 0; i < NSW; i++) {
+            mb_init(&S_.wfull[i], 1);
+            mb_init(&S_.wempty[i], 1);
+        }
+        for (int i = 0; i < NSX; i++) {
+            mb_init(&S_.xfull[i], 1);
+            mb_init(&S_.xempty[i], 1);
+        }
+        for (int i = 0; i < NACC; i++) {
+            mb_init(&S_.accfull[i], 1);
+            mb_init(&S_.accempty[i], NEPI);
+        }
+        mb_init(&S_.mma_done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    {
+        const int words = d.L * (int)(sizeof(QdbLayerW) / 8);
+        const u64 *src = reinterpret_cast<const u64 *>(a.layers);
+        u64 *dst = reinterpret_cast<u64 *>(layers);
+        for (int i = threadIdx.x; i < words; i += NTHREADS) dst[i] = src[i];
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(su32(&S_.tmem))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = S_.tmem;
+    const int L = d.L;
+
+    if (warp == 0) {
+        // ================================================================ producer
+        if (lane == 0) {
+            uint64_t pol = 0;
+            asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+            unsigned wi = 0;
+            bool ok = true;
+            auto issue = [&](int mi, int tile, int kb) -> bool {
+                const int s = wi % NSW;
+                if (wi >= (unsigned)NSW && !mb_wait(&S_.wempty[s], ((wi / NSW) - 1) & 1, c, true, 1)) return false;
+                mb_expect(&S_.wfull[s], W_TILE);
+                tma_load_2d_pol(wring + (size_t)s * W_TILE, reinterpret_cast<const CUtensorMap *>(a.wmaps) + mi, kb * 64, tile * 128, &S_.wfull[s], pol);
+                wi++;
+                return true;
+            };
+            for (int layer = 0; layer < L && ok; layer++)
+                for (int m = 0; m < 4 && ok; m++) {
+                    const Mat M = mat_of(d, m);
+                    int i0, i1;
+                    share(M, i0, i1);
+                    for (int i = i0; i < i1 && ok; i++) ok = issue(layer * 4 + m, i / M.KB, i % M.KB);
+                }
+            if (ok) {
+                const Mat M = mat_of(d, 4);
+                int t0, t1;
+                share_tiles(M, t0, t1);
+                for (int r0 = t0; r0 < t1 && ok; r0 += NACC) {
+                    const int nt = min(NACC, t1 - r0);
+                    for (int kb = 0; kb < M.KB && ok; kb++)
+                        for (int j = 0; j < nt && ok; j++) ok = issue(4 * L, r0 + j, kb);
+                }
+            }
+            // drain: the latest copy issued into each stage lands before exit
+            for (unsigned k = 0; k < (unsigned)NSW && k < wi; k++) {
+                const unsigned i = wi - 1 - k;
+                mb_wait(&S_.wfull[i % NSW], (i / NSW) & 1, c, false, 2);
+            }
+        }
+    } else if (warp == 1) {
+        // ================================================================ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc(128, Bp);
+            unsigned wi = 0, xi = 0, seg = 0;
+            bool ok = true;
+            // one item: W stage wi x X stage xi into accumulator slot
+            auto item = [&](uint32_t acc, bool first, bool last_x) -> bool {
+                const int ws = wi % NSW, xs = xi % NSX;
+                if (!mb_wait(&S_.wfull[ws], (wi / NSW) & 1, c, true, 3)) return false;
+                if (!mb_wait(&S_.xfull[xs], (xi / NSX) & 1, c, true, 4)) return false;
+                tc_fence_after();
+                const uint32_t wb = su32(wring + (size_t)ws * W_TILE);
+                const uint32_t xb = su32(xring + (size_t)xs * XST);
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const u64 ad = sm_desc(wb + k * 32);
+                    mma_bf16(acc, ad, sm_desc(xb + k * 32), idesc, (first && k == 0) ? 0u : 1u);
+                    mma_bf16(acc, ad, sm_desc(xb + Bp * 128 + k * 32), idesc, 1u);
+                }
+                mma_commit(&S_.wempty[ws]);
+                wi++;
+                if (last_x) {
+                    mma_commit(&S_.xempty[xs]);
+                    xi++;
+                }
+                return true;
+            };
+            auto begin_seg = [&](unsigned sg) -> bool {
+                const int slot = sg % NACC;
+                if (sg >= (unsigned)NACC &&
+                    !mb_wait(&S_.accempty[slot], ((sg / NACC) - 1) & 1, c, true, 5))
+                    return false;
+                tc_fence_after();
+                return true;
+            };
+            for (int layer = 0; layer < L && ok; layer++)
+                for (int m = 0; m < 4 && ok; m++) {
+                    const Mat M = mat_of(d, m);
+                    int i0, i1;
+                    share(M, i0, i1);
+                    for (int i = i0; i < i1 && ok;) {
+                        const int tile = i / M.KB;
+                        const int iend = min(i1, (tile + 1) * M.KB);
+                        if (!(ok = begin_seg(seg))) break;
+                        const uint32_t acc = tmem + (uint32_t)((seg % NACC) * Bp);
+                        for (int k = i; k < iend && ok; k++) ok = item(acc, k == i, true);
+                        if (ok) mma_commit(&S_.accfull[seg % NACC]);
+                        seg++;
+                        i = iend;
+                    }
+                }
+            if (ok) {
+                const Mat M = mat_of(d, 4);
+                int t0, t1;
+                share_tiles(M, t0, t1);
+                for (int r0 = t0; r0 < t1 && ok; r0 += NACC) {
+                    const int nt = min(NACC, t1 - r0);
+                    for (int j = 0; j < nt && ok; j++) ok = begin_seg(seg + j);
+                    for (int kb = 0; kb < M.KB && ok; kb++)
+                        for (int j = 0; j < nt && ok; j++)
+                            ok = item(tmem + (uint32_t)(((seg + j) % NACC) * Bp), kb == 0, j == nt - 1);
+                    for (int j = 0; j < nt && ok; j++) mma_commit(&S_.accfull[(seg + j) % NACC]);
+                    seg += nt;
+                }
+            }
+            // every MMA issued by this thread completes before TMEM is released
+            mma_commit(&S_.mma_done);
+            mb_wait(&S_.mma_done, 0, c, false, 6);
+        }
+    } else if (warp < BLD0) {
+        // ================================================================ epilogue
+        const int q = warp & 3;  // TMEM lanes 32q..32q+31
+        const int et = threadIdx.x - EPI0 * 32;
+        unsigned seg = 0;
+        bool ok = true;
+        // waits for accumulator slot of segment sg; uniform over the warp
+        auto acc_ready = [&](unsigned sg) -> bool {
+            if (!ok || warp_aborted(c)) return false;
+            if (!mb_wait_warp(&S_.accfull[sg % NACC], (sg / NACC) & 1, c, 7)) return false;
+            tc_fence_after();
+            return true;
+        };
+        auto acc_release = [&](unsigned sg) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mb_arrive(&S_.accempty[sg % NACC]);
+        };
+        auto phase_done = [&](int idx) {
+            __threadfence();
+            epi_sync();
+            if (et == 0) signal(a.cnt + idx);
+        };
+        // ---- set-up: clear the accumulation targets of layer 0 (qkv, gu)
+        {
+            const size_t nq = (size_t)(d.Hq + 2 * d.Hkv) * QDB_HD * Bp, ng = (size_t)2 * d.I * Bp;
+            const size_t q0 = nq * blockIdx.x / G, q1 = nq * (blockIdx.x + 1) / G;
+            const size_t g0 = ng * blockIdx.x / G, g1 = ng * (blockIdx.x + 1) / G;
+            for (size_t i = q0 + et; i < q1; i += NEPI * 32) a.qkv[i] = 0.f;
+            for (size_t i = g0 + et; i < g1; i += NEPI * 32) a.gu[i] = 0.f;
+        }
+        __threadfence();
+        work_sync();  // with the builders' embedding writes: then one signal
+        for (int layer = 0; layer < L; layer++) {
+            for (int m = 0; m < 4; m++) {
+                const Mat M = mat_of(d, m);
+                float *out = m == 0 ? a.qkv : (m == 2 ? a.gu : a.x);
+                if (m == 0 && (int)blockIdx.x < B) {
+                    // input-norm statistic of utterance blockIdx.x (after the previous layer)
+                    if (warp == EPI0 && wait_count_warp(a.cnt + (layer ? cidx(layer - 1, 4) : 0), G, c, 20)) {
+                        const float r = row_inv_rms(a.x, d.h, Bp, blockIdx.x, d.eps);
+                        if (lane == 0) st_tag(a.stats + ((size_t)layer * 3 + 0) * 64 + blockIdx.x, r, ep);
+                    }
+                }
+                if (m == 1) {
+                    // attention of this layer is complete everywhere: qkv is free, and so is gu
+                    // (read by the previous layer's down builders): clear this CTA's slices
+                    if (wait_count_warp(a.cnt + cidx(layer, 1), G, c, 21)) {
+                        const size_t nq = (size_t)(d.Hq + 2 * d.Hkv) * QDB_HD * Bp, ng = (size_t)2 * d.I * Bp;
+                        const size_t q0 = nq * blockIdx.x / G, q1 = nq * (blockIdx.x + 1) / G;
+                        const size_t g0 = ng * blockIdx.x / G, g1 = ng * (blockIdx.x + 1) / G;
+                        for (size_t i = q0 + et; i < q1; i += NEPI * 32) a.qkv[i] = 0.f;
+                        if (layer > 0)
+                            for (size_t i = g0 + et; i < g1; i += NEPI * 32) a.gu[i] = 0.f;
+                    }
+                }
+                if (m == 2 && (int)blockIdx.x < B) {
+                    // post-attention-norm statistic (x after this layer's O)
+                    if (warp == EPI0 && wait_count_warp(a.cnt + cidx(layer, 2), G, c, 22)) {
+                        const float r = row_inv_rms(a.x, d.h, Bp, blockIdx.x, d.eps);
+                        if (lane == 0) st_tag(a.stats + ((size_t)layer * 3 + 1) * 64 + blockIdx.x, r, ep);
+                    }
+                }
+                int i0, i1;
+                share(M, i0, i1);
+                for (int i = i0; i < i1;) {
+                    const int tile = i / M.KB;
+                    const int iend = min(i1, (tile + 1) * M.KB);
+                    if (acc_ready(seg)) {
+                        const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((seg % NACC) * Bp);
+                        const int row = tile * 128 + 32 * q + lane;
+                        float *dst = out + (size_t)row * Bp;
+                        for (int c0 = 0; c0 < Bp; c0 += 16) {
+                            float v[16];
+                            tmem_ld16(tbase + (uint32_t)c0, v);
+                            if (row < M.N)
+#pragma unroll
+                                for (int j = 0; j < 16; j += 4) red_add_v4(dst + c0 + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        }
+                    } else {
+                        ok = false;
+                    }
+                    acc_release(seg);
+                    seg++;
+                    i = iend;
+                }
+                phase_done(cidx(layer, m == 0 ? 0 : m + 1));
+            }
+        }
+        // ---- lm_head: scaled logits, running argmax per utterance
+        const Mat M = mat_of(d, 4);
+        if ((int)blockIdx.x < B && warp == EPI0 && wait_count_warp(a.cnt + cidx(L - 1, 4), G, c, 23)) {
+            const float r = row_inv_rms(a.x, d.h, Bp, blockIdx.x, d.eps);
+            if (lane == 0) st_tag(a.stats + ((size_t)L * 3 + 2) * 64 + blockIdx.x, r, ep);
+        }
+        for (int b = et; b < Bp; b += NEPI * 32)
+            lm_r3[b] = b < B ? poll_tag(a.stats + ((size_t)L * 3 + 2) * 64 + b, ep, c, 24) : 0.f;
+        u64 best[2] = {0ull, 0ull};  // lane keeps utterances lane and lane + 32
+        epi_sync();
+        int t0, t1;
+        share_tiles(M, t0, t1);
+        for (int r0 = t0; r0 < t1; r0 += NACC) {
+            const int nt = min(NACC, t1 - r0);
+            for (int j = 0; j < nt; j++, seg++) {
+                const int tile = r0 + j;
+                if (acc_ready(seg)) {
+                    const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((seg % NACC) * Bp);
+                    const int row = tile * 128 + 32 * q + lane;
+                    const bool live = row < M.N && !(a.mask_eos && (row == QDB_ENDOFTEXT || row == QDB_IM_END));
+                    for (int c0 = 0; c0 < Bp; c0 += 16) {
+                        float v[16];
+                        tmem_ld16(tbase + (uint32_t)c0, v);
+#pragma unroll
+                        for (int jj = 0; jj < 16; jj++) {
+                            const int b = c0 + jj;
+                            const float lg = v[jj] * lm_r3[b];
+                            if (a.logits_out && row < M.N && b < B) a.logits_out[(size_t)b * M.N + row] = lg;
+                            u64 key = (live && b < B && !isnan(lg)) ? argmax_key(lg, row) : 0ull;
+#pragma unroll
+                            for (int o = 16; o > 0; o >>= 1) {
+                                const u64 other = __shfl_xor_sync(0xffffffffu, key, o);
+                                key = other > key ? other : key;
+                            }
+                            if (lane == (b & 31)) {
+                                u64 &bk = best[b >> 5];
+                                bk = key > bk ? key : bk;
+                            }
+                        }
+                    }
+                } else {
+                    ok = false;
+                }
+                acc_release(seg);
+            }
+        }
+        // combine the 4 epilogue warps, then the CTA's candidates go to the global keys
+        lm_best[q][lane] = best[0];
+        lm_best[q][lane + 32] = best[1];
+        epi_sync();
+        for (int b = et; b < B; b += NEPI * 32) {
+            u64 k = 0ull;
+#pragma unroll
+            for (int w = 0; w < NEPI; w++) k = lm_best[w][b] > k ? lm_best[w][b] : k;
+            if (k) atomicMax(a.best + b, k);
+        }
+    } else {
+        // ================================================================ builders
+        const int bw = warp - BLD0;  // builder warp 0..7
+        const int bt = threadIdx.x - BLD0 * 32;
+        unsigned xi = 0;
+        // ---- set-up: residual x = embedding rows (column b), [h][Bp]
+        {
+            const size_t n = (size_t)d.h * Bp;
+            const size_t i0 = n * blockIdx.x / G, i1 = n * (blockIdx.x + 1) / G;
+            for (size_t i = i0 + bt; i < i1; i += NBLD * 32) {
+                const int k = (int)(i / Bp), b = (int)(i % Bp);
+                float v = 0.f;
+                if (b < B) {
+                    if (a.tok_in) {
+                        int tok = a.tok_in[(size_t)step * B + b];
+                        if (tok < 0 || tok >= d.V) {
+                            set_error(a.err, QDB_ERR_BAD_ARG);
+                            tok = 0;
+                        }
+                        v = __uint_as_float(((uint32_t)a.embed[(size_t)tok * d.h + k]) << 16);
+                    } else {
+                        v = a.x_in[(size_t)b * d.h + k];
+                    }
+                }
+                a.x[i] = v;
+            }
+        }
+        __threadfence();
+        work_sync();
+        if (bt == 0) {
+            __threadfence();
+            signal(a.cnt + 0);
+        }
+        // one X tile: wait for the stage, build it (warp xi % 8), hand it to the MMA
+        auto x_tile = [&](auto fetch) {
+            const int s = xi % NSX;
+            if ((int)(xi % NBLD) == bw && !warp_aborted(c)) {
+                bool ok = xi < (unsigned)NSX || mb_wait_warp(&S_.xempty[s], ((xi / NSX) - 1) & 1, c, 8);
+                if (ok) {
+                    build_tile(xring + (size_t)s * XST, Bp, B, fetch);
+                    if (lane == 0) mb_arrive(&S_.xfull[s]);
+                }
+            }
+            xi++;
+        };
+        for (int layer = 0; layer < L; layer++) {
+            const QdbLayerW &lw = layers[layer];
+            // ---- QKV: X = x * w_in
+            {
+                const Mat M = mat_of(d, 0);
+                int i0, i1;
+                share(M, i0, i1);
+                if (i1 > i0) wait_count_warp(a.cnt + (layer ? cidx(layer - 1, 4) : 0), G, c, 30);
+                for (int i = i0; i < i1; i++) {
+                    const int k0 = (i % M.KB) * 64;
+                    x_tile([&](int kk, int b) { return __ldcg(a.x + (size_t)(k0 + kk) * Bp + b) * lw.in_norm[k0 + kk]; });
+                }
+            }
+            // ---- attention units
+            {
+                const int Sp = a.splits;
+                const int units = B * d.Hkv * Sp;
+                if ((int)blockIdx.x < units) wait_count_warp(a.cnt + cidx(layer, 0), G, c, 31);
+                for (int u = blockIdx.x; u < units; u += G) {
+                    const int b = u / (d.Hkv * Sp), g = (u / Sp) % d.Hkv, s = u % Sp;
+                    if (bt == 0) asm_->r1 = poll_tag(a.stats + ((size_t)layer * 3 + 0) * 64 + b, ep, c, 32);
+                    bld_sync();
+                    const float r1 = asm_->r1;
+                    const QdbRowKV rk = a.rows[b];
+                    const int pos = rk.pos + step;
+                    if (!check_or_record(pos < rk.cap && pos < a.rope_cap, a.err, 2, pos, rk.cap)) {
+                        *c.abort = 1;
+                        break;
+                    }
+                    attn_unit<R>(a, lw, layer, b, g, s, Sp, r1, asm_, obuf, c);
+                }
+                __threadfence();
+                bld_sync();
+                if (bt == 0) signal(a.cnt + cidx(layer, 1));
+            }
+            // ---- O: X = merged attention output (splits combined per utterance)
+            {
+                const Mat M = mat_of(d, 1);
+                int i0, i1;
+                share(M, i0, i1);
+                if (i1 > i0) wait_count_warp(a.cnt + cidx(layer, 1), G, c, 33);
+                const int Sp = a.splits;
+                for (int i = i0; i < i1; i++) {
+                    const int k0 = (i % M.KB) * 64;
+                    const int hq = k0 / QDB_HD, d0 = k0 % QDB_HD;
+                    // this lane's utterances (lane, lane + 32): weight of each split's partial
+                    float f[2][MAX_SPLITS];
+#pragma unroll
+                    for (int j = 0; j < 2; j++) {
+                        const int b = lane + 32 * j;
+                        float mx = -INFINITY, ls = 0.f, mv[MAX_SPLITS];
+#pragma unroll
+                        for (int s = 0; s < MAX_SPLITS; s++) {
+                            mv[s] = (b < B && s < Sp)
+                                        ? __ldcg(a.part + (((size_t)b * d.Hq + hq) * Sp + s) * (2 + QDB_HD)) : -INFINITY;
+                            mx = fmaxf(mx, mv[s]);
+                        }
+#pragma unroll
+                        for (int s = 0; s < MAX_SPLITS; s++) {
+                            f[j][s] = (mx == -INFINITY || mv[s] == -INFINITY) ? 0.f : expf(mv[s] - mx);
+                            if (b < B && s < Sp)
+                                ls += __ldcg(a.part + (((size_t)b * d.Hq + hq) * Sp + s) * (2 + QDB_HD) + 1) * f[j][s];
+                        }
+                        const float inv = ls > 0.f ? 1.0f / ls : 0.f;
+#pragma unroll
+                        for (int s = 0; s < MAX_SPLITS; s++) f[j][s] *= inv;
+                    }
+                    x_tile([&](int kk, int b) {
+                        const float *p = a.part + ((size_t)b * d.Hq + hq) * Sp * (2 + QDB_HD) + 2 + d0 + kk;
+                        const int j = b >> 5;
+                        float o = 0.f;
+#pragma unroll
+                        for (int s = 0; s < MAX_SPLITS; s++)
+                            if (s < Sp) o += f[j][s] * __ldcg(p + (size_t)s * (2 + QDB_HD));
+                        return o;
+                    });
+                }
+            }
+            // ---- GU: X = x * w_post (after this layer's O)
+            {
+                const Mat M = mat_of(d, 2);
+                int i0, i1;
+                share(M, i0, i1);
+                if (i1 > i0) wait_count_warp(a.cnt + cidx(layer, 2), G, c, 34);
+                for (int i = i0; i < i1; i++) {
+                    const int k0 = (i % M.KB) * 64;
+                    x_tile([&](int kk, int b) { return __ldcg(a.x + (size_t)(k0 + kk) * Bp + b) * lw.post_norm[k0 + kk]; });
+                }
+            }
+            // ---- DOWN: X = silu(r g) * (r u)
+            {
+                const Mat M = mat_of(d, 3);
+                int i0, i1;
+                share(M, i0, i1);
+                float r2[2] = {0.f, 0.f};
+                if (i1 > i0) {
+                    wait_count_warp(a.cnt + cidx(layer, 3), G, c, 35);
+                    for (int j = 0; j < 2; j++) {
+                        const int b = lane + 32 * j;
+                        if (b < B) r2[j] = poll_tag(a.stats + ((size_t)layer * 3 + 1) * 64 + b, ep, c, 36);
+                    }
+                }
+                for (int i = i0; i < i1; i++) {
+                    const int k0 = (i % M.KB) * 64;
+                    x_tile([&](int kk, int b) {
+                        const float r = r2[b >> 5];  // b is this lane's utterance (lane or lane + 32)
+                        const float g = __ldcg(a.gu + (size_t)(2 * (k0 + kk)) * Bp + b) * r;
+                        const float u = __ldcg(a.gu + (size_t)(2 * (k0 + kk) + 1) * Bp + b) * r;
+                        return silu_mul(g, u);
+                    });
+                }
+            }
+        }
+        // ---- lm_head: X = x * w_final (the 1/rms factor scales the logits)
+        {
+            const Mat M = mat_of(d, 4);
+            int t0, t1;
+            share_tiles(M, t0, t1);
+            if (t1 > t0) wait_count_warp(a.cnt + cidx(L - 1, 4), G, c, 37);
+            for (int r0 = t0; r0 < t1; r0 += NACC)
+                for (int kb = 0; kb < M.KB; kb++) {
+                    const int k0 = kb * 64;
+                    x_tile([&](int kk, int b) { return __ldcg(a.x + (size_t)(k0 + kk) * Bp + b) * a.final_norm[k0 + kk]; });
+                }
+        }
+    }
+
+    // ---------------------------------------------------------------- wind-down
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+    }
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(a.done, 1u);
+        if (prev == gridDim.x - 1) {
+            // every CTA has passed all of its waits: publish the tokens, clear the state
+            __threadfence();
+            for (int b = 0; b < B; b++) {
+                const u64 k = atomicExch(a.best + b, 0ull);
+                if (k == 0ull) set_error(a.err, QDB_ERR_BAD_ARG);  // no candidate (aborted step)
+                a.tok_out[(size_t)step * B + b] = k ? argmax_key_index(k) : 0;
+            }
+            for (int i = 0; i < a.n_cnt; i++) a.cnt[i] = 0u;
+            __threadfence();
+            atomicExch(a.done, 0u);
+        }
+    }
+}
+
+}  // namespace
+
+// Layout of the step's dynamic shared memory for Bp utterance columns and
+// group size R: W ring, X ring, attention scratch (+ 1 KB alignment slack).
+static int smem_for(int Bp, int R, int nsw) {
+    const int att = (int)sizeof(AttnSm) + NBLD * R * QDB_HD * 4;
+    return 1024 + nsw * W_TILE + NSX * 2 * Bp * 128 + att;
+}
+
+extern "C" int qdb_bstep_ring_stages(int Bp, int R) {
+    int nsw = MAX_NSW;
+    while (nsw > 2 && smem_for(Bp, R, nsw) > 227 * 1024 - 8 * 1024) nsw--;
+    return nsw;
+}
+
+extern "C" size_t qdb_bstep_smem(int Bp, int R) { return (size_t)smem_for(Bp, R, qdb_bstep_ring_stages(Bp, R)); }
+
+extern "C" int qdb_bstep_counters(int layers) { return 1 + 5 * layers; }
+
+extern "C" cudaError_t qdb_launch_bstep(const QdbBatchArgs *args, int grid, cudaStream_t st) {
+    const QdbBatchArgs &a = *args;
+    if (a.B < 1 || a.B > 64 || a.Bp % 16 || a.Bp < a.B || a.Bp > 64) return cudaErrorInvalidValue;
+    if (a.d.L > MAX_LAYERS || a.d.h % 64 || a.d.I % 64 || a.splits < 1) return cudaErrorInvalidValue;
+    const int R = a.d.Hq / a.d.Hkv;
+    const int smem = smem_for(a.Bp, R, a.nsw);
+    void *kargs[] = {const_cast<QdbBatchArgs *>(&a)};
+    cudaError_t e;
+#define QDB_BSTEP_CASE(RR)                                                                                    \
+    case RR:                                                                                                  \
+        e = cudaFuncSetAttribute(bstep_kernel<RR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);        \
+        if (e != cudaSuccess) return e;                                                                       \
+        return cudaLaunchCooperativeKernel((const void *)bstep_kernel<RR>, dim3(grid), dim3(NTHREADS), kargs, \
+                                           (size_t)smem, st);
+    switch (R) {
+        QDB_BSTEP_CASE(1)
+        QDB_BSTEP_CASE(2)
+        QDB_BSTEP_CASE(4)
+        QDB_BSTEP_CASE(8)
+        default: return cudaErrorInvalidValue;
+    }
+#undef QDB_BSTEP_CASE
+}
+
+QDB_WAIT_LIMIT_SETTER(qdb_set_wait_limit_bstep)

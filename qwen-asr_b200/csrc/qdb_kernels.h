@@ -120,6 +120,42 @@ cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_p
                                  int n, int Hq, int Hkv, int splits, float *part, float *out,
                                  cudaStream_t st, int *err = nullptr, const int *step = nullptr,
                                  uint16_t *hi = nullptr, uint16_t *lo = nullptr);
+// ---- persistent batched decode step (qdb_bstep.cu) ----
+// One decode position of B <= 64 independent utterances in one cooperative
+// launch. Activation buffers are [feature][Bp] f32 (utterance = column).
+struct QdbBatchArgs {
+    QdbDims d;
+    int B, Bp;                    // utterances, and columns rounded up to 16 (<= 64)
+    int nsw;                      // weight-ring stages (qdb_bstep_ring_stages)
+    int splits;                   // key splits per (utterance, KV head), <= 8
+    const QdbLayerW *layers;      // device [L]
+    const void *wmaps;            // device CUtensorMap [4L + 1]: qkv, o, gu, down per layer, then embed
+    const uint16_t *embed;        // [V, h]
+    const float *final_norm;      // [h]
+    const float2 *rope;
+    int rope_cap;
+    const QdbRowKV *rows;         // device [B]: KV target and position (+ step_base) of each utterance
+    const int *tok_in;            // device tokens at tok_in[step_base * B + b], or null
+    const float *x_in;            // [B, h] embeddings when tok_in is null
+    int *tok_out;                 // device, written at tok_out[step_base * B + b]
+    float *logits_out;            // nullable [B, V]
+    int mask_eos;
+    int step_base;                // added to every position; selects the token slots
+    float *x, *qkv, *gu, *part;   // [h][Bp], [qkvd][Bp], [2I][Bp], [B][Hq][splits][2 + 128]
+    unsigned long long *stats;    // [(3L + 3) * 64] epoch-tagged 1/rms words
+    unsigned long long *best;     // [64] argmax keys, zero between launches
+    unsigned *cnt;                // [n_cnt] phase counters, zero between launches
+    int n_cnt;
+    unsigned *done;               // zero between launches
+    unsigned epoch;               // tag of this launch's statistics (never 0)
+    int *err;                     // [4]
+};
+int qdb_bstep_ring_stages(int Bp, int R);
+size_t qdb_bstep_smem(int Bp, int R);
+int qdb_bstep_counters(int layers);
+cudaError_t qdb_launch_bstep(const QdbBatchArgs *args, int grid, cudaStream_t st);
+cudaError_t qdb_set_wait_limit_bstep(long long cycles);
+
 // Tensor-core GEMM (qdb_tcgemm.cu): Y (op)= X W^T with X given as bf16 hi/lo.
 cudaError_t qdb_launch_split_bf16(const float *x, uint16_t *hi, uint16_t *lo, size_t count, cudaStream_t st);
 cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,
@@ -128,6 +164,9 @@ cudaError_t qdb_launch_swiglu_split(const float *gu, uint16_t *hi, uint16_t *lo,
 int qdb_gemm_tc_splits(int n, int N, int K, int sms);
 // Bound (cycles) on the tensor-core GEMMs' data waits, current device.
 cudaError_t qdb_set_wait_limit_tcgemm(long long cycles);
+// Writes (host memory, 128 bytes) the tensor map of a bf16 [rows, cols]
+// weight matrix for 128 x 64 tiles, 128-byte swizzle. 0 = ok.
+int qdb_make_weight_map(void *map, const uint16_t *base, int rows, int cols);
 // step (optional, device): the rows' tokens are read at tokens + *step * n
 // (embed) / written at tokens + *step * n (argmax), and positions advance by
 // *step (qk_rope_append, attn_rows): the form a captured decode step replays.

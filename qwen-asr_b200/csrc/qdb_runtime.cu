@@ -91,6 +91,18 @@ struct RowScratch {
     size_t tok_cap = 0;
 };
 
+// Scratch of the persistent batched decode step (qdb_bstep.cu), sized for its
+// largest batch (64 utterances, 8 key splits); allocated on first use.
+struct BatchScratch {
+    float *x = nullptr, *qkv = nullptr, *gu = nullptr, *part = nullptr;
+    unsigned long long *stats = nullptr, *best = nullptr;
+    unsigned *cnt = nullptr, *done = nullptr;
+    int *err = nullptr;
+    void *maps = nullptr;  // device CUtensorMap [4L + 1]
+    int n_cnt = 0;
+    unsigned epoch = 1;
+};
+
 struct qdb_model {
     qdb_config cfg;
     // captured step of qdb_forward_batch, valid while its key (row count,
@@ -137,6 +149,7 @@ struct qdb_model {
     float *h_stage = nullptr;  // pinned [max(h, V)]
     int *h_tok = nullptr;      // pinned
     RowScratch rs;
+    BatchScratch bs;
     std::vector<qdb_session *> sessions;  // live sessions (detached when the model is freed)
 };
 
@@ -303,6 +316,9 @@ extern "C" void qdb_model_free(qdb_model *m) {
     RowScratch &r = m->rs;
     cudaFree(r.X); cudaFree(r.XH); cudaFree(r.XL); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT);
     cudaFree(r.LOG); cudaFree(r.part); cudaFree(r.rowkv); cudaFree(r.tok); cudaFree(r.err); cudaFree(r.GU); cudaFree(r.step);
+    BatchScratch &b = m->bs;
+    cudaFree(b.x); cudaFree(b.qkv); cudaFree(b.gu); cudaFree(b.part); cudaFree(b.stats); cudaFree(b.best);
+    cudaFree(b.cnt); cudaFree(b.done); cudaFree(b.err); cudaFree(b.maps);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->h_tok) cudaFreeHost(m->h_tok);
     if (m->st) cudaStreamDestroy(m->st);
@@ -375,6 +391,7 @@ extern "C" int qdb_model_set_wait_limit(qdb_model *m, long long cycles) {
     CK(qdb_step_kernel_w6()->set_wait_limit(cycles));
     CK(qdb_step_kernel_w7()->set_wait_limit(cycles));
     CK(qdb_set_wait_limit_tcgemm(cycles));
+    CK(qdb_set_wait_limit_bstep(cycles));
     return 0;
 }
 
@@ -821,6 +838,143 @@ static int ensure_tok(qdb_model *m, size_t count) {
     return 0;
 }
 
+// ------------------------------------------------------------------ persistent batched step
+static constexpr int BSTEP_MAX_B = 64, BSTEP_MAX_SPLITS = 8;
+
+// The persistent step serves batches of up to 64 utterances; QWEN_ASR_B200_BATCH=graph
+// forces the launch-per-kernel graph path (A/B measurements), which also serves
+// larger batches.
+static bool bstep_usable(qdb_model *m, int n) {
+    if (n < 1 || n > BSTEP_MAX_B) return false;
+    const char *v = getenv("QWEN_ASR_B200_BATCH");
+    if (v && !strcmp(v, "graph")) return false;
+    int dev_smem = 0;
+    cudaDeviceGetAttribute(&dev_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device);
+    const int Bp = (n + 15) / 16 * 16;
+    return qdb_bstep_smem(Bp, m->cfg.heads / m->cfg.kv_heads) + 2048 <= (size_t)dev_smem;
+}
+
+static int ensure_bstep(qdb_model *m) {
+    BatchScratch &b = m->bs;
+    if (b.x) return 0;
+    const size_t h = m->cfg.hidden, I = m->cfg.intermediate, L = m->cfg.layers;
+    const size_t qkvd = (size_t)m->qd + 2 * m->kvd;
+    b.n_cnt = qdb_bstep_counters((int)L);
+    if (dev_alloc(&b.x, h * BSTEP_MAX_B) || dev_alloc(&b.qkv, qkvd * BSTEP_MAX_B) ||
+        dev_alloc(&b.gu, 2 * I * BSTEP_MAX_B) ||
+        dev_alloc(&b.part, (size_t)BSTEP_MAX_B * m->cfg.heads * BSTEP_MAX_SPLITS * (2 + QDB_HD)) ||
+        dev_alloc(&b.stats, (3 * L + 3) * 64) || dev_alloc(&b.best, 64) || dev_alloc(&b.cnt, (size_t)b.n_cnt) ||
+        dev_alloc(&b.done, 1) || dev_alloc(&b.err, 4)) {
+        std::string e = g_err;
+        cudaFree(b.x); cudaFree(b.qkv); cudaFree(b.gu); cudaFree(b.part); cudaFree(b.stats); cudaFree(b.best);
+        cudaFree(b.cnt); cudaFree(b.done); cudaFree(b.err);
+        b = BatchScratch();
+        g_err = e;
+        return -1;
+    }
+    CK(cudaMemset(b.gu, 0, 2 * I * BSTEP_MAX_B * 4));
+    CK(cudaMemset(b.qkv, 0, qkvd * BSTEP_MAX_B * 4));
+    CK(cudaMemset(b.stats, 0, (3 * L + 3) * 64 * 8));
+    CK(cudaMemset(b.best, 0, 64 * 8));
+    CK(cudaMemset(b.cnt, 0, (size_t)b.n_cnt * 4));
+    CK(cudaMemset(b.done, 0, 4));
+    CK(cudaMemset(b.err, 0, 16));
+    // weight tensor maps: qkv, o, gu, down of every layer, then the embedding
+    const int nmaps = 4 * (int)L + 1;
+    std::vector<unsigned char> maps((size_t)nmaps * 128);
+    for (size_t l = 0; l < L; l++) {
+        const QdbLayerW &lw = m->layers_host[l];
+        unsigned char *p = maps.data() + l * 4 * 128;
+        if (qdb_make_weight_map(p, lw.qkv, (int)qkvd, (int)h) || qdb_make_weight_map(p + 128, lw.o, (int)h, m->qd) ||
+            qdb_make_weight_map(p + 256, lw.gu, (int)(2 * I), (int)h) ||
+            qdb_make_weight_map(p + 384, lw.down, (int)h, (int)I))
+            return fail("weight tensor map of layer %zu", l);
+    }
+    if (qdb_make_weight_map(maps.data() + L * 4 * 128, m->embed, m->cfg.vocab, (int)h))
+        return fail("embedding tensor map");
+    CK(cudaMalloc(&b.maps, maps.size()));
+    CK(cudaMemcpy(b.maps, maps.data(), maps.size(), cudaMemcpyHostToDevice));
+    return 0;
+}
+
+// Key splits per (utterance, KV head): enough attention units to occupy the
+// grid evenly (at least 32 keys per split).
+static int bstep_splits(qdb_model *m, int n, int max_ctx) {
+    const int base = n * m->cfg.kv_heads, G = m->sms;
+    int best = 1;
+    double best_eff = 0.0;
+    for (int s = 1; s <= BSTEP_MAX_SPLITS; s++) {
+        if (s > 1 && (max_ctx + s - 1) / s < 32) break;
+        const int units = base * s;
+        const double eff = (double)units / ((double)G * ((units + G - 1) / G));
+        if (eff > best_eff + 0.05) {
+            best_eff = eff;
+            best = s;
+        }
+        if (eff >= 0.9) break;
+    }
+    return best;
+}
+
+// One launch of the persistent step over the n rows whose QdbRowKV entries are
+// in rs.rowkv. tok_in / x_in: device tokens (slots step_base * n + b) or f32
+// embeddings [n, h]; tok_out slots step_base * n + b.
+static int launch_bstep(qdb_model *m, int n, int max_ctx, const int *tok_in, const float *x_in, int *tok_out,
+                        float *logits, int step_base, int splits) {
+    if (launch_gate()) return -1;
+    BatchScratch &b = m->bs;
+    QdbBatchArgs a;
+    memset(&a, 0, sizeof(a));
+    a.d = m->d;
+    a.B = n;
+    a.Bp = (n + 15) / 16 * 16;
+    a.nsw = qdb_bstep_ring_stages(a.Bp, m->cfg.heads / m->cfg.kv_heads);
+    a.splits = splits;
+    a.layers = m->layers_dev;
+    a.wmaps = b.maps;
+    a.embed = m->embed;
+    a.final_norm = m->final_norm;
+    a.rope = m->rope;
+    a.rope_cap = m->rope_cap;
+    a.rows = m->rs.rowkv;
+    a.tok_in = tok_in;
+    a.x_in = x_in;
+    a.tok_out = tok_out;
+    a.logits_out = logits;
+    a.mask_eos = m->mask_eos;
+    a.step_base = step_base;
+    a.x = b.x;
+    a.qkv = b.qkv;
+    a.gu = b.gu;
+    a.part = b.part;
+    a.stats = b.stats;
+    a.best = b.best;
+    a.cnt = b.cnt;
+    a.n_cnt = b.n_cnt;
+    a.done = b.done;
+    if (++b.epoch == 0) b.epoch = 1;
+    a.epoch = b.epoch;
+    a.err = b.err;
+    (void)max_ctx;
+    CK(qdb_launch_bstep(&a, m->sms, m->st));
+    return 0;
+}
+
+static int check_bstep_err(qdb_model *m) {
+    int ev[4] = {0, 0, 0, 0};
+    CK(cudaMemcpy(ev, m->bs.err, sizeof(ev), cudaMemcpyDeviceToHost));
+    if (ev[0]) {
+        cudaMemset(m->bs.err, 0, sizeof(ev));
+        cudaDeviceSynchronize();
+        return fail("device error code %d in the batched decode step (%s; check %d: %d %d)", ev[0],
+                    ev[0] == 1   ? "a bounded wait ran out"
+                    : ev[0] == 2 ? "invalid token or no argmax candidate"
+                                 : "an access refused by a bounds check",
+                    ev[1], ev[2], ev[3]);
+    }
+    return 0;
+}
+
 extern "C" int qdb_forward_batch(qdb_session *const *sessions, int n, const float *embeds, const int *pos,
                                  int *tokens_out, float *logits_out) {
     g_err.clear();
@@ -830,6 +984,18 @@ extern "C" int qdb_forward_batch(qdb_session *const *sessions, int n, const floa
     if (batch_setup(sessions, n, pos, 0, &m, &maxp) || ensure_tok(m, n)) return -1;
     CK(cudaMemcpyAsync(m->rs.X, embeds, (size_t)n * m->cfg.hidden * 4, cudaMemcpyHostToDevice, m->st));
     RowScratch &r = m->rs;
+    if (bstep_usable(m, n)) {
+        if (ensure_bstep(m) ||
+            launch_bstep(m, n, maxp + 1, nullptr, r.X, r.tok, logits_out ? r.LOG : nullptr, 0,
+                         bstep_splits(m, n, maxp + 1)))
+            return -1;
+        CK(cudaMemcpyAsync(tokens_out, r.tok, sizeof(int) * n, cudaMemcpyDeviceToHost, m->st));
+        if (logits_out)
+            CK(cudaMemcpyAsync(logits_out, r.LOG, sizeof(float) * (size_t)n * m->cfg.vocab, cudaMemcpyDeviceToHost,
+                               m->st));
+        CK(cudaStreamSynchronize(m->st));
+        return check_bstep_err(m);
+    }
     auto step = [&]() { return run_rows(m, n, false, r.rowkv, 0, nullptr, 0, maxp + 1) || batch_tail(m, n, r.tok); };
     const int S = std::min(64, std::max(1, (maxp + 1 + 64 * QDB_AR_ITERS - 1) / (64 * QDB_AR_ITERS)));
     // the captured launches bake in the row count, the split count, every
@@ -885,6 +1051,16 @@ extern "C" int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, cons
     for (int b = 0; b < n; b++)
         if (first_tokens[b] < 0 || first_tokens[b] >= m->cfg.vocab) return fail("row %d: token out of range", b);
     CK(cudaMemcpyAsync(m->rs.tok, first_tokens, sizeof(int) * n, cudaMemcpyHostToDevice, m->st));
+    if (bstep_usable(m, n)) {
+        if (ensure_bstep(m)) return -1;
+        const int S = bstep_splits(m, n, maxp + n_steps);
+        for (int i = 0; i < n_steps; i++)
+            if (launch_bstep(m, n, maxp + 1 + i, m->rs.tok, nullptr, m->rs.tok + n, nullptr, i, S)) return -1;
+        CK(cudaMemcpyAsync(tokens_out, m->rs.tok + n, sizeof(int) * (size_t)n * n_steps, cudaMemcpyDeviceToHost,
+                           m->st));
+        CK(cudaStreamSynchronize(m->st));
+        return check_bstep_err(m);
+    }
     // One step reads its tokens and position offset from the device step
     // counter, so the same launch sequence serves every step: step 0 runs
     // directly (it also sizes the scratch), the rest replay a CUDA graph of

@@ -545,6 +545,12 @@ cudaError_t launch_persist(const uint16_t *W, const uint16_t *Xh, const uint16_t
 
 QDB_WAIT_LIMIT_SETTER(qdb_set_wait_limit_tcgemm)
 
+// Tensor map of a bf16 weight matrix [rows, cols] for 128-row x 64-column
+// tiles with 128-byte swizzle (the batched decode step's weight stream).
+extern "C" int qdb_make_weight_map(void *map, const uint16_t *base, int rows, int cols) {
+    return make_map(reinterpret_cast<CUtensorMap *>(map), base, rows, cols, TC_BM) ? 0 : -1;
+}
+
 extern "C" cudaError_t qdb_launch_split_bf16(const float *x, uint16_t *hi, uint16_t *lo, size_t count,
                                              cudaStream_t st) {
     if (!count) return cudaSuccess;

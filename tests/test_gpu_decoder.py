@@ -303,3 +303,49 @@ def test_prefill_attention_groupings(pkg, synth, heads, kv_heads, chunks):
         otok, _, olg = o.forward(emb[i])
         assert_logits_close(lg, olg, f"R={heads // kv_heads} pos {i}")
         assert tok == otok or margin_top2(olg) <= MARGIN
+
+
+@pytest.mark.parametrize("n", [1, 17, 64])
+def test_persistent_batch_step_matches_graph_path(pkg, synth, monkeypatch, n):
+    """The persistent batched step (one cooperative launch, n <= 64) against
+    the launch-per-kernel graph path on the same sessions: tokens equal under
+    the margin rule and logits within the parity bar, at 1, 17 (padded to 32
+    columns) and 64 rows, with several key splits."""
+    cfg = synth.PRESETS["small"]
+    ws = synth.WeightSet(cfg, seed=31, norm_jitter=0.1)
+    model = pkg.Model(ws, device=0, mask_eos=True)
+    lens = [5 + (37 * b) % 300 for b in range(n)]
+    embs = [synth.audio_embeddings(cfg, L + 2, seed=500 + b) for b, L in enumerate(lens)]
+    sa = [model.session(320) for _ in range(n)]
+    sg = [model.session(320) for _ in range(n)]
+    for b in range(n):
+        sa[b].prefill(embs[b][:lens[b]], 0)
+        sg[b].prefill(embs[b][:lens[b]], 0)
+    for step in range(2):
+        x = np.stack([embs[b][lens[b] + step] for b in range(n)])
+        pos = [lens[b] + step for b in range(n)]
+        ta, la = pkg.forward_batch(sa, x, pos, want_logits=True)
+        monkeypatch.setenv("QWEN_ASR_B200_BATCH", "graph")
+        tg, lg = pkg.forward_batch(sg, x, pos, want_logits=True)
+        monkeypatch.delenv("QWEN_ASR_B200_BATCH")
+        for b in range(n):
+            assert_logits_close(la[b], lg[b], f"n={n} step {step} row {b}")
+            assert ta[b] == tg[b] or margin_top2(lg[b], mask_eos=True) <= MARGIN
+
+
+def test_batch_above_64_rows_uses_graph_path(pkg, synth):
+    """More than 64 rows: the graph path serves the call; rows agree with the
+    per-session step."""
+    cfg = synth.PRESETS["tiny"]
+    ws = synth.WeightSet(cfg, seed=32, norm_jitter=0.1)
+    model = pkg.Model(ws, device=0, mask_eos=True)
+    n = 70
+    emb = synth.audio_embeddings(cfg, 12, seed=9)
+    sess = [model.session(16) for _ in range(n)]
+    for s in sess:
+        s.prefill(emb[:10], 0)
+    got = pkg.forward_batch(sess, np.stack([emb[10]] * n), [10] * n)
+    ref = model.session(16)
+    ref.prefill(emb[:10], 0)
+    want, _, lg = ref.forward(emb[10], 10, want_logits=True)
+    assert all(t == want for t in got) or margin_top2(lg, mask_eos=True) <= MARGIN
