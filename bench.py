@@ -12,11 +12,12 @@ same JSON line carries a `b1` object with the batch-1 configs c0 (0.6B, 10 s,
 `--config c0|c1|c3` makes a batch-1 config the headline instead (replicas on
 N>1, weak scaling).
 
-One timed step = this rank's utterances: prefill of every prompt followed by
-the greedy decode loop. `value` = decoded tokens (all ranks) / decode time
+One timed step = this rank's utterances: one batched prefill of every prompt
+(qdb_prefill_batch: all rows in one row batch) followed by the greedy decode
+loop (one persistent kernel launch per position). `value` = decoded tokens (all ranks) / decode time
 (max over ranks), inputs resident in HBM (device embedding lookup, device
 greedy loop). `e2e` = the same metric through the reference-facing C ABI with
-host buffers: host f32 prompt embeddings (pinned) through qdb_prefill, then
+host buffers: host f32 prompt embeddings (pinned) through qdb_prefill(_batch), then
 one host embedding row in and one token out per utterance per decode step
 (the qwen_asr.c:729-759 caller loop; qdb_forward_batch for batches).
 
@@ -199,14 +200,17 @@ def measure(pkg, synth, cfg_name, world, rank, local, steps, warmup, clocks=None
     stream = torch.cuda.ExternalStream(model.stream_handle, device=torch.device("cuda", local))
     cap = P + n_dec + 8
     sessions = [model.session(cap) for _ in range(n_local)]
-    emb_dev = [torch.from_numpy(e[:-1]).to(f"cuda:{local}") for e in embs]
+    # every prompt of this rank back to back: one batched prefill
+    emb_dev = torch.from_numpy(np.concatenate([e[:-1] for e in embs])).to(f"cuda:{local}")
     torch.cuda.synchronize()
 
     def one_step(timing):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         ev[0].record(stream)
-        for s, e in zip(sessions, emb_dev):
-            s.prefill_device(e.data_ptr(), P, 0)
+        if n_local == 1:
+            sessions[0].prefill_device(emb_dev.data_ptr(), P, 0)
+        else:
+            pkg.prefill_batch_device(sessions, emb_dev.data_ptr(), [P] * n_local, [0] * n_local)
         ev[1].record(stream)
         if n_local == 1:
             toks = sessions[0].decode_greedy(last_tok, P, n_dec)
@@ -238,14 +242,17 @@ def measure(pkg, synth, cfg_name, world, rank, local, steps, warmup, clocks=None
 
     # e2e through the reference-facing ABI with host buffers (pinned inputs)
     pinned = [torch.from_numpy(e).pin_memory() for e in embs]
+    prompts = torch.from_numpy(np.concatenate([e[:-1] for e in embs])).pin_memory()
     emb_tab = ws.embed  # host bf16 table, the caller's mmap
     e2e_ev = []
 
     def e2e_step():
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         ev[0].record(stream)
-        for s, e in zip(sessions, pinned):
-            s.prefill(e.numpy()[:-1], 0)
+        if n_local == 1:
+            sessions[0].prefill(prompts.numpy(), 0)
+        else:
+            pkg.prefill_batch(sessions, prompts.numpy(), [0] * n_local, lens=[P] * n_local)
         ev[1].record(stream)
         if n_local == 1:
             s = sessions[0]
@@ -293,19 +300,17 @@ def summarize(m, cfg_name, world, steps):
     launch_s = (m["dec_ms"] / 1e3) / (steps * n_dec)
     achieved = bytes_per_step / launch_s / 1e9
     peak, peak_kind = measured_peaks()
-    kernel = "step_kernel" if n_local == 1 else "rows_decode"
+    kernel = "step_kernel" if n_local == 1 else "bstep_kernel"
     return dict(value=value, e2e_value=e2e_value, achieved=achieved, peak=peak, peak_kind=peak_kind,
                 frac=achieved / peak, kernel=kernel, bytes_per_step=bytes_per_step,
                 traffic=step_traffic_from_profile(kernel, cfg_name))
 
 
 def launches_per_step(cfg, n_local, n_dec):
-    # per prefill, per layer: 2 norms, 4 GEMMs, q/k RoPE + KV append, attention, bf16 split of the
-    # SwiGLU output; per batched decode step: embed, 10 per layer (2 norms, 4 GEMMs, RoPE/append,
-    # attention units, split merge, SwiGLU split), final norm, lm_head GEMM, argmax, step advance;
-    # b=1 decode: one persistent step kernel per token
-    L = cfg.layers
-    return (L * 9) * n_local + (n_dec if n_local == 1 else n_dec * (L * 10 + 5))
+    # one prefill (all of the rank's prompts in one row batch), per layer: 2 norms, 4 GEMMs, q/k RoPE +
+    # KV append, attention, bf16 split of the SwiGLU output; decode: one persistent step kernel per
+    # token (b=1: qdb_step.cu; up to 64 utterances: qdb_bstep.cu)
+    return cfg.layers * 9 + n_dec
 
 
 def run_ours(args):

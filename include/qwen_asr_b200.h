@@ -106,6 +106,19 @@ int qdb_prefill(qdb_session *s, const float *embeds, int seq_len, int start_pos)
 /* Same with a DEVICE pointer to the embeddings (no host copy). */
 int qdb_prefill_device(qdb_session *s, const float *embeds_dev, int seq_len, int start_pos);
 
+/* Prefill of n independent sessions of one model in ONE row batch (no
+ * reference counterpart: the reference prefills one utterance per process):
+ * session i appends seq_lens[i] positions at start_pos[i]; embeds holds the
+ * rows of all sessions back to back (host f32 [sum(seq_lens), hidden]). The
+ * projections run as one tensor-core GEMM over every row; attention stays
+ * causal within each session. Equivalent to n qdb_prefill calls. */
+int qdb_prefill_batch(qdb_session *const *sessions, int n, const float *embeds,
+                      const int *seq_lens, const int *start_pos);
+
+/* Same with a DEVICE pointer to the embeddings. */
+int qdb_prefill_batch_device(qdb_session *const *sessions, int n, const float *embeds_dev,
+                             const int *seq_lens, const int *start_pos);
+
 /* ---- One decode step, replaces qwen_decoder_forward (qwen_asr_decoder.c:388-476) ----
  * Runs position `pos` with the host f32 embedding [hidden]; returns the greedy
  * token. hidden_out (nullable, host, [hidden]) receives the final-normed hidden

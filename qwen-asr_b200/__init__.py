@@ -54,6 +54,9 @@ ABI = {
     "qdb_session_reserve": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "qdb_prefill": (ctypes.c_int, [ctypes.c_void_p, _f32p, ctypes.c_int, ctypes.c_int]),
     "qdb_prefill_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int]),
+    "qdb_prefill_batch": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _f32p, _i32p, _i32p]),
+    "qdb_prefill_batch_device": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_void_p,
+                                                _i32p, _i32p]),
     "qdb_forward": (ctypes.c_int, [ctypes.c_void_p, _f32p, ctypes.c_int, _f32p, _f32p]),
     "qdb_decode_greedy": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _i32p]),
     "qdb_forward_batch": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _f32p, _i32p, _i32p, _f32p]),
@@ -232,6 +235,34 @@ class Session:
 def _handles(sessions):
     arr = (ctypes.c_void_p * len(sessions))(*[s.h for s in sessions])
     return arr
+
+
+def prefill_batch(sessions, embeds, start_pos, lens=None):
+    """Prefill of several sessions as one row batch. embeds: a list of f32
+    [n_i, hidden] arrays (one per session), or, with lens, one f32 array of
+    all rows back to back. start_pos: first position of each session."""
+    n = len(sessions)
+    sp = np.ascontiguousarray(start_pos, dtype=np.int32)
+    if lens is None:
+        ln = np.array([0 if e is None else len(e) for e in embeds], np.int32)
+        rows = [np.asarray(e, np.float32) for e in embeds if e is not None and len(e)]
+        cat = np.ascontiguousarray(np.concatenate(rows, axis=0)) if rows else np.zeros((1, 1), np.float32)
+    else:
+        ln = np.ascontiguousarray(lens, dtype=np.int32)
+        cat = np.ascontiguousarray(embeds, dtype=np.float32)
+    if lib.qdb_prefill_batch(_handles(sessions), n, _ptr(cat, _f32p), _ptr(ln, _i32p), _ptr(sp, _i32p)):
+        raise _err("qdb_prefill_batch")
+
+
+def prefill_batch_device(sessions, dev_ptr: int, lens, start_pos):
+    """prefill_batch with the rows already on the device (dev_ptr: f32
+    [sum(lens), hidden])."""
+    n = len(sessions)
+    ln = np.ascontiguousarray(lens, dtype=np.int32)
+    sp = np.ascontiguousarray(start_pos, dtype=np.int32)
+    if lib.qdb_prefill_batch_device(_handles(sessions), n, ctypes.c_void_p(dev_ptr), _ptr(ln, _i32p),
+                                    _ptr(sp, _i32p)):
+        raise _err("qdb_prefill_batch_device")
 
 
 def forward_batch(sessions, embeds: np.ndarray, pos, want_logits: bool = False):

@@ -149,9 +149,8 @@ __device__ __forceinline__ void put8_split(unsigned char *hi, unsigned char *lo,
 
 template <int R>
 __global__ void __launch_bounds__(AT_THREADS, 1)
-    attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                   const float *__restrict__ q,
-                   int cap, int start_pos, int n, int Hq, float *__restrict__ out, int *err, uint16_t *hi,
+    attn_tc_kernel(const CUtensorMap *__restrict__ maps, const QdbAttnSeg *__restrict__ segs, int layer, int Hkv,
+                   const float *__restrict__ q, int Hq, float *__restrict__ out, int *err, uint16_t *hi,
                    uint16_t *lo) {
     constexpr int QT = AT_M / R;  // query positions per CTA
     extern __shared__ __align__(1024) unsigned char smem_dyn[];
@@ -164,8 +163,21 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     unsigned char *Ph = sm + 6 * AT_TILE, *Pl = sm + 8 * AT_TILE; // [2 key blocks] each
     unsigned char *Vt = sm + 10 * AT_TILE;                        // [2 key blocks]: rows = dims
 
+    // segment = one session's prompt rows; its K/V maps cover all layers
+    const QdbAttnSeg sg = segs[blockIdx.z];
+    const int cap = sg.cap, start_pos = sg.start_pos, n = sg.n;
+    const int i0 = blockIdx.x * QT;
+    if (i0 >= n) return;  // shorter segment than the grid's longest (uniform per CTA)
+    const CUtensorMap *tmK = maps + 2 * blockIdx.z, *tmV = tmK + 1;
+    q += (size_t)sg.row0 * Hq * QDB_HD;
+    out += (size_t)sg.row0 * Hq * QDB_HD;
+    if (hi) {
+        hi += (size_t)sg.row0 * Hq * QDB_HD;
+        lo += (size_t)sg.row0 * Hq * QDB_HD;
+    }
     const int t = threadIdx.x, warp = t >> 5;
-    const int g = blockIdx.y, i0 = blockIdx.x * QT;
+    const int g = blockIdx.y;
+    const int kv_row0 = (layer * Hkv + g) * cap;  // this layer's KV head g in the all-layer map
     const int half = warp >> 2;                     // this thread's half of the row's columns
     const int r = 32 * (warp & 3) + (t & 31), p = r / R, h = r % R;  // MMA row: position i0 + p, head g*R + h
     const bool row_ok = i0 + p < n;
@@ -216,8 +228,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     // thread 0: K tile k0 by TMA, then S = Q K^T into TMEM; false = a wait ran out
     auto s_tile = [&](int k0) -> bool {
         mb_expect(&barK, 2 * AT_TILE);
-        tma_load_2d(Kt, &tmK, 0, g * cap + k0, &barK);
-        tma_load_2d(Kt + AT_TILE, &tmK, 64, g * cap + k0, &barK);
+        tma_load_2d(Kt, tmK, 0, kv_row0 + k0, &barK);
+        tma_load_2d(Kt + AT_TILE, tmK, 64, kv_row0 + k0, &barK);
         if (!mb_wait(&barK, phK, err)) return false;
         phK ^= 1;
         tc_fence_after();
@@ -292,8 +304,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                 s_ok = 0;
             } else {
                 mb_expect(&barK, 2 * AT_TILE);
-                tma_load_2d(Kt, &tmV, 0, g * cap + k0, &barK);
-                tma_load_2d(Kt + AT_TILE, &tmV, 64, g * cap + k0, &barK);
+                tma_load_2d(Kt, tmV, 0, kv_row0 + k0, &barK);
+                tma_load_2d(Kt + AT_TILE, tmV, 64, kv_row0 + k0, &barK);
             }
         }
         __syncthreads();
@@ -404,48 +416,54 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn_at() {
 }
 
 template <int R>
-cudaError_t launch_at(const CUtensorMap &mk, const CUtensorMap &mv, const float *q, int cap, int start_pos, int n,
-                      int Hq, int Hkv, float *out, int *err, cudaStream_t st, uint16_t *hi, uint16_t *lo) {
+cudaError_t launch_at(const CUtensorMap *maps, const QdbAttnSeg *segs, int nseg, int max_n, int layer, int Hq, int Hkv,
+                      const float *q, float *out, int *err, cudaStream_t st, uint16_t *hi, uint16_t *lo) {
     const int smem = 12 * AT_TILE + 1024;  // Q hi/lo, K, P hi/lo, V^T + alignment slack
     cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     constexpr int QT = AT_M / R;
-    dim3 grid((n + QT - 1) / QT, Hkv);
-    attn_tc_kernel<R><<<grid, AT_THREADS, smem, st>>>(mk, mv, q, cap, start_pos, n, Hq, out, err, hi, lo);
+    dim3 grid((max_n + QT - 1) / QT, Hkv, nseg);
+    attn_tc_kernel<R><<<grid, AT_THREADS, smem, st>>>(maps, segs, layer, Hkv, q, Hq, out, err, hi, lo);
     return cudaGetLastError();
 }
 
 }  // namespace
 
-// Causal prefill attention for positions [start_pos, start_pos + n) of one
-// layer on the tensor cores. q: f32 [n, Hq*128] (normed, rotated); kc/vc: the
-// session's fp16 caches [L][Hkv][cap][128], already holding keys
-// [0, start_pos + n) of this layer; out: f32 [n, Hq*128].
-extern "C" cudaError_t qdb_launch_attn_prefill_tc(const float *q, const uint16_t *kc, const uint16_t *vc, int cap,
-                                                  int layer, int start_pos, int n, int Hq, int Hkv, float *out,
-                                                  int *err, cudaStream_t st, uint16_t *hi, uint16_t *lo) {
-    if (n <= 0) return cudaSuccess;
-    if (Hkv <= 0 || Hq % Hkv || cap <= 0 || start_pos + n > cap) return cudaErrorInvalidValue;
-    if (((uintptr_t)q | (uintptr_t)kc | (uintptr_t)vc | (uintptr_t)out) & 15) return cudaErrorInvalidValue;
+// Tensor map (written to host memory, 128 bytes) of one session's fp16 K or V
+// cache [L][Hkv][cap][128] as [L * Hkv * cap rows][128]: 64-column x 128-row
+// boxes, 128-byte swizzle. 0 = ok.
+extern "C" int qdb_attn_kv_map(void *map, const uint16_t *cache, int L, int Hkv, int cap) {
     auto fn = encode_fn_at();
-    if (!fn) return cudaErrorNotSupported;
-    const size_t layer_off = (size_t)layer * Hkv * cap * QDB_HD;
-    // K and V of this layer: [Hkv * cap rows][128] fp16, 64-column x 128-row boxes, 128-byte swizzle
-    CUtensorMap mk, mv;
-    cuuint64_t dims[2] = {(cuuint64_t)QDB_HD, (cuuint64_t)Hkv * (cuuint64_t)cap};
+    if (!fn || ((uintptr_t)cache & 15)) return -1;
+    cuuint64_t dims[2] = {(cuuint64_t)QDB_HD, (cuuint64_t)L * Hkv * (cuuint64_t)cap};
     cuuint64_t strides[1] = {(cuuint64_t)QDB_HD * 2};
     cuuint32_t box[2] = {64, (cuuint32_t)AT_N};
     cuuint32_t es[2] = {1, 1};
-    for (int i = 0; i < 2; i++)
-        if (fn(i ? &mv : &mk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t *>((i ? vc : kc) + layer_off), dims,
-               strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-            return cudaErrorInvalidValue;
+    return fn(reinterpret_cast<CUtensorMap *>(map), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t *>(cache),
+              dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS
+               ? 0
+               : -1;
+}
+
+// Causal prefill attention of one layer for nseg sessions at once on the
+// tensor cores. Segment i: prompt rows [row0, row0 + n) of q / out are the
+// session's positions [start_pos, start_pos + n); its K and V maps
+// (qdb_attn_kv_map) are maps[2i] and maps[2i + 1] (device memory); the caches
+// already hold keys [0, start_pos + n) of this layer. q: f32 [rows, Hq*128]
+// (normed, rotated); out: f32 [rows, Hq*128], or its bf16 split into hi/lo.
+extern "C" cudaError_t qdb_launch_attn_prefill_tc(const void *maps, const QdbAttnSeg *segs, int nseg, int max_n,
+                                                  int layer, int Hq, int Hkv, const float *q, float *out, int *err,
+                                                  cudaStream_t st, uint16_t *hi, uint16_t *lo) {
+    if (nseg <= 0 || max_n <= 0) return cudaSuccess;
+    if (Hkv <= 0 || Hq % Hkv || !maps || !segs) return cudaErrorInvalidValue;
+    if (((uintptr_t)q | (uintptr_t)out | (uintptr_t)maps) & 15) return cudaErrorInvalidValue;
+    const CUtensorMap *m = reinterpret_cast<const CUtensorMap *>(maps);
     switch (Hq / Hkv) {
-        case 1: return launch_at<1>(mk, mv, q, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
-        case 2: return launch_at<2>(mk, mv, q, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
-        case 4: return launch_at<4>(mk, mv, q, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
-        case 8: return launch_at<8>(mk, mv, q, cap, start_pos, n, Hq, Hkv, out, err, st, hi, lo);
+        case 1: return launch_at<1>(m, segs, nseg, max_n, layer, Hq, Hkv, q, out, err, st, hi, lo);
+        case 2: return launch_at<2>(m, segs, nseg, max_n, layer, Hq, Hkv, q, out, err, st, hi, lo);
+        case 4: return launch_at<4>(m, segs, nseg, max_n, layer, Hq, Hkv, q, out, err, st, hi, lo);
+        case 8: return launch_at<8>(m, segs, nseg, max_n, layer, Hq, Hkv, q, out, err, st, hi, lo);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -155,6 +155,17 @@ __device__ bool mb_wait_warp(u64 *b, unsigned par, const Ctl &c, int site) {
     }
 }
 
+// Progress word w of this CTA (diagnostics of a wait that ran out): 0 W tiles
+// issued, 1 W tiles consumed by the MMA, 2 X tiles consumed, 3 accumulator
+// segments issued, 4 segments drained by the epilogue, 5 epilogue phase
+// (layer * 8 + matrix), 6 X tiles built, 7 builder phase, 8 the MMA's current
+// wait (3 W tile, 4 X tile, 5 accumulator slot, 0 none), 9..16 per builder
+// warp: X tile it works on (bit 31 set while it waits for the stage).
+constexpr int PROG_WORDS = 17;
+__device__ __forceinline__ void progress(const QdbBatchArgs &a, int w, unsigned v) {
+    if (a.prog) *(volatile unsigned *)(a.prog + blockIdx.x * PROG_WORDS + w) = v;
+}
+
 // Phase counter: this CTA's part is done (the caller fenced its writes).
 __device__ __forceinline__ void signal(unsigned *cnt) { atomicAdd(cnt, 1u); }
 
@@ -312,40 +323,38 @@ struct Smem {
 // ---------------------------------------------------------------- builders: X tiles
 // Writes the X tile (Bp rows = utterances, 64 columns = k0..k0+63) into the
 // stage as bf16 hi and lo with the 128-byte swizzle: element (b, k) at byte
-// (b/8)*1024 + (b%8)*128 + (((k/8) ^ (b%8)) * 16) + (k%8)*2. One warp per tile:
-// lane = utterance b (and b + 32). The f32 source value of (b, k0 + k) is
-// `fetch(k, b)`; for a fixed k the lanes read consecutive utterances, which the
-// [feature][Bp] layout of every activation buffer makes one coalesced access.
+// (b/8)*1024 + (b%8)*128 + (((k/8) ^ (b%8)) * 16) + (k%8)*2. All 8 builder
+// warps build every tile together: builder thread bt takes utterance
+// b = bt % Bp and the 8-column chunks bt / Bp, bt / Bp + 256 / Bp, ... The f32
+// source value of (b, k0 + k) is `fetch(k, b)`; for a fixed k consecutive
+// threads read consecutive utterances, which the [feature][Bp] layout of every
+// activation buffer makes one coalesced access.
 template <typename F>
-__device__ __forceinline__ void build_tile(unsigned char *xs, int Bp, int B, F fetch) {
-    const int lane = threadIdx.x & 31;
+__device__ __forceinline__ void build_tile(unsigned char *xs, int Bp, int B, int bt, F fetch) {
     unsigned char *hi = xs, *lo = xs + Bp * 128;
-    for (int b = lane; b < Bp; b += 32) {
-        const uint32_t rb = (uint32_t)(b >> 3) * 1024u + (uint32_t)(b & 7) * 128u;
-        float v[64];  // all 64 loads in flight before the first conversion
+    const int b = bt % Bp;
+    const uint32_t rb = (uint32_t)(b >> 3) * 1024u + (uint32_t)(b & 7) * 128u;
+    for (int cc = bt / Bp; cc < 8; cc += (NBLD * 32) / Bp) {
+        float v[8];
         if (b < B) {
 #pragma unroll
-            for (int k = 0; k < 64; k++) v[k] = fetch(k, b);
+            for (int i = 0; i < 8; i++) v[i] = fetch(cc * 8 + i, b);
         } else {
 #pragma unroll
-            for (int k = 0; k < 64; k++) v[k] = 0.f;
+            for (int i = 0; i < 8; i++) v[i] = 0.f;
         }
+        uint32_t h[4], l[4];
 #pragma unroll
-        for (int cc = 0; cc < 8; cc++) {
-            uint32_t h[4], l[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const float v0 = v[cc * 8 + 2 * i], v1 = v[cc * 8 + 2 * i + 1];
-                const uint16_t h0 = f32_to_bf16_rn(v0), h1 = f32_to_bf16_rn(v1);
-                const uint16_t l0 = f32_to_bf16_rn(v0 - __uint_as_float((uint32_t)h0 << 16));
-                const uint16_t l1 = f32_to_bf16_rn(v1 - __uint_as_float((uint32_t)h1 << 16));
-                h[i] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-                l[i] = (uint32_t)l0 | ((uint32_t)l1 << 16);
-            }
-            const uint32_t off = rb + (uint32_t)((cc ^ (b & 7)) * 16);
-            *reinterpret_cast<uint4 *>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
-            *reinterpret_cast<uint4 *>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+        for (int i = 0; i < 4; i++) {
+            const uint16_t h0 = f32_to_bf16_rn(v[2 * i]), h1 = f32_to_bf16_rn(v[2 * i + 1]);
+            const uint16_t l0 = f32_to_bf16_rn(v[2 * i] - __uint_as_float((uint32_t)h0 << 16));
+            const uint16_t l1 = f32_to_bf16_rn(v[2 * i + 1] - __uint_as_float((uint32_t)h1 << 16));
+            h[i] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+            l[i] = (uint32_t)l0 | ((uint32_t)l1 << 16);
         }
+        const uint32_t off = rb + (uint32_t)((cc ^ (b & 7)) * 16);
+        *reinterpret_cast<uint4 *>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4 *>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
     }
     // generic-proxy writes -> visible to the tensor core's async proxy
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -606,7 +615,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
             mb_init(&S_.wempty[i], 1);
         }
         for (int i = 0; i < NSX; i++) {
-            mb_init(&S_.xfull[i], 1);
+            mb_init(&S_.xfull[i], NBLD);  // every builder warp writes part of each X tile
             mb_init(&S_.xempty[i], 1);
         }
         for (int i = 0; i < NACC; i++) {
@@ -644,8 +653,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                 const int s = wi % NSW;
                 if (wi >= (unsigned)NSW && !mb_wait(&S_.wempty[s], ((wi / NSW) - 1) & 1, c, true, 1)) return false;
                 mb_expect(&S_.wfull[s], W_TILE);
-                tma_load_2d_pol(wring + (size_t)s * W_TILE, reinterpret_cast<const CUtensorMap *>(a.wmaps) + mi, kb * 64, tile * 128, &S_.wfull[s], pol);
+                tma_load_2d_pol(wring + (size_t)s * W_TILE, reinterpret_cast<const CUtensorMap *>(a.wmaps) + mi, kb * 64,
+                                tile * 128, &S_.wfull[s], pol);
                 wi++;
+                progress(a, 0, wi);
                 return true;
             };
             for (int layer = 0; layer < L && ok; layer++)
@@ -680,8 +691,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
             // one item: W stage wi x X stage xi into accumulator slot
             auto item = [&](uint32_t acc, bool first, bool last_x) -> bool {
                 const int ws = wi % NSW, xs = xi % NSX;
+                progress(a, 8, 3);
                 if (!mb_wait(&S_.wfull[ws], (wi / NSW) & 1, c, true, 3)) return false;
+                progress(a, 8, 4);
                 if (!mb_wait(&S_.xfull[xs], (xi / NSX) & 1, c, true, 4)) return false;
+                progress(a, 8, 0);
                 tc_fence_after();
                 const uint32_t wb = su32(wring + (size_t)ws * W_TILE);
                 const uint32_t xb = su32(xring + (size_t)xs * XST);
@@ -693,18 +707,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                 }
                 mma_commit(&S_.wempty[ws]);
                 wi++;
+                progress(a, 1, wi);
                 if (last_x) {
                     mma_commit(&S_.xempty[xs]);
                     xi++;
+                    progress(a, 2, xi);
                 }
                 return true;
             };
             auto begin_seg = [&](unsigned sg) -> bool {
                 const int slot = sg % NACC;
+                progress(a, 8, 5);
                 if (sg >= (unsigned)NACC &&
                     !mb_wait(&S_.accempty[slot], ((sg / NACC) - 1) & 1, c, true, 5))
                     return false;
                 tc_fence_after();
+                progress(a, 3, sg + 1);
                 return true;
             };
             for (int layer = 0; layer < L && ok; layer++)
@@ -758,6 +776,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mb_arrive(&S_.accempty[sg % NACC]);
+            if (warp == EPI0 && lane == 0) progress(a, 4, sg + 1);
         };
         auto phase_done = [&](int idx) {
             __threadfence();
@@ -778,6 +797,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
             for (int m = 0; m < 4; m++) {
                 const Mat M = mat_of(d, m);
                 float *out = m == 0 ? a.qkv : (m == 2 ? a.gu : a.x);
+                if (warp == EPI0 && lane == 0) progress(a, 5, (unsigned)(layer * 8 + m + 1));
                 if (m == 0 && (int)blockIdx.x < B) {
                     // input-norm statistic of utterance blockIdx.x (after the previous layer)
                     if (warp == EPI0 && wait_count_warp(a.cnt + (layer ? cidx(layer - 1, 4) : 0), G, c, 20)) {
@@ -832,6 +852,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
         }
         // ---- lm_head: scaled logits, running argmax per utterance
         const Mat M = mat_of(d, 4);
+        if (warp == EPI0 && lane == 0) progress(a, 5, (unsigned)(L * 8 + 5));
         if ((int)blockIdx.x < B && warp == EPI0 && wait_count_warp(a.cnt + cidx(L - 1, 4), G, c, 23)) {
             const float r = row_inv_rms(a.x, d.h, Bp, blockIdx.x, d.eps);
             if (lane == 0) st_tag(a.stats + ((size_t)L * 3 + 2) * 64 + blockIdx.x, r, ep);
@@ -919,14 +940,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
             __threadfence();
             signal(a.cnt + 0);
         }
-        // one X tile: wait for the stage, build it (warp xi % 8), hand it to the MMA
+        // One X tile, built by all builder warps: each waits for the stage (a
+        // warp is at most one tile ahead of the slowest, so its parity wait
+        // cannot alias an older phase), writes its part, and arrives.
+        const int my_b = bt % Bp;  // the utterance this thread fills in every tile
         auto x_tile = [&](auto fetch) {
             const int s = xi % NSX;
-            if ((int)(xi % NBLD) == bw && !warp_aborted(c)) {
-                bool ok = xi < (unsigned)NSX || mb_wait_warp(&S_.xempty[s], ((xi / NSX) - 1) & 1, c, 8);
+            if (!warp_aborted(c)) {
+                if (lane == 0) progress(a, 9 + bw, xi | 0x80000000u);
+                const bool ok = xi < (unsigned)NSX || mb_wait_warp(&S_.xempty[s], ((xi / NSX) - 1) & 1, c, 8);
+                if (lane == 0) progress(a, 9 + bw, xi);
                 if (ok) {
-                    build_tile(xring + (size_t)s * XST, Bp, B, fetch);
-                    if (lane == 0) mb_arrive(&S_.xfull[s]);
+                    build_tile(xring + (size_t)s * XST, Bp, B, bt, fetch);
+                    if (lane == 0) {
+                        mb_arrive(&S_.xfull[s]);
+                        if (bw == 0) progress(a, 6, xi + 1);
+                    }
                 }
             }
             xi++;
@@ -934,6 +963,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
         for (int layer = 0; layer < L; layer++) {
             const QdbLayerW &lw = layers[layer];
             // ---- QKV: X = x * w_in
+            if (bt == 0) progress(a, 7, (unsigned)(layer * 8 + 1));
             {
                 const Mat M = mat_of(d, 0);
                 int i0, i1;
@@ -945,6 +975,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                 }
             }
             // ---- attention units
+            if (bt == 0) progress(a, 7, (unsigned)(layer * 8 + 2));
             {
                 const int Sp = a.splits;
                 const int units = B * d.Hkv * Sp;
@@ -967,6 +998,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                 if (bt == 0) signal(a.cnt + cidx(layer, 1));
             }
             // ---- O: X = merged attention output (splits combined per utterance)
+            if (bt == 0) progress(a, 7, (unsigned)(layer * 8 + 3));
             {
                 const Mat M = mat_of(d, 1);
                 int i0, i1;
@@ -976,40 +1008,39 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                 for (int i = i0; i < i1; i++) {
                     const int k0 = (i % M.KB) * 64;
                     const int hq = k0 / QDB_HD, d0 = k0 % QDB_HD;
-                    // this lane's utterances (lane, lane + 32): weight of each split's partial
-                    float f[2][MAX_SPLITS];
-#pragma unroll
-                    for (int j = 0; j < 2; j++) {
-                        const int b = lane + 32 * j;
-                        float mx = -INFINITY, ls = 0.f, mv[MAX_SPLITS];
+                    // weight of each split's partial for this thread's utterance
+                    float f[MAX_SPLITS];
+                    {
+                        const int b = my_b;
+                        float mx = -INFINITY, ls = 0.f;
 #pragma unroll
                         for (int s = 0; s < MAX_SPLITS; s++) {
-                            mv[s] = (b < B && s < Sp)
-                                        ? __ldcg(a.part + (((size_t)b * d.Hq + hq) * Sp + s) * (2 + QDB_HD)) : -INFINITY;
-                            mx = fmaxf(mx, mv[s]);
+                            f[s] = (b < B && s < Sp)
+                                       ? __ldcg(a.part + (((size_t)b * d.Hq + hq) * Sp + s) * (2 + QDB_HD)) : -INFINITY;
+                            mx = fmaxf(mx, f[s]);
                         }
 #pragma unroll
                         for (int s = 0; s < MAX_SPLITS; s++) {
-                            f[j][s] = (mx == -INFINITY || mv[s] == -INFINITY) ? 0.f : expf(mv[s] - mx);
+                            f[s] = (mx == -INFINITY || f[s] == -INFINITY) ? 0.f : expf(f[s] - mx);
                             if (b < B && s < Sp)
-                                ls += __ldcg(a.part + (((size_t)b * d.Hq + hq) * Sp + s) * (2 + QDB_HD) + 1) * f[j][s];
+                                ls += __ldcg(a.part + (((size_t)b * d.Hq + hq) * Sp + s) * (2 + QDB_HD) + 1) * f[s];
                         }
                         const float inv = ls > 0.f ? 1.0f / ls : 0.f;
 #pragma unroll
-                        for (int s = 0; s < MAX_SPLITS; s++) f[j][s] *= inv;
+                        for (int s = 0; s < MAX_SPLITS; s++) f[s] *= inv;
                     }
                     x_tile([&](int kk, int b) {
                         const float *p = a.part + ((size_t)b * d.Hq + hq) * Sp * (2 + QDB_HD) + 2 + d0 + kk;
-                        const int j = b >> 5;
                         float o = 0.f;
 #pragma unroll
                         for (int s = 0; s < MAX_SPLITS; s++)
-                            if (s < Sp) o += f[j][s] * __ldcg(p + (size_t)s * (2 + QDB_HD));
+                            if (s < Sp) o += f[s] * __ldcg(p + (size_t)s * (2 + QDB_HD));
                         return o;
                     });
                 }
             }
             // ---- GU: X = x * w_post (after this layer's O)
+            if (bt == 0) progress(a, 7, (unsigned)(layer * 8 + 4));
             {
                 const Mat M = mat_of(d, 2);
                 int i0, i1;
@@ -1021,30 +1052,28 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                 }
             }
             // ---- DOWN: X = silu(r g) * (r u)
+            if (bt == 0) progress(a, 7, (unsigned)(layer * 8 + 5));
             {
                 const Mat M = mat_of(d, 3);
                 int i0, i1;
                 share(M, i0, i1);
-                float r2[2] = {0.f, 0.f};
+                float r2 = 0.f;  // post-attention-norm factor of this thread's utterance
                 if (i1 > i0) {
                     wait_count_warp(a.cnt + cidx(layer, 3), G, c, 35);
-                    for (int j = 0; j < 2; j++) {
-                        const int b = lane + 32 * j;
-                        if (b < B) r2[j] = poll_tag(a.stats + ((size_t)layer * 3 + 1) * 64 + b, ep, c, 36);
-                    }
+                    if (my_b < B) r2 = poll_tag(a.stats + ((size_t)layer * 3 + 1) * 64 + my_b, ep, c, 36);
                 }
                 for (int i = i0; i < i1; i++) {
                     const int k0 = (i % M.KB) * 64;
                     x_tile([&](int kk, int b) {
-                        const float r = r2[b >> 5];  // b is this lane's utterance (lane or lane + 32)
-                        const float g = __ldcg(a.gu + (size_t)(2 * (k0 + kk)) * Bp + b) * r;
-                        const float u = __ldcg(a.gu + (size_t)(2 * (k0 + kk) + 1) * Bp + b) * r;
+                        const float g = __ldcg(a.gu + (size_t)(2 * (k0 + kk)) * Bp + b) * r2;
+                        const float u = __ldcg(a.gu + (size_t)(2 * (k0 + kk) + 1) * Bp + b) * r2;
                         return silu_mul(g, u);
                     });
                 }
             }
         }
         // ---- lm_head: X = x * w_final (the 1/rms factor scales the logits)
+        if (bt == 0) progress(a, 7, (unsigned)(L * 8 + 6));
         {
             const Mat M = mat_of(d, 4);
             int t0, t1;

@@ -109,11 +109,20 @@ cudaError_t qdb_launch_qk_rope_append_single(const float *qkv, float *q_out, con
                                              int layer, int n, int Hq, int Hkv, const float *q_norm,
                                              const float *k_norm, const float2 *rope, float eps,
                                              cudaStream_t st);
-// Causal attention of n query rows of ONE session (rows at start_pos + i) on
-// the tensor cores (tcgen05); err: device error words (bounded waits).
-// hi/lo (optional): write the output as its bf16 split [n, Hq*128] instead of f32 out.
-cudaError_t qdb_launch_attn_prefill_tc(const float *q, const uint16_t *kc, const uint16_t *vc, int cap, int layer,
-                                       int start_pos, int n, int Hq, int Hkv, float *out, int *err, cudaStream_t st,
+// Causal prefill attention on the tensor cores (tcgen05) for several sessions
+// at once (qdb_attn_tc.cu). Segment = one session's prompt rows.
+struct QdbAttnSeg {
+    int row0;       // first row of the segment in q / out
+    int start_pos;  // position of that row
+    int n;          // rows
+    int cap;        // the session's KV capacity
+};
+// K or V cache map of one session over all layers (host memory, 128 bytes).
+int qdb_attn_kv_map(void *map, const uint16_t *cache, int L, int Hkv, int cap);
+// maps: device [2 * nseg] (K, V per segment); max_n: longest segment.
+// hi/lo (optional): write the output as its bf16 split [rows, Hq*128] instead of f32 out.
+cudaError_t qdb_launch_attn_prefill_tc(const void *maps, const QdbAttnSeg *segs, int nseg, int max_n, int layer,
+                                       int Hq, int Hkv, const float *q, float *out, int *err, cudaStream_t st,
                                        uint16_t *hi = nullptr, uint16_t *lo = nullptr);
 // Independent rows (one query each) over per-row caches.
 cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
@@ -149,6 +158,7 @@ struct QdbBatchArgs {
     unsigned *done;               // zero between launches
     unsigned epoch;               // tag of this launch's statistics (never 0)
     int *err;                     // [4]
+    unsigned *prog;               // nullable [grid][8]: progress of each role (read after a failed wait)
 };
 int qdb_bstep_ring_stages(int Bp, int R);
 size_t qdb_bstep_smem(int Bp, int R);

@@ -87,6 +87,9 @@ struct RowScratch {
     size_t part_cap = 0;
     QdbRowKV *rowkv = nullptr;
     int rowkv_cap = 0;
+    void *amaps = nullptr;         // device CUtensorMap [2 * aseg_cap]: K, V map of each prefill segment
+    QdbAttnSeg *asegs = nullptr;   // device [aseg_cap]
+    int aseg_cap = 0;
     int *tok = nullptr;
     size_t tok_cap = 0;
 };
@@ -98,6 +101,7 @@ struct BatchScratch {
     unsigned long long *stats = nullptr, *best = nullptr;
     unsigned *cnt = nullptr, *done = nullptr;
     int *err = nullptr;
+    unsigned *prog = nullptr;  // [sms][8] progress words (diagnostics)
     void *maps = nullptr;  // device CUtensorMap [4L + 1]
     int n_cnt = 0;
     unsigned epoch = 1;
@@ -316,9 +320,10 @@ extern "C" void qdb_model_free(qdb_model *m) {
     RowScratch &r = m->rs;
     cudaFree(r.X); cudaFree(r.XH); cudaFree(r.XL); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT);
     cudaFree(r.LOG); cudaFree(r.part); cudaFree(r.rowkv); cudaFree(r.tok); cudaFree(r.err); cudaFree(r.GU); cudaFree(r.step);
+    cudaFree(r.amaps); cudaFree(r.asegs);
     BatchScratch &b = m->bs;
     cudaFree(b.x); cudaFree(b.qkv); cudaFree(b.gu); cudaFree(b.part); cudaFree(b.stats); cudaFree(b.best);
-    cudaFree(b.cnt); cudaFree(b.done); cudaFree(b.err); cudaFree(b.maps);
+    cudaFree(b.cnt); cudaFree(b.done); cudaFree(b.err); cudaFree(b.maps); cudaFree(b.prog);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->h_tok) cudaFreeHost(m->h_tok);
     if (m->st) cudaStreamDestroy(m->st);
@@ -681,11 +686,21 @@ static int ensure_rows(qdb_model *m, int n, bool logits) {
     return 0;
 }
 
-// One transformer stack over the rows already in rs.X. single: all rows belong
-// to one session and are consecutive positions (prefill); otherwise row b uses
-// rowkv[b] at position rowkv[b].pos + pos_off (multi-utterance decode).
-static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, int pos_off, const qdb_session *s1,
-                    int start_pos, int max_ctx = 1, const int *step = nullptr) {
+// Prompt rows of a prefill: nseg sessions whose K/V maps and segments are in
+// rs.amaps / rs.asegs. per_row: rs.rowkv holds one entry per row (several
+// sessions); otherwise one entry for a single session whose row i is at
+// position rowkv[0].pos + i.
+struct PrefillPlan {
+    int nseg, max_n;
+    bool per_row;
+};
+
+// One transformer stack over the rows already in rs.X. pf: prefill rows
+// (causal attention over each session's cache, tensor cores); null: decode
+// rows, row b uses rowkv[b] at position rowkv[b].pos + pos_off (+ *step).
+static int run_rows(qdb_model *m, int n, const PrefillPlan *pf, const QdbRowKV *row0_dev, int pos_off, int max_ctx = 1,
+                    const int *step = nullptr) {
+    const bool single = pf != nullptr;
     if (launch_gate()) return -1;
     RowScratch &r = m->rs;
     const int h = m->cfg.hidden, I = m->cfg.intermediate, Hq = m->cfg.heads, Hkv = m->cfg.kv_heads;
@@ -728,9 +743,13 @@ static int run_rows(qdb_model *m, int n, bool single, const QdbRowKV *row0_dev, 
                                    qkvd));
         if (gemm(lw.qkv, r.QKV, qkvd, h, 0, qkv_split)) return -1;
         if (single) {
-            CK(qdb_launch_qk_rope_append_single(r.QKV, r.Q, row0_dev, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
-                                                m->cfg.eps, m->st));
-            CK(qdb_launch_attn_prefill_tc(r.Q, s1->kc, s1->vc, s1->cap, l, start_pos, n, Hq, Hkv, r.ATT, r.err, m->st,
+            if (pf->per_row)
+                CK(qdb_launch_qk_rope_append(r.QKV, r.Q, row0_dev, 0, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
+                                             m->cfg.eps, m->st));
+            else
+                CK(qdb_launch_qk_rope_append_single(r.QKV, r.Q, row0_dev, l, n, Hq, Hkv, lw.q_norm, lw.k_norm,
+                                                    m->rope, m->cfg.eps, m->st));
+            CK(qdb_launch_attn_prefill_tc(r.amaps, r.asegs, pf->nseg, pf->max_n, l, Hq, Hkv, r.Q, r.ATT, r.err, m->st,
                                           r.XH, r.XL));
         } else {
             CK(qdb_launch_qk_rope_append(r.QKV, r.Q, row0_dev, pos_off, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
@@ -767,23 +786,88 @@ static int check_rows_err(qdb_model *m) {
     return 0;
 }
 
+// Prefill of nsess sessions in one row batch: session i appends lens[i]
+// positions at starts[i]; embeds holds all rows back to back (host or device).
+static int prefill_rows(qdb_session *const *ss, int nsess, const int *lens, const int *starts, const float *embeds,
+                        bool device_ptr) {
+    g_err.clear();
+    if (!ss || nsess <= 0 || !lens || !starts) return fail("bad prefill arguments");
+    if (!ss[0]) return fail("null session");
+    qdb_model *m = ss[0]->m;
+    if (!m) return fail("session's model has been freed");
+    long long total = 0;
+    int max_n = 0;
+    for (int i = 0; i < nsess; i++) {
+        if (!ss[i]) return fail("null session %d", i);
+        if (ss[i]->m != m) return fail("session %d: sessions must share one (live) model", i);
+        if (lens[i] < 0 || starts[i] < 0) return fail("session %d: negative length or position", i);
+        total += lens[i];
+        max_n = std::max(max_n, lens[i]);
+    }
+    if (total == 0) return 0;
+    if (!embeds) return fail("null embeddings");
+    if (total > (1 << 22)) return fail("prefill of %lld rows exceeds the 4M-row limit", total);
+    const int T = (int)total;
+    if (set_dev(m)) return -1;
+    for (int i = 0; i < nsess; i++)
+        if (lens[i] && prep_pos(ss[i], starts[i] + lens[i] - 1)) return -1;
+    if (ensure_rows(m, T, false)) return -1;
+    RowScratch &r = m->rs;
+    if (nsess > r.aseg_cap) {
+        cudaFree(r.amaps);
+        cudaFree(r.asegs);
+        r.amaps = nullptr;
+        r.asegs = nullptr;
+        r.aseg_cap = 0;
+        unsigned char *mp = nullptr;
+        if (dev_alloc(&mp, (size_t)nsess * 256) || dev_alloc(&r.asegs, (size_t)nsess)) {
+            cudaFree(mp);
+            return -1;
+        }
+        r.amaps = mp;
+        r.aseg_cap = nsess;
+    }
+    const size_t h = m->cfg.hidden;
+    CK(cudaMemcpyAsync(r.X, embeds, (size_t)T * h * 4, device_ptr ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                       m->st));
+    // segments (empty ones dropped), their K/V maps, and the per-row KV targets
+    std::vector<unsigned char> maps;
+    std::vector<QdbAttnSeg> segs;
+    std::vector<QdbRowKV> rk;
+    int row = 0;
+    for (int i = 0; i < nsess; i++) {
+        if (!lens[i]) continue;
+        qdb_session *s = ss[i];
+        segs.push_back(QdbAttnSeg{row, starts[i], lens[i], s->cap});
+        const size_t at = maps.size();
+        maps.resize(at + 256);
+        if (qdb_attn_kv_map(maps.data() + at, s->kc, m->cfg.layers, m->cfg.kv_heads, s->cap) ||
+            qdb_attn_kv_map(maps.data() + at + 128, s->vc, m->cfg.layers, m->cfg.kv_heads, s->cap))
+            return fail("KV tensor map of session %d", i);
+        if (nsess > 1)
+            for (int j = 0; j < lens[i]; j++) rk.push_back(QdbRowKV{s->kc, s->vc, s->cap, starts[i] + j});
+        else
+            rk.push_back(QdbRowKV{s->kc, s->vc, s->cap, starts[i]});
+        row += lens[i];
+    }
+    CK(cudaMemcpyAsync(r.amaps, maps.data(), maps.size(), cudaMemcpyHostToDevice, m->st));
+    CK(cudaMemcpyAsync(r.asegs, segs.data(), sizeof(QdbAttnSeg) * segs.size(), cudaMemcpyHostToDevice, m->st));
+    CK(cudaMemcpyAsync(r.rowkv, rk.data(), sizeof(QdbRowKV) * rk.size(), cudaMemcpyHostToDevice, m->st));
+    const PrefillPlan pf{(int)segs.size(), max_n, nsess > 1};
+    const int rc = run_rows(m, T, &pf, r.rowkv, 0);
+    cudaError_t e = cudaStreamSynchronize(m->st);  // (the staging vectors outlive the copies)
+    if (rc) return -1;
+    if (e != cudaSuccess) return fail("prefill: %s", cudaGetErrorString(e));
+    return check_rows_err(m);
+}
+
 static int prefill_impl(qdb_session *s, const float *embeds, bool device_ptr, int seq_len, int start_pos) {
     g_err.clear();
     if (!s) return fail("null session");
     if (!s->m) return fail("session's model has been freed");
     if (seq_len < 0 || start_pos < 0) return fail("negative length or position");
     if (seq_len == 0) return 0;
-    if (!embeds) return fail("null embeddings");
-    qdb_model *m = s->m;
-    if (set_dev(m) || prep_pos(s, start_pos + seq_len - 1) || ensure_rows(m, seq_len, false)) return -1;
-    const size_t h = m->cfg.hidden;
-    CK(cudaMemcpyAsync(m->rs.X, embeds, (size_t)seq_len * h * 4,
-                       device_ptr ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, m->st));
-    QdbRowKV rk{s->kc, s->vc, s->cap, start_pos};
-    CK(cudaMemcpyAsync(m->rs.rowkv, &rk, sizeof(rk), cudaMemcpyHostToDevice, m->st));
-    if (run_rows(m, seq_len, true, m->rs.rowkv, 0, s, start_pos)) return -1;
-    CK(cudaStreamSynchronize(m->st));
-    return check_rows_err(m);
+    return prefill_rows(&s, 1, &seq_len, &start_pos, embeds, device_ptr);
 }
 
 extern "C" int qdb_prefill(qdb_session *s, const float *embeds, int seq_len, int start_pos) {
@@ -792,6 +876,16 @@ extern "C" int qdb_prefill(qdb_session *s, const float *embeds, int seq_len, int
 
 extern "C" int qdb_prefill_device(qdb_session *s, const float *embeds_dev, int seq_len, int start_pos) {
     return prefill_impl(s, embeds_dev, true, seq_len, start_pos);
+}
+
+extern "C" int qdb_prefill_batch(qdb_session *const *sessions, int n, const float *embeds, const int *seq_lens,
+                                 const int *start_pos) {
+    return prefill_rows(sessions, n, seq_lens, start_pos, embeds, false);
+}
+
+extern "C" int qdb_prefill_batch_device(qdb_session *const *sessions, int n, const float *embeds_dev,
+                                        const int *seq_lens, const int *start_pos) {
+    return prefill_rows(sessions, n, seq_lens, start_pos, embeds_dev, true);
 }
 
 static int batch_setup(qdb_session *const *ss, int n, const int *pos, int extra_steps, qdb_model **mo,
@@ -864,7 +958,7 @@ static int ensure_bstep(qdb_model *m) {
         dev_alloc(&b.gu, 2 * I * BSTEP_MAX_B) ||
         dev_alloc(&b.part, (size_t)BSTEP_MAX_B * m->cfg.heads * BSTEP_MAX_SPLITS * (2 + QDB_HD)) ||
         dev_alloc(&b.stats, (3 * L + 3) * 64) || dev_alloc(&b.best, 64) || dev_alloc(&b.cnt, (size_t)b.n_cnt) ||
-        dev_alloc(&b.done, 1) || dev_alloc(&b.err, 4)) {
+        dev_alloc(&b.done, 1) || dev_alloc(&b.err, 4) || dev_alloc(&b.prog, (size_t)m->sms * 17)) {
         std::string e = g_err;
         cudaFree(b.x); cudaFree(b.qkv); cudaFree(b.gu); cudaFree(b.part); cudaFree(b.stats); cudaFree(b.best);
         cudaFree(b.cnt); cudaFree(b.done); cudaFree(b.err);
@@ -879,6 +973,7 @@ static int ensure_bstep(qdb_model *m) {
     CK(cudaMemset(b.cnt, 0, (size_t)b.n_cnt * 4));
     CK(cudaMemset(b.done, 0, 4));
     CK(cudaMemset(b.err, 0, 16));
+    CK(cudaMemset(b.prog, 0, (size_t)m->sms * 17 * 4));
     // weight tensor maps: qkv, o, gu, down of every layer, then the embedding
     const int nmaps = 4 * (int)L + 1;
     std::vector<unsigned char> maps((size_t)nmaps * 128);
@@ -955,6 +1050,7 @@ static int launch_bstep(qdb_model *m, int n, int max_ctx, const int *tok_in, con
     if (++b.epoch == 0) b.epoch = 1;
     a.epoch = b.epoch;
     a.err = b.err;
+    a.prog = b.prog;
     (void)max_ctx;
     CK(qdb_launch_bstep(&a, m->sms, m->st));
     return 0;
@@ -964,13 +1060,34 @@ static int check_bstep_err(qdb_model *m) {
     int ev[4] = {0, 0, 0, 0};
     CK(cudaMemcpy(ev, m->bs.err, sizeof(ev), cudaMemcpyDeviceToHost));
     if (ev[0]) {
+        // progress of the CTA that gave up, and the slowest / fastest of each word over all CTAs
+        constexpr int PW = 17;
+        std::vector<unsigned> pg((size_t)m->sms * PW);
+        std::string prog;
+        if (cudaMemcpy(pg.data(), m->bs.prog, pg.size() * 4, cudaMemcpyDeviceToHost) == cudaSuccess) {
+            char buf[1024];
+            const int c = (ev[2] >= 0 && ev[2] < m->sms) ? ev[2] : 0;
+            int o = snprintf(buf, sizeof(buf), "; progress of CTA %d:", c);
+            for (int w = 0; w < PW; w++) o += snprintf(buf + o, sizeof(buf) - o, " %x", pg[(size_t)c * PW + w]);
+            o += snprintf(buf + o, sizeof(buf) - o, "; min/max:");
+            for (int w = 0; w < 9 && o < (int)sizeof(buf) - 24; w++) {
+                unsigned lo = ~0u, hi = 0;
+                for (int k = 0; k < m->sms; k++) {
+                    lo = std::min(lo, pg[(size_t)k * PW + w]);
+                    hi = std::max(hi, pg[(size_t)k * PW + w]);
+                }
+                o += snprintf(buf + o, sizeof(buf) - o, " %u/%u", lo, hi);
+            }
+            prog = buf;
+        }
         cudaMemset(m->bs.err, 0, sizeof(ev));
+        cudaMemset(m->bs.prog, 0, pg.size() * 4);
         cudaDeviceSynchronize();
-        return fail("device error code %d in the batched decode step (%s; check %d: %d %d)", ev[0],
+        return fail("device error code %d in the batched decode step (%s; check %d: %d %d%s)", ev[0],
                     ev[0] == 1   ? "a bounded wait ran out"
                     : ev[0] == 2 ? "invalid token or no argmax candidate"
                                  : "an access refused by a bounds check",
-                    ev[1], ev[2], ev[3]);
+                    ev[1], ev[2], ev[3], prog.c_str());
     }
     return 0;
 }
@@ -996,7 +1113,7 @@ extern "C" int qdb_forward_batch(qdb_session *const *sessions, int n, const floa
         CK(cudaStreamSynchronize(m->st));
         return check_bstep_err(m);
     }
-    auto step = [&]() { return run_rows(m, n, false, r.rowkv, 0, nullptr, 0, maxp + 1) || batch_tail(m, n, r.tok); };
+    auto step = [&]() { return run_rows(m, n, nullptr, r.rowkv, 0, maxp + 1) || batch_tail(m, n, r.tok); };
     const int S = std::min(64, std::max(1, (maxp + 1 + 64 * QDB_AR_ITERS - 1) / (64 * QDB_AR_ITERS)));
     // the captured launches bake in the row count, the split count, every
     // scratch pointer, the RoPE table (reallocated when a session grows past
@@ -1071,7 +1188,7 @@ extern "C" int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, cons
     CK(cudaMemsetAsync(r.step, 0, sizeof(int), m->st));
     auto one_step = [&]() -> int {
         CK(qdb_launch_embed_rows(m->embed, r.tok, r.X, n, m->cfg.hidden, m->cfg.vocab, m->st, r.step));
-        if (run_rows(m, n, false, r.rowkv, 0, nullptr, 0, ctx_last, r.step) || batch_tail(m, n, r.tok + n, r.step))
+        if (run_rows(m, n, nullptr, r.rowkv, 0, ctx_last, r.step) || batch_tail(m, n, r.tok + n, r.step))
             return -1;
         CK(qdb_launch_step_advance(r.step, m->st));
         return 0;

@@ -349,3 +349,31 @@ def test_batch_above_64_rows_uses_graph_path(pkg, synth):
     ref.prefill(emb[:10], 0)
     want, _, lg = ref.forward(emb[10], 10, want_logits=True)
     assert all(t == want for t in got) or margin_top2(lg, mask_eos=True) <= MARGIN
+
+
+def test_prefill_batch_equals_separate_prefills(pkg, synth):
+    """qdb_prefill_batch over sessions of different lengths and start
+    positions (one row batch, segmented tensor-core attention) leaves every
+    cache as separate qdb_prefill calls do: the next step's logits agree."""
+    cfg = synth.PRESETS["small"]
+    ws = synth.WeightSet(cfg, seed=33, norm_jitter=0.1)
+    model = pkg.Model(ws, device=0)
+    lens = [37, 1, 130, 0, 64]
+    starts = [0, 5, 12, 0, 0]
+    emb = [synth.audio_embeddings(cfg, st + L + 1, seed=600 + i) for i, (st, L) in enumerate(zip(starts, lens))]
+    sa = [model.session(8) for _ in lens]
+    sb = [model.session(256) for _ in lens]
+    for i, st in enumerate(starts):  # shared history before the batched part
+        if st:
+            sa[i].prefill(emb[i][:st], 0)
+            sb[i].prefill(emb[i][:st], 0)
+    pkg.prefill_batch(sa, [emb[i][starts[i]:starts[i] + lens[i]] for i in range(len(lens))], starts)
+    for i in range(len(lens)):
+        if lens[i]:
+            sb[i].prefill(emb[i][starts[i]:starts[i] + lens[i]], starts[i])
+    for i in range(len(lens)):
+        p = starts[i] + lens[i]
+        ta, _, la = sa[i].forward(emb[i][p], p, want_logits=True)
+        tb, _, lb = sb[i].forward(emb[i][p], p, want_logits=True)
+        assert_logits_close(la, lb, f"session {i}")
+        assert ta == tb or margin_top2(lb) <= MARGIN
