@@ -162,6 +162,20 @@ int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, const int *firs
  * (qwen_asr.c:606-607, :714-715) at the granularity of one step. */
 int qdb_trace_step(qdb_session *s, int token, int pos, unsigned long long *trace_out, int max_words);
 
+/* Profiling of the persistent batched step (qdb_forward_batch's path for up
+ * to 64 rows): runs one step like qdb_forward_batch (its tokens are dropped)
+ * with globaltimer stamps. trace_out receives [ctas][events] values (ns); the
+ * events of each CTA are, per layer: QKV inputs ready, QKV X tiles built,
+ * attention start, attention end, O inputs ready, QKV drained, O drained,
+ * DOWN drained; then lm_head inputs ready, lm_head drained, end. After those
+ * [ctas][events] words come [ctas][256] detail stamps of layer 1 (per CTA:
+ * 0..63 MMA item start, 64..127 X tile build start, 128..191 X tile built,
+ * 192..223 epilogue segment ready, 224..255 segment drained; 0 = unused), so
+ * max_words must hold ctas * (events + 256). Returns the number of events per
+ * CTA, or -1. */
+int qdb_trace_batch_step(qdb_session *const *sessions, int n, const float *embeds, const int *pos,
+                         unsigned long long *trace_out, int max_words);
+
 /* One decode step that allocates nothing. No counterpart in the reference.
  *
  * For callers that must not allocate GPU memory while decoding: code running

@@ -68,6 +68,8 @@ ABI = {
     "qdb_model_set_wait_limit": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_longlong]),
     "qdb_trace_step": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                       ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]),
+    "qdb_trace_batch_step": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _f32p, _i32p,
+                                            ctypes.POINTER(ctypes.c_uint64), ctypes.c_int]),
 }
 
 
@@ -277,6 +279,24 @@ def forward_batch(sessions, embeds: np.ndarray, pos, want_logits: bool = False):
                              _ptr(log, _f32p) if log is not None else None):
         raise _err("qdb_forward_batch")
     return (out, log) if want_logits else out
+
+
+def trace_batch_step(sessions, embeds: np.ndarray, pos, max_ctas: int = 1024) -> np.ndarray:
+    """One persistent batched step with per-phase globaltimer stamps: returns
+    ([ctas, events], [ctas, 256] layer-1 detail) ns (include/qwen_asr_b200.h)."""
+    n = len(sessions)
+    L = sessions[0].model.cfg.layers
+    ev = 8 * L + 3
+    e = np.ascontiguousarray(embeds, dtype=np.float32)
+    p = np.ascontiguousarray(pos, dtype=np.int32)
+    buf = np.zeros(max_ctas * (ev + 256), np.uint64)
+    k = lib.qdb_trace_batch_step(_handles(sessions), n, _ptr(e, _f32p), _ptr(p, _i32p),
+                                 buf.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), buf.size)
+    if k < 0:
+        raise _err("qdb_trace_batch_step")
+    t = buf[:max_ctas * ev].reshape(-1, ev)
+    ctas = int((t[:, -1] != 0).sum())
+    return t[:ctas], buf[ctas * ev:ctas * ev + ctas * 256].reshape(ctas, 256)
 
 
 def decode_greedy_batch(sessions, first_tokens, pos, n_steps: int) -> np.ndarray:

@@ -68,10 +68,14 @@ constexpr int BLD0 = 6, NBLD = 8;      // builder warps 6..13
 constexpr int NACC = 8;                // accumulator slots in TMEM
 constexpr int W_TILE = 128 * 64 * 2;   // one weight tile (16 KB)
 constexpr int MAX_NSW = 8;             // W ring stages (at most)
-constexpr int NSX = 4;                 // X ring stages
+constexpr int NGRP = 4, GRP_WARPS = 2;  // builder groups: group g builds X tiles xi % 4 == g
+constexpr int GRP_T = GRP_WARPS * 32;
+constexpr int NSX = NGRP;              // X ring stages (stage g belongs to group g)
+constexpr int AK = 64;                 // keys per attention chunk
+constexpr int ACHUNK = AK * QDB_HD * 2 * 2;  // K + V of one chunk (32 KB)
+constexpr int XRING_MIN = 2 * ACHUNK;  // the X ring doubles as the attention K/V staging (2 chunks)
 constexpr int MAX_LAYERS = 32;
 constexpr int ATT_KEYS = 8;            // keys per builder warp per attention step
-constexpr int MAX_SPLITS = 8;          // key splits per (utterance, KV head)
 
 // ---------------------------------------------------------------- small helpers
 __device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -164,6 +168,25 @@ __device__ bool mb_wait_warp(u64 *b, unsigned par, const Ctl &c, int site) {
 constexpr int PROG_WORDS = 17;
 __device__ __forceinline__ void progress(const QdbBatchArgs &a, int w, unsigned v) {
     if (a.prog) *(volatile unsigned *)(a.prog + blockIdx.x * PROG_WORDS + w) = v;
+}
+
+__device__ __forceinline__ void stamp(const QdbBatchArgs &a, int idx) {
+    if (a.trace) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        a.trace[(size_t)blockIdx.x * qdb_bstep_trace_events(a.d.L) + idx] = t;
+    }
+}
+
+// Detail stamps of layer 1 (profiling): slot = 0..63 MMA item start (both
+// operands ready), 64..127 X tile build start, 128..191 X tile built, 192..223
+// epilogue segment ready, 224..255 segment drained; index within the layer.
+__device__ __forceinline__ void dstamp(const QdbBatchArgs &a, int slot) {
+    if (a.detail && slot >= 0 && slot < 256) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        a.detail[(size_t)blockIdx.x * 256 + slot] = t;
+    }
 }
 
 // Phase counter: this CTA's part is done (the caller fenced its writes).
@@ -315,46 +338,84 @@ struct Smem {
     u64 wfull[MAX_NSW], wempty[MAX_NSW];
     u64 xfull[NSX], xempty[NSX];
     u64 accfull[NACC], accempty[NACC];
+    u64 afull[2];  // attention K/V chunks (staged in the X ring)
     u64 mma_done;
     uint32_t tmem;
     int abort;
 };
 
 // ---------------------------------------------------------------- builders: X tiles
+// L2 load (activations are written by other SMs during the launch: never
+// through L1).
+__device__ __forceinline__ float ld_l2(const float *p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+
+// X tile sources: the tile's value at (utterance b, column k0 + k) is
+//   XW      src[(k0+k)*Bp + b] * w[k0+k]                  (norm weight)
+//   PLAIN   src[(k0+k)*Bp + b]
+//   SWIGLU  silu(r g) * (r u), g = src[2(k0+k)*Bp + b], u = src[(2(k0+k)+1)*Bp + b]
+enum { SRC_XW = 0, SRC_PLAIN = 1, SRC_SWIGLU = 2 };
+
 // Writes the X tile (Bp rows = utterances, 64 columns = k0..k0+63) into the
 // stage as bf16 hi and lo with the 128-byte swizzle: element (b, k) at byte
-// (b/8)*1024 + (b%8)*128 + (((k/8) ^ (b%8)) * 16) + (k%8)*2. All 8 builder
-// warps build every tile together: builder thread bt takes utterance
-// b = bt % Bp and the 8-column chunks bt / Bp, bt / Bp + 256 / Bp, ... The f32
-// source value of (b, k0 + k) is `fetch(k, b)`; for a fixed k consecutive
+// (b/8)*1024 + (b%8)*128 + (((k/8) ^ (b%8)) * 16) + (k%8)*2. A group of 2
+// builder warps builds a tile: thread gt takes utterance b = gt % Bp and the
+// 8-column chunks gt / Bp + i * (64 / Bp); for a fixed column consecutive
 // threads read consecutive utterances, which the [feature][Bp] layout of every
-// activation buffer makes one coalesced access.
-template <typename F>
-__device__ __forceinline__ void build_tile(unsigned char *xs, int Bp, int B, int bt, F fetch) {
+// activation buffer makes one coalesced access. All loads of a round (4 chunks,
+// 2 for SwiGLU) are issued before the first value is used.
+template <int MODE>
+__device__ __forceinline__ void build_tile(unsigned char *xs, int Bp, int B, int gt, const float *src,
+                                           const float *w, float r, int k0) {
+    constexpr int TPR = MODE == SRC_SWIGLU ? 2 : 4;  // chunks per round
     unsigned char *hi = xs, *lo = xs + Bp * 128;
-    const int b = bt % Bp;
+    const int b = gt % Bp, c0 = gt / Bp, cstep = GRP_T / Bp, ntask = 8 / cstep;
     const uint32_t rb = (uint32_t)(b >> 3) * 1024u + (uint32_t)(b & 7) * 128u;
-    for (int cc = bt / Bp; cc < 8; cc += (NBLD * 32) / Bp) {
-        float v[8];
-        if (b < B) {
+    for (int t0 = 0; t0 < ntask; t0 += TPR) {
+        float v[TPR][8], u[MODE == SRC_SWIGLU ? TPR : 1][8];
 #pragma unroll
-            for (int i = 0; i < 8; i++) v[i] = fetch(cc * 8 + i, b);
-        } else {
+        for (int t = 0; t < TPR; t++) {
+            const int k = k0 + (c0 + (t0 + t) * cstep) * 8;
+            const bool live = t0 + t < ntask && b < B;
 #pragma unroll
-            for (int i = 0; i < 8; i++) v[i] = 0.f;
+            for (int i = 0; i < 8; i++) {
+                if (MODE == SRC_SWIGLU) {
+                    v[t][i] = live ? ld_l2(src + (size_t)(2 * (k + i)) * Bp + b) : 0.f;
+                    u[t][i] = live ? ld_l2(src + (size_t)(2 * (k + i) + 1) * Bp + b) : 0.f;
+                } else {
+                    v[t][i] = live ? ld_l2(src + (size_t)(k + i) * Bp + b) : 0.f;
+                }
+            }
         }
-        uint32_t h[4], l[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint16_t h0 = f32_to_bf16_rn(v[2 * i]), h1 = f32_to_bf16_rn(v[2 * i + 1]);
-            const uint16_t l0 = f32_to_bf16_rn(v[2 * i] - __uint_as_float((uint32_t)h0 << 16));
-            const uint16_t l1 = f32_to_bf16_rn(v[2 * i + 1] - __uint_as_float((uint32_t)h1 << 16));
-            h[i] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-            l[i] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+        for (int t = 0; t < TPR; t++) {
+            if (t0 + t >= ntask) break;
+            const int cc = c0 + (t0 + t) * cstep;
+            if (MODE == SRC_XW) {
+                const float4 wa = __ldg(reinterpret_cast<const float4 *>(w + k0 + cc * 8));
+                const float4 wb = __ldg(reinterpret_cast<const float4 *>(w + k0 + cc * 8 + 4));
+                v[t][0] *= wa.x; v[t][1] *= wa.y; v[t][2] *= wa.z; v[t][3] *= wa.w;
+                v[t][4] *= wb.x; v[t][5] *= wb.y; v[t][6] *= wb.z; v[t][7] *= wb.w;
+            } else if (MODE == SRC_SWIGLU) {
+#pragma unroll
+                for (int i = 0; i < 8; i++) v[t][i] = silu_mul(v[t][i] * r, u[t][i] * r);
+            }
+            uint32_t h[4], l[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint16_t h0 = f32_to_bf16_rn(v[t][2 * i]), h1 = f32_to_bf16_rn(v[t][2 * i + 1]);
+                const uint16_t l0 = f32_to_bf16_rn(v[t][2 * i] - __uint_as_float((uint32_t)h0 << 16));
+                const uint16_t l1 = f32_to_bf16_rn(v[t][2 * i + 1] - __uint_as_float((uint32_t)h1 << 16));
+                h[i] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+                l[i] = (uint32_t)l0 | ((uint32_t)l1 << 16);
+            }
+            const uint32_t off = rb + (uint32_t)((cc ^ (b & 7)) * 16);
+            *reinterpret_cast<uint4 *>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<uint4 *>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
         }
-        const uint32_t off = rb + (uint32_t)((cc ^ (b & 7)) * 16);
-        *reinterpret_cast<uint4 *>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4 *>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
     }
     // generic-proxy writes -> visible to the tensor core's async proxy
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -369,6 +430,7 @@ struct AttnSm {
     float2 rope[QDB_HD / 2];
     float m[NBLD][8], l[NBLD][8];
     float r1;
+    int last;  // this unit merges the splits of its (utterance, KV head)
 };
 
 // Per-head RMSNorm then NeoX rotation of one 128-float head in smem, one warp
@@ -402,11 +464,29 @@ __device__ __forceinline__ void work_sync() {  // builders + epilogue
     asm volatile("bar.sync 3, %0;" ::"n"((NBLD + NEPI) * 32) : "memory");
 }
 
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, u64 *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(su32(dst)),
+        "l"(src), "r"(bytes), "r"(su32(bar))
+        : "memory");
+}
+
 // One attention unit (utterance b, KV head g, split s of S) by the 8 builder
-// warps: partial (m, l, o[128]) of each of the R query heads into part.
+// warps: partial (m, l, o[128]) of each of the R query heads. The unit's keys
+// [p0, p1) are contiguous in the cache: thread 0 streams them in 64-key
+// chunks (K and V, 32 KB) with cp.async.bulk into two stages of the X ring
+// (idle between the QKV and O phases); the first two chunks are requested
+// before q/k/v are read. Each warp takes 8 keys of a chunk: 4 lanes per key
+// over 32 dims for q.k (16-byte pieces rotated per lane against bank
+// conflicts), then 4 dims per lane for p.V; the R query heads share every K/V
+// read. This step's own row (position pos) comes from smem, rounded like the
+// cache. ach: chunks streamed so far by this CTA (stage / parity of the next).
+// Partials go to part in [feature][Bp] layout: o at ((s*qd + head*128 + d) *
+// Bp + b), then (m, l) at (qd*S*Bp + ((s*Hq + head)*2 + {0,1}) * Bp + b).
 template <int R>
 __device__ void attn_unit(const QdbBatchArgs &a, const QdbLayerW &lw, int layer, int b, int g, int s, int S,
-                          float r1, AttnSm *sm, float *obuf, const Ctl &c) {
+                          float r1, AttnSm *sm, float *obuf, unsigned char *stg, u64 *afull, unsigned &ach,
+                          const Ctl &c) {
     const QdbDims &d = a.d;
     const int lane = threadIdx.x & 31, warp = (threadIdx.x >> 5) - BLD0, t = threadIdx.x - BLD0 * 32;
     const QdbRowKV rk = a.rows[b];
@@ -420,6 +500,19 @@ __device__ void attn_unit(const QdbBatchArgs &a, const QdbLayerW &lw, int layer,
     uint16_t *kc = rk.kc + head_base;
     uint16_t *vc = rk.vc + head_base;
     const bool owns_new = (p0 <= pos && pos < p1);
+    const int nch = p1 > p0 ? (p1 - p0 + AK - 1) / AK : 0;
+    auto issue = [&](int ci) {
+        const unsigned it = ach + (unsigned)ci;
+        unsigned char *st = stg + (size_t)(it & 1) * ACHUNK;
+        const int k0 = p0 + ci * AK;
+        const unsigned bytes = (unsigned)(min(AK, p1 - k0) * QDB_HD * 2);
+        mb_expect(&afull[it & 1], 2 * bytes);
+        bulk_g2s(st, kc + (size_t)k0 * QDB_HD, bytes, &afull[it & 1]);
+        bulk_g2s(st + AK * QDB_HD * 2, vc + (size_t)k0 * QDB_HD, bytes, &afull[it & 1]);
+    };
+    int issued = 0;  // (thread 0)
+    if (t == 0)
+        for (; issued < nch && issued < 2; issued++) issue(issued);
     // q/k/v of this utterance (column b of qkv), times the input-norm factor
     for (int i = t; i < (R + 2) * QDB_HD; i += NBLD * 32) {
         const int hh = i / QDB_HD, dd = i % QDB_HD;
@@ -464,22 +557,30 @@ __device__ void attn_unit(const QdbBatchArgs &a, const QdbLayerW &lw, int layer,
 #pragma unroll
         for (int e = 0; e < 4; e++) o[h][e] = 0.f;
     }
-    if (!warp_aborted(c)) {
-        for (int base = p0 + warp * ATT_KEYS; base < p1; base += NBLD * ATT_KEYS) {
+    for (int ci = 0; ci < nch; ci++) {
+        const unsigned it = ach + (unsigned)ci;
+        const unsigned char *st = stg + (size_t)(it & 1) * ACHUNK;
+        const bool ok = !warp_aborted(c) && mb_wait_warp(&afull[it & 1], (it >> 1) & 1, c, 40);
+        if (ok) {
+            const int base = p0 + ci * AK + warp * ATT_KEYS;  // this warp's 8 keys
             const int j = base + kk;
             const bool valid = j < p1;
             uint4 kv4[4];
+            const int rot = (sub + kk) & 3;
             if (valid) {
-                if (j == pos) {  // this step's row, from smem (same rounding as the cache)
+                if (j == pos) {
                     const float *kn = sm->knew + sub * 32;
 #pragma unroll
-                    for (int u = 0; u < 4; u++)
-                        kv4[u] = make_uint4(kv_pack2(kn[u * 8 + 0], kn[u * 8 + 1]), kv_pack2(kn[u * 8 + 2], kn[u * 8 + 3]),
-                                            kv_pack2(kn[u * 8 + 4], kn[u * 8 + 5]), kv_pack2(kn[u * 8 + 6], kn[u * 8 + 7]));
+                    for (int u = 0; u < 4; u++) {
+                        const int uu = (u + rot) & 3;
+                        kv4[u] = make_uint4(kv_pack2(kn[uu * 8 + 0], kn[uu * 8 + 1]), kv_pack2(kn[uu * 8 + 2], kn[uu * 8 + 3]),
+                                            kv_pack2(kn[uu * 8 + 4], kn[uu * 8 + 5]), kv_pack2(kn[uu * 8 + 6], kn[uu * 8 + 7]));
+                    }
                 } else {
-                    const uint4 *kp = reinterpret_cast<const uint4 *>(kc + (size_t)j * QDB_HD + sub * 32);
+                    const uint4 *kp = reinterpret_cast<const uint4 *>(st + (size_t)(warp * ATT_KEYS + kk) * QDB_HD * 2) +
+                                      sub * 4;
 #pragma unroll
-                    for (int u = 0; u < 4; u++) kv4[u] = __ldcg(kp + u);
+                    for (int u = 0; u < 4; u++) kv4[u] = kp[(u + rot) & 3];
                 }
             }
             uint2 vv[ATT_KEYS];
@@ -491,21 +592,25 @@ __device__ void attn_unit(const QdbBatchArgs &a, const QdbLayerW &lw, int layer,
                     vv[tt] = make_uint2(kv_pack2(sm->vnew[lane * 4], sm->vnew[lane * 4 + 1]),
                                         kv_pack2(sm->vnew[lane * 4 + 2], sm->vnew[lane * 4 + 3]));
                 else
-                    vv[tt] = __ldcg(reinterpret_cast<const uint2 *>(vc + (size_t)jt * QDB_HD + lane * 4));
+                    vv[tt] = *reinterpret_cast<const uint2 *>(st + AK * QDB_HD * 2 +
+                                                              (size_t)(warp * ATT_KEYS + tt) * QDB_HD * 2 + lane * 8);
             }
             float sc[R];
 #pragma unroll
             for (int h = 0; h < R; h++) {
-                float acc = 0.f;
+                float a0 = 0.f, a1 = 0.f;
                 if (valid) {
                     const float *qv = sm->q[h] + sub * 32;
 #pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const float4 qa = *reinterpret_cast<const float4 *>(qv + u * 8);
-                        const float4 qb = *reinterpret_cast<const float4 *>(qv + u * 8 + 4);
-                        acc = dot8_kv(kv4[u], qa, qb, acc);
+                    for (int u = 0; u < 4; u += 2) {
+                        const int ua = (u + rot) & 3, ub = (u + 1 + rot) & 3;
+                        a0 = dot8_kv(kv4[u], *reinterpret_cast<const float4 *>(qv + ua * 8),
+                                     *reinterpret_cast<const float4 *>(qv + ua * 8 + 4), a0);
+                        a1 = dot8_kv(kv4[u + 1], *reinterpret_cast<const float4 *>(qv + ub * 8),
+                                     *reinterpret_cast<const float4 *>(qv + ub * 8 + 4), a1);
                     }
                 }
+                float acc = a0 + a1;
                 acc += __shfl_xor_sync(0xffffffffu, acc, 1);
                 acc += __shfl_xor_sync(0xffffffffu, acc, 2);
                 sc[h] = valid ? acc * scale : -INFINITY;
@@ -537,7 +642,15 @@ __device__ void attn_unit(const QdbBatchArgs &a, const QdbLayerW &lw, int layer,
                 m[h] = mn;
             }
         }
+        bld_sync();  // every warp is done with this stage
+        if (t == 0 && ci + 2 < nch && !*c.abort) issue(issued++);
     }
+    if (t == 0)  // after an abort, the copies still in flight land before the stage is reused or the CTA exits
+        for (int ci = issued > 2 ? issued - 2 : 0; ci < issued; ci++) {
+            const unsigned it = ach + (unsigned)ci;
+            mb_wait(&afull[it & 1], (it >> 1) & 1, c, false, 41);
+        }
+    ach += (unsigned)nch;
     // merge the warps' partials; write the unit's partial of each query head
 #pragma unroll
     for (int h = 0; h < R; h++) {
@@ -549,6 +662,10 @@ __device__ void attn_unit(const QdbBatchArgs &a, const QdbLayerW &lw, int layer,
         for (int e = 0; e < 4; e++) obuf[((size_t)warp * R + h) * QDB_HD + lane * 4 + e] = o[h][e];
     }
     bld_sync();
+    // One split: the normalised output goes straight to attn [qd][Bp]. Several:
+    // each unit writes its partial; the last of the S units of (b, g) to
+    // finish (a counter per (b, g), reset by that unit) merges them.
+    float *part_ml = a.part + (size_t)qd * S * Bp;
     for (int i = t; i < R * QDB_HD; i += NBLD * 32) {
         const int h = i / QDB_HD, dd = i % QDB_HD;
         float M = -INFINITY;
@@ -563,12 +680,44 @@ __device__ void attn_unit(const QdbBatchArgs &a, const QdbLayerW &lw, int layer,
                 O += obuf[((size_t)w * R + h) * QDB_HD + dd] * f;
             }
         }
-        float *dst = a.part + (((size_t)b * d.Hq + g * R + h) * S + s) * (2 + QDB_HD);
-        if (dd == 0) {
-            dst[0] = M;
-            dst[1] = L;
+        const int head = g * R + h;
+        if (S == 1) {
+            a.attn[((size_t)head * QDB_HD + dd) * Bp + b] = L > 0.f ? O / L : 0.f;
+        } else {
+            a.part[((size_t)s * qd + head * QDB_HD + dd) * Bp + b] = O;
+            if (dd == 0) {
+                part_ml[(((size_t)s * d.Hq + head) * 2 + 0) * Bp + b] = M;
+                part_ml[(((size_t)s * d.Hq + head) * 2 + 1) * Bp + b] = L;
+            }
         }
-        dst[2 + dd] = O;
+    }
+    if (S > 1) {
+        __threadfence();
+        bld_sync();
+        if (t == 0) {
+            unsigned *cnt = a.acnt + (size_t)b * d.Hkv + g;
+            const unsigned prev = atomicAdd(cnt, 1u);
+            sm->last = prev == (unsigned)(S - 1);
+            if (sm->last) atomicExch(cnt, 0u);
+            __threadfence();
+        }
+        bld_sync();
+        if (sm->last) {
+            for (int i = t; i < R * QDB_HD; i += NBLD * 32) {
+                const int h = i / QDB_HD, dd = i % QDB_HD, head = g * R + h;
+                float M = -INFINITY;
+                for (int q = 0; q < S; q++) M = fmaxf(M, ld_l2(part_ml + (((size_t)q * d.Hq + head) * 2) * Bp + b));
+                float L = 0.f, O = 0.f;
+                if (M != -INFINITY)
+                    for (int q = 0; q < S; q++) {
+                        const float mq = ld_l2(part_ml + (((size_t)q * d.Hq + head) * 2) * Bp + b);
+                        const float f = mq == -INFINITY ? 0.f : expf(mq - M);
+                        L += ld_l2(part_ml + (((size_t)q * d.Hq + head) * 2 + 1) * Bp + b) * f;
+                        O += ld_l2(a.part + ((size_t)q * qd + head * QDB_HD + dd) * Bp + b) * f;
+                    }
+                a.attn[((size_t)head * QDB_HD + dd) * Bp + b] = L > 0.f ? O / L : 0.f;
+            }
+        }
     }
     bld_sync();  // smem reused by the next unit
 }
@@ -602,7 +751,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
     unsigned char *wring = smem;
     unsigned char *xring = wring + (size_t)NSW * W_TILE;
     const int XST = 2 * Bp * 128;  // one X stage: hi + lo
-    AttnSm *asm_ = reinterpret_cast<AttnSm *>(xring + (size_t)NSX * XST);
+    const int xring_bytes = NSX * XST > XRING_MIN ? NSX * XST : XRING_MIN;
+    AttnSm *asm_ = reinterpret_cast<AttnSm *>(xring + (size_t)xring_bytes);
     float *obuf = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(asm_) + sizeof(AttnSm));
     const Ctl c{&S_.abort, a.err};
     const unsigned ep = a.epoch;
@@ -615,9 +765,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
             mb_init(&S_.wempty[i], 1);
         }
         for (int i = 0; i < NSX; i++) {
-            mb_init(&S_.xfull[i], NBLD);  // every builder warp writes part of each X tile
+            mb_init(&S_.xfull[i], GRP_WARPS);  // both warps of the owning builder group write the tile
             mb_init(&S_.xempty[i], 1);
         }
+        for (int i = 0; i < 2; i++) mb_init(&S_.afull[i], 1);
         for (int i = 0; i < NACC; i++) {
             mb_init(&S_.accfull[i], 1);
             mb_init(&S_.accempty[i], NEPI);
@@ -687,6 +838,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
         if (lane == 0) {
             const uint32_t idesc = instr_desc(128, Bp);
             unsigned wi = 0, xi = 0, seg = 0;
+            int l1_item = -1000;  // item index within layer 1 (detail stamps)
             bool ok = true;
             // one item: W stage wi x X stage xi into accumulator slot
             auto item = [&](uint32_t acc, bool first, bool last_x) -> bool {
@@ -696,6 +848,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                 progress(a, 8, 4);
                 if (!mb_wait(&S_.xfull[xs], (xi / NSX) & 1, c, true, 4)) return false;
                 progress(a, 8, 0);
+                dstamp(a, l1_item++);
                 tc_fence_after();
                 const uint32_t wb = su32(wring + (size_t)ws * W_TILE);
                 const uint32_t xb = su32(xring + (size_t)xs * XST);
@@ -727,6 +880,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
             };
             for (int layer = 0; layer < L && ok; layer++)
                 for (int m = 0; m < 4 && ok; m++) {
+                    if (layer == 1 && m == 0) l1_item = 0;
+                    if (layer == 2 && m == 0) l1_item = -1000;
                     const Mat M = mat_of(d, m);
                     int i0, i1;
                     share(M, i0, i1);
@@ -764,6 +919,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
         const int q = warp & 3;  // TMEM lanes 32q..32q+31
         const int et = threadIdx.x - EPI0 * 32;
         unsigned seg = 0;
+        int l1_seg = -1000;
         bool ok = true;
         // waits for accumulator slot of segment sg; uniform over the warp
         auto acc_ready = [&](unsigned sg) -> bool {
@@ -782,6 +938,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
             __threadfence();
             epi_sync();
             if (et == 0) signal(a.cnt + idx);
+        };
+        auto epi_stamp = [&](int idx) {
+            if (et == 0) stamp(a, idx);
         };
         // ---- set-up: clear the accumulation targets of layer 0 (qkv, gu)
         {
@@ -826,10 +985,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                 }
                 int i0, i1;
                 share(M, i0, i1);
+                if (layer == 1 && m == 0) l1_seg = 0;
+                if (layer == 2) l1_seg = -1000;
                 for (int i = i0; i < i1;) {
                     const int tile = i / M.KB;
                     const int iend = min(i1, (tile + 1) * M.KB);
-                    if (acc_ready(seg)) {
+                    const bool rdy = acc_ready(seg);
+                    if (et == 0) dstamp(a, 192 + l1_seg);
+                    if (rdy) {
                         const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((seg % NACC) * Bp);
                         const int row = tile * 128 + 32 * q + lane;
                         float *dst = out + (size_t)row * Bp;
@@ -844,10 +1007,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                         ok = false;
                     }
                     acc_release(seg);
+                    if (et == 0) dstamp(a, 224 + l1_seg);
+                    l1_seg++;
                     seg++;
                     i = iend;
                 }
                 phase_done(cidx(layer, m == 0 ? 0 : m + 1));
+                if (m == 0) epi_stamp(layer * 8 + 5);
+                if (m == 1) epi_stamp(layer * 8 + 6);
+                if (m == 3) epi_stamp(layer * 8 + 7);
             }
         }
         // ---- lm_head: scaled logits, running argmax per utterance
@@ -897,6 +1065,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                 acc_release(seg);
             }
         }
+        epi_stamp(8 * L + 1);
         // combine the 4 epilogue warps, then the CTA's candidates go to the global keys
         lm_best[q][lane] = best[0];
         lm_best[q][lane + 32] = best[1];
@@ -940,46 +1109,65 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
             __threadfence();
             signal(a.cnt + 0);
         }
-        // One X tile, built by all builder warps: each waits for the stage (a
-        // warp is at most one tile ahead of the slowest, so its parity wait
-        // cannot alias an older phase), writes its part, and arrives.
-        const int my_b = bt % Bp;  // the utterance this thread fills in every tile
-        auto x_tile = [&](auto fetch) {
+        // X tile xi is built by builder group xi % NGRP (2 warps) into stage
+        // xi % NSX, which only that group ever writes: a group waits for its
+        // own stage's previous tile, so its parity wait cannot alias an older
+        // phase. Up to NGRP tiles are built at once.
+        const int grp = bw / GRP_WARPS, gt = bt % GRP_T;
+        int l1_tile = -1000;  // X tile index within layer 1 (detail stamps)
+        const int my_b = gt % Bp;  // the utterance this thread fills in every tile
+        auto x_tile = [&](int mode, const float *src, const float *w, float r, int k0) {
             const int s = xi % NSX;
-            if (!warp_aborted(c)) {
+            if ((int)(xi % NGRP) == grp && !warp_aborted(c)) {
                 if (lane == 0) progress(a, 9 + bw, xi | 0x80000000u);
                 const bool ok = xi < (unsigned)NSX || mb_wait_warp(&S_.xempty[s], ((xi / NSX) - 1) & 1, c, 8);
                 if (lane == 0) progress(a, 9 + bw, xi);
                 if (ok) {
-                    build_tile(xring + (size_t)s * XST, Bp, B, bt, fetch);
+                    if (gt == 0) dstamp(a, 64 + l1_tile);
+                    unsigned char *xs = xring + (size_t)s * XST;
+                    if (mode == SRC_XW) build_tile<SRC_XW>(xs, Bp, B, gt, src, w, r, k0);
+                    else if (mode == SRC_PLAIN) build_tile<SRC_PLAIN>(xs, Bp, B, gt, src, w, r, k0);
+                    else build_tile<SRC_SWIGLU>(xs, Bp, B, gt, src, w, r, k0);
+                    if (gt == 0) dstamp(a, 128 + l1_tile);
                     if (lane == 0) {
                         mb_arrive(&S_.xfull[s]);
-                        if (bw == 0) progress(a, 6, xi + 1);
+                        if ((bw & 1) == 0) progress(a, 6, xi + 1);
                     }
                 }
             }
             xi++;
+            l1_tile++;
         };
+        // phase start: one warp polls the counter, the builders then move together
+        auto phase_wait = [&](int idx, int site) {
+            if (bw == 0) wait_count_warp(a.cnt + idx, G, c, site);
+            bld_sync();
+        };
+        unsigned ach = 0;  // attention chunks streamed by this CTA
         for (int layer = 0; layer < L; layer++) {
             const QdbLayerW &lw = layers[layer];
+            l1_tile = layer == 1 ? 0 : -1000;
             // ---- QKV: X = x * w_in
             if (bt == 0) progress(a, 7, (unsigned)(layer * 8 + 1));
             {
                 const Mat M = mat_of(d, 0);
                 int i0, i1;
                 share(M, i0, i1);
-                if (i1 > i0) wait_count_warp(a.cnt + (layer ? cidx(layer - 1, 4) : 0), G, c, 30);
+                phase_wait(layer ? cidx(layer - 1, 4) : 0, 30);
+                if (bt == 0) stamp(a, layer * 8 + 0);
                 for (int i = i0; i < i1; i++) {
                     const int k0 = (i % M.KB) * 64;
-                    x_tile([&](int kk, int b) { return __ldcg(a.x + (size_t)(k0 + kk) * Bp + b) * lw.in_norm[k0 + kk]; });
+                    x_tile(SRC_XW, a.x, lw.in_norm, 0.f, k0);
                 }
+                if (bt == 0) stamp(a, layer * 8 + 1);
             }
             // ---- attention units
             if (bt == 0) progress(a, 7, (unsigned)(layer * 8 + 2));
             {
                 const int Sp = a.splits;
                 const int units = B * d.Hkv * Sp;
-                if ((int)blockIdx.x < units) wait_count_warp(a.cnt + cidx(layer, 0), G, c, 31);
+                phase_wait(cidx(layer, 0), 31);
+                if (bt == 0) stamp(a, layer * 8 + 2);
                 for (int u = blockIdx.x; u < units; u += G) {
                     const int b = u / (d.Hkv * Sp), g = (u / Sp) % d.Hkv, s = u % Sp;
                     if (bt == 0) asm_->r1 = poll_tag(a.stats + ((size_t)layer * 3 + 0) * 64 + b, ep, c, 32);
@@ -991,11 +1179,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                         *c.abort = 1;
                         break;
                     }
-                    attn_unit<R>(a, lw, layer, b, g, s, Sp, r1, asm_, obuf, c);
+                    attn_unit<R>(a, lw, layer, b, g, s, Sp, r1, asm_, obuf, xring, S_.afull, ach, c);
                 }
                 __threadfence();
                 bld_sync();
-                if (bt == 0) signal(a.cnt + cidx(layer, 1));
+                if (bt == 0) {
+                    stamp(a, layer * 8 + 3);
+                    signal(a.cnt + cidx(layer, 1));
+                }
             }
             // ---- O: X = merged attention output (splits combined per utterance)
             if (bt == 0) progress(a, 7, (unsigned)(layer * 8 + 3));
@@ -1003,40 +1194,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                 const Mat M = mat_of(d, 1);
                 int i0, i1;
                 share(M, i0, i1);
-                if (i1 > i0) wait_count_warp(a.cnt + cidx(layer, 1), G, c, 33);
-                const int Sp = a.splits;
+                phase_wait(cidx(layer, 1), 33);
+                if (bt == 0) stamp(a, layer * 8 + 4);
                 for (int i = i0; i < i1; i++) {
                     const int k0 = (i % M.KB) * 64;
-                    const int hq = k0 / QDB_HD, d0 = k0 % QDB_HD;
-                    // weight of each split's partial for this thread's utterance
-                    float f[MAX_SPLITS];
-                    {
-                        const int b = my_b;
-                        float mx = -INFINITY, ls = 0.f;
-#pragma unroll
-                        for (int s = 0; s < MAX_SPLITS; s++) {
-                            f[s] = (b < B && s < Sp)
-                                       ? __ldcg(a.part + (((size_t)b * d.Hq + hq) * Sp + s) * (2 + QDB_HD)) : -INFINITY;
-                            mx = fmaxf(mx, f[s]);
-                        }
-#pragma unroll
-                        for (int s = 0; s < MAX_SPLITS; s++) {
-                            f[s] = (mx == -INFINITY || f[s] == -INFINITY) ? 0.f : expf(f[s] - mx);
-                            if (b < B && s < Sp)
-                                ls += __ldcg(a.part + (((size_t)b * d.Hq + hq) * Sp + s) * (2 + QDB_HD) + 1) * f[s];
-                        }
-                        const float inv = ls > 0.f ? 1.0f / ls : 0.f;
-#pragma unroll
-                        for (int s = 0; s < MAX_SPLITS; s++) f[s] *= inv;
-                    }
-                    x_tile([&](int kk, int b) {
-                        const float *p = a.part + ((size_t)b * d.Hq + hq) * Sp * (2 + QDB_HD) + 2 + d0 + kk;
-                        float o = 0.f;
-#pragma unroll
-                        for (int s = 0; s < MAX_SPLITS; s++)
-                            if (s < Sp) o += f[s] * __ldcg(p + (size_t)s * (2 + QDB_HD));
-                        return o;
-                    });
+                    x_tile(SRC_PLAIN, a.attn, nullptr, 0.f, k0);
                 }
             }
             // ---- GU: X = x * w_post (after this layer's O)
@@ -1045,10 +1207,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                 const Mat M = mat_of(d, 2);
                 int i0, i1;
                 share(M, i0, i1);
-                if (i1 > i0) wait_count_warp(a.cnt + cidx(layer, 2), G, c, 34);
+                phase_wait(cidx(layer, 2), 34);
                 for (int i = i0; i < i1; i++) {
                     const int k0 = (i % M.KB) * 64;
-                    x_tile([&](int kk, int b) { return __ldcg(a.x + (size_t)(k0 + kk) * Bp + b) * lw.post_norm[k0 + kk]; });
+                    x_tile(SRC_XW, a.x, lw.post_norm, 0.f, k0);
                 }
             }
             // ---- DOWN: X = silu(r g) * (r u)
@@ -1058,17 +1220,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                 int i0, i1;
                 share(M, i0, i1);
                 float r2 = 0.f;  // post-attention-norm factor of this thread's utterance
-                if (i1 > i0) {
-                    wait_count_warp(a.cnt + cidx(layer, 3), G, c, 35);
-                    if (my_b < B) r2 = poll_tag(a.stats + ((size_t)layer * 3 + 1) * 64 + my_b, ep, c, 36);
-                }
+                phase_wait(cidx(layer, 3), 35);
+                if (i1 > i0 && my_b < B) r2 = poll_tag(a.stats + ((size_t)layer * 3 + 1) * 64 + my_b, ep, c, 36);
                 for (int i = i0; i < i1; i++) {
                     const int k0 = (i % M.KB) * 64;
-                    x_tile([&](int kk, int b) {
-                        const float g = __ldcg(a.gu + (size_t)(2 * (k0 + kk)) * Bp + b) * r2;
-                        const float u = __ldcg(a.gu + (size_t)(2 * (k0 + kk) + 1) * Bp + b) * r2;
-                        return silu_mul(g, u);
-                    });
+                    x_tile(SRC_SWIGLU, a.gu, nullptr, r2, k0);
                 }
             }
         }
@@ -1078,11 +1234,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
             const Mat M = mat_of(d, 4);
             int t0, t1;
             share_tiles(M, t0, t1);
-            if (t1 > t0) wait_count_warp(a.cnt + cidx(L - 1, 4), G, c, 37);
+            phase_wait(cidx(L - 1, 4), 37);
+            if (bt == 0) stamp(a, 8 * L + 0);
             for (int r0 = t0; r0 < t1; r0 += NACC)
                 for (int kb = 0; kb < M.KB; kb++) {
                     const int k0 = kb * 64;
-                    x_tile([&](int kk, int b) { return __ldcg(a.x + (size_t)(k0 + kk) * Bp + b) * a.final_norm[k0 + kk]; });
+                    x_tile(SRC_XW, a.x, a.final_norm, 0.f, k0);
                 }
         }
     }
@@ -1094,6 +1251,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
     }
     if (threadIdx.x == 0) {
+        stamp(a, 8 * L + 2);
         __threadfence();
         const unsigned prev = atomicAdd(a.done, 1u);
         if (prev == gridDim.x - 1) {
@@ -1117,7 +1275,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
 // group size R: W ring, X ring, attention scratch (+ 1 KB alignment slack).
 static int smem_for(int Bp, int R, int nsw) {
     const int att = (int)sizeof(AttnSm) + NBLD * R * QDB_HD * 4;
-    return 1024 + nsw * W_TILE + NSX * 2 * Bp * 128 + att;
+    const int xr = NSX * 2 * Bp * 128 > XRING_MIN ? NSX * 2 * Bp * 128 : XRING_MIN;
+    return 1024 + nsw * W_TILE + xr + att;
 }
 
 extern "C" int qdb_bstep_ring_stages(int Bp, int R) {
@@ -1132,7 +1291,7 @@ extern "C" int qdb_bstep_counters(int layers) { return 1 + 5 * layers; }
 
 extern "C" cudaError_t qdb_launch_bstep(const QdbBatchArgs *args, int grid, cudaStream_t st) {
     const QdbBatchArgs &a = *args;
-    if (a.B < 1 || a.B > 64 || a.Bp % 16 || a.Bp < a.B || a.Bp > 64) return cudaErrorInvalidValue;
+    if (a.B < 1 || a.B > 64 || a.Bp < a.B || (a.Bp != 16 && a.Bp != 32 && a.Bp != 64)) return cudaErrorInvalidValue;
     if (a.d.L > MAX_LAYERS || a.d.h % 64 || a.d.I % 64 || a.splits < 1) return cudaErrorInvalidValue;
     const int R = a.d.Hq / a.d.Hkv;
     const int smem = smem_for(a.Bp, R, a.nsw);

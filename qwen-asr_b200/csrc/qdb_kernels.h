@@ -134,7 +134,7 @@ cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_p
 // launch. Activation buffers are [feature][Bp] f32 (utterance = column).
 struct QdbBatchArgs {
     QdbDims d;
-    int B, Bp;                    // utterances, and columns rounded up to 16 (<= 64)
+    int B, Bp;                    // utterances, and tile columns (16, 32 or 64)
     int nsw;                      // weight-ring stages (qdb_bstep_ring_stages)
     int splits;                   // key splits per (utterance, KV head), <= 8
     const QdbLayerW *layers;      // device [L]
@@ -150,7 +150,9 @@ struct QdbBatchArgs {
     float *logits_out;            // nullable [B, V]
     int mask_eos;
     int step_base;                // added to every position; selects the token slots
-    float *x, *qkv, *gu, *part;   // [h][Bp], [qkvd][Bp], [2I][Bp], [B][Hq][splits][2 + 128]
+    float *x, *qkv, *gu, *attn;   // [h][Bp], [qkvd][Bp], [2I][Bp], [Hq*128][Bp] (merged attention output)
+    float *part;                  // attention partials (splits > 1): o [splits][Hq*128][Bp], then (m, l) [splits][Hq][2][Bp]
+    unsigned *acnt;               // [64 * Hkv] finished splits per (utterance, KV head), zero between layers
     unsigned long long *stats;    // [(3L + 3) * 64] epoch-tagged 1/rms words
     unsigned long long *best;     // [64] argmax keys, zero between launches
     unsigned *cnt;                // [n_cnt] phase counters, zero between launches
@@ -158,8 +160,14 @@ struct QdbBatchArgs {
     unsigned *done;               // zero between launches
     unsigned epoch;               // tag of this launch's statistics (never 0)
     int *err;                     // [4]
-    unsigned *prog;               // nullable [grid][8]: progress of each role (read after a failed wait)
+    unsigned *prog;               // nullable [grid][17]: progress of each role (read after a failed wait)
+    unsigned long long *trace;    // nullable [grid][qdb_bstep_trace_events(L)] globaltimer stamps (ns)
+    unsigned long long *detail;   // nullable [grid][256]: layer-1 item stamps (profiling)
 };
+// Trace events of one batched step per CTA: per layer {QKV inputs ready, QKV X
+// tiles built, attention start, attention end, O inputs ready, QKV drained, O
+// drained, DOWN drained}, then {LM inputs ready, LM drained, end}.
+__host__ __device__ static inline int qdb_bstep_trace_events(int layers) { return 8 * layers + 3; }
 int qdb_bstep_ring_stages(int Bp, int R);
 size_t qdb_bstep_smem(int Bp, int R);
 int qdb_bstep_counters(int layers);

@@ -97,7 +97,8 @@ struct RowScratch {
 // Scratch of the persistent batched decode step (qdb_bstep.cu), sized for its
 // largest batch (64 utterances, 8 key splits); allocated on first use.
 struct BatchScratch {
-    float *x = nullptr, *qkv = nullptr, *gu = nullptr, *part = nullptr;
+    float *x = nullptr, *qkv = nullptr, *gu = nullptr, *part = nullptr, *attn = nullptr;
+    unsigned *acnt = nullptr;
     unsigned long long *stats = nullptr, *best = nullptr;
     unsigned *cnt = nullptr, *done = nullptr;
     int *err = nullptr;
@@ -323,7 +324,8 @@ extern "C" void qdb_model_free(qdb_model *m) {
     cudaFree(r.amaps); cudaFree(r.asegs);
     BatchScratch &b = m->bs;
     cudaFree(b.x); cudaFree(b.qkv); cudaFree(b.gu); cudaFree(b.part); cudaFree(b.stats); cudaFree(b.best);
-    cudaFree(b.cnt); cudaFree(b.done); cudaFree(b.err); cudaFree(b.maps); cudaFree(b.prog);
+    cudaFree(b.cnt); cudaFree(b.done); cudaFree(b.err); cudaFree(b.maps); cudaFree(b.prog); cudaFree(b.attn);
+    cudaFree(b.acnt);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->h_tok) cudaFreeHost(m->h_tok);
     if (m->st) cudaStreamDestroy(m->st);
@@ -938,14 +940,16 @@ static constexpr int BSTEP_MAX_B = 64, BSTEP_MAX_SPLITS = 8;
 // The persistent step serves batches of up to 64 utterances; QWEN_ASR_B200_BATCH=graph
 // forces the launch-per-kernel graph path (A/B measurements), which also serves
 // larger batches.
+// Utterance columns of the step's tiles: 16, 32 or 64.
+static int bstep_cols(int n) { return n <= 16 ? 16 : (n <= 32 ? 32 : 64); }
+
 static bool bstep_usable(qdb_model *m, int n) {
     if (n < 1 || n > BSTEP_MAX_B) return false;
     const char *v = getenv("QWEN_ASR_B200_BATCH");
     if (v && !strcmp(v, "graph")) return false;
     int dev_smem = 0;
     cudaDeviceGetAttribute(&dev_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device);
-    const int Bp = (n + 15) / 16 * 16;
-    return qdb_bstep_smem(Bp, m->cfg.heads / m->cfg.kv_heads) + 2048 <= (size_t)dev_smem;
+    return qdb_bstep_smem(bstep_cols(n), m->cfg.heads / m->cfg.kv_heads) + 2048 <= (size_t)dev_smem;
 }
 
 static int ensure_bstep(qdb_model *m) {
@@ -958,10 +962,11 @@ static int ensure_bstep(qdb_model *m) {
         dev_alloc(&b.gu, 2 * I * BSTEP_MAX_B) ||
         dev_alloc(&b.part, (size_t)BSTEP_MAX_B * m->cfg.heads * BSTEP_MAX_SPLITS * (2 + QDB_HD)) ||
         dev_alloc(&b.stats, (3 * L + 3) * 64) || dev_alloc(&b.best, 64) || dev_alloc(&b.cnt, (size_t)b.n_cnt) ||
-        dev_alloc(&b.done, 1) || dev_alloc(&b.err, 4) || dev_alloc(&b.prog, (size_t)m->sms * 17)) {
+        dev_alloc(&b.done, 1) || dev_alloc(&b.err, 4) || dev_alloc(&b.prog, (size_t)m->sms * 17) ||
+        dev_alloc(&b.attn, (size_t)m->qd * BSTEP_MAX_B) || dev_alloc(&b.acnt, (size_t)BSTEP_MAX_B * m->cfg.kv_heads)) {
         std::string e = g_err;
         cudaFree(b.x); cudaFree(b.qkv); cudaFree(b.gu); cudaFree(b.part); cudaFree(b.stats); cudaFree(b.best);
-        cudaFree(b.cnt); cudaFree(b.done); cudaFree(b.err);
+        cudaFree(b.cnt); cudaFree(b.done); cudaFree(b.err); cudaFree(b.prog); cudaFree(b.attn); cudaFree(b.acnt);
         b = BatchScratch();
         g_err = e;
         return -1;
@@ -974,6 +979,7 @@ static int ensure_bstep(qdb_model *m) {
     CK(cudaMemset(b.done, 0, 4));
     CK(cudaMemset(b.err, 0, 16));
     CK(cudaMemset(b.prog, 0, (size_t)m->sms * 17 * 4));
+    CK(cudaMemset(b.acnt, 0, (size_t)BSTEP_MAX_B * m->cfg.kv_heads * 4));
     // weight tensor maps: qkv, o, gu, down of every layer, then the embedding
     const int nmaps = 4 * (int)L + 1;
     std::vector<unsigned char> maps((size_t)nmaps * 128);
@@ -1015,15 +1021,20 @@ static int bstep_splits(qdb_model *m, int n, int max_ctx) {
 // in rs.rowkv. tok_in / x_in: device tokens (slots step_base * n + b) or f32
 // embeddings [n, h]; tok_out slots step_base * n + b.
 static int launch_bstep(qdb_model *m, int n, int max_ctx, const int *tok_in, const float *x_in, int *tok_out,
-                        float *logits, int step_base, int splits) {
+                        float *logits, int step_base, int splits, unsigned long long *trace = nullptr,
+                        unsigned long long *detail = nullptr) {
     if (launch_gate()) return -1;
     BatchScratch &b = m->bs;
     QdbBatchArgs a;
     memset(&a, 0, sizeof(a));
     a.d = m->d;
     a.B = n;
-    a.Bp = (n + 15) / 16 * 16;
+    a.Bp = bstep_cols(n);
     a.nsw = qdb_bstep_ring_stages(a.Bp, m->cfg.heads / m->cfg.kv_heads);
+    if (const char *v = getenv("QWEN_ASR_B200_BSTEP_NSW")) {  // tuning: fewer weight-ring stages
+        const int k = atoi(v);
+        if (k >= 2 && k < a.nsw) a.nsw = k;
+    }
     a.splits = splits;
     a.layers = m->layers_dev;
     a.wmaps = b.maps;
@@ -1042,6 +1053,8 @@ static int launch_bstep(qdb_model *m, int n, int max_ctx, const int *tok_in, con
     a.qkv = b.qkv;
     a.gu = b.gu;
     a.part = b.part;
+    a.attn = b.attn;
+    a.acnt = b.acnt;
     a.stats = b.stats;
     a.best = b.best;
     a.cnt = b.cnt;
@@ -1051,6 +1064,8 @@ static int launch_bstep(qdb_model *m, int n, int max_ctx, const int *tok_in, con
     a.epoch = b.epoch;
     a.err = b.err;
     a.prog = b.prog;
+    a.trace = trace;
+    a.detail = detail;
     (void)max_ctx;
     CK(qdb_launch_bstep(&a, m->sms, m->st));
     return 0;
@@ -1155,6 +1170,32 @@ extern "C" int qdb_forward_batch(qdb_session *const *sessions, int n, const floa
                            m->st));
     CK(cudaStreamSynchronize(m->st));
     return check_rows_err(m);
+}
+
+extern "C" int qdb_trace_batch_step(qdb_session *const *sessions, int n, const float *embeds, const int *pos,
+                                    unsigned long long *trace_out, int max_words) {
+    g_err.clear();
+    qdb_model *m = nullptr;
+    if (!embeds || !trace_out) return fail("null argument");
+    int maxp = 0;
+    if (batch_setup(sessions, n, pos, 0, &m, &maxp) || ensure_tok(m, n)) return -1;
+    if (!bstep_usable(m, n)) return fail("the persistent batched step does not serve %d rows", n);
+    const int ev = qdb_bstep_trace_events(m->cfg.layers);
+    const size_t words = (size_t)m->sms * (ev + 256);  // phase stamps, then layer-1 detail stamps
+    if ((size_t)max_words < words) return fail("trace buffer needs %zu words", words);
+    unsigned long long *tr = nullptr;
+    if (ensure_bstep(m) || dev_alloc(&tr, words)) return -1;
+    int rc = 0;
+    if (cudaMemsetAsync(tr, 0, words * 8, m->st) != cudaSuccess ||
+        cudaMemcpyAsync(m->rs.X, embeds, (size_t)n * m->cfg.hidden * 4, cudaMemcpyHostToDevice, m->st) != cudaSuccess ||
+        launch_bstep(m, n, maxp + 1, nullptr, m->rs.X, m->rs.tok, nullptr, 0, bstep_splits(m, n, maxp + 1), tr,
+                     tr + (size_t)m->sms * ev) ||
+        cudaMemcpyAsync(trace_out, tr, words * 8, cudaMemcpyDeviceToHost, m->st) != cudaSuccess ||
+        cudaStreamSynchronize(m->st) != cudaSuccess)
+        rc = -1;
+    cudaFree(tr);
+    if (rc) return g_err.empty() ? fail("batched trace step failed") : -1;
+    return check_bstep_err(m) ? -1 : ev;
 }
 
 extern "C" int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, const int *first_tokens, const int *pos,
