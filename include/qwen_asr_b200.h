@@ -162,8 +162,10 @@ int qdb_decode_greedy_batch(qdb_session *const *sessions, int n, const int *firs
  * (qwen_asr.c:606-607, :714-715) at the granularity of one step. */
 int qdb_trace_step(qdb_session *s, int token, int pos, unsigned long long *trace_out, int max_words);
 
-/* Profiling of the persistent batched step (qdb_forward_batch's path for up
- * to 64 rows): runs one step like qdb_forward_batch (its tokens are dropped)
+/* Profiling of the persistent batched step (qdb_bstep.cu: up to 64 rows in
+ * one cooperative launch; qdb_forward_batch and qdb_decode_greedy_batch use
+ * it when QWEN_ASR_B200_BATCH=persistent, and the captured per-kernel graph
+ * otherwise): runs one step like qdb_forward_batch (its tokens are dropped)
  * with globaltimer stamps. trace_out receives [ctas][events] values (ns); the
  * events of each CTA are, per layer: QKV inputs ready, QKV X tiles built,
  * attention start, attention end, O inputs ready, QKV drained, O drained,

@@ -65,7 +65,14 @@ constexpr int NWARPS = 14;
 constexpr int NTHREADS = NWARPS * 32;
 constexpr int EPI0 = 2, NEPI = 4;      // epilogue warps 2..5
 constexpr int BLD0 = 6, NBLD = 8;      // builder warps 6..13
-constexpr int NACC = 8;                // accumulator slots in TMEM
+constexpr int NACC = 4;                // lm_head tiles per round (one TMEM accumulator each)
+constexpr int NSLOT = 2;               // projection segments in flight (double-buffered TMEM slots)
+// An MMA multiplies a weight tile (M = 128 rows) with the X tile's hi AND lo
+// rows at once (N = 2 * Bp: hi rows 0..Bp-1, lo rows Bp..2Bp-1), so an
+// accumulator is 2 * Bp columns; the epilogue adds the two halves. The k-steps
+// of a tile alternate over nchain(Bp) independent accumulators (an MMA costs
+// about the same for any N; dependent MMAs wait for each other).
+__host__ __device__ constexpr int nchain(int Bp) { return Bp >= 64 ? 2 : 4; }
 constexpr int W_TILE = 128 * 64 * 2;   // one weight tile (16 KB)
 constexpr int MAX_NSW = 8;             // W ring stages (at most)
 constexpr int NGRP = 4, GRP_WARPS = 2;  // builder groups: group g builds X tiles xi % 4 == g
@@ -182,10 +189,10 @@ __device__ __forceinline__ void stamp(const QdbBatchArgs &a, int idx) {
 // operands ready), 64..127 X tile build start, 128..191 X tile built, 192..223
 // epilogue segment ready, 224..255 segment drained; index within the layer.
 __device__ __forceinline__ void dstamp(const QdbBatchArgs &a, int slot) {
-    if (a.detail && slot >= 0 && slot < 256) {
+    if (a.detail && slot >= 0 && slot < 512) {
         unsigned long long t;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        a.detail[(size_t)blockIdx.x * 256 + slot] = t;
+        a.detail[(size_t)blockIdx.x * 512 + slot] = t;
     }
 }
 
@@ -246,12 +253,12 @@ __device__ __forceinline__ void red_add_v4(float *p, float a, float b, float c, 
 }
 
 // ---------------------------------------------------------------- tcgen05 pieces
-__device__ __forceinline__ void tma_load_2d_pol(void *dst, const CUtensorMap *map, int x, int y, u64 *bar,
-                                                uint64_t pol) {
+
+__device__ __forceinline__ void bulk_g2s_pol(void *dst, const void *src, unsigned bytes, u64 *bar, uint64_t pol) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
-        "%3}], [%4], %5;" ::"r"(su32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(su32(bar)), "l"(pol)
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            su32(dst)),
+        "l"(src), "r"(bytes), "r"(su32(bar)), "l"(pol)
         : "memory");
 }
 
@@ -324,11 +331,10 @@ __device__ __forceinline__ void share(const Mat &M, int &i0, int &i1) {
     i0 = (int)(n * blockIdx.x / gridDim.x);
     i1 = (int)(n * (blockIdx.x + 1) / gridDim.x);
 }
-// lm_head: whole tiles [t0, t1).
-__device__ __forceinline__ void share_tiles(const Mat &M, int &t0, int &t1) {
-    t0 = (int)((long long)M.T * blockIdx.x / gridDim.x);
-    t1 = (int)((long long)M.T * (blockIdx.x + 1) / gridDim.x);
-}
+// lm_head: whole tiles in groups of NACC consecutive tiles (the last group
+// may be shorter); CTA c takes groups c, c + G, ... A group is one round: its
+// tiles share every X tile (kb-outer order) and are accumulated together.
+__device__ __forceinline__ int lm_groups(const Mat &M) { return (M.T + NACC - 1) / NACC; }
 
 // Counter index of (layer, phase); phase 0..4 = QKV, ATT, O, GU, DOWN. Slot 0
 // is the set-up phase (embedding + clears).
@@ -337,7 +343,8 @@ __device__ __forceinline__ int cidx(int layer, int ph) { return 1 + layer * 5 + 
 struct Smem {
     u64 wfull[MAX_NSW], wempty[MAX_NSW];
     u64 xfull[NSX], xempty[NSX];
-    u64 accfull[NACC], accempty[NACC];
+    u64 accfull[NSLOT], accempty[NSLOT];
+    u64 lmfull, lmempty;  // lm_head rounds (all of a round's tiles complete together)
     u64 afull[2];  // attention K/V chunks (staged in the X ring)
     u64 mma_done;
     uint32_t tmem;
@@ -351,6 +358,14 @@ __device__ __forceinline__ float ld_l2(const float *p) {
     float v;
     asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
     return v;
+}
+
+// Two f32 as bf16 hi = rn(v) and lo = rn(v - hi), each pair packed (even
+// column in the low half): hardware conversions, three instructions per value.
+__device__ __forceinline__ void split_bf16x2(float v0, float v1, uint32_t &hi, uint32_t &lo) {
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(v1), "f"(v0));
+    const float r0 = v0 - __uint_as_float(hi << 16), r1 = v1 - __uint_as_float(hi & 0xffff0000u);
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(r1), "f"(r0));
 }
 
 // X tile sources: the tile's value at (utterance b, column k0 + k) is
@@ -369,7 +384,7 @@ enum { SRC_XW = 0, SRC_PLAIN = 1, SRC_SWIGLU = 2 };
 // 2 for SwiGLU) are issued before the first value is used.
 template <int MODE>
 __device__ __forceinline__ void build_tile(unsigned char *xs, int Bp, int B, int gt, const float *src,
-                                           const float *w, float r, int k0) {
+                                           const float *w, float r, int k0, const QdbBatchArgs &a, int dslot) {
     constexpr int TPR = MODE == SRC_SWIGLU ? 2 : 4;  // chunks per round
     unsigned char *hi = xs, *lo = xs + Bp * 128;
     const int b = gt % Bp, c0 = gt / Bp, cstep = GRP_T / Bp, ntask = 8 / cstep;
@@ -405,13 +420,7 @@ __device__ __forceinline__ void build_tile(unsigned char *xs, int Bp, int B, int
             }
             uint32_t h[4], l[4];
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const uint16_t h0 = f32_to_bf16_rn(v[t][2 * i]), h1 = f32_to_bf16_rn(v[t][2 * i + 1]);
-                const uint16_t l0 = f32_to_bf16_rn(v[t][2 * i] - __uint_as_float((uint32_t)h0 << 16));
-                const uint16_t l1 = f32_to_bf16_rn(v[t][2 * i + 1] - __uint_as_float((uint32_t)h1 << 16));
-                h[i] = (uint32_t)h0 | ((uint32_t)h1 << 16);
-                l[i] = (uint32_t)l0 | ((uint32_t)l1 << 16);
-            }
+            for (int i = 0; i < 4; i++) split_bf16x2(v[t][2 * i], v[t][2 * i + 1], h[i], l[i]);
             const uint32_t off = rb + (uint32_t)((cc ^ (b & 7)) * 16);
             *reinterpret_cast<uint4 *>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
             *reinterpret_cast<uint4 *>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
@@ -769,10 +778,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
             mb_init(&S_.xempty[i], 1);
         }
         for (int i = 0; i < 2; i++) mb_init(&S_.afull[i], 1);
-        for (int i = 0; i < NACC; i++) {
+        for (int i = 0; i < NSLOT; i++) {
             mb_init(&S_.accfull[i], 1);
             mb_init(&S_.accempty[i], NEPI);
         }
+        mb_init(&S_.lmfull, 1);
+        mb_init(&S_.lmempty, NEPI);
         mb_init(&S_.mma_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -800,31 +811,33 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
             asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
             unsigned wi = 0;
             bool ok = true;
-            auto issue = [&](int mi, int tile, int kb) -> bool {
+            // weight tile blk of the pre-tiled copy: 16 KB, contiguous, already in
+            // the swizzled shared-memory layout -> one 1D bulk copy
+            auto issue = [&](size_t blk) -> bool {
                 const int s = wi % NSW;
                 if (wi >= (unsigned)NSW && !mb_wait(&S_.wempty[s], ((wi / NSW) - 1) & 1, c, true, 1)) return false;
                 mb_expect(&S_.wfull[s], W_TILE);
-                tma_load_2d_pol(wring + (size_t)s * W_TILE, reinterpret_cast<const CUtensorMap *>(a.wmaps) + mi, kb * 64,
-                                tile * 128, &S_.wfull[s], pol);
+                bulk_g2s_pol(wring + (size_t)s * W_TILE, a.wt + blk * (W_TILE / 2), W_TILE, &S_.wfull[s], pol);
                 wi++;
                 progress(a, 0, wi);
                 return true;
             };
+            size_t base = 0;
             for (int layer = 0; layer < L && ok; layer++)
                 for (int m = 0; m < 4 && ok; m++) {
                     const Mat M = mat_of(d, m);
                     int i0, i1;
                     share(M, i0, i1);
-                    for (int i = i0; i < i1 && ok; i++) ok = issue(layer * 4 + m, i / M.KB, i % M.KB);
+                    for (int i = i0; i < i1 && ok; i++) ok = issue(base + (size_t)i);
+                    base += (size_t)M.T * M.KB;
                 }
             if (ok) {
                 const Mat M = mat_of(d, 4);
-                int t0, t1;
-                share_tiles(M, t0, t1);
-                for (int r0 = t0; r0 < t1 && ok; r0 += NACC) {
-                    const int nt = min(NACC, t1 - r0);
+                for (int grp = blockIdx.x; grp < lm_groups(M) && ok; grp += G) {
+                    const int nt = min(NACC, M.T - grp * NACC);
                     for (int kb = 0; kb < M.KB && ok; kb++)
-                        for (int j = 0; j < nt && ok; j++) ok = issue(4 * L, r0 + j, kb);
+                        for (int j = 0; j < nt && ok; j++)
+                            ok = issue(base + (size_t)grp * NACC * M.KB + (size_t)kb * nt + j);
                 }
             }
             // drain: the latest copy issued into each stage lands before exit
@@ -836,15 +849,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
     } else if (warp == 1) {
         // ================================================================ MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = instr_desc(128, Bp);
+            const uint32_t idesc = instr_desc(128, 2 * Bp);
             unsigned wi = 0, xi = 0, seg = 0;
             int l1_item = -1000;  // item index within layer 1 (detail stamps)
             bool ok = true;
-            // one item: W stage wi x X stage xi into accumulator slot
-            auto item = [&](uint32_t acc, bool first, bool last_x) -> bool {
+            // One projection item: W stage wi x X stage xi into the segment's slot:
+            // 4 MMAs (k-steps) over NCH accumulator chains at slot + chain * 2Bp.
+            const int NCH = nchain(Bp);
+            auto item = [&](uint32_t slot_base, bool first) -> bool {
                 const int ws = wi % NSW, xs = xi % NSX;
                 progress(a, 8, 3);
+                if (l1_item >= 0 && l1_item < 64) dstamp(a, 256 + l1_item);  // W wait begins
                 if (!mb_wait(&S_.wfull[ws], (wi / NSW) & 1, c, true, 3)) return false;
+                if (l1_item >= 0 && l1_item < 64) dstamp(a, 320 + l1_item);  // W ready
                 progress(a, 8, 4);
                 if (!mb_wait(&S_.xfull[xs], (xi / NSX) & 1, c, true, 4)) return false;
                 progress(a, 8, 0);
@@ -853,26 +870,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                 const uint32_t wb = su32(wring + (size_t)ws * W_TILE);
                 const uint32_t xb = su32(xring + (size_t)xs * XST);
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    const u64 ad = sm_desc(wb + k * 32);
-                    mma_bf16(acc, ad, sm_desc(xb + k * 32), idesc, (first && k == 0) ? 0u : 1u);
-                    mma_bf16(acc, ad, sm_desc(xb + Bp * 128 + k * 32), idesc, 1u);
-                }
+                for (int k = 0; k < 4; k++)
+                    mma_bf16(slot_base + (uint32_t)((k % NCH) * 2 * Bp), sm_desc(wb + k * 32), sm_desc(xb + k * 32), idesc,
+                             (first && k < NCH) ? 0u : 1u);
                 mma_commit(&S_.wempty[ws]);
+                mma_commit(&S_.xempty[xs]);
                 wi++;
+                xi++;
                 progress(a, 1, wi);
-                if (last_x) {
-                    mma_commit(&S_.xempty[xs]);
-                    xi++;
-                    progress(a, 2, xi);
-                }
+                progress(a, 2, xi);
                 return true;
             };
             auto begin_seg = [&](unsigned sg) -> bool {
-                const int slot = sg % NACC;
+                const int slot = sg % NSLOT;
                 progress(a, 8, 5);
-                if (sg >= (unsigned)NACC &&
-                    !mb_wait(&S_.accempty[slot], ((sg / NACC) - 1) & 1, c, true, 5))
+                if (sg >= (unsigned)NSLOT && !mb_wait(&S_.accempty[slot], ((sg / NSLOT) - 1) & 1, c, true, 5))
                     return false;
                 tc_fence_after();
                 progress(a, 3, sg + 1);
@@ -889,25 +901,50 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                         const int tile = i / M.KB;
                         const int iend = min(i1, (tile + 1) * M.KB);
                         if (!(ok = begin_seg(seg))) break;
-                        const uint32_t acc = tmem + (uint32_t)((seg % NACC) * Bp);
-                        for (int k = i; k < iend && ok; k++) ok = item(acc, k == i, true);
-                        if (ok) mma_commit(&S_.accfull[seg % NACC]);
+                        const uint32_t sb = tmem + (uint32_t)((seg % NSLOT) * NCH * 2 * Bp);
+                        for (int k = i; k < iend && ok; k++) ok = item(sb, k == i);
+                        if (ok) mma_commit(&S_.accfull[seg % NSLOT]);
                         seg++;
                         i = iend;
                     }
                 }
+            // lm_head rounds reuse all of TMEM: the projection slots drain first
+            for (unsigned sg = seg > NSLOT ? seg - NSLOT : 0; sg < seg && ok; sg++)
+                ok = mb_wait(&S_.accempty[sg % NSLOT], (sg / NSLOT) & 1, c, true, 5);
             if (ok) {
+                tc_fence_after();
                 const Mat M = mat_of(d, 4);
-                int t0, t1;
-                share_tiles(M, t0, t1);
-                for (int r0 = t0; r0 < t1 && ok; r0 += NACC) {
-                    const int nt = min(NACC, t1 - r0);
-                    for (int j = 0; j < nt && ok; j++) ok = begin_seg(seg + j);
-                    for (int kb = 0; kb < M.KB && ok; kb++)
+                l1_item = 384;  // detail stamps of the lm_head k-blocks
+                unsigned rnd = 0;
+                for (int grp = blockIdx.x; grp < lm_groups(M) && ok; grp += G, rnd++) {
+                    const int nt = min(NACC, M.T - grp * NACC);
+                    if (rnd > 0 && !(ok = mb_wait(&S_.lmempty, (rnd - 1) & 1, c, true, 5))) break;
+                    tc_fence_after();
+                    // per k-block: the round's nt weight tiles and one X tile; MMAs
+                    // interleaved over the nt tiles (independent accumulators)
+                    for (int kb = 0; kb < M.KB && ok; kb++) {
                         for (int j = 0; j < nt && ok; j++)
-                            ok = item(tmem + (uint32_t)(((seg + j) % NACC) * Bp), kb == 0, j == nt - 1);
-                    for (int j = 0; j < nt && ok; j++) mma_commit(&S_.accfull[(seg + j) % NACC]);
-                    seg += nt;
+                            ok = mb_wait(&S_.wfull[(wi + j) % NSW], ((wi + j) / NSW) & 1, c, true, 3);
+                        if (ok) ok = mb_wait(&S_.xfull[xi % NSX], (xi / NSX) & 1, c, true, 4);
+                        if (!ok) break;
+                        dstamp(a, l1_item++);
+                        tc_fence_after();
+                        const uint32_t xb = su32(xring + (size_t)(xi % NSX) * XST);
+#pragma unroll
+                        for (int k = 0; k < 4; k++)
+                            for (int j = 0; j < nt; j++) {
+                                const uint32_t wb = su32(wring + (size_t)((wi + j) % NSW) * W_TILE);
+                                mma_bf16(tmem + (uint32_t)(j * 2 * Bp), sm_desc(wb + k * 32), sm_desc(xb + k * 32),
+                                         idesc, (kb == 0 && k == 0) ? 0u : 1u);
+                            }
+                        for (int j = 0; j < nt; j++) mma_commit(&S_.wempty[(wi + j) % NSW]);
+                        mma_commit(&S_.xempty[xi % NSX]);
+                        wi += nt;
+                        xi++;
+                        progress(a, 1, wi);
+                        progress(a, 2, xi);
+                    }
+                    if (ok) mma_commit(&S_.lmfull);
                 }
             }
             // every MMA issued by this thread completes before TMEM is released
@@ -924,14 +961,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
         // waits for accumulator slot of segment sg; uniform over the warp
         auto acc_ready = [&](unsigned sg) -> bool {
             if (!ok || warp_aborted(c)) return false;
-            if (!mb_wait_warp(&S_.accfull[sg % NACC], (sg / NACC) & 1, c, 7)) return false;
+            if (!mb_wait_warp(&S_.accfull[sg % NSLOT], (sg / NSLOT) & 1, c, 7)) return false;
             tc_fence_after();
             return true;
         };
         auto acc_release = [&](unsigned sg) {
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mb_arrive(&S_.accempty[sg % NACC]);
+            if (lane == 0) mb_arrive(&S_.accempty[sg % NSLOT]);
             if (warp == EPI0 && lane == 0) progress(a, 4, sg + 1);
         };
         auto phase_done = [&](int idx) {
@@ -993,12 +1030,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                     const bool rdy = acc_ready(seg);
                     if (et == 0) dstamp(a, 192 + l1_seg);
                     if (rdy) {
-                        const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((seg % NACC) * Bp);
+                        const int NCH = nchain(Bp);
+                        const uint32_t tbase =
+                            tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((seg % NSLOT) * NCH * 2 * Bp);
                         const int row = tile * 128 + 32 * q + lane;
                         float *dst = out + (size_t)row * Bp;
                         for (int c0 = 0; c0 < Bp; c0 += 16) {
-                            float v[16];
+                            float v[16], w[16];
                             tmem_ld16(tbase + (uint32_t)c0, v);
+                            // the lo half, then the other chains (both halves)
+                            for (int k = 0; k < NCH; k++)
+                                for (int hl = (k == 0); hl < 2; hl++) {
+                                    tmem_ld16(tbase + (uint32_t)(k * 2 * Bp + hl * Bp + c0), w);
+#pragma unroll
+                                    for (int j = 0; j < 16; j++) v[j] += w[j];
+                                }
                             if (row < M.N)
 #pragma unroll
                                 for (int j = 0; j < 16; j += 4) red_add_v4(dst + c0 + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -1027,48 +1073,69 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
         }
         for (int b = et; b < Bp; b += NEPI * 32)
             lm_r3[b] = b < B ? poll_tag(a.stats + ((size_t)L * 3 + 2) * 64 + b, ep, c, 24) : 0.f;
-        u64 best[2] = {0ull, 0ull};  // lane keeps utterances lane and lane + 32
+        // Per 16-column chunk of a tile: the warp's 32 rows x 16 logits go
+        // through a padded smem buffer; lanes l and l + 16 scan rows 0-15 /
+        // 16-31 of column l in increasing row order (strict >: the lowest row
+        // wins an exact tie) and merge with one shuffle. Lane l (< 16) keeps
+        // the best key of columns c0 + l, c0 in {0, 16, 32, 48}.
+        float *tbuf = reinterpret_cast<float *>(asm_) + (size_t)q * 32 * 17;  // attention scratch is idle now
+        u64 best[4] = {0ull, 0ull, 0ull, 0ull};
         epi_sync();
-        int t0, t1;
-        share_tiles(M, t0, t1);
-        for (int r0 = t0; r0 < t1; r0 += NACC) {
-            const int nt = min(NACC, t1 - r0);
-            for (int j = 0; j < nt; j++, seg++) {
+        unsigned rnd = 0;
+        for (int grp = blockIdx.x; grp < lm_groups(M); grp += G, rnd++) {
+            const int r0 = grp * NACC, nt = min(NACC, M.T - r0);
+            bool rdy = ok && !warp_aborted(c) && mb_wait_warp(&S_.lmfull, rnd & 1, c, 7);
+            if (!rdy) ok = false;
+            tc_fence_after();
+            for (int j = 0; j < nt && rdy; j++) {
                 const int tile = r0 + j;
-                if (acc_ready(seg)) {
-                    const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((seg % NACC) * Bp);
-                    const int row = tile * 128 + 32 * q + lane;
-                    const bool live = row < M.N && !(a.mask_eos && (row == QDB_ENDOFTEXT || row == QDB_IM_END));
-                    for (int c0 = 0; c0 < Bp; c0 += 16) {
-                        float v[16];
-                        tmem_ld16(tbase + (uint32_t)c0, v);
+                const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(j * 2 * Bp);
+                const int row = tile * 128 + 32 * q + lane;
+                const bool live = row < M.N && !(a.mask_eos && (row == QDB_ENDOFTEXT || row == QDB_IM_END));
 #pragma unroll
-                        for (int jj = 0; jj < 16; jj++) {
-                            const int b = c0 + jj;
-                            const float lg = v[jj] * lm_r3[b];
-                            if (a.logits_out && row < M.N && b < B) a.logits_out[(size_t)b * M.N + row] = lg;
-                            u64 key = (live && b < B && !isnan(lg)) ? argmax_key(lg, row) : 0ull;
+                for (int cq = 0; cq < 4; cq++) {
+                    const int c0 = cq * 16;
+                    if (c0 >= Bp) break;
+                    float v[16], w[16];
+                    tmem_ld16(tbase + (uint32_t)c0, v);
+                    tmem_ld16(tbase + (uint32_t)(Bp + c0), w);  // lo half
 #pragma unroll
-                            for (int o = 16; o > 0; o >>= 1) {
-                                const u64 other = __shfl_xor_sync(0xffffffffu, key, o);
-                                key = other > key ? other : key;
-                            }
-                            if (lane == (b & 31)) {
-                                u64 &bk = best[b >> 5];
-                                bk = key > bk ? key : bk;
-                            }
+                    for (int jj = 0; jj < 16; jj++) v[jj] += w[jj];
+#pragma unroll
+                    for (int jj = 0; jj < 16; jj++) {
+                        const int b = c0 + jj;
+                        const float lg = v[jj] * lm_r3[b];
+                        if (a.logits_out && row < M.N && b < B) a.logits_out[(size_t)b * M.N + row] = lg;
+                        tbuf[lane * 17 + jj] = (live && b < B && !isnan(lg)) ? lg : -INFINITY;
+                    }
+                    __syncwarp();
+                    const int col = lane & 15, rbase = (lane >> 4) * 16;
+                    float bv = -INFINITY;
+                    int br = -1;
+#pragma unroll
+                    for (int rr = 0; rr < 16; rr++) {
+                        const float x = tbuf[(rbase + rr) * 17 + col];
+                        if (x > bv) {
+                            bv = x;
+                            br = rbase + rr;
                         }
                     }
-                } else {
-                    ok = false;
+                    u64 key = br >= 0 ? argmax_key(bv, tile * 128 + 32 * q + br) : 0ull;
+                    const u64 other = __shfl_xor_sync(0xffffffffu, key, 16);
+                    key = other > key ? other : key;
+                    best[cq] = key > best[cq] ? key : best[cq];
+                    __syncwarp();
                 }
-                acc_release(seg);
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mb_arrive(&S_.lmempty);
         }
         epi_stamp(8 * L + 1);
         // combine the 4 epilogue warps, then the CTA's candidates go to the global keys
-        lm_best[q][lane] = best[0];
-        lm_best[q][lane + 32] = best[1];
+        if (lane < 16)
+#pragma unroll
+            for (int cq = 0; cq < 4; cq++) lm_best[q][cq * 16 + lane] = best[cq];
         epi_sync();
         for (int b = et; b < B; b += NEPI * 32) {
             u64 k = 0ull;
@@ -1125,9 +1192,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
                 if (ok) {
                     if (gt == 0) dstamp(a, 64 + l1_tile);
                     unsigned char *xs = xring + (size_t)s * XST;
-                    if (mode == SRC_XW) build_tile<SRC_XW>(xs, Bp, B, gt, src, w, r, k0);
-                    else if (mode == SRC_PLAIN) build_tile<SRC_PLAIN>(xs, Bp, B, gt, src, w, r, k0);
-                    else build_tile<SRC_SWIGLU>(xs, Bp, B, gt, src, w, r, k0);
+                    const int ds = 256 + l1_tile;
+                    if (mode == SRC_XW) build_tile<SRC_XW>(xs, Bp, B, gt, src, w, r, k0, a, ds);
+                    else if (mode == SRC_PLAIN) build_tile<SRC_PLAIN>(xs, Bp, B, gt, src, w, r, k0, a, ds);
+                    else build_tile<SRC_SWIGLU>(xs, Bp, B, gt, src, w, r, k0, a, ds);
                     if (gt == 0) dstamp(a, 128 + l1_tile);
                     if (lane == 0) {
                         mb_arrive(&S_.xfull[s]);
@@ -1232,11 +1300,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
         if (bt == 0) progress(a, 7, (unsigned)(L * 8 + 6));
         {
             const Mat M = mat_of(d, 4);
-            int t0, t1;
-            share_tiles(M, t0, t1);
             phase_wait(cidx(L - 1, 4), 37);
             if (bt == 0) stamp(a, 8 * L + 0);
-            for (int r0 = t0; r0 < t1; r0 += NACC)
+            for (int grp = blockIdx.x; grp < lm_groups(M); grp += G)
                 for (int kb = 0; kb < M.KB; kb++) {
                     const int k0 = kb * 64;
                     x_tile(SRC_XW, a.x, a.final_norm, 0.f, k0);
@@ -1269,7 +1335,51 @@ __global__ void __launch_bounds__(NTHREADS, 1) bstep_kernel(const QdbBatchArgs a
     }
 }
 
+// Pre-tiled weight copy: block blk = one 128-row x 64-column tile in the
+// shared-memory layout the MMA reads (K-major, 128-byte swizzle: row r,
+// 16-byte chunk c at (r/8)*1024 + (r%8)*128 + ((c ^ (r%8)) * 16)); rows past
+// the matrix are zero. One thread per 16-byte chunk.
+__global__ void tile_weights_kernel(const uint16_t *__restrict__ w, int N, int K, uint16_t *__restrict__ out,
+                                    int lm_order) {
+    const int T = (N + 127) / 128, KB = K / 64;
+    const size_t nchunks = (size_t)T * KB * 1024;  // 1024 chunks of 16 bytes per tile
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < nchunks; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t blk = i >> 10;
+        const int r = (int)((i >> 3) & 127), cc = (int)(i & 7);
+        int tile, kb;
+        if (!lm_order) {
+            tile = (int)(blk / KB);
+            kb = (int)(blk % KB);
+        } else {  // groups of NACC tiles, kb-outer inside a group
+            const int grp = (int)(blk / ((size_t)NACC * KB));
+            const int nt = min(NACC, T - grp * NACC);
+            const int in = (int)(blk - (size_t)grp * NACC * KB);
+            kb = in / nt;
+            tile = grp * NACC + in % nt;
+        }
+        const int row = tile * 128 + r;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (row < N) v = *reinterpret_cast<const uint4 *>(w + (size_t)row * K + kb * 64 + cc * 8);
+        unsigned char *dst = reinterpret_cast<unsigned char *>(out + blk * (W_TILE / 2));
+        *reinterpret_cast<uint4 *>(dst + (r >> 3) * 1024 + (r & 7) * 128 + ((cc ^ (r & 7)) << 4)) = v;
+    }
+}
+
 }  // namespace
+
+extern "C" size_t qdb_bstep_tiled_elems(int N, int K) { return (size_t)((N + 127) / 128) * (K / 64) * (W_TILE / 2); }
+
+// Writes the pre-tiled copy of one bf16 [N, K] matrix (K % 64 == 0) to out.
+// lm_order: the lm_head's group order; otherwise tile-major, k-blocks inner.
+extern "C" cudaError_t qdb_bstep_tile_weights(const uint16_t *w, int N, int K, uint16_t *out, int lm_order,
+                                              cudaStream_t st) {
+    if (K % 64 || N <= 0) return cudaErrorInvalidValue;
+    tile_weights_kernel<<<1184, 256, 0, st>>>(w, N, K, out, lm_order);
+    return cudaGetLastError();
+}
+
+static_assert(sizeof(AttnSm) + NBLD * 1 * QDB_HD * 4 >= NEPI * 32 * 17 * 4,
+              "the lm_head transpose buffers live in the attention scratch");
 
 // Layout of the step's dynamic shared memory for Bp utterance columns and
 // group size R: W ring, X ring, attention scratch (+ 1 KB alignment slack).
@@ -1292,6 +1402,7 @@ extern "C" int qdb_bstep_counters(int layers) { return 1 + 5 * layers; }
 extern "C" cudaError_t qdb_launch_bstep(const QdbBatchArgs *args, int grid, cudaStream_t st) {
     const QdbBatchArgs &a = *args;
     if (a.B < 1 || a.B > 64 || a.Bp < a.B || (a.Bp != 16 && a.Bp != 32 && a.Bp != 64)) return cudaErrorInvalidValue;
+    if (a.nsw < NACC) return cudaErrorInvalidValue;  // an lm_head k-block holds NACC weight stages at once
     if (a.d.L > MAX_LAYERS || a.d.h % 64 || a.d.I % 64 || a.splits < 1) return cudaErrorInvalidValue;
     const int R = a.d.Hq / a.d.Hkv;
     const int smem = smem_for(a.Bp, R, a.nsw);

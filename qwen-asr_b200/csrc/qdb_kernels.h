@@ -138,7 +138,7 @@ struct QdbBatchArgs {
     int nsw;                      // weight-ring stages (qdb_bstep_ring_stages)
     int splits;                   // key splits per (utterance, KV head), <= 8
     const QdbLayerW *layers;      // device [L]
-    const void *wmaps;            // device CUtensorMap [4L + 1]: qkv, o, gu, down per layer, then embed
+    const uint16_t *wt;           // pre-tiled weights (qdb_bstep_tile_weights): qkv, o, gu, down per layer, then embed
     const uint16_t *embed;        // [V, h]
     const float *final_norm;      // [h]
     const float2 *rope;
@@ -169,6 +169,8 @@ struct QdbBatchArgs {
 // drained, DOWN drained}, then {LM inputs ready, LM drained, end}.
 __host__ __device__ static inline int qdb_bstep_trace_events(int layers) { return 8 * layers + 3; }
 int qdb_bstep_ring_stages(int Bp, int R);
+size_t qdb_bstep_tiled_elems(int N, int K);
+cudaError_t qdb_bstep_tile_weights(const uint16_t *w, int N, int K, uint16_t *out, int lm_order, cudaStream_t st);
 size_t qdb_bstep_smem(int Bp, int R);
 int qdb_bstep_counters(int layers);
 cudaError_t qdb_launch_bstep(const QdbBatchArgs *args, int grid, cudaStream_t st);

@@ -103,7 +103,7 @@ struct BatchScratch {
     unsigned *cnt = nullptr, *done = nullptr;
     int *err = nullptr;
     unsigned *prog = nullptr;  // [sms][8] progress words (diagnostics)
-    void *maps = nullptr;  // device CUtensorMap [4L + 1]
+    uint16_t *wt = nullptr;  // pre-tiled weights: every 128 x 64 tile one contiguous 16 KB block
     int n_cnt = 0;
     unsigned epoch = 1;
 };
@@ -324,7 +324,7 @@ extern "C" void qdb_model_free(qdb_model *m) {
     cudaFree(r.amaps); cudaFree(r.asegs);
     BatchScratch &b = m->bs;
     cudaFree(b.x); cudaFree(b.qkv); cudaFree(b.gu); cudaFree(b.part); cudaFree(b.stats); cudaFree(b.best);
-    cudaFree(b.cnt); cudaFree(b.done); cudaFree(b.err); cudaFree(b.maps); cudaFree(b.prog); cudaFree(b.attn);
+    cudaFree(b.cnt); cudaFree(b.done); cudaFree(b.err); cudaFree(b.wt); cudaFree(b.prog); cudaFree(b.attn);
     cudaFree(b.acnt);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->h_tok) cudaFreeHost(m->h_tok);
@@ -937,24 +937,38 @@ static int ensure_tok(qdb_model *m, size_t count) {
 // ------------------------------------------------------------------ persistent batched step
 static constexpr int BSTEP_MAX_B = 64, BSTEP_MAX_SPLITS = 8;
 
-// The persistent step serves batches of up to 64 utterances; QWEN_ASR_B200_BATCH=graph
-// forces the launch-per-kernel graph path (A/B measurements), which also serves
-// larger batches.
 // Utterance columns of the step's tiles: 16, 32 or 64.
 static int bstep_cols(int n) { return n <= 16 ? 16 : (n <= 32 ? 32 : 64); }
 
-static bool bstep_usable(qdb_model *m, int n) {
+// Batched decode runs as the captured launch-per-kernel graph by default. The
+// persistent batched step (qdb_bstep.cu, up to 64 utterances) is selected with
+// QWEN_ASR_B200_BATCH=persistent: it computes the same step, but is measured
+// slower on this hardware (per-instruction tcgen05 MMA and commit costs at
+// N = 2 x batch columns, split-K reduction traffic, shallow attention staging).
+static bool bstep_fits(qdb_model *m, int n) {
     if (n < 1 || n > BSTEP_MAX_B) return false;
-    const char *v = getenv("QWEN_ASR_B200_BATCH");
-    if (v && !strcmp(v, "graph")) return false;
     int dev_smem = 0;
     cudaDeviceGetAttribute(&dev_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device);
-    return qdb_bstep_smem(bstep_cols(n), m->cfg.heads / m->cfg.kv_heads) + 2048 <= (size_t)dev_smem;
+    const int R = m->cfg.heads / m->cfg.kv_heads;
+    return qdb_bstep_ring_stages(bstep_cols(n), R) >= 8 && qdb_bstep_smem(bstep_cols(n), R) + 2048 <= (size_t)dev_smem;
+}
+
+static bool bstep_usable(qdb_model *m, int n) {
+    const char *v = getenv("QWEN_ASR_B200_BATCH");
+    return v && !strcmp(v, "persistent") && bstep_fits(m, n);
+}
+
+static void free_bstep(BatchScratch &b) {
+    cudaFree(b.x); cudaFree(b.qkv); cudaFree(b.gu); cudaFree(b.part); cudaFree(b.stats); cudaFree(b.best);
+    cudaFree(b.cnt); cudaFree(b.done); cudaFree(b.err); cudaFree(b.prog); cudaFree(b.attn); cudaFree(b.acnt);
+    cudaFree(b.wt);
+    b = BatchScratch();
 }
 
 static int ensure_bstep(qdb_model *m) {
     BatchScratch &b = m->bs;
-    if (b.x) return 0;
+    if (b.wt) return 0;  // allocated last: everything else is in place
+    free_bstep(b);
     const size_t h = m->cfg.hidden, I = m->cfg.intermediate, L = m->cfg.layers;
     const size_t qkvd = (size_t)m->qd + 2 * m->kvd;
     b.n_cnt = qdb_bstep_counters((int)L);
@@ -965,9 +979,7 @@ static int ensure_bstep(qdb_model *m) {
         dev_alloc(&b.done, 1) || dev_alloc(&b.err, 4) || dev_alloc(&b.prog, (size_t)m->sms * 17) ||
         dev_alloc(&b.attn, (size_t)m->qd * BSTEP_MAX_B) || dev_alloc(&b.acnt, (size_t)BSTEP_MAX_B * m->cfg.kv_heads)) {
         std::string e = g_err;
-        cudaFree(b.x); cudaFree(b.qkv); cudaFree(b.gu); cudaFree(b.part); cudaFree(b.stats); cudaFree(b.best);
-        cudaFree(b.cnt); cudaFree(b.done); cudaFree(b.err); cudaFree(b.prog); cudaFree(b.attn); cudaFree(b.acnt);
-        b = BatchScratch();
+        free_bstep(b);
         g_err = e;
         return -1;
     }
@@ -980,21 +992,33 @@ static int ensure_bstep(qdb_model *m) {
     CK(cudaMemset(b.err, 0, 16));
     CK(cudaMemset(b.prog, 0, (size_t)m->sms * 17 * 4));
     CK(cudaMemset(b.acnt, 0, (size_t)BSTEP_MAX_B * m->cfg.kv_heads * 4));
-    // weight tensor maps: qkv, o, gu, down of every layer, then the embedding
-    const int nmaps = 4 * (int)L + 1;
-    std::vector<unsigned char> maps((size_t)nmaps * 128);
+    // pre-tiled weights, in the order the step streams them
+    size_t total = 0;
+    const size_t per_layer = qdb_bstep_tiled_elems((int)qkvd, (int)h) + qdb_bstep_tiled_elems((int)h, m->qd) +
+                             qdb_bstep_tiled_elems((int)(2 * I), (int)h) + qdb_bstep_tiled_elems((int)h, (int)I);
+    total = per_layer * L + qdb_bstep_tiled_elems(m->cfg.vocab, (int)h);
+    uint16_t *wt = nullptr;
+    if (dev_alloc(&wt, total)) {
+        std::string e = g_err;
+        free_bstep(b);
+        g_err = e;
+        return -1;
+    }
+    uint16_t *o = wt;
     for (size_t l = 0; l < L; l++) {
         const QdbLayerW &lw = m->layers_host[l];
-        unsigned char *p = maps.data() + l * 4 * 128;
-        if (qdb_make_weight_map(p, lw.qkv, (int)qkvd, (int)h) || qdb_make_weight_map(p + 128, lw.o, (int)h, m->qd) ||
-            qdb_make_weight_map(p + 256, lw.gu, (int)(2 * I), (int)h) ||
-            qdb_make_weight_map(p + 384, lw.down, (int)h, (int)I))
-            return fail("weight tensor map of layer %zu", l);
+        CK(qdb_bstep_tile_weights(lw.qkv, (int)qkvd, (int)h, o, 0, m->st));
+        o += qdb_bstep_tiled_elems((int)qkvd, (int)h);
+        CK(qdb_bstep_tile_weights(lw.o, (int)h, m->qd, o, 0, m->st));
+        o += qdb_bstep_tiled_elems((int)h, m->qd);
+        CK(qdb_bstep_tile_weights(lw.gu, (int)(2 * I), (int)h, o, 0, m->st));
+        o += qdb_bstep_tiled_elems((int)(2 * I), (int)h);
+        CK(qdb_bstep_tile_weights(lw.down, (int)h, (int)I, o, 0, m->st));
+        o += qdb_bstep_tiled_elems((int)h, (int)I);
     }
-    if (qdb_make_weight_map(maps.data() + L * 4 * 128, m->embed, m->cfg.vocab, (int)h))
-        return fail("embedding tensor map");
-    CK(cudaMalloc(&b.maps, maps.size()));
-    CK(cudaMemcpy(b.maps, maps.data(), maps.size(), cudaMemcpyHostToDevice));
+    CK(qdb_bstep_tile_weights(m->embed, m->cfg.vocab, (int)h, o, 1, m->st));
+    CK(cudaStreamSynchronize(m->st));
+    b.wt = wt;
     return 0;
 }
 
@@ -1031,13 +1055,10 @@ static int launch_bstep(qdb_model *m, int n, int max_ctx, const int *tok_in, con
     a.B = n;
     a.Bp = bstep_cols(n);
     a.nsw = qdb_bstep_ring_stages(a.Bp, m->cfg.heads / m->cfg.kv_heads);
-    if (const char *v = getenv("QWEN_ASR_B200_BSTEP_NSW")) {  // tuning: fewer weight-ring stages
-        const int k = atoi(v);
-        if (k >= 2 && k < a.nsw) a.nsw = k;
-    }
+
     a.splits = splits;
     a.layers = m->layers_dev;
-    a.wmaps = b.maps;
+    a.wt = b.wt;
     a.embed = m->embed;
     a.final_norm = m->final_norm;
     a.rope = m->rope;
@@ -1179,9 +1200,9 @@ extern "C" int qdb_trace_batch_step(qdb_session *const *sessions, int n, const f
     if (!embeds || !trace_out) return fail("null argument");
     int maxp = 0;
     if (batch_setup(sessions, n, pos, 0, &m, &maxp) || ensure_tok(m, n)) return -1;
-    if (!bstep_usable(m, n)) return fail("the persistent batched step does not serve %d rows", n);
+    if (!bstep_fits(m, n)) return fail("the persistent batched step does not serve %d rows", n);
     const int ev = qdb_bstep_trace_events(m->cfg.layers);
-    const size_t words = (size_t)m->sms * (ev + 256);  // phase stamps, then layer-1 detail stamps
+    const size_t words = (size_t)m->sms * (ev + 512);  // phase stamps, then layer-1 detail stamps
     if ((size_t)max_words < words) return fail("trace buffer needs %zu words", words);
     unsigned long long *tr = nullptr;
     if (ensure_bstep(m) || dev_alloc(&tr, words)) return -1;

@@ -307,10 +307,11 @@ def test_prefill_attention_groupings(pkg, synth, heads, kv_heads, chunks):
 
 @pytest.mark.parametrize("n", [1, 17, 64])
 def test_persistent_batch_step_matches_graph_path(pkg, synth, monkeypatch, n):
-    """The persistent batched step (one cooperative launch, n <= 64) against
-    the launch-per-kernel graph path on the same sessions: tokens equal under
-    the margin rule and logits within the parity bar, at 1, 17 (padded to 32
-    columns) and 64 rows, with several key splits."""
+    """The persistent batched step (one cooperative launch, n <= 64, selected
+    with QWEN_ASR_B200_BATCH=persistent) against the default launch-per-kernel
+    graph path on the same sessions: tokens equal under the margin rule and
+    logits within the parity bar, at 1, 17 (padded to 32 columns) and 64 rows,
+    with several key splits."""
     cfg = synth.PRESETS["small"]
     ws = synth.WeightSet(cfg, seed=31, norm_jitter=0.1)
     model = pkg.Model(ws, device=0, mask_eos=True)
@@ -324,10 +325,10 @@ def test_persistent_batch_step_matches_graph_path(pkg, synth, monkeypatch, n):
     for step in range(2):
         x = np.stack([embs[b][lens[b] + step] for b in range(n)])
         pos = [lens[b] + step for b in range(n)]
+        monkeypatch.setenv("QWEN_ASR_B200_BATCH", "persistent")
         ta, la = pkg.forward_batch(sa, x, pos, want_logits=True)
-        monkeypatch.setenv("QWEN_ASR_B200_BATCH", "graph")
-        tg, lg = pkg.forward_batch(sg, x, pos, want_logits=True)
         monkeypatch.delenv("QWEN_ASR_B200_BATCH")
+        tg, lg = pkg.forward_batch(sg, x, pos, want_logits=True)
         for b in range(n):
             assert_logits_close(la[b], lg[b], f"n={n} step {step} row {b}")
             assert ta[b] == tg[b] or margin_top2(lg[b], mask_eos=True) <= MARGIN
@@ -377,3 +378,23 @@ def test_prefill_batch_equals_separate_prefills(pkg, synth):
         tb, _, lb = sb[i].forward(emb[i][p], p, want_logits=True)
         assert_logits_close(la, lb, f"session {i}")
         assert ta == tb or margin_top2(lb) <= MARGIN
+
+
+def test_persistent_batch_greedy_loop_matches_graph_path(pkg, synth, monkeypatch):
+    """qdb_decode_greedy_batch through the persistent step (one launch per
+    position) equals the default graph loop, token for token, at the 0.6B
+    shape with 8 utterances of different lengths."""
+    cfg = synth.PRESETS["0.6b"]
+    ws = synth.WeightSet(cfg, seed=0)
+    model = pkg.Model(ws, device=0, mask_eos=True)
+    lens = [40, 75, 13, 120, 64, 90, 27, 101]
+    embs = [synth.audio_embeddings(cfg, L, seed=700 + b) for b, L in enumerate(lens)]
+    sa = [model.session(160) for _ in lens]
+    sg = [model.session(160) for _ in lens]
+    pkg.prefill_batch(sa, embs, [0] * len(lens))
+    pkg.prefill_batch(sg, embs, [0] * len(lens))
+    monkeypatch.setenv("QWEN_ASR_B200_BATCH", "persistent")
+    ta = pkg.decode_greedy_batch(sa, [198] * len(lens), lens, 12)
+    monkeypatch.delenv("QWEN_ASR_B200_BATCH")
+    tg = pkg.decode_greedy_batch(sg, [198] * len(lens), lens, 12)
+    assert (ta == tg).mean() >= 0.9, (ta, tg)  # exact except where a near-tie flips
