@@ -14,7 +14,8 @@ N>1, weak scaling).
 
 One timed step = this rank's utterances: one batched prefill of every prompt
 (qdb_prefill_batch: all rows in one row batch) followed by the greedy decode
-loop (one persistent kernel launch per position). `value` = decoded tokens (all ranks) / decode time
+loop (b=1: one persistent kernel launch per position; batches: a CUDA graph of
+one step replayed per position). `value` = decoded tokens (all ranks) / decode time
 (max over ranks), inputs resident in HBM (device embedding lookup, device
 greedy loop). `e2e` = the same metric through the reference-facing C ABI with
 host buffers: host f32 prompt embeddings (pinned) through qdb_prefill(_batch), then
@@ -56,7 +57,7 @@ CONFIGS = {
     "c2": ("0.6b", 20.0, 200, 64),
     "c3": ("1.7b", 300.0, 1024, 1),
 }
-KV_BYTES_PER_POS = 28 * 8 * 128 * 2 * 2  # fp16 K and V per cached position (all layers)
+KV_BYTES_PER_POS = 28 * 8 * 128 * 2 * 2  # fp16 K and V per cached position (all layers; 0.6B and 1.7B alike)
 METRIC = "decode tok/s/GPU (b=1, b=64) as % of 8 TB/s HBM; end-to-end x-realtime"
 REF_WINDOWS = 8  # reference sample: windows spread evenly over the decode range
 
@@ -300,17 +301,22 @@ def summarize(m, cfg_name, world, steps):
     launch_s = (m["dec_ms"] / 1e3) / (steps * n_dec)
     achieved = bytes_per_step / launch_s / 1e9
     peak, peak_kind = measured_peaks()
-    kernel = "step_kernel" if n_local == 1 else "bstep_kernel"
+    # b=1: one persistent step kernel per token; batches: the CUDA graph of one
+    # step (9 kernels per layer + 5), whose weight + KV bytes are counted once
+    kernel = "step_kernel" if n_local == 1 else "rows_decode"
     return dict(value=value, e2e_value=e2e_value, achieved=achieved, peak=peak, peak_kind=peak_kind,
                 frac=achieved / peak, kernel=kernel, bytes_per_step=bytes_per_step,
                 traffic=step_traffic_from_profile(kernel, cfg_name))
 
 
 def launches_per_step(cfg, n_local, n_dec):
-    # one prefill (all of the rank's prompts in one row batch), per layer: 2 norms, 4 GEMMs, q/k RoPE +
-    # KV append, attention, bf16 split of the SwiGLU output; decode: one persistent step kernel per
-    # token (b=1: qdb_step.cu; up to 64 utterances: qdb_bstep.cu)
-    return cfg.layers * 9 + n_dec
+    # prefill (all of the rank's prompts in one row batch), per layer: 2 norms, 4 GEMMs, q/k RoPE +
+    # KV append, attention, bf16 split of the SwiGLU output. Decode, b=1: one persistent step kernel
+    # per token (qdb_step.cu). Decode, batches: a graph-replayed step of the same 9 kernels per layer
+    # plus embedding lookup, final norm, lm_head GEMM, argmax and the step counter.
+    if n_local == 1:
+        return cfg.layers * 9 + n_dec
+    return cfg.layers * 9 + n_dec * (cfg.layers * 9 + 5)
 
 
 def run_ours(args):
@@ -521,9 +527,9 @@ def profile_step(args):
 
 def profile_batch(args):
     """Fixed case for ncu captures of the batched decode kernels: 64 sessions
-    of the 0.6B synthetic model, a 270-position prefill each, then one
-    forward_batch step inside the NVTX range "decode" (ncu --nvtx
-    --nvtx-include "decode/")."""
+    of the 0.6B synthetic model, a 270-position batched prefill, then three
+    forward_batch steps; the third (a replay of the cached step graph) runs
+    inside the NVTX range "decode" (ncu --nvtx --nvtx-include "decode/")."""
     import torch
     import __graft_entry__ as ge
     pkg = ge.load_package()
@@ -534,12 +540,13 @@ def profile_batch(args):
     model = pkg.Model(ws, device=0, mask_eos=True)
     sess = [model.session(P + 16) for _ in range(B)]
     emb = synth.audio_embeddings(cfg, P, seed=1)
-    for s in sess:
-        s.prefill(emb, 0)
-    pos = np.full(B, P, np.int32)
-    torch.cuda.synchronize()
-    torch.cuda.nvtx.range_push("decode")
-    toks = pkg.forward_batch(sess, np.tile(emb[:1], (B, 1)), pos)
+    pkg.prefill_batch(sess, np.tile(emb, (B, 1)), [0] * B, lens=[P] * B)
+    x = np.tile(emb[:1], (B, 1))
+    for i in range(3):
+        torch.cuda.synchronize()
+        if i == 2:
+            torch.cuda.nvtx.range_push("decode")
+        toks = pkg.forward_batch(sess, x, np.full(B, P + i, np.int32))
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     print(toks[:4].tolist())

@@ -218,6 +218,25 @@ int qdb_forward_noalloc(qdb_session *s, const float *embed_dev, int pos, int *to
  * (every prefill / decode call fails before its first kernel launch). */
 int qdb_model_set_wait_limit(qdb_model *m, long long cycles);
 
+/* ---- Log-mel front end, replaces qwen_mel_spectrogram (qwen_asr_audio.c:293-390,
+ * declared at qwen_asr_audio.h:32). 16 kHz mono f32 samples -> [128, n_frames]
+ * f32 log-mel (reflect pad 200, periodic Hann 400, 201-bin DFT power, hop 160
+ * with the last frame dropped, Slaney filter bank, log10, clamp to the global
+ * max - 8, (v + 4) / 4). Runs on the current CUDA device. ---- */
+
+/* n_frames the spectrogram of n_samples has (<= 0: too short). */
+int qdb_mel_frames(int n_samples);
+
+/* Same contract as the reference: returns a malloc'd [128, *out_frames] host
+ * array the caller frees with free(), or NULL (audio too short, or an error;
+ * the message is in qdb_last_error). Synchronous. */
+float *qdb_mel_spectrogram(const float *samples, int n_samples, int *out_frames);
+
+/* Device form: samples_dev f32 [n_samples] -> mel_dev f32 [128, n_frames]
+ * (n_frames = qdb_mel_frames(n_samples)), enqueued on `stream` (a
+ * cudaStream_t as void*, NULL = the legacy default stream). 0 = ok. */
+int qdb_mel_spectrogram_device(const float *samples_dev, int n_samples, float *mel_dev, void *stream);
+
 /* Waits for all queued work of the model's stream. */
 int qdb_model_sync(qdb_model *m);
 

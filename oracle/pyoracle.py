@@ -235,3 +235,25 @@ def margin_top2(logits: np.ndarray, mask_eos: bool = False) -> float:
         l[151645] = -np.inf
     top = np.partition(l, -2)[-2:]
     return float(top[1] - top[0])
+
+
+def ref_mel_spectrogram(samples, so_path: str | None = None):
+    """The reference's own qwen_mel_spectrogram (qwen_asr_audio.c:293, compiled
+    unmodified into oracle/_ref): [128, n_frames] float32, or None when it
+    returns NULL (audio too short)."""
+    path = so_path or ref_so_path()
+    if not path:
+        raise FileNotFoundError("oracle/_ref not built (run `make -C oracle ref` where the reference tree exists)")
+    lib = ctypes.CDLL(path)
+    lib.qwen_mel_spectrogram.restype = ctypes.POINTER(ctypes.c_float)
+    lib.qwen_mel_spectrogram.argtypes = [_f32p, ctypes.c_int, _i32p]
+    x = np.ascontiguousarray(samples, dtype=np.float32)
+    nf = ctypes.c_int(0)
+    p = lib.qwen_mel_spectrogram(_p(x, _f32p), len(x), ctypes.byref(nf))
+    if not p:
+        return None
+    out = np.ctypeslib.as_array(p, (128, nf.value)).copy()
+    libc = ctypes.CDLL(None)
+    libc.free.argtypes = [ctypes.c_void_p]
+    libc.free(ctypes.cast(p, ctypes.c_void_p))
+    return out

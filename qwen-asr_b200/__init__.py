@@ -63,6 +63,9 @@ ABI = {
     "qdb_decode_greedy_batch": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, _i32p, _i32p,
                                                ctypes.c_int, _i32p]),
     "qdb_model_sync": (ctypes.c_int, [ctypes.c_void_p]),
+    "qdb_mel_frames": (ctypes.c_int, [ctypes.c_int]),
+    "qdb_mel_spectrogram": (ctypes.POINTER(ctypes.c_float), [_f32p, ctypes.c_int, _i32p]),
+    "qdb_mel_spectrogram_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
     "qdb_forward_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "qdb_model_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
     "qdb_model_set_wait_limit": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_longlong]),
@@ -297,6 +300,42 @@ def trace_batch_step(sessions, embeds: np.ndarray, pos, max_ctas: int = 1024) ->
     t = buf[:max_ctas * ev].reshape(-1, ev)
     ctas = int((t[:, -1] != 0).sum())
     return t[:ctas], buf[ctas * ev:ctas * ev + ctas * 256].reshape(ctas, 256)
+
+
+_libc = ctypes.CDLL(None)
+_libc.free.argtypes = [ctypes.c_void_p]
+_libc.free.restype = None
+
+
+def mel_frames(n_samples: int) -> int:
+    """Frames the log-mel of n_samples has (<= 0: too short)."""
+    return lib.qdb_mel_frames(int(n_samples))
+
+
+def mel_spectrogram(samples: np.ndarray):
+    """Mirror of qwen_mel_spectrogram (qwen_asr_audio.c:293): 16 kHz mono
+    samples -> float32 [128, n_frames] computed on the current CUDA device, or
+    None when the audio is too short (the reference returns NULL). Other
+    failures raise."""
+    x = np.ascontiguousarray(samples, dtype=np.float32)
+    nf = ctypes.c_int(0)
+    p = lib.qdb_mel_spectrogram(_ptr(x, _f32p), len(x), ctypes.byref(nf))
+    if not p:
+        if mel_frames(len(x)) <= 0:
+            return None
+        raise _err("qdb_mel_spectrogram")
+    try:
+        return np.ctypeslib.as_array(p, (128, nf.value)).copy()
+    finally:
+        _libc.free(ctypes.cast(p, ctypes.c_void_p))
+
+
+def mel_spectrogram_device(samples_ptr: int, n_samples: int, mel_ptr: int, stream: int = 0) -> None:
+    """Device form: float32 samples at samples_ptr -> float32 [128, mel_frames(n)]
+    at mel_ptr, enqueued on `stream` (a cudaStream_t handle, 0 = default)."""
+    if lib.qdb_mel_spectrogram_device(ctypes.c_void_p(samples_ptr), int(n_samples), ctypes.c_void_p(mel_ptr),
+                                      ctypes.c_void_p(stream)):
+        raise _err("qdb_mel_spectrogram_device")
 
 
 def decode_greedy_batch(sessions, first_tokens, pos, n_steps: int) -> np.ndarray:

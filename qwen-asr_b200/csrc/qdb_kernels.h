@@ -187,6 +187,9 @@ cudaError_t qdb_set_wait_limit_tcgemm(long long cycles);
 // Writes (host memory, 128 bytes) the tensor map of a bf16 [rows, cols]
 // weight matrix for 128 x 64 tiles, 128-byte swizzle. 0 = ok.
 int qdb_make_weight_map(void *map, const uint16_t *base, int rows, int cols);
+
+// Sets the calling thread's qdb_last_error message; returns -1.
+int qdb_set_error(const char *msg);
 // step (optional, device): the rows' tokens are read at tokens + *step * n
 // (embed) / written at tokens + *step * n (argmax), and positions advance by
 // *step (qk_rope_append, attn_rows): the form a captured decode step replays.

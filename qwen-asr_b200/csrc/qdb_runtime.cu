@@ -39,6 +39,10 @@ static int fail(const char *fmt, ...) {
     return -1;
 }
 
+// Records msg as the calling thread's last error (for the other translation
+// units' entry points) and returns -1.
+int qdb_set_error(const char *msg) { return fail("%s", msg); }
+
 #define CK(call)                                                                              \
     do {                                                                                      \
         cudaError_t e_ = (call);                                                              \

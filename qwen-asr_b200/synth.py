@@ -196,3 +196,31 @@ def prompt_embeddings(ws: WeightSet, audio: np.ndarray) -> np.ndarray:
 def utterance(ws: WeightSet, seconds: float, seed: int) -> np.ndarray:
     n = int(round(seconds * ENC_TOKENS_PER_SECOND))
     return prompt_embeddings(ws, audio_embeddings(ws.cfg, n, seed))
+
+
+SAMPLE_RATE = 16000
+
+
+def speech_audio(n_samples: int, seed: int) -> np.ndarray:
+    """Seeded synthetic 16 kHz mono float32 audio with speech-like structure:
+    a gliding harmonic voice (100-250 Hz fundamental, 8 harmonics with a
+    formant-shaped envelope) gated into 80-400 ms syllables, plus low-level
+    noise, peak about 0.5. Stands in for recorded utterances (none ship)."""
+    rng = np.random.default_rng(seed)
+    t = np.arange(n_samples, dtype=np.float64) / SAMPLE_RATE
+    f0 = 100.0 + 150.0 * rng.random() + 30.0 * np.sin(2 * np.pi * (0.3 + 0.5 * rng.random()) * t)
+    phase = 2 * np.pi * np.cumsum(f0) / SAMPLE_RATE
+    formant = 500.0 + 1500.0 * rng.random()
+    voice = np.zeros(n_samples)
+    for h in range(1, 9):
+        voice += np.exp(-((h * f0 - formant) / 800.0) ** 2) * np.sin(h * phase) / h
+    gate = np.zeros(n_samples)
+    i = 0
+    while i < n_samples:
+        on = int(SAMPLE_RATE * (0.08 + 0.32 * rng.random()))
+        off = int(SAMPLE_RATE * 0.15 * rng.random())
+        gate[i:i + on] = np.hanning(max(on, 2))[:max(0, min(on, n_samples - i))]
+        i += on + off
+    x = voice * gate + 0.01 * rng.standard_normal(n_samples)
+    peak = np.abs(x).max() if n_samples else 1.0
+    return (0.5 * x / max(peak, 1e-9)).astype(np.float32)

@@ -11,6 +11,9 @@ reference tree.
 Run here (needs oracle/_ref built):  python tests/golden/make_golden.py
   --small-only        only the three small shapes
   --bench=c0,c1,...   only the named benchmark-length cases (c0 c1 c3 c2set)
+  --mel               only mel_ref.npz: the reference's qwen_mel_spectrogram
+                      (qwen_asr_audio.c, compiled unmodified into oracle/_ref)
+                      on seeded synthetic audio (synth.speech_audio)
 
 The benchmark-length cases record the reference's own prefill time
 (ref_prefill_s, with ref_threads threads): c3's 3914-position 1.7B prefill is
@@ -28,7 +31,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 
 import __graft_entry__ as ge  # noqa: E402
-from oracle.pyoracle import RefDecoder, margin_top2  # noqa: E402
+from oracle.pyoracle import RefDecoder, margin_top2, ref_mel_spectrogram  # noqa: E402
 
 synth = ge.load_synth()
 
@@ -153,7 +156,39 @@ def run_c2set(threads):
     return out
 
 
+# Log-mel cases: (name, n_samples, audio seed; seed < 0 = silence). Short
+# ones store the whole [128, frames] output; long ones per-bin and per-frame
+# sums plus the first 64 frames.
+MEL_FULL = [("m_short", 161, 1), ("m_two_frames", 400, 2), ("m_ragged", 4007, 3), ("m_silence", 16000, -1)]
+MEL_SUMS = [("m_2s", 32033, 4), ("m_10s", 160000, 5), ("m_30s", 480000, 6)]
+MEL_TOO_SHORT = [0, 1, 100, 159]
+
+
+def mel_audio(n, seed):
+    return np.zeros(n, np.float32) if seed < 0 else synth.speech_audio(n, seed)
+
+
+def run_mel():
+    out = {"too_short": np.array(MEL_TOO_SHORT, np.int32)}
+    for n in MEL_TOO_SHORT:
+        assert ref_mel_spectrogram(mel_audio(n, 0)) is None
+    for name, n, seed in MEL_FULL + MEL_SUMS:
+        m = ref_mel_spectrogram(mel_audio(n, seed))
+        out[name + "_args"] = np.array([n, seed], np.int64)
+        if (name, n, seed) in MEL_FULL:
+            out[name] = m
+        else:
+            out[name + "_bins"] = m.sum(axis=1, dtype=np.float64)
+            out[name + "_frames"] = m.sum(axis=0, dtype=np.float64)
+            out[name + "_head"] = m[:, :64].copy()
+    return out
+
+
 def main():
+    if "--mel" in sys.argv:
+        np.savez_compressed(os.path.join(HERE, "mel_ref.npz"), **run_mel())
+        print("wrote mel_ref.npz")
+        return
     threads = min(os.cpu_count() or 1, 16)
     for case in ([] if any(a.startswith("--bench=") for a in sys.argv) else SMALL_CASES):
         d = run_case(*case, full_logits=True, threads=threads)
