@@ -218,6 +218,68 @@ int qdb_forward_noalloc(qdb_session *s, const float *embed_dev, int pos, int *to
  * (every prefill / decode call fails before its first kernel launch). */
 int qdb_model_set_wait_limit(qdb_model *m, long long cycles);
 
+/* ---- Streaming scheduler: many concurrent streams of one model, the
+ * decoder side of the streaming mode (stream_impl, qwen_asr.c:1214-2152).
+ * Each call processes chunk k of every stream together: prompt rebuild with
+ * the rolled-back text prefix, KV rewind to the longest unchanged prompt
+ * prefix, ONE row-batched prefill of all deltas, ONE device greedy loop over
+ * all streams, then the reference's commit rules on token ids (repeat-run
+ * suppression, fixed frontier, overlap de-duplication, degeneration /
+ * stagnation recovery, periodic re-anchoring). The encoder and its window
+ * cache stay with the caller, which clears that cache when a stream reports
+ * a reset. Emitted pieces are token ids. ---- */
+typedef struct qdb_streams qdb_streams;
+
+typedef struct {
+    int max_new_tokens;  /* decode steps per chunk (ctx->stream_max_new_tokens, 32) */
+    int rollback;        /* ctx->stream_rollback (5) */
+    int unfixed_chunks;  /* ctx->stream_unfixed_chunks (2) */
+    int past_text;       /* ctx->past_text_conditioning (0 by default in the reference) */
+    /* prompt template; a NULL pointer selects the reference's ids
+     * (PROMPT_PREFIX_HEAD / _TAIL / PROMPT_SUFFIX_BASE, qwen_asr.c:339-347) */
+    const int *head_tokens; int n_head_tokens;
+    const int *tail_tokens; int n_tail_tokens;
+    const int *suffix_tokens; int n_suffix_tokens;
+    const int *prompt_tokens; int n_prompt_tokens; /* ctx->prompt_tokens (NULL = none) */
+    const int *force_tokens; int n_force_tokens;   /* ctx->force_prompt_tokens (NULL = none) */
+    int asr_text_token;  /* <asr_text> id (<= 0: 151704) */
+} qdb_stream_config;
+
+/* n_streams sessions on model m; cfg NULL = the reference defaults
+ * (qwen_asr.c:238-242). NULL on error. */
+qdb_streams *qdb_streams_create(qdb_model *m, int n_streams, const qdb_stream_config *cfg);
+void qdb_streams_free(qdb_streams *s);
+
+/* One chunk of every stream. audio[i]: host f32 [audio_len[i], hidden], the
+ * encoder output this chunk's prompt carries (cached windows + re-encoded
+ * tail); audio_len[i] <= 0 skips stream i for this chunk (the reference's
+ * "no encoder output" path). is_final[i]: last chunk of stream i.
+ * Outputs (optional): n_emitted[i] text tokens committed this chunk (read
+ * them with qdb_streams_tokens), reset[i] 1 = recovery reset, 2 = periodic
+ * re-anchor (the caller clears its encoder window cache). 0 = ok. */
+int qdb_streams_chunk(qdb_streams *s, const float *const *audio, const int *audio_len, const int *is_final,
+                      int *n_emitted, int *reset);
+
+/* Token history of stream i: which 0 = emitted text tokens, 1 = raw history
+ * (prefix + generated, qwen_asr.c raw_tokens), 2 = stable candidate. Copies
+ * up to cap ids into buf (may be NULL) and returns the full count, or -1. */
+int qdb_streams_tokens(const qdb_streams *s, int stream, int which, int *buf, int cap);
+
+/* Counters of stream i into out[8]: chunk index, chunks decoded, prefill rows
+ * (total), prefill rows reused, decode steps counted as the reference counts
+ * n_generated, the last chunk's n_generated, its reused prefix, its prefill
+ * length. 0 = ok. */
+int qdb_streams_stats(const qdb_streams *s, int stream, long long *out);
+
+/* Restarts stream i as a new stream (empty history, chunk 0, no prefix to
+ * reuse); its KV storage is kept. 0 = ok. */
+int qdb_streams_reset(qdb_streams *s, int stream);
+
+/* Device time of the last qdb_streams_chunk call: ms[0] the batched prefill
+ * (with the prompt rows' upload), ms[1] the greedy loop; counts[0] streams that
+ * ran, counts[1] prompt rows prefilled. Either pointer may be NULL. 0 = ok. */
+int qdb_streams_last_chunk(const qdb_streams *s, float *ms, int *counts);
+
 /* ---- Log-mel front end, replaces qwen_mel_spectrogram (qwen_asr_audio.c:293-390,
  * declared at qwen_asr_audio.h:32). 16 kHz mono f32 samples -> [128, n_frames]
  * f32 log-mel (reflect pad 200, periodic Hann 400, 201-bin DFT power, hop 160

@@ -64,6 +64,14 @@ ABI = {
                                                ctypes.c_int, _i32p]),
     "qdb_model_sync": (ctypes.c_int, [ctypes.c_void_p]),
     "qdb_mel_frames": (ctypes.c_int, [ctypes.c_int]),
+    "qdb_streams_create": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
+    "qdb_streams_free": (None, [ctypes.c_void_p]),
+    "qdb_streams_chunk": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), _i32p, _i32p, _i32p,
+                                         _i32p]),
+    "qdb_streams_tokens": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, _i32p, ctypes.c_int]),
+    "qdb_streams_stats": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_longlong)]),
+    "qdb_streams_reset": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
+    "qdb_streams_last_chunk": (ctypes.c_int, [ctypes.c_void_p, _f32p, _i32p]),
     "qdb_mel_spectrogram": (ctypes.POINTER(ctypes.c_float), [_f32p, ctypes.c_int, _i32p]),
     "qdb_mel_spectrogram_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
     "qdb_forward_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
@@ -300,6 +308,96 @@ def trace_batch_step(sessions, embeds: np.ndarray, pos, max_ctas: int = 1024) ->
     t = buf[:max_ctas * ev].reshape(-1, ev)
     ctas = int((t[:, -1] != 0).sum())
     return t[:ctas], buf[ctas * ev:ctas * ev + ctas * 256].reshape(ctas, 256)
+
+
+class QdbStreamConfig(ctypes.Structure):
+    _fields_ = [("max_new_tokens", ctypes.c_int), ("rollback", ctypes.c_int), ("unfixed_chunks", ctypes.c_int),
+                ("past_text", ctypes.c_int),
+                ("head_tokens", _i32p), ("n_head_tokens", ctypes.c_int),
+                ("tail_tokens", _i32p), ("n_tail_tokens", ctypes.c_int),
+                ("suffix_tokens", _i32p), ("n_suffix_tokens", ctypes.c_int),
+                ("prompt_tokens", _i32p), ("n_prompt_tokens", ctypes.c_int),
+                ("force_tokens", _i32p), ("n_force_tokens", ctypes.c_int),
+                ("asr_text_token", ctypes.c_int)]
+
+
+class Streams:
+    """Many concurrent streams of one model (qdb_streams_*): the decoder side of
+    the reference's streaming mode (stream_impl, qwen_asr.c:1214-2152), one
+    chunk of every stream per call. Token-template keys (head, tail, suffix,
+    prompt, force) take id lists; None keeps the reference's ids."""
+
+    def __init__(self, model: Model, n_streams: int, max_new_tokens=32, rollback=5, unfixed_chunks=2,
+                 past_text=False, head=None, tail=None, suffix=None, prompt=None, force=None, asr_text_token=0):
+        self.model = model
+        self.n = n_streams
+        c = QdbStreamConfig(max_new_tokens, rollback, unfixed_chunks, 1 if past_text else 0)
+        self._keep = []
+        for name, v in (("head", head), ("tail", tail), ("suffix", suffix), ("prompt", prompt), ("force", force)):
+            if v is not None:
+                a = np.ascontiguousarray(v, dtype=np.int32)
+                self._keep.append(a)
+                setattr(c, name + "_tokens", _ptr(a, _i32p))
+                setattr(c, "n_" + name + "_tokens", len(a))
+        c.asr_text_token = asr_text_token
+        self.h = lib.qdb_streams_create(model.h, n_streams, ctypes.byref(c))
+        if not self.h:
+            raise _err("qdb_streams_create")
+
+    def chunk(self, audio, is_final):
+        """audio: list of float32 [rows, hidden] arrays (None or 0 rows = no
+        encoder output this chunk); is_final: list of bools. Returns
+        (n_emitted, reset) int arrays."""
+        arrs = [None if a is None else np.ascontiguousarray(a, dtype=np.float32) for a in audio]
+        ptrs = (ctypes.c_void_p * self.n)(*[a.ctypes.data if a is not None and a.size else None for a in arrs])
+        lens = np.array([0 if a is None else (a.shape[0] if a.size else 0) for a in arrs], np.int32)
+        fin = np.ascontiguousarray(is_final, dtype=np.int32)
+        ne = np.zeros(self.n, np.int32)
+        rs = np.zeros(self.n, np.int32)
+        if lib.qdb_streams_chunk(self.h, ptrs, _ptr(lens, _i32p), _ptr(fin, _i32p), _ptr(ne, _i32p),
+                                 _ptr(rs, _i32p)):
+            raise _err("qdb_streams_chunk")
+        return ne, rs
+
+    def tokens(self, i: int, which: str = "emitted") -> np.ndarray:
+        w = {"emitted": 0, "raw": 1, "stable": 2}[which]
+        n = lib.qdb_streams_tokens(self.h, i, w, None, 0)
+        if n < 0:
+            raise _err("qdb_streams_tokens")
+        out = np.zeros(max(n, 1), np.int32)
+        lib.qdb_streams_tokens(self.h, i, w, _ptr(out, _i32p), n)
+        return out[:n]
+
+    def stats(self, i: int) -> dict:
+        v = (ctypes.c_longlong * 8)()
+        if lib.qdb_streams_stats(self.h, i, v):
+            raise _err("qdb_streams_stats")
+        keys = ("chunk_idx", "chunks", "prefill_total", "prefill_reused", "decoded", "last_generated",
+                "last_reused", "last_prefill_len")
+        return dict(zip(keys, list(v)))
+
+    def reset(self, i: int):
+        """Restart stream i as a new stream (its KV storage is kept)."""
+        if lib.qdb_streams_reset(self.h, i):
+            raise _err("qdb_streams_reset")
+
+    def last_chunk(self) -> dict:
+        """Device ms of the last chunk's prefill and greedy loop, streams run, rows prefilled."""
+        ms = np.zeros(2, np.float32)
+        cnt = np.zeros(2, np.int32)
+        lib.qdb_streams_last_chunk(self.h, _ptr(ms, _f32p), _ptr(cnt, _i32p))
+        return {"prefill_ms": float(ms[0]), "decode_ms": float(ms[1]), "active": int(cnt[0]), "rows": int(cnt[1])}
+
+    def close(self):
+        if self.h and not _exiting[0]:
+            lib.qdb_streams_free(self.h)
+        self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 _libc = ctypes.CDLL(None)

@@ -190,6 +190,15 @@ int qdb_make_weight_map(void *map, const uint16_t *base, int rows, int cols);
 
 // Sets the calling thread's qdb_last_error message; returns -1.
 int qdb_set_error(const char *msg);
+
+// What the host-side modules (stream scheduler) need of a finalized model.
+struct qdb_model;
+struct QdbModelInfo {
+    const uint16_t *embed;  // device bf16 [vocab, hidden]
+    int hidden, vocab, device;
+    cudaStream_t stream;
+};
+int qdb_model_internals(qdb_model *m, QdbModelInfo *out);
 // step (optional, device): the rows' tokens are read at tokens + *step * n
 // (embed) / written at tokens + *step * n (argmax), and positions advance by
 // *step (qk_rope_append, attn_rows): the form a captured decode step replays.

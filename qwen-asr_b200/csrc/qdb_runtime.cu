@@ -170,6 +170,17 @@ struct qdb_session {
 
 extern "C" const char *qdb_last_error(void) { return g_err.c_str(); }
 
+int qdb_model_internals(qdb_model *m, QdbModelInfo *out) {
+    if (!m || !out) return fail("null model");
+    if (!m->finalized) return fail("model not finalized");
+    out->embed = m->embed;
+    out->hidden = m->cfg.hidden;
+    out->vocab = m->cfg.vocab;
+    out->device = m->device;
+    out->stream = m->st;
+    return 0;
+}
+
 extern "C" int qdb_device_count(void) {
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess) {

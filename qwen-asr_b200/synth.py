@@ -224,3 +224,64 @@ def speech_audio(n_samples: int, seed: int) -> np.ndarray:
     x = voice * gate + 0.01 * rng.standard_normal(n_samples)
     peak = np.abs(x).max() if n_samples else 1.0
     return (0.5 * x / max(peak, 1e-9)).astype(np.float32)
+
+
+class SyntheticEncoder:
+    """Stand-in for one stream's encoder and its window cache (qwen_asr.c:1506-1674):
+    completed windows of `window_s` seconds keep fixed rows (seeded per window
+    index), the partial tail window is re-encoded each chunk (rows seeded by
+    its length), at most `max_windows` completed windows stay (eviction), and
+    clear() drops the cache like stream_clear_enc_cache. Rows per second
+    follow the encoder's 13 tokens per 100 mel frames (qwen_asr_encoder.c:186-211).
+    Synthetic data for the streaming scheduler's tests and benchmark."""
+
+    def __init__(self, hidden, seed, chunk_s=2.0, window_s=8.0, max_windows=4, scale=1.0, bank=None):
+        # bank: optional f32 [rows, hidden]; rows are then seeded picks from it
+        # (cheap enough for hundreds of streams) instead of fresh draws
+        self.h, self.seed, self.scale, self.bank = hidden, seed, scale, bank
+        self.chunk, self.window, self.max_windows = chunk_s, window_s, max_windows
+        self.cursor = 0.0
+        self.next_window = 0.0
+        self.cache = []  # (start_s, rows)
+
+    @staticmethod
+    def rows_for(seconds):
+        frames = int(round(seconds * 100))
+        full, rem = divmod(frames, 100)
+        n = full * 13
+        if rem:
+            w = rem
+            for _ in range(3):
+                w = (w - 1) // 2 + 1
+            n += w
+        return n
+
+    def _rows(self, key, n):
+        rng = np.random.default_rng([self.seed, *key])
+        if self.bank is not None:
+            return self.bank[rng.integers(0, len(self.bank), n)]
+        return (self.scale * rng.standard_normal((n, self.h))).astype(np.float32)
+
+    def advance(self, total_s):
+        """Audio rows of the next chunk (None when the stream has ended)."""
+        if self.cursor >= total_s:
+            return None, True
+        self.cursor = min(self.cursor + self.chunk, total_s)
+        full_end = int(self.cursor / self.window) * self.window
+        while self.next_window < full_end:
+            self.cache.append((self.next_window, self._rows((int(self.next_window * 1000), 0),
+                                                             self.rows_for(self.window))))
+            self.next_window += self.window
+        parts = []
+        if full_end < self.cursor:
+            tail_s = self.cursor - full_end
+            parts.append(self._rows((int(full_end * 1000), int(tail_s * 1000)), self.rows_for(tail_s)))
+        while len(self.cache) > self.max_windows:
+            self.cache.pop(0)
+        rows = [r for _, r in self.cache] + parts
+        audio = np.concatenate(rows) if rows else np.zeros((0, self.h), np.float32)
+        return audio, self.cursor >= total_s
+
+    def clear(self):
+        self.cache = []
+        self.next_window = int(self.cursor / self.window) * self.window
