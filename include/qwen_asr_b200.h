@@ -252,8 +252,9 @@ void qdb_streams_free(qdb_streams *s);
 
 /* One chunk of every stream. audio[i]: host f32 [audio_len[i], hidden], the
  * encoder output this chunk's prompt carries (cached windows + re-encoded
- * tail); audio_len[i] <= 0 skips stream i for this chunk (the reference's
- * "no encoder output" path). is_final[i]: last chunk of stream i.
+ * tail); audio_len[i] == 0 is the reference's "no encoder output" path (the
+ * chunk counts but decodes nothing); audio_len[i] < 0 leaves stream i out of
+ * this call untouched. is_final[i]: last chunk of stream i.
  * Outputs (optional): n_emitted[i] text tokens committed this chunk (read
  * them with qdb_streams_tokens), reset[i] 1 = recovery reset, 2 = periodic
  * re-anchor (the caller clears its encoder window cache). 0 = ok. */

@@ -257,3 +257,61 @@ def ref_mel_spectrogram(samples, so_path: str | None = None):
     libc.free.argtypes = [ctypes.c_void_p]
     libc.free(ctypes.cast(p, ctypes.c_void_p))
     return out
+
+
+class RefEncoder:
+    """The reference's own qwen_encoder_load / qwen_encoder_forward
+    (qwen_asr_encoder.c, compiled unmodified into oracle/_ref) over a
+    synth.EncoderWeightSet blob."""
+
+    def __init__(self, ews, threads: int = 1, so_path: str | None = None):
+        path = so_path or ref_so_path()
+        if not path:
+            raise FileNotFoundError("oracle/_ref not built (run `make -C oracle ref` where the reference tree exists)")
+        lib = ctypes.CDLL(path)
+        lib.refh_encoder_create.restype = ctypes.c_void_p
+        lib.refh_encoder_create.argtypes = [_i32p, ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p,
+                                            ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64),
+                                            _i32p, _i32p, ctypes.POINTER(ctypes.c_int64), ctypes.c_int]
+        lib.refh_encoder_forward.restype = ctypes.c_int
+        lib.refh_encoder_forward.argtypes = [ctypes.c_void_p, _f32p, ctypes.c_int, _f32p, ctypes.c_int]
+        lib.refh_encoder_free.argtypes = [ctypes.c_void_p]
+        self.lib, self.ews, self.cfg = lib, ews, ews.cfg
+        names, offs, sizes, shapes = ews.table()
+        n = len(names)
+        ecfg = np.array(ews.cfg.as_tuple(), dtype=np.int32)
+        name_blob = b"".join(nm.encode() + b"\0" for nm in names)
+        offs_a = np.array(offs, dtype=np.int64)
+        sizes_a = np.array(sizes, dtype=np.int64)
+        dt = np.full(n, 2, dtype=np.int32)  # DTYPE_BF16
+        nd = np.array([2 if s[1] else 1 for s in shapes], dtype=np.int32)
+        sh = np.array(shapes, dtype=np.int64).reshape(-1)
+        self._keep = (ecfg, name_blob, offs_a, sizes_a, dt, nd, sh)
+        self.h = lib.refh_encoder_create(_p(ecfg, _i32p), ctypes.c_void_p(ews.blob.ctypes.data), n, name_blob,
+                                         _p(offs_a, ctypes.POINTER(ctypes.c_int64)),
+                                         _p(sizes_a, ctypes.POINTER(ctypes.c_int64)), _p(dt, _i32p), _p(nd, _i32p),
+                                         _p(sh, ctypes.POINTER(ctypes.c_int64)), threads)
+        if not self.h:
+            raise RuntimeError("reference qwen_encoder_load failed")
+
+    def forward(self, mel):
+        """mel f32 [128, frames] -> f32 [seq, output_dim]"""
+        mel = np.ascontiguousarray(mel, dtype=np.float32)
+        frames = mel.shape[1]
+        cap = frames  # seq <= frames
+        out = np.empty((cap, self.cfg.output_dim), np.float32)
+        n = self.lib.refh_encoder_forward(self.h, _p(mel, _f32p), frames, _p(out, _f32p), cap)
+        if n < 0:
+            raise RuntimeError("reference qwen_encoder_forward failed")
+        return out[:n].copy()
+
+    def close(self):
+        if self.h:
+            self.lib.refh_encoder_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

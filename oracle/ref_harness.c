@@ -18,6 +18,8 @@
  *   switch; this is the benchmark's fixed-length-decode convention.
  * - Logits: after each step ctx->dec_x holds the final-normed hidden state
  *   (qwen_asr_decoder.c:474); logits are that vector times the tied embedding.
+ * - Audio encoder (refh_encoder_*): qwen_encoder_load / qwen_encoder_forward
+ *   (qwen_asr_encoder.c) over a tensor table of the same kind.
  */
 #include "qwen_asr.h"
 #include "qwen_asr_kernels.h"
@@ -72,13 +74,12 @@ typedef struct {
     multi_safetensors_t *ms;
 } refh_t;
 
-/* cfg = {hidden, layers, heads, kv_heads, head_dim, intermediate, vocab}.
- * names: n_tensors NUL-terminated strings back to back. offsets are byte
- * offsets into blob; dtypes use safetensor_dtype_t; shapes are [n][2]. */
-void *refh_create(const int *cfg, float eps, float theta, const uint8_t *blob,
-                  int n_tensors, const char *names, const int64_t *offsets,
-                  const int64_t *nbytes, const int *dtypes, const int *ndims,
-                  const int64_t *shapes, int n_threads) {
+/* In-memory tensor table over one blob (the loaders read tensors by name
+ * through multi_safetensors_find). Shapes are [n][2]; tensors of more
+ * dimensions are passed flattened to two (the loaders use only the element
+ * count). */
+static refh_t *table_create(const uint8_t *blob, int n_tensors, const char *names, const int64_t *offsets,
+                            const int64_t *nbytes, const int *dtypes, const int *ndims, const int64_t *shapes) {
     if (n_tensors > SAFETENSORS_MAX_TENSORS) return NULL;
     refh_t *h = (refh_t *)calloc(1, sizeof(*h));
     h->sf = (safetensors_file_t *)calloc(1, sizeof(safetensors_file_t));
@@ -102,6 +103,18 @@ void *refh_create(const int *cfg, float eps, float theta, const uint8_t *blob,
     }
     h->ms->shards[0] = h->sf;
     h->ms->num_shards = 1;
+    return h;
+}
+
+/* cfg = {hidden, layers, heads, kv_heads, head_dim, intermediate, vocab}.
+ * names: n_tensors NUL-terminated strings back to back. offsets are byte
+ * offsets into blob; dtypes use safetensor_dtype_t; shapes are [n][2]. */
+void *refh_create(const int *cfg, float eps, float theta, const uint8_t *blob,
+                  int n_tensors, const char *names, const int64_t *offsets,
+                  const int64_t *nbytes, const int *dtypes, const int *ndims,
+                  const int64_t *shapes, int n_threads) {
+    refh_t *h = table_create(blob, n_tensors, names, offsets, nbytes, dtypes, ndims, shapes);
+    if (!h) return NULL;
 
     qwen_config_t *c = &h->ctx->config;
     c->dec_hidden = cfg[0];
@@ -206,4 +219,66 @@ void refh_free(void *hp) {
     free(h->ms);
     free(h->sf);
     free(h);
+}
+
+/* ---- Audio encoder: the reference's qwen_encoder_load / qwen_encoder_forward
+ * (qwen_asr_encoder.c:66-168, :171-372) over the same kind of tensor table.
+ * ecfg = {d_model, layers, heads, head_dim, ffn_dim, output_dim}; the window
+ * settings are the reference's defaults (qwen_asr.c:183 and the config
+ * detection: n_window 50, n_window_infer 800, chunk 100). */
+void *refh_encoder_create(const int *ecfg, const uint8_t *blob, int n_tensors, const char *names,
+                          const int64_t *offsets, const int64_t *nbytes, const int *dtypes, const int *ndims,
+                          const int64_t *shapes, int n_threads) {
+    refh_t *h = table_create(blob, n_tensors, names, offsets, nbytes, dtypes, ndims, shapes);
+    if (!h) return NULL;
+    qwen_config_t *c = &h->ctx->config;
+    c->enc_d_model = ecfg[0];
+    c->enc_layers = ecfg[1];
+    c->enc_heads = ecfg[2];
+    c->enc_head_dim = ecfg[3];
+    c->enc_ffn_dim = ecfg[4];
+    c->enc_output_dim = ecfg[5];
+    c->enc_n_window = 50;
+    c->enc_n_window_infer = 800;
+    c->enc_chunk_size = 100;
+    c->enc_conv_proj_dim = QWEN_CONV_HIDDEN * 16;
+    h->ctx->safetensors = h->ms;
+    qwen_set_threads(n_threads > 0 ? n_threads : 1);
+    if (qwen_encoder_load(&h->ctx->encoder, h->ms, c) != 0) {
+        free(h->ctx); free(h->ms); free(h->sf); free(h);
+        return NULL;
+    }
+    return h;
+}
+
+/* mel [128, frames] -> out [seq_len, output_dim] (up to cap_rows rows);
+ * returns seq_len, or -1. */
+int refh_encoder_forward(void *hp, const float *mel, int frames, float *out, int cap_rows) {
+    refh_t *h = (refh_t *)hp;
+    int seq = 0;
+    float *e = qwen_encoder_forward(h->ctx, mel, frames, &seq);
+    if (!e) return -1;
+    int n = seq < cap_rows ? seq : cap_rows;
+    if (out) memcpy(out, e, sizeof(float) * (size_t)n * h->ctx->config.enc_output_dim);
+    free(e);
+    return seq;
+}
+
+void refh_encoder_free(void *hp) {
+    refh_t *h = (refh_t *)hp;
+    if (!h) return;
+    qwen_encoder_t *enc = &h->ctx->encoder;
+    free(enc->conv1_weight); free(enc->conv1_bias); free(enc->conv2_weight); free(enc->conv2_bias);
+    free(enc->conv3_weight); free(enc->conv3_bias); free(enc->conv_out_weight);
+    for (int i = 0; i < h->ctx->config.enc_layers; i++) {
+        qwen_enc_layer_t *l = &enc->layers[i];
+        free(l->wq_weight); free(l->wq_bias); free(l->wk_weight); free(l->wk_bias);
+        free(l->wv_weight); free(l->wv_bias); free(l->wo_weight); free(l->wo_bias);
+        free(l->attn_norm_weight); free(l->attn_norm_bias);
+        free(l->fc1_weight); free(l->fc1_bias); free(l->fc2_weight); free(l->fc2_bias);
+        free(l->ffn_norm_weight); free(l->ffn_norm_bias);
+    }
+    free(enc->ln_post_weight); free(enc->ln_post_bias);
+    free(enc->proj1_weight); free(enc->proj1_bias); free(enc->proj2_weight); free(enc->proj2_bias);
+    free(h->ctx); free(h->ms); free(h->sf); free(h);
 }

@@ -345,12 +345,12 @@ class Streams:
             raise _err("qdb_streams_create")
 
     def chunk(self, audio, is_final):
-        """audio: list of float32 [rows, hidden] arrays (None or 0 rows = no
-        encoder output this chunk); is_final: list of bools. Returns
-        (n_emitted, reset) int arrays."""
+        """audio: list of float32 [rows, hidden] arrays (0 rows = no encoder
+        output this chunk, None = stream not in this call); is_final: list of
+        bools. Returns (n_emitted, reset) int arrays."""
         arrs = [None if a is None else np.ascontiguousarray(a, dtype=np.float32) for a in audio]
         ptrs = (ctypes.c_void_p * self.n)(*[a.ctypes.data if a is not None and a.size else None for a in arrs])
-        lens = np.array([0 if a is None else (a.shape[0] if a.size else 0) for a in arrs], np.int32)
+        lens = np.array([-1 if a is None else (a.shape[0] if a.size else 0) for a in arrs], np.int32)
         fin = np.ascontiguousarray(is_final, dtype=np.int32)
         ne = np.zeros(self.n, np.int32)
         rs = np.zeros(self.n, np.int32)

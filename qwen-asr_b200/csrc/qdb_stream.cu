@@ -29,6 +29,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <thread>
 #include <vector>
 
 #include "../../include/qwen_asr_b200.h"
@@ -122,6 +123,26 @@ struct qdb_streams {
 };
 
 namespace {
+
+// Runs fn(j) for j in [0, n) on up to 16 host threads (the per-stream host
+// work of a chunk: prefix comparison and the copies of audio rows, about a
+// megabyte per stream, is independent across streams).
+template <typename F>
+void parallel_for(int n, F fn) {
+    const int hw = (int)std::max(1u, std::thread::hardware_concurrency());
+    const int T = std::min({16, hw, (n + 7) / 8});
+    if (T <= 1) {
+        for (int j = 0; j < n; j++) fn(j);
+        return;
+    }
+    std::vector<std::thread> th;
+    th.reserve(T);
+    for (int t = 0; t < T; t++)
+        th.emplace_back([&, t] {
+            for (int j = t; j < n; j += T) fn(j);
+        });
+    for (auto &x : th) x.join();
+}
 
 template <typename T>
 int grow_dev(T **p, size_t *cap, size_t need) {
@@ -340,16 +361,14 @@ extern "C" int qdb_streams_chunk(qdb_streams *S, const float *const *audio, cons
     const int n = (int)S->st.size(), h = S->info.hidden;
     const qdb_stream_config &c = S->cfg;
     if (cudaSetDevice(S->info.device) != cudaSuccess) return qdb_set_error("qdb_streams_chunk: cudaSetDevice failed");
-    // ---- prompts, prefix reuse, deltas (host)
+    // ---- prompts (host, serial: small integer work and validation)
     std::vector<int> act;  // streams with audio this chunk
-    std::vector<qdb_session *> pf_sess;
-    std::vector<int> pf_len, pf_start, all_desc;
-    size_t up_rows = 0;
     for (int i = 0; i < n; i++) {
         Stream &s = S->st[i];
         if (n_emitted) n_emitted[i] = 0;
         if (reset) reset[i] = 0;
-        if (audio_len[i] <= 0) {  // no encoder output: the chunk is skipped (qwen_asr.c:1649-1654)
+        if (audio_len[i] < 0) continue;  // not part of this call
+        if (audio_len[i] == 0) {  // no encoder output: the chunk is skipped (qwen_asr.c:1649-1654)
             s.chunk_idx++;
             continue;
         }
@@ -373,14 +392,16 @@ extern "C" int qdb_streams_chunk(qdb_streams *S, const float *const *audio, cons
         s.desc.insert(s.desc.end(), s.raw.begin() + off, s.raw.begin() + off + n_pref);
         for (int k = off; k < off + n_pref; k++)
             if (s.raw[k] < 0 || s.raw[k] >= S->info.vocab) return qdb_set_error("qdb_streams_chunk: token out of range");
-        const int total = (int)s.desc.size();
-        s.prefill_len = total - 1;
+        s.prefill_len = (int)s.desc.size() - 1;
         s.audio_rows = audio_len[i];
-        // longest unchanged prefix of the previous prefill (qwen_asr.c:1750-1762)
+    }
+    // ---- longest unchanged prefix of the previous prefill (qwen_asr.c:1750-1762), per stream in parallel
+    parallel_for((int)act.size(), [&](int j) {
+        Stream &s = S->st[act[j]];
         int reused = 0;
         if (s.prev_len > 0) {
             const int cmp = std::min(s.prefill_len, s.prev_len);
-            const float *a_new = audio[i];
+            const float *a_new = audio[act[j]];
             while (reused < cmp) {
                 const int dn = s.desc[reused], dp = s.prev_desc[reused];
                 bool same;
@@ -394,23 +415,27 @@ extern "C" int qdb_streams_chunk(qdb_streams *S, const float *const *audio, cons
             }
         }
         s.reused = reused;
-        const int delta = s.prefill_len - reused;
+    });
+    // ---- deltas: KV capacity, row descriptors, staging offsets (serial)
+    std::vector<qdb_session *> pf_sess;
+    std::vector<int> pf_len, pf_start, all_desc;
+    std::vector<size_t> stage_off(act.size(), 0);
+    size_t up_rows = 0;
+    for (size_t j = 0; j < act.size(); j++) {
+        Stream &s = S->st[act[j]];
         if (qdb_session_reserve(s.sess, s.prefill_len + c.max_new_tokens + 1)) return -1;
-        if (delta > 0) {
+        stage_off[j] = up_rows;
+        if (s.prefill_len > s.reused) {
             pf_sess.push_back(s.sess);
-            pf_len.push_back(delta);
-            pf_start.push_back(reused);
-            for (int r = reused; r < s.prefill_len; r++) {
+            pf_len.push_back(s.prefill_len - s.reused);
+            pf_start.push_back(s.reused);
+            for (int r = s.reused; r < s.prefill_len; r++) {
                 const int d = s.desc[r];
-                if (d >= 0) {
-                    all_desc.push_back(d);
-                } else {
-                    all_desc.push_back(-(int)(++up_rows));  // staged audio row up_rows - 1
-                }
+                all_desc.push_back(d >= 0 ? d : -(int)(++up_rows));  // staged audio row up_rows - 1
             }
         }
         s.prefill_total += s.prefill_len;
-        s.prefill_reused += reused;
+        s.prefill_reused += s.reused;
     }
     S->last_ms[0] = S->last_ms[1] = 0.f;
     S->last_rows = (int)all_desc.size();
@@ -432,12 +457,13 @@ extern "C" int qdb_streams_chunk(qdb_streams *S, const float *const *audio, cons
                 return qdb_set_error("qdb_streams_chunk: out of pinned host memory");
             S->h_audio_cap = cap;
         }
-        size_t k = 0;
-        for (int i : act) {
-            Stream &s = S->st[i];
+        parallel_for((int)act.size(), [&](int j) {
+            const Stream &s = S->st[act[j]];
+            size_t k = stage_off[j];
             for (int r = s.reused; r < s.prefill_len; r++)
-                if (s.desc[r] < 0) memcpy(S->h_audio + (k++) * h, audio[i] + (size_t)(-s.desc[r] - 1) * h, sizeof(float) * h);
-        }
+                if (s.desc[r] < 0)
+                    memcpy(S->h_audio + (k++) * h, audio[act[j]] + (size_t)(-s.desc[r] - 1) * h, sizeof(float) * h);
+        });
         if (grow_dev(&S->d_desc, &S->desc_cap, all_desc.size()) ||
             grow_dev(&S->d_audio, &S->audio_cap, std::max<size_t>(up_rows * h, 1)) ||
             grow_dev(&S->d_rows, &S->rows_cap, all_desc.size() * h))
@@ -471,10 +497,10 @@ extern "C" int qdb_streams_chunk(qdb_streams *S, const float *const *audio, cons
         cudaEventElapsedTime(&S->last_ms[1], S->ev[1], S->ev[2]);
     }
     // ---- bookkeeping
-    std::vector<int> gen(steps);
-    for (int j = 0; j < na; j++) {
+    parallel_for(na, [&](int j) {
         const int i = act[j];
         Stream &s = S->st[i];
+        std::vector<int> gen(steps);
         for (int t = 0; t < steps; t++) gen[t] = S->h_tokens[(size_t)t * na + j];
         // keep this prompt for the next chunk's prefix comparison
         s.prev_desc.assign(s.desc.begin(), s.desc.begin() + s.prefill_len);
@@ -486,7 +512,7 @@ extern "C" int qdb_streams_chunk(qdb_streams *S, const float *const *audio, cons
         if (n_emitted) n_emitted[i] = s.last_emitted;
         if (reset) reset[i] = s.last_reset;
         s.chunk_idx++;
-    }
+    });
     return 0;
 }
 

@@ -285,3 +285,119 @@ class SyntheticEncoder:
     def clear(self):
         self.cache = []
         self.next_window = int(self.cursor / self.window) * self.window
+
+
+# ---------------------------------------------------------------- audio encoder
+CONV_HIDDEN = 480  # QWEN_CONV_HIDDEN (qwen_asr.h:39)
+
+
+@dataclasses.dataclass(frozen=True)
+class EncoderConfig:
+    d_model: int
+    layers: int
+    heads: int
+    head_dim: int
+    ffn: int
+    output_dim: int
+
+    def as_tuple(self):
+        return (self.d_model, self.layers, self.heads, self.head_dim, self.ffn, self.output_dim)
+
+
+# encoder shapes (qwen_asr.h:48-53); the small ones feed the small decoder presets
+ENC_PRESETS = {
+    "0.6b": EncoderConfig(896, 18, 14, 64, 3584, 1024),
+    "1.7b": EncoderConfig(1024, 24, 16, 64, 4096, 2048),
+    "tiny": EncoderConfig(128, 2, 2, 64, 256, 256),
+    "small": EncoderConfig(256, 2, 4, 64, 512, 512),
+}
+
+
+def encoder_tensor_specs(ec: EncoderConfig):
+    """(name, shape) of every encoder tensor, reference naming (qwen_asr_encoder.c:66-168)."""
+    p = "thinker.audio_tower."
+    d = ec.d_model
+    specs = [(p + "conv2d1.weight", (CONV_HIDDEN, 1, 3, 3)), (p + "conv2d1.bias", (CONV_HIDDEN,)),
+             (p + "conv2d2.weight", (CONV_HIDDEN, CONV_HIDDEN, 3, 3)), (p + "conv2d2.bias", (CONV_HIDDEN,)),
+             (p + "conv2d3.weight", (CONV_HIDDEN, CONV_HIDDEN, 3, 3)), (p + "conv2d3.bias", (CONV_HIDDEN,)),
+             (p + "conv_out.weight", (d, CONV_HIDDEN * 16))]
+    for i in range(ec.layers):
+        q = f"{p}layers.{i}."
+        specs += [(q + "self_attn.q_proj.weight", (d, d)), (q + "self_attn.q_proj.bias", (d,)),
+                  (q + "self_attn.k_proj.weight", (d, d)), (q + "self_attn.k_proj.bias", (d,)),
+                  (q + "self_attn.v_proj.weight", (d, d)), (q + "self_attn.v_proj.bias", (d,)),
+                  (q + "self_attn.out_proj.weight", (d, d)), (q + "self_attn.out_proj.bias", (d,)),
+                  (q + "self_attn_layer_norm.weight", (d,)), (q + "self_attn_layer_norm.bias", (d,)),
+                  (q + "fc1.weight", (ec.ffn, d)), (q + "fc1.bias", (ec.ffn,)),
+                  (q + "fc2.weight", (d, ec.ffn)), (q + "fc2.bias", (d,)),
+                  (q + "final_layer_norm.weight", (d,)), (q + "final_layer_norm.bias", (d,))]
+    specs += [(p + "ln_post.weight", (d,)), (p + "ln_post.bias", (d,)),
+              (p + "proj1.weight", (d, d)), (p + "proj1.bias", (d,)),
+              (p + "proj2.weight", (ec.output_dim, d)), (p + "proj2.bias", (ec.output_dim,))]
+    return specs
+
+
+class EncoderWeightSet:
+    """All encoder tensors of one synthetic model in one bf16 host blob:
+    matrices, conv kernels and biases N(0, std) (std 0.02 by default), LayerNorm
+    weights 1 and biases 0 (plus optional jitter). `scale_by_fan_in` draws
+    matrices and conv kernels with std 1/sqrt(fan_in) instead, which keeps
+    activations O(1) through the stack (parity tests use it so that every
+    stage contributes)."""
+
+    def __init__(self, ec: EncoderConfig, seed: int = 0, std: float = 0.02, norm_jitter: float = 0.0,
+                 scale_by_fan_in: bool = False):
+        import torch
+
+        self.cfg = ec
+        self.specs = encoder_tensor_specs(ec)
+        self.offsets, self.shapes = {}, {}
+        off = 0
+        for name, shape in self.specs:
+            n = int(np.prod(shape))
+            self.offsets[name] = off
+            self.shapes[name] = shape
+            off += (n + 127) // 128 * 128
+        self.blob = np.empty(off, dtype=np.uint16)
+        g = torch.Generator().manual_seed(seed)
+        for name, shape in self.specs:
+            if "norm" in name or "ln_post" in name:
+                base = torch.ones(shape) if name.endswith("weight") else torch.zeros(shape)
+                t = base + (norm_jitter * torch.randn(shape, generator=g) if norm_jitter else 0)
+            elif name.endswith("bias"):
+                t = torch.randn(shape, generator=g) * std
+            else:
+                fan_in = int(np.prod(shape[1:]))
+                s = 1.0 / np.sqrt(fan_in) if scale_by_fan_in else std
+                t = torch.randn(shape, generator=g) * s
+            self.view(name)[...] = t.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16).reshape(shape)
+
+    def view(self, name):
+        off = self.offsets[name]
+        shape = self.shapes[name]
+        return self.blob[off:off + int(np.prod(shape))].reshape(shape)
+
+    def f32(self, name):
+        return bf16_to_f32(self.view(name))
+
+    def table(self):
+        """(names, byte offsets, byte sizes, shapes flattened to 2-D) for the reference loader."""
+        names, offs, sizes, shapes = [], [], [], []
+        for name, s in self.specs:
+            names.append(name)
+            offs.append(self.offsets[name] * 2)
+            sizes.append(int(np.prod(s)) * 2)
+            shapes.append((s[0], int(np.prod(s[1:])) if len(s) > 1 else 0))
+        return names, offs, sizes, shapes
+
+
+def encoder_tokens(mel_frames: int, chunk: int = 100) -> int:
+    """Encoder output rows for mel_frames (qwen_asr_encoder.c:186-211): per
+    100-frame chunk, three stride-2 convolutions."""
+    n = 0
+    for c0 in range(0, mel_frames, chunk):
+        w = min(chunk, mel_frames - c0)
+        for _ in range(3):
+            w = (w - 1) // 2 + 1
+        n += w
+    return n

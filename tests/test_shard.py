@@ -62,8 +62,9 @@ def _worker(rank, world, port, mode, q):
             os._exit(3)          # leaves between steps, before the timing collective
         first, cnt = shard.shard_range(64, world, rank)
         vals = shard.max_over_ranks([10.0 + rank, 5.0 - rank, float(cnt)])
+        sums = shard.sum_over_ranks([float(cnt), 1.0])
         dist.barrier()
-        q.put((rank, ("ok", first, cnt, vals)))
+        q.put((rank, ("ok", first, cnt, vals + sums)))
         dist.destroy_process_group()
     except Exception as e:  # noqa: BLE001 - reported to the parent
         q.put((rank, ("error", type(e).__name__)))
@@ -93,7 +94,7 @@ def test_gloo_two_ranks_max_and_placement():
     for r in range(2):
         tag, first, cnt, vals = out[r]
         assert tag == "ok" and (first, cnt) == (32 * r, 32)
-        assert vals == [11.0, 5.0, 32.0]   # every rank sees the slowest rank's time
+        assert vals == [11.0, 5.0, 32.0, 64.0, 2.0]   # the slowest rank's time; whole-job counts
 
 
 def test_gloo_rank_failure_detected_by_survivor():

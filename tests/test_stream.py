@@ -279,9 +279,15 @@ def test_streams_skip_chunk_and_config_errors(pkg, ws):
     S = pkg.Streams(model, 2, max_new_tokens=4, **template())
     e = synth.SyntheticEncoder(CFG.hidden, 1)
     a, _ = e.advance(4.0)
-    ne, rs = S.chunk([a, None], [False, False])  # stream 1 has no encoder output: skipped
+    empty = np.zeros((0, CFG.hidden), np.float32)
+    ne, rs = S.chunk([a, empty], [False, False])  # stream 1 has no encoder output: the chunk is skipped
     assert S.stats(1)["chunk_idx"] == 1 and S.stats(1)["chunks"] == 0
     assert S.stats(0)["chunks"] == 1 and S.stats(0)["last_generated"] == 4
+    ne, rs = S.chunk([None, a], [False, False])  # stream 0 not in this call: untouched
+    assert S.stats(0)["chunk_idx"] == 1 and S.stats(1)["chunk_idx"] == 2 and S.stats(1)["chunks"] == 1
+    S.reset(1)
+    assert S.stats(1)["chunk_idx"] == 0 and len(S.tokens(1, "raw")) == 0
+    assert S.last_chunk()["active"] == 1
     S.close()
     with pytest.raises(pkg.QdbError):
         pkg.Streams(model, 2)  # the reference's template ids exceed the tiny vocabulary
