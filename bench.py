@@ -293,6 +293,131 @@ def measure(pkg, synth, cfg_name, world, rank, local, steps, warmup, clocks=None
                 e2e_steps=e2e_steps, h2d=h2d, d2h=d2h, clk=clk, wall=wall, setup_s=setup_s)
 
 
+def measure_pipeline(pkg, synth, cfg_name, first, n_local, local, steps, warmup=1):
+    """Whole offline pipeline on the GPU for this rank's utterances of cfg_name:
+    PCM (pinned host) -> log-mel (qdb_mel) -> encoder (qdb_encoder) -> prompt rows
+    (qdb_build_prompt_device) -> one batched prefill -> greedy decode, tokens back
+    to the host. Returns per-stage device ms per step and the step total."""
+    import torch
+
+    preset, seconds, n_dec, n_utt = CONFIGS[cfg_name]
+    cfg, ecfg = synth.PRESETS[preset], synth.ENC_PRESETS[preset]
+    ws = synth.WeightSet(cfg, seed=0)
+    ews = synth.EncoderWeightSet(ecfg, seed=0)
+    model = pkg.Model(ws, device=local, mask_eos=True)
+    enc = pkg.Encoder(ews, device=local)
+    dev = torch.device("cuda", local)
+    seeds = [utterance_seed(cfg_name, u) for u in range(first, first + n_local)]
+    freqs = [synth.bench_tone_hz(sd) if n_utt > 1 else 440.0 for sd in seeds]
+    pcm = [torch.from_numpy(synth.bench_pcm(seconds, sd, f)).pin_memory() for sd, f in zip(seeds, freqs)]
+    ns = [p.numel() for p in pcm]
+    frames = [pkg.mel_frames(n) for n in ns]
+    toks = [pkg.Encoder.tokens(f) for f in frames]
+    samples_dev = torch.empty(sum(ns), dtype=torch.float32, device=dev)
+    mel_dev = torch.empty(128 * sum(frames), dtype=torch.float32, device=dev)
+    audio_dev = torch.empty((sum(toks), cfg.hidden), dtype=torch.float32, device=dev)
+    pre = [t % cfg.vocab for t in synth.PROMPT_PREFIX]
+    suf = [t % cfg.vocab for t in synth.PROMPT_SUFFIX]
+    desc, lens, a0 = [], [], 0
+    for t in toks:
+        rows = pre + [-(a0 + r + 1) for r in range(t)] + suf
+        desc += rows[:-1]  # the prefill takes all rows but the last (a token, fed to the first step)
+        lens.append(len(rows) - 1)
+        a0 += t
+    emb_dev = torch.empty((len(desc), cfg.hidden), dtype=torch.float32, device=dev)
+    sessions = [model.session(max(lens) + n_dec + 8) for _ in range(n_local)]
+    es = torch.cuda.ExternalStream(enc.stream_handle, device=dev)
+    ms_ = torch.cuda.ExternalStream(model.stream_handle, device=dev)
+
+    def step(rec):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        ev[0].record(es)
+        so = 0
+        with torch.cuda.stream(es):
+            for p, n in zip(pcm, ns):
+                samples_dev[so:so + n].copy_(p, non_blocking=True)
+                so += n
+        ev[1].record(es)
+        so = mo = 0
+        for n, f in zip(ns, frames):
+            pkg.mel_spectrogram_device(samples_dev.data_ptr() + 4 * so, n, mel_dev.data_ptr() + 4 * mo,
+                                       enc.stream_handle)
+            so += n
+            mo += 128 * f
+        ev[2].record(es)
+        mo = ao = 0
+        for f, t in zip(frames, toks):
+            enc.forward_device(mel_dev.data_ptr() + 4 * mo, f, audio_dev.data_ptr() + 4 * ao * cfg.hidden)
+            mo += 128 * f
+            ao += t
+        ev[3].record(es)
+        ms_.wait_event(ev[3])
+        model.build_prompt_device(desc, audio_dev.data_ptr(), emb_dev.data_ptr())
+        if n_local == 1:
+            sessions[0].prefill_device(emb_dev.data_ptr(), lens[0], 0)
+        else:
+            pkg.prefill_batch_device(sessions, emb_dev.data_ptr(), lens, [0] * n_local)
+        ev[4].record(ms_)
+        if n_local == 1:
+            out = sessions[0].decode_greedy(suf[-1], lens[0], n_dec)
+        else:
+            out = pkg.decode_greedy_batch(sessions, [suf[-1]] * n_local, lens, n_dec)
+        ev[5].record(ms_)
+        if rec is not None:
+            rec.append(ev)
+        return out
+
+    for _ in range(warmup):
+        step(None)
+    torch.cuda.synchronize()
+    rec = []
+    for _ in range(steps):
+        step(rec)
+    torch.cuda.synchronize()
+    names = ("h2d", "mel", "encoder", "prompt+prefill", "decode")
+    stage = {k: sum(r[i].elapsed_time(r[i + 1]) for r in rec) / steps for i, k in enumerate(names)}
+    total = sum(r[0].elapsed_time(r[5]) for r in rec) / steps
+    for s_ in sessions:
+        s_.close()
+    enc.close()
+    model.close()
+    return {"stage_ms": {k: round(v, 3) for k, v in stage.items()}, "total_ms": total,
+            "audio_s": seconds * n_local, "tokens": n_dec * n_local, "encoder_tokens": sum(toks),
+            "ews": ews, "mel_frames": frames[0]}
+
+
+def cpu_pipeline_sample(synth, ws, ews, cfg_name, dec_tok_s):
+    """The reference's CPU stages for one utterance of cfg_name on this host:
+    qwen_mel_spectrogram and qwen_encoder_forward (oracle/_ref), prefill, and
+    the greedy decode at the per-token rate measured by the CPU baseline."""
+    from oracle.pyoracle import RefDecoder, RefEncoder, ref_mel_spectrogram
+    preset, seconds, n_dec, n_utt = CONFIGS[cfg_name]
+    th = ref_threads()
+    sd = utterance_seed(cfg_name, 0)
+    x = synth.bench_pcm(seconds, sd, synth.bench_tone_hz(sd) if n_utt > 1 else 440.0)
+    t0 = time.perf_counter()
+    mel = ref_mel_spectrogram(x)
+    t1 = time.perf_counter()
+    re_ = RefEncoder(ews, threads=th)
+    t2 = time.perf_counter()
+    audio = re_.forward(mel)
+    t3 = time.perf_counter()
+    re_.close()
+    emb = synth.prompt_embeddings(ws, audio)
+    rd = RefDecoder(ws, threads=th)
+    t4 = time.perf_counter()
+    rd.prefill(emb[:-1])
+    t5 = time.perf_counter()
+    rd.close()
+    dec_s = n_dec / dec_tok_s
+    total = (t1 - t0) + (t3 - t2) + (t5 - t4) + dec_s
+    return {"stage_s": {"mel": round(t1 - t0, 3), "encoder": round(t3 - t2, 3), "prefill": round(t5 - t4, 3),
+                        "decode": round(dec_s, 3)},
+            "x_realtime": round(seconds / total, 3), "cores": th, "kind": "reference",
+            "sample": f"one utterance ({seconds:g} s): reference mel, encoder and prefill timed once; decode = "
+                      f"{n_dec} tokens at the CPU baseline's measured {dec_tok_s:.2f} tok/s"}
+
+
 def summarize(m, cfg_name, world, steps):
     """Rates and roofline of one measure() result whose times are already the
     max over ranks."""
@@ -385,8 +510,25 @@ def run_ours(args):
                         "prefill_ms": round(mb["pre_ms"] / min(steps, 5), 3),
                         "steps": min(steps, 5), "workload": config_block(name, 1, 1, mb["P"])["workload"]}
         result["b1"] = b1
+    if not args.no_pipeline:
+        first, n_local_p = shard.shard_range(n_utt, world, rank) if n_utt > 1 else (0, 1)
+        pl = measure_pipeline(pkg, synth, args.config, first, n_local_p, local, min(steps, 3))
+        tot = shard.max_over_ranks([pl["total_ms"]] + list(pl["stage_ms"].values()), device=f"cuda:{local}")
+        audio_all = seconds * (n_utt if n_utt > 1 else world)
+        result["pipeline"] = {
+            "x_realtime": round(audio_all / (tot[0] / 1e3), 2),
+            "tok_s": round((m["n_dec"] * (n_utt if n_utt > 1 else world)) / (tot[0] / 1e3), 2),
+            "ms_per_step": round(tot[0], 3),
+            "stage_ms": dict(zip(pl["stage_ms"].keys(), [round(v, 3) for v in tot[1:]])),
+            "path": "pinned PCM -> qdb_mel_spectrogram_device -> qdb_encoder_forward_device -> "
+                    "qdb_build_prompt_device -> batched prefill -> device greedy loop -> tokens on the host",
+            "stages_on_gpu": "all (mel, encoder, prefill, decode)",
+            "encoder_tokens_per_step": pl["encoder_tokens"]}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(synth, m["ws"], m["embs"][0], args.config)
+        if "pipeline" in result:
+            result["cpu_baseline"]["pipeline"] = cpu_pipeline_sample(
+                synth, m["ws"], pl["ews"], args.config, result["cpu_baseline"]["value"])
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
@@ -798,6 +940,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-b1", action="store_true", help="skip the in-line batch-1 (c0, c1) measurements")
+    ap.add_argument("--no-pipeline", action="store_true", help="skip the audio -> tokens pipeline measurement")
     ap.add_argument("--profile-step", action="store_true", help="small fixed case for ncu (no timing)")
     ap.add_argument("--profile-batch", action="store_true", help="batched-decode case for ncu (no timing)")
     args = ap.parse_args()

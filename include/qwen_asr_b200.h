@@ -281,6 +281,61 @@ int qdb_streams_reset(qdb_streams *s, int stream);
  * ran, counts[1] prompt rows prefilled. Either pointer may be NULL. 0 = ok. */
 int qdb_streams_last_chunk(const qdb_streams *s, float *ms, int *counts);
 
+/* Prompt rows on the device (the offline path's input embeddings,
+ * qwen_asr.c:626-700): desc[r] >= 0 is a token id (its embedding row),
+ * desc[r] < 0 is row -(desc[r] + 1) of audio_dev [*, hidden] (the encoder
+ * output); out_dev [n_rows, hidden] f32. Enqueued on the model's stream;
+ * desc is host memory and may be reused on return. 0 = ok. */
+int qdb_build_prompt_device(qdb_model *m, const int *desc, int n_rows, const float *audio_dev, float *out_dev);
+
+/* ---- Audio encoder, replaces qwen_encoder_load / qwen_encoder_forward
+ * (qwen_asr_encoder.c:66-168, :171-372). Conv2D stem per 100-frame chunk,
+ * transformer layers with windowed bidirectional attention, projection to the
+ * decoder width, all on the GPU. ---- */
+typedef struct qdb_encoder qdb_encoder;
+
+typedef struct {
+    int d_model, layers, heads, head_dim, ffn_dim, output_dim; /* qwen_config_t enc_* (qwen_asr.h:48-53) */
+} qdb_encoder_config;
+
+/* Empty encoder on `device` (head_dim 64, heads * 64 = d_model, d_model and
+ * ffn_dim multiples of 64). NULL on error. */
+qdb_encoder *qdb_encoder_create(const qdb_encoder_config *cfg, int device);
+void qdb_encoder_free(qdb_encoder *e);
+
+/* Weights in the reference loader's forms: conv kernels and all biases /
+ * norms f32 (load_f32), matrices bf16 (load_bf16_as_f32's source).
+ * conv1 [480, 1, 3, 3], conv2 / conv3 [480, 480, 3, 3], biases [480];
+ * conv_out [d_model, 7680]. */
+int qdb_encoder_set_stem(qdb_encoder *e, const float *conv1_w, const float *conv1_b, const float *conv2_w,
+                         const float *conv2_b, const float *conv3_w, const float *conv3_b,
+                         const uint16_t *conv_out_w);
+/* Layer i: q/k/v/out [d, d] + biases, attention LayerNorm, fc1 [ffn, d],
+ * fc2 [d, ffn] + biases, FFN LayerNorm. */
+int qdb_encoder_set_layer(qdb_encoder *e, int i, const uint16_t *wq, const float *bq, const uint16_t *wk,
+                          const float *bk, const uint16_t *wv, const float *bv, const uint16_t *wo, const float *bo,
+                          const float *ln1_w, const float *ln1_b, const uint16_t *fc1_w, const float *fc1_b,
+                          const uint16_t *fc2_w, const float *fc2_b, const float *ln2_w, const float *ln2_b);
+/* ln_post, proj1 [d, d], proj2 [output_dim, d] with biases. */
+int qdb_encoder_set_post(qdb_encoder *e, const float *ln_w, const float *ln_b, const uint16_t *proj1_w,
+                         const float *proj1_b, const uint16_t *proj2_w, const float *proj2_b);
+/* Checks every weight was set. */
+int qdb_encoder_finalize(qdb_encoder *e);
+
+/* Output rows for mel_frames (13 per full 100-frame chunk). */
+int qdb_encoder_tokens(int mel_frames);
+
+/* Same contract as qwen_encoder_forward: host mel [128, mel_frames] ->
+ * malloc'd host [tokens, output_dim] (caller frees), token count in
+ * *out_seq_len; NULL on error. Synchronous. */
+float *qdb_encoder_forward(qdb_encoder *e, const float *mel, int mel_frames, int *out_seq_len);
+
+/* Device form on the encoder's stream (qdb_encoder_stream): mel_dev
+ * [128, mel_frames] -> out_dev [qdb_encoder_tokens(mel_frames), output_dim].
+ * Returns the token count, or -1. */
+int qdb_encoder_forward_device(qdb_encoder *e, const float *mel_dev, int mel_frames, float *out_dev);
+void *qdb_encoder_stream(qdb_encoder *e);
+
 /* ---- Log-mel front end, replaces qwen_mel_spectrogram (qwen_asr_audio.c:293-390,
  * declared at qwen_asr_audio.h:32). 16 kHz mono f32 samples -> [128, n_frames]
  * f32 log-mel (reflect pad 200, periodic Hann 400, 201-bin DFT power, hop 160

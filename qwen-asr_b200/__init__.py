@@ -64,6 +64,19 @@ ABI = {
                                                ctypes.c_int, _i32p]),
     "qdb_model_sync": (ctypes.c_int, [ctypes.c_void_p]),
     "qdb_mel_frames": (ctypes.c_int, [ctypes.c_int]),
+    "qdb_build_prompt_device": (ctypes.c_int, [ctypes.c_void_p, _i32p, ctypes.c_int, ctypes.c_void_p,
+                                               ctypes.c_void_p]),
+    "qdb_encoder_create": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int]),
+    "qdb_encoder_free": (None, [ctypes.c_void_p]),
+    "qdb_encoder_set_stem": (ctypes.c_int, [ctypes.c_void_p] + [_f32p] * 6 + [_u16p]),
+    "qdb_encoder_set_layer": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int] + [_u16p, _f32p] * 4 + [_f32p, _f32p]
+                              + [_u16p, _f32p] * 2 + [_f32p, _f32p]),
+    "qdb_encoder_set_post": (ctypes.c_int, [ctypes.c_void_p, _f32p, _f32p, _u16p, _f32p, _u16p, _f32p]),
+    "qdb_encoder_finalize": (ctypes.c_int, [ctypes.c_void_p]),
+    "qdb_encoder_tokens": (ctypes.c_int, [ctypes.c_int]),
+    "qdb_encoder_forward": (ctypes.POINTER(ctypes.c_float), [ctypes.c_void_p, _f32p, ctypes.c_int, _i32p]),
+    "qdb_encoder_forward_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
+    "qdb_encoder_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
     "qdb_streams_create": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "qdb_streams_free": (None, [ctypes.c_void_p]),
     "qdb_streams_chunk": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), _i32p, _i32p, _i32p,
@@ -162,6 +175,14 @@ class Model:
     def stream_handle(self) -> int:
         """cudaStream_t of this model (for torch.cuda.ExternalStream)."""
         return lib.qdb_model_stream(self.h) or 0
+
+    def build_prompt_device(self, desc, audio_ptr: int, out_ptr: int):
+        """Prompt rows on the device: desc[r] >= 0 token id, < 0 audio row -(desc[r]+1)
+        of audio_ptr [*, hidden]; out_ptr [len(desc), hidden] f32 (model's stream)."""
+        d = np.ascontiguousarray(desc, dtype=np.int32)
+        if lib.qdb_build_prompt_device(self.h, _ptr(d, _i32p), len(d), ctypes.c_void_p(audio_ptr),
+                                       ctypes.c_void_p(out_ptr)):
+            raise _err("qdb_build_prompt_device")
 
     def session(self, capacity: int = 1024) -> "Session":
         return Session(self, capacity)
@@ -391,6 +412,88 @@ class Streams:
     def close(self):
         if self.h and not _exiting[0]:
             lib.qdb_streams_free(self.h)
+        self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class QdbEncoderConfig(ctypes.Structure):
+    _fields_ = [(k, ctypes.c_int) for k in ("d_model", "layers", "heads", "head_dim", "ffn_dim", "output_dim")]
+
+
+class Encoder:
+    """Device copy of the audio encoder (replaces qwen_encoder_load,
+    qwen_asr_encoder.c:66-168). `weights` is a synth.EncoderWeightSet or any
+    object with .cfg (d_model, layers, heads, head_dim, ffn, output_dim) and
+    .view(name) / .f32(name) over the reference's tensor names."""
+
+    def __init__(self, weights, device: int = 0):
+        ec = weights.cfg
+        self.cfg = ec
+        c = QdbEncoderConfig(ec.d_model, ec.layers, ec.heads, ec.head_dim, ec.ffn, ec.output_dim)
+        self.h = lib.qdb_encoder_create(ctypes.byref(c), device)
+        if not self.h:
+            raise _err("qdb_encoder_create")
+        p = "thinker.audio_tower."
+        f = lambda n: np.ascontiguousarray(weights.f32(p + n), dtype=np.float32)
+        u = lambda n: np.ascontiguousarray(weights.view(p + n))
+        stem = [f("conv2d1.weight"), f("conv2d1.bias"), f("conv2d2.weight"), f("conv2d2.bias"),
+                f("conv2d3.weight"), f("conv2d3.bias")]
+        cout = u("conv_out.weight")
+        if lib.qdb_encoder_set_stem(self.h, *[_ptr(a, _f32p) for a in stem], _ptr(cout, _u16p)):
+            raise _err("qdb_encoder_set_stem")
+        for i in range(ec.layers):
+            q = f"layers.{i}."
+            args = []
+            for nm in ("q_proj", "k_proj", "v_proj", "out_proj"):
+                args += [u(q + f"self_attn.{nm}.weight"), f(q + f"self_attn.{nm}.bias")]
+            args += [f(q + "self_attn_layer_norm.weight"), f(q + "self_attn_layer_norm.bias")]
+            args += [u(q + "fc1.weight"), f(q + "fc1.bias"), u(q + "fc2.weight"), f(q + "fc2.bias")]
+            args += [f(q + "final_layer_norm.weight"), f(q + "final_layer_norm.bias")]
+            ptrs = [_ptr(a, _u16p if a.dtype == np.uint16 else _f32p) for a in args]
+            if lib.qdb_encoder_set_layer(self.h, i, *ptrs):
+                raise _err(f"qdb_encoder_set_layer({i})")
+        post = [f("ln_post.weight"), f("ln_post.bias"), u("proj1.weight"), f("proj1.bias"), u("proj2.weight"),
+                f("proj2.bias")]
+        if lib.qdb_encoder_set_post(self.h, *[_ptr(a, _u16p if a.dtype == np.uint16 else _f32p) for a in post]):
+            raise _err("qdb_encoder_set_post")
+        if lib.qdb_encoder_finalize(self.h):
+            raise _err("qdb_encoder_finalize")
+
+    @staticmethod
+    def tokens(mel_frames: int) -> int:
+        return lib.qdb_encoder_tokens(int(mel_frames))
+
+    def forward(self, mel: np.ndarray) -> np.ndarray:
+        """Mirror of qwen_encoder_forward: mel [128, frames] -> [tokens, output_dim]."""
+        m = np.ascontiguousarray(mel, dtype=np.float32)
+        n = ctypes.c_int(0)
+        p = lib.qdb_encoder_forward(self.h, _ptr(m, _f32p), m.shape[1], ctypes.byref(n))
+        if not p:
+            raise _err("qdb_encoder_forward")
+        try:
+            return np.ctypeslib.as_array(p, (n.value, self.cfg.output_dim)).copy()
+        finally:
+            _libc.free(ctypes.cast(p, ctypes.c_void_p))
+
+    def forward_device(self, mel_ptr: int, frames: int, out_ptr: int) -> int:
+        """Device form on the encoder's stream; returns the token count."""
+        n = lib.qdb_encoder_forward_device(self.h, ctypes.c_void_p(mel_ptr), int(frames), ctypes.c_void_p(out_ptr))
+        if n < 0:
+            raise _err("qdb_encoder_forward_device")
+        return n
+
+    @property
+    def stream_handle(self) -> int:
+        return lib.qdb_encoder_stream(self.h) or 0
+
+    def close(self):
+        if self.h and not _exiting[0]:
+            lib.qdb_encoder_free(self.h)
         self.h = None
 
     def __del__(self):

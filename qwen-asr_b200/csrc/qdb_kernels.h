@@ -182,6 +182,10 @@ cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh, const uint
                                int mode, int splits, int *err, cudaStream_t st);
 cudaError_t qdb_launch_swiglu_split(const float *gu, uint16_t *hi, uint16_t *lo, size_t count, cudaStream_t st);
 int qdb_gemm_tc_splits(int n, int N, int K, int sms);
+// Same with an optional f32 bias [N] added to every output (once, also under split-K).
+extern "C" cudaError_t qdb_launch_gemm_tc_bias(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y,
+                                               int n, int N, int K, int mode, int splits, int *err, cudaStream_t st,
+                                               const float *bias);
 // Bound (cycles) on the tensor-core GEMMs' data waits, current device.
 cudaError_t qdb_set_wait_limit_tcgemm(long long cycles);
 // Writes (host memory, 128 bytes) the tensor map of a bf16 [rows, cols]

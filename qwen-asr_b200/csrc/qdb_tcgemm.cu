@@ -142,7 +142,7 @@ template <int BN, int S>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXh,
                    const __grid_constant__ CUtensorMap tmXl, float *__restrict__ Y, int n, int N, int K, int mode,
-                   int kb_per, int *err) {
+                   int kb_per, int *err, const float *__restrict__ bias) {
     constexpr int A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
     constexpr int B_BYTES = BN * TC_BK * 2;
     constexpr int STAGE = A_BYTES + 2 * B_BYTES;
@@ -243,11 +243,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         tc_fence_after();
         const int wrow = m0 + 32 * q + lane;
+        // bias[wrow] is added once, by the first K-split
+        const float bb = (bias && blockIdx.z == 0 && wrow < N) ? bias[wrow] : 0.f;
         if (ok) {
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 float v[32];
                 tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+#pragma unroll
+                for (int j = 0; j < 32; j++) v[j] += bb;
 #pragma unroll
                 for (int j = 0; j < 32; j++) {
                     const int arow = a0 + c0 + j;
@@ -327,12 +331,15 @@ bool make_map(CUtensorMap *m, const void *base, int rows, int cols, int box_rows
 // (weight rows m0 + 32q + lane), columns [col0, col0 + BN) (activation rows a0..).
 template <int BN>
 __device__ __forceinline__ void epilogue_tile(uint32_t tcol, int q, int lane, int m0, int a0, float *__restrict__ Y,
-                                              int n, int N, int mode) {
+                                              int n, int N, int mode, const float *__restrict__ bias) {
     const int wrow = m0 + 32 * q + lane;
+    const float bb = (bias && wrow < N) ? bias[wrow] : 0.f;
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
         tmem_ld32(tcol + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] += bb;
         if (mode == 1) {  // residual add: all 32 loads in flight before the stores
             float y[32];
 #pragma unroll
@@ -371,7 +378,7 @@ template <int BN, int S>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_persist_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXh,
                            const __grid_constant__ CUtensorMap tmXl, float *__restrict__ Y, int n, int N, int K,
-                           int mode, int *err) {
+                           int mode, int *err, const float *__restrict__ bias) {
     constexpr int A_BYTES = TC_BM * TC_BK * 2;
     constexpr int B_BYTES = BN * TC_BK * 2;
     constexpr int STAGE = A_BYTES + 2 * B_BYTES;
@@ -469,7 +476,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             tc_fence_after();
-            epilogue_tile<BN>(tmem + (uint32_t)(b * BN), q, lane, (tile / ny) * TC_BM, (tile % ny) * BN, Y, n, N, mode);
+            epilogue_tile<BN>(tmem + (uint32_t)(b * BN), q, lane, (tile / ny) * TC_BM, (tile % ny) * BN, Y, n, N, mode,
+                              bias);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&acc_empty[b])) : "memory");
@@ -484,7 +492,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
 template <int BN, int S>
 cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,
-                      int mode, int splits, int *err, cudaStream_t st) {
+                      int mode, int splits, int *err, cudaStream_t st, const float *bias) {
     CUtensorMap mw, mh, ml;
     if (!make_map(&mw, W, N, K, TC_BM) || !make_map(&mh, Xh, n, K, BN) || !make_map(&ml, Xl, n, K, BN))
         return cudaErrorInvalidValue;
@@ -506,7 +514,7 @@ cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl,
     attr[0].val.programmaticStreamSerializationAllowed = QDB_GEMM_PDL;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, S>, mw, mh, ml, Y, n, N, K, mode, kb_per, err);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, S>, mw, mh, ml, Y, n, N, K, mode, kb_per, err, bias);
 }
 
 
@@ -515,7 +523,7 @@ cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl,
 #endif
 template <int BN, int S>
 cudaError_t launch_persist(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,
-                           int mode, int *err, cudaStream_t st) {
+                           int mode, int *err, cudaStream_t st, const float *bias) {
     CUtensorMap mw, mh, ml;
     if (!make_map(&mw, W, N, K, TC_BM) || !make_map(&mh, Xh, n, K, BN) || !make_map(&ml, Xl, n, K, BN))
         return cudaErrorInvalidValue;
@@ -538,7 +546,7 @@ cudaError_t launch_persist(const uint16_t *W, const uint16_t *Xh, const uint16_t
     attr[0].val.programmaticStreamSerializationAllowed = QDB_GEMM_PDL;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_persist_kernel<BN, S>, mw, mh, ml, Y, n, N, K, mode, err);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_persist_kernel<BN, S>, mw, mh, ml, Y, n, N, K, mode, err, bias);
 }
 
 }  // namespace
@@ -569,15 +577,23 @@ extern "C" cudaError_t qdb_launch_swiglu_split(const float *gu, uint16_t *hi, ui
 // splits > 1 (mode 3 only) divides K across CTAs so that skinny problems
 // (few weight-row tiles) still spread the weight stream over the whole GPU.
 // K % 64 == 0; all base pointers 16-byte aligned; N even for mode 2.
-extern "C" cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n,
-                                          int N, int K, int mode, int splits, int *err, cudaStream_t st) {
+// bias (optional, f32 [N]) is added to every output (once per element, also
+// under split-K).
+extern "C" cudaError_t qdb_launch_gemm_tc_bias(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y,
+                                               int n, int N, int K, int mode, int splits, int *err, cudaStream_t st,
+                                               const float *bias) {
     if (n <= 0) return cudaSuccess;
     if (K % TC_BK || (mode == 2 && (N & 1)) || mode < 0 || mode > 3) return cudaErrorInvalidValue;
     if (splits < 1 || (splits > 1 && mode != 3)) return cudaErrorInvalidValue;
     if (((uintptr_t)W | (uintptr_t)Xh | (uintptr_t)Xl) & 15) return cudaErrorInvalidValue;
-    if (n <= 64) return launch_tc<64, 6>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st);
-    if (QDB_GEMM_PERSIST && splits == 1) return launch_persist<128, 4>(W, Xh, Xl, Y, n, N, K, mode, err, st);
-    return launch_tc<128, 4>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st);
+    if (n <= 64) return launch_tc<64, 6>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, bias);
+    if (QDB_GEMM_PERSIST && splits == 1) return launch_persist<128, 4>(W, Xh, Xl, Y, n, N, K, mode, err, st, bias);
+    return launch_tc<128, 4>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, bias);
+}
+
+extern "C" cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n,
+                                          int N, int K, int mode, int splits, int *err, cudaStream_t st) {
+    return qdb_launch_gemm_tc_bias(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, nullptr);
 }
 
 #ifndef QDB_SPLIT_WAVES

@@ -401,3 +401,20 @@ def encoder_tokens(mel_frames: int, chunk: int = 100) -> int:
             w = (w - 1) // 2 + 1
         n += w
     return n
+
+
+def bench_pcm(seconds: float, seed: int, freq: float = 440.0, noise: float = 0.1, tone: float = 0.05) -> np.ndarray:
+    """The benchmark configurations' synthetic audio: seeded white noise (sigma
+    `noise` of full scale) plus a `freq` Hz sine of amplitude `tone`, quantised
+    to 16-bit PCM and read back as the reference's WAV loader does (s16 / 32768)."""
+    n = int(round(seconds * SAMPLE_RATE))
+    rng = np.random.default_rng(seed)
+    t = np.arange(n, dtype=np.float64) / SAMPLE_RATE
+    x = noise * rng.standard_normal(n) + tone * np.sin(2 * np.pi * freq * t)
+    pcm = np.clip(np.round(x * 32768.0), -32768, 32767).astype(np.int16)
+    return (pcm.astype(np.float32) / 32768.0).astype(np.float32)
+
+
+def bench_tone_hz(seed: int) -> float:
+    """c2's per-utterance sine frequency, uniform in 100-2000 Hz from the seed."""
+    return float(np.random.default_rng(seed + 1_000_000).uniform(100.0, 2000.0))

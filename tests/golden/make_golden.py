@@ -11,6 +11,10 @@ reference tree.
 Run here (needs oracle/_ref built):  python tests/golden/make_golden.py
   --small-only        only the three small shapes
   --bench=c0,c1,...   only the named benchmark-length cases (c0 c1 c3 c2set)
+  --enc               only enc_ref.npz: the reference's qwen_encoder_forward
+                      (qwen_asr_encoder.c, compiled unmodified into oracle/_ref)
+                      on synthetic encoder weights and the log-mel of seeded
+                      synthetic audio (mel by oracle/mel_oracle.py)
   --mel               only mel_ref.npz: the reference's qwen_mel_spectrogram
                       (qwen_asr_audio.c, compiled unmodified into oracle/_ref)
                       on seeded synthetic audio (synth.speech_audio)
@@ -31,7 +35,8 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 
 import __graft_entry__ as ge  # noqa: E402
-from oracle.pyoracle import RefDecoder, margin_top2, ref_mel_spectrogram  # noqa: E402
+from oracle.pyoracle import RefDecoder, RefEncoder, margin_top2, ref_mel_spectrogram  # noqa: E402
+from oracle import mel_oracle  # noqa: E402
 
 synth = ge.load_synth()
 
@@ -184,7 +189,50 @@ def run_mel():
     return out
 
 
+# Encoder cases: (name, preset, weight std or "fan_in", norm jitter, audio samples, audio seed, full output?)
+ENC_CASES = [
+    ("e_tiny", "tiny", "fan_in", 0.1, 69333, 21, True),         # 433 frames: a partial last chunk
+    ("e_tiny_long", "tiny", "fan_in", 0.1, 321000, 22, False),  # 2006 frames: 3 attention windows
+    ("e_06b", "0.6b", 0.02, 0.0, 48000, 23, True),              # real 0.6B shape, 3 s
+    ("e_17b", "1.7b", 0.02, 0.0, 32000, 24, False),             # real 1.7B shape, 2 s
+]
+
+
+def enc_weights(preset, std, jitter):
+    ec = synth.ENC_PRESETS[preset]
+    if std == "fan_in":
+        return synth.EncoderWeightSet(ec, seed=0, norm_jitter=jitter, scale_by_fan_in=True)
+    return synth.EncoderWeightSet(ec, seed=0, std=std, norm_jitter=jitter)
+
+
+def enc_mel(n, seed):
+    return mel_oracle.mel_spectrogram(synth.speech_audio(n, seed))
+
+
+def run_enc(threads):
+    out = {}
+    for name, preset, std, jit, n, seed, full in ENC_CASES:
+        ews = enc_weights(preset, std, jit)
+        ref = RefEncoder(ews, threads=threads)
+        y = ref.forward(enc_mel(n, seed))
+        ref.close()
+        out[name + "_args"] = np.array([n, seed], np.int64)
+        out[name + "_shape"] = np.array(y.shape, np.int64)
+        if full:
+            out[name] = y
+        else:
+            out[name + "_head"] = y[:8].copy()
+            out[name + "_rowsum"] = y.sum(axis=1, dtype=np.float64)
+            out[name + "_rowsq"] = (y.astype(np.float64) ** 2).sum(axis=1)
+        print("encoder", name, y.shape, float(np.abs(y).max()))
+    return out
+
+
 def main():
+    if "--enc" in sys.argv:
+        np.savez_compressed(os.path.join(HERE, "enc_ref.npz"), **run_enc(min(os.cpu_count() or 1, 16)))
+        print("wrote enc_ref.npz")
+        return
     if "--mel" in sys.argv:
         np.savez_compressed(os.path.join(HERE, "mel_ref.npz"), **run_mel())
         print("wrote mel_ref.npz")
