@@ -328,16 +328,22 @@ def measure_pipeline(pkg, synth, cfg_name, first, n_local, local, steps, warmup=
     sessions = [model.session(max(lens) + n_dec + 8) for _ in range(n_local)]
     es = torch.cuda.ExternalStream(enc.stream_handle, device=dev)
     ms_ = torch.cuda.ExternalStream(model.stream_handle, device=dev)
+    # The PCM copies run on a torch-owned stream: torch's pinned-memory pool
+    # records an event on every stream a pinned block was used on when the
+    # block is freed, so that stream must outlive the tensors (the library's
+    # streams die with their objects).
+    cs = torch.cuda.Stream(device=dev)
 
     def step(rec):
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
-        ev[0].record(es)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+        ev[0].record(cs)
         so = 0
-        with torch.cuda.stream(es):
+        with torch.cuda.stream(cs):
             for p, n in zip(pcm, ns):
                 samples_dev[so:so + n].copy_(p, non_blocking=True)
                 so += n
-        ev[1].record(es)
+        ev[1].record(cs)
+        es.wait_event(ev[1])
         so = mo = 0
         for n, f in zip(ns, frames):
             pkg.mel_spectrogram_device(samples_dev.data_ptr() + 4 * so, n, mel_dev.data_ptr() + 4 * mo,
@@ -353,16 +359,17 @@ def measure_pipeline(pkg, synth, cfg_name, first, n_local, local, steps, warmup=
         ev[3].record(es)
         ms_.wait_event(ev[3])
         model.build_prompt_device(desc, audio_dev.data_ptr(), emb_dev.data_ptr())
+        ev[4].record(ms_)
         if n_local == 1:
             sessions[0].prefill_device(emb_dev.data_ptr(), lens[0], 0)
         else:
             pkg.prefill_batch_device(sessions, emb_dev.data_ptr(), lens, [0] * n_local)
-        ev[4].record(ms_)
+        ev[5].record(ms_)
         if n_local == 1:
             out = sessions[0].decode_greedy(suf[-1], lens[0], n_dec)
         else:
             out = pkg.decode_greedy_batch(sessions, [suf[-1]] * n_local, lens, n_dec)
-        ev[5].record(ms_)
+        ev[6].record(ms_)
         if rec is not None:
             rec.append(ev)
         return out
@@ -374,9 +381,11 @@ def measure_pipeline(pkg, synth, cfg_name, first, n_local, local, steps, warmup=
     for _ in range(steps):
         step(rec)
     torch.cuda.synchronize()
-    names = ("h2d", "mel", "encoder", "prompt+prefill", "decode")
+    names = ("h2d", "mel", "encoder", "prompt", "prefill", "decode")
     stage = {k: sum(r[i].elapsed_time(r[i + 1]) for r in rec) / steps for i, k in enumerate(names)}
-    total = sum(r[0].elapsed_time(r[5]) for r in rec) / steps
+    total = sum(r[0].elapsed_time(r[6]) for r in rec) / steps
+    torch.cuda.synchronize()
+    del pcm, rec
     for s_ in sessions:
         s_.close()
     enc.close()

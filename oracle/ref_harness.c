@@ -264,9 +264,13 @@ int refh_encoder_forward(void *hp, const float *mel, int frames, float *out, int
     return seq;
 }
 
+/* Defined only by the drop-in encoder (qwen-asr_b200/dropin). */
+void qwen_encoder_release(qwen_ctx_t *ctx) __attribute__((weak));
+
 void refh_encoder_free(void *hp) {
     refh_t *h = (refh_t *)hp;
     if (!h) return;
+    if (qwen_encoder_release) qwen_encoder_release(h->ctx);
     qwen_encoder_t *enc = &h->ctx->encoder;
     free(enc->conv1_weight); free(enc->conv1_bias); free(enc->conv2_weight); free(enc->conv2_bias);
     free(enc->conv3_weight); free(enc->conv3_bias); free(enc->conv_out_weight);

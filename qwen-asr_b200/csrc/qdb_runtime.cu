@@ -159,6 +159,11 @@ struct qdb_model {
     int *h_tok = nullptr;      // pinned
     RowScratch rs;
     BatchScratch bs;
+    // weight upload staging (two pinned buffers; freed at finalize)
+    unsigned char *up_buf[2] = {nullptr, nullptr};
+    cudaEvent_t up_ev[2] = {nullptr, nullptr};
+    int up_next = 0;
+    double up_bytes = 0;
     std::vector<qdb_session *> sessions;  // live sessions (detached when the model is freed)
 };
 
@@ -341,10 +346,78 @@ extern "C" void qdb_model_free(qdb_model *m) {
     cudaFree(b.x); cudaFree(b.qkv); cudaFree(b.gu); cudaFree(b.part); cudaFree(b.stats); cudaFree(b.best);
     cudaFree(b.cnt); cudaFree(b.done); cudaFree(b.err); cudaFree(b.wt); cudaFree(b.prog); cudaFree(b.attn);
     cudaFree(b.acnt);
+    for (int i = 0; i < 2; i++) {
+        if (m->up_buf[i]) cudaFreeHost(m->up_buf[i]);
+        if (m->up_ev[i]) cudaEventDestroy(m->up_ev[i]);
+    }
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->h_tok) cudaFreeHost(m->h_tok);
     if (m->st) cudaStreamDestroy(m->st);
     delete m;
+}
+
+// ---- weight upload: pinned double-buffered staging (the reference loader
+// maps the safetensors file and reads the bf16 matrices in place,
+// qwen_asr_safetensors.c:194-228; here they cross PCIe once). A chunk is
+// copied into one pinned buffer by the host while the other one's DMA runs;
+// sources that are already pinned go straight to the device.
+constexpr size_t UP_CHUNK = 32u << 20;
+
+static bool host_pinned(const void *p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+}
+
+static int up_ready(qdb_model *m) {
+    for (int i = 0; i < 2; i++) {
+        if (!m->up_buf[i]) CK(cudaMallocHost((void **)&m->up_buf[i], UP_CHUNK));
+        if (!m->up_ev[i]) CK(cudaEventCreateWithFlags(&m->up_ev[i], cudaEventDisableTiming));
+    }
+    return 0;
+}
+
+// rows rows of row_bytes each, source row r at src + r * src_pitch, to
+// dst + r * dst_pitch (device); contiguous when both pitches equal row_bytes.
+static int upload_rows(qdb_model *m, void *dst, size_t dst_pitch, const void *src, size_t src_pitch, size_t row_bytes,
+                       size_t rows) {
+    m->up_bytes += (double)row_bytes * rows;
+    if (host_pinned(src)) {
+        CK(cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, row_bytes, rows, cudaMemcpyHostToDevice, m->st));
+        return 0;
+    }
+    if (up_ready(m)) return -1;
+    const size_t per = std::max<size_t>(1, UP_CHUNK / row_bytes);
+    for (size_t r0 = 0; r0 < rows; r0 += per) {
+        const size_t n = std::min(per, rows - r0);
+        const int b = m->up_next;
+        m->up_next ^= 1;
+        CK(cudaEventSynchronize(m->up_ev[b]));  // this buffer's previous DMA is done
+        unsigned char *st = m->up_buf[b];
+        const unsigned char *s0 = (const unsigned char *)src + r0 * src_pitch;
+        if (src_pitch == row_bytes) {
+            memcpy(st, s0, n * row_bytes);
+        } else {
+            for (size_t r = 0; r < n; r++) memcpy(st + r * row_bytes, s0 + r * src_pitch, row_bytes);
+        }
+        CK(cudaMemcpy2DAsync((unsigned char *)dst + r0 * dst_pitch, dst_pitch, st, row_bytes, row_bytes, n,
+                             cudaMemcpyHostToDevice, m->st));
+        CK(cudaEventRecord(m->up_ev[b], m->st));
+    }
+    return 0;
+}
+
+static int upload(qdb_model *m, void *dst, const void *src, size_t bytes) {
+    // contiguous: as rows of 1 MiB plus a tail
+    const size_t rb = 1u << 20, full = bytes / rb, tail = bytes % rb;
+    if (full && upload_rows(m, dst, rb, src, rb, rb, full)) return -1;
+    if (tail && upload_rows(m, (unsigned char *)dst + full * rb, tail, (const unsigned char *)src + full * rb, tail,
+                            tail, 1))
+        return -1;
+    return 0;
 }
 
 extern "C" int qdb_model_set_embed(qdb_model *m, const uint16_t *embed, const float *final_norm) {
@@ -352,8 +425,9 @@ extern "C" int qdb_model_set_embed(qdb_model *m, const uint16_t *embed, const fl
     if (!m || !embed || !final_norm) return fail("null argument");
     if (set_dev(m)) return -1;
     const size_t h = m->cfg.hidden;
-    CK(cudaMemcpy(m->embed, embed, (size_t)m->cfg.vocab * h * 2, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(m->final_norm, final_norm, h * 4, cudaMemcpyHostToDevice));
+    if (upload(m, m->embed, embed, (size_t)m->cfg.vocab * h * 2) || upload(m, m->final_norm, final_norm, h * 4))
+        return -1;
+    CK(cudaStreamSynchronize(m->st));  // the caller's buffers are free to go on return
     m->embed_set = true;
     return 0;
 }
@@ -370,19 +444,16 @@ extern "C" int qdb_model_set_layer(qdb_model *m, int layer, const uint16_t *wq, 
     if (set_dev(m)) return -1;
     const size_t h = m->cfg.hidden, I = m->cfg.intermediate, qd = m->qd, kvd = m->kvd;
     uint16_t *b = m->w + m->layer_elems * layer;
-    CK(cudaMemcpy(b + m->off_qkv, wq, qd * h * 2, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(b + m->off_qkv + qd * h, wk, kvd * h * 2, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(b + m->off_qkv + (qd + kvd) * h, wv, kvd * h * 2, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(b + m->off_o, wo, h * qd * 2, cudaMemcpyHostToDevice));
     // gate row j -> fused row 2j, up row j -> fused row 2j+1
-    CK(cudaMemcpy2D(b + m->off_gu, 4 * h, gate, 2 * h, 2 * h, I, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy2D(b + m->off_gu + h, 4 * h, up, 2 * h, 2 * h, I, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(b + m->off_down, down, h * I * 2, cudaMemcpyHostToDevice));
     float *nb = m->norms + m->norm_stride * layer;
-    CK(cudaMemcpy(nb, input_norm, h * 4, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(nb + h, post_attn_norm, h * 4, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(nb + 2 * h, q_norm, QDB_HD * 4, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(nb + 2 * h + QDB_HD, k_norm, QDB_HD * 4, cudaMemcpyHostToDevice));
+    if (upload(m, b + m->off_qkv, wq, qd * h * 2) || upload(m, b + m->off_qkv + qd * h, wk, kvd * h * 2) ||
+        upload(m, b + m->off_qkv + (qd + kvd) * h, wv, kvd * h * 2) || upload(m, b + m->off_o, wo, h * qd * 2) ||
+        upload_rows(m, b + m->off_gu, 4 * h, gate, 2 * h, 2 * h, I) ||
+        upload_rows(m, b + m->off_gu + h, 4 * h, up, 2 * h, 2 * h, I) || upload(m, b + m->off_down, down, h * I * 2) ||
+        upload(m, nb, input_norm, h * 4) || upload(m, nb + h, post_attn_norm, h * 4) ||
+        upload(m, nb + 2 * h, q_norm, QDB_HD * 4) || upload(m, nb + 2 * h + QDB_HD, k_norm, QDB_HD * 4))
+        return -1;
+    CK(cudaStreamSynchronize(m->st));  // the caller's buffers are free to go on return
     m->layer_set[layer] = 1;
     return 0;
 }
@@ -394,7 +465,14 @@ extern "C" int qdb_model_finalize(qdb_model *m) {
     for (int l = 0; l < m->cfg.layers; l++)
         if (!m->layer_set[l]) return fail("layer %d not set", l);
     if (set_dev(m)) return -1;
+    CK(cudaStreamSynchronize(m->st));
     CK(cudaDeviceSynchronize());
+    for (int i = 0; i < 2; i++) {
+        if (m->up_buf[i]) cudaFreeHost(m->up_buf[i]);
+        if (m->up_ev[i]) cudaEventDestroy(m->up_ev[i]);
+        m->up_buf[i] = nullptr;
+        m->up_ev[i] = nullptr;
+    }
     m->finalized = true;
     return 0;
 }

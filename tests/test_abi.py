@@ -70,14 +70,16 @@ def test_library_is_sm100a_only():
 
 
 def test_dropin_adapter_exports_reference_symbols(pkg, synth):
-    """The drop-in decoder exports the reference's three decoder symbols and,
+    """The drop-in adapters export the reference's decoder, encoder and mel
+    symbols (the reference's own qwen_mel_spectrogram renamed away) and,
     with no GPU, fails loudly inside the reference's qwen_decoder_load."""
     from oracle.pyoracle import RefDecoder
     p = os.path.join(REPO, "oracle", "_ref", "dropin", "libqwen_dropin.so")
     if not os.path.exists(p):
         pytest.skip("drop-in harness not built (needs the reference tree)")
     lib = ctypes.CDLL(p)
-    for sym in ("qwen_decoder_load", "qwen_decoder_prefill", "qwen_decoder_forward", "qwen_decoder_release"):
+    for sym in ("qwen_decoder_load", "qwen_decoder_prefill", "qwen_decoder_forward", "qwen_decoder_release",
+                "qwen_encoder_load", "qwen_encoder_forward", "qwen_encoder_release", "qwen_mel_spectrogram"):
         assert hasattr(lib, sym)
     if has_gpu():
         return

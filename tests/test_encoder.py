@@ -158,3 +158,22 @@ def test_gpu_encoder_device_form_and_reuse(pkg):
     _ = enc.forward(np.tile(mel, (1, 5)))
     check_against_gold("e_tiny", enc.forward(mel))
     enc.close()
+
+
+def _dropin_so():
+    p = os.path.join(REPO, "oracle", "_ref", "dropin", "libqwen_dropin.so")
+    return p if os.path.exists(p) else None
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(_dropin_so() is None, reason="drop-in harness not built (needs the reference tree)")
+@pytest.mark.parametrize("name", ["e_tiny", "e_06b"])
+def test_dropin_encoder_through_reference_loader(name):
+    """qwen_encoder_load / qwen_encoder_forward of the drop-in adapter
+    (qwen-asr_b200/dropin/qwen_asr_encoder_b200.c), driven by the same harness
+    and the reference's own safetensors loader as the reference encoder."""
+    from oracle.pyoracle import RefEncoder
+    ews, mel = case_inputs(name)
+    enc = RefEncoder(ews, so_path=_dropin_so())
+    check_against_gold(name, enc.forward(mel))
+    enc.close()

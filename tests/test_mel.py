@@ -146,3 +146,19 @@ def test_gpu_device_form_on_stream(pkg):
     # a second, shorter call reuses the grown scratch
     y = x[:5000].copy()
     np.testing.assert_allclose(pkg.mel_spectrogram(y), mel_oracle.mel_spectrogram(y), atol=TOL, rtol=0)
+
+
+def _dropin_so():
+    p = os.path.join(REPO, "oracle", "_ref", "dropin", "libqwen_dropin.so")
+    return p if os.path.exists(p) else None
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(_dropin_so() is None, reason="drop-in harness not built (needs the reference tree)")
+def test_dropin_mel_replaces_reference_symbol():
+    """qwen_mel_spectrogram of the drop-in adapter (qwen-asr_b200/dropin/
+    qwen_asr_mel_b200.c), resolved by symbol like the reference's caller does."""
+    from oracle.pyoracle import ref_mel_spectrogram
+    for name in FULL:
+        np.testing.assert_allclose(ref_mel_spectrogram(audio(name), so_path=_dropin_so()), GOLD[name], atol=TOL, rtol=0)
+    assert ref_mel_spectrogram(np.ones(100, np.float32), so_path=_dropin_so()) is None
