@@ -334,6 +334,16 @@ float *qdb_encoder_forward(qdb_encoder *e, const float *mel, int mel_frames, int
  * [128, mel_frames] -> out_dev [qdb_encoder_tokens(mel_frames), output_dim].
  * Returns the token count, or -1. */
 int qdb_encoder_forward_device(qdb_encoder *e, const float *mel_dev, int mel_frames, float *out_dev);
+
+/* Many utterances in one pass (no reference counterpart: the reference
+ * encodes one utterance per call): mel_dev[u] [128, mel_frames[u]] (device)
+ * -> out_dev [sum of tokens, output_dim], utterance u's rows after those of
+ * 0..u-1. The row-wise stages (convolutions, projections, norms) run once
+ * over all utterances; attention windows restart at each utterance, so each
+ * utterance's rows equal its own qdb_encoder_forward_device. Returns the total
+ * token count, or -1. */
+int qdb_encoder_forward_batch_device(qdb_encoder *e, int n_utt, const float *const *mel_dev, const int *mel_frames,
+                                     float *out_dev);
 void *qdb_encoder_stream(qdb_encoder *e);
 
 /* ---- Log-mel front end, replaces qwen_mel_spectrogram (qwen_asr_audio.c:293-390,

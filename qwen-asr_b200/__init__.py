@@ -77,6 +77,8 @@ ABI = {
     "qdb_encoder_forward": (ctypes.POINTER(ctypes.c_float), [ctypes.c_void_p, _f32p, ctypes.c_int, _i32p]),
     "qdb_encoder_forward_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "qdb_encoder_stream": (ctypes.c_void_p, [ctypes.c_void_p]),
+    "qdb_encoder_forward_batch_device": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_void_p),
+                                                        _i32p, ctypes.c_void_p]),
     "qdb_streams_create": (ctypes.c_void_p, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "qdb_streams_free": (None, [ctypes.c_void_p]),
     "qdb_streams_chunk": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p), _i32p, _i32p, _i32p,
@@ -486,6 +488,16 @@ class Encoder:
         if n < 0:
             raise _err("qdb_encoder_forward_device")
         return n
+
+    def forward_batch_device(self, mel_ptrs, frames, out_ptr: int) -> int:
+        """Many utterances in one pass (device pointers); returns the total token count."""
+        n = len(mel_ptrs)
+        ptrs = (ctypes.c_void_p * n)(*mel_ptrs)
+        f = np.ascontiguousarray(frames, dtype=np.int32)
+        r = lib.qdb_encoder_forward_batch_device(self.h, n, ptrs, _ptr(f, _i32p), ctypes.c_void_p(out_ptr))
+        if r < 0:
+            raise _err("qdb_encoder_forward_batch_device")
+        return r
 
     @property
     def stream_handle(self) -> int:

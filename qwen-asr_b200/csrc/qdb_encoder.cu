@@ -51,6 +51,8 @@ constexpr int KP = CH * 16;                                                     
 constexpr int GROUP = 32;                                                          // chunks per stem group
 
 struct EncChunk {
+    const float *mel;       // the chunk's utterance: mel [128, frames]
+    int frames;             // its mel row stride
     int f0, w, w1, w2, w3;  // first mel frame, widths after each convolution
     int p1, p2, p3, t0;     // row offsets (within the group) of conv1/2/3 outputs, first token
 };
@@ -69,8 +71,7 @@ __device__ __forceinline__ void split_store(uint16_t *hi, uint16_t *lo, size_t i
 
 // conv1: mel [128, frames] -> Y1 [(chunk, oh, ow), 480] pre-GELU (+bias).
 // One CTA per (oh, chunk).
-__global__ void __launch_bounds__(256) conv1_kernel(const float *__restrict__ mel, int frames,
-                                                    const EncChunk *__restrict__ ch, const float *__restrict__ w,
+__global__ void __launch_bounds__(256) conv1_kernel(const EncChunk *__restrict__ ch, const float *__restrict__ w,
                                                     const float *__restrict__ b, float *__restrict__ Y1) {
     __shared__ float rows[3][CHUNK + 2];
     __shared__ float ws[CH * 9];
@@ -80,7 +81,7 @@ __global__ void __launch_bounds__(256) conv1_kernel(const float *__restrict__ me
     for (int i = threadIdx.x; i < 3 * (CHUNK + 2); i += blockDim.x) {
         const int r = i / (CHUNK + 2), t = i % (CHUNK + 2) - 1;  // t in [-1, CHUNK]
         const int fr = 2 * oh - 1 + r;
-        rows[r][t + 1] = (fr >= 0 && fr < NMEL && t >= 0 && t < c.w) ? mel[(size_t)fr * frames + c.f0 + t] : 0.f;
+        rows[r][t + 1] = (fr >= 0 && fr < NMEL && t >= 0 && t < c.w) ? c.mel[(size_t)fr * c.frames + c.f0 + t] : 0.f;
     }
     __syncthreads();
     for (int i = threadIdx.x; i < c.w1 * CH; i += blockDim.x) {
@@ -203,19 +204,22 @@ __global__ void gelu_split_kernel(const float *__restrict__ y, size_t count, uin
     if (i < count) split_store(hi, lo, i, gelu_f(y[i]));
 }
 
-// Bidirectional attention inside windows of WIN_TOK tokens
-// (qwen_bidirectional_attention, qwen_asr_kernels.c:1003-1048), head_dim 64.
+// Bidirectional attention inside windows of at most WIN_TOK tokens
+// (qwen_bidirectional_attention, qwen_asr_kernels.c:1003-1048), head_dim 64;
+// the windows restart at each utterance's first token.
 // qkv [n, 3d] (q | k | v, each head h at columns h*64); output as the bf16
 // split of [n, d]. One CTA per (window, head), one warp per query row.
 constexpr int AW = 4;  // warps
-__global__ void __launch_bounds__(AW * 32) win_attn_kernel(const float *__restrict__ qkv, int n, int d, float scale,
-                                                           uint16_t *__restrict__ hi, uint16_t *__restrict__ lo) {
+__global__ void __launch_bounds__(AW * 32) win_attn_kernel(const float *__restrict__ qkv, const int2 *__restrict__ wins,
+                                                           int d, float scale, uint16_t *__restrict__ hi,
+                                                           uint16_t *__restrict__ lo) {
     extern __shared__ float sm[];
     float *K = sm;                        // [WIN_TOK][65]
     float *V = K + WIN_TOK * 65;          // [WIN_TOK][64]
     float *Q = V + WIN_TOK * 64;          // [AW][64]
     float *P = Q + AW * 64;               // [AW][WIN_TOK]
-    const int w0 = blockIdx.x * WIN_TOK, L = min(WIN_TOK, n - w0), h = blockIdx.y;
+    const int2 win = wins[blockIdx.x];  // (first token, tokens) of this window
+    const int w0 = win.x, L = win.y, h = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t rs = (size_t)3 * d;
     for (int i = threadIdx.x; i < L * 64; i += blockDim.x) {
@@ -297,7 +301,10 @@ struct qdb_encoder {
     uint16_t *xh = nullptr, *xl = nullptr;  // bf16 split [rows, K] of the current GEMM input
     size_t cap_split = 0;
     float *y1 = nullptr, *y2 = nullptr, *y3 = nullptr;  // stem group outputs
-    EncChunk *d_chunks = nullptr;
+    EncChunk *d_chunks_all = nullptr;
+    size_t cap_chunks = 0;
+    int2 *d_wins = nullptr;
+    size_t cap_wins = 0;
     int *err = nullptr;
     float *mel_dev = nullptr, *out_dev = nullptr;
     size_t cap_mel = 0, cap_out = 0;
@@ -432,7 +439,7 @@ extern "C" qdb_encoder *qdb_encoder_create(const qdb_encoder_config *cfg, int de
     e->layers.resize(c.layers);
     e->layer_set.assign(c.layers, 0);
     if (cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking) != cudaSuccess ||
-        enc_alloc(e, &e->d_chunks, GROUP * 4) || enc_alloc(e, &e->err, 4) ||
+        enc_alloc(e, &e->err, 4) ||
         cudaMemset(e->err, 0, 16) != cudaSuccess) {
         qdb_encoder_free(e);
         return nullptr;
@@ -446,7 +453,8 @@ extern "C" void qdb_encoder_free(qdb_encoder *e) {
     if (e->st) cudaStreamSynchronize(e->st);
     for (void *p : e->allocs) cudaFree(p);
     for (void *p : {(void *)e->x, (void *)e->big, (void *)e->xh, (void *)e->xl, (void *)e->y1, (void *)e->y2,
-                    (void *)e->y3, (void *)e->mel_dev, (void *)e->out_dev})
+                    (void *)e->y3, (void *)e->mel_dev, (void *)e->out_dev, (void *)e->d_chunks_all,
+                    (void *)e->d_wins})
         cudaFree(p);
     if (e->st) cudaStreamDestroy(e->st);
     delete e;
@@ -521,34 +529,71 @@ extern "C" int qdb_encoder_finalize(qdb_encoder *e) {
 
 extern "C" void *qdb_encoder_stream(qdb_encoder *e) { return e ? (void *)e->st : nullptr; }
 
-// mel_dev [128, frames] (device) -> out_dev [tokens, output_dim] (device), on
-// the encoder's stream. Returns the token count, or -1.
-extern "C" int qdb_encoder_forward_device(qdb_encoder *e, const float *mel_dev, int frames, float *out_dev) {
+// n utterances: mel_dev[u] [128, frames[u]] (device) -> out_dev [sum of
+// tokens, output_dim] (device), utterance u's rows after those of 0..u-1, on
+// the encoder's stream. Every row-wise stage runs once over all utterances'
+// tokens; attention windows restart at each utterance. Returns the token
+// count, or -1.
+extern "C" int qdb_encoder_forward_batch_device(qdb_encoder *e, int n_utt, const float *const *mel_dev,
+                                                const int *frames, float *out_dev) {
     if (!e || !e->finalized) return qdb_set_error("qdb_encoder_forward: encoder not finalized");
-    if (!mel_dev || !out_dev || frames <= 0) return qdb_set_error("qdb_encoder_forward: no input");
+    if (n_utt <= 0 || !mel_dev || !frames || !out_dev) return qdb_set_error("qdb_encoder_forward: no input");
+    for (int u = 0; u < n_utt; u++)
+        if (!mel_dev[u] || frames[u] <= 0) return qdb_set_error("qdb_encoder_forward: empty utterance");
     if (cudaSetDevice(e->device) != cudaSuccess) return qdb_set_error("qdb_encoder: cudaSetDevice failed");
-    const int d = e->cfg.d_model, ntok = qdb_encoder_tokens(frames);
+    const int d = e->cfg.d_model;
+    // chunks of every utterance, windows of every utterance
+    std::vector<EncChunk> all;
+    std::vector<int2> wins;
+    int ntok = 0;
+    for (int u = 0; u < n_utt; u++) {
+        const int t_u = qdb_encoder_tokens(frames[u]);
+        for (int f0 = 0; f0 < frames[u]; f0 += CHUNK) {
+            EncChunk k{};
+            k.mel = mel_dev[u];
+            k.frames = frames[u];
+            k.f0 = f0;
+            k.w = std::min(CHUNK, frames[u] - f0);
+            k.w1 = (k.w - 1) / 2 + 1;
+            k.w2 = (k.w1 - 1) / 2 + 1;
+            k.w3 = (k.w2 - 1) / 2 + 1;
+            all.push_back(k);
+        }
+        for (int w0 = 0; w0 < t_u; w0 += WIN_TOK) wins.push_back(make_int2(ntok + w0, std::min(WIN_TOK, t_u - w0)));
+        ntok += t_u;
+    }
     if (grow_scratch(e, ntok)) return -1;
-    const int nchunks = (frames + CHUNK - 1) / CHUNK;
     if (!e->y1 && (cudaMalloc(&e->y1, (size_t)GROUP * 3200 * CH * 4) != cudaSuccess ||
                    cudaMalloc(&e->y2, (size_t)GROUP * 800 * CH * 4) != cudaSuccess ||
                    cudaMalloc(&e->y3, (size_t)GROUP * 208 * CH * 4) != cudaSuccess))
         return qdb_set_error("qdb_encoder: out of device memory (stem)");
+    if (wins.size() > e->cap_wins) {
+        cudaFree(e->d_wins);
+        e->d_wins = nullptr;
+        e->cap_wins = 0;
+        if (cudaMalloc(&e->d_wins, wins.size() * sizeof(int2)) != cudaSuccess)
+            return qdb_set_error("qdb_encoder: out of device memory (windows)");
+        e->cap_wins = wins.size();
+    }
     cudaStream_t st = e->st;
-    // ---- convolution stem, GROUP chunks at a time
-    std::vector<EncChunk> tab;
+    if (cudaMemcpyAsync(e->d_wins, wins.data(), wins.size() * sizeof(int2), cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return qdb_set_error("qdb_encoder: window table upload failed");
+    // ---- convolution stem, GROUP chunks at a time (any mix of utterances)
+    const int nchunks = (int)all.size();
+    if ((size_t)nchunks > e->cap_chunks) {
+        cudaFree(e->d_chunks_all);
+        e->d_chunks_all = nullptr;
+        e->cap_chunks = 0;
+        if (cudaMalloc(&e->d_chunks_all, sizeof(EncChunk) * nchunks) != cudaSuccess)
+            return qdb_set_error("qdb_encoder: out of device memory (chunk table)");
+        e->cap_chunks = nchunks;
+    }
     int tok = 0;
     for (int g0 = 0; g0 < nchunks; g0 += GROUP) {
         const int ng = std::min(GROUP, nchunks - g0);
-        tab.assign(ng, EncChunk{});
         int p1 = 0, p2 = 0, p3 = 0, t0 = 0;
-        for (int c = 0; c < ng; c++) {
-            EncChunk &k = tab[c];
-            k.f0 = (g0 + c) * CHUNK;
-            k.w = std::min(CHUNK, frames - k.f0);
-            k.w1 = (k.w - 1) / 2 + 1;
-            k.w2 = (k.w1 - 1) / 2 + 1;
-            k.w3 = (k.w2 - 1) / 2 + 1;
+        for (int c = g0; c < g0 + ng; c++) {
+            EncChunk &k = all[c];
             k.p1 = p1;
             k.p2 = p2;
             k.p3 = p3;
@@ -558,33 +603,33 @@ extern "C" int qdb_encoder_forward_device(qdb_encoder *e, const float *mel_dev, 
             p3 += 16 * k.w3;
             t0 += k.w3;
         }
-        if (cudaMemcpyAsync(e->d_chunks, tab.data(), sizeof(EncChunk) * ng, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        EncChunk *tab = e->d_chunks_all + g0;
+        if (cudaMemcpyAsync(tab, all.data() + g0, sizeof(EncChunk) * ng, cudaMemcpyHostToDevice, st) != cudaSuccess)
             return qdb_set_error("qdb_encoder: chunk table upload failed");
-        conv1_kernel<<<dim3(64, ng), 256, 0, st>>>(mel_dev, frames, e->d_chunks, e->c1w, e->c1b, e->y1);
-        im2col_gelu_kernel<<<dim3(32 * 25, ng), 256, 0, st>>>(e->y1, e->d_chunks, 2, e->xh, e->xl);
+        conv1_kernel<<<dim3(64, ng), 256, 0, st>>>(tab, e->c1w, e->c1b, e->y1);
+        im2col_gelu_kernel<<<dim3(32 * 25, ng), 256, 0, st>>>(e->y1, tab, 2, e->xh, e->xl);
         if (gemm(e, e->c2w, e->y2, p2, CH, KCP, 0, e->c2b) || (e->c2lo && gemm(e, e->c2lo, e->y2, p2, CH, KCP, 1, nullptr)))
             return -1;
-        im2col_gelu_kernel<<<dim3(16 * 13, ng), 256, 0, st>>>(e->y2, e->d_chunks, 3, e->xh, e->xl);
+        im2col_gelu_kernel<<<dim3(16 * 13, ng), 256, 0, st>>>(e->y2, tab, 3, e->xh, e->xl);
         if (gemm(e, e->c3w, e->y3, p3, CH, KCP, 0, e->c3b) || (e->c3lo && gemm(e, e->c3lo, e->y3, p3, CH, KCP, 1, nullptr)))
             return -1;
-        // the projection input rows of this group land at their token rows in a [tok, 7680] split;
-        // the stem scratch (xh/xl) is reused by the next group, so project this group now
-        stem_gather_kernel<<<dim3(13, ng), 256, 0, st>>>(e->y3, e->d_chunks, 0, e->xh, e->xl);
-        pe_fill_kernel<<<dim3(13, ng), 256, 0, st>>>(e->d_chunks, tok, e->x, d);
-        if (qdb_launch_gemm_tc_bias(e->cout, e->xh, e->xl, e->x + (size_t)tok * d, t0, d, KP, 1, 1, e->err, st,
-                                    nullptr) != cudaSuccess)
-            return qdb_set_error("qdb_encoder: conv_out GEMM launch failed");
+        // this group's projection input rows, then its projection (the stem
+        // scratch is reused by the next group)
+        stem_gather_kernel<<<dim3(13, ng), 256, 0, st>>>(e->y3, tab, 0, e->xh, e->xl);
+        pe_fill_kernel<<<dim3(13, ng), 256, 0, st>>>(tab, tok, e->x, d);
+        if (gemm(e, e->cout, e->x + (size_t)tok * d, t0, d, KP, 1, nullptr)) return -1;
         tok += t0;
     }
-    // ---- transformer layers over all tokens (windows of WIN_TOK)
-    const int n = ntok, nwin = (n + WIN_TOK - 1) / WIN_TOK;
+    // ---- transformer layers over all tokens
+    const int n = ntok, nwin = (int)wins.size();
     const size_t asmem = (size_t)(WIN_TOK * 129 + AW * (64 + WIN_TOK)) * 4;
     for (int l = 0; l < e->cfg.layers; l++) {
         const EncLayer &L = e->layers[l];
         layernorm_split_kernel<<<n, 256, 0, st>>>(e->x, L.ln1w, L.ln1b, d, 1e-5f, e->xh, e->xl);
         if (gemm(e, L.wqkv, e->big, n, 3 * d, d, 0, L.bqkv)) return -1;
-        win_attn_kernel<<<dim3(nwin, e->cfg.heads), AW * 32, asmem, st>>>(e->big, n, d, 1.0f / sqrtf((float)e->cfg.head_dim),
-                                                                         e->xh, e->xl);
+        win_attn_kernel<<<dim3(nwin, e->cfg.heads), AW * 32, asmem, st>>>(e->big, e->d_wins, d,
+                                                                         1.0f / sqrtf((float)e->cfg.head_dim), e->xh,
+                                                                         e->xl);
         if (gemm(e, L.wo, e->x, n, d, d, 1, L.bo)) return -1;
         layernorm_split_kernel<<<n, 256, 0, st>>>(e->x, L.ln2w, L.ln2b, d, 1e-5f, e->xh, e->xl);
         if (gemm(e, L.fc1, e->big, n, e->cfg.ffn_dim, d, 0, L.b1)) return -1;
@@ -600,6 +645,12 @@ extern "C" int qdb_encoder_forward_device(qdb_encoder *e, const float *mel_dev, 
     const cudaError_t le = cudaGetLastError();
     if (le != cudaSuccess) return qdb_set_error(cudaGetErrorString(le));
     return n;
+}
+
+// One utterance: mel_dev [128, frames] (device) -> out_dev [tokens,
+// output_dim] (device), on the encoder's stream. Returns the token count, or -1.
+extern "C" int qdb_encoder_forward_device(qdb_encoder *e, const float *mel_dev, int frames, float *out_dev) {
+    return qdb_encoder_forward_batch_device(e, 1, &mel_dev, &frames, out_dev);
 }
 
 // Drop-in for qwen_encoder_forward (qwen_asr_encoder.c:171): host mel

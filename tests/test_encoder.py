@@ -177,3 +177,28 @@ def test_dropin_encoder_through_reference_loader(name):
     enc = RefEncoder(ews, so_path=_dropin_so())
     check_against_gold(name, enc.forward(mel))
     enc.close()
+
+
+@pytest.mark.gpu
+def test_gpu_encoder_batch_equals_separate_calls(pkg):
+    """Utterances of different lengths in one pass: each one's rows equal its
+    own forward (windows restart per utterance)."""
+    import torch
+    ews = synth.EncoderWeightSet(synth.ENC_PRESETS["tiny"], seed=8, norm_jitter=0.1, scale_by_fan_in=True)
+    frames = [1500, 37, 900, 1, 260, 2150]  # windows cut mid-utterance, a 1-frame utterance
+    mels = [np.random.default_rng(f).uniform(-1.0, 1.5, (128, f)).astype(np.float32) for f in frames]
+    enc = pkg.Encoder(ews)
+    sep = [enc.forward(m) for m in mels]
+    dm = [torch.from_numpy(m).cuda() for m in mels]
+    n = sum(pkg.Encoder.tokens(f) for f in frames)
+    out = torch.empty((n, ews.cfg.output_dim), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    assert enc.forward_batch_device([t.data_ptr() for t in dm], frames, out.data_ptr()) == n
+    torch.cuda.ExternalStream(enc.stream_handle).synchronize()
+    got = out.cpu().numpy()
+    r = 0
+    for y, m in zip(sep, mels):
+        close(got[r:r + len(y)], y, 1e-4, 1e-4)  # split-K vs persistent GEMM tiling only
+        close(y, enc_oracle.encoder_forward(ews, m))
+        r += len(y)
+    enc.close()
