@@ -203,6 +203,9 @@ struct QdbModelInfo {
     cudaStream_t stream;
 };
 int qdb_model_internals(qdb_model *m, QdbModelInfo *out);
+// prompt rows: desc_dev[r] >= 0 token id, < 0 audio row -(desc+1) (qdb_stream.cu)
+cudaError_t qdb_launch_prompt_rows(const uint16_t *embed, const int *desc_dev, const float *audio_dev, float *out_dev,
+                                   int n_rows, int hidden, cudaStream_t st);
 // step (optional, device): the rows' tokens are read at tokens + *step * n
 // (embed) / written at tokens + *step * n (argmax), and positions advance by
 // *step (qk_rope_append, attn_rows): the form a captured decode step replays.

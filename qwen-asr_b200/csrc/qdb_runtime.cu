@@ -159,6 +159,10 @@ struct qdb_model {
     int *h_tok = nullptr;      // pinned
     RowScratch rs;
     BatchScratch bs;
+    // prompt-row descriptors: pinned host staging + device copy (grow-only)
+    int *pdesc_host = nullptr, *pdesc_dev = nullptr;
+    int pdesc_cap = 0;
+    cudaEvent_t pdesc_ev = nullptr;
     // weight upload staging (two pinned buffers; freed at finalize)
     unsigned char *up_buf[2] = {nullptr, nullptr};
     cudaEvent_t up_ev[2] = {nullptr, nullptr};
@@ -174,6 +178,40 @@ struct qdb_session {
 };
 
 extern "C" const char *qdb_last_error(void) { return g_err.c_str(); }
+
+// Prompt rows on the device for the offline path (qwen_asr.c:626-700 builds
+// them on the host): desc[r] >= 0 is a token id (its embedding row), desc[r] < 0
+// is audio row -(desc[r] + 1) of audio_dev. The descriptors go through a
+// pinned buffer of the model (no allocation or pageable copy per call).
+extern "C" int qdb_build_prompt_device(qdb_model *m, const int *desc, int n_rows, const float *audio_dev,
+                                       float *out_dev) {
+    g_err.clear();
+    if (!m || !m->finalized) return fail("qdb_build_prompt_device: model not finalized");
+    if (!desc || n_rows <= 0 || !out_dev) return fail("qdb_build_prompt_device: bad arguments");
+    for (int r = 0; r < n_rows; r++) {
+        if (desc[r] >= m->cfg.vocab) return fail("qdb_build_prompt_device: token %d out of range", desc[r]);
+        if (desc[r] < 0 && !audio_dev) return fail("qdb_build_prompt_device: audio rows without audio");
+    }
+    CK(cudaSetDevice(m->device));
+    if (!m->pdesc_ev) CK(cudaEventCreateWithFlags(&m->pdesc_ev, cudaEventDisableTiming));
+    CK(cudaEventSynchronize(m->pdesc_ev));  // the previous call's copy has left the pinned buffer
+    if (n_rows > m->pdesc_cap) {
+        if (m->pdesc_host) cudaFreeHost(m->pdesc_host);
+        if (m->pdesc_dev) cudaFree(m->pdesc_dev);
+        m->pdesc_host = nullptr;
+        m->pdesc_dev = nullptr;
+        m->pdesc_cap = 0;
+        const int cap = std::max(n_rows, 4096);
+        CK(cudaMallocHost((void **)&m->pdesc_host, sizeof(int) * cap));
+        if (dev_alloc(&m->pdesc_dev, (size_t)cap)) return -1;
+        m->pdesc_cap = cap;
+    }
+    memcpy(m->pdesc_host, desc, sizeof(int) * n_rows);
+    CK(cudaMemcpyAsync(m->pdesc_dev, m->pdesc_host, sizeof(int) * n_rows, cudaMemcpyHostToDevice, m->st));
+    CK(cudaEventRecord(m->pdesc_ev, m->st));
+    CK(qdb_launch_prompt_rows(m->embed, m->pdesc_dev, audio_dev, out_dev, n_rows, m->cfg.hidden, m->st));
+    return 0;
+}
 
 int qdb_model_internals(qdb_model *m, QdbModelInfo *out) {
     if (!m || !out) return fail("null model");
@@ -350,6 +388,9 @@ extern "C" void qdb_model_free(qdb_model *m) {
         if (m->up_buf[i]) cudaFreeHost(m->up_buf[i]);
         if (m->up_ev[i]) cudaEventDestroy(m->up_ev[i]);
     }
+    if (m->pdesc_host) cudaFreeHost(m->pdesc_host);
+    if (m->pdesc_dev) cudaFree(m->pdesc_dev);
+    if (m->pdesc_ev) cudaEventDestroy(m->pdesc_ev);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->h_tok) cudaFreeHost(m->h_tok);
     if (m->st) cudaStreamDestroy(m->st);

@@ -561,28 +561,10 @@ extern "C" int qdb_streams_last_chunk(const qdb_streams *S, float *ms, int *coun
     return 0;
 }
 
-// Prompt rows on the device for the offline path (qwen_asr.c:626-700 builds
-// them on the host): desc[r] >= 0 is a token id (its embedding row), desc[r] < 0
-// is audio row -(desc[r] + 1) of audio_dev [*, hidden] (e.g. the encoder's
-// output). out_dev [n_rows, hidden] f32, on the model's stream.
-extern "C" int qdb_build_prompt_device(qdb_model *m, const int *desc, int n_rows, const float *audio_dev,
-                                       float *out_dev) {
-    QdbModelInfo info{};
-    if (qdb_model_internals(m, &info)) return -1;
-    if (!desc || n_rows <= 0 || !out_dev) return qdb_set_error("qdb_build_prompt_device: bad arguments");
-    for (int r = 0; r < n_rows; r++) {
-        if (desc[r] >= info.vocab) return qdb_set_error("qdb_build_prompt_device: token out of range");
-        if (desc[r] < 0 && !audio_dev) return qdb_set_error("qdb_build_prompt_device: audio rows without audio");
-    }
-    if (cudaSetDevice(info.device) != cudaSuccess) return qdb_set_error("qdb_build_prompt_device: cudaSetDevice");
-    int *d = nullptr;
-    if (cudaMallocAsync((void **)&d, sizeof(int) * n_rows, info.stream) != cudaSuccess)
-        return qdb_set_error("qdb_build_prompt_device: out of device memory");
-    cudaError_t e = cudaMemcpyAsync(d, desc, sizeof(int) * n_rows, cudaMemcpyHostToDevice, info.stream);
-    if (e == cudaSuccess) {
-        prompt_rows_kernel<<<n_rows, 256, 0, info.stream>>>(info.embed, d, audio_dev, out_dev, info.hidden);
-        e = cudaGetLastError();
-    }
-    cudaFreeAsync(d, info.stream);
-    return e == cudaSuccess ? 0 : qdb_set_error(cudaGetErrorString(e));
+// Launcher for the prompt-row builder (qdb_build_prompt_device, qdb_runtime.cu).
+cudaError_t qdb_launch_prompt_rows(const uint16_t *embed, const int *desc_dev, const float *audio_dev, float *out_dev,
+                                   int n_rows, int hidden, cudaStream_t st) {
+    if (n_rows <= 0) return cudaSuccess;
+    prompt_rows_kernel<<<n_rows, 256, 0, st>>>(embed, desc_dev, audio_dev, out_dev, hidden);
+    return cudaGetLastError();
 }
