@@ -200,7 +200,9 @@ def measure(pkg, synth, cfg_name, world, rank, local, steps, warmup, clocks=None
     embs = [synth.utterance(ws, seconds, utterance_seed(cfg_name, u)) for u in range(first, first + n_local)]
     P = embs[0].shape[0] - 1  # prefill length; the last prompt position is token 198
     last_tok = synth.PROMPT_SUFFIX[-1]
-    model = pkg.Model(ws, device=local, mask_eos=True)
+    t_up = time.perf_counter()
+    model = pkg.Model(ws, device=local, mask_eos=True)  # weight upload: staged through pinned buffers
+    upload_s = time.perf_counter() - t_up
     setup_s = time.time() - t0
     stream = torch.cuda.ExternalStream(model.stream_handle, device=torch.device("cuda", local))
     cap = P + n_dec + 8
@@ -290,7 +292,7 @@ def measure(pkg, synth, cfg_name, world, rank, local, steps, warmup, clocks=None
     torch.cuda.synchronize()
     return dict(cfg=cfg, ws=ws, embs=embs, P=P, n_dec=n_dec, n_utt=n_utt, n_local=n_local, seconds=seconds,
                 pre_ms=pre_ms, dec_ms=dec_ms, tot_ms=tot_ms, e2e_dec_ms=e2e_dec_ms, e2e_tot_ms=e2e_tot_ms,
-                e2e_steps=e2e_steps, h2d=h2d, d2h=d2h, clk=clk, wall=wall, setup_s=setup_s)
+                e2e_steps=e2e_steps, h2d=h2d, d2h=d2h, clk=clk, wall=wall, setup_s=setup_s, upload_s=upload_s)
 
 
 def measure_pipeline(pkg, synth, cfg_name, first, n_local, local, steps, warmup=1):
@@ -511,6 +513,10 @@ def run_ours(args):
         "clocks": m["clk"],
         "wall_s": round(m["wall"], 3),
         "setup_s": round(m["setup_s"], 1),
+        "weight_upload": {"s": round(m["upload_s"], 3), "bytes": int(weight_bytes(m["cfg"])),
+                          "gb_s": round(weight_bytes(m["cfg"]) / m["upload_s"] / 1e9, 2),
+                          "path": "qdb_model_set_* from pageable host memory (the reference's mmap case), "
+                                  "double-buffered pinned staging"},
     }
     if rank == 0 and world == 1 and not args.no_b1 and args.config == "c2":
         b1 = {}
@@ -940,6 +946,33 @@ def profile_batch(args):
     print(toks[:4].tolist())
 
 
+def profile_encoder(args):
+    """Fixed case for ncu captures of the audio front end: log-mel and encoder
+    of one 30 s 0.6B utterance (seeded PCM), run twice, the second time inside
+    the NVTX range "frontend" (ncu --nvtx --nvtx-include "frontend/")."""
+    import torch
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    synth = ge.load_synth()
+    ews = synth.EncoderWeightSet(synth.ENC_PRESETS["0.6b"], seed=0)
+    enc = pkg.Encoder(ews)
+    x = torch.from_numpy(synth.bench_pcm(30.0, 1)).cuda()
+    f = pkg.mel_frames(x.numel())
+    mel = torch.empty(128 * f, device="cuda")
+    out = torch.empty((pkg.Encoder.tokens(f), ews.cfg.output_dim), device="cuda")
+    es = torch.cuda.ExternalStream(enc.stream_handle)
+    for i in range(2):
+        torch.cuda.synchronize()
+        if i == 1:
+            torch.cuda.nvtx.range_push("frontend")
+        pkg.mel_spectrogram_device(x.data_ptr(), x.numel(), mel.data_ptr(), enc.stream_handle)
+        enc.forward_device(mel.data_ptr(), f, out.data_ptr())
+        es.synchronize()
+    torch.cuda.nvtx.range_pop()
+    print(out.shape, float(out.abs().max()))
+    enc.close()
+
+
 def free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -958,6 +991,7 @@ def main():
     ap.add_argument("--no-pipeline", action="store_true", help="skip the audio -> tokens pipeline measurement")
     ap.add_argument("--profile-step", action="store_true", help="small fixed case for ncu (no timing)")
     ap.add_argument("--profile-batch", action="store_true", help="batched-decode case for ncu (no timing)")
+    ap.add_argument("--profile-encoder", action="store_true", help="mel + encoder case for ncu (no timing)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -971,6 +1005,9 @@ def main():
         print(f"bench.py: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE", file=sys.stderr)
     if args.profile_batch:
         profile_batch(args)
+        return
+    if args.profile_encoder:
+        profile_encoder(args)
         return
     if args.profile_step:
         profile_step(args)

