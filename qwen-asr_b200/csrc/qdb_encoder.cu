@@ -230,7 +230,8 @@ __global__ void __launch_bounds__(AW * 32) win_attn_kernel(const float *__restri
     }
     __syncthreads();
     float *q = Q + warp * 64, *p = P + warp * WIN_TOK;
-    for (int i = warp; i < L; i += AW) {
+    // query rows of this window split over gridDim.z CTAs (each loads the window's K/V)
+    for (int i = blockIdx.z * AW + warp; i < L; i += AW * gridDim.z) {
         const float *qr = qkv + (size_t)(w0 + i) * rs + h * 64;
         q[lane] = qr[lane];
         q[lane + 32] = qr[lane + 32];
@@ -623,11 +624,15 @@ extern "C" int qdb_encoder_forward_batch_device(qdb_encoder *e, int n_utt, const
     // ---- transformer layers over all tokens
     const int n = ntok, nwin = (int)wins.size();
     const size_t asmem = (size_t)(WIN_TOK * 129 + AW * (64 + WIN_TOK)) * 4;
+    // few windows (one short utterance) leave most SMs idle: split the
+    // windows' query rows over more CTAs until there are ~2 per SM
+    int qsplit = 1;
+    while (qsplit < 8 && nwin * e->cfg.heads * qsplit < 2 * e->sms) qsplit *= 2;
     for (int l = 0; l < e->cfg.layers; l++) {
         const EncLayer &L = e->layers[l];
         layernorm_split_kernel<<<n, 256, 0, st>>>(e->x, L.ln1w, L.ln1b, d, 1e-5f, e->xh, e->xl);
         if (gemm(e, L.wqkv, e->big, n, 3 * d, d, 0, L.bqkv)) return -1;
-        win_attn_kernel<<<dim3(nwin, e->cfg.heads), AW * 32, asmem, st>>>(e->big, e->d_wins, d,
+        win_attn_kernel<<<dim3(nwin, e->cfg.heads, qsplit), AW * 32, asmem, st>>>(e->big, e->d_wins, d,
                                                                          1.0f / sqrtf((float)e->cfg.head_dim), e->xh,
                                                                          e->xl);
         if (gemm(e, L.wo, e->x, n, d, d, 1, L.bo)) return -1;
