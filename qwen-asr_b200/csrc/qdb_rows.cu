@@ -129,12 +129,18 @@ constexpr int AR_WARPS = 8, AR_KEYS = 8;
 // and the 8 warps take 8 keys each per chunk. K chunks are read with the
 // 16-byte piece order rotated per lane, which keeps the quarter-warp
 // LDS.128 phases free of bank conflicts.
-constexpr int AB_STAGES = 3, AB_KEYS = 64, AB_HALF = AB_KEYS * QDB_HD * 2, AB_STAGE = 2 * AB_HALF;
+#ifndef QDB_AR_STAGES
+#define QDB_AR_STAGES 2  // bulk-copy ring stages (32 KB each); 2 x 3 CTAs per SM measured best
+#endif
+#ifndef QDB_AR_MINB
+#define QDB_AR_MINB 3  // CTAs per SM the register budget is sized for
+#endif
+constexpr int AB_STAGES = QDB_AR_STAGES, AB_KEYS = 64, AB_HALF = AB_KEYS * QDB_HD * 2, AB_STAGE = 2 * AB_HALF;
 typedef unsigned long long u64r;
 __device__ __forceinline__ uint32_t su32r(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 template <int R>
-__global__ void __launch_bounds__(AR_WARPS * 32, 2) attn_rows_bulk_kernel(const float *q, const QdbRowKV *rows,
+__global__ void __launch_bounds__(AR_WARPS * 32, QDB_AR_MINB) attn_rows_bulk_kernel(const float *q, const QdbRowKV *rows,
                                                                          int row_pos_offset, int layer, int Hq,
                                                                          int Hkv, int S, float *part, int *err,
                                                                          const int *step, float *out, uint16_t *hi,

@@ -585,6 +585,9 @@ extern "C" cudaError_t qdb_launch_swiglu_split(const float *gu, uint16_t *hi, ui
 // splits > 1 (mode 3 only) divides K across CTAs so that skinny problems
 // (few weight-row tiles) still spread the weight stream over the whole GPU.
 // K % 64 == 0; all base pointers 16-byte aligned; N even for mode 2.
+#ifndef QDB_DEC_STAGES
+#define QDB_DEC_STAGES 3  // ring stages of the <= 64-row (decode) GEMM: 97 KB, 2 CTAs per SM
+#endif
 // bias (optional, f32 [N]) is added to every output (once per element, also
 // under split-K).
 extern "C" cudaError_t qdb_launch_gemm_tc_bias(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y,
@@ -600,7 +603,7 @@ extern "C" cudaError_t qdb_launch_gemm_tc_bias(const uint16_t *W, const uint16_t
             return launch_persist<128, 4, true>(W, Xh, Xl, Y, n, N, K, mode, err, st, bias);
         return launch_tc<128, 4, true>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, bias);
     }
-    if (n <= 64) return launch_tc<64, 6, false>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, nullptr);
+    if (n <= 64) return launch_tc<64, QDB_DEC_STAGES, false>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, nullptr);
     if (QDB_GEMM_PERSIST && splits == 1)
         return launch_persist<128, 4, false>(W, Xh, Xl, Y, n, N, K, mode, err, st, nullptr);
     return launch_tc<128, 4, false>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, nullptr);
@@ -612,10 +615,10 @@ extern "C" cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh,
 }
 
 #ifndef QDB_SPLIT_WAVES
-#define QDB_SPLIT_WAVES 1    // CTAs targeted per SM by split-K
+#define QDB_SPLIT_WAVES 2    // CTAs targeted per SM by split-K (two fit: 3-stage ring)
 #endif
 #ifndef QDB_SPLIT_MIN_KB
-#define QDB_SPLIT_MIN_KB 2   // fewest 64-wide k-blocks one split-K CTA takes
+#define QDB_SPLIT_MIN_KB 1   // fewest 64-wide k-blocks one split-K CTA takes
 #endif
 // Split count for a skinny GEMM: about QDB_SPLIT_WAVES CTAs per SM, each
 // with at least QDB_SPLIT_MIN_KB k-blocks (short CTAs are all set-up).
