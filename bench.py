@@ -644,10 +644,12 @@ def run_streams_ours(args):
         wall = time.perf_counter() - w0
         lc = S.last_chunk()
         toks = sum(S.stats(i)["last_generated"] for i in range(n_local))
-        ctx = np.mean([S.stats(i)["last_prefill_len"] for i in range(n_local)])
+        pls = [S.stats(i)["last_prefill_len"] for i in range(n_local)]
+        ctx = np.mean(pls)
+        ctx_max = max(pls) + max_new
         after_round(rs, fin)
         if record is not None:
-            record.append(dict(ev=ev, wall=wall, toks=toks, ctx=ctx, h2d=h2d, lc=lc,
+            record.append(dict(ev=ev, wall=wall, toks=toks, ctx=ctx, ctx_max=ctx_max, h2d=h2d, lc=lc,
                                audio_s=C4_CHUNK_S * sum(a is not None for a in audio)))
 
     for _ in range(args.warmup):
@@ -702,7 +704,10 @@ def run_streams_ours(args):
                      "frac": round(achieved / peak, 4), "traffic": None, "kernel": "rows_decode",
                      "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                      "bytes_per_launch": int(bytes_step)},
-        "gpu_launches": int(args.steps * (cfg.layers * 9 + 1 + max_new * (cfg.layers * 9 + 5))),
+        # prefill: 9 kernels per layer + prompt rows; greedy step: 9 per layer, +1 (the split
+        # merge) when a row holds more than 512 keys, + embedding, final norm, lm_head, argmax, counter
+        "gpu_launches": int(sum(cfg.layers * 9 + 1 + max_new * (cfg.layers * (9 + (r["ctx_max"] > 512)) + 5)
+                                for r in rec)),
         "clocks": clk, "setup_s": round(setup_s, 1),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -585,6 +585,12 @@ extern "C" cudaError_t qdb_launch_swiglu_split(const float *gu, uint16_t *hi, ui
 // splits > 1 (mode 3 only) divides K across CTAs so that skinny problems
 // (few weight-row tiles) still spread the weight stream over the whole GPU.
 // K % 64 == 0; all base pointers 16-byte aligned; N even for mode 2.
+#ifndef QDB_PF_BN
+#define QDB_PF_BN 128     // activation rows per tile of the persistent (prefill) GEMM
+#endif
+#ifndef QDB_PF_STAGES
+#define QDB_PF_STAGES 4   // its ring stages
+#endif
 #ifndef QDB_DEC_STAGES
 #define QDB_DEC_STAGES 3  // ring stages of the <= 64-row (decode) GEMM: 97 KB, 2 CTAs per SM
 #endif
@@ -605,7 +611,7 @@ extern "C" cudaError_t qdb_launch_gemm_tc_bias(const uint16_t *W, const uint16_t
     }
     if (n <= 64) return launch_tc<64, QDB_DEC_STAGES, false>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, nullptr);
     if (QDB_GEMM_PERSIST && splits == 1)
-        return launch_persist<128, 4, false>(W, Xh, Xl, Y, n, N, K, mode, err, st, nullptr);
+        return launch_persist<QDB_PF_BN, QDB_PF_STAGES, false>(W, Xh, Xl, Y, n, N, K, mode, err, st, nullptr);
     return launch_tc<128, 4, false>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, nullptr);
 }
 
