@@ -13,7 +13,7 @@
 //
 // One CTA per 128 weight rows x BN activation rows. Warp roles:
 //   warp 0       TMA producer: W / Xhi / Xlo K-slices (64 bf16 = 128 B, 128B
-//                swizzle) into an S-stage shared-memory ring (no multicast)
+//                swizzle) into an S-stage shared-memory ring (each CTA loads its own tiles)
 //   warp 1       allocates TMEM; one thread issues tcgen05.mma (M=128, N=BN,
 //                K=16, kind::f16 bf16 x bf16 -> f32), commits stages back
 //   warps 2..5   epilogue: tcgen05.ld of the accumulator (each warp its 32
