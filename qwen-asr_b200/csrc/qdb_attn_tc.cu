@@ -10,10 +10,11 @@
 //
 //   S = Q K^T      A = Q rows (fp16 hi + lo of the f32 q, written by threads),
 //                  B = 128 cached keys (fp16, TMA 2D with 128-byte swizzle)
-//   pass 1         row max m and denominator l over all key tiles
-//   pass 2         recompute S; P = exp(s - m) / l as fp16 hi + lo (threads);
-//                  V^T (dims x keys) transposed into smem by threads;
-//                  O += P V  (A = P, B = V^T), accumulated in TMEM
+//   per key tile  online softmax: row max of S, P = exp(s - m) as fp16 hi +
+//                  lo (threads), the running max raised (O rescaled in
+//                  TMEM) only when it grows by more than 8; V^T (dims x
+//                  keys) transposed into smem by threads; O += P V (A = P,
+//                  B = V^T) in TMEM; O / l in the epilogue
 //
 // All operands are K-major with 128-byte swizzle (the layout the TMA writes
 // for the K tile and the threads write for Q, P and V^T). The activation
@@ -121,6 +122,21 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
+        "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+        "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
+        "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
 }
 
 // Byte offset of 16-byte chunk c (8 fp16 columns) of row r in a 128-row x
@@ -247,62 +263,22 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         return true;
     };
 
-    // ---- pass 1: row max and softmax denominator
-    float m = -INFINITY, l = 0.f;
-#pragma unroll 1
-    for (int kt = 0; kt < ntiles; kt++) {
-        const int k0 = kt * AT_N;
-        if (t == 0 && !s_tile(k0)) s_ok = 0;
-        __syncthreads();
-        if (!s_ok) break;
-        tc_fence_after();
-#pragma unroll 1
-        for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
-            float v[32];
-            tmem_ld32(tS + lane_base + c0, v);
-            float cm = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 32; j++) {
-                const bool ok = row_ok && k0 + c0 + j <= qpos;
-                v[j] = ok ? v[j] * scale : -INFINITY;
-                cm = fmaxf(cm, v[j]);
-            }
-            if (cm != -INFINITY) {
-                const float mn = fmaxf(m, cm);
-                float s = 0.f;
-#pragma unroll
-                for (int j = 0; j < 32; j++) s += (v[j] == -INFINITY) ? 0.f : expf(v[j] - mn);
-                l = (m == -INFINITY ? 0.f : l * expf(m - mn)) + s;
-                m = mn;
-            }
-        }
-        tc_fence_before();
-        __syncthreads();
-    }
-    {  // combine the two column halves of each row
-        __shared__ float cm_m[AT_THREADS], cm_l[AT_THREADS];
-        cm_m[t] = m;
-        cm_l[t] = l;
-        __syncthreads();
-        const float m2 = cm_m[t ^ 128], l2 = cm_l[t ^ 128];
-        const float mn = fmaxf(m, m2);
-        if (mn != -INFINITY) {
-            l = (m == -INFINITY ? 0.f : l * expf(m - mn)) + (m2 == -INFINITY ? 0.f : l2 * expf(m2 - mn));
-            m = mn;
-        }
-    }
-    const float inv_l = l > 0.f ? 1.0f / l : 0.f;
-
-    // ---- pass 2: P = softmax row (exact m, l), O += P V
-    // Once S of a tile is computed the K buffer is free: the V tile is loaded
-    // into it by TMA while the threads write P, then transposed smem -> smem.
+    // ---- one pass over the key tiles (online softmax): per tile the row max
+    // of S, then P = exp(s - m) with the row's running max m, O += P V. m is
+    // raised (and O, l rescaled by exp(m_old - m_new) in TMEM) only when a
+    // tile's max exceeds it by more than RESCALE, so P <= e^RESCALE: numerator
+    // and denominator always share one m, and the rescale is rare after the
+    // first tiles. The epilogue divides by l.
+    constexpr float RESCALE = 8.0f;
+    __shared__ float xch[AT_THREADS];  // the two column halves' tile maxima
+    float m = -INFINITY, l = 0.f;      // running max (same in both halves of a row), this half's sum
 #pragma unroll 1
     for (int kt = 0; kt < ntiles && s_ok; kt++) {
         const int k0 = kt * AT_N;
         if (t == 0) {
             if (!s_tile(k0)) {
                 s_ok = 0;
-            } else {
+            } else {  // the K buffer is free once S is done: V of this tile into it
                 mb_expect(&barK, 2 * AT_TILE);
                 tma_load_2d(Kt, tmV, 0, kv_row0 + k0, &barK);
                 tma_load_2d(Kt + AT_TILE, tmV, 64, kv_row0 + k0, &barK);
@@ -311,26 +287,51 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         __syncthreads();
         if (!s_ok) break;
         tc_fence_after();
+        float v[64];
+        tmem_ld32(tS + lane_base + half * 64, v);
+        tmem_ld32(tS + lane_base + half * 64 + 32, v + 32);
+        float cm = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 64; j++) {
+            const bool ok = row_ok && k0 + half * 64 + j <= qpos;
+            v[j] = ok ? v[j] * scale : -INFINITY;
+            cm = fmaxf(cm, v[j]);
+        }
+        xch[t] = cm;
+        __syncthreads();
+        cm = fmaxf(cm, xch[t ^ 128]);
+        if (cm > m + RESCALE || (m == -INFINITY && cm != -INFINITY)) {
+            if (m != -INFINITY) {  // O holds earlier tiles: rescale this half of the row
+                const float f = expf(m - cm);
+                l *= f;
+                float o[32];
 #pragma unroll 1
-        for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
-            float v[32];
-            tmem_ld32(tS + lane_base + c0, v);
+                for (int c0 = half * 64; c0 < half * 64 + 64; c0 += 32) {
+                    tmem_ld32(tO + lane_base + c0, o);
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-                const bool ok = row_ok && k0 + c0 + j <= qpos;
-                v[j] = ok ? expf(v[j] * scale - m) * inv_l : 0.f;
+                    for (int j = 0; j < 32; j++) o[j] *= f;
+                    tmem_st32(tO + lane_base + c0, o);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             }
+            m = cm;
+        }
 #pragma unroll
-            for (int q8 = 0; q8 < 4; q8++) {
-                const int col = c0 + q8 * 8;  // key column within the tile
-                put8_split(Ph + (col >> 6) * AT_TILE, Pl + (col >> 6) * AT_TILE, r, (col & 63) >> 3, v + q8 * 8);
-            }
+        for (int j = 0; j < 64; j++) {
+            v[j] = v[j] == -INFINITY ? 0.f : expf(v[j] - m);
+            l += v[j];
+        }
+#pragma unroll
+        for (int q8 = 0; q8 < 8; q8++) {
+            const int col = half * 64 + q8 * 8;  // key column within the tile
+            put8_split(Ph + (col >> 6) * AT_TILE, Pl + (col >> 6) * AT_TILE, r, (col & 63) >> 3, v + q8 * 8);
         }
         // V^T: thread t owns dim t; 8 keys per 16-byte chunk; keys past kend -> 0
         if (t == 0 && s_ok) {
             if (!mb_wait(&barK, phK, err)) s_ok = 0;
             phK ^= 1;
         }
+        tc_fence_before();
         __syncthreads();
         if (s_ok) {
             const int d = t & 127;  // dim; keys of half t >> 7
@@ -369,6 +370,11 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
         __syncthreads();
     }
+    // the row's denominator: both halves' sums (same m)
+    xch[t] = l;
+    __syncthreads();
+    l += xch[t ^ 128];
+    const float inv_l = l > 0.f ? 1.0f / l : 0.f;
     // ---- epilogue: O row -> out
     if (s_ok && ntiles > 0) {
         tc_fence_after();
@@ -379,6 +385,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             float v[32];
             tmem_ld32(tO + lane_base + c0, v);
             if (!row_ok) continue;
+#pragma unroll
+            for (int j = 0; j < 32; j++) v[j] *= inv_l;
             if (hi) {  // the bf16 split the O-projection GEMM reads
 #pragma unroll
                 for (int j = 0; j < 32; j += 2) {
