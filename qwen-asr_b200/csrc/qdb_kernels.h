@@ -209,8 +209,10 @@ cudaError_t qdb_launch_prompt_rows(const uint16_t *embed, const int *desc_dev, c
 // step (optional, device): the rows' tokens are read at tokens + *step * n
 // (embed) / written at tokens + *step * n (argmax), and positions advance by
 // *step (qk_rope_append, attn_rows): the form a captured decode step replays.
+// keys (optional, device, [2n] zeros): the vocabulary is split over several
+// CTAs per row, combined through keys (left at zero again).
 cudaError_t qdb_launch_argmax_rows(const float *logits, int n, int V, int mask_eos, int *tokens,
-                                   cudaStream_t st, const int *step = nullptr);
+                                   cudaStream_t st, const int *step = nullptr, unsigned long long *keys = nullptr);
 cudaError_t qdb_launch_embed_rows(const uint16_t *embed, const int *tokens, float *x, int n, int h, int V,
                                   cudaStream_t st, const int *step = nullptr);
 cudaError_t qdb_launch_step_advance(int *step, cudaStream_t st);

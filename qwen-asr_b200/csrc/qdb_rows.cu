@@ -21,6 +21,7 @@ __global__ void __launch_bounds__(RN_THREADS) rmsnorm_rows_kernel(const float *x
     __shared__ float red[RN_THREADS / 32];
     pdl_enter();
     const int t = threadIdx.x;
+
     const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)blockIdx.x * h);
     const int h4 = h >> 2;
     float4 v[RN_VEC];
@@ -350,6 +351,49 @@ __global__ void attn_rows_merge_kernel(const float *part, int S, int Hq, float *
 }
 
 // ---------------------------------------------------------------- argmax / embed
+// Sliced form: gridDim.y CTAs per row each take a slice of the vocabulary and
+// fold its best (value, lowest index) key into keys[row] with a 64-bit
+// atomicMax; the row's last CTA (counter keys[n + row]) writes the token and
+// leaves both words at zero for the next call. Same key, so the same token.
+constexpr int AM_SLICES = 16, AM_THREADS = 256;
+__global__ void __launch_bounds__(AM_THREADS) argmax_rows_sliced_kernel(const float *logits, int V, int mask_eos,
+                                                                         int *tokens, const int *step,
+                                                                         unsigned long long *keys) {
+    pdl_enter();
+    __shared__ unsigned long long red[AM_THREADS / 32];
+    __shared__ bool last;
+    const int row = blockIdx.x, n = gridDim.x;
+    const float *lr = logits + (size_t)row * V;
+    const int per = (V + gridDim.y - 1) / gridDim.y, i0 = blockIdx.y * per, i1 = min(V, i0 + per);
+    unsigned long long best = 0ull;
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+        if (mask_eos && (i == QDB_ENDOFTEXT || i == QDB_IM_END)) continue;
+        const float v = lr[i];
+        if (isnan(v)) continue;
+        const unsigned long long k = argmax_key(v, i);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+        best = t > best ? t : best;
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < AM_THREADS / 32; w++) best = red[w] > best ? red[w] : best;
+        if (best) atomicMax(&keys[row], best);
+        __threadfence();
+        last = atomicAdd(&keys[n + row], 1ull) == (unsigned long long)(gridDim.y - 1);
+        if (last) {
+            __threadfence();
+            const unsigned long long k = atomicExch(&keys[row], 0ull);
+            keys[n + row] = 0ull;
+            tokens[(step ? (size_t)*step * n : 0) + row] = k ? argmax_key_index(k) : 0;
+        }
+    }
+}
+
 __global__ void argmax_rows_kernel(const float *logits, int V, int mask_eos, int *tokens, const int *step) {
     pdl_enter();
     __shared__ unsigned long long red[32];
@@ -464,8 +508,11 @@ extern "C" cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows
 }
 
 extern "C" cudaError_t qdb_launch_argmax_rows(const float *logits, int n, int V, int mask_eos, int *tokens,
-                                              cudaStream_t st, const int *step) {
+                                              cudaStream_t st, const int *step, unsigned long long *keys) {
     if (n <= 0) return cudaSuccess;
+    if (keys)
+        return pdl_launch(argmax_rows_sliced_kernel, dim3(n, AM_SLICES), dim3(AM_THREADS), 0, st, logits, V, mask_eos,
+                          tokens, step, keys);
     return pdl_launch(argmax_rows_kernel, dim3(n), dim3(1024), 0, st, logits, V, mask_eos, tokens, step);
 }
 

@@ -87,6 +87,7 @@ struct RowScratch {
     int *step = nullptr;                    // [1] step counter of a captured batched decode step
     float *LOG = nullptr;  // [cap, V] only for batched decode
     int log_cap = 0;
+    unsigned long long *amax = nullptr;  // [2 * log_cap] sliced-argmax keys and counters (kept at zero)
     float *part = nullptr;
     size_t part_cap = 0;
     QdbRowKV *rowkv = nullptr;
@@ -378,7 +379,7 @@ extern "C" void qdb_model_free(qdb_model *m) {
     cudaFree(m->err); cudaFree(m->tok_dev);
     RowScratch &r = m->rs;
     cudaFree(r.X); cudaFree(r.XH); cudaFree(r.XL); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT);
-    cudaFree(r.LOG); cudaFree(r.part); cudaFree(r.rowkv); cudaFree(r.tok); cudaFree(r.err); cudaFree(r.GU); cudaFree(r.step);
+    cudaFree(r.LOG); cudaFree(r.amax); cudaFree(r.part); cudaFree(r.rowkv); cudaFree(r.tok); cudaFree(r.err); cudaFree(r.GU); cudaFree(r.step);
     cudaFree(r.amaps); cudaFree(r.asegs);
     BatchScratch &b = m->bs;
     cudaFree(b.x); cudaFree(b.qkv); cudaFree(b.gu); cudaFree(b.part); cudaFree(b.stats); cudaFree(b.best);
@@ -801,9 +802,12 @@ static int ensure_rows(qdb_model *m, int n, bool logits) {
     }
     if (logits && n > r.log_cap) {
         cudaFree(r.LOG);
+        cudaFree(r.amax);
         r.LOG = nullptr;
+        r.amax = nullptr;
         r.log_cap = 0;
-        if (dev_alloc(&r.LOG, (size_t)n * m->cfg.vocab)) return -1;
+        if (dev_alloc(&r.LOG, (size_t)n * m->cfg.vocab) || dev_alloc(&r.amax, (size_t)2 * n)) return -1;
+        CK(cudaMemset(r.amax, 0, sizeof(unsigned long long) * 2 * n));
         r.log_cap = n;
     }
     if (n <= 64 && !r.GU && dev_alloc(&r.GU, (size_t)64 * 2 * I)) return -1;
@@ -1053,7 +1057,7 @@ static int batch_tail(qdb_model *m, int n, int *tok_dev, const int *step = nullp
     RowScratch &r = m->rs;
     CK(qdb_launch_rmsnorm_rows(r.X, m->final_norm, r.XH, r.XL, n, m->cfg.hidden, m->cfg.eps, m->st));
     CK(qdb_launch_gemm_tc(m->embed, r.XH, r.XL, r.LOG, n, m->cfg.vocab, m->cfg.hidden, 0, 1, r.err, m->st));
-    CK(qdb_launch_argmax_rows(r.LOG, n, m->cfg.vocab, m->mask_eos, tok_dev, m->st, step));
+    CK(qdb_launch_argmax_rows(r.LOG, n, m->cfg.vocab, m->mask_eos, tok_dev, m->st, step, r.amax));
     return 0;
 }
 
@@ -1291,7 +1295,7 @@ extern "C" int qdb_forward_batch(qdb_session *const *sessions, int n, const floa
     auto graph_key = [&]() {
         return std::vector<const void *>{(const void *)(intptr_t)n, (const void *)(intptr_t)S,
                                          (const void *)(intptr_t)m->mask_eos, m->rope, r.X, r.XH, r.XL, r.QKV, r.Q,
-                                         r.ATT, r.ACT, r.LOG, r.part, r.GU, r.tok, r.err, r.rowkv};
+                                         r.ATT, r.ACT, r.LOG, r.part, r.GU, r.tok, r.err, r.rowkv, r.amax};
     };
     const std::vector<const void *> key = graph_key();
     if (m->fb_exec && key == m->fb_key) {
