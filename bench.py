@@ -978,6 +978,30 @@ def profile_encoder(args):
     enc.close()
 
 
+def profile_prefill(args):
+    """Fixed case for ncu captures of the prefill kernels: one 2048-position
+    prefill of the 1.7B synthetic model (seeded rows), run twice, the second
+    time inside the NVTX range "prefill" (ncu --nvtx --nvtx-include "prefill/")."""
+    import torch
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    synth = ge.load_synth()
+    cfg = synth.PRESETS["1.7b"]
+    ws = synth.WeightSet(cfg, seed=0)
+    model = pkg.Model(ws, device=0, mask_eos=True)
+    s = model.session(2048 + 8)
+    emb = torch.from_numpy(synth.audio_embeddings(cfg, 2048, seed=1)).cuda()
+    for i in range(2):
+        torch.cuda.synchronize()
+        if i == 1:
+            torch.cuda.nvtx.range_push("prefill")
+        s.prefill_device(emb.data_ptr(), 2048, 0)
+        model.sync()
+    torch.cuda.nvtx.range_pop()
+    s.close()
+    model.close()
+
+
 def free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -997,6 +1021,7 @@ def main():
     ap.add_argument("--profile-step", action="store_true", help="small fixed case for ncu (no timing)")
     ap.add_argument("--profile-batch", action="store_true", help="batched-decode case for ncu (no timing)")
     ap.add_argument("--profile-encoder", action="store_true", help="mel + encoder case for ncu (no timing)")
+    ap.add_argument("--profile-prefill", action="store_true", help="1.7B 2048-position prefill for ncu (no timing)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -1013,6 +1038,9 @@ def main():
         return
     if args.profile_encoder:
         profile_encoder(args)
+        return
+    if args.profile_prefill:
+        profile_prefill(args)
         return
     if args.profile_step:
         profile_step(args)
