@@ -12,9 +12,9 @@
 //                  B = 128 cached keys (fp16, TMA 2D with 128-byte swizzle)
 //   per key tile  online softmax: row max of S, P = exp(s - m) as fp16 hi +
 //                  lo (threads), the running max raised (O rescaled in
-//                  TMEM) only when it grows by more than 8; V^T (dims x
-//                  keys) transposed into smem by threads; O += P V (A = P,
-//                  B = V^T) in TMEM; O / l in the epilogue
+//                  TMEM) only when it grows by more than 8; O += P V in TMEM
+//                  with V straight from its TMA tile as an MN-major B operand
+//                  (keys along K, dims along N); O / l in the epilogue
 //
 // All operands are K-major with 128-byte swizzle (the layout the TMA writes
 // for the K tile and the threads write for Q, P and V^T). The activation
@@ -82,6 +82,19 @@ __device__ __forceinline__ u64 sm_desc(uint32_t saddr) {
     u64 d = 0;
     d |= (u64)((saddr >> 4) & 0x3fffu);
     d |= (u64)1 << 16;
+    d |= (u64)(1024 >> 4) << 32;
+    d |= (u64)1 << 46;
+    d |= (u64)2 << 61;
+    return d;
+}
+
+// MN-major operand descriptor, 128-byte swizzle: rows of 128 bytes (64 fp16
+// of the N dimension) along K, 8-row atoms 1024 B apart (stride offset), the
+// next 64 N-elements lbo bytes away (leading offset).
+__device__ __forceinline__ u64 sm_desc_mn(uint32_t saddr, uint32_t lbo) {
+    u64 d = 0;
+    d |= (u64)((saddr >> 4) & 0x3fffu);
+    d |= (u64)((lbo >> 4) & 0x3fffu) << 16;
     d |= (u64)(1024 >> 4) << 32;
     d |= (u64)1 << 46;
     d |= (u64)2 << 61;
@@ -177,7 +190,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
     unsigned char *Qh = sm, *Ql = sm + 2 * AT_TILE;              // [2 dim blocks] each
     unsigned char *Kt = sm + 4 * AT_TILE;                         // [2 dim blocks] (TMA)
     unsigned char *Ph = sm + 6 * AT_TILE, *Pl = sm + 8 * AT_TILE; // [2 key blocks] each
-    unsigned char *Vt = sm + 10 * AT_TILE;                        // [2 key blocks]: rows = dims
 
     // segment = one session's prompt rows; its K/V maps cover all layers
     const QdbAttnSeg sg = segs[blockIdx.z];
@@ -326,7 +338,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             const int col = half * 64 + q8 * 8;  // key column within the tile
             put8_split(Ph + (col >> 6) * AT_TILE, Pl + (col >> 6) * AT_TILE, r, (col & 63) >> 3, v + q8 * 8);
         }
-        // V^T: thread t owns dim t; 8 keys per 16-byte chunk; keys past kend -> 0
+        // V: wait for its tile
         if (t == 0 && s_ok) {
             if (!mb_wait(&barK, phK, err)) s_ok = 0;
             phK ^= 1;
@@ -334,21 +346,15 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         tc_fence_before();
         __syncthreads();
         if (s_ok) {
-            const int d = t & 127;  // dim; keys of half t >> 7
-            const unsigned char *vsrc = Kt + (d >> 6) * AT_TILE;
-            const int vc8 = (d & 63) >> 3, ve = d & 7;
-#pragma unroll 2
-            for (int c = (t >> 7) * 8; c < (t >> 7) * 8 + 8; c++) {
-                uint32_t w[4];
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const int ka = c * 8 + 2 * i;
-                    const uint32_t lo = k0 + ka < kend ? *reinterpret_cast<const uint16_t *>(vsrc + swz(ka, vc8) + ve * 2) : 0u;
-                    const uint32_t hi =
-                        k0 + ka + 1 < kend ? *reinterpret_cast<const uint16_t *>(vsrc + swz(ka + 1, vc8) + ve * 2) : 0u;
-                    w[i] = lo | (hi << 16);
+            // V as loaded is the MN-major B operand already; only the rows past
+            // the last valid key (stale cache memory) are cleared
+            const int nvalid = kend - k0;
+            if (nvalid < AT_N) {
+                for (int i = t; i < (AT_N - nvalid) * 16; i += AT_THREADS) {
+                    const int key = nvalid + (i >> 4), chunk = i & 15;  // 16 chunks of 16 B: 2 dim halves x 8
+                    *reinterpret_cast<uint4 *>(Kt + (chunk >> 3) * AT_TILE + swz(key, chunk & 7)) =
+                        make_uint4(0u, 0u, 0u, 0u);
                 }
-                *reinterpret_cast<uint4 *>(Vt + (c >> 3) * AT_TILE + swz(d, c & 7)) = make_uint4(w[0], w[1], w[2], w[3]);
             }
         }
         fence_async_smem();
@@ -360,9 +366,11 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
             for (int kb = 0; kb < 2; kb++)
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
-                    const u64 bv = sm_desc(su32(Vt + kb * AT_TILE) + k * 32);
-                    mma_f16(tO, sm_desc(su32(Ph + kb * AT_TILE) + k * 32), bv, idesc, (kt | kb | k) ? 1u : 0u);
-                    mma_f16(tO, sm_desc(su32(Pl + kb * AT_TILE) + k * 32), bv, idesc, 1u);
+                    // B = V as loaded: keys along K, dims along N (MN-major)
+                    const u64 bv = sm_desc_mn(su32(Kt) + (kb * 64 + k * 16) * 128, AT_TILE);
+                    const uint32_t id = idesc | (1u << 16);  // bit 16: B is MN-major
+                    mma_f16(tO, sm_desc(su32(Ph + kb * AT_TILE) + k * 32), bv, id, (kt | kb | k) ? 1u : 0u);
+                    mma_f16(tO, sm_desc(su32(Pl + kb * AT_TILE) + k * 32), bv, id, 1u);
                 }
             mma_commit(&barO);
             if (!mb_wait(&barO, phO, err)) s_ok = 0;
@@ -426,7 +434,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn_at() {
 template <int R>
 cudaError_t launch_at(const CUtensorMap *maps, const QdbAttnSeg *segs, int nseg, int max_n, int layer, int Hq, int Hkv,
                       const float *q, float *out, int *err, cudaStream_t st, uint16_t *hi, uint16_t *lo) {
-    const int smem = 12 * AT_TILE + 1024;  // Q hi/lo, K, P hi/lo, V^T + alignment slack
+    const int smem = 10 * AT_TILE + 1024;  // Q hi/lo, K (then V), P hi/lo + alignment slack
     cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     constexpr int QT = AT_M / R;

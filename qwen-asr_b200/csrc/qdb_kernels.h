@@ -182,6 +182,10 @@ cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh, const uint
                                int mode, int splits, int *err, cudaStream_t st);
 cudaError_t qdb_launch_swiglu_split(const float *gu, uint16_t *hi, uint16_t *lo, size_t count, cudaStream_t st);
 int qdb_gemm_tc_splits(int n, int N, int K, int sms);
+// Prefill gate/up + SwiGLU written as the bf16 split [n, N/2] (n > 64).
+extern "C" cudaError_t qdb_launch_gemm_tc_swiglu_split(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl,
+                                                       uint16_t *yhi, uint16_t *ylo, int n, int N, int K, int *err,
+                                                       cudaStream_t st);
 // Same with an optional f32 bias [N] added to every output (once, also under split-K).
 extern "C" cudaError_t qdb_launch_gemm_tc_bias(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y,
                                                int n, int N, int K, int mode, int splits, int *err, cudaStream_t st,

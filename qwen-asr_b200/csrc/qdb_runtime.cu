@@ -82,6 +82,7 @@ struct RowScratch {
     int cap = 0;
     float *X = nullptr, *QKV = nullptr, *Q = nullptr, *ATT = nullptr, *ACT = nullptr;
     uint16_t *XH = nullptr, *XL = nullptr;  // bf16 hi/lo of the current GEMM input [cap, max(h, qd, I)]
+    uint16_t *XH2 = nullptr, *XL2 = nullptr;  // [cap, I]: the SwiGLU split written by the gate/up GEMM (rows > 64)
     float *GU = nullptr;                    // [64, 2I] gate/up sums of split-K decode GEMMs
     int *err = nullptr;                     // [4] device error words of the tensor-core GEMMs
     int *step = nullptr;                    // [1] step counter of a captured batched decode step
@@ -379,7 +380,7 @@ extern "C" void qdb_model_free(qdb_model *m) {
     cudaFree(m->err); cudaFree(m->tok_dev);
     RowScratch &r = m->rs;
     cudaFree(r.X); cudaFree(r.XH); cudaFree(r.XL); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT);
-    cudaFree(r.LOG); cudaFree(r.amax); cudaFree(r.part); cudaFree(r.rowkv); cudaFree(r.tok); cudaFree(r.err); cudaFree(r.GU); cudaFree(r.step);
+    cudaFree(r.XH2); cudaFree(r.XL2); cudaFree(r.LOG); cudaFree(r.amax); cudaFree(r.part); cudaFree(r.rowkv); cudaFree(r.tok); cudaFree(r.err); cudaFree(r.GU); cudaFree(r.step);
     cudaFree(r.amaps); cudaFree(r.asegs);
     BatchScratch &b = m->bs;
     cudaFree(b.x); cudaFree(b.qkv); cudaFree(b.gu); cudaFree(b.part); cudaFree(b.stats); cudaFree(b.best);
@@ -790,13 +791,15 @@ static int ensure_rows(qdb_model *m, int n, bool logits) {
         int cap = r.cap ? r.cap : 64;
         while (cap < n) cap *= 2;
         cudaFree(r.X); cudaFree(r.XH); cudaFree(r.XL); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT);
+        cudaFree(r.XH2); cudaFree(r.XL2);
         r.X = r.QKV = r.Q = r.ATT = r.ACT = nullptr;
-        r.XH = r.XL = nullptr;
+        r.XH = r.XL = r.XH2 = r.XL2 = nullptr;
         r.cap = 0;
         const size_t kmax = std::max<size_t>(std::max<size_t>(h, (size_t)m->qd), I);
         if (dev_alloc(&r.X, cap * h) || dev_alloc(&r.XH, cap * kmax) || dev_alloc(&r.XL, cap * kmax) ||
             dev_alloc(&r.QKV, cap * (size_t)(m->qd + 2 * m->kvd)) || dev_alloc(&r.Q, cap * (size_t)m->qd) ||
-            dev_alloc(&r.ATT, cap * (size_t)m->qd) || dev_alloc(&r.ACT, cap * I))
+            dev_alloc(&r.ATT, cap * (size_t)m->qd) || dev_alloc(&r.ACT, cap * I) || dev_alloc(&r.XH2, cap * I) ||
+            dev_alloc(&r.XL2, cap * I))
             return -1;
         r.cap = cap;
     }
@@ -906,6 +909,12 @@ static int run_rows(qdb_model *m, int n, const PrefillPlan *pf, const QdbRowKV *
             // split-K: gate/up sums into GU, then SwiGLU straight into the bf16 split
             if (gemm(lw.gu, r.GU, 2 * I, h, 0, true)) return -1;
             CK(qdb_launch_swiglu_split(r.GU, r.XH, r.XL, (size_t)n * I, m->st));
+        } else if (n > 64) {
+            // gate/up, SwiGLU and the bf16 split in one GEMM epilogue (into the
+            // second split buffers: the GEMM still reads its input from the first)
+            CK(qdb_launch_gemm_tc_swiglu_split(lw.gu, r.XH, r.XL, r.XH2, r.XL2, n, 2 * I, h, r.err, m->st));
+            CK(qdb_launch_gemm_tc(lw.down, r.XH2, r.XL2, r.X, n, h, I, 1, 1, r.err, m->st));
+            continue;
         } else {
             CK(qdb_launch_gemm_tc(lw.gu, r.XH, r.XL, r.ACT, n, 2 * I, h, 2, 1, r.err, m->st));
             CK(qdb_launch_split_bf16(r.ACT, r.XH, r.XL, (size_t)n * I, m->st));

@@ -336,7 +336,8 @@ bool make_map(CUtensorMap *m, const void *base, int rows, int cols, int box_rows
 // (weight rows m0 + 32q + lane), columns [col0, col0 + BN) (activation rows a0..).
 template <int BN, bool BIAS>
 __device__ __forceinline__ void epilogue_tile(uint32_t tcol, int q, int lane, int m0, int a0, float *__restrict__ Y,
-                                              int n, int N, int mode, const float *__restrict__ bias) {
+                                              int n, int N, int mode, const float *__restrict__ bias,
+                                              uint16_t *__restrict__ ylo) {
     const int wrow = m0 + 32 * q + lane;
     float bb = 0.f;
     if (BIAS) bb = wrow < N ? bias[wrow] : 0.f;
@@ -365,9 +366,19 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tcol, int q, int lane, in
 #pragma unroll
         for (int j = 0; j < 32; j++) {
             const int arow = a0 + c0 + j;
-            if (mode == 2) {
+            if (mode == 2 || mode == 4) {
                 const float u = __shfl_down_sync(0xffffffffu, v[j], 1);
-                if (arow < n && (lane & 1) == 0 && wrow + 1 < N) Y[(size_t)arow * (N / 2) + wrow / 2] = silu_mul(v[j], u);
+                if (arow < n && (lane & 1) == 0 && wrow + 1 < N) {
+                    const size_t at = (size_t)arow * (N / 2) + wrow / 2;
+                    const float g = silu_mul(v[j], u);
+                    if (mode == 2) {
+                        Y[at] = g;
+                    } else {  // the bf16 split the down GEMM reads: hi into Y (as bf16), lo into ylo
+                        const uint16_t hb = f32_to_bf16_rn(g);
+                        reinterpret_cast<uint16_t *>(Y)[at] = hb;
+                        ylo[at] = f32_to_bf16_rn(g - __uint_as_float((uint32_t)hb << 16));
+                    }
+                }
             } else if (arow < n && wrow < N) {
                 float *dst = Y + (size_t)arow * N + wrow;
                 if (mode == 3) atomicAdd(dst, v[j]);
@@ -386,7 +397,7 @@ template <int BN, int S, bool BIAS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_persist_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXh,
                            const __grid_constant__ CUtensorMap tmXl, float *__restrict__ Y, int n, int N, int K,
-                           int mode, int *err, const float *__restrict__ bias) {
+                           int mode, int *err, const float *__restrict__ bias, uint16_t *__restrict__ ylo) {
     constexpr int A_BYTES = TC_BM * TC_BK * 2;
     constexpr int B_BYTES = BN * TC_BK * 2;
     constexpr int STAGE = A_BYTES + 2 * B_BYTES;
@@ -485,7 +496,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (!ok) break;
             tc_fence_after();
             epilogue_tile<BN, BIAS>(tmem + (uint32_t)(b * BN), q, lane, (tile / ny) * TC_BM, (tile % ny) * BN, Y, n, N, mode,
-                              bias);
+                              bias, ylo);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&acc_empty[b])) : "memory");
@@ -531,7 +542,7 @@ cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl,
 #endif
 template <int BN, int S, bool BIAS>
 cudaError_t launch_persist(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,
-                           int mode, int *err, cudaStream_t st, const float *bias) {
+                           int mode, int *err, cudaStream_t st, const float *bias, uint16_t *ylo = nullptr) {
     CUtensorMap mw, mh, ml;
     if (!make_map(&mw, W, N, K, TC_BM) || !make_map(&mh, Xh, n, K, BN) || !make_map(&ml, Xl, n, K, BN))
         return cudaErrorInvalidValue;
@@ -554,7 +565,7 @@ cudaError_t launch_persist(const uint16_t *W, const uint16_t *Xh, const uint16_t
     attr[0].val.programmaticStreamSerializationAllowed = QDB_GEMM_PDL;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_persist_kernel<BN, S, BIAS>, mw, mh, ml, Y, n, N, K, mode, err, bias);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_persist_kernel<BN, S, BIAS>, mw, mh, ml, Y, n, N, K, mode, err, bias, ylo);
 }
 
 }  // namespace
@@ -613,6 +624,18 @@ extern "C" cudaError_t qdb_launch_gemm_tc_bias(const uint16_t *W, const uint16_t
     if (QDB_GEMM_PERSIST && splits == 1)
         return launch_persist<QDB_PF_BN, QDB_PF_STAGES, false>(W, Xh, Xl, Y, n, N, K, mode, err, st, nullptr);
     return launch_tc<128, 4, false>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, nullptr);
+}
+
+// Prefill gate/up with the SwiGLU and the bf16 split fused into the epilogue:
+// interleaved (gate, up) rows of W -> yhi / ylo [n, N/2] bf16 (hi + lo = the
+// SwiGLU value), the input of the down GEMM. n > 64 (persistent kernel), N even.
+extern "C" cudaError_t qdb_launch_gemm_tc_swiglu_split(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl,
+                                                       uint16_t *yhi, uint16_t *ylo, int n, int N, int K, int *err,
+                                                       cudaStream_t st) {
+    if (n <= 64 || (N & 1) || K % TC_BK || !yhi || !ylo) return cudaErrorInvalidValue;
+    if (((uintptr_t)W | (uintptr_t)Xh | (uintptr_t)Xl) & 15) return cudaErrorInvalidValue;
+    return launch_persist<QDB_PF_BN, QDB_PF_STAGES, false>(W, Xh, Xl, reinterpret_cast<float *>(yhi), n, N, K, 4, err,
+                                                          st, nullptr, ylo);
 }
 
 extern "C" cudaError_t qdb_launch_gemm_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n,
