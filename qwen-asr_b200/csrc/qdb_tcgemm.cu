@@ -138,11 +138,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
-template <int BN, int S, bool BIAS>
+template <int BN, int S, bool BIAS, int MODE>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXh,
                    const __grid_constant__ CUtensorMap tmXl, float *__restrict__ Y, int n, int N, int K, int mode,
                    int kb_per, int *err, const float *__restrict__ bias) {
+    if (MODE >= 0) mode = MODE;  // fixed-mode instantiations (decode) compile one store path
     constexpr int A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
     constexpr int B_BYTES = BN * TC_BK * 2;
     constexpr int STAGE = A_BYTES + 2 * B_BYTES;
@@ -509,7 +510,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 }
 
-template <int BN, int S, bool BIAS>
+template <int BN, int S, bool BIAS, int MODE = -1>
 cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,
                       int mode, int splits, int *err, cudaStream_t st, const float *bias) {
     CUtensorMap mw, mh, ml;
@@ -517,7 +518,7 @@ cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl,
         return cudaErrorInvalidValue;
     constexpr int STAGE = TC_BM * TC_BK * 2 + 2 * BN * TC_BK * 2;
     const int smem = S * STAGE + 1024;  // + slack to round the base up to 1024 B
-    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, S, BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<BN, S, BIAS, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid((N + TC_BM - 1) / TC_BM, (n + BN - 1) / BN);
     const int nk = K / TC_BK;
@@ -533,7 +534,7 @@ cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl,
     attr[0].val.programmaticStreamSerializationAllowed = QDB_GEMM_PDL;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, S, BIAS>, mw, mh, ml, Y, n, N, K, mode, kb_per, err, bias);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, S, BIAS, MODE>, mw, mh, ml, Y, n, N, K, mode, kb_per, err, bias);
 }
 
 
@@ -602,6 +603,9 @@ extern "C" cudaError_t qdb_launch_swiglu_split(const float *gu, uint16_t *hi, ui
 #ifndef QDB_PF_STAGES
 #define QDB_PF_STAGES 4   // its ring stages
 #endif
+#ifndef QDB_DEC_FIXED_MODE
+#define QDB_DEC_FIXED_MODE 1  // decode GEMMs as fixed-mode instantiations
+#endif
 #ifndef QDB_DEC_STAGES
 #define QDB_DEC_STAGES 3  // ring stages of the <= 64-row (decode) GEMM: 97 KB, 2 CTAs per SM
 #endif
@@ -620,7 +624,17 @@ extern "C" cudaError_t qdb_launch_gemm_tc_bias(const uint16_t *W, const uint16_t
             return launch_persist<128, 4, true>(W, Xh, Xl, Y, n, N, K, mode, err, st, bias);
         return launch_tc<128, 4, true>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, bias);
     }
-    if (n <= 64) return launch_tc<64, QDB_DEC_STAGES, false>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, nullptr);
+    if (n <= 64) {
+        if (QDB_DEC_FIXED_MODE) {
+            switch (mode) {
+                case 0: return launch_tc<64, QDB_DEC_STAGES, false, 0>(W, Xh, Xl, Y, n, N, K, 0, splits, err, st, nullptr);
+                case 1: return launch_tc<64, QDB_DEC_STAGES, false, 1>(W, Xh, Xl, Y, n, N, K, 1, splits, err, st, nullptr);
+                case 3: return launch_tc<64, QDB_DEC_STAGES, false, 3>(W, Xh, Xl, Y, n, N, K, 3, splits, err, st, nullptr);
+                default: break;
+            }
+        }
+        return launch_tc<64, QDB_DEC_STAGES, false>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, nullptr);
+    }
     if (QDB_GEMM_PERSIST && splits == 1)
         return launch_persist<QDB_PF_BN, QDB_PF_STAGES, false>(W, Xh, Xl, Y, n, N, K, mode, err, st, nullptr);
     return launch_tc<128, 4, false>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, nullptr);
