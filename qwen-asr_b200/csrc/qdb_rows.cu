@@ -122,7 +122,10 @@ __global__ void qk_rope_append_kernel(const float *qkv, float *q_out, const QdbR
 // the unnormalised partial (m, l, o[128]) of each query head; the merge
 // kernel combines the splits (same online-softmax algebra as
 // qwen_causal_attention, qwen_asr_kernels.c:1050-1141).
-constexpr int AR_WARPS = 8, AR_KEYS = 8;
+#ifndef QDB_AR_WARPS
+#define QDB_AR_WARPS 8  // warps per unit CTA (each takes AR_KEYS keys of a chunk)
+#endif
+constexpr int AR_WARPS = QDB_AR_WARPS, AR_KEYS = 8;
 
 // The unit is computed from a shared-memory ring: the unit's K and V rows are
 // contiguous in the cache, so thread 0 streams them in 64-key chunks with
@@ -136,7 +139,7 @@ constexpr int AR_WARPS = 8, AR_KEYS = 8;
 #ifndef QDB_AR_MINB
 #define QDB_AR_MINB 3  // CTAs per SM the register budget is sized for
 #endif
-constexpr int AB_STAGES = QDB_AR_STAGES, AB_KEYS = 64, AB_HALF = AB_KEYS * QDB_HD * 2, AB_STAGE = 2 * AB_HALF;
+constexpr int AB_STAGES = QDB_AR_STAGES, AB_KEYS = AR_WARPS * AR_KEYS, AB_HALF = AB_KEYS * QDB_HD * 2, AB_STAGE = 2 * AB_HALF;
 typedef unsigned long long u64r;
 __device__ __forceinline__ uint32_t su32r(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
