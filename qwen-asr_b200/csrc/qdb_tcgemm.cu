@@ -394,11 +394,12 @@ __device__ __forceinline__ void epilogue_tile(uint32_t tcol, int q, int lane, in
 // the CTAs of a wave share weight tiles in L2). The TMA ring runs on across
 // tiles, and the accumulator is double-buffered in TMEM (2 x BN columns):
 // the MMA warp fills one buffer while the epilogue warps drain the other.
-template <int BN, int S, bool BIAS>
+template <int BN, int S, bool BIAS, int MODE>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_persist_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXh,
                            const __grid_constant__ CUtensorMap tmXl, float *__restrict__ Y, int n, int N, int K,
                            int mode, int *err, const float *__restrict__ bias, uint16_t *__restrict__ ylo) {
+    if (MODE >= 0) mode = MODE;  // fixed-mode instantiations compile one store path
     constexpr int A_BYTES = TC_BM * TC_BK * 2;
     constexpr int B_BYTES = BN * TC_BK * 2;
     constexpr int STAGE = A_BYTES + 2 * B_BYTES;
@@ -541,7 +542,7 @@ cudaError_t launch_tc(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl,
 #ifndef QDB_GEMM_PERSIST
 #define QDB_GEMM_PERSIST 1  // prefill shapes: persistent CTAs with a double-buffered TMEM accumulator
 #endif
-template <int BN, int S, bool BIAS>
+template <int BN, int S, bool BIAS, int MODE = -1>
 cudaError_t launch_persist(const uint16_t *W, const uint16_t *Xh, const uint16_t *Xl, float *Y, int n, int N, int K,
                            int mode, int *err, cudaStream_t st, const float *bias, uint16_t *ylo = nullptr) {
     CUtensorMap mw, mh, ml;
@@ -550,7 +551,7 @@ cudaError_t launch_persist(const uint16_t *W, const uint16_t *Xh, const uint16_t
     constexpr int STAGE = TC_BM * TC_BK * 2 + 2 * BN * TC_BK * 2;
     const int smem = S * STAGE + 1024;
     cudaError_t e =
-        cudaFuncSetAttribute(tc_gemm_persist_kernel<BN, S, BIAS>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaFuncSetAttribute(tc_gemm_persist_kernel<BN, S, BIAS, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
@@ -566,7 +567,7 @@ cudaError_t launch_persist(const uint16_t *W, const uint16_t *Xh, const uint16_t
     attr[0].val.programmaticStreamSerializationAllowed = QDB_GEMM_PDL;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tc_gemm_persist_kernel<BN, S, BIAS>, mw, mh, ml, Y, n, N, K, mode, err, bias, ylo);
+    return cudaLaunchKernelEx(&cfg, tc_gemm_persist_kernel<BN, S, BIAS, MODE>, mw, mh, ml, Y, n, N, K, mode, err, bias, ylo);
 }
 
 }  // namespace
@@ -603,6 +604,9 @@ extern "C" cudaError_t qdb_launch_swiglu_split(const float *gu, uint16_t *hi, ui
 #ifndef QDB_PF_STAGES
 #define QDB_PF_STAGES 4   // its ring stages
 #endif
+#ifndef QDB_PF_FIXED_MODE
+#define QDB_PF_FIXED_MODE 1  // prefill GEMMs as fixed-mode instantiations
+#endif
 #ifndef QDB_DEC_FIXED_MODE
 #define QDB_DEC_FIXED_MODE 1  // decode GEMMs as fixed-mode instantiations
 #endif
@@ -635,8 +639,15 @@ extern "C" cudaError_t qdb_launch_gemm_tc_bias(const uint16_t *W, const uint16_t
         }
         return launch_tc<64, QDB_DEC_STAGES, false>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, nullptr);
     }
-    if (QDB_GEMM_PERSIST && splits == 1)
+    if (QDB_GEMM_PERSIST && splits == 1) {
+        // fixed modes only at prefill row counts: the decode-size logits GEMM
+        // (n <= 64, mode 0) measured ~0.3% slower on its fixed-mode build
+        if (QDB_PF_FIXED_MODE && n > 64 && mode == 0)
+            return launch_persist<QDB_PF_BN, QDB_PF_STAGES, false, 0>(W, Xh, Xl, Y, n, N, K, 0, err, st, nullptr);
+        if (QDB_PF_FIXED_MODE && n > 64 && mode == 1)
+            return launch_persist<QDB_PF_BN, QDB_PF_STAGES, false, 1>(W, Xh, Xl, Y, n, N, K, 1, err, st, nullptr);
         return launch_persist<QDB_PF_BN, QDB_PF_STAGES, false>(W, Xh, Xl, Y, n, N, K, mode, err, st, nullptr);
+    }
     return launch_tc<128, 4, false>(W, Xh, Xl, Y, n, N, K, mode, splits, err, st, nullptr);
 }
 
@@ -648,6 +659,9 @@ extern "C" cudaError_t qdb_launch_gemm_tc_swiglu_split(const uint16_t *W, const 
                                                        cudaStream_t st) {
     if (n <= 64 || (N & 1) || K % TC_BK || !yhi || !ylo) return cudaErrorInvalidValue;
     if (((uintptr_t)W | (uintptr_t)Xh | (uintptr_t)Xl) & 15) return cudaErrorInvalidValue;
+    if (QDB_PF_FIXED_MODE)
+        return launch_persist<QDB_PF_BN, QDB_PF_STAGES, false, 4>(W, Xh, Xl, reinterpret_cast<float *>(yhi), n, N, K, 4,
+                                                                 err, st, nullptr, ylo);
     return launch_persist<QDB_PF_BN, QDB_PF_STAGES, false>(W, Xh, Xl, reinterpret_cast<float *>(yhi), n, N, K, 4, err,
                                                           st, nullptr, ylo);
 }
