@@ -124,11 +124,13 @@ int qdb_attn_kv_map(void *map, const uint16_t *cache, int L, int Hkv, int cap);
 cudaError_t qdb_launch_attn_prefill_tc(const void *maps, const QdbAttnSeg *segs, int nseg, int max_n, int layer,
                                        int Hq, int Hkv, const float *q, float *out, int *err, cudaStream_t st,
                                        uint16_t *hi = nullptr, uint16_t *lo = nullptr);
-// Independent rows (one query each) over per-row caches.
+// Independent rows (one query each) over per-row caches. cnt (optional,
+// [n * Hkv], all zero and left at zero): the last split of each unit merges
+// the partials itself; without it a merge launch follows when splits > 1.
 cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
                                  int n, int Hq, int Hkv, int splits, float *part, float *out,
                                  cudaStream_t st, int *err = nullptr, const int *step = nullptr,
-                                 uint16_t *hi = nullptr, uint16_t *lo = nullptr);
+                                 uint16_t *hi = nullptr, uint16_t *lo = nullptr, unsigned *cnt = nullptr);
 // ---- persistent batched decode step (qdb_bstep.cu) ----
 // One decode position of B <= 64 independent utterances in one cooperative
 // launch. Activation buffers are [feature][Bp] f32 (utterance = column).

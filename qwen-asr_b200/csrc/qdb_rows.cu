@@ -143,12 +143,37 @@ constexpr int AB_STAGES = QDB_AR_STAGES, AB_KEYS = AR_WARPS * AR_KEYS, AB_HALF =
 typedef unsigned long long u64r;
 __device__ __forceinline__ uint32_t su32r(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
+// Combines the S unnormalised partials (m, l, o[128]) of one query head at
+// dimension dd (L2 reads: other CTAs wrote them) and stores the normalised
+// output as f32 or as the bf16 hi/lo split of the O-projection input.
+__device__ __forceinline__ void attn_merge_store(const float *src, int S, int dd, size_t at, float *out, uint16_t *hi,
+                                                 uint16_t *lo) {
+    float M = -INFINITY;
+    for (int s = 0; s < S; s++) M = fmaxf(M, __ldcg(src + s * (2 + QDB_HD)));
+    float L = 0.f, O = 0.f;
+    for (int s = 0; s < S; s++) {
+        const float ms = __ldcg(src + s * (2 + QDB_HD));
+        if (ms == -INFINITY) continue;
+        const float f = expf(ms - M);
+        L += __ldcg(src + s * (2 + QDB_HD) + 1) * f;
+        O += __ldcg(src + s * (2 + QDB_HD) + 2 + dd) * f;
+    }
+    const float v = L > 0.f ? O / L : 0.f;
+    if (hi) {
+        const uint16_t b = f32_to_bf16_rn(v);
+        hi[at] = b;
+        lo[at] = f32_to_bf16_rn(v - __uint_as_float((uint32_t)b << 16));
+    } else {
+        out[at] = v;
+    }
+}
+
 template <int R>
 __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AR_MINB) attn_rows_bulk_kernel(const float *q, const QdbRowKV *rows,
                                                                          int row_pos_offset, int layer, int Hq,
                                                                          int Hkv, int S, float *part, int *err,
                                                                          const int *step, float *out, uint16_t *hi,
-                                                                         uint16_t *lo) {
+                                                                         uint16_t *lo, unsigned *cnt) {
     pdl_enter();
     extern __shared__ __align__(128) unsigned char ring[];
     __shared__ __align__(16) float qs[R][QDB_HD];
@@ -325,32 +350,290 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AR_MINB) attn_rows_bulk_ker
         }
         dst[2 + dd] = O;
     }
+    if (S == 1 || !cnt) return;
+    // The unit's last split to finish (counter cnt[row * Hkv + g], left at
+    // zero) merges the S partials: no separate merge launch.
+    __shared__ int last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        last = atomicAdd(&cnt[blockIdx.x], 1u) == (unsigned)(S - 1);
+        if (last) cnt[blockIdx.x] = 0u;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int t = threadIdx.x; t < R * QDB_HD; t += blockDim.x) {
+        const int h = t / QDB_HD, dd = t % QDB_HD;
+        attn_merge_store(part + ((size_t)row * Hq + g * R + h) * S * (2 + QDB_HD), S, dd,
+                         (size_t)row * Hq * QDB_HD + (size_t)(g * R + h) * QDB_HD + dd, out, hi, lo);
+    }
+}
+
+// ---------------------------------------------------------------- fragment (MMA) form
+// The same unit (row, KV head g, split s) on the tensor cores' warp-level
+// MMA (m16n8k16, f16 in, f32 accumulate): the unit is bound by instruction
+// issue in the lane-dot form above (~160 instructions per KB of K/V), and
+// fragments do the q.K and p.V products in a few instructions per 8 x 16
+// tile. Precision: K and V are the cache's fp16 values exactly; q and p are
+// carried as fp16 hi + lo pairs (two MMAs each, ~22 significant bits), so the
+// scores and the output match the f32 form to ~1e-6 relative.
+// Layout: each chunk's 64 K and V rows are copied in 16-byte pieces
+// (cp.async) into a 272-byte row stride (conflict-free ldmatrix); warp w scores keys [8w, 8w + 8) with the R
+// query heads as MMA rows, every warp runs the same softmax over the chunk's
+// 64 x R scores (shared memory), and warp w accumulates output dims
+// [16w, 16w + 16) (p as the A operand, V through ldmatrix.trans).
+#ifndef QDB_AR_MMA
+#define QDB_AR_MMA 1  // fragment form for the batched-decode attention units
+#endif
+#ifndef QDB_AM_MINB
+#define QDB_AM_MINB 3  // CTAs per SM the fragment form's register budget is sized for
+#endif
+#ifndef QDB_AM_STAGES
+#define QDB_AM_STAGES 2  // chunk slots of the fragment form (34 KB each)
+#endif
+constexpr int AM_STAGES = QDB_AM_STAGES;
+constexpr int AM_LDB = (QDB_HD + 8) * 2;             // padded row stride in bytes (272)
+constexpr int AM_HALF = AB_KEYS * AM_LDB, AM_STAGE = 2 * AM_HALF;
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+    // rows 8..15 of A are zero (a1 = a3 = 0): only rows 0..7 carry query heads
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// (x, y) as packed fp16 hi and the fp16 residual lo: x ~ hi.x + lo.x
+__device__ __forceinline__ void split_h2(float x, float y, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __floats2half2_rn(x, y);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x - hf.x, y - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+template <int R>
+__global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kernel(const float *q, const QdbRowKV *rows,
+                                                                        int row_pos_offset, int layer, int Hq,
+                                                                        int Hkv, int S, float *part, int *err,
+                                                                        const int *step, float *out, uint16_t *hi,
+                                                                        uint16_t *lo, unsigned *cnt) {
+    static_assert(AR_WARPS * 16 == QDB_HD && AR_WARPS * 8 == AB_KEYS && R <= 8, "fragment form shape");
+    constexpr int PLD = AB_KEYS + 8;  // p row stride in halves (144 bytes: conflict-free ldmatrix)
+    pdl_enter();
+    extern __shared__ __align__(128) unsigned char ring[];
+    constexpr int QLD = QDB_HD + 8;  // q row stride in halves (272 bytes)
+    // q and p of the chunk as fp16 hi / lo rows; row R is zeros, and the
+    // ldmatrix lanes of MMA rows R..7 all point at it
+    __shared__ __align__(16) uint16_t qsm[2][R + 1][QLD];
+    __shared__ __align__(16) uint16_t ps[2][R + 1][PLD];
+    __shared__ float smax[AR_WARPS][R], ssum[AR_WARPS][R];
+    __shared__ int last;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g4 = lane >> 2, t4 = lane & 3;
+    const int row = blockIdx.x / Hkv, g = blockIdx.x % Hkv, s = blockIdx.y;
+    const QdbRowKV rk = rows[row];
+    const int pos = rk.pos + row_pos_offset + (step ? *step : 0);
+    const int ctx = pos + 1;
+    const int per = (ctx + S - 1) / S;
+    const int p0 = s * per, p1 = min(ctx, p0 + per);
+    const int nch = p1 > p0 ? (p1 - p0 + AB_KEYS - 1) / AB_KEYS : 0;
+    const size_t head_base = ((size_t)layer * Hkv + g) * (size_t)rk.cap * QDB_HD;
+    // this thread's 16-byte pieces: piece tp of keys tk, tk + 16, tk + 32, tk + 48
+    constexpr int PIECES = QDB_HD * 2 / 16, KSTEP = AR_WARPS * 32 / PIECES;
+    const int tk = threadIdx.x / PIECES, tp = threadIdx.x % PIECES;
+    const uint16_t *kc = rk.kc + head_base + (size_t)tk * QDB_HD + tp * 8;
+    const uint16_t *vc = rk.vc + head_base + (size_t)tk * QDB_HD + tp * 8;
+    const uint32_t sdst = su32r(ring) + tk * AM_LDB + tp * 16;
+    auto issue = [&](int c) {  // one cp.async commit group per chunk slot (empty past the last chunk)
+        if (c < nch) {
+            const int k0 = p0 + c * AB_KEYS, nk = min(AB_KEYS, p1 - k0);
+            const uint32_t d = sdst + (uint32_t)(c % AM_STAGES) * AM_STAGE;
+#pragma unroll
+            for (int j = 0; j < AB_KEYS / KSTEP; j++) {
+                if (tk + j * KSTEP < nk) {
+                    const size_t src = (size_t)(k0 + j * KSTEP) * QDB_HD;
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + j * KSTEP * AM_LDB),
+                                 "l"(kc + src)
+                                 : "memory");
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + AM_HALF + j * KSTEP * AM_LDB),
+                                 "l"(vc + src)
+                                 : "memory");
+                }
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    for (int c = 0; c < AM_STAGES; c++) issue(c);
+    for (int i = threadIdx.x; i < 2 * (R + 1) * PLD; i += blockDim.x) (&ps[0][0][0])[i] = 0;
+    for (int i = threadIdx.x; i < (R + 1) * QDB_HD / 2; i += blockDim.x) {  // q as hi / lo pairs
+        const int h = i / (QDB_HD / 2), d = (i % (QDB_HD / 2)) * 2;
+        uint32_t qh = 0u, ql = 0u;
+        if (h < R) {
+            const float2 v =
+                *reinterpret_cast<const float2 *>(q + (size_t)row * Hq * QDB_HD + (size_t)(g * R + h) * QDB_HD + d);
+            split_h2(v.x, v.y, qh, ql);
+        }
+        *reinterpret_cast<uint32_t *>(&qsm[0][h][d]) = qh;
+        *reinterpret_cast<uint32_t *>(&qsm[1][h][d]) = ql;
+    }
+    // scores in log2 units: p = 2^(s' - m'), s' = q.k / sqrt(128) x log2(e)
+    const float scale2 = 1.4426950408889634f / sqrtf((float)QDB_HD);
+    float m = -INFINITY, l = 0.f;
+    float o[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    const int mi = lane >> 3;
+    const uint32_t kb = su32r(ring) + (warp * 8 + (lane & 7)) * AM_LDB + mi * 16;
+    const uint32_t vb = su32r(ring) + AM_HALF + ((mi & 1) * 8 + (lane & 7)) * AM_LDB + (warp * 16 + (mi >> 1) * 8) * 2;
+    const int arow = (lane & 7) < R ? (lane & 7) : R;  // MMA row of this ldmatrix lane (R: the zero row)
+    const uint32_t pb = su32r(&ps[0][arow][(mi & 1) * 8]);  // x2: cols +0 (lanes 0-7) / +8 (lanes 8-15)
+    const uint32_t qb = su32r(&qsm[0][arow][mi * 8]);       // x4: cols +0, +8 of k-step 2 k2 and of 2 k2 + 1
+    for (int c = 0; c < nch; c++) {
+        const uint32_t so = (uint32_t)(c % AM_STAGES) * AM_STAGE;
+        const int k0 = p0 + c * AB_KEYS, nk = min(AB_KEYS, p1 - k0);
+        if (nk < AB_KEYS) {  // rows past the last key: zero V (p = 0 must not meet stale non-finite values)
+            unsigned char *st = ring + so;
+            for (int i = threadIdx.x; i < (AB_KEYS - nk) * PIECES; i += blockDim.x)
+                *reinterpret_cast<uint4 *>(st + AM_HALF + (size_t)(nk + i / PIECES) * AM_LDB + (i % PIECES) * 16) =
+                    make_uint4(0u, 0u, 0u, 0u);
+        }
+        // this thread's copies of chunk c are done (later slots may still be
+        // in flight); the barrier makes every thread's copies visible
+        asm volatile("cp.async.wait_group %0;" ::"n"(AM_STAGES - 1) : "memory");
+        __syncthreads();
+        // 1. scores of keys [8 warp, 8 warp + 8) and their max per head
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k2 = 0; k2 < 4; k2++) {
+            uint32_t b[4], ah[4], al[4];
+            ldsm_x4(b, kb + so + k2 * 64);
+            ldsm_x4(ah, qb + k2 * 64);
+            ldsm_x4(al, qb + k2 * 64 + (R + 1) * QLD * 2);
+            mma16816(sc, ah[0], ah[1], b[0], b[1]);
+            mma16816(sc, al[0], al[1], b[0], b[1]);
+            mma16816(sc, ah[2], ah[3], b[2], b[3]);
+            mma16816(sc, al[2], al[3], b[2], b[3]);
+        }
+        const int kl = warp * 8 + t4 * 2;
+        const float s0 = kl < nk ? sc[0] * scale2 : -INFINITY, s1 = kl + 1 < nk ? sc[1] * scale2 : -INFINITY;
+        float lm = fmaxf(s0, s1);
+        lm = fmaxf(lm, __shfl_xor_sync(0xffffffffu, lm, 1));
+        lm = fmaxf(lm, __shfl_xor_sync(0xffffffffu, lm, 2));
+        if (g4 < R && t4 == 0) smax[warp][g4] = lm;
+        __syncthreads();
+        // 2. p of these keys under the chunk's running max; partial sums
+        float corr = 1.f;
+        if (g4 < R) {
+            float mc = smax[0][g4];
+#pragma unroll
+            for (int w = 1; w < AR_WARPS; w++) mc = fmaxf(mc, smax[w][g4]);
+            const float mn = fmaxf(m, mc);  // finite: every chunk holds a key
+            corr = exp2f(m - mn);
+            m = mn;
+            const float e0 = exp2f(s0 - mn), e1 = exp2f(s1 - mn);
+            float sum = e0 + e1;
+            sum += __shfl_xor_sync(0xfu << (lane & 28), sum, 1);
+            sum += __shfl_xor_sync(0xfu << (lane & 28), sum, 2);
+            if (t4 == 0) ssum[warp][g4] = sum;
+            uint32_t h2, l2;
+            split_h2(e0, e1, h2, l2);
+            *reinterpret_cast<uint32_t *>(&ps[0][g4][kl]) = h2;
+            *reinterpret_cast<uint32_t *>(&ps[1][g4][kl]) = l2;
+        }
+        __syncthreads();
+        // 3. o[:, 16 warp .. 16 warp + 16) = corr o + p V
+        if (g4 < R) {
+            float sum = ssum[0][g4];
+#pragma unroll
+            for (int w = 1; w < AR_WARPS; w++) sum += ssum[w][g4];
+            l = l * corr + sum;
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) o[nt][e] *= corr;
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++) {
+            uint32_t b[4], ah[2], al[2];
+            ldsm_x4_t(b, vb + so + ks * 16 * AM_LDB);
+            asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+                         : "=r"(ah[0]), "=r"(ah[1])
+                         : "r"(pb + ks * 32));
+            asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+                         : "=r"(al[0]), "=r"(al[1])
+                         : "r"(pb + ks * 32 + (R + 1) * PLD * 2));
+            mma16816(o[0], ah[0], ah[1], b[0], b[1]);
+            mma16816(o[0], al[0], al[1], b[0], b[1]);
+            mma16816(o[1], ah[0], ah[1], b[2], b[3]);
+            mma16816(o[1], al[0], al[1], b[2], b[3]);
+        }
+        __syncthreads();  // the stage, p and the partial maxima / sums are free
+        issue(c + AM_STAGES);
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    // lane (g4 < R) holds head g4 at dims 16 warp + 8 nt + 2 t4 + {0, 1}
+    if (g4 < R) {
+        const int h = g4;
+#pragma unroll
+        for (int nt = 0; nt < 2; nt++) {
+            const int dd = warp * 16 + nt * 8 + t4 * 2;
+            if (S == 1) {
+                const float inv = l > 0.f ? 1.f / l : 0.f;
+                const size_t at = (size_t)row * Hq * QDB_HD + (size_t)(g * R + h) * QDB_HD + dd;
+                const float v0 = o[nt][0] * inv, v1 = o[nt][1] * inv;
+                if (hi) {
+                    const uint16_t b0 = f32_to_bf16_rn(v0), b1 = f32_to_bf16_rn(v1);
+                    hi[at] = b0;
+                    hi[at + 1] = b1;
+                    lo[at] = f32_to_bf16_rn(v0 - __uint_as_float((uint32_t)b0 << 16));
+                    lo[at + 1] = f32_to_bf16_rn(v1 - __uint_as_float((uint32_t)b1 << 16));
+                } else {
+                    out[at] = v0;
+                    out[at + 1] = v1;
+                }
+            } else {
+                // partial in natural-log units, as the merge expects
+                float *dst = part + (((size_t)row * Hq + g * R + h) * S + s) * (2 + QDB_HD);
+                if (warp == 0 && nt == 0 && t4 == 0) {
+                    dst[0] = m * 0.6931471805599453f;
+                    dst[1] = l;
+                }
+                dst[2 + dd] = o[nt][0];
+                dst[3 + dd] = o[nt][1];
+            }
+        }
+    }
+    if (S == 1 || !cnt) return;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        last = atomicAdd(&cnt[blockIdx.x], 1u) == (unsigned)(S - 1);
+        if (last) cnt[blockIdx.x] = 0u;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int t = threadIdx.x; t < R * QDB_HD; t += blockDim.x) {
+        const int h = t / QDB_HD, dd = t % QDB_HD;
+        attn_merge_store(part + ((size_t)row * Hq + g * R + h) * S * (2 + QDB_HD), S, dd,
+                         (size_t)row * Hq * QDB_HD + (size_t)(g * R + h) * QDB_HD + dd, out, hi, lo);
+    }
 }
 
 // hi/lo (optional): write the bf16 split the O-projection GEMM reads instead of f32 out.
 __global__ void attn_rows_merge_kernel(const float *part, int S, int Hq, float *out, uint16_t *hi, uint16_t *lo) {
     pdl_enter();
     const int row = blockIdx.x, h = blockIdx.y, dd = threadIdx.x;
-    const float *src = part + ((size_t)row * Hq + h) * S * (2 + QDB_HD);
-    float M = -INFINITY;
-    for (int s = 0; s < S; s++) M = fmaxf(M, src[s * (2 + QDB_HD)]);
-    float L = 0.f, O = 0.f;
-    for (int s = 0; s < S; s++) {
-        const float ms = src[s * (2 + QDB_HD)];
-        if (ms == -INFINITY) continue;
-        const float f = expf(ms - M);
-        L += src[s * (2 + QDB_HD) + 1] * f;
-        O += src[s * (2 + QDB_HD) + 2 + dd] * f;
-    }
-    const float v = L > 0.f ? O / L : 0.f;
-    const size_t at = (size_t)row * Hq * QDB_HD + (size_t)h * QDB_HD + dd;
-    if (hi) {
-        const uint16_t b = f32_to_bf16_rn(v);
-        hi[at] = b;
-        lo[at] = f32_to_bf16_rn(v - __uint_as_float((uint32_t)b << 16));
-    } else {
-        out[at] = v;
-    }
+    attn_merge_store(part + ((size_t)row * Hq + h) * S * (2 + QDB_HD), S, dd,
+                     (size_t)row * Hq * QDB_HD + (size_t)h * QDB_HD + dd, out, hi, lo);
 }
 
 // ---------------------------------------------------------------- argmax / embed
@@ -482,31 +765,39 @@ extern "C" cudaError_t qdb_launch_qk_rope_append_single(const float *qkv, float 
 template <int R>
 static cudaError_t attn_rows_launch(dim3 grid, const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
                                     int Hq, int Hkv, int S, float *part, int *err, cudaStream_t st, const int *step,
-                                    float *out, uint16_t *hi, uint16_t *lo) {
+                                    float *out, uint16_t *hi, uint16_t *lo, unsigned *cnt) {
+    if (QDB_AR_MMA && (S == 1 || cnt)) {
+        const int smem = AM_STAGES * AM_STAGE;
+        cudaError_t e =
+            cudaFuncSetAttribute(attn_rows_mma_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        return pdl_launch(attn_rows_mma_kernel<R>, grid, dim3(AR_WARPS * 32), (size_t)smem, st, q, rows,
+                          row_pos_offset, layer, Hq, Hkv, S, part, err, step, out, hi, lo, cnt);
+    }
     const int smem = AB_STAGES * AB_STAGE;
     cudaError_t e = cudaFuncSetAttribute(attn_rows_bulk_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     return pdl_launch(attn_rows_bulk_kernel<R>, grid, dim3(AR_WARPS * 32), (size_t)smem, st, q, rows, row_pos_offset,
-                      layer, Hq, Hkv, S, part, err, step, out, hi, lo);
+                      layer, Hq, Hkv, S, part, err, step, out, hi, lo, cnt);
 }
 
 extern "C" cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
                                             int n, int Hq, int Hkv, int S, float *part, float *out,
                                             cudaStream_t st, int *err, const int *step, uint16_t *hi,
-                                            uint16_t *lo) {
+                                            uint16_t *lo, unsigned *cnt) {
     if (n <= 0) return cudaSuccess;
-    dim3 grid(n * Hkv, S);
     cudaError_t e0;
+    dim3 grid(n * Hkv, S);
     switch (Hq / Hkv) {
-        case 1: e0 = attn_rows_launch<1>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo); break;
-        case 2: e0 = attn_rows_launch<2>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo); break;
-        case 4: e0 = attn_rows_launch<4>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo); break;
-        case 8: e0 = attn_rows_launch<8>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo); break;
+        case 1: e0 = attn_rows_launch<1>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo, cnt); break;
+        case 2: e0 = attn_rows_launch<2>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo, cnt); break;
+        case 4: e0 = attn_rows_launch<4>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo, cnt); break;
+        case 8: e0 = attn_rows_launch<8>(grid, q, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo, cnt); break;
         default: return cudaErrorInvalidValue;
     }
     if (e0 != cudaSuccess) return e0;
     cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess || S == 1) return e;  // S == 1: the units wrote the output
+    if (e != cudaSuccess || S == 1 || cnt) return e;  // S == 1 or cnt: the units wrote the output
     return pdl_launch(attn_rows_merge_kernel, dim3(n, Hq), dim3(QDB_HD), 0, st, part, S, Hq, out, hi, lo);
 }
 

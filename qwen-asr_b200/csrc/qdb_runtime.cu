@@ -91,6 +91,8 @@ struct RowScratch {
     unsigned long long *amax = nullptr;  // [2 * log_cap] sliced-argmax keys and counters (kept at zero)
     float *part = nullptr;
     size_t part_cap = 0;
+    unsigned *acnt = nullptr;  // [acnt_cap] split counters of the decode attention units (kept at zero)
+    int acnt_cap = 0;
     QdbRowKV *rowkv = nullptr;
     int rowkv_cap = 0;
     void *amaps = nullptr;         // device CUtensorMap [2 * aseg_cap]: K, V map of each prefill segment
@@ -380,7 +382,7 @@ extern "C" void qdb_model_free(qdb_model *m) {
     cudaFree(m->err); cudaFree(m->tok_dev);
     RowScratch &r = m->rs;
     cudaFree(r.X); cudaFree(r.XH); cudaFree(r.XL); cudaFree(r.QKV); cudaFree(r.Q); cudaFree(r.ATT); cudaFree(r.ACT);
-    cudaFree(r.XH2); cudaFree(r.XL2); cudaFree(r.LOG); cudaFree(r.amax); cudaFree(r.part); cudaFree(r.rowkv); cudaFree(r.tok); cudaFree(r.err); cudaFree(r.GU); cudaFree(r.step);
+    cudaFree(r.XH2); cudaFree(r.XL2); cudaFree(r.LOG); cudaFree(r.amax); cudaFree(r.part); cudaFree(r.acnt); cudaFree(r.rowkv); cudaFree(r.tok); cudaFree(r.err); cudaFree(r.GU); cudaFree(r.step);
     cudaFree(r.amaps); cudaFree(r.asegs);
     BatchScratch &b = m->bs;
     cudaFree(b.x); cudaFree(b.qkv); cudaFree(b.gu); cudaFree(b.part); cudaFree(b.stats); cudaFree(b.best);
@@ -863,6 +865,14 @@ static int run_rows(qdb_model *m, int n, const PrefillPlan *pf, const QdbRowKV *
             if (dev_alloc(&r.part, need)) return -1;
             r.part_cap = need;
         }
+        if (n * Hkv > r.acnt_cap) {
+            cudaFree(r.acnt);
+            r.acnt = nullptr;
+            r.acnt_cap = 0;
+            if (dev_alloc(&r.acnt, (size_t)n * Hkv)) return -1;
+            CK(cudaMemsetAsync(r.acnt, 0, sizeof(unsigned) * (size_t)n * Hkv, m->st));
+            r.acnt_cap = n * Hkv;
+        }
     }
     // Y (op)= X W^T from the bf16 split in XH/XL. Skinny problems (decode
     // batches of <= 64 rows) use split-K with atomic accumulation: mode 0
@@ -898,7 +908,7 @@ static int run_rows(qdb_model *m, int n, const PrefillPlan *pf, const QdbRowKV *
             CK(qdb_launch_qk_rope_append(r.QKV, r.Q, row0_dev, pos_off, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
                                          m->cfg.eps, m->st, step));
             CK(qdb_launch_attn_rows(r.Q, row0_dev, pos_off, l, n, Hq, Hkv, S, r.part, r.ATT, m->st, r.err, step,
-                                    r.XH, r.XL));
+                                    r.XH, r.XL, r.acnt));
         }
         // (both attention paths write the O-projection's bf16 split directly)
         if (gemm(lw.o, r.X, h, m->qd, 1)) return -1;
@@ -1304,7 +1314,7 @@ extern "C" int qdb_forward_batch(qdb_session *const *sessions, int n, const floa
     auto graph_key = [&]() {
         return std::vector<const void *>{(const void *)(intptr_t)n, (const void *)(intptr_t)S,
                                          (const void *)(intptr_t)m->mask_eos, m->rope, r.X, r.XH, r.XL, r.QKV, r.Q,
-                                         r.ATT, r.ACT, r.LOG, r.part, r.GU, r.tok, r.err, r.rowkv, r.amax};
+                                         r.ATT, r.ACT, r.LOG, r.part, r.acnt, r.GU, r.tok, r.err, r.rowkv, r.amax};
     };
     const std::vector<const void *> key = graph_key();
     if (m->fb_exec && key == m->fb_key) {
