@@ -389,6 +389,9 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AR_MINB) attn_rows_bulk_ker
 #ifndef QDB_AM_MINB
 #define QDB_AM_MINB 3  // CTAs per SM the fragment form's register budget is sized for
 #endif
+#ifndef QDB_AM_EARLY
+#define QDB_AM_EARLY 0  // copy chunks of earlier steps' keys before the dependency wait (measured slower)
+#endif
 #ifndef QDB_AM_STAGES
 #define QDB_AM_STAGES 2  // chunk slots of the fragment form (34 KB each)
 #endif
@@ -430,7 +433,7 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kern
                                                                         uint16_t *lo, unsigned *cnt) {
     static_assert(AR_WARPS * 16 == QDB_HD && AR_WARPS * 8 == AB_KEYS && R <= 8, "fragment form shape");
     constexpr int PLD = AB_KEYS + 8;  // p row stride in halves (144 bytes: conflict-free ldmatrix)
-    pdl_enter();
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     extern __shared__ __align__(128) unsigned char ring[];
     constexpr int QLD = QDB_HD + 8;  // q row stride in halves (272 bytes)
     // q and p of the chunk as fp16 hi / lo rows; row R is zeros, and the
@@ -441,12 +444,7 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kern
     __shared__ int last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, g4 = lane >> 2, t4 = lane & 3;
     const int row = blockIdx.x / Hkv, g = blockIdx.x % Hkv, s = blockIdx.y;
-    const QdbRowKV rk = rows[row];
-    const int pos = rk.pos + row_pos_offset + (step ? *step : 0);
-    const int ctx = pos + 1;
-    const int per = (ctx + S - 1) / S;
-    const int p0 = s * per, p1 = min(ctx, p0 + per);
-    const int nch = p1 > p0 ? (p1 - p0 + AB_KEYS - 1) / AB_KEYS : 0;
+    const QdbRowKV rk = rows[row];  // written by the host before the launch
     const size_t head_base = ((size_t)layer * Hkv + g) * (size_t)rk.cap * QDB_HD;
     // this thread's 16-byte pieces: piece tp of keys tk, tk + 16, tk + 32, tk + 48
     constexpr int PIECES = QDB_HD * 2 / 16, KSTEP = AR_WARPS * 32 / PIECES;
@@ -454,26 +452,47 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kern
     const uint16_t *kc = rk.kc + head_base + (size_t)tk * QDB_HD + tp * 8;
     const uint16_t *vc = rk.vc + head_base + (size_t)tk * QDB_HD + tp * 8;
     const uint32_t sdst = su32r(ring) + tk * AM_LDB + tp * 16;
+    auto copy_chunk = [&](int c, int k0, int nk) {
+        const uint32_t d = sdst + (uint32_t)(c % AM_STAGES) * AM_STAGE;
+#pragma unroll
+        for (int j = 0; j < AB_KEYS / KSTEP; j++) {
+            if (tk + j * KSTEP < nk) {
+                const size_t src = (size_t)(k0 + j * KSTEP) * QDB_HD;
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + j * KSTEP * AM_LDB), "l"(kc + src)
+                             : "memory");
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + AM_HALF + j * KSTEP * AM_LDB),
+                             "l"(vc + src)
+                             : "memory");
+            }
+        }
+    };
+    // Before waiting on the previous kernel: whole chunks of keys written by
+    // earlier steps. Only the current position's key is written by this
+    // step's RoPE kernel; the step counter read here may still lag the
+    // step's own increment by one, which only lowers the bound.
+    int early = 0;
+    if (S == 1 && QDB_AM_EARLY) {
+        const int old_keys = rk.pos + row_pos_offset + (step ? *(volatile const int *)step : 0);
+        while (early < AM_STAGES && (early + 1) * AB_KEYS <= old_keys) {
+            copy_chunk(early, early * AB_KEYS, AB_KEYS);
+            asm volatile("cp.async.commit_group;" ::: "memory");
+            early++;
+        }
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int pos = rk.pos + row_pos_offset + (step ? *step : 0);
+    const int ctx = pos + 1;
+    const int per = (ctx + S - 1) / S;
+    const int p0 = s * per, p1 = min(ctx, p0 + per);
+    const int nch = p1 > p0 ? (p1 - p0 + AB_KEYS - 1) / AB_KEYS : 0;
     auto issue = [&](int c) {  // one cp.async commit group per chunk slot (empty past the last chunk)
         if (c < nch) {
-            const int k0 = p0 + c * AB_KEYS, nk = min(AB_KEYS, p1 - k0);
-            const uint32_t d = sdst + (uint32_t)(c % AM_STAGES) * AM_STAGE;
-#pragma unroll
-            for (int j = 0; j < AB_KEYS / KSTEP; j++) {
-                if (tk + j * KSTEP < nk) {
-                    const size_t src = (size_t)(k0 + j * KSTEP) * QDB_HD;
-                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + j * KSTEP * AM_LDB),
-                                 "l"(kc + src)
-                                 : "memory");
-                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d + AM_HALF + j * KSTEP * AM_LDB),
-                                 "l"(vc + src)
-                                 : "memory");
-                }
-            }
+            const int k0 = p0 + c * AB_KEYS;
+            copy_chunk(c, k0, min(AB_KEYS, p1 - k0));
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    for (int c = 0; c < AM_STAGES; c++) issue(c);
+    for (int c = early; c < AM_STAGES; c++) issue(c);
     for (int i = threadIdx.x; i < 2 * (R + 1) * PLD; i += blockDim.x) (&ps[0][0][0])[i] = 0;
     for (int i = threadIdx.x; i < (R + 1) * QDB_HD / 2; i += blockDim.x) {  // q as hi / lo pairs
         const int h = i / (QDB_HD / 2), d = (i % (QDB_HD / 2)) * 2;
