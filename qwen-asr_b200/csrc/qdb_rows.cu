@@ -392,6 +392,9 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AR_MINB) attn_rows_bulk_ker
 #ifndef QDB_AM_EARLY
 #define QDB_AM_EARLY 0  // copy chunks of earlier steps' keys before the dependency wait (measured slower)
 #endif
+#ifndef QDB_AM_BAR3
+#define QDB_AM_BAR3 0  // three block barriers per chunk (the refill moves after the next chunk's first): no gain measured
+#endif
 #ifndef QDB_AM_STAGES
 #define QDB_AM_STAGES 2  // chunk slots of the fragment form (34 KB each)
 #endif
@@ -526,8 +529,14 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kern
         }
         // this thread's copies of chunk c are done (later slots may still be
         // in flight); the barrier makes every thread's copies visible
-        asm volatile("cp.async.wait_group %0;" ::"n"(AM_STAGES - 1) : "memory");
+        if (QDB_AM_BAR3 && c > 0)
+            asm volatile("cp.async.wait_group %0;" ::"n"(AM_STAGES - 2) : "memory");
+        else
+            asm volatile("cp.async.wait_group %0;" ::"n"(AM_STAGES - 1) : "memory");
         __syncthreads();
+        // with QDB_AM_BAR3 the slot of chunk c - 1 is refilled here: the
+        // barrier above is the proof that every warp is done with it
+        if (QDB_AM_BAR3 && c > 0) issue(c + AM_STAGES - 1);
         // 1. scores of keys [8 warp, 8 warp + 8) and their max per head
         float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -594,8 +603,10 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kern
             mma16816(o[1], ah[0], ah[1], b[2], b[3]);
             mma16816(o[1], al[0], al[1], b[2], b[3]);
         }
-        __syncthreads();  // the stage, p and the partial maxima / sums are free
-        issue(c + AM_STAGES);
+        if (!QDB_AM_BAR3) {
+            __syncthreads();  // the stage, p and the partial maxima / sums are free
+            issue(c + AM_STAGES);
+        }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     // lane (g4 < R) holds head g4 at dims 16 warp + 8 nt + 2 t4 + {0, 1}
