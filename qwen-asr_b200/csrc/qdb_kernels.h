@@ -131,6 +131,13 @@ cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows, int row_p
                                  int n, int Hq, int Hkv, int splits, float *part, float *out,
                                  cudaStream_t st, int *err = nullptr, const int *step = nullptr,
                                  uint16_t *hi = nullptr, uint16_t *lo = nullptr, unsigned *cnt = nullptr);
+// Fused form of qdb_launch_qk_rope_append + qdb_launch_attn_rows (qkv: the
+// raw [n, (Hq + 2 Hkv) * 128] QKV rows; cnt required). cudaErrorNotSupported
+// when the fused form is built out: launch the two instead.
+cudaError_t qdb_launch_attn_rows_rope(const float *qkv, const QdbRowKV *rows, int row_pos_offset, int layer, int n,
+                                      int Hq, int Hkv, int S, const float *q_norm, const float *k_norm,
+                                      const float2 *rope, float eps, float *part, float *out, cudaStream_t st,
+                                      int *err, const int *step, uint16_t *hi, uint16_t *lo, unsigned *cnt);
 // ---- persistent batched decode step (qdb_bstep.cu) ----
 // One decode position of B <= 64 independent utterances in one cooperative
 // launch. Activation buffers are [feature][Bp] f32 (utterance = column).

@@ -370,6 +370,13 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AR_MINB) attn_rows_bulk_ker
     }
 }
 
+// QK-norm / RoPE inputs of the fused form (qkv == nullptr: q is read as is)
+struct AttnRope {
+    const float *qkv, *q_norm, *k_norm;
+    const float2 *rope;
+    float eps;
+};
+
 // ---------------------------------------------------------------- fragment (MMA) form
 // The same unit (row, KV head g, split s) on the tensor cores' warp-level
 // MMA (m16n8k16, f16 in, f32 accumulate): the unit is bound by instruction
@@ -391,6 +398,9 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AR_MINB) attn_rows_bulk_ker
 #endif
 #ifndef QDB_AM_EARLY
 #define QDB_AM_EARLY 0  // copy chunks of earlier steps' keys before the dependency wait (measured slower)
+#endif
+#ifndef QDB_AR_FUSED_ROPE
+#define QDB_AR_FUSED_ROPE 0  // QK-norm, RoPE and the K/V append inside the decode attention units (measured: no gain)
 #endif
 #ifndef QDB_AM_BAR3
 #define QDB_AM_BAR3 0  // three block barriers per chunk (the refill moves after the next chunk's first): no gain measured
@@ -433,7 +443,7 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kern
                                                                         int row_pos_offset, int layer, int Hq,
                                                                         int Hkv, int S, float *part, int *err,
                                                                         const int *step, float *out, uint16_t *hi,
-                                                                        uint16_t *lo, unsigned *cnt) {
+                                                                        uint16_t *lo, unsigned *cnt, AttnRope rp) {
     static_assert(AR_WARPS * 16 == QDB_HD && AR_WARPS * 8 == AB_KEYS && R <= 8, "fragment form shape");
     constexpr int PLD = AB_KEYS + 8;  // p row stride in halves (144 bytes: conflict-free ldmatrix)
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -495,18 +505,74 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kern
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    for (int c = early; c < AM_STAGES; c++) issue(c);
+    // With rp.qkv the unit also does the QK-norm, RoPE and cache append of
+    // its own heads (the work of qk_rope_append_kernel): the split holding
+    // key pos writes K/V row pos, and that chunk is copied only after the
+    // block barrier that follows the write.
+    const bool own_kv = rp.qkv && p0 <= pos && pos < p1;
+    int pro = AM_STAGES;  // prologue chunks issued before the append
+    if (own_kv)
+        for (int c = early; c < AM_STAGES; c++)
+            if (c < nch && p0 + (c + 1) * AB_KEYS > pos) {
+                pro = c;
+                break;
+            }
+    for (int c = early; c < pro; c++) issue(c);
     for (int i = threadIdx.x; i < 2 * (R + 1) * PLD; i += blockDim.x) (&ps[0][0][0])[i] = 0;
-    for (int i = threadIdx.x; i < (R + 1) * QDB_HD / 2; i += blockDim.x) {  // q as hi / lo pairs
-        const int h = i / (QDB_HD / 2), d = (i % (QDB_HD / 2)) * 2;
-        uint32_t qh = 0u, ql = 0u;
-        if (h < R) {
-            const float2 v =
-                *reinterpret_cast<const float2 *>(q + (size_t)row * Hq * QDB_HD + (size_t)(g * R + h) * QDB_HD + d);
-            split_h2(v.x, v.y, qh, ql);
+    if (rp.qkv) {
+        if (threadIdx.x < QDB_HD) {  // the zero row
+            qsm[0][R][threadIdx.x] = 0;
+            qsm[1][R][threadIdx.x] = 0;
         }
-        *reinterpret_cast<uint32_t *>(&qsm[0][h][d]) = qh;
-        *reinterpret_cast<uint32_t *>(&qsm[1][h][d]) = ql;
+        // warp w < R: query head g R + w; warp R: key head g; warp R + 1: value head g
+        if (warp < R + 2 && (warp < R || own_kv)) {
+            const int slot = warp < R ? g * R + warp : (warp == R ? Hq + g : Hq + Hkv + g);
+            const float *src = rp.qkv + (size_t)row * (Hq + 2 * Hkv) * QDB_HD + (size_t)slot * QDB_HD;
+            float e[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) e[i] = src[lane + 32 * i];
+            if (warp <= R) {
+                const float *w = warp < R ? rp.q_norm : rp.k_norm;
+                const float ss = warp_sum(e[0] * e[0] + e[1] * e[1] + e[2] * e[2] + e[3] * e[3]);
+                const float inv = 1.0f / sqrtf(ss / (float)QDB_HD + rp.eps);
+#pragma unroll
+                for (int i = 0; i < 4; i++) e[i] = e[i] * inv * w[lane + 32 * i];
+                const float2 *rr = rp.rope + (size_t)pos * (QDB_HD / 2);
+#pragma unroll
+                for (int i = 0; i < 2; i++) {
+                    const float2 cs = rr[lane + 32 * i];
+                    const float x1 = e[i], x2 = e[i + 2];
+                    e[i] = x1 * cs.x - x2 * cs.y;
+                    e[i + 2] = x2 * cs.x + x1 * cs.y;
+                }
+            }
+            if (warp < R) {
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const __half h = __float2half_rn(e[i]);
+                    qsm[0][warp][lane + 32 * i] = __half_as_ushort(h);
+                    qsm[1][warp][lane + 32 * i] = __half_as_ushort(__float2half_rn(e[i] - __half2float(h)));
+                }
+            } else {
+                uint16_t *dst = (warp == R ? rk.kc : rk.vc) + head_base + (size_t)pos * QDB_HD;
+#pragma unroll
+                for (int i = 0; i < 4; i++) dst[lane + 32 * i] = f32_to_kv(e[i]);
+            }
+        }
+        __syncthreads();  // q in shared memory; row pos in the cache for this CTA's copies
+        for (int c = pro; c < AM_STAGES; c++) issue(c);
+    } else {
+        for (int i = threadIdx.x; i < (R + 1) * QDB_HD / 2; i += blockDim.x) {  // q as hi / lo pairs
+            const int h = i / (QDB_HD / 2), d = (i % (QDB_HD / 2)) * 2;
+            uint32_t qh = 0u, ql = 0u;
+            if (h < R) {
+                const float2 v = *reinterpret_cast<const float2 *>(q + (size_t)row * Hq * QDB_HD +
+                                                                   (size_t)(g * R + h) * QDB_HD + d);
+                split_h2(v.x, v.y, qh, ql);
+            }
+            *reinterpret_cast<uint32_t *>(&qsm[0][h][d]) = qh;
+            *reinterpret_cast<uint32_t *>(&qsm[1][h][d]) = ql;
+        }
     }
     // scores in log2 units: p = 2^(s' - m'), s' = q.k / sqrt(128) x log2(e)
     const float scale2 = 1.4426950408889634f / sqrtf((float)QDB_HD);
@@ -795,14 +861,15 @@ extern "C" cudaError_t qdb_launch_qk_rope_append_single(const float *qkv, float 
 template <int R>
 static cudaError_t attn_rows_launch(dim3 grid, const float *q, const QdbRowKV *rows, int row_pos_offset, int layer,
                                     int Hq, int Hkv, int S, float *part, int *err, cudaStream_t st, const int *step,
-                                    float *out, uint16_t *hi, uint16_t *lo, unsigned *cnt) {
+                                    float *out, uint16_t *hi, uint16_t *lo, unsigned *cnt,
+                                    AttnRope rp = AttnRope{nullptr, nullptr, nullptr, nullptr, 0.f}) {
     if (QDB_AR_MMA && (S == 1 || cnt)) {
         const int smem = AM_STAGES * AM_STAGE;
         cudaError_t e =
             cudaFuncSetAttribute(attn_rows_mma_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         return pdl_launch(attn_rows_mma_kernel<R>, grid, dim3(AR_WARPS * 32), (size_t)smem, st, q, rows,
-                          row_pos_offset, layer, Hq, Hkv, S, part, err, step, out, hi, lo, cnt);
+                          row_pos_offset, layer, Hq, Hkv, S, part, err, step, out, hi, lo, cnt, rp);
     }
     const int smem = AB_STAGES * AB_STAGE;
     cudaError_t e = cudaFuncSetAttribute(attn_rows_bulk_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -829,6 +896,30 @@ extern "C" cudaError_t qdb_launch_attn_rows(const float *q, const QdbRowKV *rows
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || S == 1 || cnt) return e;  // S == 1 or cnt: the units wrote the output
     return pdl_launch(attn_rows_merge_kernel, dim3(n, Hq), dim3(QDB_HD), 0, st, part, S, Hq, out, hi, lo);
+}
+
+// Fused form: QK-norm, RoPE and the K/V append of the decode rows inside the
+// attention units (replaces qdb_launch_qk_rope_append + qdb_launch_attn_rows).
+// cudaErrorNotSupported: the fused form is built out; the caller launches the two.
+extern "C" cudaError_t qdb_launch_attn_rows_rope(const float *qkv, const QdbRowKV *rows, int row_pos_offset,
+                                                 int layer, int n, int Hq, int Hkv, int S, const float *q_norm,
+                                                 const float *k_norm, const float2 *rope, float eps, float *part,
+                                                 float *out, cudaStream_t st, int *err, const int *step,
+                                                 uint16_t *hi, uint16_t *lo, unsigned *cnt) {
+    if (!QDB_AR_MMA || !QDB_AR_FUSED_ROPE || !cnt) return cudaErrorNotSupported;
+    if (n <= 0) return cudaSuccess;
+    const AttnRope rp{qkv, q_norm, k_norm, rope, eps};
+    dim3 grid(n * Hkv, S);
+    cudaError_t e0;
+    switch (Hq / Hkv) {
+        case 1: e0 = attn_rows_launch<1>(grid, nullptr, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo, cnt, rp); break;
+        case 2: e0 = attn_rows_launch<2>(grid, nullptr, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo, cnt, rp); break;
+        case 4: e0 = attn_rows_launch<4>(grid, nullptr, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo, cnt, rp); break;
+        case 8: e0 = attn_rows_launch<8>(grid, nullptr, rows, row_pos_offset, layer, Hq, Hkv, S, part, err, st, step, out, hi, lo, cnt, rp); break;
+        default: return cudaErrorInvalidValue;
+    }
+    if (e0 != cudaSuccess) return e0;
+    return cudaGetLastError();
 }
 
 extern "C" cudaError_t qdb_launch_argmax_rows(const float *logits, int n, int V, int mask_eos, int *tokens,

@@ -905,10 +905,17 @@ static int run_rows(qdb_model *m, int n, const PrefillPlan *pf, const QdbRowKV *
             CK(qdb_launch_attn_prefill_tc(r.amaps, r.asegs, pf->nseg, pf->max_n, l, Hq, Hkv, r.Q, r.ATT, r.err, m->st,
                                           r.XH, r.XL));
         } else {
-            CK(qdb_launch_qk_rope_append(r.QKV, r.Q, row0_dev, pos_off, l, n, Hq, Hkv, lw.q_norm, lw.k_norm, m->rope,
-                                         m->cfg.eps, m->st, step));
-            CK(qdb_launch_attn_rows(r.Q, row0_dev, pos_off, l, n, Hq, Hkv, S, r.part, r.ATT, m->st, r.err, step,
-                                    r.XH, r.XL, r.acnt));
+            const cudaError_t fe =
+                qdb_launch_attn_rows_rope(r.QKV, row0_dev, pos_off, l, n, Hq, Hkv, S, lw.q_norm, lw.k_norm, m->rope,
+                                          m->cfg.eps, r.part, r.ATT, m->st, r.err, step, r.XH, r.XL, r.acnt);
+            if (fe == cudaErrorNotSupported) {
+                CK(qdb_launch_qk_rope_append(r.QKV, r.Q, row0_dev, pos_off, l, n, Hq, Hkv, lw.q_norm, lw.k_norm,
+                                             m->rope, m->cfg.eps, m->st, step));
+                CK(qdb_launch_attn_rows(r.Q, row0_dev, pos_off, l, n, Hq, Hkv, S, r.part, r.ATT, m->st, r.err, step,
+                                        r.XH, r.XL, r.acnt));
+            } else {
+                CK(fe);
+            }
         }
         // (both attention paths write the O-projection's bf16 split directly)
         if (gemm(lw.o, r.X, h, m->qd, 1)) return -1;
