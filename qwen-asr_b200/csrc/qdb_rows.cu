@@ -399,6 +399,9 @@ struct AttnRope {
 #ifndef QDB_AM_EARLY
 #define QDB_AM_EARLY 0  // copy chunks of earlier steps' keys before the dependency wait (measured slower)
 #endif
+#ifndef QDB_AM_CHAINS
+#define QDB_AM_CHAINS 0  // independent MMA accumulation chains (hi / lo, even / odd k-steps): measured slower
+#endif
 #ifndef QDB_AR_FUSED_ROPE
 #define QDB_AR_FUSED_ROPE 0  // QK-norm, RoPE and the K/V append inside the decode attention units (measured: no gain)
 #endif
@@ -578,6 +581,9 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kern
     const float scale2 = 1.4426950408889634f / sqrtf((float)QDB_HD);
     float m = -INFINITY, l = 0.f;
     float o[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#if QDB_AM_CHAINS
+    float ol[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#endif
     const int mi = lane >> 3;
     const uint32_t kb = su32r(ring) + (warp * 8 + (lane & 7)) * AM_LDB + mi * 16;
     const uint32_t vb = su32r(ring) + AM_HALF + ((mi & 1) * 8 + (lane & 7)) * AM_LDB + (warp * 16 + (mi >> 1) * 8) * 2;
@@ -605,6 +611,24 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kern
         if (QDB_AM_BAR3 && c > 0) issue(c + AM_STAGES - 1);
         // 1. scores of keys [8 warp, 8 warp + 8) and their max per head
         float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#if QDB_AM_CHAINS
+        {  // four independent accumulation chains of four MMAs each
+            float c1[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f}, c3[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int k2 = 0; k2 < 4; k2++) {
+                uint32_t b[4], ah[4], al[4];
+                ldsm_x4(b, kb + so + k2 * 64);
+                ldsm_x4(ah, qb + k2 * 64);
+                ldsm_x4(al, qb + k2 * 64 + (R + 1) * QLD * 2);
+                mma16816(sc, ah[0], ah[1], b[0], b[1]);
+                mma16816(c1, al[0], al[1], b[0], b[1]);
+                mma16816(c2, ah[2], ah[3], b[2], b[3]);
+                mma16816(c3, al[2], al[3], b[2], b[3]);
+            }
+#pragma unroll
+            for (int e = 0; e < 4; e++) sc[e] = (sc[e] + c2[e]) + (c1[e] + c3[e]);
+        }
+#else
 #pragma unroll
         for (int k2 = 0; k2 < 4; k2++) {
             uint32_t b[4], ah[4], al[4];
@@ -616,6 +640,7 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kern
             mma16816(sc, ah[2], ah[3], b[2], b[3]);
             mma16816(sc, al[2], al[3], b[2], b[3]);
         }
+#endif
         const int kl = warp * 8 + t4 * 2;
         const float s0 = kl < nk ? sc[0] * scale2 : -INFINITY, s1 = kl + 1 < nk ? sc[1] * scale2 : -INFINITY;
         float lm = fmaxf(s0, s1);
@@ -653,7 +678,12 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kern
 #pragma unroll
         for (int nt = 0; nt < 2; nt++)
 #pragma unroll
-            for (int e = 0; e < 4; e++) o[nt][e] *= corr;
+            for (int e = 0; e < 4; e++) {
+                o[nt][e] *= corr;
+#if QDB_AM_CHAINS
+                ol[nt][e] *= corr;
+#endif
+            }
 #pragma unroll
         for (int ks = 0; ks < 4; ks++) {
             uint32_t b[4], ah[2], al[2];
@@ -665,9 +695,14 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kern
                          : "=r"(al[0]), "=r"(al[1])
                          : "r"(pb + ks * 32 + (R + 1) * PLD * 2));
             mma16816(o[0], ah[0], ah[1], b[0], b[1]);
-            mma16816(o[0], al[0], al[1], b[0], b[1]);
             mma16816(o[1], ah[0], ah[1], b[2], b[3]);
+#if QDB_AM_CHAINS
+            mma16816(ol[0], al[0], al[1], b[0], b[1]);  // the p lo products: their own chains
+            mma16816(ol[1], al[0], al[1], b[2], b[3]);
+#else
+            mma16816(o[0], al[0], al[1], b[0], b[1]);
             mma16816(o[1], al[0], al[1], b[2], b[3]);
+#endif
         }
         if (!QDB_AM_BAR3) {
             __syncthreads();  // the stage, p and the partial maxima / sums are free
@@ -675,6 +710,12 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kern
         }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
+#if QDB_AM_CHAINS
+#pragma unroll
+    for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) o[nt][e] += ol[nt][e];
+#endif
     // lane (g4 < R) holds head g4 at dims 16 warp + 8 nt + 2 t4 + {0, 1}
     if (g4 < R) {
         const int h = g4;
