@@ -382,9 +382,11 @@ struct AttnRope {
 // MMA (m16n8k16, f16 in, f32 accumulate): the unit is bound by instruction
 // issue in the lane-dot form above (~160 instructions per KB of K/V), and
 // fragments do the q.K and p.V products in a few instructions per 8 x 16
-// tile. Precision: K and V are the cache's fp16 values exactly; q and p are
-// carried as fp16 hi + lo pairs (two MMAs each, ~22 significant bits), so the
-// scores and the output match the f32 form to ~1e-6 relative.
+// tile. Precision: K and V are the cache's fp16 values exactly; q is carried
+// as an fp16 hi + lo pair (two MMAs, ~22 significant bits), so the scores
+// match the f32 form to ~1e-6 relative; p in [0, 1] is rounded to fp16
+// (relative error <= 2^-11 per weight, averaging out over the keys: the
+// same order as the fp16 cache rounding of V itself), f32 accumulation.
 // Layout: each chunk's 64 K and V rows are copied in 16-byte pieces
 // (cp.async) into a 272-byte row stride (conflict-free ldmatrix); warp w scores keys [8w, 8w + 8) with the R
 // query heads as MMA rows, every warp runs the same softmax over the chunk's
@@ -398,6 +400,9 @@ struct AttnRope {
 #endif
 #ifndef QDB_AM_EARLY
 #define QDB_AM_EARLY 0  // copy chunks of earlier steps' keys before the dependency wait (measured slower)
+#endif
+#ifndef QDB_AM_PLO
+#define QDB_AM_PLO 0  // 1: p carried as fp16 hi + lo in p.V (twice the p.V MMAs); 0: fp16 p
 #endif
 #ifndef QDB_AM_CHAINS
 #define QDB_AM_CHAINS 0  // independent MMA accumulation chains (hi / lo, even / odd k-steps): measured slower
@@ -700,8 +705,10 @@ __global__ void __launch_bounds__(AR_WARPS * 32, QDB_AM_MINB) attn_rows_mma_kern
             mma16816(ol[0], al[0], al[1], b[0], b[1]);  // the p lo products: their own chains
             mma16816(ol[1], al[0], al[1], b[2], b[3]);
 #else
-            mma16816(o[0], al[0], al[1], b[0], b[1]);
-            mma16816(o[1], al[0], al[1], b[2], b[3]);
+            if (QDB_AM_PLO) {
+                mma16816(o[0], al[0], al[1], b[0], b[1]);
+                mma16816(o[1], al[0], al[1], b[2], b[3]);
+            }
 #endif
         }
         if (!QDB_AM_BAR3) {
