@@ -10,16 +10,18 @@
 //
 //   S = Q K^T      A = Q rows (fp16 hi + lo of the f32 q, written by threads),
 //                  B = 128 cached keys (fp16, TMA 2D with 128-byte swizzle)
-//   per key tile  online softmax: row max of S, P = exp(s - m) as fp16 hi +
-//                  lo (threads), the running max raised (O rescaled in
+//   per key tile  online softmax: row max of S, P = exp(s - m) as fp16
+//                  (threads), the running max raised (O rescaled in
 //                  TMEM) only when it grows by more than 8; O += P V in TMEM
 //                  with V straight from its TMA tile as an MN-major B operand
 //                  (keys along K, dims along N); O / l in the epilogue
 //
 // All operands are K-major with 128-byte swizzle (the layout the TMA writes
-// for the K tile and the threads write for Q, P and V^T). The activation
-// halves keep ~22 mantissa bits of the f32 q and p; K and V are the cache's
-// own fp16 values, so the products are exact up to f32 accumulation.
+// for the K tile and the threads write for Q and P). The q halves keep ~22
+// mantissa bits of the f32 q; P in [0, 1] is rounded to fp16 (relative error
+// <= 2^-11 per weight, the order of the fp16 cache rounding of V; the hi + lo
+// form is QDB_AT_PLO=1); K and V are the cache's own fp16 values; f32
+// accumulation.
 // Every mbarrier wait is bounded (error word + early exit); TMEM is always
 // released.
 #include <cuda.h>
@@ -160,6 +162,19 @@ __device__ __forceinline__ uint32_t swz(int r, int c) {
 
 __device__ __forceinline__ uint32_t h2u(__half a, __half b) {
     return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+}
+
+#ifndef QDB_AT_PLO
+#define QDB_AT_PLO 0  // 1: P as fp16 hi + lo tiles (two P.V MMAs per step); 0: P as fp16
+#endif
+
+// Writes 8 f32 values as fp16 (tile hi), chunk c of row r.
+__device__ __forceinline__ void put8_hi(unsigned char *hi, int r, int c, const float *v) {
+    __half h[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) h[i] = __float2half_rn(v[i]);
+    *reinterpret_cast<uint4 *>(hi + swz(r, c)) =
+        make_uint4(h2u(h[0], h[1]), h2u(h[2], h[3]), h2u(h[4], h[5]), h2u(h[6], h[7]));
 }
 
 // Writes 8 f32 values as fp16 hi (tile hi) and lo = fp16(v - hi) (tile lo),
@@ -336,7 +351,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
 #pragma unroll
         for (int q8 = 0; q8 < 8; q8++) {
             const int col = half * 64 + q8 * 8;  // key column within the tile
-            put8_split(Ph + (col >> 6) * AT_TILE, Pl + (col >> 6) * AT_TILE, r, (col & 63) >> 3, v + q8 * 8);
+            if (QDB_AT_PLO)
+                put8_split(Ph + (col >> 6) * AT_TILE, Pl + (col >> 6) * AT_TILE, r, (col & 63) >> 3, v + q8 * 8);
+            else
+                put8_hi(Ph + (col >> 6) * AT_TILE, r, (col & 63) >> 3, v + q8 * 8);
         }
         // V: wait for its tile
         if (t == 0 && s_ok) {
@@ -370,7 +388,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                     const u64 bv = sm_desc_mn(su32(Kt) + (kb * 64 + k * 16) * 128, AT_TILE);
                     const uint32_t id = idesc | (1u << 16);  // bit 16: B is MN-major
                     mma_f16(tO, sm_desc(su32(Ph + kb * AT_TILE) + k * 32), bv, id, (kt | kb | k) ? 1u : 0u);
-                    mma_f16(tO, sm_desc(su32(Pl + kb * AT_TILE) + k * 32), bv, id, 1u);
+                    if (QDB_AT_PLO) mma_f16(tO, sm_desc(su32(Pl + kb * AT_TILE) + k * 32), bv, id, 1u);
                 }
             mma_commit(&barO);
             if (!mb_wait(&barO, phO, err)) s_ok = 0;
