@@ -398,3 +398,30 @@ def test_persistent_batch_greedy_loop_matches_graph_path(pkg, synth, monkeypatch
     monkeypatch.delenv("QWEN_ASR_B200_BATCH")
     tg = pkg.decode_greedy_batch(sg, [198] * len(lens), lens, 12)
     assert (ta == tg).mean() >= 0.9, (ta, tg)  # exact except where a near-tie flips
+
+
+@pytest.mark.parametrize("heads,kv_heads", [(4, 4), (4, 2), (8, 2), (8, 1)])
+def test_batched_decode_long_contexts_groupings(pkg, synth, heads, kv_heads):
+    """qdb_forward_batch with contexts past one 512-key attention unit (the
+    rows' keys split over up to 3 units whose last finisher merges the
+    partials inside the attention kernel; a 40-key row leaves units empty),
+    for 1, 2, 4 and 8 query heads per KV head, against per-session
+    qdb_forward (the b=1 step kernel)."""
+    cfg = synth.Config(256, 2, heads, kv_heads, 128, 512, 600)
+    ws = synth.WeightSet(cfg, seed=10, norm_jitter=0.1)
+    model = pkg.Model(ws, device=0, mask_eos=True)
+    lens = [1100, 40, 530, 700]
+    embs = [synth.audio_embeddings(cfg, L + 3, seed=800 + b) for b, L in enumerate(lens)]
+    sb = [model.session(L + 8) for L in lens]
+    ss = [model.session(L + 8) for L in lens]
+    for b, L in enumerate(lens):
+        sb[b].prefill(embs[b][:L], 0)
+        ss[b].prefill(embs[b][:L], 0)
+    for step in range(3):
+        x = np.stack([embs[b][L + step] for b, L in enumerate(lens)])
+        pos = [L + step for L in lens]
+        got, logits = pkg.forward_batch(sb, x, pos, want_logits=True)
+        for b in range(len(lens)):
+            want, _, lg = ss[b].forward(x[b], pos[b], want_logits=True)
+            assert_logits_close(logits[b], lg, f"R={heads // kv_heads} row {b} step {step}")
+            assert got[b] == want or margin_top2(lg, mask_eos=True) <= MARGIN, (step, b)
