@@ -490,7 +490,21 @@ extern "C" int qdb_streams_chunk(qdb_streams *S, const float *const *audio, cons
         pos[j] = s.prefill_len;
     }
     S->h_tokens.resize((size_t)na * steps);
-    if (qdb_decode_greedy_batch(ds.data(), na, first.data(), pos.data(), steps, S->h_tokens.data())) return -1;
+    // Keep this prompt for the next chunk's prefix comparison: host copies of
+    // the rows (hundreds of MB per round at 256 streams) that depend only on
+    // this call's inputs, made on a host thread while the GPU runs the greedy
+    // loop (nothing reads prev_* until the next call).
+    std::thread saver([&] {
+        parallel_for(na, [&](int j) {
+            Stream &s = S->st[act[j]];
+            s.prev_desc.assign(s.desc.begin(), s.desc.begin() + s.prefill_len);
+            s.prev_audio.assign(audio[act[j]], audio[act[j]] + (size_t)s.audio_rows * h);
+            s.prev_len = s.prefill_len;
+        });
+    });
+    const int grc = qdb_decode_greedy_batch(ds.data(), na, first.data(), pos.data(), steps, S->h_tokens.data());
+    saver.join();
+    if (grc) return -1;
     cudaEventRecord(S->ev[2], st);
     if (cudaEventSynchronize(S->ev[2]) == cudaSuccess) {
         cudaEventElapsedTime(&S->last_ms[0], S->ev[0], S->ev[1]);
@@ -502,10 +516,6 @@ extern "C" int qdb_streams_chunk(qdb_streams *S, const float *const *audio, cons
         Stream &s = S->st[i];
         std::vector<int> gen(steps);
         for (int t = 0; t < steps; t++) gen[t] = S->h_tokens[(size_t)t * na + j];
-        // keep this prompt for the next chunk's prefix comparison
-        s.prev_desc.assign(s.desc.begin(), s.desc.begin() + s.prefill_len);
-        s.prev_audio.assign(audio[i], audio[i] + (size_t)s.audio_rows * h);
-        s.prev_len = s.prefill_len;
         commit_chunk(S, s, gen.data(), steps, is_final[i] != 0);
         s.decoded += s.last_generated;
         s.chunks_done++;
