@@ -491,7 +491,7 @@ extern "C" int qdb_streams_chunk(qdb_streams *S, const float *const *audio, cons
     }
     S->h_tokens.resize((size_t)na * steps);
     // Keep this prompt for the next chunk's prefix comparison: host copies of
-    // the rows (hundreds of MB per round at 256 streams) that depend only on
+    // the rows (hundreds of MB per call at 256 streams) that depend only on
     // this call's inputs, made on a host thread while the GPU runs the greedy
     // loop (nothing reads prev_* until the next call).
     std::thread saver([&] {
